@@ -1,0 +1,210 @@
+"""Generate golden fixtures by running the reference implementation on the CPU.
+
+Usage (in a checkout that has the reference sources):
+
+    CXX=/usr/bin/g++ python tests/golden/gen_golden.py --reference <path-to-onetensor-scope>
+
+* Mask fixtures: ``SpectralBias.build_pointer_blockmask`` (model/attn_bias.py:623-874)
+  run unmodified, with its Gumbel noise drawn from the same seeded generator
+  the reference uses (model/attn_bias.py:768-771) and recorded as g.
+* Attention fixtures: ``torch.compile(flex_attention)`` on the CPU (Inductor's
+  C++ flex template), called the way scoped_medium.py:459-466 calls it with a
+  scalar-form restatement of the score_mod closure of scoped_medium.py:425-457
+  (the vectorised closure does not lower in Inductor; the scalar form is the
+  same arithmetic), and the qk_aug augmentation of scoped_medium.py:380-423.
+  Eager flex_attention is not used: it ignores the BlockMask's kv lists.
+  The CPU flex path returns no lse (``return_lse`` is unsupported there), so
+  only the outputs are pinned; lse is pinned through the float64 restatement.
+
+Outputs: tests/golden/mask_<case>.npz and tests/golden/attn_<case>.npz.
+The reference is read only at generation time; the tests never import it.
+"""
+from __future__ import annotations
+
+import argparse
+import math
+import os
+import sys
+
+import numpy as np
+import torch
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+ROOT = os.path.dirname(os.path.dirname(HERE))
+sys.path.insert(0, ROOT)
+sys.path.insert(0, HERE)
+
+import cases as C  # noqa: E402
+from oracle import mask_oracle as MO  # noqa: E402
+from oracle import attn_oracle as AO  # noqa: E402
+
+SMALL = 1 << 16
+
+
+def make_sb(SpectralBias, case, H):
+    sb = SpectralBias(
+        head_dim=64, num_heads=H, L_train=max(case["T"], 256), K=2, M=case["M"],
+        use_pointer_mask=True,
+        pointer_local_blocks=case["local"], pointer_half_blocks=case["half"],
+        pointer_global_blocks=case["glob"], pointer_budget_blocks=case["budget"],
+        pointer_budget_is_total=case["total"], pointer_budget_temp=case["temp"],
+        pointer_radius_mode=case["mode"], pointer_qblock_rep=case.get("rep", "last"),
+        pointer_doc_clamp=case.get("doc_clamp", True),
+        gumbel_topk=bool(case.get("gumbel_k", 0)), gumbel_topk_k=case.get("gumbel_k", 0),
+        gumbel_topk_tau=case.get("gumbel_tau", 1.0), gumbel_topk_seed=case.get("gumbel_seed", 0),
+        pointer_reset_len=case.get("reset_len", 0),
+    )
+    sb.set_pointer_mask_state(enabled=case.get("ptr_enabled", True),
+                              half_blocks=case.get("half_active", case["half"]),
+                              global_blocks=case.get("glob_active", case["glob"]))
+    if case.get("reset_len", 0):
+        sb.set_pointer_reset_state(enabled=True, reset_len=case["reset_len"])
+    if case.get("gumbel_k", 0):
+        sb.train()
+    else:
+        sb.eval()
+    return sb
+
+
+def run_mask_case(SpectralBias, name, case):
+    H, T, bs, M = case["H"], case["T"], case["bs"], case["M"]
+    QB = T // bs
+    docs = C.mask_docs(case)
+    t_rep = (np.arange(QB) + 1) * bs - 1
+    if case["source"] == "select":
+        logits, g = C.selection_inputs(case)
+        centres = MO.select_pointer_blocks(logits, g, M=M, tau=case["sel_tau"])
+        budget = C.budget_only(case)
+        delta = np.zeros((1, H, T, M), dtype=np.float32)
+        delta[0, :, t_rep, :] = (t_rep[None, :, None] - centres.astype(np.int64) * bs).astype(np.float32).transpose(1, 0, 2)
+        in_hash = C.input_hash(logits, g, budget, docs)
+    else:
+        delta, budget = C.delta_budget_inputs(case)
+        centres = None
+        in_hash = C.input_hash(delta, budget, docs)
+    pi = np.full((1, H, T, M), 1.0 / M, dtype=np.float32)
+    sb = make_sb(SpectralBias, case, H)
+    gumbel_g = None
+    if case.get("gumbel_k", 0):
+        gen = torch.Generator(device="cpu")
+        gen.manual_seed(int(case.get("gumbel_seed", 0)))
+        u = torch.rand((H, QB, M), generator=gen, dtype=torch.float32)
+        gumbel_g = (-torch.log(-torch.log(u + 1e-9) + 1e-9)).numpy()
+    bm = sb.build_pointer_blockmask(docs=torch.from_numpy(docs), delta_star=torch.from_numpy(delta),
+                                    pi=torch.from_numpy(pi), budget_logits=torch.from_numpy(budget),
+                                    block_size=bs)
+    kv_num = bm.kv_num_blocks[0].numpy()
+    kv_idx = bm.kv_indices[0].numpy()
+    q_num = bm.q_num_blocks[0].numpy()
+    q_idx = bm.q_indices[0].numpy()
+    # representatives as the reference forms them (model/attn_bias.py:714-719)
+    dt = torch.from_numpy(delta)[0]
+    bt = torch.from_numpy(budget)[0]
+    if case.get("rep", "last") == "last":
+        delta_rep = dt[:, torch.from_numpy(t_rep)].numpy()
+        budget_rep = bt[:, torch.from_numpy(t_rep)].numpy()
+    else:
+        delta_rep = dt.reshape(H, QB, bs, M).mean(dim=2).numpy()
+        budget_rep = bt.reshape(H, QB, bs, M).mean(dim=2).numpy()
+    out = dict(in_hash=np.array(in_hash), kv_num=kv_num, q_num=q_num,
+               kv_indices_hash=np.array(C.arr_hash(kv_idx)), q_indices_hash=np.array(C.arr_hash(q_idx)))
+    if gumbel_g is not None:
+        out["gumbel_g"] = gumbel_g
+    if not case.get("large"):
+        out["delta_rep"] = delta_rep.astype(np.float32)
+        out["budget_rep"] = budget_rep.astype(np.float32)
+        if kv_idx.size <= SMALL:
+            out["kv_indices"] = kv_idx
+            out["q_indices"] = q_idx
+        else:
+            max_kv = case["local"] + (M * (2 * case["half"] + 1) if case["half"] > 0 else M) + min(case["glob"], QB)
+            w = min(max_kv, QB)
+            out["kv_indices_prefix"] = kv_idx[..., :w]
+    np.savez_compressed(os.path.join(HERE, f"mask_{name}.npz"), **out)
+    print(f"mask {name}: QB={QB} sum(kv_num)={int(kv_num.sum())}")
+
+
+def scalar_score_mod(cc, cs, cos_wD, sin_wD, b0, slope, dm, wd, *, K, beta, gate, lam, tau):
+    """Scalar-index form of the score_mod closure of scoped_medium.py:425-457
+    (per-frequency accumulation in the same order)."""
+    def score_mod(score, b, h, q_idx, kv_idx):
+        delta = torch.clamp(q_idx - kv_idx, min=0)
+        bias = torch.zeros_like(score)
+        for kk in range(K):
+            bias = bias + cc[b, h, q_idx, kk] * cos_wD[kk, delta] + cs[b, h, q_idx, kk] * sin_wD[kk, delta]
+        df = delta.to(torch.float32)
+        if b0 is not None:
+            bias = bias - b0[b, h, q_idx]
+        if slope is not None:
+            bias = bias + slope[b, h, q_idx] * df
+        if gate != "none" and lam > 0:
+            x = ((df - dm[b, h, q_idx]).abs() - wd[b, h, q_idx]) / tau
+            if gate == "relu":
+                bias = bias - lam * torch.relu(x)
+            else:
+                bias = bias - lam * torch.nn.functional.softplus(x)
+        return score + beta * bias
+    return score_mod
+
+
+def run_attn_case(SpectralBias, name, case):
+    from torch.nn.attention.flex_attention import flex_attention
+    H, T, bs, K = case["H"], case["T"], case["bs"], case["K"]
+    QB = T // bs
+    x = C.attn_inputs(case)
+    docs = torch.from_numpy(C.attn_docs(case))
+    kn = C.attn_mask_knobs(case)
+    mcase = dict(H=H, T=T, bs=bs, M=kn["M"], local=kn["local"], half=kn["half"], glob=kn["glob"],
+                 budget=kn["budget"], total=kn["total"], temp=kn["temp"], mode="pi", seed=case["seed"])
+    sb = make_sb(SpectralBias, mcase, H)
+    g = torch.Generator().manual_seed(case["seed"] + 5)
+    delta = torch.rand(1, H, T, kn["M"], generator=g) * T * 0.8
+    budget = torch.randn(1, H, T, kn["M"], generator=g)
+    pi = torch.full((1, H, T, kn["M"]), 1.0 / kn["M"])
+    bm = sb.build_pointer_blockmask(docs=docs, delta_star=delta, pi=pi, budget_logits=budget, block_size=bs)
+    cos_wD, sin_wD = AO.trig_tables(x["omegas"], T)
+    scale, beta, lam, tau = 0.12, 0.5, 0.2, 64.0
+    fa = torch.compile(flex_attention, dynamic=False)
+    q, k, v = (x[n][None] for n in ("q", "k", "v"))
+    if case["impl"] == "score_mod":
+        sm = scalar_score_mod(x["coeff_cos"][None], x["coeff_sin"][None], cos_wD, sin_wD,
+                              x["b0"][None] if case["b0"] else None,
+                              x["slope"][None] if case["slope"] else None,
+                              x["delta_main"][None], x["width"][None], K=K, beta=beta,
+                              gate=case["gate"], lam=lam, tau=tau)
+        out = fa(q, k, v, block_mask=bm, score_mod=sm, scale=scale)
+    else:
+        qa, ka, va = AO.qk_aug_inputs(x["q"], x["k"], x["v"], x["coeff_cos"], x["coeff_sin"], cos_wD, sin_wD,
+                                      beta=beta, scale=scale, slope=x["slope"] if case["slope"] else None)
+        out = fa(qa[None], ka[None], va[None], block_mask=bm, scale=scale)
+        out = out[..., :64]
+    rows = np.linspace(0, T - 1, C.ATTN_ROWS).astype(np.int64)
+    np.savez_compressed(os.path.join(HERE, f"attn_{name}.npz"),
+                        out_rows=out[0][:, rows].float().numpy(), rows=rows,
+                        kv_num=bm.kv_num_blocks[0].numpy(), kv_indices=bm.kv_indices[0].numpy(),
+                        delta_rep=delta[0][:, (torch.arange(QB) + 1) * bs - 1].numpy(),
+                        budget_rep=budget[0][:, (torch.arange(QB) + 1) * bs - 1].numpy(),
+                        in_hash=np.array(C.input_hash(*(x[n].numpy() for n in sorted(x)))))
+    print(f"attn {name}: done")
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--reference", required=True, help="path of the onetensor/scope checkout")
+    ap.add_argument("--only", default="")
+    a = ap.parse_args()
+    sys.path.insert(0, a.reference)
+    from model.attn_bias import SpectralBias
+    torch.set_num_threads(os.cpu_count() or 1)
+    for name, case in C.MASK_CASES.items():
+        if a.only and a.only not in name:
+            continue
+        run_mask_case(SpectralBias, name, case)
+    for name, case in C.ATTN_CASES.items():
+        if a.only and a.only not in name:
+            continue
+        run_attn_case(SpectralBias, name, case)
+
+
+if __name__ == "__main__":
+    main()
