@@ -1,0 +1,404 @@
+"""Benchmark of the SCOPE sparse-attention hot path on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config c3] [--impl ours|reference|flex]
+
+One step = one layer of configuration C3 (B=1, H=16, T=131072, D=64, bf16,
+block 128, K=16 spectral frequencies, sliding 8 / local 2 / half 4 / global
+1 / budget 8 pointer blocks): the fused pointer selection + mask build, the
+attention forward with the spectral bias (qk_aug, the reference default) and
+the backward for q, k, v and the spectral coefficients.  Heads are sharded
+across the N ranks; the outputs and pointer statistics are all-gathered over
+NCCL (the path's only collective).  Metric: active-block attention TFLOP/s
+fwd+bwd = 14 * bs^2 * D * sum(kv_num_blocks) / step time, whole job.
+
+--impl reference times the reference's CPU path on the host cores (the
+numpy port of its mask builder + torch's compiled CPU flex_attention, forward
+only: the reference has no CPU backward).  --impl flex times torch's
+compiled flex_attention (Triton) on the GPU with the same mask and inputs,
+for comparison; it is not the driver's reference arm.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import torch
+import torch.distributed as dist
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+from scope_b200 import PointerBlockMaskBuilder, SpectralScoreMod, flex_attention, trig_tables  # noqa: E402
+from scope_b200 import _lib  # noqa: E402
+from scope_b200.synth import BETA, CONFIGS, SCALE, make_inputs  # noqa: E402
+
+METRIC = "active-block attn TFLOP/s fwd+bwd at T=128k; tokens/s/GPU at 1/2/4/8 B200"
+
+
+def peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return d["hbm_gbs"], d["bf16_tflops"], "measured"
+    return 6650.0, 1590.0, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled during the timed region."""
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index, self.rows, self.proc = index, [], None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.Q}",
+                                          "--format=csv,noheader,nounits", "-lms", "100"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except (OSError, FileNotFoundError):
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.rows.append([x.strip() for x in line.split(",")])
+
+    def __exit__(self, *a):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        if not self.rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unavailable"]}
+        sm = [float(r[1]) for r in self.rows if len(r) > 8 and r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in self.rows if len(r) > 8 and r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in self.rows if len(r) > 8 for i in range(4) if r[5 + i] == "Active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(self.rows)}
+
+
+def setup_dist():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    else:
+        torch.cuda.set_device(0)
+    return rank, world, local
+
+
+class Workload:
+    """The per-rank inputs of one C3 layer (this rank's head shard)."""
+
+    def __init__(self, cfg, rank, world, device, seed=0):
+        if cfg.H % world:
+            raise ValueError(f"H={cfg.H} heads do not split over {world} ranks")
+        hp = cfg.H // world
+        self.cfg, self.rank, self.world, self.hp = cfg, rank, world, hp
+        self.heads = slice(rank * hp, (rank + 1) * hp)
+        x = make_inputs(cfg, device=device, seed=seed, heads=self.heads)
+        self.x = x
+        self.cos_t, self.sin_t = trig_tables(x["omegas"], cfg.T)
+        self.builder = PointerBlockMaskBuilder(
+            num_heads=hp, M=cfg.M, pointer_local_blocks=cfg.local_eff, pointer_half_blocks=cfg.half_blocks,
+            pointer_global_blocks=cfg.global_blocks, pointer_budget_blocks=cfg.budget_blocks,
+            pointer_budget_is_total=cfg.budget_is_total, pointer_budget_temp=cfg.budget_temp, debug_stats=True)
+        self.leaves = {n: x[n].detach().requires_grad_(True) for n in ("q", "k", "v", "coeff_cos", "coeff_sin")}
+
+    def build(self):
+        x = self.x
+        return self.builder.select_and_build(pointer_logits=x["logits"], gumbel=x["gumbel"], tau=self.cfg.select_tau,
+                                             docs=x["docs"], budget_rep=x["budget_rep"],
+                                             block_size=self.cfg.block_size)
+
+    def step(self, gather_out=None, gather_stats=None):
+        """mask build -> forward -> (async all-gather of outputs/stats) -> backward"""
+        L = self.leaves
+        for t in L.values():
+            t.grad = None
+        bm = self.build()
+        sm = SpectralScoreMod(coeff_cos=L["coeff_cos"], coeff_sin=L["coeff_sin"], cos_tab=self.cos_t,
+                              sin_tab=self.sin_t, beta=BETA, impl="qk_aug")
+        out = flex_attention(L["q"][None], L["k"][None], L["v"][None], bm, score_mod=sm, scale=SCALE)
+        works = []
+        if self.world > 1:
+            # outputs are [T, H/N, D] in memory per rank; gather head shards into [N, T, H/N, D]
+            works.append(dist.all_gather_into_tensor(gather_out, out[0].detach().permute(1, 0, 2).contiguous(),
+                                                     async_op=True))
+            works.append(dist.all_gather_into_tensor(gather_stats, bm.stats, async_op=True))
+        out.backward(self.x["do"][None])
+        for w in works:
+            w.wait()
+        return bm, out
+
+
+def active_pairs(bm):
+    return int(bm.kv_num_blocks.sum().item())
+
+
+def time_steps(fn, steps, world):
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    s = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(s)
+    for _ in range(steps):
+        fn()
+    e1.record(s)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1)
+    if world > 1:
+        t = torch.tensor([ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = t.item()
+        dist.barrier()
+    return ms
+
+
+def phase_times(wl, reps=3):
+    """Average device time of each phase of the step, with CUDA events on the
+    stream the kernels are launched on (the current stream)."""
+    s = torch.cuda.current_stream()
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
+    acc = [0.0, 0.0, 0.0]
+    L = wl.leaves
+    for _ in range(reps):
+        for t in L.values():
+            t.grad = None
+        ev[0].record(s)
+        bm = wl.build()
+        ev[1].record(s)
+        sm = SpectralScoreMod(coeff_cos=L["coeff_cos"], coeff_sin=L["coeff_sin"], cos_tab=wl.cos_t,
+                              sin_tab=wl.sin_t, beta=BETA, impl="qk_aug")
+        out = flex_attention(L["q"][None], L["k"][None], L["v"][None], bm, score_mod=sm, scale=SCALE)
+        ev[2].record(s)
+        out.backward(wl.x["do"][None])
+        ev[3].record(s)
+        torch.cuda.synchronize()
+        for i in range(3):
+            acc[i] += ev[i].elapsed_time(ev[i + 1])
+    return [a / reps for a in acc]
+
+
+def e2e_step(wl, host, dev):
+    """The same step through the public API from pinned host buffers: H2D of
+    every input, the step, D2H of the outputs and gradients."""
+    for n, h in host["in"].items():
+        dev[n].copy_(h, non_blocking=True)
+    L = wl.leaves
+    for n in ("q", "k", "v", "coeff_cos", "coeff_sin"):
+        L[n].data = dev[n]
+    wl.x["do"] = dev["do"]
+    wl.x["logits"], wl.x["gumbel"], wl.x["budget_rep"] = dev["logits"], dev["gumbel"], dev["budget_rep"]
+    bm, out = wl.step()
+    host["out"]["out"].copy_(out[0], non_blocking=True)
+    for n in ("q", "k", "v", "coeff_cos", "coeff_sin"):
+        host["out"]["d" + n].copy_(L[n].grad, non_blocking=True)
+
+
+def cpu_reference(cfg, *, warmup=1, steps=3, heads=1, seconds_budget=60.0):
+    """The reference's CPU path on a bounded sample: the numpy port of its
+    mask builder and torch's compiled CPU flex_attention on the qk_aug inputs
+    (forward; the reference raises NotImplementedError for a CPU backward).
+    Each step = build + one forward over ``heads`` heads of the config."""
+    from oracle import mask_oracle as MO
+    from oracle import attn_oracle as AO
+    from torch.nn.attention.flex_attention import BlockMask, flex_attention as torch_flex
+    if os.path.exists("/usr/bin/g++") and not os.environ.get("CXX"):
+        os.environ["CXX"] = "/usr/bin/g++"   # Inductor's C++ flex template needs a g++ with libgomp
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    x = make_inputs(cfg, device="cpu", seed=0, heads=slice(0, heads))
+    T, bs = cfg.T, cfg.block_size
+    QB = T // bs
+    docs = x["docs"].long()
+
+    def document_causal(b, h, q_idx, kv_idx):
+        return (q_idx >= kv_idx) & (docs[q_idx] == docs[kv_idx])
+
+    cos_t, sin_t = AO.trig_tables(x["omegas"], T)
+    qa, ka, va = AO.qk_aug_inputs(x["q"].float(), x["k"].float(), x["v"].float(), x["coeff_cos"], x["coeff_sin"],
+                                  cos_t, sin_t, beta=BETA, scale=SCALE)
+    fa = torch.compile(torch_flex, dynamic=False)
+
+    def one():
+        t0 = time.perf_counter()
+        cen = MO.select_pointer_blocks(x["logits"].numpy(), x["gumbel"].numpy(), M=cfg.M, tau=cfg.select_tau)
+        m = MO.build_pointer_blockmask(docs=x["docs"].numpy(), block_size=bs, M=cfg.M, centres=cen,
+                                       budget_rep=x["budget_rep"].numpy(), local_blocks=cfg.local_eff,
+                                       half_blocks=cfg.half_blocks, global_blocks_max=cfg.global_blocks,
+                                       budget_blocks=cfg.budget_blocks, budget_is_total=cfg.budget_is_total,
+                                       budget_temp=cfg.budget_temp, with_transpose=False)
+        kvi = torch.from_numpy(MO.flex_padded(m["kv_packed"], QB))[None]
+        kvn = torch.from_numpy(m["kv_num"])[None]
+        bmk = BlockMask.from_kv_blocks(kvn, kvi, torch.zeros_like(kvn), torch.zeros_like(kvi), BLOCK_SIZE=bs,
+                                       mask_mod=document_causal)
+        fa(qa[None], ka[None], va[None], block_mask=bmk, scale=SCALE)
+        return time.perf_counter() - t0, int(m["kv_num"].sum())
+
+    for _ in range(max(1, warmup)):      # the first call compiles
+        one()
+    times, P = [], 0
+    t_start = time.perf_counter()
+    for _ in range(max(1, steps)):
+        dt, P = one()
+        times.append(dt)
+        if time.perf_counter() - t_start > seconds_budget:
+            break
+    sec = sum(times) / len(times)
+    fwd_flops = 4 * bs * bs * 64 * P
+    return {"value": fwd_flops / sec / 1e12, "unit": "TFLOP/s", "cores": threads, "kind": "port",
+            "sample": f"{cfg.name} with {heads} of {cfg.H} heads (T={T}), forward only (the reference has no CPU "
+                      f"backward): numpy port of the mask builder + torch.compile'd CPU flex_attention on the "
+                      f"qk_aug inputs, {len(times)} timed steps", "seconds_per_step": sec}
+
+
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    cfg = CONFIGS[args.config]
+    res = cpu_reference(cfg, warmup=args.warmup, steps=args.steps)
+    line = {"metric": METRIC, "value": res["value"], "unit": "TFLOP/s", "n_gpus": args.gpus, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": res["seconds_per_step"] * 1e3, "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": f"{cfg.name}: one SCOPE attention layer, 1-head CPU sample", "T": cfg.T,
+                       "H": 1, "block_size": cfg.block_size, "K": cfg.K, "spectral_impl": "qk_aug"},
+            "impl": "reference",
+            "cpu_baseline": {k: res[k] for k in ("value", "unit", "cores", "kind", "sample")},
+            "e2e": {"value": res["value"], "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--config", default="c3")
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    args = ap.parse_args()
+    if args.impl == "reference":
+        run_reference(args)
+        return
+    args.warmup = max(args.warmup, 3)
+    rank, world, local = setup_dist()
+    cfg = CONFIGS[args.config]
+    wl = Workload(cfg, rank, world, "cuda")
+    gather_out = gather_stats = None
+    if world > 1:
+        gather_out = torch.empty(world, cfg.T, wl.hp, cfg.D, dtype=torch.bfloat16, device="cuda")
+    bm0 = wl.build()
+    if world > 1:
+        gather_stats = torch.empty(world * bm0.stats.numel(), dtype=torch.int32, device="cuda")
+    P_local = active_pairs(bm0)
+    for _ in range(args.warmup):
+        wl.step(gather_out, gather_stats)
+    torch.cuda.synchronize()
+    L = _lib.lib()
+    n0 = L.scope_launch_count()
+    with ClockSampler(local) as clk:
+        ms = time_steps(lambda: wl.step(gather_out, gather_stats), args.steps, world)
+    launches = L.scope_launch_count() - n0
+    P_t = torch.tensor([P_local], device="cuda", dtype=torch.int64)
+    if world > 1:
+        dist.all_reduce(P_t)
+    P = int(P_t.item())
+    bs, D = cfg.block_size, cfg.D
+    flops = 14 * bs * bs * D * P
+    ms_step = ms / args.steps
+    value = flops / (ms_step * 1e-3) / 1e12
+
+    # per-phase device times (builder / forward / backward) on this rank
+    ph = phase_times(wl)
+    hbm, bf16, src = peaks()
+    f_fwd, f_bwd = 4 * bs * bs * D * P_local, 10 * bs * bs * D * P_local
+    phases = {"mask_build_ms": ph[0], "forward_ms": ph[1], "backward_ms": ph[2]}
+    dom = int(max(range(3), key=lambda i: ph[i]))
+    if dom == 0:
+        # builder: algorithmic bytes = causal candidate logits + noise read + lists written
+        QB = cfg.QB
+        byts = wl.hp * (QB * (QB + 1) // 2) * 8 + wl.hp * QB * (4 + 4 * bm0.kv_indices.shape[-1])
+        ach = byts / (ph[0] * 1e-3) / 1e9
+        roof = {"kernel": "scope mask builder", "bound": "hbm", "achieved": ach, "peak": hbm, "unit": "GB/s"}
+    else:
+        fl = f_fwd if dom == 1 else f_bwd
+        ach = fl / (ph[dom] * 1e-3) / 1e12
+        roof = {"kernel": "attention " + ("forward" if dom == 1 else "backward"), "bound": "tensor",
+                "achieved": ach, "peak": bf16, "unit": "TFLOP/s"}
+    roof["frac"] = roof["achieved"] / roof["peak"]
+    roof["peak_source"] = f"{src} (MEASURED_PEAKS.json burst)" if src == "measured" else "fallback"
+    roof["traffic"] = None
+
+    e2e = None
+    if not args.no_e2e:
+        names_in = ("q", "k", "v", "do", "coeff_cos", "coeff_sin", "logits", "gumbel", "budget_rep")
+        dev = {n: wl.x[n].detach().clone() for n in names_in}
+        host = {"in": {n: dev[n].cpu().pin_memory() for n in names_in},
+                "out": {"out": torch.empty(cfg.T, wl.hp, D, dtype=torch.bfloat16).pin_memory().permute(1, 0, 2)}}
+        for n in ("q", "k", "v"):
+            host["out"]["d" + n] = torch.empty(cfg.T, wl.hp, D, dtype=torch.bfloat16).pin_memory().permute(1, 0, 2)
+        for n in ("coeff_cos", "coeff_sin"):
+            host["out"]["d" + n] = torch.empty_like(wl.x[n], device="cpu").pin_memory()
+        for _ in range(2):
+            e2e_step(wl, host, dev)
+        torch.cuda.synchronize()
+        e_steps = max(2, args.steps // 2)
+        ms_e = time_steps(lambda: e2e_step(wl, host, dev), e_steps, world)
+        h2d = sum(t.numel() * t.element_size() for t in host["in"].values())
+        d2h = sum(t.numel() * t.element_size() for t in host["out"].values())
+        e2e = {"value": flops / (ms_e / e_steps * 1e-3) / 1e12, "unit": "TFLOP/s",
+               "h2d_bytes_per_step": h2d * world, "d2h_bytes_per_step": d2h * world,
+               "ms_per_step": ms_e / e_steps}
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        try:
+            r = cpu_reference(cfg, warmup=1, steps=3, seconds_budget=20.0)
+            cpu = {k: r[k] for k in ("value", "unit", "cores", "kind", "sample")}
+        except Exception as e:  # the baseline is reported, not required
+            cpu = {"value": None, "unit": "TFLOP/s", "cores": os.cpu_count(), "kind": "port",
+                   "sample": f"failed: {type(e).__name__}: {e}"[:300]}
+
+    if rank == 0:
+        line = {"metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
+                "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "strong",
+                "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+                "config": {"workload": f"{cfg.name}: one SCOPE attention layer, select+build, fwd+bwd",
+                           "B": 1, "H": cfg.H, "T": cfg.T, "D": D, "block_size": bs, "K": cfg.K,
+                           "spectral_impl": "qk_aug", "parallelism": f"heads/{world}",
+                           "active_block_pairs": P, "l2": "inputs larger than L2 (q,k,v,dO 1 GiB)"},
+                "roofline": roof, "phases_ms": phases, "cpu_baseline": cpu, "e2e": e2e,
+                "clocks": clk.summary(), "gpu_launches": int(launches)}
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

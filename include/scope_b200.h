@@ -1,0 +1,223 @@
+/*
+ * scope_b200 -- C ABI of the B200 (sm_100a) SCOPE sparse-attention hot path.
+ *
+ * Three parts, each replacing one piece of the reference (onetensor/scope):
+ *   1. the pointer block-mask builder       <- SpectralBias.build_pointer_blockmask
+ *                                              (model/attn_bias.py:623-874)
+ *   2. the spectral bias inside the tile    <- the score_mod closure / qk_aug
+ *                                              augmentation (scoped_medium.py:380-457)
+ *   3. block-sparse causal attention fwd/bwd <- flex_attention(q, k, v, block_mask=,
+ *                                              score_mod=, scale=) (scoped_medium.py:459-476)
+ *
+ * Conventions
+ *   - Every pointer is a device pointer; every call takes the caller's stream
+ *     and launches only on it.  No call synchronises the host.
+ *   - The library allocates no device memory.  Buffers (including the
+ *     workspace whose size scope_workspace_bytes() returns) belong to the caller.
+ *   - Strides are in elements.  The last dimension of q/k/v/out/dO/dq/dk/dv
+ *     is contiguous; head and token strides are free, so the [B,H,T,D] views
+ *     of [B,T,H,D] tensors that the reference passes work unchanged.
+ *   - Return value: SCOPE_OK (0) or a negative scope_status; scope_error_string()
+ *     names it.  Kernels that find a bad index or give up a bounded wait set
+ *     bits in the optional `err_flag` word (read it after the stream drains).
+ */
+#ifndef SCOPE_B200_H
+#define SCOPE_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct CUstream_st *scope_stream_t; /* == cudaStream_t */
+
+typedef enum scope_status {
+    SCOPE_OK = 0,
+    SCOPE_ERR_INVALID = -1,     /* bad shape, size or knob (ValueError on the Python side) */
+    SCOPE_ERR_DTYPE = -2,       /* unsupported dtype combination */
+    SCOPE_ERR_ALIGN = -3,       /* pointer or stride not aligned as required */
+    SCOPE_ERR_CUDA = -4,        /* a CUDA launch or runtime call failed */
+    SCOPE_ERR_UNSUPPORTED = -5, /* device is not sm_100 or configuration unsupported */
+    SCOPE_ERR_WORKSPACE = -6    /* workspace missing or too small */
+} scope_status;
+
+typedef enum scope_dtype { SCOPE_F32 = 0, SCOPE_BF16 = 1 } scope_dtype;
+
+typedef enum scope_bias_mode {
+    SCOPE_BIAS_NONE = 0,     /* plain block-sparse attention */
+    SCOPE_BIAS_SCORE_MOD = 1,/* exact score_mod semantics (scoped_medium.py:425-457) */
+    SCOPE_BIAS_QK_AUG = 2    /* qk_aug augmentation (scoped_medium.py:380-423), the reference default */
+} scope_bias_mode;
+
+typedef enum scope_gate { SCOPE_GATE_NONE = 0, SCOPE_GATE_SOFTPLUS = 1, SCOPE_GATE_RELU = 2 } scope_gate;
+
+/* device error-word bits */
+#define SCOPE_DEVERR_INDEX   0x1  /* a kv / q block index outside [0, QB) was skipped */
+#define SCOPE_DEVERR_TIMEOUT 0x2  /* a bounded pipeline wait gave up */
+#define SCOPE_DEVERR_SHAPE   0x4  /* a list longer than its buffer was truncated */
+
+/* ------------------------------------------------------------------------ */
+/* 1. pointer block-mask builder                                              */
+/* ------------------------------------------------------------------------ */
+
+/* Document / reset starts and document ranges per block.
+ * Replaces model/attn_bias.py:681-709 (doc_start_blk_ptr / doc_start_blk_local)
+ * and adds the per-block document min/max used to classify attention tiles.
+ * out: int32 [4, QB] = {doc_start_blk_ptr, doc_start_blk_local, doc_min, doc_max}.
+ * docs may be NULL (one document). */
+int scope_block_info(const int32_t *docs, int32_t T, int32_t block_size,
+                     int32_t doc_clamp, int32_t reset_active, int32_t reset_len,
+                     int32_t *out, scope_stream_t stream);
+
+typedef struct ScopeMaskArgs {
+    int32_t H, QB, M, block_size;
+    /* Pointer source, exactly one of:
+     *  (a) selection: Gumbel top-M over causal candidate blocks kb <= qb of
+     *      scores = sel_logits / sel_tau + sel_gumbel   (both [H,QB,>=QB] f32)
+     *  (b) delta_rep [H,QB,M] f32: the representative Δ* (model/attn_bias.py:714-719) */
+    const float *sel_logits, *sel_gumbel;
+    int64_t sel_head_stride, sel_row_stride;
+    float sel_tau;
+    const float *delta_rep;
+    int64_t delta_head_stride, delta_row_stride, delta_m_stride;
+    /* budget logits of each peak [H,QB,M] (model/attn_bias.py:716) */
+    const float *budget_rep;
+    int64_t budget_head_stride, budget_row_stride, budget_m_stride;
+    /* Gumbel peak masking (model/attn_bias.py:763-777): g [H,QB,M] contiguous, k, tau; NULL = off */
+    const float *peak_gumbel;
+    int32_t gumbel_k;
+    float gumbel_tau;
+    /* [4,QB] from scope_block_info */
+    const int32_t *block_info;
+    /* knobs, already resolved as the reference resolves them */
+    int32_t local_blocks;  /* min(max(1, L), QB) */
+    int32_t half_blocks;   /* max(0, ptr_half_blocks) */
+    int32_t half_active;   /* schedule cap (_pointer_half_blocks_active) */
+    int32_t ptr_enabled;   /* _pointer_mask_active */
+    int32_t global_max;    /* min(pointer_global_blocks, QB) */
+    int32_t global_active; /* clamp(active global blocks, 0, global_max) */
+    int32_t radius_mode;   /* 0 = "fixed", 1 = "pi" */
+    int32_t budget_rem;    /* integer radius budget (model/attn_bias.py:724-734) */
+    float budget_temp;     /* max(pointer_budget_temp, 1e-6) */
+    /* outputs */
+    int32_t *kv_num;       /* [H,QB] */
+    int32_t *kv_indices;   /* [H,QB,kv_stride] */
+    int32_t kv_stride;     /* >= max_kv (compact) or == QB with flex_padded */
+    int32_t flex_padded;   /* 1: the reference's QB-column layout (model/attn_bias.py:854-862) */
+    uint32_t *q_bitmap;    /* optional [H,QB,ceil(QB/32)]: bit qb of row (h,kb) = kb visible from qb */
+    int32_t *r_m_out;      /* optional [H,QB,M] radii */
+    int32_t *centres_out;  /* optional [H,QB,M] pointer centres */
+    int32_t *stats;        /* optional: kv_unique_hist[max_kv+1] | radius_hist[half+1] |
+                              extra_sum_hist[max(1,half*M)+1] | zero-radius count (int32, accumulated) */
+    int32_t *err_flag;     /* optional device error word */
+} ScopeMaskArgs;
+
+/* Number of list entries before de-duplication: L + M*(2p+1) + G (p > 0) or L + M + G. */
+int32_t scope_mask_max_kv(int32_t local_blocks, int32_t M, int32_t half_blocks, int32_t global_max);
+
+/* Builds the pointer block mask.  Replaces SpectralBias.build_pointer_blockmask
+ * (model/attn_bias.py:623-874) minus BlockMask.from_kv_blocks' dense transpose,
+ * which the q_bitmap replaces.  The caller zeroes q_bitmap and stats. */
+int scope_mask_build(const ScopeMaskArgs *args, scope_stream_t stream);
+
+/* torch BlockMask q-side layout from the bitmap: q_num [H,KB], q_indices [H,KB,QB]
+ * (valid q-blocks ascending, then the rest ascending) -- what
+ * BlockMask.from_kv_blocks -> _transpose_ordered produces
+ * (torch/nn/attention/flex_attention.py:412-415).  q_indices may be NULL. */
+int scope_mask_transpose(const uint32_t *q_bitmap, int32_t H, int32_t QB,
+                         int32_t *q_num, int32_t *q_indices, scope_stream_t stream);
+
+/* ------------------------------------------------------------------------ */
+/* 2. spectral bias helpers                                                   */
+/* ------------------------------------------------------------------------ */
+
+/* bf16 trig tables cos/sin(fp32(w_k*d)), d in [0,L)  (model/attn_bias.py:326-340).
+ * omegas [K] f32; cos_out/sin_out [K,L] bf16 (raw 16-bit). */
+int scope_trig_tables(const float *omegas, int32_t K, int32_t L,
+                      uint16_t *cos_out, uint16_t *sin_out, scope_stream_t stream);
+
+/* Augmented dims of the qk_aug mode (scoped_medium.py:380-421):
+ *   q_aug[h,t] = s*[A*cos_t + B*sin_t, A*sin_t - B*cos_t, (-slope)], zero padded to d_aug,
+ *   k_aug[t]   = s*[cos_t, sin_t, (t)], zero padded,  s = sqrt(beta/scale),
+ * rounded to `dtype`.  coeff [H,T,K] f32 contiguous; slope [H,T] or NULL;
+ * q_aug [H,T,d_aug]; k_aug [T,d_aug] (head independent). */
+int scope_qk_aug_prepare(const float *coeff_cos, const float *coeff_sin, const float *slope,
+                         const uint16_t *cos_tab, const uint16_t *sin_tab, int32_t tab_len,
+                         int32_t H, int32_t T, int32_t K, int32_t d_aug, float beta, float scale,
+                         int32_t dtype, void *q_aug, void *k_aug, scope_stream_t stream);
+
+/* ------------------------------------------------------------------------ */
+/* 3. block-sparse attention                                                  */
+/* ------------------------------------------------------------------------ */
+
+typedef struct ScopeAttnArgs {
+    int32_t H, T, D, block_size;     /* D == 64; block_size == 128 (or 64/256 on the CUDA-core path) */
+    int32_t dtype;                    /* scope_dtype of q,k,v,out,dout,dq,dk,dv */
+    const void *q, *k, *v;
+    int64_t q_sh, q_st, k_sh, k_st, v_sh, v_st;   /* head / token strides */
+    void *out;
+    int64_t o_sh, o_st;
+    float *lse;                       /* [H,T] natural-log logsumexp (written by fwd, read by bwd) */
+    /* block mask (kv side for fwd/dQ, q side for dK/dV) */
+    const int32_t *kv_num;            /* [H,QB] */
+    const int32_t *kv_indices;        /* [H,QB,kv_stride] */
+    int32_t kv_stride;
+    const uint32_t *q_bitmap;         /* [H,QB,ceil(QB/32)] (backward) */
+    const int32_t *block_info;        /* [4,QB] (rows 2,3: doc min/max) or NULL */
+    const int32_t *docs;              /* [T] document ids or NULL (causal only) */
+    float scale;
+    /* spectral bias */
+    int32_t bias_mode;                /* scope_bias_mode */
+    int32_t K;
+    const float *coeff_cos, *coeff_sin;           /* [H,T,K] */
+    const uint16_t *cos_tab, *sin_tab;            /* [K,tab_len] bf16 */
+    int32_t tab_len;
+    const float *b0, *slope, *delta_main, *width; /* [H,T] each or NULL */
+    int32_t gate;                     /* scope_gate */
+    float beta, gate_lambda, gate_tau;
+    const void *q_aug, *k_aug;        /* qk_aug: from scope_qk_aug_prepare */
+    int32_t d_aug;                    /* multiple of 16 (0 when bias_mode != QK_AUG) */
+    /* backward only */
+    const void *dout;
+    int64_t do_sh, do_st;
+    void *dq, *dk, *dv;
+    int64_t dq_sh, dq_st, dk_sh, dk_st, dv_sh, dv_st;
+    float *dcoeff_cos, *dcoeff_sin;   /* [H,T,K] or NULL */
+    float *db0, *dslope, *ddelta_main, *dwidth; /* [H,T] or NULL */
+    void *workspace;
+    size_t workspace_bytes;
+    int32_t *err_flag;                /* optional device error word */
+} ScopeAttnArgs;
+
+/* Forward: out and lse.  Replaces the flex_attention forward at
+ * scoped_medium.py:459-466 (score_mod) and :422 (qk_aug). */
+int scope_attn_fwd(const ScopeAttnArgs *args, scope_stream_t stream);
+
+/* Backward: dq, dk, dv and the gradients of the captured bias tensors
+ * (dcoeff_cos/dcoeff_sin, db0, dslope, ddelta_main, dwidth when given).
+ * Replaces flex_attention's autograd backward (scoped_medium.py:2520). */
+int scope_attn_bwd(const ScopeAttnArgs *args, scope_stream_t stream);
+
+/* Workspace bytes scope_attn_bwd needs for these arguments. */
+size_t scope_workspace_bytes(const ScopeAttnArgs *args);
+
+/* Name of a scope_status value. */
+const char *scope_error_string(int status);
+
+/* Struct layout self-check for bindings: which = 0 (ScopeMaskArgs) or 1
+ * (ScopeAttnArgs); what = 0 (sizeof) or 1 (offset of the last field, err_flag). */
+size_t scope_abi_layout(int which, int what);
+
+/* Number of kernels this library has launched in this process (all devices).
+ * Host-side counter used by benchmarks to report their kernel launches. */
+uint64_t scope_launch_count(void);
+
+/* 1 if the current device can run the tensor-core (sm_100a) kernels. */
+int scope_device_supported(void);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* SCOPE_B200_H */

@@ -1,0 +1,24 @@
+"""scope_b200: the SCOPE sparse-attention hot path, B200-native (sm_100a).
+
+Replaces, behind the reference's own interfaces:
+  * SpectralBias.build_pointer_blockmask  -> PointerBlockMaskBuilder / build_mask
+  * the spectral score_mod / qk_aug bias   -> SpectralScoreMod (evaluated in-kernel)
+  * flex_attention(q, k, v, block_mask, score_mod, scale) -> flex_attention
+Every op runs hand-written CUDA through the C ABI of libscope_b200.so
+(include/scope_b200.h); there is no CPU fallback.
+"""
+from . import _lib
+from .attention import SpectralScoreMod, aug_dims, flex_attention, trig_tables
+from .mask import PointerBlockMaskBuilder, ScopeBlockMask, block_info, build_mask
+
+__all__ = [
+    "PointerBlockMaskBuilder", "ScopeBlockMask", "SpectralScoreMod", "aug_dims", "block_info", "build_mask",
+    "flex_attention", "trig_tables", "load_library",
+]
+
+
+def load_library():
+    """Load libscope_b200.so and check the C struct layouts against ctypes."""
+    _lib.lib()
+    _lib.check_abi()
+    return _lib.lib()

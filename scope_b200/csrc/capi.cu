@@ -1,0 +1,116 @@
+// extern "C" attention entry points: argument validation and dispatch.
+//
+// bf16 inputs with the qk_aug (or no) bias and 128-token blocks run on the
+// tcgen05 tensor-core kernels; float32 inputs and the exact score_mod
+// closure run on the CUDA-core kernels.  Nothing here falls back silently: a
+// combination neither path supports returns an error status.
+#include <atomic>
+#include <cmath>
+#include <cstddef>
+#include <cstring>
+
+#include "common.cuh"
+
+int scope_simt_fwd(const ScopeAttnArgs &a, cudaStream_t s);
+int scope_simt_bwd(const ScopeAttnArgs &a, cudaStream_t s);
+int scope_tc_fwd(const ScopeAttnArgs &a, cudaStream_t s);
+int scope_tc_bwd(const ScopeAttnArgs &a, cudaStream_t s);
+bool scope_tc_eligible(const ScopeAttnArgs &a, bool bwd);
+
+namespace {
+
+int validate(const ScopeAttnArgs &a, bool bwd) {
+    if (a.H <= 0 || a.T <= 0 || a.D != 64) return SCOPE_ERR_INVALID;
+    if (a.block_size != 64 && a.block_size != 128 && a.block_size != 256) return SCOPE_ERR_INVALID;
+    if (a.T % a.block_size != 0) return SCOPE_ERR_INVALID;
+    if (a.dtype != SCOPE_F32 && a.dtype != SCOPE_BF16) return SCOPE_ERR_DTYPE;
+    if (!a.q || !a.k || !a.v || !a.out || !a.kv_num || !a.kv_indices || a.kv_stride < 1) return SCOPE_ERR_INVALID;
+    if (!(a.scale > 0.f) || !std::isfinite(a.scale)) return SCOPE_ERR_INVALID;
+    switch (a.bias_mode) {
+        case SCOPE_BIAS_NONE:
+            if (a.d_aug != 0) return SCOPE_ERR_INVALID;
+            break;
+        case SCOPE_BIAS_SCORE_MOD:
+            if (a.K < 1 || a.K > 16 || !a.coeff_cos || !a.coeff_sin || !a.cos_tab || !a.sin_tab) return SCOPE_ERR_INVALID;
+            if (a.tab_len < a.T || a.d_aug != 0) return SCOPE_ERR_INVALID;
+            if (a.gate != SCOPE_GATE_NONE && (!a.delta_main || !a.width || !(a.gate_tau != 0.f))) return SCOPE_ERR_INVALID;
+            if (a.gate < 0 || a.gate > 2) return SCOPE_ERR_INVALID;
+            break;
+        case SCOPE_BIAS_QK_AUG:
+            if (!a.q_aug || !a.k_aug || a.d_aug < 16 || a.d_aug > 64 || a.d_aug % 16) return SCOPE_ERR_INVALID;
+            if (bwd && (a.dcoeff_cos || a.dcoeff_sin) && (a.K < 1 || !a.cos_tab || !a.sin_tab || a.tab_len < a.T ||
+                                                          2 * a.K + (a.slope ? 1 : 0) > a.d_aug))
+                return SCOPE_ERR_INVALID;
+            break;
+        default:
+            return SCOPE_ERR_INVALID;
+    }
+    if (bwd) {
+        if (!a.dout || !a.dq || !a.dk || !a.dv || !a.lse || !a.q_bitmap) return SCOPE_ERR_INVALID;
+        if (!a.workspace || a.workspace_bytes < scope_workspace_bytes(&a)) return SCOPE_ERR_WORKSPACE;
+        if (reinterpret_cast<uintptr_t>(a.workspace) & 255) return SCOPE_ERR_ALIGN;
+    }
+    return SCOPE_OK;
+}
+
+}  // namespace
+
+extern "C" size_t scope_workspace_bytes(const ScopeAttnArgs *a) {
+    if (!a || a->H <= 0 || a->T <= 0) return 0;
+    // delta_i = rowsum(dO * O), float32 [H, T]
+    size_t b = (size_t)a->H * (size_t)a->T * sizeof(float);
+    return (b + 255) & ~(size_t)255;
+}
+
+extern "C" int scope_attn_fwd(const ScopeAttnArgs *args, scope_stream_t stream) {
+    if (!args) return SCOPE_ERR_INVALID;
+    int st = validate(*args, false);
+    if (st) return st;
+    cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    if (scope_tc_eligible(*args, false)) return scope_tc_fwd(*args, s);
+    if (args->block_size > 128) return SCOPE_ERR_UNSUPPORTED;
+    return scope_simt_fwd(*args, s);
+}
+
+extern "C" int scope_attn_bwd(const ScopeAttnArgs *args, scope_stream_t stream) {
+    if (!args) return SCOPE_ERR_INVALID;
+    int st = validate(*args, true);
+    if (st) return st;
+    cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    if (scope_tc_eligible(*args, true)) return scope_tc_bwd(*args, s);
+    if (args->block_size > 128) return SCOPE_ERR_UNSUPPORTED;
+    return scope_simt_bwd(*args, s);
+}
+
+extern "C" const char *scope_error_string(int status) {
+    switch (status) {
+        case SCOPE_OK: return "ok";
+        case SCOPE_ERR_INVALID: return "invalid argument";
+        case SCOPE_ERR_DTYPE: return "unsupported dtype";
+        case SCOPE_ERR_ALIGN: return "misaligned pointer or stride";
+        case SCOPE_ERR_CUDA: return "CUDA error";
+        case SCOPE_ERR_UNSUPPORTED: return "unsupported device or configuration";
+        case SCOPE_ERR_WORKSPACE: return "workspace missing or too small";
+        default: return "unknown status";
+    }
+}
+
+extern "C" size_t scope_abi_layout(int which, int what) {
+    // which: 0 ScopeMaskArgs, 1 ScopeAttnArgs; what: 0 sizeof, 1 offset of the last field
+    if (which == 0) return what == 0 ? sizeof(ScopeMaskArgs) : offsetof(ScopeMaskArgs, err_flag);
+    if (which == 1) return what == 0 ? sizeof(ScopeAttnArgs) : offsetof(ScopeAttnArgs, err_flag);
+    return 0;
+}
+
+static std::atomic<uint64_t> g_launches{0};
+void scope_note_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
+extern "C" uint64_t scope_launch_count(void) { return g_launches.load(std::memory_order_relaxed); }
+
+extern "C" int scope_device_supported(void) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return 0;
+    int major = 0, minor = 0;
+    cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev);
+    cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev);
+    return (major == 10 && minor == 0) ? 1 : 0;
+}

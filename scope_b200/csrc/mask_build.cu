@@ -1,0 +1,551 @@
+// Pointer block-mask builder for B200.
+//
+// Replaces SpectralBias.build_pointer_blockmask (model/attn_bias.py:623-874).
+// Design: one warp owns one (head, query block) row for the whole build --
+// pointer selection (a warp-wide Gumbel top-M over the causal candidates),
+// radius allocation, the union of local / pointer / global windows and the
+// de-duplicating pack all happen in registers and a per-warp shared-memory
+// list, so a row costs one pass over its candidate logits and nothing else
+// touches HBM.  The torch BlockMask's q-side transpose, which the reference
+// gets from a dense [H,QB,QB] matrix and an argsort
+// (torch/nn/attention/flex_attention.py:412-415), becomes one bit per
+// (kb, qb) pair set with atomicOr into a bitmap the backward walks directly.
+//
+// Float32 steps use explicitly rounded intrinsics in the reference's
+// operation order (no FMA contraction), so integer outputs are bit-identical
+// to the reference given the same inputs and noise.
+#include <algorithm>
+#include <climits>
+#include <cmath>
+
+#include "common.cuh"
+
+namespace scope {
+namespace mask {
+
+constexpr int kMaxM = 16;
+constexpr int kWarps = 8;
+
+// --------------------------------------------------------------------------
+// document / reset starts per block (model/attn_bias.py:681-709)
+// --------------------------------------------------------------------------
+// Pass 1, one warp per block: the last change point inside the block, whether
+// the block's first token is a change point, and the block's doc id range.
+__global__ void block_info_pass1(const int32_t *__restrict__ docs, int T, int bs, int QB,
+                                 int32_t *__restrict__ out) {
+    int b = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    int lane = threadIdx.x & 31;
+    if (b >= QB) return;
+    int base = b * bs;
+    int last = -1, mn = INT_MAX, mx = INT_MIN;
+    for (int i = lane; i < bs; i += 32) {
+        int t = base + i;
+        int d = docs ? docs[t] : 0;
+        bool chg = (t == 0) || (docs && docs[t] != docs[t - 1]);
+        if (chg) last = t;
+        mn = min(mn, d);
+        mx = max(mx, d);
+    }
+#pragma unroll
+    for (int o = 16; o; o >>= 1) {
+        last = max(last, __shfl_xor_sync(0xffffffffu, last, o));
+        mn = min(mn, __shfl_xor_sync(0xffffffffu, mn, o));
+        mx = max(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    }
+    if (lane == 0) {
+        bool first_chg = (base == 0) || (docs && docs[base] != docs[base - 1]);
+        out[b] = last;
+        out[QB + b] = first_chg ? base : -1;
+        out[2 * QB + b] = mn;
+        out[3 * QB + b] = mx;
+    }
+}
+
+// Pass 2, one CTA: running max of change points -> doc_start_token at the
+// representative (last) and first token of each block, then the clamps.
+__global__ void __launch_bounds__(1024) block_info_pass2(int QB, int bs, int doc_clamp, int reset_active,
+                                                        int reset_len, int32_t *__restrict__ out) {
+    __shared__ int warp_max[32];
+    const int tid = threadIdx.x, nt = blockDim.x;
+    const int per = (QB + nt - 1) / nt;
+    const int b0 = tid * per, b1 = min(QB, b0 + per);
+    int local = -1;
+    for (int b = b0; b < b1; ++b) local = max(local, out[b]);
+    // exclusive block-wide max-scan of the per-thread maxima
+    int lane = tid & 31, w = tid >> 5;
+    int incl = local;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        int y = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl = max(incl, y);
+    }
+    if (lane == 31) warp_max[w] = incl;
+    __syncthreads();
+    if (w == 0) {
+        int v = (lane < (nt >> 5)) ? warp_max[lane] : -1;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            int y = __shfl_up_sync(0xffffffffu, v, o);
+            if (lane >= o) v = max(v, y);
+        }
+        warp_max[lane] = v;
+    }
+    __syncthreads();
+    int excl = __shfl_up_sync(0xffffffffu, incl, 1);
+    if (lane == 0) excl = -1;
+    if (w > 0) excl = max(excl, warp_max[w - 1]);
+    int run = excl;
+    for (int b = b0; b < b1; ++b) {
+        int last = out[b], first = out[QB + b];
+        int dsl_tok = max(run, first);
+        run = max(run, last);
+        int dsp_tok = run;
+        int dsp = dsp_tok / bs, dsl = dsl_tok / bs;
+        if (!doc_clamp) dsp = dsl = 0;
+        if (reset_active && reset_len > 0) {
+            long long t_rep = (long long)(b + 1) * bs - 1;
+            long long st = (long long)b * bs;
+            dsp = max(dsp, (int)(((t_rep / reset_len) * reset_len) / bs));
+            dsl = max(dsl, (int)(((st / reset_len) * reset_len) / bs));
+        }
+        out[b] = dsp;
+        out[QB + b] = dsl;
+    }
+}
+
+// --------------------------------------------------------------------------
+// the per-row builder
+// --------------------------------------------------------------------------
+struct BuildParams {
+    ScopeMaskArgs a;
+    int max_kv;      // entries before de-duplication
+    int per_warp;    // ints of shared memory per warp
+    int n_stats;     // ints of the statistics block
+    int words;       // bitmap words per row
+};
+
+__device__ __forceinline__ bool better(float av, int ai, float bv, int bi) {
+    return av > bv || (av == bv && ai < bi);
+}
+
+// insert (s, kb) into a descending top-M list held in registers
+__device__ __forceinline__ void topm_insert(float (&v)[kMaxM], int (&id)[kMaxM], int M, float s, int kb) {
+    if (!better(s, kb, v[M - 1], id[M - 1])) return;
+    bool done = false;
+#pragma unroll
+    for (int j = kMaxM - 1; j >= 0; --j) {
+        if (j < M && !done) {
+            if (j > 0 && better(s, kb, v[j - 1], id[j - 1])) {
+                v[j] = v[j - 1];
+                id[j] = id[j - 1];
+            } else {
+                v[j] = s;
+                id[j] = kb;
+                done = true;
+            }
+        }
+    }
+}
+
+__device__ __forceinline__ void topm_pop(float (&v)[kMaxM], int (&id)[kMaxM], int M) {
+#pragma unroll
+    for (int j = 0; j < kMaxM - 1; ++j) {
+        if (j + 1 < M) {
+            v[j] = v[j + 1];
+            id[j] = id[j + 1];
+        }
+    }
+    v[M - 1] = -INFINITY;
+    id[M - 1] = INT_MAX;
+}
+
+// Gumbel top-M over candidates kb in [0, qb]; winners in descending score
+// order (ties to the lower block) go to cen[0..M); missing ones become qb.
+__device__ void select_row(const ScopeMaskArgs &a, int h, int qb, int lane, int *cen) {
+    const int M = a.M;
+    float v[kMaxM];
+    int id[kMaxM];
+#pragma unroll
+    for (int j = 0; j < kMaxM; ++j) {
+        v[j] = -INFINITY;
+        id[j] = INT_MAX;
+    }
+    const float *lrow = a.sel_logits + (int64_t)h * a.sel_head_stride + (int64_t)qb * a.sel_row_stride;
+    const float *grow = a.sel_gumbel + (int64_t)h * a.sel_head_stride + (int64_t)qb * a.sel_row_stride;
+    const float tau = a.sel_tau;
+    const int n = qb + 1;
+    const bool vec = (a.QB % 4 == 0) && (a.sel_row_stride % 4 == 0) && (a.sel_head_stride % 4 == 0) &&
+                     ((reinterpret_cast<uintptr_t>(a.sel_logits) & 15) == 0) &&
+                     ((reinterpret_cast<uintptr_t>(a.sel_gumbel) & 15) == 0);
+    if (vec) {
+        // two float4 pairs in flight per lane per step
+        for (int base = lane * 4; base < n; base += 256) {
+            int b2 = base + 128;
+            float4 l0 = __ldg(reinterpret_cast<const float4 *>(lrow + base));
+            float4 g0 = __ldg(reinterpret_cast<const float4 *>(grow + base));
+            float4 l1 = make_float4(0.f, 0.f, 0.f, 0.f), g1 = l1;
+            if (b2 < n) {
+                l1 = __ldg(reinterpret_cast<const float4 *>(lrow + b2));
+                g1 = __ldg(reinterpret_cast<const float4 *>(grow + b2));
+            }
+            float lv[8] = {l0.x, l0.y, l0.z, l0.w, l1.x, l1.y, l1.z, l1.w};
+            float gv[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
+#pragma unroll
+            for (int e = 0; e < 8; ++e) {
+                int kb = (e < 4) ? base + e : b2 + e - 4;
+                if (kb < n) topm_insert(v, id, M, __fadd_rn(__fdiv_rn(lv[e], tau), gv[e]), kb);
+            }
+        }
+    } else {
+        for (int kb = lane; kb < n; kb += 32) {
+            float s = __fadd_rn(__fdiv_rn(__ldg(lrow + kb), tau), __ldg(grow + kb));
+            topm_insert(v, id, M, s, kb);
+        }
+    }
+    for (int r = 0; r < M; ++r) {
+        float bv = v[0];
+        int bi = id[0];
+#pragma unroll
+        for (int o = 16; o; o >>= 1) {
+            float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+            int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+            if (better(ov, oi, bv, bi)) {
+                bv = ov;
+                bi = oi;
+            }
+        }
+        if (bi != INT_MAX && id[0] == bi) topm_pop(v, id, M);
+        if (lane == 0) cen[r] = (bi == INT_MAX) ? qb : bi;
+    }
+    __syncwarp();
+}
+
+__global__ void __launch_bounds__(kWarps * 32) build_kernel(const BuildParams P) {
+    extern __shared__ int smem[];
+    const ScopeMaskArgs &a = P.a;
+    const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    int *vals = smem + wid * P.per_warp;
+    int *flag = vals + P.max_kv;
+    int *outl = flag + P.max_kv;
+    int *cen = outl + P.max_kv;           // [kMaxM]
+    int *rad = cen + kMaxM;               // [kMaxM]
+    float *alloc = reinterpret_cast<float *>(rad + kMaxM);  // [kMaxM]
+    float *frac = alloc + kMaxM;          // [kMaxM]
+    int *hist = smem + nw * P.per_warp;   // [n_stats] per CTA
+    const bool want_stats = a.stats != nullptr;
+    if (want_stats)
+        for (int i = threadIdx.x; i < P.n_stats; i += blockDim.x) hist[i] = 0;
+    __syncthreads();
+
+    const int H = a.H, QB = a.QB, M = a.M, L = a.local_blocks, p = a.half_blocks, G = a.global_max;
+    const int span = 2 * p + 1;
+    const int n = P.max_kv;
+    const int *dspA = a.block_info;
+    const int *dslA = a.block_info + QB;
+    const int rows = H * QB;
+    const int hist_r = n + 1;                       // radius histogram offset
+    const int hist_e = hist_r + p + 1;              // extra-sum histogram offset
+    const int max_extra = max(1, p * M);
+    const int hist_z = hist_e + max_extra + 1;      // zero-radius count
+
+    for (int row = blockIdx.x * nw + wid; row < rows; row += gridDim.x * nw) {
+        const int h = row / QB, qb = row - h * QB;
+        const int dsp = dspA[qb], dsl = dslA[qb];
+
+        // ---- pointer centres (model/attn_bias.py:779-784) ----
+        if (a.sel_logits) {
+            select_row(a, h, qb, lane, cen);
+        } else if (lane < M) {
+            float d = a.delta_rep[(int64_t)h * a.delta_head_stride + (int64_t)qb * a.delta_row_stride +
+                                  (int64_t)lane * a.delta_m_stride];
+            float key = __fsub_rn((float)((qb + 1) * a.block_size - 1), d);
+            key = fmaxf(key, 0.0f);
+            long long kt = (long long)key;
+            long long cb = kt / a.block_size;
+            cen[lane] = (int)(cb < (long long)INT_MAX ? cb : (long long)INT_MAX);
+        }
+        __syncwarp();
+        if (lane < M) {
+            int c = min(cen[lane], qb);
+            if (!a.ptr_enabled) c = qb;
+            cen[lane] = max(c, dsp);
+        }
+
+        // ---- radius allocation (model/attn_bias.py:721-761) ----
+        const float *brow = a.budget_rep + (int64_t)h * a.budget_head_stride + (int64_t)qb * a.budget_row_stride;
+        int r = 0;
+        if (a.radius_mode == 0) {
+            r = a.half_active;
+        } else if (a.budget_rem > 0) {
+            if (lane == 0) {
+                float rem = (float)a.budget_rem;
+                for (int m = 0; m < M - 1; ++m) {
+                    float u = __fdiv_rn(brow[(int64_t)m * a.budget_m_stride], a.budget_temp);
+                    float v = __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-u)));
+                    float bb = __fmul_rn(v, rem);
+                    alloc[m] = bb;
+                    rem = __fsub_rn(rem, bb);
+                }
+                alloc[M - 1] = rem;
+            }
+            __syncwarp();
+            float fl = 0.f, fr = 0.f;
+            if (lane < M) {
+                fl = floorf(alloc[lane]);
+                fr = __fsub_rn(alloc[lane], fl);
+                frac[lane] = fr;
+            }
+            int fsum = (lane < M) ? (int)fl : 0;
+#pragma unroll
+            for (int o = 16; o; o >>= 1) fsum += __shfl_xor_sync(0xffffffffu, fsum, o);
+            __syncwarp();
+            if (lane < M) {
+                int rem_int = min(max(a.budget_rem - fsum, 0), M);
+                int rank = 0;
+                for (int j = 0; j < M; ++j) {
+                    float fj = frac[j];
+                    rank += (fj > fr) || (fj == fr && j < lane);
+                }
+                float extra = fl + ((rank < rem_int) ? 1.0f : 0.0f);
+                r = min(max((int)extra, 0), p);
+            }
+        }
+        r = min(r, a.half_active);
+        if (!a.ptr_enabled) r = 0;
+        // Gumbel peak masking (model/attn_bias.py:763-777)
+        if (a.peak_gumbel && a.gumbel_k > 0 && a.gumbel_k < M && p > 0) {
+            float s = -INFINITY;
+            if (lane < M)
+                s = __fadd_rn(__fdiv_rn(brow[(int64_t)lane * a.budget_m_stride], a.gumbel_tau),
+                              a.peak_gumbel[(int64_t)row * M + lane]);
+            int rank = 0;
+            for (int j = 0; j < M; ++j) {
+                float sj = __shfl_sync(0xffffffffu, s, j);
+                rank += (sj > s) || (sj == s && j < lane);
+            }
+            if (rank >= a.gumbel_k) r = 0;
+        }
+        if (lane < M) rad[lane] = r;
+        __syncwarp();
+
+        // ---- window pieces (model/attn_bias.py:786-825) ----
+        for (int pos = lane; pos < n; pos += 32) {
+            int val;
+            if (pos < L) {
+                val = max(max(qb - pos, 0), dsl);
+            } else if (pos < L + M * span) {
+                int q = pos - L;
+                int m = q / span;
+                int c = cen[m];
+                if (p > 0) {
+                    int o = q - m * span - p;
+                    int w = min(max(c + o, 0), QB - 1);
+                    w = max(min(w, qb), dsp);
+                    val = (abs(o) <= rad[m]) ? w : c;
+                } else {
+                    val = c;
+                }
+            } else {
+                int i = pos - L - M * span;
+                int g = min(dsp + i, qb);
+                val = (i < a.global_active) ? g : qb;
+            }
+            vals[pos] = val;
+        }
+        __syncwarp();
+
+        // ---- de-duplicate and pack (model/attn_bias.py:828-837) ----
+        int first_cnt = 0;
+        for (int pos = lane; pos < n; pos += 32) {
+            int v = vals[pos];
+            int f = 1;
+            for (int q = 0; q < pos; ++q)
+                if (vals[q] == v) {
+                    f = 0;
+                    break;
+                }
+            flag[pos] = f;
+            first_cnt += f;
+        }
+#pragma unroll
+        for (int o = 16; o; o >>= 1) first_cnt += __shfl_xor_sync(0xffffffffu, first_cnt, o);
+        const int num = first_cnt;
+        __syncwarp();
+        for (int pos = lane; pos < n; pos += 32) {
+            int v = vals[pos];
+            int f = flag[pos];
+            int dst = f ? 0 : num;
+            for (int q = 0; q < n; ++q) {
+                int vq = vals[q], fq = flag[q];
+                if (f) dst += (fq && vq < v);
+                else dst += (!fq && (vq < v || (vq == v && q < pos)));
+            }
+            outl[dst] = v;
+        }
+        __syncwarp();
+
+        // ---- outputs ----
+        if (lane == 0) a.kv_num[row] = num;
+        int32_t *krow = a.kv_indices + (int64_t)row * a.kv_stride;
+        if (a.flex_padded) {
+            for (int j = lane; j < QB; j += 32) krow[j] = (j < n) ? outl[j] : outl[0];
+        } else {
+            int wlen = min(n, a.kv_stride);
+            for (int j = lane; j < wlen; j += 32) krow[j] = outl[j];
+            if (n > a.kv_stride && lane == 0) set_err(a.err_flag, SCOPE_DEVERR_SHAPE);
+        }
+        if (a.q_bitmap) {
+            for (int j = lane; j < num; j += 32) {
+                int kb = outl[j];
+                if (kb >= 0 && kb < QB)
+                    atomicOr(a.q_bitmap + ((int64_t)h * QB + kb) * P.words + (qb >> 5), 1u << (qb & 31));
+                else
+                    set_err(a.err_flag, SCOPE_DEVERR_INDEX);
+            }
+        }
+        if (lane < M) {
+            if (a.r_m_out) a.r_m_out[(int64_t)row * M + lane] = rad[lane];
+            if (a.centres_out) a.centres_out[(int64_t)row * M + lane] = cen[lane];
+        }
+        if (want_stats) {
+            int rr = (lane < M) ? rad[lane] : 0;
+            int esum = rr;
+#pragma unroll
+            for (int o = 16; o; o >>= 1) esum += __shfl_xor_sync(0xffffffffu, esum, o);
+            if (lane == 0) {
+                atomicAdd(&hist[min(num, n)], 1);
+                atomicAdd(&hist[hist_e + min(esum, max_extra)], 1);
+            }
+            if (lane < M) {
+                atomicAdd(&hist[hist_r + min(max(rr, 0), p)], 1);
+                if (rr == 0) atomicAdd(&hist[hist_z], 1);
+            }
+        }
+        __syncwarp();
+    }
+    if (want_stats) {
+        __syncthreads();
+        for (int i = threadIdx.x; i < P.n_stats; i += blockDim.x)
+            if (hist[i]) atomicAdd(a.stats + i, hist[i]);
+    }
+}
+
+// --------------------------------------------------------------------------
+// q-side lists in torch's layout, from the bitmap
+// --------------------------------------------------------------------------
+__global__ void transpose_kernel(const uint32_t *__restrict__ bm, int H, int QB, int words,
+                                 int32_t *__restrict__ q_num, int32_t *__restrict__ q_idx) {
+    int row = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;   // (h, kb)
+    int lane = threadIdx.x & 31;
+    if (row >= H * QB) return;
+    const uint32_t *r = bm + (int64_t)row * words;
+    int cnt = 0;
+    for (int w = lane; w < words; w += 32) cnt += __popc(r[w]);
+#pragma unroll
+    for (int o = 16; o; o >>= 1) cnt += __shfl_xor_sync(0xffffffffu, cnt, o);
+    if (lane == 0) q_num[row] = cnt;
+    if (!q_idx) return;
+    int32_t *out = q_idx + (int64_t)row * QB;
+    int seen_set = 0, seen_unset = 0;   // running counts over earlier chunks
+    for (int w0 = 0; w0 < words; w0 += 32) {
+        int w = w0 + lane;
+        uint32_t bits = (w < words) ? r[w] : 0u;
+        int nvalid = min(32, QB - w * 32);
+        if (w >= words) nvalid = 0;
+        uint32_t vmask = (nvalid >= 32) ? 0xffffffffu : ((nvalid > 0) ? ((1u << nvalid) - 1u) : 0u);
+        bits &= vmask;
+        int ns = __popc(bits), nu = __popc(vmask & ~bits);
+        int ps = ns, pu = nu;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            int ys = __shfl_up_sync(0xffffffffu, ps, o), yu = __shfl_up_sync(0xffffffffu, pu, o);
+            if (lane >= o) {
+                ps += ys;
+                pu += yu;
+            }
+        }
+        int es = seen_set + ps - ns, eu = seen_unset + pu - nu;
+        for (int b = 0; b < nvalid; ++b) {
+            int qb = w * 32 + b;
+            if ((bits >> b) & 1u) out[es++] = qb;
+            else out[cnt + eu++] = qb;
+        }
+        seen_set += __shfl_sync(0xffffffffu, ps, 31);
+        seen_unset += __shfl_sync(0xffffffffu, pu, 31);
+    }
+}
+
+}  // namespace mask
+}  // namespace scope
+
+using namespace scope;
+
+extern "C" int32_t scope_mask_max_kv(int32_t local_blocks, int32_t M, int32_t half_blocks, int32_t global_max) {
+    return local_blocks + (half_blocks > 0 ? M * (2 * half_blocks + 1) : M) + global_max;
+}
+
+extern "C" int scope_block_info(const int32_t *docs, int32_t T, int32_t block_size, int32_t doc_clamp,
+                                int32_t reset_active, int32_t reset_len, int32_t *out, scope_stream_t stream) {
+    if (T <= 0 || block_size <= 0 || T % block_size != 0 || !out) return SCOPE_ERR_INVALID;
+    int QB = T / block_size;
+    cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    mask::block_info_pass1<<<ceil_div(QB * 32, 256), 256, 0, s>>>(docs, T, block_size, QB, out);
+    SCOPE_CHECK_LAUNCH();
+    mask::block_info_pass2<<<1, 1024, 0, s>>>(QB, block_size, doc_clamp, reset_active, reset_len, out);
+    SCOPE_CHECK_LAUNCH();
+    return SCOPE_OK;
+}
+
+extern "C" int scope_mask_build(const ScopeMaskArgs *args, scope_stream_t stream) {
+    if (!args) return SCOPE_ERR_INVALID;
+    const ScopeMaskArgs &a = *args;
+    if (a.H <= 0 || a.QB <= 0 || a.M <= 0 || a.M > mask::kMaxM || a.block_size <= 0) return SCOPE_ERR_INVALID;
+    if ((a.sel_logits == nullptr) == (a.delta_rep == nullptr)) return SCOPE_ERR_INVALID;
+    if (a.sel_logits && (!a.sel_gumbel || a.sel_row_stride < a.QB)) return SCOPE_ERR_INVALID;
+    if (!a.budget_rep && a.radius_mode == 1 && a.budget_rem > 0) return SCOPE_ERR_INVALID;
+    if (!a.block_info || !a.kv_num || !a.kv_indices) return SCOPE_ERR_INVALID;
+    if (a.local_blocks < 1 || a.local_blocks > a.QB || a.half_blocks < 0 || a.global_max < 0 ||
+        a.global_max > a.QB || a.global_active < 0 || a.global_active > a.global_max)
+        return SCOPE_ERR_INVALID;
+    if (a.radius_mode == 1 && a.budget_rem > 0 && !(a.budget_temp > 0.f)) return SCOPE_ERR_INVALID;
+    if (a.sel_logits && !(a.sel_tau > 0.f)) return SCOPE_ERR_INVALID;
+    if (a.peak_gumbel && !(a.gumbel_tau > 0.f)) return SCOPE_ERR_INVALID;
+    int max_kv = scope_mask_max_kv(a.local_blocks, a.M, a.half_blocks, a.global_max);
+    if (a.flex_padded ? (a.kv_stride != a.QB) : (a.kv_stride < max_kv)) return SCOPE_ERR_INVALID;
+    mask::BuildParams P;
+    P.a = a;
+    P.max_kv = max_kv;
+    P.per_warp = 3 * max_kv + 4 * mask::kMaxM;
+    P.n_stats = (max_kv + 1) + (a.half_blocks + 1) + (std::max(1, a.half_blocks * a.M) + 1) + 1;
+    P.words = (a.QB + 31) / 32;
+    int nwarps = mask::kWarps;
+    size_t smem = (size_t)(nwarps * P.per_warp + P.n_stats) * sizeof(int);
+    while (smem > 160 * 1024 && nwarps > 1) {
+        nwarps >>= 1;
+        smem = (size_t)(nwarps * P.per_warp + P.n_stats) * sizeof(int);
+    }
+    if (smem > 200 * 1024) return SCOPE_ERR_INVALID;
+    cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    if (smem > 48 * 1024 &&
+        cudaFuncSetAttribute(mask::build_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
+        return SCOPE_ERR_CUDA;
+    int dev = 0, sms = 148;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    int rows = a.H * a.QB;
+    int grid = std::min(ceil_div(rows, nwarps), sms * 8);
+    mask::build_kernel<<<grid, nwarps * 32, smem, s>>>(P);
+    SCOPE_CHECK_LAUNCH();
+    return SCOPE_OK;
+}
+
+extern "C" int scope_mask_transpose(const uint32_t *q_bitmap, int32_t H, int32_t QB, int32_t *q_num,
+                                    int32_t *q_indices, scope_stream_t stream) {
+    if (!q_bitmap || !q_num || H <= 0 || QB <= 0) return SCOPE_ERR_INVALID;
+    int words = (QB + 31) / 32;
+    int rows = H * QB;
+    mask::transpose_kernel<<<ceil_div(rows * 32, 256), 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+        q_bitmap, H, QB, words, q_num, q_indices);
+    SCOPE_CHECK_LAUNCH();
+    return SCOPE_OK;
+}

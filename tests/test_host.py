@@ -1,0 +1,77 @@
+"""Host-side checks that need no GPU: the C-ABI library loads, exports every
+symbol the header declares, its struct layouts match the ctypes mirror, and
+argument validation rejects bad calls before touching the device."""
+import ctypes
+import os
+import re
+
+import pytest
+
+import scope_b200
+from scope_b200 import _lib
+from scope_b200.attention import aug_dims
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def header_functions():
+    src = open(os.path.join(ROOT, "include", "scope_b200.h")).read()
+    src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
+    return sorted(set(re.findall(r"\b(scope_[a-z0-9_]+)\s*\(", src)))
+
+
+def test_library_exports_every_declared_symbol():
+    L = scope_b200.load_library()
+    names = header_functions()
+    assert len(names) >= 12
+    for n in names:
+        assert hasattr(L, n), n
+    assert set(names) == set(_lib.SIGNATURES), "ctypes signatures must cover the header exactly"
+
+
+def test_struct_layouts_match():
+    _lib.check_abi()
+
+
+def test_error_strings():
+    L = _lib.lib()
+    assert L.scope_error_string(0) == b"ok"
+    assert L.scope_error_string(-1) == b"invalid argument"
+    assert L.scope_error_string(-6) == b"workspace missing or too small"
+    assert L.scope_error_string(-99) == b"unknown status"
+
+
+def test_validation_rejects_before_launch():
+    L = _lib.lib()
+    a = _lib.ScopeAttnArgs()
+    assert L.scope_attn_fwd(ctypes.byref(a), None) == -1          # empty args
+    a.H, a.T, a.D, a.block_size, a.dtype = 2, 256, 32, 128, 1
+    assert L.scope_attn_fwd(ctypes.byref(a), None) == -1          # head_dim 32
+    a.D, a.dtype = 64, 7
+    assert L.scope_attn_fwd(ctypes.byref(a), None) == -2          # dtype
+    m = _lib.ScopeMaskArgs()
+    assert L.scope_mask_build(ctypes.byref(m), None) == -1
+    m.H, m.QB, m.M, m.block_size = 1, 4, 17, 128
+    assert L.scope_mask_build(ctypes.byref(m), None) == -1        # M > 16
+    assert L.scope_block_info(None, 100, 128, 1, 0, 0, None, None) == -1
+    assert L.scope_qk_aug_prepare(None, None, None, None, None, 0, 1, 1, 1, 16, 0.5, 0.12, 1, None, None, None) == -1
+    a2 = _lib.ScopeAttnArgs()
+    a2.H, a2.T = 16, 131072
+    assert L.scope_workspace_bytes(ctypes.byref(a2)) == 16 * 131072 * 4
+
+
+def test_mask_max_kv():
+    L = _lib.lib()
+    assert L.scope_mask_max_kv(8, 8, 4, 1) == 8 + 8 * 9 + 1
+    assert L.scope_mask_max_kv(8, 4, 0, 1) == 13
+
+
+def test_aug_dims():
+    assert aug_dims(8, False) == 16 and aug_dims(8, True) == 32
+    assert aug_dims(16, False) == 32 and aug_dims(16, True) == 48
+
+
+def test_ops_registered():
+    import torch
+    assert hasattr(torch.ops.scope, "sparse_attn")
+    assert hasattr(torch.ops.scope, "sparse_attn_bwd")
