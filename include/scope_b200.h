@@ -188,8 +188,13 @@ typedef struct ScopeAttnArgs {
     float *db0, *dslope, *ddelta_main, *dwidth; /* [H,T] or NULL */
     void *workspace;
     size_t workspace_bytes;
+    int32_t flags;                    /* SCOPE_FLAG_* */
     int32_t *err_flag;                /* optional device error word */
 } ScopeAttnArgs;
+
+/* ScopeAttnArgs.flags: run the CUDA-core kernels even where the tensor-core
+ * kernels apply (cross-checking one implementation against the other). */
+#define SCOPE_FLAG_CUDA_CORES 0x1
 
 /* Forward: out and lse.  Replaces the flex_attention forward at
  * scoped_medium.py:459-466 (score_mod) and :422 (qk_aug). */

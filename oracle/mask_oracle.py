@@ -229,6 +229,8 @@ def select_pointer_blocks(logits, g, *, M: int, tau: float):
     s = np.where(causal[None], s, -np.inf).astype(np.float64)
     # stable sort on (-score); -inf candidates sort last, then by index
     order = np.argsort(-s, axis=-1, kind="stable")[..., :M]
+    if order.shape[-1] < M:          # fewer candidate blocks than peaks
+        order = np.concatenate([order, np.zeros((H, QB, M - order.shape[-1]), order.dtype)], -1)
     out = order.astype(np.int32)
     nvalid = np.minimum(np.arange(QB) + 1, M)
     slot = np.arange(M)
@@ -385,7 +387,9 @@ def pointer_stats(kv_num, r_m, *, max_kv: int, half_blocks: int, M: int):
     (model/attn_bias.py:839-849): kv_unique_hist, ptr_radius_hist,
     ptr_extra_sum_hist and the count of zero radii."""
     kv_hist = np.bincount(np.asarray(kv_num).ravel(), minlength=max_kv + 1)[: max_kv + 1]
-    rad = np.asarray(r_m).ravel()
+    # the reference's radius buffer has half_blocks+1 bins; radii above can only
+    # come from a schedule cap above the call's half width and land in the top bin
+    rad = np.clip(np.asarray(r_m).ravel(), 0, half_blocks)
     pr_hist = np.bincount(rad, minlength=half_blocks + 1)[: half_blocks + 1]
     max_extra = max(1, half_blocks * M)
     es = np.minimum(np.asarray(r_m).sum(-1), max_extra).ravel()

@@ -10,10 +10,11 @@ Every op runs hand-written CUDA through the C ABI of libscope_b200.so
 from . import _lib
 from .attention import SpectralScoreMod, aug_dims, flex_attention, trig_tables
 from .mask import PointerBlockMaskBuilder, ScopeBlockMask, block_info, build_mask
+from ._lib import device_errors
 
 __all__ = [
     "PointerBlockMaskBuilder", "ScopeBlockMask", "SpectralScoreMod", "aug_dims", "block_info", "build_mask",
-    "flex_attention", "trig_tables", "load_library",
+    "flex_attention", "trig_tables", "load_library", "device_errors",
 ]
 
 

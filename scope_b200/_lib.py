@@ -73,6 +73,7 @@ class ScopeAttnArgs(ctypes.Structure):
         ("db0", P), ("dslope", P), ("ddelta_main", P), ("dwidth", P),
         ("workspace", P),
         ("workspace_bytes", ctypes.c_size_t),
+        ("flags", I32),
         ("err_flag", P),
     ]
 
@@ -132,6 +133,40 @@ def check_abi() -> None:
         if size != ctypes.sizeof(S) or last != S.err_flag.offset:
             raise RuntimeError(f"scope_b200 ABI mismatch for {S.__name__}: C sizeof={size} last={last}, "
                                f"ctypes sizeof={ctypes.sizeof(S)} last={S.err_flag.offset}")
+
+
+FLAG_CUDA_CORES = 0x1
+DEVERR_INDEX, DEVERR_TIMEOUT, DEVERR_SHAPE = 0x1, 0x2, 0x4
+
+_err_words = {}
+
+
+def err_word_ptr(device) -> int:
+    """Address of this device's error word (int32, zero-initialised), which
+    every launch from this package passes as ``err_flag``."""
+    import torch
+    dev = torch.device(device)
+    idx = dev.index if dev.index is not None else torch.cuda.current_device()
+    t = _err_words.get(idx)
+    if t is None:
+        t = torch.zeros(1, dtype=torch.int32, device=torch.device("cuda", idx))
+        _err_words[idx] = t
+    return t.data_ptr()
+
+
+def device_errors(device=None, reset: bool = True) -> int:
+    """Error bits the kernels have set on a device since the last reset
+    (synchronises with the device)."""
+    import torch
+    dev = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
+    idx = dev.index if dev.index is not None else torch.cuda.current_device()
+    t = _err_words.get(idx)
+    if t is None:
+        return 0
+    v = int(t.item())
+    if reset:
+        t.zero_()
+    return v
 
 
 def ptr(t) -> int | None:

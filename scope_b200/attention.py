@@ -74,7 +74,7 @@ def _hd(t: Optional[Tensor]) -> Optional[Tensor]:
 
 def _attn_args(q, k, v, out, lse, kv_num, kv_indices, q_bitmap, block_info, docs,
                coeff_cos, coeff_sin, cos_tab, sin_tab, b0, slope, delta_main, width,
-               scale, beta, bias_mode, gate, gate_lambda, gate_tau, block_size, q_aug, k_aug):
+               scale, beta, bias_mode, gate, gate_lambda, gate_tau, block_size, q_aug, k_aug, cuda_cores=False):
     a = _lib.ScopeAttnArgs()
     H, T, D = q.shape
     a.H, a.T, a.D, a.block_size = H, T, D, block_size
@@ -104,6 +104,8 @@ def _attn_args(q, k, v, out, lse, kv_num, kv_indices, q_bitmap, block_info, docs
     a.gate, a.beta, a.gate_lambda, a.gate_tau = gate, beta, gate_lambda, gate_tau
     a.q_aug, a.k_aug = _lib.ptr(q_aug), _lib.ptr(k_aug)
     a.d_aug = 0 if q_aug is None else q_aug.shape[-1]
+    a.flags = _lib.FLAG_CUDA_CORES if cuda_cores else 0
+    a.err_flag = _lib.err_word_ptr(q.device)
     return a
 
 
@@ -155,7 +157,7 @@ def sparse_attn(q: Tensor, k: Tensor, v: Tensor, kv_num: Tensor, kv_indices: Ten
                 coeff_sin: Optional[Tensor], cos_tab: Optional[Tensor], sin_tab: Optional[Tensor],
                 b0: Optional[Tensor], slope: Optional[Tensor], delta_main: Optional[Tensor],
                 width: Optional[Tensor], scale: float, beta: float, bias_mode: int, gate: int,
-                gate_lambda: float, gate_tau: float, block_size: int) -> tuple[Tensor, Tensor]:
+                gate_lambda: float, gate_tau: float, block_size: int, cuda_cores: bool) -> tuple[Tensor, Tensor]:
     _check_inputs(q, k, v, kv_num, kv_indices, block_size)
     H, T, D = q.shape
     out = _new_like_layout(q)
@@ -163,14 +165,14 @@ def sparse_attn(q: Tensor, k: Tensor, v: Tensor, kv_num: Tensor, kv_indices: Ten
     q_aug, k_aug = _prepare_aug(q, coeff_cos, coeff_sin, slope, cos_tab, sin_tab, beta, scale, bias_mode)
     a = _attn_args(q, k, v, out, lse, kv_num, kv_indices, q_bitmap, block_info, docs, coeff_cos, coeff_sin,
                    cos_tab, sin_tab, b0, slope, delta_main, width, scale, beta, bias_mode, gate, gate_lambda,
-                   gate_tau, block_size, q_aug, k_aug)
+                   gate_tau, block_size, q_aug, k_aug, cuda_cores)
     _lib.check(_lib.lib().scope_attn_fwd(ctypes.byref(a), _stream(q.device)), "scope_attn_fwd")
     return out, lse
 
 
 @sparse_attn.register_fake
 def _(q, k, v, kv_num, kv_indices, q_bitmap, block_info, docs, coeff_cos, coeff_sin, cos_tab, sin_tab,
-      b0, slope, delta_main, width, scale, beta, bias_mode, gate, gate_lambda, gate_tau, block_size):
+      b0, slope, delta_main, width, scale, beta, bias_mode, gate, gate_lambda, gate_tau, block_size, cuda_cores):
     H, T, D = q.shape
     out = q.new_empty(T, H, D).permute(1, 0, 2)
     return out, q.new_empty(H, T, dtype=torch.float32)
@@ -183,7 +185,7 @@ def sparse_attn_bwd(dout: Tensor, q: Tensor, k: Tensor, v: Tensor, out: Tensor, 
                     sin_tab: Optional[Tensor], b0: Optional[Tensor], slope: Optional[Tensor],
                     delta_main: Optional[Tensor], width: Optional[Tensor], scale: float, beta: float,
                     bias_mode: int, gate: int, gate_lambda: float, gate_tau: float, block_size: int,
-                    want_bias_grads: bool) -> list[Tensor]:
+                    want_bias_grads: bool, cuda_cores: bool) -> list[Tensor]:
     H, T, D = q.shape
     if dout.stride(-1) != 1:
         dout = dout.contiguous()
@@ -191,14 +193,14 @@ def sparse_attn_bwd(dout: Tensor, q: Tensor, k: Tensor, v: Tensor, out: Tensor, 
     q_aug, k_aug = _prepare_aug(q, coeff_cos, coeff_sin, slope, cos_tab, sin_tab, beta, scale, bias_mode)
     a = _attn_args(q, k, v, out, lse, kv_num, kv_indices, q_bitmap, block_info, docs, coeff_cos, coeff_sin,
                    cos_tab, sin_tab, b0, slope, delta_main, width, scale, beta, bias_mode, gate, gate_lambda,
-                   gate_tau, block_size, q_aug, k_aug)
+                   gate_tau, block_size, q_aug, k_aug, cuda_cores)
     a.dout, a.do_sh, a.do_st = dout.data_ptr(), dout.stride(0), dout.stride(1)
     a.dq, a.dk, a.dv = dq.data_ptr(), dk.data_ptr(), dv.data_ptr()
     a.dq_sh, a.dq_st = dq.stride(0), dq.stride(1)
     a.dk_sh, a.dk_st = dk.stride(0), dk.stride(1)
     a.dv_sh, a.dv_st = dv.stride(0), dv.stride(1)
-    empty = q.new_empty(0, dtype=torch.float32)
-    dcc = dcs = db0 = dsl = ddm = dw = empty
+    # absent gradients are returned as distinct empty tensors (custom ops may not alias outputs)
+    dcc, dcs, db0, dsl, ddm, dw = (q.new_empty(0, dtype=torch.float32) for _ in range(6))
     if want_bias_grads and coeff_cos is not None:
         dcc = torch.empty_like(coeff_cos)
         dcs = torch.empty_like(coeff_sin)
@@ -225,17 +227,17 @@ def sparse_attn_bwd(dout: Tensor, q: Tensor, k: Tensor, v: Tensor, out: Tensor, 
 @sparse_attn_bwd.register_fake
 def _(dout, q, k, v, out, lse, kv_num, kv_indices, q_bitmap, block_info, docs, coeff_cos, coeff_sin, cos_tab,
       sin_tab, b0, slope, delta_main, width, scale, beta, bias_mode, gate, gate_lambda, gate_tau, block_size,
-      want_bias_grads):
+      want_bias_grads, cuda_cores):
     H, T, D = q.shape
     mk = lambda x: x.new_empty(T, H, D).permute(1, 0, 2)  # noqa: E731
-    e = q.new_empty(0, dtype=torch.float32)
-    dcc = torch.empty_like(coeff_cos) if (want_bias_grads and coeff_cos is not None) else e
-    dcs = torch.empty_like(coeff_sin) if (want_bias_grads and coeff_sin is not None) else e
-    dsl = torch.empty_like(slope) if (want_bias_grads and coeff_cos is not None and slope is not None) else e
+    e = lambda: q.new_empty(0, dtype=torch.float32)  # noqa: E731
+    dcc = torch.empty_like(coeff_cos) if (want_bias_grads and coeff_cos is not None) else e()
+    dcs = torch.empty_like(coeff_sin) if (want_bias_grads and coeff_sin is not None) else e()
+    dsl = torch.empty_like(slope) if (want_bias_grads and coeff_cos is not None and slope is not None) else e()
     sm = bias_mode == BIAS_MODES["score_mod"] and want_bias_grads and coeff_cos is not None
-    db0 = torch.empty_like(b0) if (sm and b0 is not None) else e
-    ddm = torch.empty_like(delta_main) if (sm and gate != 0 and delta_main is not None) else e
-    dw = torch.empty_like(width) if (sm and gate != 0 and delta_main is not None) else e
+    db0 = torch.empty_like(b0) if (sm and b0 is not None) else e()
+    ddm = torch.empty_like(delta_main) if (sm and gate != 0 and delta_main is not None) else e()
+    dw = torch.empty_like(width) if (sm and gate != 0 and delta_main is not None) else e()
     return [mk(q), mk(k), mk(v), dcc, dcs, db0, dsl, ddm, dw]
 
 
@@ -245,26 +247,28 @@ _TENSOR_ARGS = ("q", "k", "v", "kv_num", "kv_indices", "q_bitmap", "block_info",
 
 def _setup_context(ctx, inputs, output):
     (q, k, v, kv_num, kv_indices, q_bitmap, block_info, docs, coeff_cos, coeff_sin, cos_tab, sin_tab,
-     b0, slope, delta_main, width, scale, beta, bias_mode, gate, gate_lambda, gate_tau, block_size) = inputs
+     b0, slope, delta_main, width, scale, beta, bias_mode, gate, gate_lambda, gate_tau, block_size,
+     cuda_cores) = inputs
     out, lse = output
     ctx.save_for_backward(q, k, v, out, lse, kv_num, kv_indices, q_bitmap, block_info, docs, coeff_cos,
                           coeff_sin, cos_tab, sin_tab, b0, slope, delta_main, width)
-    ctx.scal = (scale, beta, bias_mode, gate, gate_lambda, gate_tau, block_size)
+    ctx.scal = (scale, beta, bias_mode, gate, gate_lambda, gate_tau, block_size, cuda_cores)
 
 
 def _backward(ctx, dout, dlse):
     (q, k, v, out, lse, kv_num, kv_indices, q_bitmap, block_info, docs, coeff_cos, coeff_sin, cos_tab,
      sin_tab, b0, slope, delta_main, width) = ctx.saved_tensors
-    scale, beta, bias_mode, gate, gate_lambda, gate_tau, block_size = ctx.scal
+    scale, beta, bias_mode, gate, gate_lambda, gate_tau, block_size, cuda_cores = ctx.scal
     nig = ctx.needs_input_grad
     want_bias = any(nig[i] for i in (8, 9, 12, 13, 14, 15))
     g = torch.ops.scope.sparse_attn_bwd(dout, q, k, v, out, lse, kv_num, kv_indices, q_bitmap, block_info, docs,
                                         coeff_cos, coeff_sin, cos_tab, sin_tab, b0, slope, delta_main, width,
-                                        scale, beta, bias_mode, gate, gate_lambda, gate_tau, block_size, want_bias)
+                                        scale, beta, bias_mode, gate, gate_lambda, gate_tau, block_size, want_bias,
+                                        cuda_cores)
     dq, dk, dv, dcc, dcs, db0, dsl, ddm, dw = g
     pick = lambda t: t if (t is not None and t.numel() > 0) else None  # noqa: E731
     return (dq, dk, dv, None, None, None, None, None, pick(dcc), pick(dcs), None, None, pick(db0), pick(dsl),
-            pick(ddm), pick(dw), None, None, None, None, None, None, None)
+            pick(ddm), pick(dw), None, None, None, None, None, None, None, None)
 
 
 sparse_attn.register_autograd(_backward, setup_context=_setup_context)
@@ -272,12 +276,14 @@ sparse_attn.register_autograd(_backward, setup_context=_setup_context)
 
 def flex_attention(query: Tensor, key: Tensor, value: Tensor, block_mask: ScopeBlockMask,
                    score_mod: Optional[SpectralScoreMod] = None, scale: Optional[float] = None,
-                   return_lse: bool = False):
+                   return_lse: bool = False, cuda_cores: bool = False):
     """Block-sparse attention with the SCOPE spectral bias, same call shape
     as torch's flex_attention: q, k, v [1, H, T, D] (any head/token strides,
     contiguous D), ``block_mask`` from the pointer builder, ``score_mod`` the
     captured spectral-bias state or None.  Returns [1, H, T, D] in the input
-    dtype (and the [1, H, T] float32 natural-log lse with ``return_lse``)."""
+    dtype (and the [1, H, T] float32 natural-log lse with ``return_lse``).
+    ``cuda_cores`` runs the CUDA-core kernels even where the tensor-core
+    kernels apply (to cross-check the two)."""
     squeeze = query.dim() == 4
     if squeeze and query.shape[0] != 1:
         raise ValueError("batch size must be 1 (as in the reference)")
@@ -309,7 +315,7 @@ def flex_attention(query: Tensor, key: Tensor, value: Tensor, block_mask: ScopeB
                                            docs, args["coeff_cos"], args["coeff_sin"], args["cos_tab"],
                                            args["sin_tab"], args["b0"], args["slope"], args["delta_main"],
                                            args["width"], sc, args["beta"], args["bias_mode"], args["gate"],
-                                           args["gate_lambda"], args["gate_tau"], bs)
+                                           args["gate_lambda"], args["gate_tau"], bs, bool(cuda_cores))
     if squeeze:
         out, lse = out.unsqueeze(0), lse.unsqueeze(0)
     return (out, lse) if return_lse else out

@@ -63,7 +63,7 @@ def build(verbose: bool = False, ptxas_verbose: bool = False) -> str:
     with ThreadPoolExecutor(max_workers=min(8, len(srcs))) as ex:
         objs = list(ex.map(compile_one, srcs))
     tmp = OUT + ".tmp"
-    cmd = [nvcc] + ARCH + ["-shared", "-o", tmp] + objs + ["-lcuda"] 
+    cmd = [nvcc] + ARCH + ["-shared", "-o", tmp] + objs
     r = subprocess.run(cmd, capture_output=True, text=True)
     if r.returncode != 0:
         sys.stderr.write(r.stdout + r.stderr)

@@ -1,7 +1,463 @@
-// tcgen05 / TMEM / TMA attention kernels (sm_100a).  Placeholder: the
-// tensor-core path is not enabled yet, so no configuration is eligible.
-#include "common.cuh"
+// Block-sparse SCOPE attention forward on the sm_100a tensor cores.
+//
+// One CTA computes one 128-row query block of one head against the kv
+// blocks its list names (kv_indices, in order), flash-attention style:
+//
+//   warp 0      TMA producer: Q (+ the qk_aug dims) once, then K (+aug) / V
+//               tiles of each listed kv block into a 2-stage ring.  Tiles are
+//               addressed by block index, so the sparse gather is just the
+//               TMA coordinate.  No multicast.
+//   warp 1      tcgen05 issuer (one thread): S = Q K^T (+ Qaug Kaug^T, the
+//               spectral bias of the qk_aug mode) into TMEM, then O += P V
+//               with P read from TMEM as the A operand.  It also owns the TMEM
+//               allocation.
+//   warps 2..5  softmax: one thread per query row.  S comes out of TMEM with
+//               tcgen05.ld, the document-causal mask is applied only on tiles
+//               that need it (diagonal, document boundary), exponentials are
+//               taken in the log2 domain, P goes back to TMEM as bf16, and the
+//               running max is only moved when it grows by more than 2^8
+//               (otherwise O would need a rescale through TMEM every tile).
+//
+// TMEM (256 columns per CTA, two CTAs per SM): S [0,128), O [128,192),
+// P (bf16 pairs) [192,256).  S is single buffered: the issuer starts
+// S_{j+1} as soon as the softmax threads have copied S_j to registers, so the
+// QK^T of the next tile overlaps the softmax of the current one and P V_j
+// overlaps the next softmax.
+//
+// Every mbarrier wait is bounded; a wait that gives up sets
+// SCOPE_DEVERR_TIMEOUT in the error word and the CTA winds down (draining
+// its own TMA loads, freeing TMEM) instead of hanging.
+#include <cmath>
+#include <cstring>
 
-bool scope_tc_eligible(const ScopeAttnArgs &, bool) { return false; }
-int scope_tc_fwd(const ScopeAttnArgs &, cudaStream_t) { return SCOPE_ERR_UNSUPPORTED; }
+#include "tc_ptx.cuh"
+
+namespace scope {
+namespace tcfwd {
+
+using namespace tc;
+
+constexpr int BM = 128;
+constexpr int HD = 64;
+constexpr int kThreads = 192;
+constexpr uint32_t kTmemCols = 256;
+constexpr uint32_t S_COL = 0, O_COL = 128, P_COL = 192;
+
+__host__ __device__ constexpr uint32_t align1k(uint32_t x) { return (x + 1023u) & ~1023u; }
+
+// qk_aug dims are staged as at most two sub-tiles whose rows match a swizzle
+// span (16 -> 16, 32 -> 32, 48 -> 32 + 16, 64 -> 64 bf16 columns)
+template <int DA>
+struct Aug {
+    static constexpr int A1 = (DA == 48) ? 32 : DA;
+    static constexpr int A2 = DA - A1;
+};
+
+template <int DA>
+struct Layout {
+    static constexpr uint32_t TILE = BM * HD * 2;                // 16 KiB
+    static constexpr uint32_t AUG1 = BM * Aug<DA>::A1 * 2;
+    static constexpr uint32_t AUG2 = BM * Aug<DA>::A2 * 2;
+    static constexpr uint32_t Q = 0;
+    static constexpr uint32_t QA1 = TILE;
+    static constexpr uint32_t QA2 = QA1 + AUG1;
+    static constexpr uint32_t STAGE0 = align1k(QA2 + AUG2);
+    static constexpr uint32_t K = 0, KA1 = TILE, KA2 = TILE + AUG1;
+    static constexpr uint32_t V = align1k(TILE + AUG1 + AUG2);
+    static constexpr uint32_t STAGE = V + TILE;
+    static constexpr uint32_t BAR = STAGE0 + 2 * STAGE;
+    static constexpr uint32_t TOTAL = BAR + 128;
+    static constexpr uint32_t KV_BYTES = 2 * TILE + AUG1 + AUG2;  // expected TMA bytes per stage
+    static constexpr uint32_t Q_BYTES = TILE + AUG1 + AUG2;
+};
+
+struct FwdParams {
+    int H, T, QB, kv_stride;
+    const int32_t *kv_num, *kv_idx, *block_info, *docs;
+    float scale_log2;
+    __nv_bfloat16 *out;
+    int64_t o_sh, o_st;
+    float *lse;
+    int32_t *err;
+};
+
+struct Maps {
+    CUtensorMap q, k, v, qa1, qa2, ka1, ka2;
+};
+
+template <int DA>
+__global__ void __launch_bounds__(kThreads, 2) fwd_kernel(const __grid_constant__ Maps maps, const FwdParams p) {
+    using L = Layout<DA>;
+    constexpr int A1 = Aug<DA>::A1, A2 = Aug<DA>::A2;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
+    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + L::BAR);
+    uint64_t *q_full = bars + 0, *kv_full = bars + 1, *kv_empty = bars + 3;
+    uint64_t *s_full = bars + 5, *s_free = bars + 6, *p_full = bars + 7, *o_done = bars + 8;
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 9);
+    volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
+
+    const int qb = blockIdx.x, h = blockIdx.y;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int64_t mrow = (int64_t)h * p.QB + qb;
+    const int n = p.kv_num[mrow];
+    const int32_t *list = p.kv_idx + mrow * p.kv_stride;
+
+    if (threadIdx.x == 0) {
+        mbar_init(q_full, 1);
+        mbar_init(kv_full + 0, 1);
+        mbar_init(kv_full + 1, 1);
+        mbar_init(kv_empty + 0, 1);
+        mbar_init(kv_empty + 1, 1);
+        mbar_init(s_full, 1);
+        mbar_init(s_free, 128);
+        mbar_init(p_full, 128);
+        mbar_init(o_done, 1);
+        *abort_flag = 0;
+        fence_mbar_init();
+    }
+    if (warp == 1) {
+        tmem_alloc(tmem_slot, kTmemCols);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    auto give_up = [&]() {
+        *abort_flag = 1;
+        set_err(p.err, SCOPE_DEVERR_TIMEOUT);
+    };
+    // softmax warps run warp-collective tcgen05.ld/st, so they agree on every wait's outcome
+    auto warp_wait = [&](uint64_t *bar, uint32_t parity) -> bool {
+        bool ok = !*abort_flag && mbar_wait(bar, parity);
+        return __all_sync(0xffffffffu, ok);
+    };
+
+    if (warp == 0) {
+        // ------------------------------------------------------------ producer
+        if (lane == 0 && n > 0) {
+            mbar_expect_tx(q_full, L::Q_BYTES);
+            tma_load_3d(&maps.q, smem + L::Q, q_full, 0, qb * BM, h);
+            if (A1) tma_load_3d(&maps.qa1, smem + L::QA1, q_full, 0, qb * BM, h);
+            if (A2) tma_load_3d(&maps.qa2, smem + L::QA2, q_full, A1, qb * BM, h);
+            int issued = 0;
+            for (int j = 0; j < n; ++j) {
+                const int s = j & 1;
+                if (j >= 2 && (*abort_flag || !mbar_wait(kv_empty + s, ((j >> 1) - 1) & 1))) {
+                    give_up();
+                    break;
+                }
+                int kb = list[j];
+                if (kb < 0 || kb >= p.QB) kb = 0;   // the softmax masks this tile and flags it
+                uint8_t *st = smem + L::STAGE0 + s * L::STAGE;
+                mbar_expect_tx(kv_full + s, L::KV_BYTES);
+                tma_load_3d(&maps.k, st + L::K, kv_full + s, 0, kb * BM, h);
+                if (A1) tma_load_2d(&maps.ka1, st + L::KA1, kv_full + s, 0, kb * BM);
+                if (A2) tma_load_2d(&maps.ka2, st + L::KA2, kv_full + s, A1, kb * BM);
+                tma_load_3d(&maps.v, st + L::V, kv_full + s, 0, kb * BM, h);
+                issued = j + 1;
+            }
+            // never leave the CTA with a TMA write still in flight
+            mbar_wait(q_full, 0, 1u << 20);
+            for (int j = (issued > 2 ? issued - 2 : 0); j < issued; ++j)
+                mbar_wait(kv_full + (j & 1), (j >> 1) & 1, 1u << 20);
+        }
+    } else if (warp == 1) {
+        // ------------------------------------------------------------ tcgen05 issuer
+        if (lane == 0 && n > 0) {
+            constexpr uint32_t idS = idesc_bf16(128, 128, false, false);
+            constexpr uint32_t idO = idesc_bf16(128, 64, false, true);
+            const uint32_t tS = tmem + S_COL, tO = tmem + O_COL, tP = tmem + P_COL;
+            const uint32_t sq = smem_u32(smem + L::Q);
+            bool ok = mbar_wait(q_full, 0);
+            auto issue_S = [&](int j) -> bool {
+                const int s = j & 1;
+                if (*abort_flag || !mbar_wait(kv_full + s, (j >> 1) & 1)) return false;
+                tc_fence_after();
+                const uint32_t sk = smem_u32(smem + L::STAGE0 + s * L::STAGE);
+#pragma unroll
+                for (int kk = 0; kk < HD / 16; ++kk)
+                    mma_ss(tS, kmajor_desc(sq + L::Q + kk * 32, 128), kmajor_desc(sk + L::K + kk * 32, 128), idS,
+                           kk > 0);
+#pragma unroll
+                for (int kk = 0; kk < A1 / 16; ++kk)
+                    mma_ss(tS, kmajor_desc(sq + L::QA1 - L::Q + kk * 32, A1 * 2),
+                           kmajor_desc(sk + L::KA1 + kk * 32, A1 * 2), idS, 1);
+#pragma unroll
+                for (int kk = 0; kk < A2 / 16; ++kk)
+                    mma_ss(tS, kmajor_desc(sq + L::QA2 - L::Q + kk * 32, A2 * 2),
+                           kmajor_desc(sk + L::KA2 + kk * 32, A2 * 2), idS, 1);
+                tc_commit(s_full);
+                return true;
+            };
+            ok = ok && issue_S(0);
+            for (int j = 0; ok && j < n; ++j) {
+                if (j + 1 < n) {
+                    if (*abort_flag || !mbar_wait(s_free, j & 1)) { ok = false; break; }
+                    if (!issue_S(j + 1)) { ok = false; break; }
+                }
+                if (*abort_flag || !mbar_wait(p_full, j & 1)) { ok = false; break; }
+                tc_fence_after();
+                const uint32_t sv = smem_u32(smem + L::STAGE0 + (j & 1) * L::STAGE + L::V);
+#pragma unroll
+                for (int kk = 0; kk < BM / 16; ++kk)
+                    mma_ts(tO, tP + kk * 8, mnmajor128_desc(sv + kk * 2048), idO, (j > 0 || kk > 0) ? 1u : 0u);
+                tc_commit(o_done);
+                tc_commit(kv_empty + (j & 1));
+            }
+            if (!ok) give_up();
+        }
+    } else {
+        // ------------------------------------------------------------ softmax + epilogue
+        const int quad = warp & 3;
+        const int r = quad * 32 + lane;
+        const int i = qb * BM + r;
+        const uint32_t lane_base = (uint32_t)(quad * 32) << 16;
+        const uint32_t tS = tmem + lane_base + S_COL, tO = tmem + lane_base + O_COL, tP = tmem + lane_base + P_COL;
+        const bool have_docs = p.docs != nullptr;
+        const int doc_i = have_docs ? p.docs[i] : 0;
+        const int32_t *dmin = p.block_info ? p.block_info + 2 * p.QB : nullptr;
+        const int32_t *dmax = p.block_info ? p.block_info + 3 * p.QB : nullptr;
+        const bool q_uniform = !have_docs || (dmin && dmin[qb] == dmax[qb]);
+        float m = -INFINITY, l = 0.f;
+        bool alive = true;
+        for (int j = 0; j < n && alive; ++j) {
+            int kb = list[j];
+            const bool bad = kb < 0 || kb >= p.QB;
+            if (bad && r == 0) set_err(p.err, SCOPE_DEVERR_INDEX);
+            const bool full = !bad && kb < qb &&
+                              (!have_docs || (q_uniform && dmin && dmin[kb] == dmax[kb] && dmin[kb] == dmin[qb]));
+            if (!warp_wait(s_full, j & 1)) { give_up(); alive = false; break; }
+            tc_fence_after();
+            float x[BM];
+            {
+                uint32_t u[32];
+#pragma unroll
+                for (int c = 0; c < 4; ++c) {
+                    tmem_ld32(tS + c * 32, u);
+                    tmem_wait_ld();
+#pragma unroll
+                    for (int e = 0; e < 32; ++e) x[c * 32 + e] = __uint_as_float(u[e]) * p.scale_log2;
+                }
+            }
+            tc_fence_before();
+            mbar_arrive(s_free);
+            if (!full) {
+                const int j0 = kb * BM;
+#pragma unroll
+                for (int c = 0; c < BM; ++c) {
+                    const int jt = j0 + c;
+                    bool valid = !bad && jt <= i;
+                    if (have_docs) valid = valid && (__ldg(p.docs + (bad ? 0 : jt)) == doc_i);
+                    if (!valid) x[c] = -INFINITY;
+                }
+            }
+            float mx = x[0];
+#pragma unroll
+            for (int c = 1; c < BM; ++c) mx = fmaxf(mx, x[c]);
+            float alpha = 1.f;
+            bool rescale = false;
+            if (mx > m + 8.f) {     // move the reference max only when it grows by > 2^8
+                alpha = (m == -INFINITY) ? 0.f : ex2(m - mx);
+                m = mx;
+                rescale = true;
+            }
+            const float mref = (m == -INFINITY) ? 0.f : m;
+            float rs = 0.f;
+#pragma unroll
+            for (int c = 0; c < BM; ++c) {
+                x[c] = ex2(x[c] - mref);
+                rs += x[c];
+            }
+            l = l * alpha + rs;
+            if (j > 0) {
+                if (!warp_wait(o_done, (j - 1) & 1)) { give_up(); alive = false; break; }
+                tc_fence_after();
+                if (rescale) {
+#pragma unroll
+                    for (int c = 0; c < HD / 16; ++c) {
+                        uint32_t o[16];
+                        tmem_ld16(tO + c * 16, o);
+                        tmem_wait_ld();
+#pragma unroll
+                        for (int e = 0; e < 16; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * alpha);
+                        tmem_st16(tO + c * 16, o);
+                    }
+                }
+            }
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {
+                uint32_t pk[16];
+#pragma unroll
+                for (int e = 0; e < 16; ++e) pk[e] = pack_bf16(x[c * 32 + 2 * e], x[c * 32 + 2 * e + 1]);
+                tmem_st16(tP + c * 16, pk);
+            }
+            tmem_wait_st();
+            tc_fence_before();
+            mbar_arrive(p_full);
+        }
+        // epilogue: O / l -> bf16, lse
+        __nv_bfloat16 *orow = p.out + (int64_t)h * p.o_sh + (int64_t)i * p.o_st;
+        const float inv = (l > 0.f) ? 1.f / l : 0.f;
+        bool have_o = false;
+        if (alive && n > 0) {
+            have_o = warp_wait(o_done, (n - 1) & 1);
+            if (!have_o) give_up();
+            tc_fence_after();
+        }
+#pragma unroll
+        for (int c = 0; c < HD / 16; ++c) {
+            uint32_t o[16];
+            if (have_o) {
+                tmem_ld16(tO + c * 16, o);
+                tmem_wait_ld();
+            } else {
+#pragma unroll
+                for (int e = 0; e < 16; ++e) o[e] = 0u;
+            }
+            uint32_t w[8];
+#pragma unroll
+            for (int e = 0; e < 8; ++e)
+                w[e] = pack_bf16(__uint_as_float(o[2 * e]) * inv, __uint_as_float(o[2 * e + 1]) * inv);
+            uint4 *dst = reinterpret_cast<uint4 *>(orow + c * 16);
+            dst[0] = make_uint4(w[0], w[1], w[2], w[3]);
+            dst[1] = make_uint4(w[4], w[5], w[6], w[7]);
+        }
+        if (p.lse)
+            p.lse[(int64_t)h * p.T + i] = (l > 0.f) ? (m + log2f(l)) * 0.69314718055994531f : -INFINITY;
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem, kTmemCols);
+    }
+}
+
+}  // namespace tcfwd
+
+// ---------------------------------------------------------------------------
+// host side: tensor maps and launch
+// ---------------------------------------------------------------------------
+namespace tchost {
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
+                                  const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+    static EncodeTiledFn fn = nullptr;
+    if (!fn) {
+        void *f = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiledFn>(f);
+    }
+    return fn;
+}
+
+CUtensorMapSwizzle swizzle_for(int row_bytes) {
+    return row_bytes == 128 ? CU_TENSOR_MAP_SWIZZLE_128B
+                            : (row_bytes == 64 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_32B);
+}
+
+// [H][T][inner] bf16 tensor with element strides (sh, st), box (box_inner, 128, 1)
+bool map3d(CUtensorMap *m, const void *base, int inner, int T, int H, int64_t st, int64_t sh, int box_inner) {
+    cuuint64_t dims[3] = {(cuuint64_t)inner, (cuuint64_t)T, (cuuint64_t)H};
+    cuuint64_t strides[2] = {(cuuint64_t)(st * 2), (cuuint64_t)(sh * 2)};
+    cuuint32_t box[3] = {(cuuint32_t)box_inner, 128u, 1u};
+    cuuint32_t es[3] = {1, 1, 1};
+    return encode_fn()(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void *>(base), dims, strides, box, es,
+                       CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle_for(box_inner * 2), CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                       CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+// [T][inner] bf16, box (box_inner, 128)
+bool map2d(CUtensorMap *m, const void *base, int inner, int T, int box_inner) {
+    cuuint64_t dims[2] = {(cuuint64_t)inner, (cuuint64_t)T};
+    cuuint64_t strides[1] = {(cuuint64_t)inner * 2};
+    cuuint32_t box[2] = {(cuuint32_t)box_inner, 128u};
+    cuuint32_t es[2] = {1, 1};
+    return encode_fn()(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void *>(base), dims, strides, box, es,
+                       CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle_for(box_inner * 2), CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                       CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
+template <int DA>
+int launch_fwd(const ScopeAttnArgs &a, cudaStream_t s) {
+    using L = tcfwd::Layout<DA>;
+    constexpr int A1 = tcfwd::Aug<DA>::A1, A2 = tcfwd::Aug<DA>::A2;
+    tcfwd::Maps maps;
+    std::memset(&maps, 0, sizeof(maps));
+    bool ok = map3d(&maps.q, a.q, 64, a.T, a.H, a.q_st, a.q_sh, 64) &&
+              map3d(&maps.k, a.k, 64, a.T, a.H, a.k_st, a.k_sh, 64) &&
+              map3d(&maps.v, a.v, 64, a.T, a.H, a.v_st, a.v_sh, 64);
+    if (A1) ok = ok && map3d(&maps.qa1, a.q_aug, DA, a.T, a.H, DA, (int64_t)a.T * DA, A1) &&
+                 map2d(&maps.ka1, a.k_aug, DA, a.T, A1);
+    if (A2) ok = ok && map3d(&maps.qa2, a.q_aug, DA, a.T, a.H, DA, (int64_t)a.T * DA, A2) &&
+                 map2d(&maps.ka2, a.k_aug, DA, a.T, A2);
+    if (!ok) return SCOPE_ERR_ALIGN;
+    tcfwd::FwdParams p;
+    p.H = a.H;
+    p.T = a.T;
+    p.QB = a.T / 128;
+    p.kv_stride = a.kv_stride;
+    p.kv_num = a.kv_num;
+    p.kv_idx = a.kv_indices;
+    p.block_info = a.block_info;
+    p.docs = a.docs;
+    p.scale_log2 = a.scale * 1.4426950408889634f;
+    p.out = reinterpret_cast<__nv_bfloat16 *>(a.out);
+    p.o_sh = a.o_sh;
+    p.o_st = a.o_st;
+    p.lse = a.lse;
+    p.err = a.err_flag;
+    const size_t smem = L::TOTAL + 1024;
+    if (cudaFuncSetAttribute(tcfwd::fwd_kernel<DA>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
+        cudaSuccess)
+        return SCOPE_ERR_CUDA;
+    dim3 grid(p.QB, a.H);
+    tcfwd::fwd_kernel<DA><<<grid, tcfwd::kThreads, smem, s>>>(maps, p);
+    SCOPE_CHECK_LAUNCH();
+    return SCOPE_OK;
+}
+
+}  // namespace tchost
+}  // namespace scope
+
+using namespace scope;
+
+bool scope_tc_eligible(const ScopeAttnArgs &a, bool bwd) {
+    if (bwd) return false;   // the tensor-core backward is not enabled yet
+    if (a.dtype != SCOPE_BF16 || a.block_size != 128 || a.D != 64) return false;
+    if (a.bias_mode == SCOPE_BIAS_SCORE_MOD) return false;
+    if (a.bias_mode == SCOPE_BIAS_QK_AUG && a.d_aug != 16 && a.d_aug != 32 && a.d_aug != 48 && a.d_aug != 64)
+        return false;
+    if (!scope_device_supported() || !tchost::encode_fn()) return false;
+    // TMA: 16-byte aligned bases and strides; the epilogue writes 16-byte vectors
+    const void *ptrs[4] = {a.q, a.k, a.v, a.out};
+    for (const void *q : ptrs)
+        if (!tchost::aligned16(q)) return false;
+    const int64_t strides[8] = {a.q_sh, a.q_st, a.k_sh, a.k_st, a.v_sh, a.v_st, a.o_sh, a.o_st};
+    for (int64_t st : strides)
+        if (st % 8) return false;
+    if (a.bias_mode == SCOPE_BIAS_QK_AUG && (!tchost::aligned16(a.q_aug) || !tchost::aligned16(a.k_aug))) return false;
+    return true;
+}
+
+int scope_tc_fwd(const ScopeAttnArgs &a, cudaStream_t s) {
+    switch (a.bias_mode == SCOPE_BIAS_QK_AUG ? a.d_aug : 0) {
+        case 0: return tchost::launch_fwd<0>(a, s);
+        case 16: return tchost::launch_fwd<16>(a, s);
+        case 32: return tchost::launch_fwd<32>(a, s);
+        case 48: return tchost::launch_fwd<48>(a, s);
+        case 64: return tchost::launch_fwd<64>(a, s);
+        default: return SCOPE_ERR_INVALID;
+    }
+}
+
 int scope_tc_bwd(const ScopeAttnArgs &, cudaStream_t) { return SCOPE_ERR_UNSUPPORTED; }

@@ -67,7 +67,7 @@ extern "C" int scope_attn_fwd(const ScopeAttnArgs *args, scope_stream_t stream) 
     int st = validate(*args, false);
     if (st) return st;
     cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-    if (scope_tc_eligible(*args, false)) return scope_tc_fwd(*args, s);
+    if (!(args->flags & SCOPE_FLAG_CUDA_CORES) && scope_tc_eligible(*args, false)) return scope_tc_fwd(*args, s);
     if (args->block_size > 128) return SCOPE_ERR_UNSUPPORTED;
     return scope_simt_fwd(*args, s);
 }
@@ -77,7 +77,7 @@ extern "C" int scope_attn_bwd(const ScopeAttnArgs *args, scope_stream_t stream) 
     int st = validate(*args, true);
     if (st) return st;
     cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-    if (scope_tc_eligible(*args, true)) return scope_tc_bwd(*args, s);
+    if (!(args->flags & SCOPE_FLAG_CUDA_CORES) && scope_tc_eligible(*args, true)) return scope_tc_bwd(*args, s);
     if (args->block_size > 128) return SCOPE_ERR_UNSUPPORTED;
     return scope_simt_bwd(*args, s);
 }

@@ -242,6 +242,7 @@ def build_mask(*, H: int, T: int, block_size: int, M: int, device,
     a.q_bitmap = qbm.data_ptr()
     a.r_m_out, a.centres_out = _lib.ptr(r_m), _lib.ptr(cen)
     a.stats = _lib.ptr(st_t)
+    a.err_flag = _lib.err_word_ptr(dev)
     st = _lib.lib().scope_mask_build(ctypes.byref(a), _stream(dev))
     _lib.check(st, "scope_mask_build")
     d = None if docs is None else docs.to(device=dev, dtype=torch.int32)
