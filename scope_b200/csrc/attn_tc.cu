@@ -160,9 +160,9 @@ __global__ void __launch_bounds__(kThreads, 2) fwd_kernel(const __grid_constant_
                 issued = j + 1;
             }
             // never leave the CTA with a TMA write still in flight
-            mbar_wait(q_full, 0, 1u << 20);
+            mbar_wait(q_full, 0, 500000000ull);
             for (int j = (issued > 2 ? issued - 2 : 0); j < issued; ++j)
-                mbar_wait(kv_full + (j & 1), (j >> 1) & 1, 1u << 20);
+                mbar_wait(kv_full + (j & 1), (j >> 1) & 1, 500000000ull);
         }
     } else if (warp == 1) {
         // ------------------------------------------------------------ tcgen05 issuer

@@ -40,10 +40,9 @@ template <> struct Elem<__nv_bfloat16> {
 
 inline int ceil_div(int a, int b) { return (a + b - 1) / b; }
 
-// Upper bound on iterations of any spin on an mbarrier or flag.  A wait that
-// reaches it records SCOPE_DEVERR_TIMEOUT and the kernel winds down instead of
-// hanging the GPU.  try_wait suspends for a hardware-chosen interval per
-// attempt, so this is several seconds of real time.
-constexpr uint32_t kSpinLimit = 1u << 22;
+// Upper bound on the wall time of any wait on an mbarrier or flag.  A wait
+// that reaches it records SCOPE_DEVERR_TIMEOUT and the kernel winds down
+// instead of hanging the GPU.
+constexpr uint64_t kWaitLimitNs = 2000000000ull;   // 2 s
 
 }  // namespace scope

@@ -44,13 +44,21 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t addr, uint32_t parity) {
         : "memory");
     return ok != 0;
 }
-// Wait for the phase with the given parity to complete, at most `limit`
-// attempts.  Returns false when the wait gave up.
-__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, uint32_t limit = kSpinLimit) {
+__device__ __forceinline__ uint64_t globaltimer_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+// Wait for the phase with the given parity to complete, for at most
+// `limit_ns` nanoseconds of wall time.  Returns false when the wait gave up.
+__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, uint64_t limit_ns = kWaitLimitNs) {
     const uint32_t a = smem_u32(bar);
-    for (uint32_t i = 0; i < limit; ++i)
+    if (mbar_try_wait(a, parity)) return true;
+    const uint64_t t0 = globaltimer_ns();
+    for (uint32_t i = 1;; ++i) {
         if (mbar_try_wait(a, parity)) return true;
-    return false;
+        if ((i & 63u) == 0 && globaltimer_ns() - t0 > limit_ns) return false;
+    }
 }
 
 // ---------------------------------------------------------------- TMA
