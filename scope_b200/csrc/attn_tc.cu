@@ -45,30 +45,24 @@ constexpr uint32_t S_COL = 0, O_COL = 128, P_COL = 192;
 
 __host__ __device__ constexpr uint32_t align1k(uint32_t x) { return (x + 1023u) & ~1023u; }
 
-// qk_aug dims are staged as at most two sub-tiles whose rows match a swizzle
-// span (16 -> 16, 32 -> 32, 48 -> 32 + 16, 64 -> 64 bf16 columns)
-template <int DA>
-struct Aug {
-    static constexpr int A1 = (DA == 48) ? 32 : DA;
-    static constexpr int A2 = DA - A1;
-};
-
+// qk_aug dims are staged as DA/16 sub-tiles of 16 bf16 columns (32-byte rows,
+// 32-byte swizzle), one MMA K-step each, so every aug width 16..64 uses the
+// same layout.
 template <int DA>
 struct Layout {
+    static constexpr int NA = DA / 16;                           // aug sub-tiles
     static constexpr uint32_t TILE = BM * HD * 2;                // 16 KiB
-    static constexpr uint32_t AUG1 = BM * Aug<DA>::A1 * 2;
-    static constexpr uint32_t AUG2 = BM * Aug<DA>::A2 * 2;
+    static constexpr uint32_t ATILE = BM * 16 * 2;               // 4 KiB
     static constexpr uint32_t Q = 0;
-    static constexpr uint32_t QA1 = TILE;
-    static constexpr uint32_t QA2 = QA1 + AUG1;
-    static constexpr uint32_t STAGE0 = align1k(QA2 + AUG2);
-    static constexpr uint32_t K = 0, KA1 = TILE, KA2 = TILE + AUG1;
-    static constexpr uint32_t V = align1k(TILE + AUG1 + AUG2);
+    static constexpr uint32_t QA = TILE;                         // + a * ATILE
+    static constexpr uint32_t STAGE0 = align1k(QA + NA * ATILE);
+    static constexpr uint32_t K = 0, KA = TILE;                  // + a * ATILE
+    static constexpr uint32_t V = align1k(TILE + NA * ATILE);
     static constexpr uint32_t STAGE = V + TILE;
     static constexpr uint32_t BAR = STAGE0 + 2 * STAGE;
     static constexpr uint32_t TOTAL = BAR + 128;
-    static constexpr uint32_t KV_BYTES = 2 * TILE + AUG1 + AUG2;  // expected TMA bytes per stage
-    static constexpr uint32_t Q_BYTES = TILE + AUG1 + AUG2;
+    static constexpr uint32_t KV_BYTES = 2 * TILE + NA * ATILE;  // expected TMA bytes per stage
+    static constexpr uint32_t Q_BYTES = TILE + NA * ATILE;
 };
 
 struct FwdParams {
@@ -82,13 +76,13 @@ struct FwdParams {
 };
 
 struct Maps {
-    CUtensorMap q, k, v, qa1, qa2, ka1, ka2;
+    CUtensorMap q, k, v, qa, ka;   // qa / ka: 16-column boxes of the qk_aug dims
 };
 
 template <int DA>
 __global__ void __launch_bounds__(kThreads, 2) fwd_kernel(const __grid_constant__ Maps maps, const FwdParams p) {
     using L = Layout<DA>;
-    constexpr int A1 = Aug<DA>::A1, A2 = Aug<DA>::A2;
+    constexpr int NA = L::NA;
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
     uint64_t *bars = reinterpret_cast<uint64_t *>(smem + L::BAR);
@@ -140,8 +134,8 @@ __global__ void __launch_bounds__(kThreads, 2) fwd_kernel(const __grid_constant_
         if (lane == 0 && n > 0) {
             mbar_expect_tx(q_full, L::Q_BYTES);
             tma_load_3d(&maps.q, smem + L::Q, q_full, 0, qb * BM, h);
-            if (A1) tma_load_3d(&maps.qa1, smem + L::QA1, q_full, 0, qb * BM, h);
-            if (A2) tma_load_3d(&maps.qa2, smem + L::QA2, q_full, A1, qb * BM, h);
+#pragma unroll
+            for (int a = 0; a < NA; ++a) tma_load_3d(&maps.qa, smem + L::QA + a * L::ATILE, q_full, 16 * a, qb * BM, h);
             int issued = 0;
             for (int j = 0; j < n; ++j) {
                 const int s = j & 1;
@@ -154,8 +148,8 @@ __global__ void __launch_bounds__(kThreads, 2) fwd_kernel(const __grid_constant_
                 uint8_t *st = smem + L::STAGE0 + s * L::STAGE;
                 mbar_expect_tx(kv_full + s, L::KV_BYTES);
                 tma_load_3d(&maps.k, st + L::K, kv_full + s, 0, kb * BM, h);
-                if (A1) tma_load_2d(&maps.ka1, st + L::KA1, kv_full + s, 0, kb * BM);
-                if (A2) tma_load_2d(&maps.ka2, st + L::KA2, kv_full + s, A1, kb * BM);
+#pragma unroll
+                for (int a = 0; a < NA; ++a) tma_load_2d(&maps.ka, st + L::KA + a * L::ATILE, kv_full + s, 16 * a, kb * BM);
                 tma_load_3d(&maps.v, st + L::V, kv_full + s, 0, kb * BM, h);
                 issued = j + 1;
             }
@@ -182,13 +176,9 @@ __global__ void __launch_bounds__(kThreads, 2) fwd_kernel(const __grid_constant_
                     mma_ss(tS, kmajor_desc(sq + L::Q + kk * 32, 128), kmajor_desc(sk + L::K + kk * 32, 128), idS,
                            kk > 0);
 #pragma unroll
-                for (int kk = 0; kk < A1 / 16; ++kk)
-                    mma_ss(tS, kmajor_desc(sq + L::QA1 - L::Q + kk * 32, A1 * 2),
-                           kmajor_desc(sk + L::KA1 + kk * 32, A1 * 2), idS, 1);
-#pragma unroll
-                for (int kk = 0; kk < A2 / 16; ++kk)
-                    mma_ss(tS, kmajor_desc(sq + L::QA2 - L::Q + kk * 32, A2 * 2),
-                           kmajor_desc(sk + L::KA2 + kk * 32, A2 * 2), idS, 1);
+                for (int a = 0; a < NA; ++a)
+                    mma_ss(tS, kmajor_desc(sq + L::QA + a * L::ATILE, 32), kmajor_desc(sk + L::KA + a * L::ATILE, 32),
+                           idS, 1);
                 tc_commit(s_full);
                 return true;
             };
@@ -390,16 +380,13 @@ bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 
 template <int DA>
 int launch_fwd(const ScopeAttnArgs &a, cudaStream_t s) {
     using L = tcfwd::Layout<DA>;
-    constexpr int A1 = tcfwd::Aug<DA>::A1, A2 = tcfwd::Aug<DA>::A2;
     tcfwd::Maps maps;
     std::memset(&maps, 0, sizeof(maps));
     bool ok = map3d(&maps.q, a.q, 64, a.T, a.H, a.q_st, a.q_sh, 64) &&
               map3d(&maps.k, a.k, 64, a.T, a.H, a.k_st, a.k_sh, 64) &&
               map3d(&maps.v, a.v, 64, a.T, a.H, a.v_st, a.v_sh, 64);
-    if (A1) ok = ok && map3d(&maps.qa1, a.q_aug, DA, a.T, a.H, DA, (int64_t)a.T * DA, A1) &&
-                 map2d(&maps.ka1, a.k_aug, DA, a.T, A1);
-    if (A2) ok = ok && map3d(&maps.qa2, a.q_aug, DA, a.T, a.H, DA, (int64_t)a.T * DA, A2) &&
-                 map2d(&maps.ka2, a.k_aug, DA, a.T, A2);
+    if (DA) ok = ok && map3d(&maps.qa, a.q_aug, DA, a.T, a.H, DA, (int64_t)a.T * DA, 16) &&
+                 map2d(&maps.ka, a.k_aug, DA, a.T, 16);
     if (!ok) return SCOPE_ERR_ALIGN;
     tcfwd::FwdParams p;
     p.H = a.H;

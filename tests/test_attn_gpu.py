@@ -136,9 +136,12 @@ def test_forward_backward_matches_oracle(name, dtype):
     assert _maxabs(res["lse"], ref["lse"]) < tol
     for n in ("dq", "dk", "dv"):
         assert _maxabs(res[n], ref[n][..., :64]) < tol, n
+    # gradients of the captured bias tensors: the bound is relative to each
+    # tensor's own scale (dslope sums dS * delta over hundreds of positions)
     for n in ("dcoeff_cos", "dcoeff_sin", "db0", "dslope", "ddelta_main", "dwidth"):
         if n in res:
-            assert _maxabs(res[n], ref[n]) < tol, n
+            scale = max(1.0, ref[n].abs().max().item())
+            assert _maxabs(res[n], ref[n]) < tol * scale, (n, _maxabs(res[n], ref[n]), scale)
 
 
 def test_bias_off_and_causal_only():
