@@ -30,6 +30,7 @@
 #include <cmath>
 #include <cstring>
 
+#include "tc_host.cuh"
 #include "tc_ptx.cuh"
 
 namespace scope {
@@ -265,7 +266,8 @@ __global__ void __launch_bounds__(kThreads, 2) fwd_kernel(const __grid_constant_
             if (j > 0) {
                 if (!warp_wait(o_done, (j - 1) & 1)) { give_up(); alive = false; break; }
                 tc_fence_after();
-                if (rescale) {
+                // tcgen05.ld/st are warp-collective: rescale O whenever any row of the warp needs it
+                if (__any_sync(0xffffffffu, rescale)) {
 #pragma unroll
                     for (int c = 0; c < HD / 16; ++c) {
                         uint32_t o[16];
@@ -333,50 +335,6 @@ __global__ void __launch_bounds__(kThreads, 2) fwd_kernel(const __grid_constant_
 // ---------------------------------------------------------------------------
 namespace tchost {
 
-typedef CUresult (*EncodeTiledFn)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
-                                  const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
-                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
-
-EncodeTiledFn encode_fn() {
-    static EncodeTiledFn fn = nullptr;
-    if (!fn) {
-        void *f = nullptr;
-        cudaDriverEntryPointQueryResult q;
-        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) == cudaSuccess &&
-            q == cudaDriverEntryPointSuccess)
-            fn = reinterpret_cast<EncodeTiledFn>(f);
-    }
-    return fn;
-}
-
-CUtensorMapSwizzle swizzle_for(int row_bytes) {
-    return row_bytes == 128 ? CU_TENSOR_MAP_SWIZZLE_128B
-                            : (row_bytes == 64 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_32B);
-}
-
-// [H][T][inner] bf16 tensor with element strides (sh, st), box (box_inner, 128, 1)
-bool map3d(CUtensorMap *m, const void *base, int inner, int T, int H, int64_t st, int64_t sh, int box_inner) {
-    cuuint64_t dims[3] = {(cuuint64_t)inner, (cuuint64_t)T, (cuuint64_t)H};
-    cuuint64_t strides[2] = {(cuuint64_t)(st * 2), (cuuint64_t)(sh * 2)};
-    cuuint32_t box[3] = {(cuuint32_t)box_inner, 128u, 1u};
-    cuuint32_t es[3] = {1, 1, 1};
-    return encode_fn()(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void *>(base), dims, strides, box, es,
-                       CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle_for(box_inner * 2), CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                       CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
-}
-// [T][inner] bf16, box (box_inner, 128)
-bool map2d(CUtensorMap *m, const void *base, int inner, int T, int box_inner) {
-    cuuint64_t dims[2] = {(cuuint64_t)inner, (cuuint64_t)T};
-    cuuint64_t strides[1] = {(cuuint64_t)inner * 2};
-    cuuint32_t box[2] = {(cuuint32_t)box_inner, 128u};
-    cuuint32_t es[2] = {1, 1};
-    return encode_fn()(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void *>(base), dims, strides, box, es,
-                       CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle_for(box_inner * 2), CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                       CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
-}
-
-bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
-
 template <int DA>
 int launch_fwd(const ScopeAttnArgs &a, cudaStream_t s) {
     using L = tcfwd::Layout<DA>;
@@ -419,20 +377,20 @@ int launch_fwd(const ScopeAttnArgs &a, cudaStream_t s) {
 using namespace scope;
 
 bool scope_tc_eligible(const ScopeAttnArgs &a, bool bwd) {
-    if (bwd) return false;   // the tensor-core backward is not enabled yet
     if (a.dtype != SCOPE_BF16 || a.block_size != 128 || a.D != 64) return false;
     if (a.bias_mode == SCOPE_BIAS_SCORE_MOD) return false;
     if (a.bias_mode == SCOPE_BIAS_QK_AUG && a.d_aug != 16 && a.d_aug != 32 && a.d_aug != 48 && a.d_aug != 64)
         return false;
     if (!scope_device_supported() || !tchost::encode_fn()) return false;
-    // TMA: 16-byte aligned bases and strides; the epilogue writes 16-byte vectors
-    const void *ptrs[4] = {a.q, a.k, a.v, a.out};
-    for (const void *q : ptrs)
-        if (!tchost::aligned16(q)) return false;
-    const int64_t strides[8] = {a.q_sh, a.q_st, a.k_sh, a.k_st, a.v_sh, a.v_st, a.o_sh, a.o_st};
-    for (int64_t st : strides)
-        if (st % 8) return false;
+    // TMA: 16-byte aligned bases and strides; epilogues write 16-byte vectors
+    const void *ptrs[8] = {a.q, a.k, a.v, a.out, a.dout, a.dq, a.dk, a.dv};
+    const int64_t strides[16] = {a.q_sh, a.q_st, a.k_sh, a.k_st, a.v_sh, a.v_st, a.o_sh, a.o_st,
+                                 a.do_sh, a.do_st, a.dq_sh, a.dq_st, a.dk_sh, a.dk_st, a.dv_sh, a.dv_st};
+    const int n = bwd ? 8 : 4;
+    for (int i = 0; i < n; ++i)
+        if (!tchost::aligned16(ptrs[i]) || strides[2 * i] % 8 || strides[2 * i + 1] % 8) return false;
     if (a.bias_mode == SCOPE_BIAS_QK_AUG && (!tchost::aligned16(a.q_aug) || !tchost::aligned16(a.k_aug))) return false;
+    if (bwd && (!a.q_bitmap || !a.lse)) return false;
     return true;
 }
 
@@ -447,4 +405,3 @@ int scope_tc_fwd(const ScopeAttnArgs &a, cudaStream_t s) {
     }
 }
 
-int scope_tc_bwd(const ScopeAttnArgs &, cudaStream_t) { return SCOPE_ERR_UNSUPPORTED; }

@@ -1,0 +1,679 @@
+// Block-sparse SCOPE attention backward on the sm_100a tensor cores.
+//
+// Three launches, all on the caller's stream:
+//   prep   delta_i = sum_d dO_i . O_i  and  lse2_i = lse_i * log2(e)   (workspace)
+//   dkv    one CTA per (head, kv block): walks the q blocks that see this kv
+//          block (the builder's q-side bitmap, ascending) and accumulates
+//          dV += P^T dO and dK += dS^T Q in TMEM.
+//   dq     one CTA per (head, q block): walks the kv list like the forward and
+//          accumulates dQ += dS K (and, for the qk_aug spectral bias, the
+//          gradient of the augmented dims, turned into dcoeff_cos /
+//          dcoeff_sin / dslope in the epilogue by the chain rule of
+//          scoped_medium.py:380-421).
+// dQ is computed by its own kernel rather than with atomics so every output
+// is written once, deterministically.
+//
+// Both kernels share one pipeline.  A 128x128 tile is processed as two
+// halves of 64 columns.  TMEM (512 columns, one CTA per SM) holds two slots of
+// {S half, dP half} (fp32, 64 + 64 columns) and the accumulators.  While the
+// four elementwise warps turn slot u into P / dS (bf16, written back over the
+// first 32 columns of the slot's S and dP halves, where the next MMAs read them
+// as their A operand), the issuer runs the QK^T / dO V^T MMAs of slot u+1 and
+// the gradient MMAs of slot u-1.  Every wait is bounded (SCOPE_DEVERR_TIMEOUT).
+#include <cmath>
+#include <cstring>
+
+#include "tc_host.cuh"
+#include "tc_ptx.cuh"
+
+namespace scope {
+namespace tcbwd {
+
+using namespace tc;
+
+constexpr int BM = 128;
+constexpr int HD = 64;
+constexpr int kThreads = 192;
+constexpr uint32_t kTmemCols = 512;
+constexpr uint32_t ACC0 = 256, ACC1 = 320;   // dV / dK   or   dQ / dQaug
+constexpr float kLog2e = 1.4426950408889634f;
+
+__host__ __device__ constexpr uint32_t align1k(uint32_t x) { return (x + 1023u) & ~1023u; }
+__device__ __forceinline__ uint32_t slot_s(int half) { return (uint32_t)half * 128u; }
+__device__ __forceinline__ uint32_t slot_dp(int half) { return (uint32_t)half * 128u + 64u; }
+
+// ------------------------------------------------------------------ prep
+__global__ void prep_kernel(const __nv_bfloat16 *__restrict__ out, int64_t o_sh, int64_t o_st,
+                            const __nv_bfloat16 *__restrict__ dout, int64_t do_sh, int64_t do_st,
+                            const float *__restrict__ lse, int H, int T, float *__restrict__ delta,
+                            float *__restrict__ lse2) {
+    int64_t row = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (row >= (int64_t)H * T) return;
+    const int h = (int)(row / T), t = (int)(row % T);
+    const uint4 *o = reinterpret_cast<const uint4 *>(out + h * o_sh + (int64_t)t * o_st);
+    const uint4 *d = reinterpret_cast<const uint4 *>(dout + h * do_sh + (int64_t)t * do_st);
+    float s = 0.f;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+        uint4 a = o[k], b = d[k];
+        const __nv_bfloat162 *pa = reinterpret_cast<const __nv_bfloat162 *>(&a);
+        const __nv_bfloat162 *pb = reinterpret_cast<const __nv_bfloat162 *>(&b);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            float2 fa = __bfloat1622float2(pa[e]), fb = __bfloat1622float2(pb[e]);
+            s = fmaf(fa.x, fb.x, s);
+            s = fmaf(fa.y, fb.y, s);
+        }
+    }
+    delta[row] = s;
+    const float l = lse[row];
+    lse2[row] = (l == -INFINITY) ? INFINITY : l * kLog2e;   // rows that saw nothing get P = 0
+}
+
+struct Params {
+    int H, T, QB, words, kv_stride;
+    const uint32_t *q_bitmap;
+    const int32_t *kv_num, *kv_idx;
+    const int32_t *block_info, *docs;
+    const float *lse2, *delta;
+    float scale, scale_log2;
+    __nv_bfloat16 *g0, *g1;           // dkv: dK, dV      dq: dQ, (unused)
+    int64_t g0_sh, g0_st, g1_sh, g1_st;
+    // dq epilogue for the qk_aug bias
+    int K, has_slope, tab_len;
+    const uint16_t *cos_tab, *sin_tab;
+    float s_aug;
+    float *dcoeff_cos, *dcoeff_sin, *dslope;
+    int32_t *err;
+};
+
+struct Maps {
+    CUtensorMap q, k, v, dout, qa, ka;
+};
+
+// helpers shared by both kernels ------------------------------------------------
+struct Ctx {
+    uint8_t *smem;
+    uint32_t tmem;
+    volatile int *abort_flag;
+    int32_t *err;
+    __device__ void give_up() {
+        *abort_flag = 1;
+        set_err(err, SCOPE_DEVERR_TIMEOUT);
+    }
+    __device__ bool wait1(uint64_t *bar, uint32_t parity) {      // single thread
+        if (*abort_flag) return false;
+        if (mbar_wait(bar, parity)) return true;
+        give_up();
+        return false;
+    }
+    __device__ bool waitw(uint64_t *bar, uint32_t parity) {      // a whole warp, uniform result
+        bool ok = !*abort_flag && mbar_wait(bar, parity);
+        ok = __all_sync(0xffffffffu, ok);
+        if (!ok) give_up();
+        return ok;
+    }
+};
+
+// load the 64 fp32 columns at taddr (one TMEM lane per thread)
+__device__ __forceinline__ void ld64(uint32_t taddr, float (&x)[64]) {
+    uint32_t u[32];
+    tmem_ld32(taddr, u);
+    tmem_wait_ld();
+#pragma unroll
+    for (int e = 0; e < 32; ++e) x[e] = __uint_as_float(u[e]);
+    tmem_ld32(taddr + 32, u);
+    tmem_wait_ld();
+#pragma unroll
+    for (int e = 0; e < 32; ++e) x[32 + e] = __uint_as_float(u[e]);
+}
+// store 64 values as 32 bf16 pairs at taddr
+__device__ __forceinline__ void st_bf16x64(uint32_t taddr, const float (&x)[64]) {
+    uint32_t pk[32];
+#pragma unroll
+    for (int e = 0; e < 32; ++e) pk[e] = pack_bf16(x[2 * e], x[2 * e + 1]);
+    tmem_st32(taddr, pk);
+}
+// 64 fp32 accumulator columns -> one bf16 row of 128 bytes in global memory
+__device__ __forceinline__ void store_row(uint32_t taddr, float mul, __nv_bfloat16 *dst, bool have) {
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+        uint32_t o[16];
+        if (have) {
+            tmem_ld16(taddr + c * 16, o);
+            tmem_wait_ld();
+        } else {
+#pragma unroll
+            for (int e = 0; e < 16; ++e) o[e] = 0u;
+        }
+        uint32_t w[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e)
+            w[e] = pack_bf16(__uint_as_float(o[2 * e]) * mul, __uint_as_float(o[2 * e + 1]) * mul);
+        uint4 *d = reinterpret_cast<uint4 *>(dst + c * 16);
+        d[0] = make_uint4(w[0], w[1], w[2], w[3]);
+        d[1] = make_uint4(w[4], w[5], w[6], w[7]);
+    }
+}
+
+// ============================================================================ dK / dV
+template <int DA>
+struct KVL {
+    static constexpr int NA = DA / 16;
+    static constexpr uint32_t TILE = BM * HD * 2, ATILE = BM * 16 * 2;
+    static constexpr uint32_t K = 0, KA = TILE, V = align1k(TILE + NA * ATILE);
+    static constexpr uint32_t STAGE0 = V + TILE;
+    static constexpr uint32_t SQ = 0, SQA = TILE, SDO = align1k(TILE + NA * ATILE), SLSE = SDO + TILE,
+                              SDEL = SLSE + 512;
+    static constexpr uint32_t STAGE = align1k(SDEL + 512);
+    static constexpr uint32_t BAR = STAGE0 + 2 * STAGE;
+    static constexpr uint32_t TOTAL = BAR + 256;
+    static constexpr uint32_t RES_BYTES = 2 * TILE + NA * ATILE;
+    static constexpr uint32_t Q_BYTES = 2 * TILE + NA * ATILE + 1024;
+};
+
+template <int DA>
+__global__ void __launch_bounds__(kThreads, 1) dkv_kernel(const __grid_constant__ Maps maps, const Params p) {
+    using L = KVL<DA>;
+    constexpr int NA = L::NA;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
+    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + L::BAR);
+    uint64_t *kv_full = bars + 0, *q_full = bars + 1, *q_empty = bars + 3, *sdp_full = bars + 5, *p_full = bars + 7,
+             *acc_done = bars + 9;
+    volatile int *stage_qb = reinterpret_cast<volatile int *>(bars + 10);
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 11);
+    Ctx cx{smem, 0, reinterpret_cast<volatile int *>(tmem_slot + 1), p.err};
+
+    const int kb = blockIdx.x, h = blockIdx.y;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t *brow = p.q_bitmap + ((int64_t)h * p.QB + kb) * p.words;
+    int nq = 0;
+    for (int w = 0; w < p.words; ++w) nq += __popc(brow[w]);
+
+    if (threadIdx.x == 0) {
+        mbar_init(kv_full, 1);
+        for (int i = 0; i < 2; ++i) {
+            mbar_init(q_full + i, 1);
+            mbar_init(q_empty + i, 1);
+            mbar_init(sdp_full + i, 1);
+            mbar_init(p_full + i, 128);
+        }
+        mbar_init(acc_done, 1);
+        *cx.abort_flag = 0;
+        fence_mbar_init();
+    }
+    if (warp == 1) {
+        tmem_alloc(tmem_slot, kTmemCols);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+    cx.tmem = tmem;
+
+    if (warp == 0) {
+        if (lane == 0 && nq > 0) {
+            mbar_expect_tx(kv_full, L::RES_BYTES);
+            tma_load_3d(&maps.k, smem + L::K, kv_full, 0, kb * BM, h);
+#pragma unroll
+            for (int a = 0; a < NA; ++a) tma_load_2d(&maps.ka, smem + L::KA + a * L::ATILE, kv_full, 16 * a, kb * BM);
+            tma_load_3d(&maps.v, smem + L::V, kv_full, 0, kb * BM, h);
+            int t = 0;
+            bool ok = true;
+            for (int w = 0; w < p.words && ok; ++w) {
+                uint32_t bits = brow[w];
+                while (bits) {
+                    const int qb = w * 32 + __ffs(bits) - 1;
+                    bits &= bits - 1;
+                    const int st = t & 1;
+                    if (t >= 2 && !cx.wait1(q_empty + st, ((t >> 1) - 1) & 1)) {
+                        ok = false;
+                        break;
+                    }
+                    uint8_t *sb = smem + L::STAGE0 + st * L::STAGE;
+                    stage_qb[st] = qb;
+                    mbar_expect_tx(q_full + st, L::Q_BYTES);
+                    tma_load_3d(&maps.q, sb + L::SQ, q_full + st, 0, qb * BM, h);
+#pragma unroll
+                    for (int a = 0; a < NA; ++a)
+                        tma_load_3d(&maps.qa, sb + L::SQA + a * L::ATILE, q_full + st, 16 * a, qb * BM, h);
+                    tma_load_3d(&maps.dout, sb + L::SDO, q_full + st, 0, qb * BM, h);
+                    const int64_t off = (int64_t)h * p.T + (int64_t)qb * BM;
+                    bulk_load(sb + L::SLSE, p.lse2 + off, 512, q_full + st);
+                    bulk_load(sb + L::SDEL, p.delta + off, 512, q_full + st);
+                    ++t;
+                }
+            }
+            mbar_wait(kv_full, 0, 500000000ull);
+            for (int j = (t > 2 ? t - 2 : 0); j < t; ++j) mbar_wait(q_full + (j & 1), (j >> 1) & 1, 500000000ull);
+        }
+    } else if (warp == 1) {
+        if (lane == 0 && nq > 0) {
+            constexpr uint32_t idS = idesc_bf16(128, 64, false, false);
+            constexpr uint32_t idG = idesc_bf16(128, 64, false, true);
+            const uint32_t sK = smem_u32(smem + L::K), sKA = smem_u32(smem + L::KA), sV = smem_u32(smem + L::V);
+            auto grad = [&](int v) -> bool {
+                const int tv = v >> 1, hv = v & 1, stv = tv & 1;
+                if (!cx.wait1(p_full + hv, tv & 1)) return false;
+                tc_fence_after();
+                const uint32_t sb = smem_u32(smem + L::STAGE0 + stv * L::STAGE);
+#pragma unroll
+                for (int kk = 0; kk < 4; ++kk)
+                    mma_ts(tmem + ACC0, tmem + slot_s(hv) + kk * 8, mnmajor128_desc(sb + L::SDO + hv * 8192 + kk * 2048),
+                           idG, (v > 0 || kk > 0) ? 1u : 0u);
+#pragma unroll
+                for (int kk = 0; kk < 4; ++kk)
+                    mma_ts(tmem + ACC1, tmem + slot_dp(hv) + kk * 8, mnmajor128_desc(sb + L::SQ + hv * 8192 + kk * 2048),
+                           idG, (v > 0 || kk > 0) ? 1u : 0u);
+                if (hv == 1) tc_commit(q_empty + stv);
+                return true;
+            };
+            bool ok = cx.wait1(kv_full, 0);
+            const int nu = 2 * nq;
+            for (int u = 0; ok && u < nu; ++u) {
+                const int t = u >> 1, half = u & 1, st = t & 1;
+                if (half == 0 && !cx.wait1(q_full + st, (t >> 1) & 1)) { ok = false; break; }
+                tc_fence_after();
+                const uint32_t sb = smem_u32(smem + L::STAGE0 + st * L::STAGE);
+#pragma unroll
+                for (int kk = 0; kk < 4; ++kk)
+                    mma_ss(tmem + slot_s(half), kmajor_desc(sK + kk * 32, 128),
+                           kmajor_desc(sb + L::SQ + half * 8192 + kk * 32, 128), idS, kk > 0);
+#pragma unroll
+                for (int a = 0; a < NA; ++a)
+                    mma_ss(tmem + slot_s(half), kmajor_desc(sKA + a * L::ATILE, 32),
+                           kmajor_desc(sb + L::SQA + a * L::ATILE + half * 2048, 32), idS, 1);
+#pragma unroll
+                for (int kk = 0; kk < 4; ++kk)
+                    mma_ss(tmem + slot_dp(half), kmajor_desc(sV + kk * 32, 128),
+                           kmajor_desc(sb + L::SDO + half * 8192 + kk * 32, 128), idS, kk > 0);
+                tc_commit(sdp_full + half);
+                if (u >= 1 && !grad(u - 1)) { ok = false; break; }
+            }
+            if (ok) ok = grad(nu - 1);
+            if (ok) tc_commit(acc_done);
+        }
+    } else {
+        const int quad = warp & 3;
+        const int c = quad * 32 + lane;
+        const int j = kb * BM + c;
+        const uint32_t lb = (uint32_t)(quad * 32) << 16;
+        const bool have_docs = p.docs != nullptr;
+        const int doc_j = have_docs ? p.docs[j] : 0;
+        const int32_t *dmin = p.block_info ? p.block_info + 2 * p.QB : nullptr;
+        const int32_t *dmax = p.block_info ? p.block_info + 3 * p.QB : nullptr;
+        const bool kv_uniform = !have_docs || (dmin && dmin[kb] == dmax[kb]);
+        bool alive = true;
+        const int nu = 2 * nq;
+        for (int u = 0; u < nu && alive; ++u) {
+            const int t = u >> 1, half = u & 1, st = t & 1;
+            if (half == 0 && !cx.waitw(q_full + st, (t >> 1) & 1)) { alive = false; break; }
+            const int qb = stage_qb[st];
+            const bool full = qb > kb && (!have_docs || (kv_uniform && dmin[qb] == dmax[qb] && dmin[qb] == dmin[kb]));
+            if (!cx.waitw(sdp_full + half, t & 1)) { alive = false; break; }
+            tc_fence_after();
+            float s[64], dp[64];
+            ld64(tmem + lb + slot_s(half), s);
+            ld64(tmem + lb + slot_dp(half), dp);
+            const uint8_t *sb = smem + L::STAGE0 + st * L::STAGE;
+            const float *LS = reinterpret_cast<const float *>(sb + L::SLSE) + half * 64;
+            const float *DL = reinterpret_cast<const float *>(sb + L::SDEL) + half * 64;
+            const int i0 = qb * BM + half * 64;
+#pragma unroll
+            for (int e = 0; e < 64; ++e) {
+                float pr = ex2(fmaf(s[e], p.scale_log2, -LS[e]));
+                if (!full) {
+                    const int i = i0 + e;
+                    bool valid = j <= i;
+                    if (have_docs) valid = valid && (__ldg(p.docs + i) == doc_j);
+                    if (!valid) pr = 0.f;
+                }
+                dp[e] = pr * (dp[e] - DL[e]);
+                s[e] = pr;
+            }
+            st_bf16x64(tmem + lb + slot_s(half), s);
+            st_bf16x64(tmem + lb + slot_dp(half), dp);
+            tmem_wait_st();
+            tc_fence_before();
+            mbar_arrive(p_full + half);
+        }
+        bool have = false;
+        if (alive && nq > 0) {
+            have = cx.waitw(acc_done, 0);
+            tc_fence_after();
+        }
+        store_row(tmem + lb + ACC0, 1.f, p.g1 + (int64_t)h * p.g1_sh + (int64_t)j * p.g1_st, have);        // dV
+        store_row(tmem + lb + ACC1, p.scale, p.g0 + (int64_t)h * p.g0_sh + (int64_t)j * p.g0_st, have);    // dK
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem, kTmemCols);
+    }
+}
+
+// ============================================================================ dQ
+template <int DA>
+struct QL {
+    static constexpr int NA = DA / 16;
+    static constexpr uint32_t TILE = BM * HD * 2, ATILE = BM * 16 * 2;
+    static constexpr uint32_t Q = 0, QA = TILE, DO = align1k(TILE + NA * ATILE);
+    static constexpr uint32_t STAGE0 = DO + TILE;
+    static constexpr uint32_t SK = 0, SKA = TILE, SV = align1k(TILE + NA * ATILE);
+    static constexpr uint32_t STAGE = SV + TILE;
+    static constexpr uint32_t BAR = STAGE0 + 2 * STAGE;
+    static constexpr uint32_t TOTAL = BAR + 256;
+    static constexpr uint32_t RES_BYTES = 2 * TILE + NA * ATILE;
+    static constexpr uint32_t KV_BYTES = 2 * TILE + NA * ATILE;
+};
+
+template <int DA>
+__global__ void __launch_bounds__(kThreads, 1) dq_kernel(const __grid_constant__ Maps maps, const Params p) {
+    using L = QL<DA>;
+    constexpr int NA = L::NA;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
+    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + L::BAR);
+    uint64_t *res_full = bars + 0, *kv_full = bars + 1, *kv_empty = bars + 3, *sdp_full = bars + 5,
+             *p_full = bars + 7, *acc_done = bars + 9;
+    volatile int *stage_kb = reinterpret_cast<volatile int *>(bars + 10);
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 11);
+    Ctx cx{smem, 0, reinterpret_cast<volatile int *>(tmem_slot + 1), p.err};
+
+    const int qb = blockIdx.x, h = blockIdx.y;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int64_t mrow = (int64_t)h * p.QB + qb;
+    const int n = p.kv_num[mrow];
+    const int32_t *list = p.kv_idx + mrow * p.kv_stride;
+
+    if (threadIdx.x == 0) {
+        mbar_init(res_full, 1);
+        for (int i = 0; i < 2; ++i) {
+            mbar_init(kv_full + i, 1);
+            mbar_init(kv_empty + i, 1);
+            mbar_init(sdp_full + i, 1);
+            mbar_init(p_full + i, 128);
+        }
+        mbar_init(acc_done, 1);
+        *cx.abort_flag = 0;
+        fence_mbar_init();
+    }
+    if (warp == 1) {
+        tmem_alloc(tmem_slot, kTmemCols);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+    cx.tmem = tmem;
+
+    if (warp == 0) {
+        if (lane == 0 && n > 0) {
+            mbar_expect_tx(res_full, L::RES_BYTES);
+            tma_load_3d(&maps.q, smem + L::Q, res_full, 0, qb * BM, h);
+#pragma unroll
+            for (int a = 0; a < NA; ++a) tma_load_3d(&maps.qa, smem + L::QA + a * L::ATILE, res_full, 16 * a, qb * BM, h);
+            tma_load_3d(&maps.dout, smem + L::DO, res_full, 0, qb * BM, h);
+            int issued = 0;
+            for (int jj = 0; jj < n; ++jj) {
+                const int st = jj & 1;
+                if (jj >= 2 && !cx.wait1(kv_empty + st, ((jj >> 1) - 1) & 1)) break;
+                int kb = list[jj];
+                if (kb < 0 || kb >= p.QB) kb = 0;   // masked by the elementwise warps
+                stage_kb[st] = list[jj];
+                uint8_t *sb = smem + L::STAGE0 + st * L::STAGE;
+                mbar_expect_tx(kv_full + st, L::KV_BYTES);
+                tma_load_3d(&maps.k, sb + L::SK, kv_full + st, 0, kb * BM, h);
+#pragma unroll
+                for (int a = 0; a < NA; ++a)
+                    tma_load_2d(&maps.ka, sb + L::SKA + a * L::ATILE, kv_full + st, 16 * a, kb * BM);
+                tma_load_3d(&maps.v, sb + L::SV, kv_full + st, 0, kb * BM, h);
+                issued = jj + 1;
+            }
+            mbar_wait(res_full, 0, 500000000ull);
+            for (int j = (issued > 2 ? issued - 2 : 0); j < issued; ++j)
+                mbar_wait(kv_full + (j & 1), (j >> 1) & 1, 500000000ull);
+        }
+    } else if (warp == 1) {
+        if (lane == 0 && n > 0) {
+            constexpr uint32_t idS = idesc_bf16(128, 64, false, false);
+            constexpr uint32_t idG = idesc_bf16(128, 64, false, true);
+            constexpr uint32_t idA = idesc_bf16(128, 16, false, true);
+            const uint32_t sQ = smem_u32(smem + L::Q), sQA = smem_u32(smem + L::QA), sDO = smem_u32(smem + L::DO);
+            auto grad = [&](int v) -> bool {
+                const int jv = v >> 1, hv = v & 1, stv = jv & 1;
+                if (!cx.wait1(p_full + hv, jv & 1)) return false;
+                tc_fence_after();
+                const uint32_t sb = smem_u32(smem + L::STAGE0 + stv * L::STAGE);
+#pragma unroll
+                for (int kk = 0; kk < 4; ++kk)
+                    mma_ts(tmem + ACC0, tmem + slot_s(hv) + kk * 8, mnmajor128_desc(sb + L::SK + hv * 8192 + kk * 2048),
+                           idG, (v > 0 || kk > 0) ? 1u : 0u);
+#pragma unroll
+                for (int a = 0; a < NA; ++a)
+#pragma unroll
+                    for (int kk = 0; kk < 4; ++kk)
+                        mma_ts(tmem + ACC1 + a * 16, tmem + slot_s(hv) + kk * 8,
+                               mnmajor32_desc(sb + L::SKA + a * L::ATILE + hv * 2048 + kk * 512), idA,
+                               (v > 0 || kk > 0) ? 1u : 0u);
+                if (hv == 1) tc_commit(kv_empty + stv);
+                return true;
+            };
+            bool ok = cx.wait1(res_full, 0);
+            const int nu = 2 * n;
+            for (int u = 0; ok && u < nu; ++u) {
+                const int jj = u >> 1, half = u & 1, st = jj & 1;
+                if (half == 0 && !cx.wait1(kv_full + st, (jj >> 1) & 1)) { ok = false; break; }
+                tc_fence_after();
+                const uint32_t sb = smem_u32(smem + L::STAGE0 + st * L::STAGE);
+#pragma unroll
+                for (int kk = 0; kk < 4; ++kk)
+                    mma_ss(tmem + slot_s(half), kmajor_desc(sQ + kk * 32, 128),
+                           kmajor_desc(sb + L::SK + half * 8192 + kk * 32, 128), idS, kk > 0);
+#pragma unroll
+                for (int a = 0; a < NA; ++a)
+                    mma_ss(tmem + slot_s(half), kmajor_desc(sQA + a * L::ATILE, 32),
+                           kmajor_desc(sb + L::SKA + a * L::ATILE + half * 2048, 32), idS, 1);
+#pragma unroll
+                for (int kk = 0; kk < 4; ++kk)
+                    mma_ss(tmem + slot_dp(half), kmajor_desc(sDO + kk * 32, 128),
+                           kmajor_desc(sb + L::SV + half * 8192 + kk * 32, 128), idS, kk > 0);
+                tc_commit(sdp_full + half);
+                if (u >= 1 && !grad(u - 1)) { ok = false; break; }
+            }
+            if (ok) ok = grad(nu - 1);
+            if (ok) tc_commit(acc_done);
+        }
+    } else {
+        const int quad = warp & 3;
+        const int r = quad * 32 + lane;
+        const int i = qb * BM + r;
+        const uint32_t lb = (uint32_t)(quad * 32) << 16;
+        const bool have_docs = p.docs != nullptr;
+        const int doc_i = have_docs ? p.docs[i] : 0;
+        const int32_t *dmin = p.block_info ? p.block_info + 2 * p.QB : nullptr;
+        const int32_t *dmax = p.block_info ? p.block_info + 3 * p.QB : nullptr;
+        const bool q_uniform = !have_docs || (dmin && dmin[qb] == dmax[qb]);
+        const int64_t hrow = (int64_t)h * p.T + i;
+        const float l2 = p.lse2[hrow], dl = p.delta[hrow];
+        bool alive = true;
+        const int nu = 2 * n;
+        for (int u = 0; u < nu && alive; ++u) {
+            const int jj = u >> 1, half = u & 1, st = jj & 1;
+            if (half == 0 && !cx.waitw(kv_full + st, (jj >> 1) & 1)) { alive = false; break; }
+            const int kb = stage_kb[st];
+            const bool bad = kb < 0 || kb >= p.QB;
+            const bool full = !bad && kb < qb &&
+                              (!have_docs || (q_uniform && dmin[kb] == dmax[kb] && dmin[kb] == dmin[qb]));
+            if (!cx.waitw(sdp_full + half, jj & 1)) { alive = false; break; }
+            tc_fence_after();
+            float s[64], dp[64];
+            ld64(tmem + lb + slot_s(half), s);
+            ld64(tmem + lb + slot_dp(half), dp);
+            const int j0 = kb * BM + half * 64;
+#pragma unroll
+            for (int e = 0; e < 64; ++e) {
+                float pr = ex2(fmaf(s[e], p.scale_log2, -l2));
+                if (!full) {
+                    const int jt = j0 + e;
+                    bool valid = !bad && jt <= i;
+                    if (have_docs) valid = valid && (__ldg(p.docs + (bad ? 0 : jt)) == doc_i);
+                    if (!valid) pr = 0.f;
+                }
+                s[e] = pr * (dp[e] - dl);
+            }
+            st_bf16x64(tmem + lb + slot_s(half), s);
+            tmem_wait_st();
+            tc_fence_before();
+            mbar_arrive(p_full + half);
+        }
+        bool have = false;
+        if (alive && n > 0) {
+            have = cx.waitw(acc_done, 0);
+            tc_fence_after();
+        }
+        store_row(tmem + lb + ACC0, p.scale, p.g0 + (int64_t)h * p.g0_sh + (int64_t)i * p.g0_st, have);   // dQ
+        if (NA > 0 && p.dcoeff_cos) {
+            // gradient of the augmented dims -> coefficients (q_aug = s [A c + B s', A s' - B c, -slope])
+            float ga[DA > 0 ? DA : 1];
+#pragma unroll
+            for (int a = 0; a < NA; ++a) {
+                uint32_t o[16];
+                if (have) {
+                    tmem_ld16(tmem + lb + ACC1 + a * 16, o);
+                    tmem_wait_ld();
+                } else {
+#pragma unroll
+                    for (int e = 0; e < 16; ++e) o[e] = 0u;
+                }
+#pragma unroll
+                for (int e = 0; e < 16; ++e) ga[a * 16 + e] = __uint_as_float(o[e]) * p.scale;
+            }
+            const int K = p.K;
+#pragma unroll
+            for (int k = 0; k < DA / 2; ++k) {
+                if (k < K) {
+                    const float cv = bf16_to_f32(p.cos_tab[(int64_t)k * p.tab_len + i]);
+                    const float sv = bf16_to_f32(p.sin_tab[(int64_t)k * p.tab_len + i]);
+                    const float g0 = ga[k], g1 = ga[(K + k) < DA ? (K + k) : 0];
+                    p.dcoeff_cos[hrow * K + k] = p.s_aug * (g0 * cv + g1 * sv);
+                    p.dcoeff_sin[hrow * K + k] = p.s_aug * (g0 * sv - g1 * cv);
+                }
+            }
+            if (p.has_slope && p.dslope) {
+                float gs = 0.f;
+#pragma unroll
+                for (int e = 0; e < (DA > 0 ? DA : 1); ++e)
+                    if (e == 2 * K) gs = ga[e];
+                p.dslope[hrow] = -p.s_aug * gs;
+            }
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem, kTmemCols);
+    }
+}
+
+}  // namespace tcbwd
+
+namespace tchost {
+
+template <int DA>
+int launch_bwd(const ScopeAttnArgs &a, cudaStream_t s) {
+    const int QB = a.T / 128;
+    float *delta = reinterpret_cast<float *>(a.workspace);
+    float *lse2 = delta + (size_t)a.H * a.T;
+    const int64_t rows = (int64_t)a.H * a.T;
+    tcbwd::prep_kernel<<<(unsigned)((rows + 255) / 256), 256, 0, s>>>(
+        reinterpret_cast<const __nv_bfloat16 *>(a.out), a.o_sh, a.o_st, reinterpret_cast<const __nv_bfloat16 *>(a.dout),
+        a.do_sh, a.do_st, a.lse, a.H, a.T, delta, lse2);
+    SCOPE_CHECK_LAUNCH();
+
+    tcbwd::Maps maps;
+    std::memset(&maps, 0, sizeof(maps));
+    bool ok = map3d(&maps.q, a.q, 64, a.T, a.H, a.q_st, a.q_sh, 64) &&
+              map3d(&maps.k, a.k, 64, a.T, a.H, a.k_st, a.k_sh, 64) &&
+              map3d(&maps.v, a.v, 64, a.T, a.H, a.v_st, a.v_sh, 64) &&
+              map3d(&maps.dout, a.dout, 64, a.T, a.H, a.do_st, a.do_sh, 64);
+    if (DA) ok = ok && map3d(&maps.qa, a.q_aug, DA, a.T, a.H, DA, (int64_t)a.T * DA, 16) &&
+                 map2d(&maps.ka, a.k_aug, DA, a.T, 16);
+    if (!ok) return SCOPE_ERR_ALIGN;
+
+    tcbwd::Params p;
+    std::memset(&p, 0, sizeof(p));
+    p.H = a.H;
+    p.T = a.T;
+    p.QB = QB;
+    p.words = (QB + 31) / 32;
+    p.kv_stride = a.kv_stride;
+    p.q_bitmap = a.q_bitmap;
+    p.kv_num = a.kv_num;
+    p.kv_idx = a.kv_indices;
+    p.block_info = a.block_info;
+    p.docs = a.docs;
+    p.lse2 = lse2;
+    p.delta = delta;
+    p.scale = a.scale;
+    p.scale_log2 = a.scale * 1.4426950408889634f;
+    p.err = a.err_flag;
+
+    // dK, dV
+    p.g0 = reinterpret_cast<__nv_bfloat16 *>(a.dk);
+    p.g0_sh = a.dk_sh;
+    p.g0_st = a.dk_st;
+    p.g1 = reinterpret_cast<__nv_bfloat16 *>(a.dv);
+    p.g1_sh = a.dv_sh;
+    p.g1_st = a.dv_st;
+    size_t smem = tcbwd::KVL<DA>::TOTAL + 1024;
+    if (cudaFuncSetAttribute(tcbwd::dkv_kernel<DA>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
+        cudaSuccess)
+        return SCOPE_ERR_CUDA;
+    tcbwd::dkv_kernel<DA><<<dim3(QB, a.H), tcbwd::kThreads, smem, s>>>(maps, p);
+    SCOPE_CHECK_LAUNCH();
+
+    // dQ (+ coefficient gradients)
+    p.g0 = reinterpret_cast<__nv_bfloat16 *>(a.dq);
+    p.g0_sh = a.dq_sh;
+    p.g0_st = a.dq_st;
+    p.g1 = nullptr;
+    if (a.bias_mode == SCOPE_BIAS_QK_AUG) {
+        p.K = a.K;
+        p.has_slope = a.slope != nullptr;
+        p.tab_len = a.tab_len;
+        p.cos_tab = a.cos_tab;
+        p.sin_tab = a.sin_tab;
+        p.s_aug = (float)sqrt((double)a.beta / (double)a.scale);
+        p.dcoeff_cos = a.dcoeff_cos;
+        p.dcoeff_sin = a.dcoeff_sin;
+        p.dslope = a.dslope;
+    }
+    smem = tcbwd::QL<DA>::TOTAL + 1024;
+    if (cudaFuncSetAttribute(tcbwd::dq_kernel<DA>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
+        cudaSuccess)
+        return SCOPE_ERR_CUDA;
+    tcbwd::dq_kernel<DA><<<dim3(QB, a.H), tcbwd::kThreads, smem, s>>>(maps, p);
+    SCOPE_CHECK_LAUNCH();
+    return SCOPE_OK;
+}
+
+}  // namespace tchost
+}  // namespace scope
+
+int scope_tc_bwd(const ScopeAttnArgs &a, cudaStream_t s) {
+    using namespace scope::tchost;
+    switch (a.bias_mode == SCOPE_BIAS_QK_AUG ? a.d_aug : 0) {
+        case 0: return launch_bwd<0>(a, s);
+        case 16: return launch_bwd<16>(a, s);
+        case 32: return launch_bwd<32>(a, s);
+        case 48: return launch_bwd<48>(a, s);
+        case 64: return launch_bwd<64>(a, s);
+        default: return SCOPE_ERR_INVALID;
+    }
+}

@@ -57,8 +57,8 @@ int validate(const ScopeAttnArgs &a, bool bwd) {
 
 extern "C" size_t scope_workspace_bytes(const ScopeAttnArgs *a) {
     if (!a || a->H <= 0 || a->T <= 0) return 0;
-    // delta_i = rowsum(dO * O), float32 [H, T]
-    size_t b = (size_t)a->H * (size_t)a->T * sizeof(float);
+    // delta_i = rowsum(dO * O) and lse_i * log2(e), float32 [H, T] each
+    size_t b = 2 * (size_t)a->H * (size_t)a->T * sizeof(float);
     return (b + 255) & ~(size_t)255;
 }
 

@@ -79,6 +79,14 @@ __device__ __forceinline__ void tma_load_3d(const CUtensorMap *m, void *dst, uin
         : "memory");
 }
 
+// contiguous global -> shared copy of `bytes` (multiple of 16, both ends 16-byte aligned)
+__device__ __forceinline__ void bulk_load(void *dst, const void *src, uint32_t bytes, uint64_t *bar) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                     smem_u32(dst)),
+                 "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(smem_u32(bar))
+                 : "memory");
+}
+
 // ---------------------------------------------------------------- tcgen05
 __device__ __forceinline__ void tmem_alloc(uint32_t *slot, uint32_t ncols) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(slot)),
@@ -171,6 +179,8 @@ __device__ __forceinline__ uint64_t kmajor_desc(uint32_t addr, uint32_t row_byte
 // MN-major tile of 64 bf16 columns (128-byte rows along N), K rows: 8-row
 // groups 1024 bytes apart.
 __device__ __forceinline__ uint64_t mnmajor128_desc(uint32_t addr) { return smem_desc(addr, 16384, 1024, SW128); }
+// MN-major tile of 16 bf16 columns (32-byte rows along N): 8-row groups 256 bytes apart.
+__device__ __forceinline__ uint64_t mnmajor32_desc(uint32_t addr) { return smem_desc(addr, 4096, 256, SW32); }
 
 // kind::f16 instruction descriptor: bf16 A and B, f32 accumulate, M x N.
 __host__ __device__ constexpr uint32_t idesc_bf16(int M, int N, bool a_mn, bool b_mn) {

@@ -138,3 +138,82 @@ def test_tc_forward_empty_rows_and_bad_indices():
     ro, rl = AO.attention(q[0:1].float().cpu(), k[0:1].float().cpu(), v[0:1].float().cpu(), mask, scale=0.12)
     rows = torch.cat([torch.arange(0, 128), torch.arange(256, T)])
     assert _maxabs(out[0, 0][rows], ro[0][rows]) < 2e-2
+
+
+def _grads(bm, x, K, do, cuda_cores=False):
+    q, k, v = (x[n].transpose(0, 1).contiguous().to(DEV, torch.bfloat16).transpose(0, 1).requires_grad_(True)
+               for n in ("q", "k", "v"))
+    sm, leaves = None, {}
+    if K:
+        ct, st = trig_tables(x["omegas"].to(DEV), q.shape[1])
+        cc = x["coeff_cos"].to(DEV).requires_grad_(True)
+        cs = x["coeff_sin"].to(DEV).requires_grad_(True)
+        sl = None if x["slope"] is None else x["slope"].to(DEV).requires_grad_(True)
+        leaves = {"dcoeff_cos": cc, "dcoeff_sin": cs}
+        if sl is not None:
+            leaves["dslope"] = sl
+        sm = SpectralScoreMod(coeff_cos=cc, coeff_sin=cs, cos_tab=ct, sin_tab=st, beta=0.5, slope=sl, impl="qk_aug")
+    out = flex_attention(q[None], k[None], v[None], bm, score_mod=sm, scale=0.12, cuda_cores=cuda_cores)
+    out.backward(do.to(DEV, torch.bfloat16)[None])
+    res = {"out": out[0], "dq": q.grad, "dk": k.grad, "dv": v.grad}
+    res.update({n: t.grad for n, t in leaves.items()})
+    return res
+
+
+def _oracle_grads(bm, x, K, docs, do):
+    T = x["q"].shape[1]
+    mask = AO.dense_mask(bm.kv_num_blocks[0].cpu().numpy(), bm.kv_indices[0].cpu().numpy(), T, 128,
+                         docs=docs.numpy())
+    q, k, v = (x[n].to(torch.bfloat16) for n in ("q", "k", "v"))
+    do = do.to(torch.bfloat16).float()
+    if not K:
+        return AO.plain_grads(q.float(), k.float(), v.float(), do, mask, scale=0.12)
+    ct, st = AO.trig_tables(x["omegas"], T)
+    qa, ka, va = AO.qk_aug_inputs(q, k, v, x["coeff_cos"], x["coeff_sin"], ct, st, beta=0.5, scale=0.12,
+                                  slope=x["slope"])
+    pad = torch.zeros(do.shape[0], T, va.shape[-1] - 64)
+    ref = AO.plain_grads(qa.float(), ka.float(), va.float(), torch.cat([do, pad], -1), mask, scale=0.12)
+    s = math.sqrt(0.5 / 0.12)
+    dqa = ref["dq"][..., 64:]
+    c = ct.to(torch.float64).transpose(0, 1)[None]
+    sn = st.to(torch.float64).transpose(0, 1)[None]
+    ref["dcoeff_cos"] = s * (dqa[..., :K] * c + dqa[..., K:2 * K] * sn)
+    ref["dcoeff_sin"] = s * (dqa[..., :K] * sn - dqa[..., K:2 * K] * c)
+    if x["slope"] is not None:
+        ref["dslope"] = -s * dqa[..., 2 * K]
+    for n in ("out", "dq", "dk", "dv"):
+        ref[n] = ref[n][..., :64]
+    return ref
+
+
+@pytest.mark.parametrize("K,slope", [(0, False), (8, False), (16, False), (16, True), (32, False)])
+@pytest.mark.parametrize("docs_kind", ["single", "multi"])
+def test_tc_backward_matches_oracle(K, slope, docs_kind):
+    T, H = 2048, 2
+    bm, x, docs = _inputs(T, H, K, slope, docs_kind, seed=11 + K)
+    do = torch.randn(H, T, 64, generator=torch.Generator().manual_seed(5))
+    device_errors(DEV)
+    res = _grads(bm, x, K, do)
+    torch.cuda.synchronize()
+    assert device_errors(DEV) == 0
+    ref = _oracle_grads(bm, x, K, docs, do)
+    for n in ("out", "dq", "dk", "dv"):
+        assert _maxabs(res[n], ref[n]) < 2e-2, n
+    for n in ("dcoeff_cos", "dcoeff_sin", "dslope"):
+        if n in res:
+            scale = max(1.0, ref[n].abs().max().item())
+            assert _maxabs(res[n], ref[n]) < 2e-2 * scale, (n, _maxabs(res[n], ref[n]), scale)
+
+
+@pytest.mark.parametrize("K", [0, 16])
+def test_tc_backward_long_lists_match_cuda_cores(K):
+    T, H = 8192, 2
+    bm, x, docs = _inputs(T, H, K, False, "multi", seed=4, M=8, half=3, local=8, glob=2)
+    do = torch.randn(H, T, 64, generator=torch.Generator().manual_seed(6))
+    a = _grads(bm, x, K, do)
+    b = _grads(bm, x, K, do, cuda_cores=True)
+    torch.cuda.synchronize()
+    assert device_errors(DEV) == 0
+    for n in a:
+        scale = max(1.0, b[n].abs().max().item())
+        assert _maxabs(a[n], b[n]) < 2e-2 * scale, n

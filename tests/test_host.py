@@ -57,7 +57,7 @@ def test_validation_rejects_before_launch():
     assert L.scope_qk_aug_prepare(None, None, None, None, None, 0, 1, 1, 1, 16, 0.5, 0.12, 1, None, None, None) == -1
     a2 = _lib.ScopeAttnArgs()
     a2.H, a2.T = 16, 131072
-    assert L.scope_workspace_bytes(ctypes.byref(a2)) == 16 * 131072 * 4
+    assert L.scope_workspace_bytes(ctypes.byref(a2)) == 2 * 16 * 131072 * 4
 
 
 def test_mask_max_kv():
