@@ -20,6 +20,7 @@
 // first 32 columns of the slot's S and dP halves, where the next MMAs read them
 // as their A operand), the issuer runs the QK^T / dO V^T MMAs of slot u+1 and
 // the gradient MMAs of slot u-1.  Every wait is bounded (SCOPE_DEVERR_TIMEOUT).
+#include <algorithm>
 #include <cmath>
 #include <cstring>
 
@@ -631,7 +632,10 @@ int launch_bwd(const ScopeAttnArgs &a, cudaStream_t s) {
     p.g1 = reinterpret_cast<__nv_bfloat16 *>(a.dv);
     p.g1_sh = a.dv_sh;
     p.g1_st = a.dv_st;
-    size_t smem = tcbwd::KVL<DA>::TOTAL + 1024;
+    // each CTA takes all 512 TMEM columns, so ask for enough shared memory that a
+    // second CTA never lands on the SM just to wait inside tcgen05.alloc
+    const size_t kOneCtaPerSm = 120 * 1024;
+    size_t smem = std::max<size_t>(tcbwd::KVL<DA>::TOTAL + 1024, kOneCtaPerSm);
     if (cudaFuncSetAttribute(tcbwd::dkv_kernel<DA>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
         cudaSuccess)
         return SCOPE_ERR_CUDA;
@@ -654,7 +658,7 @@ int launch_bwd(const ScopeAttnArgs &a, cudaStream_t s) {
         p.dcoeff_sin = a.dcoeff_sin;
         p.dslope = a.dslope;
     }
-    smem = tcbwd::QL<DA>::TOTAL + 1024;
+    smem = std::max<size_t>(tcbwd::QL<DA>::TOTAL + 1024, kOneCtaPerSm);
     if (cudaFuncSetAttribute(tcbwd::dq_kernel<DA>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
         cudaSuccess)
         return SCOPE_ERR_CUDA;
