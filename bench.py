@@ -301,6 +301,8 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--heads", type=int, default=0,
+                    help="run only this many heads of the config (a smaller case, e.g. for profiling)")
     args = ap.parse_args()
     if args.impl == "reference":
         run_reference(args)
@@ -308,6 +310,9 @@ def main():
     args.warmup = max(args.warmup, 3)
     rank, world, local = setup_dist()
     cfg = CONFIGS[args.config]
+    if args.heads:
+        import dataclasses
+        cfg = dataclasses.replace(cfg, H=args.heads)
     wl = Workload(cfg, rank, world, "cuda")
     gather_out = gather_stats = None
     if world > 1:

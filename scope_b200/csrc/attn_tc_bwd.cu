@@ -501,6 +501,11 @@ __global__ void __launch_bounds__(kThreads, 1) dq_kernel(const __grid_constant__
         const bool q_uniform = !have_docs || (dmin && dmin[qb] == dmax[qb]);
         const int64_t hrow = (int64_t)h * p.T + i;
         const float l2 = p.lse2[hrow], dl = p.delta[hrow];
+        // The slope column of k_aug holds positions * s (up to ~T*s); its dS sum
+        // cancels heavily, so it is accumulated here in fp32 from the unrounded
+        // dS instead of through the bf16 MMA.
+        const bool slope_acc = NA > 0 && p.has_slope && p.dslope;
+        float gsl = 0.f;
         bool alive = true;
         const int nu = 2 * n;
         for (int u = 0; u < nu && alive; ++u) {
@@ -526,6 +531,14 @@ __global__ void __launch_bounds__(kThreads, 1) dq_kernel(const __grid_constant__
                     if (!valid) pr = 0.f;
                 }
                 s[e] = pr * (dp[e] - dl);
+            }
+            if (slope_acc && !bad) {
+#pragma unroll
+                for (int e = 0; e < 64; ++e) {
+                    // the value scope_qk_aug_prepare stored: bf16(fp32(j) * s)
+                    const float kpos = __bfloat162float(__float2bfloat16_rn(__fmul_rn((float)(j0 + e), p.s_aug)));
+                    gsl = fmaf(s[e], kpos, gsl);
+                }
             }
             st_bf16x64(tmem + lb + slot_s(half), s);
             tmem_wait_st();
@@ -565,13 +578,7 @@ __global__ void __launch_bounds__(kThreads, 1) dq_kernel(const __grid_constant__
                     p.dcoeff_sin[hrow * K + k] = p.s_aug * (g0 * sv - g1 * cv);
                 }
             }
-            if (p.has_slope && p.dslope) {
-                float gs = 0.f;
-#pragma unroll
-                for (int e = 0; e < (DA > 0 ? DA : 1); ++e)
-                    if (e == 2 * K) gs = ga[e];
-                p.dslope[hrow] = -p.s_aug * gs;
-            }
+            if (slope_acc) p.dslope[hrow] = -p.s_aug * (gsl * p.scale);
         }
     }
     tc_fence_before();
