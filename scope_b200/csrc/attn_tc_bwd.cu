@@ -501,10 +501,13 @@ __global__ void __launch_bounds__(kThreads, 1) dq_kernel(const __grid_constant__
         const bool q_uniform = !have_docs || (dmin && dmin[qb] == dmax[qb]);
         const int64_t hrow = (int64_t)h * p.T + i;
         const float l2 = p.lse2[hrow], dl = p.delta[hrow];
-        // The slope column of k_aug holds positions * s (up to ~T*s); its dS sum
-        // cancels heavily, so it is accumulated here in fp32 from the unrounded
-        // dS instead of through the bf16 MMA.
+        // The slope column of k_aug holds positions * s (up to ~T*s).  Its dS sum
+        // is accumulated here in fp32 from the unrounded dS, against positions
+        // relative to this query row: sum_j dS_ij = 0 in exact arithmetic, so
+        // subtracting k_aug[i] changes nothing but the rounding, which would
+        // otherwise amplify the small residual of that sum by ~i*s.
         const bool slope_acc = NA > 0 && p.has_slope && p.dslope;
+        const float kpos_i = __bfloat162float(__float2bfloat16_rn(__fmul_rn((float)i, p.s_aug)));
         float gsl = 0.f;
         bool alive = true;
         const int nu = 2 * n;
@@ -537,7 +540,7 @@ __global__ void __launch_bounds__(kThreads, 1) dq_kernel(const __grid_constant__
                 for (int e = 0; e < 64; ++e) {
                     // the value scope_qk_aug_prepare stored: bf16(fp32(j) * s)
                     const float kpos = __bfloat162float(__float2bfloat16_rn(__fmul_rn((float)(j0 + e), p.s_aug)));
-                    gsl = fmaf(s[e], kpos, gsl);
+                    gsl = fmaf(s[e], kpos - kpos_i, gsl);
                 }
             }
             st_bf16x64(tmem + lb + slot_s(half), s);
