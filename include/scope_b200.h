@@ -208,6 +208,23 @@ int scope_attn_bwd(const ScopeAttnArgs *args, scope_stream_t stream);
 /* Workspace bytes scope_attn_bwd needs for these arguments. */
 size_t scope_workspace_bytes(const ScopeAttnArgs *args);
 
+/* Backward for callers that cannot allocate or pass a workspace (a CUDA graph
+ * capture that must not allocate, a plugin host that owns all device memory, a
+ * binding without a device allocator).  No counterpart in the reference.
+ * Same arguments and results as scope_attn_bwd; args->workspace is ignored and
+ * the scratch lives in one file-scope device array of
+ * scope_static_scratch_bytes() bytes (32 MiB) that every GPU loading the
+ * library holds until exit.  Problems whose scratch exceeds it
+ * (scope_workspace_bytes(args) > 32 MiB) are rejected with
+ * SCOPE_ERR_WORKSPACE.  It calls no allocator.  Its first call on a device
+ * looks up the array's device address (make that first call before any stream
+ * capture).  All calls share the array: calls whose kernels overlap on the GPU
+ * (different streams, or several devices' work on one context) race on it. */
+int scope_attn_bwd_static_scratch(const ScopeAttnArgs *args, scope_stream_t stream);
+
+/* Size in bytes of the array scope_attn_bwd_static_scratch uses. */
+size_t scope_static_scratch_bytes(void);
+
 /* Name of a scope_status value. */
 const char *scope_error_string(int status);
 
