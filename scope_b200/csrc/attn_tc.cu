@@ -218,30 +218,40 @@ __global__ void __launch_bounds__(kThreads, 2) fwd_kernel(const __grid_constant_
             int kb = list[j];
             const bool bad = kb < 0 || kb >= p.QB;
             if (bad && r == 0) set_err(p.err, SCOPE_DEVERR_INDEX);
-            const bool full = !bad && kb < qb &&
-                              (!have_docs || (q_uniform && dmin && dmin[kb] == dmax[kb] && dmin[kb] == dmin[qb]));
+            // full tile: no mask; one document: causal compare only; else per-element document ids
+            const bool same_doc = !have_docs || (q_uniform && dmin && dmin[kb] == dmax[kb] && dmin[kb] == dmin[qb]);
+            const int mk = bad ? 3 : ((kb < qb && same_doc) ? 0 : (same_doc ? 1 : 2));
             if (!warp_wait(s_full, j & 1)) { give_up(); alive = false; break; }
             tc_fence_after();
             float x[BM];
             {
-                uint32_t u[32];
+                uint32_t u0[32], u1[32], u2[32], u3[32];
+                tmem_ld32_nw(tS, u0);
+                tmem_ld32_nw(tS + 32, u1);
+                tmem_ld32_nw(tS + 64, u2);
+                tmem_ld32_nw(tS + 96, u3);
+                tmem_wait_ld();
+                pin(u0);
+                pin(u1);
+                pin(u2);
+                pin(u3);
 #pragma unroll
-                for (int c = 0; c < 4; ++c) {
-                    tmem_ld32(tS + c * 32, u);
-                    tmem_wait_ld();
-#pragma unroll
-                    for (int e = 0; e < 32; ++e) x[c * 32 + e] = __uint_as_float(u[e]) * p.scale_log2;
+                for (int e = 0; e < 32; ++e) {
+                    x[e] = __uint_as_float(u0[e]) * p.scale_log2;
+                    x[32 + e] = __uint_as_float(u1[e]) * p.scale_log2;
+                    x[64 + e] = __uint_as_float(u2[e]) * p.scale_log2;
+                    x[96 + e] = __uint_as_float(u3[e]) * p.scale_log2;
                 }
             }
             tc_fence_before();
             mbar_arrive(s_free);
-            if (!full) {
+            if (mk != 0) {
                 const int j0 = kb * BM;
+                const int lim = i - j0;                 // column c visible iff c <= lim
 #pragma unroll
                 for (int c = 0; c < BM; ++c) {
-                    const int jt = j0 + c;
-                    bool valid = !bad && jt <= i;
-                    if (have_docs) valid = valid && (__ldg(p.docs + (bad ? 0 : jt)) == doc_i);
+                    bool valid = mk != 3 && c <= lim;
+                    if (mk == 2) valid = valid && (__ldg(p.docs + j0 + c) == doc_i);
                     if (!valid) x[c] = -INFINITY;
                 }
             }

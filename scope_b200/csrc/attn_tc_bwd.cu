@@ -11,12 +11,16 @@
 //          dcoeff_sin / dslope in the epilogue by the chain rule of
 //          scoped_medium.py:380-421).
 // dQ is computed by its own kernel rather than with atomics so every output
-// is written once, deterministically.
+// is written once, deterministically.  A kv block that many q blocks see (a
+// global / sink block is seen by every q block of its document) would make one
+// dK/dV CTA walk a list of up to QB tiles; `plan` cuts such lists into chunks of
+// at most kChunk q tiles handled by separate CTAs, whose fp32 partial sums meet
+// in a small slot buffer that the last chunk of the row converts to bf16.
 //
 // Both kernels share one pipeline.  A 128x128 tile is processed as two
 // halves of 64 columns.  TMEM (512 columns, one CTA per SM) holds two slots of
 // {S half, dP half} (fp32, 64 + 64 columns) and the accumulators.  While the
-// four elementwise warps turn slot u into P / dS (bf16, written back over the
+// eight elementwise warps (two per TMEM lane quadrant, 32 columns each) turn slot u into P / dS (bf16, written back over the
 // first 32 columns of the slot's S and dP halves, where the next MMAs read them
 // as their A operand), the issuer runs the QK^T / dO V^T MMAs of slot u+1 and
 // the gradient MMAs of slot u-1.  Every wait is bounded (SCOPE_DEVERR_TIMEOUT).
@@ -34,7 +38,10 @@ using namespace tc;
 
 constexpr int BM = 128;
 constexpr int HD = 64;
-constexpr int kThreads = 192;
+constexpr int kThreads = 320;          // producer, issuer, 8 elementwise warps
+constexpr int kElem = 256;             // elementwise threads
+constexpr int kChunk = 64;             // max q tiles per dK/dV work item
+constexpr int kSlotCap = 128;          // max kv rows whose q list is split
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t ACC0 = 256, ACC1 = 320;   // dV / dK   or   dQ / dQaug
 constexpr float kLog2e = 1.4426950408889634f;
@@ -71,6 +78,15 @@ __global__ void prep_kernel(const __nv_bfloat16 *__restrict__ out, int64_t o_sh,
     lse2[row] = (l == -INFINITY) ? INFINITY : l * kLog2e;   // rows that saw nothing get P = 0
 }
 
+struct Plan {
+    const int32_t *n_items;   // [1]
+    const int4 *items;        // (h, kb, first q rank, count)
+    const int32_t *item_slot; // split slot or -1
+    const int32_t *slot_chunks;
+    int32_t *slot_done;
+    float *partial;           // [kSlotCap][128 rows][128]: dV (64) | dK (64)
+};
+
 struct Params {
     int H, T, QB, words, kv_stride;
     const uint32_t *q_bitmap;
@@ -85,6 +101,7 @@ struct Params {
     const uint16_t *cos_tab, *sin_tab;
     float s_aug;
     float *dcoeff_cos, *dcoeff_sin, *dslope;
+    Plan plan;
     int32_t *err;
 };
 
@@ -94,8 +111,6 @@ struct Maps {
 
 // helpers shared by both kernels ------------------------------------------------
 struct Ctx {
-    uint8_t *smem;
-    uint32_t tmem;
     volatile int *abort_flag;
     int32_t *err;
     __device__ void give_up() {
@@ -116,45 +131,57 @@ struct Ctx {
     }
 };
 
-// load the 64 fp32 columns at taddr (one TMEM lane per thread)
-__device__ __forceinline__ void ld64(uint32_t taddr, float (&x)[64]) {
-    uint32_t u[32];
-    tmem_ld32(taddr, u);
+__device__ __forceinline__ void elem_bar() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
+
+// S and dP columns [c0, c0+32) of a slot for this thread's TMEM lane, one wait
+__device__ __forceinline__ void ld_s_dp(uint32_t ts, uint32_t tdp, float (&s)[32], float (&dp)[32]) {
+    uint32_t a[32], b[32];
+    tmem_ld32_nw(ts, a);
+    tmem_ld32_nw(tdp, b);
     tmem_wait_ld();
+    pin(a);
+    pin(b);
 #pragma unroll
-    for (int e = 0; e < 32; ++e) x[e] = __uint_as_float(u[e]);
-    tmem_ld32(taddr + 32, u);
-    tmem_wait_ld();
-#pragma unroll
-    for (int e = 0; e < 32; ++e) x[32 + e] = __uint_as_float(u[e]);
-}
-// store 64 values as 32 bf16 pairs at taddr
-__device__ __forceinline__ void st_bf16x64(uint32_t taddr, const float (&x)[64]) {
-    uint32_t pk[32];
-#pragma unroll
-    for (int e = 0; e < 32; ++e) pk[e] = pack_bf16(x[2 * e], x[2 * e + 1]);
-    tmem_st32(taddr, pk);
-}
-// 64 fp32 accumulator columns -> one bf16 row of 128 bytes in global memory
-__device__ __forceinline__ void store_row(uint32_t taddr, float mul, __nv_bfloat16 *dst, bool have) {
-#pragma unroll
-    for (int c = 0; c < 4; ++c) {
-        uint32_t o[16];
-        if (have) {
-            tmem_ld16(taddr + c * 16, o);
-            tmem_wait_ld();
-        } else {
-#pragma unroll
-            for (int e = 0; e < 16; ++e) o[e] = 0u;
-        }
-        uint32_t w[8];
-#pragma unroll
-        for (int e = 0; e < 8; ++e)
-            w[e] = pack_bf16(__uint_as_float(o[2 * e]) * mul, __uint_as_float(o[2 * e + 1]) * mul);
-        uint4 *d = reinterpret_cast<uint4 *>(dst + c * 16);
-        d[0] = make_uint4(w[0], w[1], w[2], w[3]);
-        d[1] = make_uint4(w[4], w[5], w[6], w[7]);
+    for (int e = 0; e < 32; ++e) {
+        s[e] = __uint_as_float(a[e]);
+        dp[e] = __uint_as_float(b[e]);
     }
+}
+// 32 values as 16 bf16 pairs at taddr
+__device__ __forceinline__ void st_bf16x32(uint32_t taddr, const float (&x)[32]) {
+    uint32_t pk[16];
+#pragma unroll
+    for (int e = 0; e < 16; ++e) pk[e] = pack_bf16(x[2 * e], x[2 * e + 1]);
+    tmem_st16(taddr, pk);
+}
+// 32 fp32 accumulator columns -> 64 bytes of a bf16 row in global memory
+__device__ __forceinline__ void store_row32(uint32_t taddr, float mul, __nv_bfloat16 *dst, bool have) {
+    uint32_t o[32];
+    if (have) {
+        tmem_ld32_nw(taddr, o);
+        tmem_wait_ld();
+        pin(o);
+    } else {
+#pragma unroll
+        for (int e = 0; e < 32; ++e) o[e] = 0u;
+    }
+    uint32_t w[16];
+#pragma unroll
+    for (int e = 0; e < 16; ++e) w[e] = pack_bf16(__uint_as_float(o[2 * e]) * mul, __uint_as_float(o[2 * e + 1]) * mul);
+    uint4 *d = reinterpret_cast<uint4 *>(dst);
+#pragma unroll
+    for (int e = 0; e < 4; ++e) d[e] = make_uint4(w[4 * e], w[4 * e + 1], w[4 * e + 2], w[4 * e + 3]);
+}
+
+// Tile masking: every element of a full tile is visible; a tile whose q and kv
+// blocks lie in one document needs only the causal test (one compare); only
+// tiles that straddle a document boundary read document ids per element.
+enum MaskKind { MASK_FULL = 0, MASK_CAUSAL = 1, MASK_DOCS = 2 };
+__device__ __forceinline__ int tile_mask_kind(int qb, int kb, bool have_docs, const int32_t *dmin,
+                                              const int32_t *dmax) {
+    bool same_doc = !have_docs || (dmin && dmin[qb] == dmax[qb] && dmin[kb] == dmax[kb] && dmin[qb] == dmin[kb]);
+    if (kb < qb && same_doc) return MASK_FULL;
+    return same_doc ? MASK_CAUSAL : MASK_DOCS;
 }
 
 // ============================================================================ dK / dV
@@ -173,10 +200,28 @@ struct KVL {
     static constexpr uint32_t Q_BYTES = 2 * TILE + NA * ATILE + 1024;
 };
 
+// rank-th set bit onward of a bitmap row: the word index and remaining bits
+__device__ __forceinline__ void seek_rank(const uint32_t *row, int words, int rank, int &w, uint32_t &bits) {
+    w = 0;
+    bits = 0;
+    for (; w < words; ++w) {
+        bits = row[w];
+        const int c = __popc(bits);
+        if (rank < c) break;
+        rank -= c;
+    }
+    for (; rank > 0 && bits; --rank) bits &= bits - 1;
+}
+
 template <int DA>
 __global__ void __launch_bounds__(kThreads, 1) dkv_kernel(const __grid_constant__ Maps maps, const Params p) {
     using L = KVL<DA>;
     constexpr int NA = L::NA;
+    if ((int)blockIdx.x >= *p.plan.n_items) return;
+    const int4 item = p.plan.items[blockIdx.x];
+    const int slot = p.plan.item_slot[blockIdx.x];
+    const int h = item.x, kb = item.y, first = item.z, nq = item.w;
+
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
     uint64_t *bars = reinterpret_cast<uint64_t *>(smem + L::BAR);
@@ -184,13 +229,11 @@ __global__ void __launch_bounds__(kThreads, 1) dkv_kernel(const __grid_constant_
              *acc_done = bars + 9;
     volatile int *stage_qb = reinterpret_cast<volatile int *>(bars + 10);
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 11);
-    Ctx cx{smem, 0, reinterpret_cast<volatile int *>(tmem_slot + 1), p.err};
+    volatile int *last_flag = reinterpret_cast<volatile int *>(bars + 12);
+    Ctx cx{reinterpret_cast<volatile int *>(tmem_slot + 1), p.err};
 
-    const int kb = blockIdx.x, h = blockIdx.y;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const uint32_t *brow = p.q_bitmap + ((int64_t)h * p.QB + kb) * p.words;
-    int nq = 0;
-    for (int w = 0; w < p.words; ++w) nq += __popc(brow[w]);
 
     if (threadIdx.x == 0) {
         mbar_init(kv_full, 1);
@@ -198,10 +241,11 @@ __global__ void __launch_bounds__(kThreads, 1) dkv_kernel(const __grid_constant_
             mbar_init(q_full + i, 1);
             mbar_init(q_empty + i, 1);
             mbar_init(sdp_full + i, 1);
-            mbar_init(p_full + i, 128);
+            mbar_init(p_full + i, kElem);
         }
         mbar_init(acc_done, 1);
         *cx.abort_flag = 0;
+        *last_flag = 0;
         fence_mbar_init();
     }
     if (warp == 1) {
@@ -212,7 +256,6 @@ __global__ void __launch_bounds__(kThreads, 1) dkv_kernel(const __grid_constant_
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
-    cx.tmem = tmem;
 
     if (warp == 0) {
         if (lane == 0 && nq > 0) {
@@ -221,31 +264,31 @@ __global__ void __launch_bounds__(kThreads, 1) dkv_kernel(const __grid_constant_
 #pragma unroll
             for (int a = 0; a < NA; ++a) tma_load_2d(&maps.ka, smem + L::KA + a * L::ATILE, kv_full, 16 * a, kb * BM);
             tma_load_3d(&maps.v, smem + L::V, kv_full, 0, kb * BM, h);
+            int w;
+            uint32_t bits;
+            seek_rank(brow, p.words, first, w, bits);
             int t = 0;
-            bool ok = true;
-            for (int w = 0; w < p.words && ok; ++w) {
-                uint32_t bits = brow[w];
-                while (bits) {
-                    const int qb = w * 32 + __ffs(bits) - 1;
-                    bits &= bits - 1;
-                    const int st = t & 1;
-                    if (t >= 2 && !cx.wait1(q_empty + st, ((t >> 1) - 1) & 1)) {
-                        ok = false;
-                        break;
-                    }
-                    uint8_t *sb = smem + L::STAGE0 + st * L::STAGE;
-                    stage_qb[st] = qb;
-                    mbar_expect_tx(q_full + st, L::Q_BYTES);
-                    tma_load_3d(&maps.q, sb + L::SQ, q_full + st, 0, qb * BM, h);
-#pragma unroll
-                    for (int a = 0; a < NA; ++a)
-                        tma_load_3d(&maps.qa, sb + L::SQA + a * L::ATILE, q_full + st, 16 * a, qb * BM, h);
-                    tma_load_3d(&maps.dout, sb + L::SDO, q_full + st, 0, qb * BM, h);
-                    const int64_t off = (int64_t)h * p.T + (int64_t)qb * BM;
-                    bulk_load(sb + L::SLSE, p.lse2 + off, 512, q_full + st);
-                    bulk_load(sb + L::SDEL, p.delta + off, 512, q_full + st);
-                    ++t;
+            while (t < nq && w < p.words) {
+                if (!bits) {
+                    if (++w < p.words) bits = brow[w];
+                    continue;
                 }
+                const int qb = w * 32 + __ffs(bits) - 1;
+                bits &= bits - 1;
+                const int st = t & 1;
+                if (t >= 2 && !cx.wait1(q_empty + st, ((t >> 1) - 1) & 1)) break;
+                uint8_t *sb = smem + L::STAGE0 + st * L::STAGE;
+                stage_qb[st] = qb;
+                mbar_expect_tx(q_full + st, L::Q_BYTES);
+                tma_load_3d(&maps.q, sb + L::SQ, q_full + st, 0, qb * BM, h);
+#pragma unroll
+                for (int a = 0; a < NA; ++a)
+                    tma_load_3d(&maps.qa, sb + L::SQA + a * L::ATILE, q_full + st, 16 * a, qb * BM, h);
+                tma_load_3d(&maps.dout, sb + L::SDO, q_full + st, 0, qb * BM, h);
+                const int64_t off = (int64_t)h * p.T + (int64_t)qb * BM;
+                bulk_load(sb + L::SLSE, p.lse2 + off, 512, q_full + st);
+                bulk_load(sb + L::SDEL, p.delta + off, 512, q_full + st);
+                ++t;
             }
             mbar_wait(kv_full, 0, 500000000ull);
             for (int j = (t > 2 ? t - 2 : 0); j < t; ++j) mbar_wait(q_full + (j & 1), (j >> 1) & 1, 500000000ull);
@@ -297,7 +340,9 @@ __global__ void __launch_bounds__(kThreads, 1) dkv_kernel(const __grid_constant_
             if (ok) tc_commit(acc_done);
         }
     } else {
+        // ---------------- elementwise: thread = kv row c, 32 of the 64 columns of a half
         const int quad = warp & 3;
+        const int ch = (warp - 2) >> 2;                 // column half within the 64-column unit
         const int c = quad * 32 + lane;
         const int j = kb * BM + c;
         const uint32_t lb = (uint32_t)(quad * 32) << 16;
@@ -305,37 +350,42 @@ __global__ void __launch_bounds__(kThreads, 1) dkv_kernel(const __grid_constant_
         const int doc_j = have_docs ? p.docs[j] : 0;
         const int32_t *dmin = p.block_info ? p.block_info + 2 * p.QB : nullptr;
         const int32_t *dmax = p.block_info ? p.block_info + 3 * p.QB : nullptr;
-        const bool kv_uniform = !have_docs || (dmin && dmin[kb] == dmax[kb]);
         bool alive = true;
         const int nu = 2 * nq;
         for (int u = 0; u < nu && alive; ++u) {
             const int t = u >> 1, half = u & 1, st = t & 1;
             if (half == 0 && !cx.waitw(q_full + st, (t >> 1) & 1)) { alive = false; break; }
             const int qb = stage_qb[st];
-            const bool full = qb > kb && (!have_docs || (kv_uniform && dmin[qb] == dmax[qb] && dmin[qb] == dmin[kb]));
+            const int mk = tile_mask_kind(qb, kb, have_docs, dmin, dmax);
             if (!cx.waitw(sdp_full + half, t & 1)) { alive = false; break; }
             tc_fence_after();
-            float s[64], dp[64];
-            ld64(tmem + lb + slot_s(half), s);
-            ld64(tmem + lb + slot_dp(half), dp);
+            float s[32], dp[32];
+            ld_s_dp(tmem + lb + slot_s(half) + ch * 32, tmem + lb + slot_dp(half) + ch * 32, s, dp);
             const uint8_t *sb = smem + L::STAGE0 + st * L::STAGE;
-            const float *LS = reinterpret_cast<const float *>(sb + L::SLSE) + half * 64;
-            const float *DL = reinterpret_cast<const float *>(sb + L::SDEL) + half * 64;
-            const int i0 = qb * BM + half * 64;
+            const int col0 = half * 64 + ch * 32;       // q row within the tile of the first column
+            const float4 *LS = reinterpret_cast<const float4 *>(sb + L::SLSE) + col0 / 4;
+            const float4 *DL = reinterpret_cast<const float4 *>(sb + L::SDEL) + col0 / 4;
+            const int i0 = qb * BM + col0;
+            const int lim = j - i0;                     // column e visible iff e >= lim (causal: j <= i)
 #pragma unroll
-            for (int e = 0; e < 64; ++e) {
-                float pr = ex2(fmaf(s[e], p.scale_log2, -LS[e]));
-                if (!full) {
-                    const int i = i0 + e;
-                    bool valid = j <= i;
-                    if (have_docs) valid = valid && (__ldg(p.docs + i) == doc_j);
-                    if (!valid) pr = 0.f;
+            for (int e4 = 0; e4 < 8; ++e4) {
+                const float4 l4 = LS[e4], d4 = DL[e4];
+                const float lv[4] = {l4.x, l4.y, l4.z, l4.w}, dv[4] = {d4.x, d4.y, d4.z, d4.w};
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                    const int e = e4 * 4 + q;
+                    float pr = ex2(fmaf(s[e], p.scale_log2, -lv[q]));
+                    if (mk != MASK_FULL) {
+                        bool valid = e >= lim;
+                        if (mk == MASK_DOCS) valid = valid && (__ldg(p.docs + i0 + e) == doc_j);
+                        pr = valid ? pr : 0.f;
+                    }
+                    dp[e] = pr * (dp[e] - dv[q]);
+                    s[e] = pr;
                 }
-                dp[e] = pr * (dp[e] - DL[e]);
-                s[e] = pr;
             }
-            st_bf16x64(tmem + lb + slot_s(half), s);
-            st_bf16x64(tmem + lb + slot_dp(half), dp);
+            st_bf16x32(tmem + lb + slot_s(half) + ch * 16, s);
+            st_bf16x32(tmem + lb + slot_dp(half) + ch * 16, dp);
             tmem_wait_st();
             tc_fence_before();
             mbar_arrive(p_full + half);
@@ -345,8 +395,45 @@ __global__ void __launch_bounds__(kThreads, 1) dkv_kernel(const __grid_constant_
             have = cx.waitw(acc_done, 0);
             tc_fence_after();
         }
-        store_row(tmem + lb + ACC0, 1.f, p.g1 + (int64_t)h * p.g1_sh + (int64_t)j * p.g1_st, have);        // dV
-        store_row(tmem + lb + ACC1, p.scale, p.g0 + (int64_t)h * p.g0_sh + (int64_t)j * p.g0_st, have);    // dK
+        // dV from ACC0 (column half 0 warps), dK * scale from ACC1 (column half 1 warps)
+        const uint32_t acc = tmem + lb + (ch == 0 ? ACC0 : ACC1);
+        const float mul = ch == 0 ? 1.f : p.scale;
+        __nv_bfloat16 *dst = ch == 0 ? p.g1 + (int64_t)h * p.g1_sh + (int64_t)j * p.g1_st
+                                     : p.g0 + (int64_t)h * p.g0_sh + (int64_t)j * p.g0_st;
+        if (slot < 0) {
+            store_row32(acc, mul, dst, have);
+            store_row32(acc + 32, mul, dst + 32, have);
+        } else {
+            // a chunk of a split row: add into the row's fp32 slot; the last chunk writes bf16
+            float *part = p.plan.partial + ((size_t)slot * BM + c) * 128 + ch * 64;
+            if (have) {
+#pragma unroll
+                for (int hh = 0; hh < 2; ++hh) {
+                    uint32_t o[32];
+                    tmem_ld32_nw(acc + hh * 32, o);
+                    tmem_wait_ld();
+                    pin(o);
+#pragma unroll
+                    for (int e = 0; e < 32; ++e) atomicAdd(part + hh * 32 + e, __uint_as_float(o[e]) * mul);
+                }
+            }
+            __threadfence();
+            elem_bar();
+            if (threadIdx.x == 64) {
+                const int done = atomicAdd(p.plan.slot_done + slot, 1);
+                *last_flag = (done == p.plan.slot_chunks[slot] - 1) ? 1 : 0;
+            }
+            elem_bar();
+            if (*last_flag) {
+                __threadfence();
+                uint32_t w[32];
+#pragma unroll
+                for (int e = 0; e < 32; ++e) w[e] = pack_bf16(__ldcg(part + 2 * e), __ldcg(part + 2 * e + 1));
+                uint4 *d = reinterpret_cast<uint4 *>(dst);
+#pragma unroll
+                for (int e = 0; e < 8; ++e) d[e] = make_uint4(w[4 * e], w[4 * e + 1], w[4 * e + 2], w[4 * e + 3]);
+            }
+        }
     }
     tc_fence_before();
     __syncthreads();
@@ -354,6 +441,94 @@ __global__ void __launch_bounds__(kThreads, 1) dkv_kernel(const __grid_constant_
         tc_fence_after();
         tmem_dealloc(tmem, kTmemCols);
     }
+}
+
+// ============================================================================ dK/dV work plan
+// per (h, kb) row: number of q blocks that see it
+__global__ void plan_count_kernel(const uint32_t *__restrict__ bm, int rows, int words, int32_t *__restrict__ nq) {
+    const int row = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+    if (row >= rows) return;
+    int c = 0;
+    for (int w = lane; w < words; w += 32) c += __popc(bm[(int64_t)row * words + w]);
+#pragma unroll
+    for (int o = 16; o; o >>= 1) c += __shfl_xor_sync(0xffffffffu, c, o);
+    if (lane == 0) nq[row] = c;
+}
+
+__device__ int block_exclusive_scan(int v, int *sh, int &total) {
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    int x = v;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        int y = __shfl_up_sync(0xffffffffu, x, o);
+        if (lane >= o) x += y;
+    }
+    if (lane == 31) sh[w] = x;
+    __syncthreads();
+    if (w == 0) {
+        int y = lane < nw ? sh[lane] : 0;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            int z = __shfl_up_sync(0xffffffffu, y, o);
+            if (lane >= o) y += z;
+        }
+        sh[lane] = y;
+    }
+    __syncthreads();
+    const int excl = x - v + (w > 0 ? sh[w - 1] : 0);
+    total = sh[nw - 1];
+    __syncthreads();
+    return excl;
+}
+
+// one CTA: split items (long rows) first, then one item per remaining row
+__global__ void __launch_bounds__(1024) plan_items_kernel(const int32_t *__restrict__ nq, int rows, int KB,
+                                                          Plan plan, int4 *items, int32_t *item_slot,
+                                                          int32_t *slot_chunks, int32_t *n_items) {
+    __shared__ int sh[32];
+    const int per = (rows + blockDim.x - 1) / blockDim.x;
+    const int r0 = threadIdx.x * per, r1 = min(rows, r0 + per);
+    for (int i = threadIdx.x; i < kSlotCap; i += blockDim.x) plan.slot_done[i] = 0;
+    int nsplit = 0;
+    for (int r = r0; r < r1; ++r) nsplit += nq[r] > kChunk;
+    int tot;
+    const int slot0 = block_exclusive_scan(nsplit, sh, tot);
+    int ns_items = 0, nu_items = 0, slot = slot0;
+    for (int r = r0; r < r1; ++r) {
+        const int n = nq[r];
+        if (n > kChunk && slot < kSlotCap) {
+            ns_items += (n + kChunk - 1) / kChunk;
+            ++slot;
+        } else {
+            nu_items += 1;
+            if (n > kChunk) ++slot;
+        }
+    }
+    int tot_s, tot_u;
+    const int s_base = block_exclusive_scan(ns_items, sh, tot_s);
+    const int u_base = block_exclusive_scan(nu_items, sh, tot_u);
+    int so = s_base, uo = tot_s + u_base;
+    slot = slot0;
+    for (int r = r0; r < r1; ++r) {
+        const int n = nq[r];
+        const int h = r / KB, kb = r - h * KB;
+        if (n > kChunk && slot < kSlotCap) {
+            const int nc = (n + kChunk - 1) / kChunk;
+            slot_chunks[slot] = nc;
+            for (int c = 0; c < nc; ++c) {
+                items[so] = make_int4(h, kb, c * kChunk, min(kChunk, n - c * kChunk));
+                item_slot[so] = slot;
+                ++so;
+            }
+            ++slot;
+        } else {
+            items[uo] = make_int4(h, kb, 0, n);
+            item_slot[uo] = -1;
+            ++uo;
+            if (n > kChunk) ++slot;
+        }
+    }
+    if (threadIdx.x == 0) *n_items = tot_s + tot_u;
 }
 
 // ============================================================================ dQ
@@ -366,7 +541,8 @@ struct QL {
     static constexpr uint32_t SK = 0, SKA = TILE, SV = align1k(TILE + NA * ATILE);
     static constexpr uint32_t STAGE = SV + TILE;
     static constexpr uint32_t BAR = STAGE0 + 2 * STAGE;
-    static constexpr uint32_t TOTAL = BAR + 256;
+    static constexpr uint32_t SLOPE = BAR + 256;              // float[128]: slope partials of column half 1
+    static constexpr uint32_t TOTAL = SLOPE + 512;
     static constexpr uint32_t RES_BYTES = 2 * TILE + NA * ATILE;
     static constexpr uint32_t KV_BYTES = 2 * TILE + NA * ATILE;
 };
@@ -382,7 +558,8 @@ __global__ void __launch_bounds__(kThreads, 1) dq_kernel(const __grid_constant__
              *p_full = bars + 7, *acc_done = bars + 9;
     volatile int *stage_kb = reinterpret_cast<volatile int *>(bars + 10);
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 11);
-    Ctx cx{smem, 0, reinterpret_cast<volatile int *>(tmem_slot + 1), p.err};
+    float *slope_part = reinterpret_cast<float *>(smem + L::SLOPE);
+    Ctx cx{reinterpret_cast<volatile int *>(tmem_slot + 1), p.err};
 
     const int qb = blockIdx.x, h = blockIdx.y;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -396,7 +573,7 @@ __global__ void __launch_bounds__(kThreads, 1) dq_kernel(const __grid_constant__
             mbar_init(kv_full + i, 1);
             mbar_init(kv_empty + i, 1);
             mbar_init(sdp_full + i, 1);
-            mbar_init(p_full + i, 128);
+            mbar_init(p_full + i, kElem);
         }
         mbar_init(acc_done, 1);
         *cx.abort_flag = 0;
@@ -410,7 +587,6 @@ __global__ void __launch_bounds__(kThreads, 1) dq_kernel(const __grid_constant__
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
-    cx.tmem = tmem;
 
     if (warp == 0) {
         if (lane == 0 && n > 0) {
@@ -424,8 +600,8 @@ __global__ void __launch_bounds__(kThreads, 1) dq_kernel(const __grid_constant__
                 const int st = jj & 1;
                 if (jj >= 2 && !cx.wait1(kv_empty + st, ((jj >> 1) - 1) & 1)) break;
                 int kb = list[jj];
+                stage_kb[st] = kb;
                 if (kb < 0 || kb >= p.QB) kb = 0;   // masked by the elementwise warps
-                stage_kb[st] = list[jj];
                 uint8_t *sb = smem + L::STAGE0 + st * L::STAGE;
                 mbar_expect_tx(kv_full + st, L::KV_BYTES);
                 tma_load_3d(&maps.k, sb + L::SK, kv_full + st, 0, kb * BM, h);
@@ -490,7 +666,9 @@ __global__ void __launch_bounds__(kThreads, 1) dq_kernel(const __grid_constant__
             if (ok) tc_commit(acc_done);
         }
     } else {
+        // ---------------- elementwise: thread = q row i, 32 of the 64 columns of a half
         const int quad = warp & 3;
+        const int ch = (warp - 2) >> 2;
         const int r = quad * 32 + lane;
         const int i = qb * BM + r;
         const uint32_t lb = (uint32_t)(quad * 32) << 16;
@@ -498,7 +676,6 @@ __global__ void __launch_bounds__(kThreads, 1) dq_kernel(const __grid_constant__
         const int doc_i = have_docs ? p.docs[i] : 0;
         const int32_t *dmin = p.block_info ? p.block_info + 2 * p.QB : nullptr;
         const int32_t *dmax = p.block_info ? p.block_info + 3 * p.QB : nullptr;
-        const bool q_uniform = !have_docs || (dmin && dmin[qb] == dmax[qb]);
         const int64_t hrow = (int64_t)h * p.T + i;
         const float l2 = p.lse2[hrow], dl = p.delta[hrow];
         // The slope column of k_aug holds positions * s (up to ~T*s).  Its dS sum
@@ -516,34 +693,32 @@ __global__ void __launch_bounds__(kThreads, 1) dq_kernel(const __grid_constant__
             if (half == 0 && !cx.waitw(kv_full + st, (jj >> 1) & 1)) { alive = false; break; }
             const int kb = stage_kb[st];
             const bool bad = kb < 0 || kb >= p.QB;
-            const bool full = !bad && kb < qb &&
-                              (!have_docs || (q_uniform && dmin[kb] == dmax[kb] && dmin[kb] == dmin[qb]));
+            const int mk = bad ? MASK_DOCS : tile_mask_kind(qb, kb, have_docs, dmin, dmax);
             if (!cx.waitw(sdp_full + half, jj & 1)) { alive = false; break; }
             tc_fence_after();
-            float s[64], dp[64];
-            ld64(tmem + lb + slot_s(half), s);
-            ld64(tmem + lb + slot_dp(half), dp);
-            const int j0 = kb * BM + half * 64;
+            float s[32], dp[32];
+            ld_s_dp(tmem + lb + slot_s(half) + ch * 32, tmem + lb + slot_dp(half) + ch * 32, s, dp);
+            const int j0 = kb * BM + half * 64 + ch * 32;
+            const int lim = i - j0;                     // column e visible iff e <= lim (causal: j <= i)
 #pragma unroll
-            for (int e = 0; e < 64; ++e) {
+            for (int e = 0; e < 32; ++e) {
                 float pr = ex2(fmaf(s[e], p.scale_log2, -l2));
-                if (!full) {
-                    const int jt = j0 + e;
-                    bool valid = !bad && jt <= i;
-                    if (have_docs) valid = valid && (__ldg(p.docs + (bad ? 0 : jt)) == doc_i);
-                    if (!valid) pr = 0.f;
+                if (mk != MASK_FULL) {
+                    bool valid = e <= lim && !bad;
+                    if (mk == MASK_DOCS && have_docs) valid = valid && (__ldg(p.docs + (bad ? 0 : j0 + e)) == doc_i);
+                    pr = valid ? pr : 0.f;
                 }
                 s[e] = pr * (dp[e] - dl);
             }
             if (slope_acc && !bad) {
 #pragma unroll
-                for (int e = 0; e < 64; ++e) {
+                for (int e = 0; e < 32; ++e) {
                     // the value scope_qk_aug_prepare stored: bf16(fp32(j) * s)
                     const float kpos = __bfloat162float(__float2bfloat16_rn(__fmul_rn((float)(j0 + e), p.s_aug)));
                     gsl = fmaf(s[e], kpos - kpos_i, gsl);
                 }
             }
-            st_bf16x64(tmem + lb + slot_s(half), s);
+            st_bf16x32(tmem + lb + slot_s(half) + ch * 16, s);
             tmem_wait_st();
             tc_fence_before();
             mbar_arrive(p_full + half);
@@ -553,35 +728,42 @@ __global__ void __launch_bounds__(kThreads, 1) dq_kernel(const __grid_constant__
             have = cx.waitw(acc_done, 0);
             tc_fence_after();
         }
-        store_row(tmem + lb + ACC0, p.scale, p.g0 + (int64_t)h * p.g0_sh + (int64_t)i * p.g0_st, have);   // dQ
+        // dQ: each column half stores 32 of the 64 columns
+        store_row32(tmem + lb + ACC0 + ch * 32, p.scale,
+                    p.g0 + (int64_t)h * p.g0_sh + (int64_t)i * p.g0_st + ch * 32, have);
         if (NA > 0 && p.dcoeff_cos) {
-            // gradient of the augmented dims -> coefficients (q_aug = s [A c + B s', A s' - B c, -slope])
-            float ga[DA > 0 ? DA : 1];
+            if (ch == 1) slope_part[r] = gsl;
+            elem_bar();
+            if (ch == 0) {
+                // gradient of the augmented dims -> coefficients (q_aug = s [A c + B s', A s' - B c, -slope])
+                float ga[DA > 0 ? DA : 1];
 #pragma unroll
-            for (int a = 0; a < NA; ++a) {
-                uint32_t o[16];
-                if (have) {
-                    tmem_ld16(tmem + lb + ACC1 + a * 16, o);
-                    tmem_wait_ld();
-                } else {
+                for (int a = 0; a < NA; ++a) {
+                    uint32_t o[16];
+                    if (have) {
+                        tmem_ld16(tmem + lb + ACC1 + a * 16, o);
+                        tmem_wait_ld();
+                        pin(o);
+                    } else {
 #pragma unroll
-                    for (int e = 0; e < 16; ++e) o[e] = 0u;
+                        for (int e = 0; e < 16; ++e) o[e] = 0u;
+                    }
+#pragma unroll
+                    for (int e = 0; e < 16; ++e) ga[a * 16 + e] = __uint_as_float(o[e]) * p.scale;
                 }
+                const int K = p.K;
 #pragma unroll
-                for (int e = 0; e < 16; ++e) ga[a * 16 + e] = __uint_as_float(o[e]) * p.scale;
-            }
-            const int K = p.K;
-#pragma unroll
-            for (int k = 0; k < DA / 2; ++k) {
-                if (k < K) {
-                    const float cv = bf16_to_f32(p.cos_tab[(int64_t)k * p.tab_len + i]);
-                    const float sv = bf16_to_f32(p.sin_tab[(int64_t)k * p.tab_len + i]);
-                    const float g0 = ga[k], g1 = ga[(K + k) < DA ? (K + k) : 0];
-                    p.dcoeff_cos[hrow * K + k] = p.s_aug * (g0 * cv + g1 * sv);
-                    p.dcoeff_sin[hrow * K + k] = p.s_aug * (g0 * sv - g1 * cv);
+                for (int k = 0; k < DA / 2; ++k) {
+                    if (k < K) {
+                        const float cv = bf16_to_f32(p.cos_tab[(int64_t)k * p.tab_len + i]);
+                        const float sv = bf16_to_f32(p.sin_tab[(int64_t)k * p.tab_len + i]);
+                        const float g0 = ga[k], g1 = ga[(K + k) < DA ? (K + k) : 0];
+                        p.dcoeff_cos[hrow * K + k] = p.s_aug * (g0 * cv + g1 * sv);
+                        p.dcoeff_sin[hrow * K + k] = p.s_aug * (g0 * sv - g1 * cv);
+                    }
                 }
+                if (slope_acc) p.dslope[hrow] = -p.s_aug * ((gsl + slope_part[r]) * p.scale);
             }
-            if (slope_acc) p.dslope[hrow] = -p.s_aug * (gsl * p.scale);
         }
     }
     tc_fence_before();
@@ -596,16 +778,64 @@ __global__ void __launch_bounds__(kThreads, 1) dq_kernel(const __grid_constant__
 
 namespace tchost {
 
+// Workspace of the backward: delta, lse*log2(e), and the dK/dV work plan.
+struct BwdWorkspace {
+    size_t delta, lse2, nq, items, item_slot, n_items, slot_chunks, slot_done, partial, total;
+    int max_items;
+};
+
+BwdWorkspace bwd_workspace(int H, int T, int block_size) {
+    auto up = [](size_t x) { return (x + 255) & ~(size_t)255; };
+    BwdWorkspace w;
+    const int QB = T / block_size;
+    w.max_items = H * QB + tcbwd::kSlotCap * ((QB + tcbwd::kChunk - 1) / tcbwd::kChunk);
+    size_t o = 0;
+    w.delta = o;       o += up((size_t)H * T * 4);
+    w.lse2 = o;        o += up((size_t)H * T * 4);
+    w.nq = o;          o += up((size_t)H * QB * 4);
+    w.items = o;       o += up((size_t)w.max_items * 16);
+    w.item_slot = o;   o += up((size_t)w.max_items * 4);
+    w.n_items = o;     o += up(16);
+    w.slot_chunks = o; o += up((size_t)tcbwd::kSlotCap * 4);
+    w.slot_done = o;   o += up((size_t)tcbwd::kSlotCap * 4);
+    w.partial = o;     o += up((size_t)tcbwd::kSlotCap * 128 * 128 * 4);
+    w.total = o;
+    return w;
+}
+
 template <int DA>
 int launch_bwd(const ScopeAttnArgs &a, cudaStream_t s) {
     const int QB = a.T / 128;
-    float *delta = reinterpret_cast<float *>(a.workspace);
-    float *lse2 = delta + (size_t)a.H * a.T;
+    const BwdWorkspace ws = bwd_workspace(a.H, a.T, 128);
+    uint8_t *base = reinterpret_cast<uint8_t *>(a.workspace);
+    float *delta = reinterpret_cast<float *>(base + ws.delta);
+    float *lse2 = reinterpret_cast<float *>(base + ws.lse2);
     const int64_t rows = (int64_t)a.H * a.T;
     tcbwd::prep_kernel<<<(unsigned)((rows + 255) / 256), 256, 0, s>>>(
         reinterpret_cast<const __nv_bfloat16 *>(a.out), a.o_sh, a.o_st, reinterpret_cast<const __nv_bfloat16 *>(a.dout),
         a.do_sh, a.do_st, a.lse, a.H, a.T, delta, lse2);
     SCOPE_CHECK_LAUNCH();
+
+    // dK/dV work plan: long q lists are cut into chunks
+    tcbwd::Plan plan;
+    int32_t *nq = reinterpret_cast<int32_t *>(base + ws.nq);
+    int4 *items = reinterpret_cast<int4 *>(base + ws.items);
+    int32_t *item_slot = reinterpret_cast<int32_t *>(base + ws.item_slot);
+    int32_t *n_items = reinterpret_cast<int32_t *>(base + ws.n_items);
+    int32_t *slot_chunks = reinterpret_cast<int32_t *>(base + ws.slot_chunks);
+    plan.n_items = n_items;
+    plan.items = items;
+    plan.item_slot = item_slot;
+    plan.slot_chunks = slot_chunks;
+    plan.slot_done = reinterpret_cast<int32_t *>(base + ws.slot_done);
+    plan.partial = reinterpret_cast<float *>(base + ws.partial);
+    const int prow = a.H * QB, words = (QB + 31) / 32;
+    tcbwd::plan_count_kernel<<<(unsigned)((prow * 32 + 255) / 256), 256, 0, s>>>(a.q_bitmap, prow, words, nq);
+    SCOPE_CHECK_LAUNCH();
+    tcbwd::plan_items_kernel<<<1, 1024, 0, s>>>(nq, prow, QB, plan, items, item_slot, slot_chunks, n_items);
+    SCOPE_CHECK_LAUNCH();
+    if (cudaMemsetAsync(plan.partial, 0, (size_t)tcbwd::kSlotCap * 128 * 128 * 4, s) != cudaSuccess)
+        return SCOPE_ERR_CUDA;
 
     tcbwd::Maps maps;
     std::memset(&maps, 0, sizeof(maps));
@@ -622,7 +852,7 @@ int launch_bwd(const ScopeAttnArgs &a, cudaStream_t s) {
     p.H = a.H;
     p.T = a.T;
     p.QB = QB;
-    p.words = (QB + 31) / 32;
+    p.words = words;
     p.kv_stride = a.kv_stride;
     p.q_bitmap = a.q_bitmap;
     p.kv_num = a.kv_num;
@@ -633,6 +863,7 @@ int launch_bwd(const ScopeAttnArgs &a, cudaStream_t s) {
     p.delta = delta;
     p.scale = a.scale;
     p.scale_log2 = a.scale * 1.4426950408889634f;
+    p.plan = plan;
     p.err = a.err_flag;
 
     // dK, dV
@@ -649,7 +880,7 @@ int launch_bwd(const ScopeAttnArgs &a, cudaStream_t s) {
     if (cudaFuncSetAttribute(tcbwd::dkv_kernel<DA>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
         cudaSuccess)
         return SCOPE_ERR_CUDA;
-    tcbwd::dkv_kernel<DA><<<dim3(QB, a.H), tcbwd::kThreads, smem, s>>>(maps, p);
+    tcbwd::dkv_kernel<DA><<<ws.max_items, tcbwd::kThreads, smem, s>>>(maps, p);
     SCOPE_CHECK_LAUNCH();
 
     // dQ (+ coefficient gradients)
@@ -679,6 +910,10 @@ int launch_bwd(const ScopeAttnArgs &a, cudaStream_t s) {
 
 }  // namespace tchost
 }  // namespace scope
+
+size_t scope_bwd_workspace_bytes(int H, int T, int block_size) {
+    return scope::tchost::bwd_workspace(H, T, block_size).total;
+}
 
 int scope_tc_bwd(const ScopeAttnArgs &a, cudaStream_t s) {
     using namespace scope::tchost;

@@ -16,6 +16,7 @@ int scope_simt_bwd(const ScopeAttnArgs &a, cudaStream_t s);
 int scope_tc_fwd(const ScopeAttnArgs &a, cudaStream_t s);
 int scope_tc_bwd(const ScopeAttnArgs &a, cudaStream_t s);
 bool scope_tc_eligible(const ScopeAttnArgs &a, bool bwd);
+size_t scope_bwd_workspace_bytes(int H, int T, int block_size);
 
 namespace {
 
@@ -56,10 +57,9 @@ int validate(const ScopeAttnArgs &a, bool bwd) {
 }  // namespace
 
 extern "C" size_t scope_workspace_bytes(const ScopeAttnArgs *a) {
-    if (!a || a->H <= 0 || a->T <= 0) return 0;
-    // delta_i = rowsum(dO * O) and lse_i * log2(e), float32 [H, T] each
-    size_t b = 2 * (size_t)a->H * (size_t)a->T * sizeof(float);
-    return (b + 255) & ~(size_t)255;
+    if (!a || a->H <= 0 || a->T <= 0 || a->block_size <= 0 || a->T % a->block_size) return 0;
+    // delta_i = rowsum(dO * O), lse_i * log2(e) (float32 [H, T] each) and the dK/dV work plan
+    return scope_bwd_workspace_bytes(a->H, a->T, a->block_size);
 }
 
 extern "C" int scope_attn_fwd(const ScopeAttnArgs *args, scope_stream_t stream) {

@@ -33,14 +33,16 @@ __device__ __forceinline__ void mbar_expect_tx(uint64_t *bar, uint32_t bytes) {
                  "r"(bytes)
                  : "memory");
 }
+// try_wait with a suspend-time hint: the thread sleeps until the phase
+// completes or the hint (ns) elapses instead of spinning on issue slots.
 __device__ __forceinline__ bool mbar_try_wait(uint32_t addr, uint32_t parity) {
     uint32_t ok;
     asm volatile(
         "{\n\t.reg .pred p;\n\t"
-        "mbarrier.try_wait.parity.acquire.cta.shared::cta.b64 p, [%1], %2;\n\t"
+        "mbarrier.try_wait.parity.acquire.cta.shared::cta.b64 p, [%1], %2, %3;\n\t"
         "selp.u32 %0, 1, 0, p;\n\t}\n"
         : "=r"(ok)
-        : "r"(addr), "r"(parity)
+        : "r"(addr), "r"(parity), "r"(1000000u)
         : "memory");
     return ok != 0;
 }
@@ -55,9 +57,9 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, uint64
     const uint32_t a = smem_u32(bar);
     if (mbar_try_wait(a, parity)) return true;
     const uint64_t t0 = globaltimer_ns();
-    for (uint32_t i = 1;; ++i) {
+    for (;;) {
         if (mbar_try_wait(a, parity)) return true;
-        if ((i & 63u) == 0 && globaltimer_ns() - t0 > limit_ns) return false;
+        if (globaltimer_ns() - t0 > limit_ns) return false;
     }
 }
 
@@ -123,6 +125,13 @@ __device__ __forceinline__ void mma_ts(uint32_t d, uint32_t a, uint64_t b, uint3
         : "memory");
 }
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+// After tcgen05.wait::ld: make the loaded registers opaque so no use of them
+// is scheduled above the wait (tcgen05.ld writes them asynchronously).
+template <int N>
+__device__ __forceinline__ void pin(uint32_t (&r)[N]) {
+#pragma unroll
+    for (int i = 0; i < N; ++i) asm volatile("" : "+r"(r[i]));
+}
 __device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
 #define SCOPE_R8(b) "=r"(r[b + 0]), "=r"(r[b + 1]), "=r"(r[b + 2]), "=r"(r[b + 3]), "=r"(r[b + 4]), "=r"(r[b + 5]), "=r"(r[b + 6]), "=r"(r[b + 7])
@@ -145,6 +154,15 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32
         "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
         SCOPE_W8(0), SCOPE_W8(8), SCOPE_W8(16), SCOPE_W8(24)
         : "memory");
+}
+// loads without the wait (issue several, then one tmem_wait_ld)
+__device__ __forceinline__ void tmem_ld32_nw(uint32_t taddr, uint32_t (&r)[32]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+        "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+        "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+        : SCOPE_R8(0), SCOPE_R8(8), SCOPE_R8(16), SCOPE_R8(24)
+        : "r"(taddr));
 }
 __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
     asm volatile(

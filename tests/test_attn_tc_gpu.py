@@ -205,10 +205,15 @@ def test_tc_backward_matches_oracle(K, slope, docs_kind):
             assert _maxabs(res[n], ref[n]) < 2e-2 * scale, (n, _maxabs(res[n], ref[n]), scale)
 
 
-@pytest.mark.parametrize("K", [0, 16])
-def test_tc_backward_long_lists_match_cuda_cores(K):
-    T, H = 8192, 2
-    bm, x, docs = _inputs(T, H, K, False, "multi", seed=4, M=8, half=3, local=8, glob=2)
+@pytest.mark.parametrize("K,T,docs_kind", [(0, 8192, "multi"), (16, 16384, "single"), (16, 32768, "multi")])
+def test_tc_backward_long_lists_match_cuda_cores(K, T, docs_kind):
+    """Long q lists: the global block is seen by every q block of its document,
+    so at T >= 16384 its dK/dV list is cut into chunks that meet in the fp32
+    slot buffer; compare with the CUDA-core backward on the same inputs."""
+    H = 2 if T <= 16384 else 1
+    bm, x, docs = _inputs(T, H, K, False, docs_kind, seed=4, M=8, half=3, local=8, glob=2)
+    if T >= 16384:
+        assert int(bm.q_num_blocks.max()) > 64      # at least one split row
     do = torch.randn(H, T, 64, generator=torch.Generator().manual_seed(6))
     a = _grads(bm, x, K, do)
     b = _grads(bm, x, K, do, cuda_cores=True)

@@ -56,8 +56,9 @@ def test_validation_rejects_before_launch():
     assert L.scope_block_info(None, 100, 128, 1, 0, 0, None, None) == -1
     assert L.scope_qk_aug_prepare(None, None, None, None, None, 0, 1, 1, 1, 16, 0.5, 0.12, 1, None, None, None) == -1
     a2 = _lib.ScopeAttnArgs()
-    a2.H, a2.T = 16, 131072
-    assert L.scope_workspace_bytes(ctypes.byref(a2)) == 2 * 16 * 131072 * 4
+    a2.H, a2.T, a2.block_size = 16, 131072, 128
+    ws = L.scope_workspace_bytes(ctypes.byref(a2))
+    assert 2 * 16 * 131072 * 4 < ws < L.scope_static_scratch_bytes()   # config 3 fits the static scratch
 
 
 def test_mask_max_kv():

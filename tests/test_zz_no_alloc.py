@@ -89,7 +89,7 @@ def test_static_scratch_backward_matches_workspace_backward_twice():
 def test_static_scratch_rejects_problems_over_its_limit():
     L = _lib.lib()
     a = _lib.ScopeAttnArgs()
-    a.H, a.T = 64, 1 << 20                  # needs 2*64*2^20*4 bytes of scratch
+    a.H, a.T, a.block_size = 64, 1 << 20, 128   # needs over 2*64*2^20*4 bytes of scratch
     assert L.scope_workspace_bytes(ctypes.byref(a)) > L.scope_static_scratch_bytes()
     assert L.scope_attn_bwd_static_scratch(ctypes.byref(a), None) == -6
     with pytest.raises(ValueError, match="workspace"):
