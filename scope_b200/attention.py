@@ -157,7 +157,10 @@ def sparse_attn(q: Tensor, k: Tensor, v: Tensor, kv_num: Tensor, kv_indices: Ten
                 coeff_sin: Optional[Tensor], cos_tab: Optional[Tensor], sin_tab: Optional[Tensor],
                 b0: Optional[Tensor], slope: Optional[Tensor], delta_main: Optional[Tensor],
                 width: Optional[Tensor], scale: float, beta: float, bias_mode: int, gate: int,
-                gate_lambda: float, gate_tau: float, block_size: int, cuda_cores: bool) -> tuple[Tensor, Tensor]:
+                gate_lambda: float, gate_tau: float, block_size: int,
+                cuda_cores: bool) -> tuple[Tensor, Tensor, Tensor, Tensor]:
+    """Returns out, lse and (qk_aug mode) the augmented dims q_aug / k_aug,
+    which the backward reuses; empty tensors in the other modes."""
     _check_inputs(q, k, v, kv_num, kv_indices, block_size)
     H, T, D = q.shape
     out = _new_like_layout(q)
@@ -167,7 +170,9 @@ def sparse_attn(q: Tensor, k: Tensor, v: Tensor, kv_num: Tensor, kv_indices: Ten
                    cos_tab, sin_tab, b0, slope, delta_main, width, scale, beta, bias_mode, gate, gate_lambda,
                    gate_tau, block_size, q_aug, k_aug, cuda_cores)
     _lib.check(_lib.lib().scope_attn_fwd(ctypes.byref(a), _stream(q.device)), "scope_attn_fwd")
-    return out, lse
+    if q_aug is None:
+        q_aug, k_aug = q.new_empty(0), q.new_empty(0)
+    return out, lse, q_aug, k_aug
 
 
 @sparse_attn.register_fake
@@ -175,7 +180,12 @@ def _(q, k, v, kv_num, kv_indices, q_bitmap, block_info, docs, coeff_cos, coeff_
       b0, slope, delta_main, width, scale, beta, bias_mode, gate, gate_lambda, gate_tau, block_size, cuda_cores):
     H, T, D = q.shape
     out = q.new_empty(T, H, D).permute(1, 0, 2)
-    return out, q.new_empty(H, T, dtype=torch.float32)
+    if bias_mode == BIAS_MODES["qk_aug"]:
+        da = aug_dims(coeff_cos.shape[-1], slope is not None)
+        qa, ka = q.new_empty(H, T, da), q.new_empty(T, da)
+    else:
+        qa, ka = q.new_empty(0), q.new_empty(0)
+    return out, q.new_empty(H, T, dtype=torch.float32), qa, ka
 
 
 @torch.library.custom_op("scope::sparse_attn_bwd", mutates_args=())
@@ -183,14 +193,16 @@ def sparse_attn_bwd(dout: Tensor, q: Tensor, k: Tensor, v: Tensor, out: Tensor, 
                     kv_indices: Tensor, q_bitmap: Tensor, block_info: Tensor, docs: Optional[Tensor],
                     coeff_cos: Optional[Tensor], coeff_sin: Optional[Tensor], cos_tab: Optional[Tensor],
                     sin_tab: Optional[Tensor], b0: Optional[Tensor], slope: Optional[Tensor],
-                    delta_main: Optional[Tensor], width: Optional[Tensor], scale: float, beta: float,
+                    delta_main: Optional[Tensor], width: Optional[Tensor], q_aug: Optional[Tensor],
+                    k_aug: Optional[Tensor], scale: float, beta: float,
                     bias_mode: int, gate: int, gate_lambda: float, gate_tau: float, block_size: int,
                     want_bias_grads: bool, cuda_cores: bool) -> list[Tensor]:
     H, T, D = q.shape
     if dout.stride(-1) != 1:
         dout = dout.contiguous()
     dq, dk, dv = _new_like_layout(q), _new_like_layout(k), _new_like_layout(v)
-    q_aug, k_aug = _prepare_aug(q, coeff_cos, coeff_sin, slope, cos_tab, sin_tab, beta, scale, bias_mode)
+    if q_aug is None or q_aug.numel() == 0:
+        q_aug, k_aug = _prepare_aug(q, coeff_cos, coeff_sin, slope, cos_tab, sin_tab, beta, scale, bias_mode)
     a = _attn_args(q, k, v, out, lse, kv_num, kv_indices, q_bitmap, block_info, docs, coeff_cos, coeff_sin,
                    cos_tab, sin_tab, b0, slope, delta_main, width, scale, beta, bias_mode, gate, gate_lambda,
                    gate_tau, block_size, q_aug, k_aug, cuda_cores)
@@ -226,8 +238,8 @@ def sparse_attn_bwd(dout: Tensor, q: Tensor, k: Tensor, v: Tensor, out: Tensor, 
 
 @sparse_attn_bwd.register_fake
 def _(dout, q, k, v, out, lse, kv_num, kv_indices, q_bitmap, block_info, docs, coeff_cos, coeff_sin, cos_tab,
-      sin_tab, b0, slope, delta_main, width, scale, beta, bias_mode, gate, gate_lambda, gate_tau, block_size,
-      want_bias_grads, cuda_cores):
+      sin_tab, b0, slope, delta_main, width, q_aug, k_aug, scale, beta, bias_mode, gate, gate_lambda, gate_tau,
+      block_size, want_bias_grads, cuda_cores):
     H, T, D = q.shape
     mk = lambda x: x.new_empty(T, H, D).permute(1, 0, 2)  # noqa: E731
     e = lambda: q.new_empty(0, dtype=torch.float32)  # noqa: E731
@@ -249,22 +261,23 @@ def _setup_context(ctx, inputs, output):
     (q, k, v, kv_num, kv_indices, q_bitmap, block_info, docs, coeff_cos, coeff_sin, cos_tab, sin_tab,
      b0, slope, delta_main, width, scale, beta, bias_mode, gate, gate_lambda, gate_tau, block_size,
      cuda_cores) = inputs
-    out, lse = output
+    out, lse, q_aug, k_aug = output
+    ctx.mark_non_differentiable(lse, q_aug, k_aug)
     ctx.save_for_backward(q, k, v, out, lse, kv_num, kv_indices, q_bitmap, block_info, docs, coeff_cos,
-                          coeff_sin, cos_tab, sin_tab, b0, slope, delta_main, width)
+                          coeff_sin, cos_tab, sin_tab, b0, slope, delta_main, width, q_aug, k_aug)
     ctx.scal = (scale, beta, bias_mode, gate, gate_lambda, gate_tau, block_size, cuda_cores)
 
 
-def _backward(ctx, dout, dlse):
+def _backward(ctx, dout, dlse, dq_aug, dk_aug):
     (q, k, v, out, lse, kv_num, kv_indices, q_bitmap, block_info, docs, coeff_cos, coeff_sin, cos_tab,
-     sin_tab, b0, slope, delta_main, width) = ctx.saved_tensors
+     sin_tab, b0, slope, delta_main, width, q_aug, k_aug) = ctx.saved_tensors
     scale, beta, bias_mode, gate, gate_lambda, gate_tau, block_size, cuda_cores = ctx.scal
     nig = ctx.needs_input_grad
     want_bias = any(nig[i] for i in (8, 9, 12, 13, 14, 15))
     g = torch.ops.scope.sparse_attn_bwd(dout, q, k, v, out, lse, kv_num, kv_indices, q_bitmap, block_info, docs,
                                         coeff_cos, coeff_sin, cos_tab, sin_tab, b0, slope, delta_main, width,
-                                        scale, beta, bias_mode, gate, gate_lambda, gate_tau, block_size, want_bias,
-                                        cuda_cores)
+                                        q_aug, k_aug, scale, beta, bias_mode, gate, gate_lambda, gate_tau,
+                                        block_size, want_bias, cuda_cores)
     dq, dk, dv, dcc, dcs, db0, dsl, ddm, dw = g
     pick = lambda t: t if (t is not None and t.numel() > 0) else None  # noqa: E731
     return (dq, dk, dv, None, None, None, None, None, pick(dcc), pick(dcs), None, None, pick(db0), pick(dsl),
@@ -311,7 +324,7 @@ def flex_attention(query: Tensor, key: Tensor, value: Tensor, block_mask: ScopeB
             args.update(b0=f32(sm.b0), delta_main=f32(sm.delta_main), width=f32(sm.width),
                         gate=GATES[sm.gate] if sm.ramp_lambda > 0 else 0, gate_lambda=float(sm.ramp_lambda),
                         gate_tau=float(sm.tau))
-    out, lse = torch.ops.scope.sparse_attn(q, k, v, kv_num, kv_idx, block_mask.q_bitmap, block_mask.block_info,
+    out, lse, _, _ = torch.ops.scope.sparse_attn(q, k, v, kv_num, kv_idx, block_mask.q_bitmap, block_mask.block_info,
                                            docs, args["coeff_cos"], args["coeff_sin"], args["cos_tab"],
                                            args["sin_tab"], args["b0"], args["slope"], args["delta_main"],
                                            args["width"], sc, args["beta"], args["bias_mode"], args["gate"],

@@ -184,6 +184,63 @@ __device__ __forceinline__ int tile_mask_kind(int qb, int kb, bool have_docs, co
     return same_doc ? MASK_CAUSAL : MASK_DOCS;
 }
 
+// One 32-column piece of the dK/dV elementwise stage, thread = kv row j:
+// P = exp2(S * scale*log2e - lse2), dS = P (dP - delta), masked when MASKED.
+template <bool MASKED>
+__device__ __forceinline__ void dkv_piece(float (&s)[32], float (&dp)[32], const float4 *LS, const float4 *DL,
+                                          uint64_t c2, int mk, int lim, const int32_t *docs, int i0, int doc_j) {
+#pragma unroll
+    for (int e4 = 0; e4 < 8; ++e4) {
+        const float4 l4 = LS[e4], d4 = DL[e4];
+#pragma unroll
+        for (int q2 = 0; q2 < 2; ++q2) {
+            const int e = e4 * 4 + 2 * q2;
+            const uint64_t nl = q2 ? f2_pack(-l4.z, -l4.w) : f2_pack(-l4.x, -l4.y);
+            const uint64_t nd = q2 ? f2_pack(-d4.z, -d4.w) : f2_pack(-d4.x, -d4.y);
+            const float2 x = f2_unpack(ffma2(f2_pack(s[e], s[e + 1]), c2, nl));
+            float p0 = ex2(x.x), p1 = ex2(x.y);
+            if (MASKED) {
+                bool v0 = e >= lim, v1 = e + 1 >= lim;
+                if (mk == MASK_DOCS) {
+                    v0 = v0 && (__ldg(docs + i0 + e) == doc_j);
+                    v1 = v1 && (__ldg(docs + i0 + e + 1) == doc_j);
+                }
+                p0 = v0 ? p0 : 0.f;
+                p1 = v1 ? p1 : 0.f;
+            }
+            const float2 ds = f2_unpack(fmul2(f2_pack(p0, p1), fadd2(f2_pack(dp[e], dp[e + 1]), nd)));
+            s[e] = p0;
+            s[e + 1] = p1;
+            dp[e] = ds.x;
+            dp[e + 1] = ds.y;
+        }
+    }
+}
+
+// One 32-column piece of the dQ elementwise stage, thread = q row i; dS -> s.
+template <bool MASKED>
+__device__ __forceinline__ void dq_piece(float (&s)[32], const float (&dp)[32], uint64_t c2, uint64_t nl2,
+                                         uint64_t nd2, int mk, int lim, bool bad, const int32_t *docs, int j0,
+                                         int doc_i) {
+#pragma unroll
+    for (int e = 0; e < 32; e += 2) {
+        const float2 x = f2_unpack(ffma2(f2_pack(s[e], s[e + 1]), c2, nl2));
+        float p0 = ex2(x.x), p1 = ex2(x.y);
+        if (MASKED) {
+            bool v0 = e <= lim && !bad, v1 = e + 1 <= lim && !bad;
+            if (mk == MASK_DOCS && docs && !bad) {
+                v0 = v0 && (__ldg(docs + j0 + e) == doc_i);
+                v1 = v1 && (__ldg(docs + j0 + e + 1) == doc_i);
+            }
+            p0 = v0 ? p0 : 0.f;
+            p1 = v1 ? p1 : 0.f;
+        }
+        const float2 ds = f2_unpack(fmul2(f2_pack(p0, p1), fadd2(f2_pack(dp[e], dp[e + 1]), nd2)));
+        s[e] = ds.x;
+        s[e + 1] = ds.y;
+    }
+}
+
 // ============================================================================ dK / dV
 template <int DA>
 struct KVL {
@@ -352,11 +409,14 @@ __global__ void __launch_bounds__(kThreads, 1) dkv_kernel(const __grid_constant_
         const int32_t *dmax = p.block_info ? p.block_info + 3 * p.QB : nullptr;
         bool alive = true;
         const int nu = 2 * nq;
+        int mk = MASK_DOCS, qb = 0;
         for (int u = 0; u < nu && alive; ++u) {
             const int t = u >> 1, half = u & 1, st = t & 1;
-            if (half == 0 && !cx.waitw(q_full + st, (t >> 1) & 1)) { alive = false; break; }
-            const int qb = stage_qb[st];
-            const int mk = tile_mask_kind(qb, kb, have_docs, dmin, dmax);
+            if (half == 0) {
+                if (!cx.waitw(q_full + st, (t >> 1) & 1)) { alive = false; break; }
+                qb = stage_qb[st];
+                mk = tile_mask_kind(qb, kb, have_docs, dmin, dmax);
+            }
             if (!cx.waitw(sdp_full + half, t & 1)) { alive = false; break; }
             tc_fence_after();
             float s[32], dp[32];
@@ -367,23 +427,9 @@ __global__ void __launch_bounds__(kThreads, 1) dkv_kernel(const __grid_constant_
             const float4 *DL = reinterpret_cast<const float4 *>(sb + L::SDEL) + col0 / 4;
             const int i0 = qb * BM + col0;
             const int lim = j - i0;                     // column e visible iff e >= lim (causal: j <= i)
-#pragma unroll
-            for (int e4 = 0; e4 < 8; ++e4) {
-                const float4 l4 = LS[e4], d4 = DL[e4];
-                const float lv[4] = {l4.x, l4.y, l4.z, l4.w}, dv[4] = {d4.x, d4.y, d4.z, d4.w};
-#pragma unroll
-                for (int q = 0; q < 4; ++q) {
-                    const int e = e4 * 4 + q;
-                    float pr = ex2(fmaf(s[e], p.scale_log2, -lv[q]));
-                    if (mk != MASK_FULL) {
-                        bool valid = e >= lim;
-                        if (mk == MASK_DOCS) valid = valid && (__ldg(p.docs + i0 + e) == doc_j);
-                        pr = valid ? pr : 0.f;
-                    }
-                    dp[e] = pr * (dp[e] - dv[q]);
-                    s[e] = pr;
-                }
-            }
+            const uint64_t c2 = f2_pack(p.scale_log2, p.scale_log2);
+            if (mk == MASK_FULL) dkv_piece<false>(s, dp, LS, DL, c2, mk, lim, p.docs, i0, doc_j);
+            else dkv_piece<true>(s, dp, LS, DL, c2, mk, lim, p.docs, i0, doc_j);
             st_bf16x32(tmem + lb + slot_s(half) + ch * 16, s);
             st_bf16x32(tmem + lb + slot_dp(half) + ch * 16, dp);
             tmem_wait_st();
@@ -688,28 +734,25 @@ __global__ void __launch_bounds__(kThreads, 1) dq_kernel(const __grid_constant__
         float gsl = 0.f;
         bool alive = true;
         const int nu = 2 * n;
+        int kb = 0, mk = MASK_DOCS;
+        bool bad = true;
+        const uint64_t c2 = f2_pack(p.scale_log2, p.scale_log2), nl2 = f2_pack(-l2, -l2), nd2 = f2_pack(-dl, -dl);
         for (int u = 0; u < nu && alive; ++u) {
             const int jj = u >> 1, half = u & 1, st = jj & 1;
-            if (half == 0 && !cx.waitw(kv_full + st, (jj >> 1) & 1)) { alive = false; break; }
-            const int kb = stage_kb[st];
-            const bool bad = kb < 0 || kb >= p.QB;
-            const int mk = bad ? MASK_DOCS : tile_mask_kind(qb, kb, have_docs, dmin, dmax);
+            if (half == 0) {
+                if (!cx.waitw(kv_full + st, (jj >> 1) & 1)) { alive = false; break; }
+                kb = stage_kb[st];
+                bad = kb < 0 || kb >= p.QB;
+                mk = bad ? MASK_DOCS : tile_mask_kind(qb, kb, have_docs, dmin, dmax);
+            }
             if (!cx.waitw(sdp_full + half, jj & 1)) { alive = false; break; }
             tc_fence_after();
             float s[32], dp[32];
             ld_s_dp(tmem + lb + slot_s(half) + ch * 32, tmem + lb + slot_dp(half) + ch * 32, s, dp);
             const int j0 = kb * BM + half * 64 + ch * 32;
             const int lim = i - j0;                     // column e visible iff e <= lim (causal: j <= i)
-#pragma unroll
-            for (int e = 0; e < 32; ++e) {
-                float pr = ex2(fmaf(s[e], p.scale_log2, -l2));
-                if (mk != MASK_FULL) {
-                    bool valid = e <= lim && !bad;
-                    if (mk == MASK_DOCS && have_docs) valid = valid && (__ldg(p.docs + (bad ? 0 : j0 + e)) == doc_i);
-                    pr = valid ? pr : 0.f;
-                }
-                s[e] = pr * (dp[e] - dl);
-            }
+            if (mk == MASK_FULL) dq_piece<false>(s, dp, c2, nl2, nd2, mk, lim, bad, p.docs, j0, doc_i);
+            else dq_piece<true>(s, dp, c2, nl2, nd2, mk, lim, bad, p.docs, j0, doc_i);
             if (slope_acc && !bad) {
 #pragma unroll
                 for (int e = 0; e < 32; ++e) {

@@ -33,45 +33,74 @@ __device__ __forceinline__ void store_elem<float>(float *p, float v) { *p = v; }
 template <>
 __device__ __forceinline__ void store_elem<__nv_bfloat16>(__nv_bfloat16 *p, float v) { *p = __float2bfloat16_rn(v); }
 
-// one thread per (h, t) row of q_aug; head 0 also writes the k_aug row.
+// one thread per (h, t) row of q_aug (head 0's threads also write the k_aug
+// row t); each row is assembled in registers and stored as 16-byte vectors.
 // Operation order mirrors the eager reference: (A*c) + (B*s), then * s_scale.
 template <typename E>
+__device__ __forceinline__ void store_row(E *dst, const float *v, int n);
+template <>
+__device__ __forceinline__ void store_row<__nv_bfloat16>(__nv_bfloat16 *dst, const float *v, int n) {
+    uint4 *d = reinterpret_cast<uint4 *>(dst);
+    for (int j = 0; j < n; j += 8) {
+        __nv_bfloat162 w[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) w[e] = __floats2bfloat162_rn(v[j + 2 * e], v[j + 2 * e + 1]);
+        d[j / 8] = *reinterpret_cast<uint4 *>(w);
+    }
+}
+template <>
+__device__ __forceinline__ void store_row<float>(float *dst, const float *v, int n) {
+    float4 *d = reinterpret_cast<float4 *>(dst);
+    for (int j = 0; j < n; j += 4) d[j / 4] = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+}
+
+template <typename E, int DA>
 __global__ void qk_aug_kernel(const float *__restrict__ cc, const float *__restrict__ cs,
                               const float *__restrict__ slope, const uint16_t *__restrict__ ct,
-                              const uint16_t *__restrict__ st, int tab_len, int H, int T, int K, int da,
-                              float s, E *__restrict__ q_aug, E *__restrict__ k_aug) {
-    int64_t row = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+                              const uint16_t *__restrict__ st, int tab_len, int H, int T, int K, float s,
+                              E *__restrict__ q_aug, E *__restrict__ k_aug) {
+    const int64_t row = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (row >= (int64_t)H * T) return;
-    int t = (int)(row % T);
-    E *qo = q_aug + row * da;
-    for (int k = 0; k < K; ++k) {
-        float c = bf16_to_f32(ct[(int64_t)k * tab_len + t]);
-        float sn = bf16_to_f32(st[(int64_t)k * tab_len + t]);
-        float A = cc[row * K + k], B = cs[row * K + k];
-        float qc = __fadd_rn(__fmul_rn(A, c), __fmul_rn(B, sn));
-        float qs = __fsub_rn(__fmul_rn(A, sn), __fmul_rn(B, c));
-        store_elem(qo + k, __fmul_rn(qc, s));
-        store_elem(qo + K + k, __fmul_rn(qs, s));
-    }
-    int used = 2 * K;
-    if (slope) {
-        store_elem(qo + used, __fmul_rn(-slope[row], s));
-        ++used;
-    }
-    for (int j = used; j < da; ++j) store_elem(qo + j, 0.0f);
-    if (row < T) {   // head 0 row t: the head-independent k_aug row
-        E *ko = k_aug + (int64_t)t * da;
-        for (int k = 0; k < K; ++k) {
-            store_elem(ko + k, __fmul_rn(bf16_to_f32(ct[(int64_t)k * tab_len + t]), s));
-            store_elem(ko + K + k, __fmul_rn(bf16_to_f32(st[(int64_t)k * tab_len + t]), s));
+    const int t = (int)(row % T);
+    float v[DA], w[DA];
+#pragma unroll
+    for (int j = 0; j < DA; ++j) {
+        float qv = 0.f, kv = 0.f;
+        if (j < 2 * K) {
+            const int k = j < K ? j : j - K;
+            const float c = bf16_to_f32(__ldg(ct + (int64_t)k * tab_len + t));
+            const float sn = bf16_to_f32(__ldg(st + (int64_t)k * tab_len + t));
+            const float A = __ldg(cc + row * K + k), B = __ldg(cs + row * K + k);
+            const float x = j < K ? __fadd_rn(__fmul_rn(A, c), __fmul_rn(B, sn))
+                                  : __fsub_rn(__fmul_rn(A, sn), __fmul_rn(B, c));
+            qv = __fmul_rn(x, s);
+            kv = __fmul_rn(j < K ? c : sn, s);
+        } else if (j == 2 * K && slope) {
+            qv = __fmul_rn(-__ldg(slope + row), s);
+            kv = __fmul_rn((float)t, s);
         }
-        int u = 2 * K;
-        if (slope) {
-            store_elem(ko + u, __fmul_rn((float)t, s));
-            ++u;
-        }
-        for (int j = u; j < da; ++j) store_elem(ko + j, 0.0f);
+        v[j] = qv;
+        w[j] = kv;
     }
+    store_row<E>(q_aug + row * DA, v, DA);
+    if (row < T) store_row<E>(k_aug + (int64_t)t * DA, w, DA);   // head 0 row t: the head-independent k_aug row
+}
+
+template <typename E>
+int launch_aug(const float *cc, const float *cs, const float *slope, const uint16_t *ct, const uint16_t *st,
+               int tab_len, int H, int T, int K, int da, float s, void *q_aug, void *k_aug, cudaStream_t stream) {
+    const int64_t rows = (int64_t)H * T;
+    const unsigned grid = (unsigned)((rows + 127) / 128);
+    E *qa = reinterpret_cast<E *>(q_aug), *ka = reinterpret_cast<E *>(k_aug);
+    switch (da) {
+        case 16: qk_aug_kernel<E, 16><<<grid, 128, 0, stream>>>(cc, cs, slope, ct, st, tab_len, H, T, K, s, qa, ka); break;
+        case 32: qk_aug_kernel<E, 32><<<grid, 128, 0, stream>>>(cc, cs, slope, ct, st, tab_len, H, T, K, s, qa, ka); break;
+        case 48: qk_aug_kernel<E, 48><<<grid, 128, 0, stream>>>(cc, cs, slope, ct, st, tab_len, H, T, K, s, qa, ka); break;
+        case 64: qk_aug_kernel<E, 64><<<grid, 128, 0, stream>>>(cc, cs, slope, ct, st, tab_len, H, T, K, s, qa, ka); break;
+        default: return SCOPE_ERR_INVALID;
+    }
+    SCOPE_CHECK_LAUNCH();
+    return SCOPE_OK;
 }
 
 }  // namespace spectral
@@ -100,19 +129,14 @@ extern "C" int scope_qk_aug_prepare(const float *coeff_cos, const float *coeff_s
     if (!(scale > 0.f) || beta < 0.f) return SCOPE_ERR_INVALID;
     // the reference forms s = sqrt(beta/scale) in double precision and rounds it once
     float s = (float)sqrt((double)beta / (double)scale);
-    int64_t rows = (int64_t)H * T;
-    unsigned grid = (unsigned)((rows + 127) / 128);
+    if (d_aug > 64) return SCOPE_ERR_INVALID;
+    if ((reinterpret_cast<uintptr_t>(q_aug) | reinterpret_cast<uintptr_t>(k_aug)) & 15) return SCOPE_ERR_ALIGN;
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
     if (dtype == SCOPE_BF16)
-        spectral::qk_aug_kernel<__nv_bfloat16><<<grid, 128, 0, st>>>(
-            coeff_cos, coeff_sin, slope, cos_tab, sin_tab, tab_len, H, T, K, d_aug, s,
-            reinterpret_cast<__nv_bfloat16 *>(q_aug), reinterpret_cast<__nv_bfloat16 *>(k_aug));
-    else if (dtype == SCOPE_F32)
-        spectral::qk_aug_kernel<float><<<grid, 128, 0, st>>>(coeff_cos, coeff_sin, slope, cos_tab, sin_tab, tab_len,
-                                                              H, T, K, d_aug, s, reinterpret_cast<float *>(q_aug),
-                                                              reinterpret_cast<float *>(k_aug));
-    else
-        return SCOPE_ERR_DTYPE;
-    SCOPE_CHECK_LAUNCH();
-    return SCOPE_OK;
+        return spectral::launch_aug<__nv_bfloat16>(coeff_cos, coeff_sin, slope, cos_tab, sin_tab, tab_len, H, T, K,
+                                                   d_aug, s, q_aug, k_aug, st);
+    if (dtype == SCOPE_F32)
+        return spectral::launch_aug<float>(coeff_cos, coeff_sin, slope, cos_tab, sin_tab, tab_len, H, T, K, d_aug, s,
+                                           q_aug, k_aug, st);
+    return SCOPE_ERR_DTYPE;
 }
