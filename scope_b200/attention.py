@@ -65,11 +65,14 @@ class SpectralScoreMod:
     impl: str = "qk_aug"
 
 
-def _hd(t: Optional[Tensor]) -> Optional[Tensor]:
-    """[1,H,T,...] -> [H,T,...]"""
+def _hd(t: Optional[Tensor], rank: int) -> Optional[Tensor]:
+    """Drop a leading batch dim of size 1 from a tensor whose unbatched rank is
+    ``rank``, as a view (squeeze, whose backward is a view too; indexing with
+    t[0] would make autograd materialise a zero tensor and copy every gradient
+    into it)."""
     if t is None:
         return None
-    return t[0] if t.dim() >= 1 and t.shape[0] == 1 and t.dim() in (3, 4) else t
+    return t.squeeze(0) if t.dim() == rank + 1 and t.shape[0] == 1 else t
 
 
 def _attn_args(q, k, v, out, lse, kv_num, kv_indices, q_bitmap, block_info, docs,
@@ -300,7 +303,7 @@ def flex_attention(query: Tensor, key: Tensor, value: Tensor, block_mask: ScopeB
     squeeze = query.dim() == 4
     if squeeze and query.shape[0] != 1:
         raise ValueError("batch size must be 1 (as in the reference)")
-    q, k, v = (_hd(t) if squeeze else t for t in (query, key, value))
+    q, k, v = (_hd(t, 3) for t in (query, key, value))
     D = q.shape[-1]
     sc = float(scale) if scale is not None else 1.0 / math.sqrt(D)
     bs = block_mask.BLOCK_SIZE[0]
@@ -315,13 +318,13 @@ def flex_attention(query: Tensor, key: Tensor, value: Tensor, block_mask: ScopeB
             raise ValueError("SpectralScoreMod.impl must be score_mod|qk_aug")
         if sm.gate not in GATES:
             raise ValueError("gate must be one of: none|softplus|relu")
-        f32 = lambda t: None if t is None else _hd(t).to(torch.float32).contiguous()  # noqa: E731
-        args.update(coeff_cos=f32(sm.coeff_cos), coeff_sin=f32(sm.coeff_sin),
+        f32 = lambda t, rank: None if t is None else _hd(t, rank).to(torch.float32).contiguous()  # noqa: E731
+        args.update(coeff_cos=f32(sm.coeff_cos, 3), coeff_sin=f32(sm.coeff_sin, 3),
                     cos_tab=sm.cos_tab.to(torch.bfloat16).contiguous(),
-                    sin_tab=sm.sin_tab.to(torch.bfloat16).contiguous(), slope=f32(sm.slope),
+                    sin_tab=sm.sin_tab.to(torch.bfloat16).contiguous(), slope=f32(sm.slope, 2),
                     beta=float(sm.beta), bias_mode=BIAS_MODES[sm.impl])
         if sm.impl == "score_mod":
-            args.update(b0=f32(sm.b0), delta_main=f32(sm.delta_main), width=f32(sm.width),
+            args.update(b0=f32(sm.b0, 2), delta_main=f32(sm.delta_main, 2), width=f32(sm.width, 2),
                         gate=GATES[sm.gate] if sm.ramp_lambda > 0 else 0, gate_lambda=float(sm.ramp_lambda),
                         gate_tau=float(sm.tau))
     out, lse, _, _ = torch.ops.scope.sparse_attn(q, k, v, kv_num, kv_idx, block_mask.q_bitmap, block_mask.block_info,

@@ -40,7 +40,8 @@ using namespace tc;
 
 constexpr int BM = 128;
 constexpr int HD = 64;
-constexpr int kThreads = 192;
+constexpr int kThreads = 320;   // producer, issuer, 8 softmax warps (two per TMEM lane quadrant)
+constexpr int kSoftmax = 256;
 constexpr uint32_t kTmemCols = 256;
 constexpr uint32_t S_COL = 0, O_COL = 128, P_COL = 192;
 
@@ -61,7 +62,8 @@ struct Layout {
     static constexpr uint32_t V = align1k(TILE + NA * ATILE);
     static constexpr uint32_t STAGE = V + TILE;
     static constexpr uint32_t BAR = STAGE0 + 2 * STAGE;
-    static constexpr uint32_t TOTAL = BAR + 128;
+    static constexpr uint32_t XCH = BAR + 256;                   // float[2 parity][2 halves][128 rows] + l[2][128]
+    static constexpr uint32_t TOTAL = XCH + 3 * 1024;
     static constexpr uint32_t KV_BYTES = 2 * TILE + NA * ATILE;  // expected TMA bytes per stage
     static constexpr uint32_t Q_BYTES = TILE + NA * ATILE;
 };
@@ -89,8 +91,11 @@ __global__ void __launch_bounds__(kThreads, 2) fwd_kernel(const __grid_constant_
     uint64_t *bars = reinterpret_cast<uint64_t *>(smem + L::BAR);
     uint64_t *q_full = bars + 0, *kv_full = bars + 1, *kv_empty = bars + 3;
     uint64_t *s_full = bars + 5, *s_free = bars + 6, *p_full = bars + 7, *o_done = bars + 8;
-    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 9);
+    uint64_t *xchg = bars + 9;                                   // [4]: one per TMEM lane quadrant
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 13);
     volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
+    float *xmax = reinterpret_cast<float *>(smem + L::XCH);      // [2][2][128]
+    float *xsum = xmax + 512;                                    // [2][128]
 
     const int qb = blockIdx.x, h = blockIdx.y;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -105,9 +110,10 @@ __global__ void __launch_bounds__(kThreads, 2) fwd_kernel(const __grid_constant_
         mbar_init(kv_empty + 0, 1);
         mbar_init(kv_empty + 1, 1);
         mbar_init(s_full, 1);
-        mbar_init(s_free, 128);
-        mbar_init(p_full, 128);
+        mbar_init(s_free, kSoftmax);
+        mbar_init(p_full, kSoftmax);
         mbar_init(o_done, 1);
+        for (int q = 0; q < 4; ++q) mbar_init(xchg + q, 64);
         *abort_flag = 0;
         fence_mbar_init();
     }
@@ -202,62 +208,71 @@ __global__ void __launch_bounds__(kThreads, 2) fwd_kernel(const __grid_constant_
         }
     } else {
         // ------------------------------------------------------------ softmax + epilogue
+        // thread = (query row r, column half ch): S columns [64ch, 64ch+64), O and P columns [32ch, 32ch+32)
         const int quad = warp & 3;
+        const int ch = (warp - 2) >> 2;
         const int r = quad * 32 + lane;
         const int i = qb * BM + r;
         const uint32_t lane_base = (uint32_t)(quad * 32) << 16;
-        const uint32_t tS = tmem + lane_base + S_COL, tO = tmem + lane_base + O_COL, tP = tmem + lane_base + P_COL;
+        const uint32_t tS = tmem + lane_base + S_COL + ch * 64, tO = tmem + lane_base + O_COL + ch * 32,
+                       tP = tmem + lane_base + P_COL + ch * 32;
         const bool have_docs = p.docs != nullptr;
         const int doc_i = have_docs ? p.docs[i] : 0;
         const int32_t *dmin = p.block_info ? p.block_info + 2 * p.QB : nullptr;
         const int32_t *dmax = p.block_info ? p.block_info + 3 * p.QB : nullptr;
         const bool q_uniform = !have_docs || (dmin && dmin[qb] == dmax[qb]);
+        const uint64_t c2 = f2_pack(p.scale_log2, p.scale_log2);
         float m = -INFINITY, l = 0.f;
         bool alive = true;
+        int xphase = 0;                         // completed phases of this quadrant's exchange barrier
         for (int j = 0; j < n && alive; ++j) {
             int kb = list[j];
             const bool bad = kb < 0 || kb >= p.QB;
-            if (bad && r == 0) set_err(p.err, SCOPE_DEVERR_INDEX);
+            if (bad && r == 0 && ch == 0) set_err(p.err, SCOPE_DEVERR_INDEX);
             // full tile: no mask; one document: causal compare only; else per-element document ids
             const bool same_doc = !have_docs || (q_uniform && dmin && dmin[kb] == dmax[kb] && dmin[kb] == dmin[qb]);
             const int mk = bad ? 3 : ((kb < qb && same_doc) ? 0 : (same_doc ? 1 : 2));
             if (!warp_wait(s_full, j & 1)) { give_up(); alive = false; break; }
             tc_fence_after();
-            float x[BM];
+            float x[64];
             {
-                uint32_t u0[32], u1[32], u2[32], u3[32];
+                uint32_t u0[32], u1[32];
                 tmem_ld32_nw(tS, u0);
                 tmem_ld32_nw(tS + 32, u1);
-                tmem_ld32_nw(tS + 64, u2);
-                tmem_ld32_nw(tS + 96, u3);
                 tmem_wait_ld();
                 pin(u0);
                 pin(u1);
-                pin(u2);
-                pin(u3);
 #pragma unroll
-                for (int e = 0; e < 32; ++e) {
-                    x[e] = __uint_as_float(u0[e]) * p.scale_log2;
-                    x[32 + e] = __uint_as_float(u1[e]) * p.scale_log2;
-                    x[64 + e] = __uint_as_float(u2[e]) * p.scale_log2;
-                    x[96 + e] = __uint_as_float(u3[e]) * p.scale_log2;
+                for (int e = 0; e < 32; e += 2) {
+                    const float2 a = f2_unpack(fmul2(f2_pack(__uint_as_float(u0[e]), __uint_as_float(u0[e + 1])), c2));
+                    const float2 b = f2_unpack(fmul2(f2_pack(__uint_as_float(u1[e]), __uint_as_float(u1[e + 1])), c2));
+                    x[e] = a.x;
+                    x[e + 1] = a.y;
+                    x[32 + e] = b.x;
+                    x[32 + e + 1] = b.y;
                 }
             }
             tc_fence_before();
             mbar_arrive(s_free);
             if (mk != 0) {
-                const int j0 = kb * BM;
+                const int j0 = kb * BM + ch * 64;
                 const int lim = i - j0;                 // column c visible iff c <= lim
 #pragma unroll
-                for (int c = 0; c < BM; ++c) {
+                for (int c = 0; c < 64; ++c) {
                     bool valid = mk != 3 && c <= lim;
                     if (mk == 2) valid = valid && (__ldg(p.docs + j0 + c) == doc_i);
                     if (!valid) x[c] = -INFINITY;
                 }
             }
-            float mx = x[0];
+            float pmx = x[0];
 #pragma unroll
-            for (int c = 1; c < BM; ++c) mx = fmaxf(mx, x[c]);
+            for (int c = 1; c < 64; ++c) pmx = fmaxf(pmx, x[c]);
+            // row max across the two column halves
+            xmax[(j & 1) * 256 + ch * 128 + r] = pmx;
+            mbar_arrive(xchg + quad);
+            if (!warp_wait(xchg + quad, xphase & 1)) { give_up(); alive = false; break; }
+            ++xphase;
+            const float mx = fmaxf(pmx, xmax[(j & 1) * 256 + (1 - ch) * 128 + r]);
             float alpha = 1.f;
             bool rescale = false;
             if (mx > m + 8.f) {     // move the reference max only when it grows by > 2^8
@@ -266,11 +281,14 @@ __global__ void __launch_bounds__(kThreads, 2) fwd_kernel(const __grid_constant_
                 rescale = true;
             }
             const float mref = (m == -INFINITY) ? 0.f : m;
+            const uint64_t nm2 = f2_pack(-mref, -mref);
             float rs = 0.f;
 #pragma unroll
-            for (int c = 0; c < BM; ++c) {
-                x[c] = ex2(x[c] - mref);
-                rs += x[c];
+            for (int c = 0; c < 64; c += 2) {
+                const float2 d = f2_unpack(fadd2(f2_pack(x[c], x[c + 1]), nm2));
+                x[c] = ex2(d.x);
+                x[c + 1] = ex2(d.y);
+                rs += x[c] + x[c + 1];
             }
             l = l * alpha + rs;
             if (j > 0) {
@@ -278,57 +296,60 @@ __global__ void __launch_bounds__(kThreads, 2) fwd_kernel(const __grid_constant_
                 tc_fence_after();
                 // tcgen05.ld/st are warp-collective: rescale O whenever any row of the warp needs it
                 if (__any_sync(0xffffffffu, rescale)) {
+                    uint32_t o[32];
+                    tmem_ld32_nw(tO, o);
+                    tmem_wait_ld();
+                    pin(o);
 #pragma unroll
-                    for (int c = 0; c < HD / 16; ++c) {
-                        uint32_t o[16];
-                        tmem_ld16(tO + c * 16, o);
-                        tmem_wait_ld();
-#pragma unroll
-                        for (int e = 0; e < 16; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * alpha);
-                        tmem_st16(tO + c * 16, o);
-                    }
+                    for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * alpha);
+                    tmem_st32(tO, o);
                 }
             }
+            {
+                uint32_t pk[32];
 #pragma unroll
-            for (int c = 0; c < 4; ++c) {
-                uint32_t pk[16];
-#pragma unroll
-                for (int e = 0; e < 16; ++e) pk[e] = pack_bf16(x[c * 32 + 2 * e], x[c * 32 + 2 * e + 1]);
-                tmem_st16(tP + c * 16, pk);
+                for (int e = 0; e < 32; ++e) pk[e] = pack_bf16(x[2 * e], x[2 * e + 1]);
+                tmem_st32(tP, pk);
             }
             tmem_wait_st();
             tc_fence_before();
             mbar_arrive(p_full);
         }
-        // epilogue: O / l -> bf16, lse
-        __nv_bfloat16 *orow = p.out + (int64_t)h * p.o_sh + (int64_t)i * p.o_st;
-        const float inv = (l > 0.f) ? 1.f / l : 0.f;
+        // epilogue: row sum across the halves, O / l -> bf16, lse
         bool have_o = false;
+        if (alive) {
+            xsum[ch * 128 + r] = l;
+            mbar_arrive(xchg + quad);
+            alive = warp_wait(xchg + quad, xphase & 1);
+            if (!alive) give_up();
+        }
+        const float ltot = alive ? l + xsum[(1 - ch) * 128 + r] : 0.f;
         if (alive && n > 0) {
             have_o = warp_wait(o_done, (n - 1) & 1);
             if (!have_o) give_up();
             tc_fence_after();
         }
-#pragma unroll
-        for (int c = 0; c < HD / 16; ++c) {
-            uint32_t o[16];
+        __nv_bfloat16 *orow = p.out + (int64_t)h * p.o_sh + (int64_t)i * p.o_st + ch * 32;
+        const float inv = (ltot > 0.f) ? 1.f / ltot : 0.f;
+        {
+            uint32_t o[32];
             if (have_o) {
-                tmem_ld16(tO + c * 16, o);
+                tmem_ld32_nw(tO, o);
                 tmem_wait_ld();
+                pin(o);
             } else {
 #pragma unroll
-                for (int e = 0; e < 16; ++e) o[e] = 0u;
+                for (int e = 0; e < 32; ++e) o[e] = 0u;
             }
-            uint32_t w[8];
+            uint32_t w[16];
 #pragma unroll
-            for (int e = 0; e < 8; ++e)
-                w[e] = pack_bf16(__uint_as_float(o[2 * e]) * inv, __uint_as_float(o[2 * e + 1]) * inv);
-            uint4 *dst = reinterpret_cast<uint4 *>(orow + c * 16);
-            dst[0] = make_uint4(w[0], w[1], w[2], w[3]);
-            dst[1] = make_uint4(w[4], w[5], w[6], w[7]);
+            for (int e = 0; e < 16; ++e) w[e] = pack_bf16(__uint_as_float(o[2 * e]) * inv, __uint_as_float(o[2 * e + 1]) * inv);
+            uint4 *dst = reinterpret_cast<uint4 *>(orow);
+#pragma unroll
+            for (int e = 0; e < 4; ++e) dst[e] = make_uint4(w[4 * e], w[4 * e + 1], w[4 * e + 2], w[4 * e + 3]);
         }
-        if (p.lse)
-            p.lse[(int64_t)h * p.T + i] = (l > 0.f) ? (m + log2f(l)) * 0.69314718055994531f : -INFINITY;
+        if (p.lse && ch == 0)
+            p.lse[(int64_t)h * p.T + i] = (ltot > 0.f) ? (m + log2f(ltot)) * 0.69314718055994531f : -INFINITY;
     }
     tc_fence_before();
     __syncthreads();
