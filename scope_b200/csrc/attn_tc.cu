@@ -68,6 +68,19 @@ struct Layout {
     static constexpr uint32_t Q_BYTES = TILE + NA * ATILE;
 };
 
+// Tile classes: 0 every element visible (kv block before the q block, one
+// document), 1 one document (causal test only), 2 straddles a document boundary
+// (element document ids needed).  block_info rows 2, 3: per-block doc min / max.
+__device__ __forceinline__ int tile_kind(int qb, int kb, bool have_docs, const int32_t *block_info, int QB) {
+    bool same_doc = !have_docs;
+    if (have_docs && block_info) {
+        const int a = block_info[2 * QB + qb], b = block_info[3 * QB + qb];
+        const int c = block_info[2 * QB + kb], d = block_info[3 * QB + kb];
+        same_doc = (a == b) & (c == d) & (a == c);
+    }
+    return (kb < qb && same_doc) ? 0 : (same_doc ? 1 : 2);
+}
+
 struct FwdParams {
     int H, T, QB, kv_stride;
     const int32_t *kv_num, *kv_idx, *block_info, *docs;
@@ -93,6 +106,8 @@ __global__ void __launch_bounds__(kThreads, 2) fwd_kernel(const __grid_constant_
     uint64_t *s_full = bars + 5, *s_free = bars + 6, *p_full = bars + 7, *o_done = bars + 8;
     uint64_t *xchg = bars + 9;                                   // [4]: one per TMEM lane quadrant
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 13);
+    volatile int *stage_kb = reinterpret_cast<volatile int *>(bars + 14);   // [2] kv block of each stage
+    volatile int *stage_mk = stage_kb + 2;                                  // [2] its mask kind
     volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
     float *xmax = reinterpret_cast<float *>(smem + L::XCH);      // [2][2][128]
     float *xsum = xmax + 512;                                    // [2][128]
@@ -151,7 +166,10 @@ __global__ void __launch_bounds__(kThreads, 2) fwd_kernel(const __grid_constant_
                     break;
                 }
                 int kb = list[j];
-                if (kb < 0 || kb >= p.QB) kb = 0;   // the softmax masks this tile and flags it
+                const bool bad = kb < 0 || kb >= p.QB;
+                stage_kb[s] = kb;
+                stage_mk[s] = bad ? 3 : tile_kind(qb, kb, p.docs != nullptr, p.block_info, p.QB);
+                if (bad) kb = 0;   // the softmax masks this tile and flags it
                 uint8_t *st = smem + L::STAGE0 + s * L::STAGE;
                 mbar_expect_tx(kv_full + s, L::KV_BYTES);
                 tma_load_3d(&maps.k, st + L::K, kv_full + s, 0, kb * BM, h);
@@ -218,20 +236,16 @@ __global__ void __launch_bounds__(kThreads, 2) fwd_kernel(const __grid_constant_
                        tP = tmem + lane_base + P_COL + ch * 32;
         const bool have_docs = p.docs != nullptr;
         const int doc_i = have_docs ? p.docs[i] : 0;
-        const int32_t *dmin = p.block_info ? p.block_info + 2 * p.QB : nullptr;
-        const int32_t *dmax = p.block_info ? p.block_info + 3 * p.QB : nullptr;
-        const bool q_uniform = !have_docs || (dmin && dmin[qb] == dmax[qb]);
         const uint64_t c2 = f2_pack(p.scale_log2, p.scale_log2);
         float m = -INFINITY, l = 0.f;
         bool alive = true;
         int xphase = 0;                         // completed phases of this quadrant's exchange barrier
         for (int j = 0; j < n && alive; ++j) {
-            int kb = list[j];
-            const bool bad = kb < 0 || kb >= p.QB;
-            if (bad && r == 0 && ch == 0) set_err(p.err, SCOPE_DEVERR_INDEX);
-            // full tile: no mask; one document: causal compare only; else per-element document ids
-            const bool same_doc = !have_docs || (q_uniform && dmin && dmin[kb] == dmax[kb] && dmin[kb] == dmin[qb]);
-            const int mk = bad ? 3 : ((kb < qb && same_doc) ? 0 : (same_doc ? 1 : 2));
+            // the producer classified this tile: 0 full, 1 causal only, 2 document ids, 3 bad index
+            if (!warp_wait(kv_full + (j & 1), (j >> 1) & 1)) { give_up(); alive = false; break; }
+            const int kb = stage_kb[j & 1];
+            const int mk = stage_mk[j & 1];
+            if (mk == 3 && r == 0 && ch == 0) set_err(p.err, SCOPE_DEVERR_INDEX);
             if (!warp_wait(s_full, j & 1)) { give_up(); alive = false; break; }
             tc_fence_after();
             float x[64];

@@ -176,10 +176,16 @@ __device__ __forceinline__ void store_row32(uint32_t taddr, float mul, __nv_bflo
 // Tile masking: every element of a full tile is visible; a tile whose q and kv
 // blocks lie in one document needs only the causal test (one compare); only
 // tiles that straddle a document boundary read document ids per element.
+// The producer thread classifies each tile (it runs ahead of the elementwise
+// warps) and hands the class over in shared memory with the tile's block index.
 enum MaskKind { MASK_FULL = 0, MASK_CAUSAL = 1, MASK_DOCS = 2 };
-__device__ __forceinline__ int tile_mask_kind(int qb, int kb, bool have_docs, const int32_t *dmin,
-                                              const int32_t *dmax) {
-    bool same_doc = !have_docs || (dmin && dmin[qb] == dmax[qb] && dmin[kb] == dmax[kb] && dmin[qb] == dmin[kb]);
+__device__ __forceinline__ int tile_mask_kind(int qb, int kb, bool have_docs, const int32_t *block_info, int QB) {
+    bool same_doc = !have_docs;
+    if (have_docs && block_info) {
+        const int a = block_info[2 * QB + qb], b = block_info[3 * QB + qb];
+        const int c = block_info[2 * QB + kb], d = block_info[3 * QB + kb];
+        same_doc = (a == b) & (c == d) & (a == c);
+    }
     if (kb < qb && same_doc) return MASK_FULL;
     return same_doc ? MASK_CAUSAL : MASK_DOCS;
 }
@@ -284,9 +290,10 @@ __global__ void __launch_bounds__(kThreads, 1) dkv_kernel(const __grid_constant_
     uint64_t *bars = reinterpret_cast<uint64_t *>(smem + L::BAR);
     uint64_t *kv_full = bars + 0, *q_full = bars + 1, *q_empty = bars + 3, *sdp_full = bars + 5, *p_full = bars + 7,
              *acc_done = bars + 9;
-    volatile int *stage_qb = reinterpret_cast<volatile int *>(bars + 10);
-    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 11);
-    volatile int *last_flag = reinterpret_cast<volatile int *>(bars + 12);
+    volatile int *stage_qb = reinterpret_cast<volatile int *>(bars + 10);     // [2]
+    volatile int *stage_mk = stage_qb + 2;                                    // [2]
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 12);
+    volatile int *last_flag = reinterpret_cast<volatile int *>(bars + 13);
     Ctx cx{reinterpret_cast<volatile int *>(tmem_slot + 1), p.err};
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -336,6 +343,7 @@ __global__ void __launch_bounds__(kThreads, 1) dkv_kernel(const __grid_constant_
                 if (t >= 2 && !cx.wait1(q_empty + st, ((t >> 1) - 1) & 1)) break;
                 uint8_t *sb = smem + L::STAGE0 + st * L::STAGE;
                 stage_qb[st] = qb;
+                stage_mk[st] = tile_mask_kind(qb, kb, p.docs != nullptr, p.block_info, p.QB);
                 mbar_expect_tx(q_full + st, L::Q_BYTES);
                 tma_load_3d(&maps.q, sb + L::SQ, q_full + st, 0, qb * BM, h);
 #pragma unroll
@@ -405,8 +413,6 @@ __global__ void __launch_bounds__(kThreads, 1) dkv_kernel(const __grid_constant_
         const uint32_t lb = (uint32_t)(quad * 32) << 16;
         const bool have_docs = p.docs != nullptr;
         const int doc_j = have_docs ? p.docs[j] : 0;
-        const int32_t *dmin = p.block_info ? p.block_info + 2 * p.QB : nullptr;
-        const int32_t *dmax = p.block_info ? p.block_info + 3 * p.QB : nullptr;
         bool alive = true;
         const int nu = 2 * nq;
         int mk = MASK_DOCS, qb = 0;
@@ -415,7 +421,7 @@ __global__ void __launch_bounds__(kThreads, 1) dkv_kernel(const __grid_constant_
             if (half == 0) {
                 if (!cx.waitw(q_full + st, (t >> 1) & 1)) { alive = false; break; }
                 qb = stage_qb[st];
-                mk = tile_mask_kind(qb, kb, have_docs, dmin, dmax);
+                mk = stage_mk[st];
             }
             if (!cx.waitw(sdp_full + half, t & 1)) { alive = false; break; }
             tc_fence_after();
@@ -602,8 +608,9 @@ __global__ void __launch_bounds__(kThreads, 1) dq_kernel(const __grid_constant__
     uint64_t *bars = reinterpret_cast<uint64_t *>(smem + L::BAR);
     uint64_t *res_full = bars + 0, *kv_full = bars + 1, *kv_empty = bars + 3, *sdp_full = bars + 5,
              *p_full = bars + 7, *acc_done = bars + 9;
-    volatile int *stage_kb = reinterpret_cast<volatile int *>(bars + 10);
-    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 11);
+    volatile int *stage_kb = reinterpret_cast<volatile int *>(bars + 10);     // [2]
+    volatile int *stage_mk = stage_kb + 2;                                    // [2]
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 12);
     float *slope_part = reinterpret_cast<float *>(smem + L::SLOPE);
     Ctx cx{reinterpret_cast<volatile int *>(tmem_slot + 1), p.err};
 
@@ -647,7 +654,9 @@ __global__ void __launch_bounds__(kThreads, 1) dq_kernel(const __grid_constant__
                 if (jj >= 2 && !cx.wait1(kv_empty + st, ((jj >> 1) - 1) & 1)) break;
                 int kb = list[jj];
                 stage_kb[st] = kb;
-                if (kb < 0 || kb >= p.QB) kb = 0;   // masked by the elementwise warps
+                const bool bad = kb < 0 || kb >= p.QB;
+                stage_mk[st] = bad ? MASK_DOCS : tile_mask_kind(qb, kb, p.docs != nullptr, p.block_info, p.QB);
+                if (bad) kb = 0;   // masked by the elementwise warps
                 uint8_t *sb = smem + L::STAGE0 + st * L::STAGE;
                 mbar_expect_tx(kv_full + st, L::KV_BYTES);
                 tma_load_3d(&maps.k, sb + L::SK, kv_full + st, 0, kb * BM, h);
@@ -720,8 +729,6 @@ __global__ void __launch_bounds__(kThreads, 1) dq_kernel(const __grid_constant__
         const uint32_t lb = (uint32_t)(quad * 32) << 16;
         const bool have_docs = p.docs != nullptr;
         const int doc_i = have_docs ? p.docs[i] : 0;
-        const int32_t *dmin = p.block_info ? p.block_info + 2 * p.QB : nullptr;
-        const int32_t *dmax = p.block_info ? p.block_info + 3 * p.QB : nullptr;
         const int64_t hrow = (int64_t)h * p.T + i;
         const float l2 = p.lse2[hrow], dl = p.delta[hrow];
         // The slope column of k_aug holds positions * s (up to ~T*s).  Its dS sum
@@ -743,7 +750,7 @@ __global__ void __launch_bounds__(kThreads, 1) dq_kernel(const __grid_constant__
                 if (!cx.waitw(kv_full + st, (jj >> 1) & 1)) { alive = false; break; }
                 kb = stage_kb[st];
                 bad = kb < 0 || kb >= p.QB;
-                mk = bad ? MASK_DOCS : tile_mask_kind(qb, kb, have_docs, dmin, dmax);
+                mk = stage_mk[st];
             }
             if (!cx.waitw(sdp_full + half, jj & 1)) { alive = false; break; }
             tc_fence_after();
