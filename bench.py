@@ -65,19 +65,10 @@ class ClockSampler:
         try:
             import pynvml
             pynvml.nvmlInit()
-            # the physical GPU behind this process's device `index`
-            bus = torch.cuda.get_device_properties(self.index).pci_bus_id if hasattr(
-                torch.cuda.get_device_properties(self.index), "pci_bus_id") else None
-            h = None
-            if bus:
-                try:
-                    h = pynvml.nvmlDeviceGetHandleByPciBusId(bus)
-                except Exception:
-                    h = None
-            if h is None:
-                vis = os.environ.get("CUDA_VISIBLE_DEVICES")
-                phys = int(vis.split(",")[self.index]) if vis and vis.split(",")[self.index].isdigit() else self.index
-                h = pynvml.nvmlDeviceGetHandleByIndex(phys)
+            # the physical GPU behind this process's device `index`, by PCI address
+            pr = torch.cuda.get_device_properties(self.index)
+            bus = "%08X:%02X:%02X.0" % (int(pr.pci_domain_id), int(pr.pci_bus_id), int(pr.pci_device_id))
+            h = pynvml.nvmlDeviceGetHandleByPciBusId(bus.encode())
             self.nvml, self.h = pynvml, h
             self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM)
             self.t = threading.Thread(target=self._poll, daemon=True)
