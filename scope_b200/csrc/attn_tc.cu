@@ -64,7 +64,8 @@ struct Layout {
     static constexpr uint32_t BAR = STAGE0 + 2 * STAGE;
     static constexpr uint32_t XCH = BAR + 256;                   // float[2 parity][2 halves][128 rows] + l[2][128]
     static constexpr uint32_t TOTAL = XCH + 3 * 1024;
-    static constexpr uint32_t KV_BYTES = 2 * TILE + NA * ATILE;  // expected TMA bytes per stage
+    static constexpr uint32_t K_BYTES = TILE + NA * ATILE;       // expected TMA bytes: K (+aug) of a stage
+    static constexpr uint32_t V_BYTES = TILE;                    // V of a stage
     static constexpr uint32_t Q_BYTES = TILE + NA * ATILE;
 };
 
@@ -102,12 +103,18 @@ __global__ void __launch_bounds__(kThreads, 2) fwd_kernel(const __grid_constant_
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
     uint64_t *bars = reinterpret_cast<uint64_t *>(smem + L::BAR);
-    uint64_t *q_full = bars + 0, *kv_full = bars + 1, *kv_empty = bars + 3;
+    // K (+aug) and V of a stage have their own barriers: K is released when
+    // the S MMA that read it completes, long before P V frees V, so the next
+    // K load gets a whole softmax period of lead time.
+    uint64_t *q_full = bars + 0, *kv_full = bars + 1, *kv_empty = bars + 3;   // K halves of the stages
+    uint64_t *v_full = bars + 20, *v_empty = bars + 22;
     uint64_t *s_full = bars + 5, *s_free = bars + 6, *p_full = bars + 7, *o_done = bars + 8;
     uint64_t *xchg = bars + 9;                                   // [4]: one per TMEM lane quadrant
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 13);
-    volatile int *stage_kb = reinterpret_cast<volatile int *>(bars + 14);   // [2] kv block of each stage
-    volatile int *stage_mk = stage_kb + 2;                                  // [2] its mask kind
+    // kv block and mask kind of tile j at [j & 3]: the producer may refill a
+    // stage's K (tile j+2) while the softmax has yet to read tile j's entry
+    volatile int *stage_kb = reinterpret_cast<volatile int *>(bars + 14);   // [4]
+    volatile int *stage_mk = stage_kb + 4;                                  // [4]
     volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
     float *xmax = reinterpret_cast<float *>(smem + L::XCH);      // [2][2][128]
     float *xsum = xmax + 512;                                    // [2][128]
@@ -124,6 +131,10 @@ __global__ void __launch_bounds__(kThreads, 2) fwd_kernel(const __grid_constant_
         mbar_init(kv_full + 1, 1);
         mbar_init(kv_empty + 0, 1);
         mbar_init(kv_empty + 1, 1);
+        for (int q = 0; q < 2; ++q) {
+            mbar_init(v_full + q, 1);
+            mbar_init(v_empty + q, 1);
+        }
         mbar_init(s_full, 1);
         mbar_init(s_free, kSoftmax);
         mbar_init(p_full, kSoftmax);
@@ -158,7 +169,7 @@ __global__ void __launch_bounds__(kThreads, 2) fwd_kernel(const __grid_constant_
             tma_load_3d(&maps.q, smem + L::Q, q_full, 0, qb * BM, h);
 #pragma unroll
             for (int a = 0; a < NA; ++a) tma_load_3d(&maps.qa, smem + L::QA + a * L::ATILE, q_full, 16 * a, qb * BM, h);
-            int issued = 0;
+            int issued = 0, kissued = 0;   // stages whose V / K loads were issued
             for (int j = 0; j < n; ++j) {
                 const int s = j & 1;
                 if (j >= 2 && (*abort_flag || !mbar_wait(kv_empty + s, ((j >> 1) - 1) & 1))) {
@@ -167,60 +178,71 @@ __global__ void __launch_bounds__(kThreads, 2) fwd_kernel(const __grid_constant_
                 }
                 int kb = list[j];
                 const bool bad = kb < 0 || kb >= p.QB;
-                stage_kb[s] = kb;
-                stage_mk[s] = bad ? 3 : tile_kind(qb, kb, p.docs != nullptr, p.block_info, p.QB);
+                stage_kb[j & 3] = kb;
+                stage_mk[j & 3] = bad ? 3 : tile_kind(qb, kb, p.docs != nullptr, p.block_info, p.QB);
                 if (bad) kb = 0;   // the softmax masks this tile and flags it
                 uint8_t *st = smem + L::STAGE0 + s * L::STAGE;
-                mbar_expect_tx(kv_full + s, L::KV_BYTES);
+                mbar_expect_tx(kv_full + s, L::K_BYTES);
                 tma_load_3d(&maps.k, st + L::K, kv_full + s, 0, kb * BM, h);
 #pragma unroll
                 for (int a = 0; a < NA; ++a) tma_load_2d(&maps.ka, st + L::KA + a * L::ATILE, kv_full + s, 16 * a, kb * BM);
-                tma_load_3d(&maps.v, st + L::V, kv_full + s, 0, kb * BM, h);
-                issued = j + 1;
+                if (j >= 2 && (*abort_flag || !mbar_wait(v_empty + s, ((j >> 1) - 1) & 1))) {
+                    give_up();
+                    issued = j;
+                    kissued = j + 1;
+                    break;
+                }
+                mbar_expect_tx(v_full + s, L::V_BYTES);
+                tma_load_3d(&maps.v, st + L::V, v_full + s, 0, kb * BM, h);
+                issued = kissued = j + 1;
             }
             // never leave the CTA with a TMA write still in flight
             mbar_wait(q_full, 0, 500000000ull);
-            for (int j = (issued > 2 ? issued - 2 : 0); j < issued; ++j)
+            for (int j = (kissued > 2 ? kissued - 2 : 0); j < kissued; ++j)
                 mbar_wait(kv_full + (j & 1), (j >> 1) & 1, 500000000ull);
+            for (int j = (issued > 2 ? issued - 2 : 0); j < issued; ++j)
+                mbar_wait(v_full + (j & 1), (j >> 1) & 1, 500000000ull);
         }
     } else if (warp == 1) {
         // ------------------------------------------------------------ tcgen05 issuer
-        if (lane == 0 && n > 0) {
+        if (n > 0) {   // the whole warp; one elected lane issues
             constexpr uint32_t idS = idesc_bf16(128, 128, false, false);
             constexpr uint32_t idO = idesc_bf16(128, 64, false, true);
             const uint32_t tS = tmem + S_COL, tO = tmem + O_COL, tP = tmem + P_COL;
             const uint32_t sq = smem_u32(smem + L::Q);
-            bool ok = mbar_wait(q_full, 0);
+            bool ok = warp_wait(q_full, 0);
             auto issue_S = [&](int j) -> bool {
                 const int s = j & 1;
-                if (*abort_flag || !mbar_wait(kv_full + s, (j >> 1) & 1)) return false;
+                if (!warp_wait(kv_full + s, (j >> 1) & 1)) return false;
                 tc_fence_after();
                 const uint32_t sk = smem_u32(smem + L::STAGE0 + s * L::STAGE);
 #pragma unroll
                 for (int kk = 0; kk < HD / 16; ++kk)
-                    mma_ss(tS, kmajor_desc(sq + L::Q + kk * 32, 128), kmajor_desc(sk + L::K + kk * 32, 128), idS,
+                    mma_ss_w(tS, kmajor_desc(sq + L::Q + kk * 32, 128), kmajor_desc(sk + L::K + kk * 32, 128), idS,
                            kk > 0);
 #pragma unroll
                 for (int a = 0; a < NA; ++a)
-                    mma_ss(tS, kmajor_desc(sq + L::QA + a * L::ATILE, 32), kmajor_desc(sk + L::KA + a * L::ATILE, 32),
+                    mma_ss_w(tS, kmajor_desc(sq + L::QA + a * L::ATILE, 32), kmajor_desc(sk + L::KA + a * L::ATILE, 32),
                            idS, 1);
-                tc_commit(s_full);
+                tc_commit_w(s_full);
+                tc_commit_w(kv_empty + s);   // K of this stage may be reloaded once S is done
                 return true;
             };
             ok = ok && issue_S(0);
             for (int j = 0; ok && j < n; ++j) {
                 if (j + 1 < n) {
-                    if (*abort_flag || !mbar_wait(s_free, j & 1)) { ok = false; break; }
+                    if (!warp_wait(s_free, j & 1)) { ok = false; break; }
                     if (!issue_S(j + 1)) { ok = false; break; }
                 }
-                if (*abort_flag || !mbar_wait(p_full, j & 1)) { ok = false; break; }
+                if (!warp_wait(p_full, j & 1)) { ok = false; break; }
+                if (!warp_wait(v_full + (j & 1), (j >> 1) & 1)) { ok = false; break; }
                 tc_fence_after();
                 const uint32_t sv = smem_u32(smem + L::STAGE0 + (j & 1) * L::STAGE + L::V);
 #pragma unroll
                 for (int kk = 0; kk < BM / 16; ++kk)
-                    mma_ts(tO, tP + kk * 8, mnmajor128_desc(sv + kk * 2048), idO, (j > 0 || kk > 0) ? 1u : 0u);
-                tc_commit(o_done);
-                tc_commit(kv_empty + (j & 1));
+                    mma_ts_w(tO, tP + kk * 8, mnmajor128_desc(sv + kk * 2048), idO, (j > 0 || kk > 0) ? 1u : 0u);
+                tc_commit_w(o_done);
+                tc_commit_w(v_empty + (j & 1));
             }
             if (!ok) give_up();
         }
@@ -243,8 +265,8 @@ __global__ void __launch_bounds__(kThreads, 2) fwd_kernel(const __grid_constant_
         for (int j = 0; j < n && alive; ++j) {
             // the producer classified this tile: 0 full, 1 causal only, 2 document ids, 3 bad index
             if (!warp_wait(kv_full + (j & 1), (j >> 1) & 1)) { give_up(); alive = false; break; }
-            const int kb = stage_kb[j & 1];
-            const int mk = stage_mk[j & 1];
+            const int kb = stage_kb[j & 3];
+            const int mk = stage_mk[j & 3];
             if (mk == 3 && r == 0 && ch == 0) set_err(p.err, SCOPE_DEVERR_INDEX);
             if (!warp_wait(s_full, j & 1)) { give_up(); alive = false; break; }
             tc_fence_after();

@@ -20,10 +20,11 @@
 // Both kernels share one pipeline.  A 128x128 tile is processed as two
 // halves of 64 columns.  TMEM (512 columns, one CTA per SM) holds two slots of
 // {S half, dP half} (fp32, 64 + 64 columns) and the accumulators.  While the
-// eight elementwise warps (two per TMEM lane quadrant, 32 columns each) turn slot u into P / dS (bf16, written back over the
-// first 32 columns of the slot's S and dP halves, where the next MMAs read them
-// as their A operand), the issuer runs the QK^T / dO V^T MMAs of slot u+1 and
-// the gradient MMAs of slot u-1.  Every wait is bounded (SCOPE_DEVERR_TIMEOUT).
+// eight elementwise warps (two per TMEM lane quadrant, 32 columns each) turn
+// slot u into P / dS (bf16, written back over the S and dP columns each warp
+// read, where the next MMAs read them as their A operand), the issuer runs the
+// QK^T / dO V^T MMAs of slot u+1 and the gradient MMAs of slot u-1.  Every
+// wait is bounded (SCOPE_DEVERR_TIMEOUT).
 #include <algorithm>
 #include <cmath>
 #include <cstring>
@@ -49,6 +50,12 @@ constexpr float kLog2e = 1.4426950408889634f;
 __host__ __device__ constexpr uint32_t align1k(uint32_t x) { return (x + 1023u) & ~1023u; }
 __device__ __forceinline__ uint32_t slot_s(int half) { return (uint32_t)half * 128u; }
 __device__ __forceinline__ uint32_t slot_dp(int half) { return (uint32_t)half * 128u + 64u; }
+// The bf16 P / dS of a half go back over the fp32 columns they came from: the
+// warp holding columns [32ch, 32ch+32) writes its 16 packed columns at 32ch,
+// inside what it has already read itself (a write at 16ch would land on
+// columns the other warp of the quadrant may not have loaded yet).  K step kk
+// (16 bf16 = 8 columns) of the A operand therefore starts at column a_col(kk).
+__device__ __forceinline__ uint32_t a_col(int kk) { return (uint32_t)(kk * 8 + (kk >= 2 ? 16 : 0)); }
 
 // ------------------------------------------------------------------ prep
 __global__ void prep_kernel(const __nv_bfloat16 *__restrict__ out, int64_t o_sh, int64_t o_st,
@@ -359,50 +366,50 @@ __global__ void __launch_bounds__(kThreads, 1) dkv_kernel(const __grid_constant_
             for (int j = (t > 2 ? t - 2 : 0); j < t; ++j) mbar_wait(q_full + (j & 1), (j >> 1) & 1, 500000000ull);
         }
     } else if (warp == 1) {
-        if (lane == 0 && nq > 0) {
+        if (nq > 0) {   // the whole warp; one elected lane issues
             constexpr uint32_t idS = idesc_bf16(128, 64, false, false);
             constexpr uint32_t idG = idesc_bf16(128, 64, false, true);
             const uint32_t sK = smem_u32(smem + L::K), sKA = smem_u32(smem + L::KA), sV = smem_u32(smem + L::V);
             auto grad = [&](int v) -> bool {
                 const int tv = v >> 1, hv = v & 1, stv = tv & 1;
-                if (!cx.wait1(p_full + hv, tv & 1)) return false;
+                if (!cx.waitw(p_full + hv, tv & 1)) return false;
                 tc_fence_after();
                 const uint32_t sb = smem_u32(smem + L::STAGE0 + stv * L::STAGE);
 #pragma unroll
                 for (int kk = 0; kk < 4; ++kk)
-                    mma_ts(tmem + ACC0, tmem + slot_s(hv) + kk * 8, mnmajor128_desc(sb + L::SDO + hv * 8192 + kk * 2048),
+                    mma_ts_w(tmem + ACC0, tmem + slot_s(hv) + a_col(kk), mnmajor128_desc(sb + L::SDO + hv * 8192 + kk * 2048),
                            idG, (v > 0 || kk > 0) ? 1u : 0u);
 #pragma unroll
                 for (int kk = 0; kk < 4; ++kk)
-                    mma_ts(tmem + ACC1, tmem + slot_dp(hv) + kk * 8, mnmajor128_desc(sb + L::SQ + hv * 8192 + kk * 2048),
+                    mma_ts_w(tmem + ACC1, tmem + slot_dp(hv) + a_col(kk), mnmajor128_desc(sb + L::SQ + hv * 8192 + kk * 2048),
                            idG, (v > 0 || kk > 0) ? 1u : 0u);
-                if (hv == 1) tc_commit(q_empty + stv);
+                if (hv == 1) tc_commit_w(q_empty + stv);
                 return true;
             };
-            bool ok = cx.wait1(kv_full, 0);
+            bool ok = cx.waitw(kv_full, 0);
             const int nu = 2 * nq;
             for (int u = 0; ok && u < nu; ++u) {
                 const int t = u >> 1, half = u & 1, st = t & 1;
-                if (half == 0 && !cx.wait1(q_full + st, (t >> 1) & 1)) { ok = false; break; }
+                if (half == 0 && !cx.waitw(q_full + st, (t >> 1) & 1)) { ok = false; break; }
                 tc_fence_after();
                 const uint32_t sb = smem_u32(smem + L::STAGE0 + st * L::STAGE);
 #pragma unroll
                 for (int kk = 0; kk < 4; ++kk)
-                    mma_ss(tmem + slot_s(half), kmajor_desc(sK + kk * 32, 128),
+                    mma_ss_w(tmem + slot_s(half), kmajor_desc(sK + kk * 32, 128),
                            kmajor_desc(sb + L::SQ + half * 8192 + kk * 32, 128), idS, kk > 0);
 #pragma unroll
                 for (int a = 0; a < NA; ++a)
-                    mma_ss(tmem + slot_s(half), kmajor_desc(sKA + a * L::ATILE, 32),
+                    mma_ss_w(tmem + slot_s(half), kmajor_desc(sKA + a * L::ATILE, 32),
                            kmajor_desc(sb + L::SQA + a * L::ATILE + half * 2048, 32), idS, 1);
 #pragma unroll
                 for (int kk = 0; kk < 4; ++kk)
-                    mma_ss(tmem + slot_dp(half), kmajor_desc(sV + kk * 32, 128),
+                    mma_ss_w(tmem + slot_dp(half), kmajor_desc(sV + kk * 32, 128),
                            kmajor_desc(sb + L::SDO + half * 8192 + kk * 32, 128), idS, kk > 0);
-                tc_commit(sdp_full + half);
+                tc_commit_w(sdp_full + half);
                 if (u >= 1 && !grad(u - 1)) { ok = false; break; }
             }
             if (ok) ok = grad(nu - 1);
-            if (ok) tc_commit(acc_done);
+            if (ok) tc_commit_w(acc_done);
         }
     } else {
         // ---------------- elementwise: thread = kv row c, 32 of the 64 columns of a half
@@ -436,8 +443,8 @@ __global__ void __launch_bounds__(kThreads, 1) dkv_kernel(const __grid_constant_
             const uint64_t c2 = f2_pack(p.scale_log2, p.scale_log2);
             if (mk == MASK_FULL) dkv_piece<false>(s, dp, LS, DL, c2, mk, lim, p.docs, i0, doc_j);
             else dkv_piece<true>(s, dp, LS, DL, c2, mk, lim, p.docs, i0, doc_j);
-            st_bf16x32(tmem + lb + slot_s(half) + ch * 16, s);
-            st_bf16x32(tmem + lb + slot_dp(half) + ch * 16, dp);
+            st_bf16x32(tmem + lb + slot_s(half) + ch * 32, s);
+            st_bf16x32(tmem + lb + slot_dp(half) + ch * 32, dp);
             tmem_wait_st();
             tc_fence_before();
             mbar_arrive(p_full + half);
@@ -671,54 +678,54 @@ __global__ void __launch_bounds__(kThreads, 1) dq_kernel(const __grid_constant__
                 mbar_wait(kv_full + (j & 1), (j >> 1) & 1, 500000000ull);
         }
     } else if (warp == 1) {
-        if (lane == 0 && n > 0) {
+        if (n > 0) {   // the whole warp; one elected lane issues
             constexpr uint32_t idS = idesc_bf16(128, 64, false, false);
             constexpr uint32_t idG = idesc_bf16(128, 64, false, true);
             constexpr uint32_t idA = idesc_bf16(128, 16, false, true);
             const uint32_t sQ = smem_u32(smem + L::Q), sQA = smem_u32(smem + L::QA), sDO = smem_u32(smem + L::DO);
             auto grad = [&](int v) -> bool {
                 const int jv = v >> 1, hv = v & 1, stv = jv & 1;
-                if (!cx.wait1(p_full + hv, jv & 1)) return false;
+                if (!cx.waitw(p_full + hv, jv & 1)) return false;
                 tc_fence_after();
                 const uint32_t sb = smem_u32(smem + L::STAGE0 + stv * L::STAGE);
 #pragma unroll
                 for (int kk = 0; kk < 4; ++kk)
-                    mma_ts(tmem + ACC0, tmem + slot_s(hv) + kk * 8, mnmajor128_desc(sb + L::SK + hv * 8192 + kk * 2048),
+                    mma_ts_w(tmem + ACC0, tmem + slot_s(hv) + a_col(kk), mnmajor128_desc(sb + L::SK + hv * 8192 + kk * 2048),
                            idG, (v > 0 || kk > 0) ? 1u : 0u);
 #pragma unroll
                 for (int a = 0; a < NA; ++a)
 #pragma unroll
                     for (int kk = 0; kk < 4; ++kk)
-                        mma_ts(tmem + ACC1 + a * 16, tmem + slot_s(hv) + kk * 8,
+                        mma_ts_w(tmem + ACC1 + a * 16, tmem + slot_s(hv) + a_col(kk),
                                mnmajor32_desc(sb + L::SKA + a * L::ATILE + hv * 2048 + kk * 512), idA,
                                (v > 0 || kk > 0) ? 1u : 0u);
-                if (hv == 1) tc_commit(kv_empty + stv);
+                if (hv == 1) tc_commit_w(kv_empty + stv);
                 return true;
             };
-            bool ok = cx.wait1(res_full, 0);
+            bool ok = cx.waitw(res_full, 0);
             const int nu = 2 * n;
             for (int u = 0; ok && u < nu; ++u) {
                 const int jj = u >> 1, half = u & 1, st = jj & 1;
-                if (half == 0 && !cx.wait1(kv_full + st, (jj >> 1) & 1)) { ok = false; break; }
+                if (half == 0 && !cx.waitw(kv_full + st, (jj >> 1) & 1)) { ok = false; break; }
                 tc_fence_after();
                 const uint32_t sb = smem_u32(smem + L::STAGE0 + st * L::STAGE);
 #pragma unroll
                 for (int kk = 0; kk < 4; ++kk)
-                    mma_ss(tmem + slot_s(half), kmajor_desc(sQ + kk * 32, 128),
+                    mma_ss_w(tmem + slot_s(half), kmajor_desc(sQ + kk * 32, 128),
                            kmajor_desc(sb + L::SK + half * 8192 + kk * 32, 128), idS, kk > 0);
 #pragma unroll
                 for (int a = 0; a < NA; ++a)
-                    mma_ss(tmem + slot_s(half), kmajor_desc(sQA + a * L::ATILE, 32),
+                    mma_ss_w(tmem + slot_s(half), kmajor_desc(sQA + a * L::ATILE, 32),
                            kmajor_desc(sb + L::SKA + a * L::ATILE + half * 2048, 32), idS, 1);
 #pragma unroll
                 for (int kk = 0; kk < 4; ++kk)
-                    mma_ss(tmem + slot_dp(half), kmajor_desc(sDO + kk * 32, 128),
+                    mma_ss_w(tmem + slot_dp(half), kmajor_desc(sDO + kk * 32, 128),
                            kmajor_desc(sb + L::SV + half * 8192 + kk * 32, 128), idS, kk > 0);
-                tc_commit(sdp_full + half);
+                tc_commit_w(sdp_full + half);
                 if (u >= 1 && !grad(u - 1)) { ok = false; break; }
             }
             if (ok) ok = grad(nu - 1);
-            if (ok) tc_commit(acc_done);
+            if (ok) tc_commit_w(acc_done);
         }
     } else {
         // ---------------- elementwise: thread = q row i, 32 of the 64 columns of a half
@@ -768,7 +775,7 @@ __global__ void __launch_bounds__(kThreads, 1) dq_kernel(const __grid_constant__
                     gsl = fmaf(s[e], kpos - kpos_i, gsl);
                 }
             }
-            st_bf16x32(tmem + lb + slot_s(half) + ch * 16, s);
+            st_bf16x32(tmem + lb + slot_s(half) + ch * 32, s);
             tmem_wait_st();
             tc_fence_before();
             mbar_arrive(p_full + half);

@@ -6,7 +6,7 @@
 #include <cuda_bf16.h>
 #include <stdint.h>
 
-#include "../../include/scope_b200.h"
+#include "scope_b200.h"
 
 void scope_note_launch();
 
