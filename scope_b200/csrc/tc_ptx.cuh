@@ -33,16 +33,17 @@ __device__ __forceinline__ void mbar_expect_tx(uint64_t *bar, uint32_t bytes) {
                  "r"(bytes)
                  : "memory");
 }
-// try_wait with a suspend-time hint: the thread sleeps until the phase
-// completes or the hint (ns) elapses instead of spinning on issue slots.
+// try_wait without a suspend-time hint: the thread blocks for a
+// system-dependent time and wakes when the phase completes.  (A hint made the
+// measured arrive -> wake round trip between two warps ~35% longer on B200.)
 __device__ __forceinline__ bool mbar_try_wait(uint32_t addr, uint32_t parity) {
     uint32_t ok;
     asm volatile(
         "{\n\t.reg .pred p;\n\t"
-        "mbarrier.try_wait.parity.acquire.cta.shared::cta.b64 p, [%1], %2, %3;\n\t"
+        "mbarrier.try_wait.parity.acquire.cta.shared::cta.b64 p, [%1], %2;\n\t"
         "selp.u32 %0, 1, 0, p;\n\t}\n"
         : "=r"(ok)
-        : "r"(addr), "r"(parity), "r"(1000000u)
+        : "r"(addr), "r"(parity)
         : "memory");
     return ok != 0;
 }
@@ -125,10 +126,9 @@ __device__ __forceinline__ void mma_ts(uint32_t d, uint32_t a, uint64_t b, uint3
         : "memory");
 }
 // Warp-wide forms: the whole (converged) warp calls them with warp-uniform
-// operands and one elected lane issues the instruction.  Keeping the issuing
-// code warp-uniform lets the compiler hold descriptors in uniform registers;
-// issuing from a lone lane of a divergent branch moves every operand across
-// per instruction.
+// operands and one elected lane issues the instruction, so the issuing warp's
+// waits and loop control stay warp-uniform (the same lane is elected every
+// time, so a commit covers the MMAs issued before it).
 __device__ __forceinline__ void tc_commit_w(uint64_t *bar) {
     asm volatile(
         "{\n\t.reg .pred e;\n\telect.sync _|e, 0xffffffff;\n\t"
@@ -202,6 +202,10 @@ __device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&r)[16
         "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(taddr),
         SCOPE_W8(0), SCOPE_W8(8)
         : "memory");
+}
+__device__ __forceinline__ void tmem_st8(uint32_t taddr, const uint32_t (&r)[8]) {
+    asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"r"(taddr), SCOPE_W8(0)
+                 : "memory");
 }
 #undef SCOPE_R8
 #undef SCOPE_W8
