@@ -39,25 +39,26 @@ using namespace tc;
 
 constexpr int BM = 128;
 constexpr int HD = 64;
-constexpr int kThreads = 320;          // producer, issuer, 8 elementwise warps
+constexpr int kThreads = 352;          // producer, S/dP issuer, 8 elementwise warps, gradient issuer
+constexpr int kGradWarp = 10;
 constexpr int kElem = 256;             // elementwise threads
 constexpr int kChunk = 64;             // max q tiles per dK/dV work item
 constexpr int kSlotCap = 128;          // max kv rows whose q list is split
 constexpr uint32_t kTmemCols = 512;
 // TMEM columns (one CTA per SM owns all 512):
-//   [0, 256)    two slots of {S half, dP half}, 64 + 64 fp32 columns
-//   [256, 320)  ACC0: dV (dkv) | dQ (dq)
-//   [320, 384)  ACC1: dK (dkv) | gradient of the qk_aug dims (dq)
-//   [384, 416)  R0: resident A operand of S, bf16 pairs: K (dkv) | Q (dq)
-//   [416, 448)  R1: resident A operand of dP: V (dkv) | dO (dq)
-//   [448, 480)  RA: resident qk_aug dims: k_aug (dkv) | q_aug (dq)
-constexpr uint32_t ACC0 = 256, ACC1 = 320, R0 = 384, R1 = 416, RA = 448;
+//   [0, 384)    kSlots = 3 slots of {S half, dP half}, 64 + 64 fp32 columns
+//   [384, 448)  ACC0: dV (dkv) | dQ (dq)
+//   [448, 512)  ACC1: dK (dkv) | gradient of the qk_aug dims (dq)
+// Three slots let the S / dP MMAs of half-tile u+2 run while the elementwise
+// warps work on u and the gradient MMAs of u-1 wait for them.
+constexpr int kSlots = 3;
+constexpr uint32_t ACC0 = 384, ACC1 = 448;
 constexpr uint32_t kSmemBudget = 227 * 1024;   // dynamic shared memory per CTA
 constexpr float kLog2e = 1.4426950408889634f;
 
 __host__ __device__ constexpr uint32_t align1k(uint32_t x) { return (x + 1023u) & ~1023u; }
-__device__ __forceinline__ uint32_t slot_s(int half) { return (uint32_t)half * 128u; }
-__device__ __forceinline__ uint32_t slot_dp(int half) { return (uint32_t)half * 128u + 64u; }
+__device__ __forceinline__ uint32_t slot_s(int k) { return (uint32_t)k * 128u; }
+__device__ __forceinline__ uint32_t slot_dp(int k) { return (uint32_t)k * 128u + 64u; }
 // The bf16 P / dS of a half go back over the fp32 columns they came from: the
 // warp holding columns [32ch, 32ch+32) writes its 16 packed columns at 32ch,
 // inside what it has already read itself (a write at 16ch would land on
@@ -117,10 +118,6 @@ struct Params {
     float s_aug;
     float *dcoeff_cos, *dcoeff_sin, *dslope;
     Plan plan;
-    // rows of the operands the elementwise warps put in TMEM: r0 / r1 [H, T, 64]
-    // (dkv: K, V   dq: Q, dO) and ra (dkv: k_aug [T, DA]   dq: q_aug [H, T, DA])
-    const __nv_bfloat16 *r0, *r1, *ra;
-    int64_t r0_sh, r0_st, r1_sh, r1_st, ra_sh;
     int32_t *err;
 };
 
@@ -154,61 +151,36 @@ __device__ __forceinline__ void elem_bar() { asm volatile("bar.sync 1, 256;" :::
 
 // mbarriers and small shared state of a backward CTA
 struct Bars {
-    uint64_t res_full;                 // resident operands are in TMEM (elementwise arrivals)
+    uint64_t res_full;                 // the CTA's resident tiles are in shared memory
     uint64_t acc_done;                 // every MMA of the CTA completed
     uint64_t full[4], empty[4];        // streamed stage ring
-    uint64_t sdp_full[2];              // S / dP of a half are in TMEM
-    uint64_t p_full[2];                // P / dS of a half are back in TMEM (elementwise arrivals)
+    uint64_t sdp_full[kSlots];         // S / dP of a half are in a TMEM slot
+    uint64_t p_full[kSlots];           // P / dS of that half are back in the slot (elementwise arrivals)
+    uint64_t slot_free[kSlots];        // the gradient MMAs that read the slot completed
+    uint64_t drain[2];                 // each issuing warp's MMAs completed (before TMEM is freed)
     volatile int stage_blk[4];         // block index of the tile in each stage
     volatile int stage_mk[4];          // its mask kind
     uint32_t tmem_slot;
     volatile int abort_flag, last_flag, pad;
     __device__ void init(int nst) {
-        mbar_init(&res_full, kElem);
+        mbar_init(&res_full, 1);
         mbar_init(&acc_done, 1);
         for (int i = 0; i < nst; ++i) {
             mbar_init(&full[i], 1);
             mbar_init(&empty[i], 1);
         }
-        for (int i = 0; i < 2; ++i) {
+        for (int i = 0; i < kSlots; ++i) {
             mbar_init(&sdp_full[i], 1);
             mbar_init(&p_full[i], kElem);
+            mbar_init(&slot_free[i], 1);
         }
+        mbar_init(&drain[0], 1);
+        mbar_init(&drain[1], 1);
         abort_flag = 0;
         last_flag = 0;
         fence_mbar_init();
     }
 };
-
-// The CTA's resident operands go to TMEM as A operands (bf16 pairs, lane =
-// row): this thread writes row `row` of r0 / r1 (dims [32ch, 32ch+32) ->
-// columns [16ch, 16ch+16)) and the 16-dim chunks a of ra with a % 2 == ch.
-template <int DA>
-__device__ __forceinline__ void load_resident(const Params &p, int h, int row, uint32_t tl, int ch) {
-    auto row32 = [](const __nv_bfloat16 *src, uint32_t taddr) {
-        const uint4 *s4 = reinterpret_cast<const uint4 *>(src);
-        uint32_t w[16];
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-            const uint4 v = __ldg(s4 + e);
-            w[4 * e] = v.x;
-            w[4 * e + 1] = v.y;
-            w[4 * e + 2] = v.z;
-            w[4 * e + 3] = v.w;
-        }
-        tmem_st16(taddr, w);
-    };
-    row32(p.r0 + h * p.r0_sh + (int64_t)row * p.r0_st + ch * 32, tl + R0 + ch * 16);
-    row32(p.r1 + h * p.r1_sh + (int64_t)row * p.r1_st + ch * 32, tl + R1 + ch * 16);
-#pragma unroll
-    for (int a = 0; a < DA / 16; ++a) {
-        if ((a & 1) != ch) continue;
-        const uint4 *s4 = reinterpret_cast<const uint4 *>(p.ra + h * p.ra_sh + (int64_t)row * DA + a * 16);
-        const uint4 v0 = __ldg(s4), v1 = __ldg(s4 + 1);
-        const uint32_t w[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
-        tmem_st8(tl + RA + a * 8, w);
-    }
-}
 
 // S and dP columns [c0, c0+32) of a slot for this thread's TMEM lane, one wait
 __device__ __forceinline__ void ld_s_dp(uint32_t ts, uint32_t tdp, float (&s)[32], float (&dp)[32]) {
@@ -325,16 +297,20 @@ __device__ __forceinline__ void dq_piece(float (&s)[32], const float (&dp)[32], 
 }
 
 // ============================================================================ dK / dV
-// Streamed per q tile (ring of NST stages): Q, the q_aug dims, dO, lse2, delta.
+// Resident: K, the k_aug dims, V.  Streamed per q tile (ring of NST stages):
+// Q, the q_aug dims, dO, lse2, delta.
 template <int DA>
 struct KVL {
     static constexpr int NA = DA / 16;
     static constexpr uint32_t TILE = BM * HD * 2, ATILE = BM * 16 * 2;
+    static constexpr uint32_t K = 0, KA = TILE, V = align1k(TILE + NA * ATILE);
+    static constexpr uint32_t STAGE0 = V + TILE;
     static constexpr uint32_t SQ = 0, SQA = TILE, SDO = align1k(TILE + NA * ATILE), SLSE = SDO + TILE,
                               SDEL = SLSE + 512;
     static constexpr uint32_t STAGE = align1k(SDEL + 512);
-    static constexpr int NST = 4 * STAGE + 2048 <= kSmemBudget ? 4 : 3;
-    static constexpr uint32_t BAR = NST * STAGE;
+    static constexpr int NST = STAGE0 + 4 * STAGE + 2048 <= kSmemBudget ? 4 : 3;
+    static constexpr uint32_t BAR = STAGE0 + NST * STAGE;
+    static constexpr uint32_t RES_BYTES = 2 * TILE + NA * ATILE;
     static constexpr uint32_t TOTAL = BAR + sizeof(Bars);
     static constexpr uint32_t Q_BYTES = 2 * TILE + NA * ATILE + 1024;
 };
@@ -380,8 +356,13 @@ __global__ void __launch_bounds__(kThreads, 1) dkv_kernel(const __grid_constant_
     const uint32_t tmem = B.tmem_slot;
 
     if (warp == 0) {
-        // ---------------- producer: the q tiles that see this kv block, ascending
+        // ---------------- producer: K / V once, then the q tiles that see this kv block, ascending
         if (lane == 0 && nq > 0) {
+            mbar_expect_tx(&B.res_full, L::RES_BYTES);
+            tma_load_3d(&maps.k, smem + L::K, &B.res_full, 0, kb * BM, h);
+#pragma unroll
+            for (int a = 0; a < NA; ++a) tma_load_2d(&maps.ka, smem + L::KA + a * L::ATILE, &B.res_full, 16 * a, kb * BM);
+            tma_load_3d(&maps.v, smem + L::V, &B.res_full, 0, kb * BM, h);
             int w;
             uint32_t bits;
             seek_rank(brow, p.words, first, w, bits);
@@ -395,7 +376,7 @@ __global__ void __launch_bounds__(kThreads, 1) dkv_kernel(const __grid_constant_
                 bits &= bits - 1;
                 const int st = t % NST;
                 if (t >= NST && !cx.wait1(&B.empty[st], ((t / NST) - 1) & 1)) break;
-                uint8_t *sb = smem + st * L::STAGE;
+                uint8_t *sb = smem + L::STAGE0 + st * L::STAGE;
                 B.stage_blk[st] = qb;
                 B.stage_mk[st] = tile_mask_kind(qb, kb, p.docs != nullptr, p.block_info, p.QB);
                 mbar_expect_tx(&B.full[st], L::Q_BYTES);
@@ -410,56 +391,72 @@ __global__ void __launch_bounds__(kThreads, 1) dkv_kernel(const __grid_constant_
                 ++t;
             }
             // never leave the CTA with a TMA write still in flight
+            mbar_wait(&B.res_full, 0, 500000000ull);
             for (int j = (t > NST ? t - NST : 0); j < t; ++j) mbar_wait(&B.full[j % NST], (j / NST) & 1, 500000000ull);
         }
     } else if (warp == 1) {
-        // ---------------- tcgen05 issuer (whole warp, one elected lane issues)
+        // ---------------- S / dP issuer (whole warp, one elected lane issues)
         if (nq > 0) {
             constexpr uint32_t idS = idesc_bf16(128, 64, false, false);
-            constexpr uint32_t idG = idesc_bf16(128, 64, false, true);
-            auto grad = [&](int v) -> bool {
-                const int tv = v >> 1, hv = v & 1, stv = tv % NST;
-                if (!cx.waitw(&B.p_full[hv], tv & 1)) return false;
-                tc_fence_after();
-                const uint32_t sb = smem_u32(smem + stv * L::STAGE);
-#pragma unroll
-                for (int kk = 0; kk < 4; ++kk)
-                    mma_ts_w(tmem + ACC0, tmem + slot_s(hv) + a_col(kk),
-                             mnmajor128_desc(sb + L::SDO + hv * 8192 + kk * 2048), idG, (v > 0 || kk > 0) ? 1u : 0u);
-#pragma unroll
-                for (int kk = 0; kk < 4; ++kk)
-                    mma_ts_w(tmem + ACC1, tmem + slot_dp(hv) + a_col(kk),
-                             mnmajor128_desc(sb + L::SQ + hv * 8192 + kk * 2048), idG, (v > 0 || kk > 0) ? 1u : 0u);
-                if (hv == 1) tc_commit_w(&B.empty[stv]);
-                return true;
-            };
-            // K, V and the k_aug rows are written to TMEM by the elementwise warps
+            const uint32_t sK = smem_u32(smem + L::K), sKA = smem_u32(smem + L::KA), sV = smem_u32(smem + L::V);
             bool ok = cx.waitw(&B.res_full, 0);
-            tc_fence_after();
             const int nu = 2 * nq;
+            // half-tile u: S / dP into slot u % 3 once the gradient MMAs of u - 3 released it
             for (int u = 0; ok && u < nu; ++u) {
-                const int t = u >> 1, half = u & 1, st = t % NST;
+                const int t = u >> 1, half = u & 1, st = t % NST, k = u % kSlots;
                 if (half == 0 && !cx.waitw(&B.full[st], (t / NST) & 1)) { ok = false; break; }
+                if (u >= kSlots && !cx.waitw(&B.slot_free[k], ((u / kSlots) - 1) & 1)) { ok = false; break; }
                 tc_fence_after();
-                const uint32_t sb = smem_u32(smem + st * L::STAGE);
+                const uint32_t sb = smem_u32(smem + L::STAGE0 + st * L::STAGE);
                 // S^T = K Q^T (+ Kaug Qaug^T), dP^T = V dO^T: 128 kv rows x 64 q columns of this half
 #pragma unroll
                 for (int kk = 0; kk < 4; ++kk)
-                    mma_ts_w(tmem + slot_s(half), tmem + R0 + kk * 8,
+                    mma_ss_w(tmem + slot_s(k), kmajor_desc(sK + kk * 32, 128),
                              kmajor_desc(sb + L::SQ + half * 8192 + kk * 32, 128), idS, kk > 0);
 #pragma unroll
                 for (int a = 0; a < NA; ++a)
-                    mma_ts_w(tmem + slot_s(half), tmem + RA + a * 8,
+                    mma_ss_w(tmem + slot_s(k), kmajor_desc(sKA + a * L::ATILE, 32),
                              kmajor_desc(sb + L::SQA + a * L::ATILE + half * 2048, 32), idS, 1);
 #pragma unroll
                 for (int kk = 0; kk < 4; ++kk)
-                    mma_ts_w(tmem + slot_dp(half), tmem + R1 + kk * 8,
+                    mma_ss_w(tmem + slot_dp(k), kmajor_desc(sV + kk * 32, 128),
                              kmajor_desc(sb + L::SDO + half * 8192 + kk * 32, 128), idS, kk > 0);
-                tc_commit_w(&B.sdp_full[half]);
-                if (u >= 1 && !grad(u - 1)) { ok = false; break; }
+                tc_commit_w(&B.sdp_full[k]);
             }
-            if (ok) ok = grad(nu - 1);
+            if (!ok) cx.give_up();
+            tc_commit_w(&B.drain[0]);   // TMEM is freed only after this warp's MMAs completed
+            mbar_wait(&B.drain[0], 0, 500000000ull);
+        }
+    } else if (warp == kGradWarp) {
+        // ---------------- gradient issuer (whole warp): a second issuing warp, so
+        // the S / dP MMAs and these queue on the tensor pipe side by side and
+        // neither warp's waits leave it idle
+        if (nq > 0) {
+            constexpr uint32_t idG = idesc_bf16(128, 64, false, true);
+            auto grad = [&](int v) -> bool {
+                const int tv = v >> 1, hv = v & 1, stv = tv % NST, kv = v % kSlots;
+                if (!cx.waitw(&B.p_full[kv], (v / kSlots) & 1)) return false;
+                tc_fence_after();
+                const uint32_t sb = smem_u32(smem + L::STAGE0 + stv * L::STAGE);
+#pragma unroll
+                for (int kk = 0; kk < 4; ++kk)
+                    mma_ts_w(tmem + ACC0, tmem + slot_s(kv) + a_col(kk),
+                             mnmajor128_desc(sb + L::SDO + hv * 8192 + kk * 2048), idG, (v > 0 || kk > 0) ? 1u : 0u);
+#pragma unroll
+                for (int kk = 0; kk < 4; ++kk)
+                    mma_ts_w(tmem + ACC1, tmem + slot_dp(kv) + a_col(kk),
+                             mnmajor128_desc(sb + L::SQ + hv * 8192 + kk * 2048), idG, (v > 0 || kk > 0) ? 1u : 0u);
+                tc_commit_w(&B.slot_free[kv]);
+                if (hv == 1) tc_commit_w(&B.empty[stv]);
+                return true;
+            };
+            const int nu = 2 * nq;
+            bool ok = true;
+            for (int v = 0; ok && v < nu; ++v) ok = grad(v);
             if (ok) tc_commit_w(&B.acc_done);
+            else cx.give_up();
+            tc_commit_w(&B.drain[1]);
+            mbar_wait(&B.drain[1], 0, 500000000ull);
         }
     } else {
         // ---------------- elementwise: thread = kv row c, 32 of the 64 columns of a half
@@ -472,25 +469,19 @@ __global__ void __launch_bounds__(kThreads, 1) dkv_kernel(const __grid_constant_
         const int doc_j = have_docs ? p.docs[j] : 0;
         bool alive = true;
         const int nu = 2 * nq;
-        if (nq > 0) {
-            load_resident<DA>(p, h, j, tmem + lb, ch);
-            tmem_wait_st();
-            tc_fence_before();
-            mbar_arrive(&B.res_full);
-        }
         int mk = MASK_DOCS, qb = 0;
         for (int u = 0; u < nu && alive; ++u) {
-            const int t = u >> 1, half = u & 1, st = t % NST;
+            const int t = u >> 1, half = u & 1, st = t % NST, k = u % kSlots;
             if (half == 0) {
                 if (!cx.waitw(&B.full[st], (t / NST) & 1)) { alive = false; break; }
                 qb = B.stage_blk[st];
                 mk = B.stage_mk[st];
             }
-            if (!cx.waitw(&B.sdp_full[half], t & 1)) { alive = false; break; }
+            if (!cx.waitw(&B.sdp_full[k], (u / kSlots) & 1)) { alive = false; break; }
             tc_fence_after();
             float s[32], dp[32];
-            ld_s_dp(tmem + lb + slot_s(half) + ch * 32, tmem + lb + slot_dp(half) + ch * 32, s, dp);
-            const uint8_t *sb = smem + st * L::STAGE;
+            ld_s_dp(tmem + lb + slot_s(k) + ch * 32, tmem + lb + slot_dp(k) + ch * 32, s, dp);
+            const uint8_t *sb = smem + L::STAGE0 + st * L::STAGE;
             const int col0 = half * 64 + ch * 32;       // q row within the tile of the first column
             const float4 *LS = reinterpret_cast<const float4 *>(sb + L::SLSE) + col0 / 4;
             const float4 *DL = reinterpret_cast<const float4 *>(sb + L::SDEL) + col0 / 4;
@@ -499,11 +490,11 @@ __global__ void __launch_bounds__(kThreads, 1) dkv_kernel(const __grid_constant_
             const uint64_t c2 = f2_pack(p.scale_log2, p.scale_log2);
             if (mk == MASK_FULL) dkv_piece<false>(s, dp, LS, DL, c2, mk, lim, p.docs, i0, doc_j);
             else dkv_piece<true>(s, dp, LS, DL, c2, mk, lim, p.docs, i0, doc_j);
-            st_bf16x32(tmem + lb + slot_s(half) + ch * 32, s);
-            st_bf16x32(tmem + lb + slot_dp(half) + ch * 32, dp);
+            st_bf16x32(tmem + lb + slot_s(k) + ch * 32, s);
+            st_bf16x32(tmem + lb + slot_dp(k) + ch * 32, dp);
             tmem_wait_st();
             tc_fence_before();
-            mbar_arrive(&B.p_full[half]);
+            mbar_arrive(&B.p_full[k]);
         }
         bool have = false;
         if (alive && nq > 0) {
@@ -647,15 +638,19 @@ __global__ void __launch_bounds__(1024) plan_items_kernel(const int32_t *__restr
 }
 
 // ============================================================================ dQ
-// Streamed per kv tile (ring of NST stages): K, the k_aug dims, V.
+// Resident: Q, the q_aug dims, dO.  Streamed per kv tile (ring of NST
+// stages): K, the k_aug dims, V.
 template <int DA>
 struct QL {
     static constexpr int NA = DA / 16;
     static constexpr uint32_t TILE = BM * HD * 2, ATILE = BM * 16 * 2;
+    static constexpr uint32_t Q = 0, QA = TILE, DO = align1k(TILE + NA * ATILE);
+    static constexpr uint32_t STAGE0 = DO + TILE;
     static constexpr uint32_t SK = 0, SKA = TILE, SV = align1k(TILE + NA * ATILE);
     static constexpr uint32_t STAGE = SV + TILE;
-    static constexpr int NST = 4 * STAGE + 2048 <= kSmemBudget ? 4 : 3;
-    static constexpr uint32_t BAR = NST * STAGE;
+    static constexpr int NST = STAGE0 + 4 * STAGE + 2048 <= kSmemBudget ? 4 : 3;
+    static constexpr uint32_t BAR = STAGE0 + NST * STAGE;
+    static constexpr uint32_t RES_BYTES = 2 * TILE + NA * ATILE;
     static constexpr uint32_t SLOPE = align1k(BAR + sizeof(Bars));   // float[128]: slope partials of column half 1
     static constexpr uint32_t TOTAL = SLOPE + 512;
     static constexpr uint32_t KV_BYTES = 2 * TILE + NA * ATILE;
@@ -688,8 +683,14 @@ __global__ void __launch_bounds__(kThreads, 1) dq_kernel(const __grid_constant__
     const uint32_t tmem = B.tmem_slot;
 
     if (warp == 0) {
-        // ---------------- producer: the kv tiles of this q block's list, in order
+        // ---------------- producer: Q / dO once, then the kv tiles of this q block's list, in order
         if (lane == 0 && n > 0) {
+            mbar_expect_tx(&B.res_full, L::RES_BYTES);
+            tma_load_3d(&maps.q, smem + L::Q, &B.res_full, 0, qb * BM, h);
+#pragma unroll
+            for (int a = 0; a < NA; ++a)
+                tma_load_3d(&maps.qa, smem + L::QA + a * L::ATILE, &B.res_full, 16 * a, qb * BM, h);
+            tma_load_3d(&maps.dout, smem + L::DO, &B.res_full, 0, qb * BM, h);
             int issued = 0;
             for (int jj = 0; jj < n; ++jj) {
                 const int st = jj % NST;
@@ -699,7 +700,7 @@ __global__ void __launch_bounds__(kThreads, 1) dq_kernel(const __grid_constant__
                 const bool bad = kb < 0 || kb >= p.QB;
                 B.stage_mk[st] = bad ? MASK_DOCS : tile_mask_kind(qb, kb, p.docs != nullptr, p.block_info, p.QB);
                 if (bad) kb = 0;   // masked by the elementwise warps
-                uint8_t *sb = smem + st * L::STAGE;
+                uint8_t *sb = smem + L::STAGE0 + st * L::STAGE;
                 mbar_expect_tx(&B.full[st], L::KV_BYTES);
                 tma_load_3d(&maps.k, sb + L::SK, &B.full[st], 0, kb * BM, h);
 #pragma unroll
@@ -708,61 +709,77 @@ __global__ void __launch_bounds__(kThreads, 1) dq_kernel(const __grid_constant__
                 tma_load_3d(&maps.v, sb + L::SV, &B.full[st], 0, kb * BM, h);
                 issued = jj + 1;
             }
+            mbar_wait(&B.res_full, 0, 500000000ull);
             for (int j = (issued > NST ? issued - NST : 0); j < issued; ++j)
                 mbar_wait(&B.full[j % NST], (j / NST) & 1, 500000000ull);
         }
     } else if (warp == 1) {
-        // ---------------- tcgen05 issuer (whole warp, one elected lane issues)
+        // ---------------- S / dP issuer (whole warp, one elected lane issues)
         if (n > 0) {
             constexpr uint32_t idS = idesc_bf16(128, 64, false, false);
+            const uint32_t sQ = smem_u32(smem + L::Q), sQA = smem_u32(smem + L::QA), sDO = smem_u32(smem + L::DO);
+            bool ok = cx.waitw(&B.res_full, 0);
+            const int nu = 2 * n;
+            // half-tile u: S / dP into slot u % 3 once the gradient MMAs of u - 3 released it
+            for (int u = 0; ok && u < nu; ++u) {
+                const int jj = u >> 1, half = u & 1, st = jj % NST, k = u % kSlots;
+                if (half == 0 && !cx.waitw(&B.full[st], (jj / NST) & 1)) { ok = false; break; }
+                if (u >= kSlots && !cx.waitw(&B.slot_free[k], ((u / kSlots) - 1) & 1)) { ok = false; break; }
+                tc_fence_after();
+                const uint32_t sb = smem_u32(smem + L::STAGE0 + st * L::STAGE);
+                // S = Q K^T (+ Qaug Kaug^T), dP = dO V^T: 128 q rows x 64 kv columns of this half
+#pragma unroll
+                for (int kk = 0; kk < 4; ++kk)
+                    mma_ss_w(tmem + slot_s(k), kmajor_desc(sQ + kk * 32, 128),
+                             kmajor_desc(sb + L::SK + half * 8192 + kk * 32, 128), idS, kk > 0);
+#pragma unroll
+                for (int a = 0; a < NA; ++a)
+                    mma_ss_w(tmem + slot_s(k), kmajor_desc(sQA + a * L::ATILE, 32),
+                             kmajor_desc(sb + L::SKA + a * L::ATILE + half * 2048, 32), idS, 1);
+#pragma unroll
+                for (int kk = 0; kk < 4; ++kk)
+                    mma_ss_w(tmem + slot_dp(k), kmajor_desc(sDO + kk * 32, 128),
+                             kmajor_desc(sb + L::SV + half * 8192 + kk * 32, 128), idS, kk > 0);
+                tc_commit_w(&B.sdp_full[k]);
+            }
+            if (!ok) cx.give_up();
+            tc_commit_w(&B.drain[0]);   // TMEM is freed only after this warp's MMAs completed
+            mbar_wait(&B.drain[0], 0, 500000000ull);
+        }
+    } else if (warp == kGradWarp) {
+        // ---------------- gradient issuer (whole warp): a second issuing warp, so
+        // the S / dP MMAs and these queue on the tensor pipe side by side and
+        // neither warp's waits leave it idle
+        if (n > 0) {
             constexpr uint32_t idG = idesc_bf16(128, 64, false, true);
             constexpr uint32_t idA = idesc_bf16(128, 16, false, true);
             auto grad = [&](int v) -> bool {
-                const int jv = v >> 1, hv = v & 1, stv = jv % NST;
-                if (!cx.waitw(&B.p_full[hv], jv & 1)) return false;
+                const int jv = v >> 1, hv = v & 1, stv = jv % NST, kv = v % kSlots;
+                if (!cx.waitw(&B.p_full[kv], (v / kSlots) & 1)) return false;
                 tc_fence_after();
-                const uint32_t sb = smem_u32(smem + stv * L::STAGE);
+                const uint32_t sb = smem_u32(smem + L::STAGE0 + stv * L::STAGE);
 #pragma unroll
                 for (int kk = 0; kk < 4; ++kk)
-                    mma_ts_w(tmem + ACC0, tmem + slot_s(hv) + a_col(kk),
+                    mma_ts_w(tmem + ACC0, tmem + slot_s(kv) + a_col(kk),
                              mnmajor128_desc(sb + L::SK + hv * 8192 + kk * 2048), idG, (v > 0 || kk > 0) ? 1u : 0u);
 #pragma unroll
                 for (int a = 0; a < NA; ++a)
 #pragma unroll
                     for (int kk = 0; kk < 4; ++kk)
-                        mma_ts_w(tmem + ACC1 + a * 16, tmem + slot_s(hv) + a_col(kk),
+                        mma_ts_w(tmem + ACC1 + a * 16, tmem + slot_s(kv) + a_col(kk),
                                  mnmajor32_desc(sb + L::SKA + a * L::ATILE + hv * 2048 + kk * 512), idA,
                                  (v > 0 || kk > 0) ? 1u : 0u);
+                tc_commit_w(&B.slot_free[kv]);
                 if (hv == 1) tc_commit_w(&B.empty[stv]);
                 return true;
             };
-            // Q, dO and the q_aug rows are written to TMEM by the elementwise warps
-            bool ok = cx.waitw(&B.res_full, 0);
-            tc_fence_after();
             const int nu = 2 * n;
-            for (int u = 0; ok && u < nu; ++u) {
-                const int jj = u >> 1, half = u & 1, st = jj % NST;
-                if (half == 0 && !cx.waitw(&B.full[st], (jj / NST) & 1)) { ok = false; break; }
-                tc_fence_after();
-                const uint32_t sb = smem_u32(smem + st * L::STAGE);
-                // S = Q K^T (+ Qaug Kaug^T), dP = dO V^T: 128 q rows x 64 kv columns of this half
-#pragma unroll
-                for (int kk = 0; kk < 4; ++kk)
-                    mma_ts_w(tmem + slot_s(half), tmem + R0 + kk * 8,
-                             kmajor_desc(sb + L::SK + half * 8192 + kk * 32, 128), idS, kk > 0);
-#pragma unroll
-                for (int a = 0; a < NA; ++a)
-                    mma_ts_w(tmem + slot_s(half), tmem + RA + a * 8,
-                             kmajor_desc(sb + L::SKA + a * L::ATILE + half * 2048, 32), idS, 1);
-#pragma unroll
-                for (int kk = 0; kk < 4; ++kk)
-                    mma_ts_w(tmem + slot_dp(half), tmem + R1 + kk * 8,
-                             kmajor_desc(sb + L::SV + half * 8192 + kk * 32, 128), idS, kk > 0);
-                tc_commit_w(&B.sdp_full[half]);
-                if (u >= 1 && !grad(u - 1)) { ok = false; break; }
-            }
-            if (ok) ok = grad(nu - 1);
+            bool ok = true;
+            for (int v = 0; ok && v < nu; ++v) ok = grad(v);
             if (ok) tc_commit_w(&B.acc_done);
+            else cx.give_up();
+            tc_commit_w(&B.drain[1]);
+            mbar_wait(&B.drain[1], 0, 500000000ull);
         }
     } else {
         // ---------------- elementwise: thread = q row i, 32 of the 64 columns of a half
@@ -774,12 +791,6 @@ __global__ void __launch_bounds__(kThreads, 1) dq_kernel(const __grid_constant__
         const bool have_docs = p.docs != nullptr;
         const int doc_i = have_docs ? p.docs[i] : 0;
         const int64_t hrow = (int64_t)h * p.T + i;
-        if (n > 0) {
-            load_resident<DA>(p, h, i, tmem + lb, ch);
-            tmem_wait_st();
-            tc_fence_before();
-            mbar_arrive(&B.res_full);
-        }
         const float l2 = p.lse2[hrow], dl = p.delta[hrow];
         // The slope column of k_aug holds positions * s (up to ~T*s).  Its dS sum
         // is accumulated here in fp32 from the unrounded dS, against positions
@@ -795,17 +806,17 @@ __global__ void __launch_bounds__(kThreads, 1) dq_kernel(const __grid_constant__
         bool bad = true;
         const uint64_t c2 = f2_pack(p.scale_log2, p.scale_log2), nl2 = f2_pack(-l2, -l2), nd2 = f2_pack(-dl, -dl);
         for (int u = 0; u < nu && alive; ++u) {
-            const int jj = u >> 1, half = u & 1, st = jj % NST;
+            const int jj = u >> 1, half = u & 1, st = jj % NST, k = u % kSlots;
             if (half == 0) {
                 if (!cx.waitw(&B.full[st], (jj / NST) & 1)) { alive = false; break; }
                 kb = B.stage_blk[st];
                 bad = kb < 0 || kb >= p.QB;
                 mk = B.stage_mk[st];
             }
-            if (!cx.waitw(&B.sdp_full[half], jj & 1)) { alive = false; break; }
+            if (!cx.waitw(&B.sdp_full[k], (u / kSlots) & 1)) { alive = false; break; }
             tc_fence_after();
             float s[32], dp[32];
-            ld_s_dp(tmem + lb + slot_s(half) + ch * 32, tmem + lb + slot_dp(half) + ch * 32, s, dp);
+            ld_s_dp(tmem + lb + slot_s(k) + ch * 32, tmem + lb + slot_dp(k) + ch * 32, s, dp);
             const int j0 = kb * BM + half * 64 + ch * 32;
             const int lim = i - j0;                     // column e visible iff e <= lim (causal: j <= i)
             if (mk == MASK_FULL) dq_piece<false>(s, dp, c2, nl2, nd2, mk, lim, bad, p.docs, j0, doc_i);
@@ -818,10 +829,10 @@ __global__ void __launch_bounds__(kThreads, 1) dq_kernel(const __grid_constant__
                     gsl = fmaf(s[e], kpos - kpos_i, gsl);
                 }
             }
-            st_bf16x32(tmem + lb + slot_s(half) + ch * 32, s);
+            st_bf16x32(tmem + lb + slot_s(k) + ch * 32, s);
             tmem_wait_st();
             tc_fence_before();
-            mbar_arrive(&B.p_full[half]);
+            mbar_arrive(&B.p_full[k]);
         }
         bool have = false;
         if (alive && n > 0) {
@@ -966,15 +977,7 @@ int launch_bwd(const ScopeAttnArgs &a, cudaStream_t s) {
     p.plan = plan;
     p.err = a.err_flag;
 
-    // dK, dV: K, V and k_aug rows resident
-    p.r0 = reinterpret_cast<const __nv_bfloat16 *>(a.k);
-    p.r0_sh = a.k_sh;
-    p.r0_st = a.k_st;
-    p.r1 = reinterpret_cast<const __nv_bfloat16 *>(a.v);
-    p.r1_sh = a.v_sh;
-    p.r1_st = a.v_st;
-    p.ra = reinterpret_cast<const __nv_bfloat16 *>(a.k_aug);
-    p.ra_sh = 0;
+    // dK, dV
     p.g0 = reinterpret_cast<__nv_bfloat16 *>(a.dk);
     p.g0_sh = a.dk_sh;
     p.g0_st = a.dk_st;
@@ -991,15 +994,7 @@ int launch_bwd(const ScopeAttnArgs &a, cudaStream_t s) {
     tcbwd::dkv_kernel<DA><<<ws.max_items, tcbwd::kThreads, smem, s>>>(maps, p);
     SCOPE_CHECK_LAUNCH();
 
-    // dQ (+ coefficient gradients): Q, dO and q_aug rows resident
-    p.r0 = reinterpret_cast<const __nv_bfloat16 *>(a.q);
-    p.r0_sh = a.q_sh;
-    p.r0_st = a.q_st;
-    p.r1 = reinterpret_cast<const __nv_bfloat16 *>(a.dout);
-    p.r1_sh = a.do_sh;
-    p.r1_st = a.do_st;
-    p.ra = reinterpret_cast<const __nv_bfloat16 *>(a.q_aug);
-    p.ra_sh = (int64_t)a.T * DA;
+    // dQ (+ coefficient gradients)
     p.g0 = reinterpret_cast<__nv_bfloat16 *>(a.dq);
     p.g0_sh = a.dq_sh;
     p.g0_st = a.dq_st;
