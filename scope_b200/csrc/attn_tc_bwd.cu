@@ -46,25 +46,25 @@ constexpr int kChunk = 64;             // max q tiles per dK/dV work item
 constexpr int kSlotCap = 128;          // max kv rows whose q list is split
 constexpr uint32_t kTmemCols = 512;
 // TMEM columns (one CTA per SM owns all 512):
-//   [0, 384)    kSlots = 3 slots of {S half, dP half}, 64 + 64 fp32 columns
+//   [0, 256)    two S buffers: S (dq) or S^T (dkv) of a 128 x 128 tile, fp32;
+//               P / dS go back into the buffer as bf16 pairs, over columns the
+//               writing warp has already read
+//   [256, 384)  DP: dP (dq) or dP^T (dkv) of the tile, fp32, one buffer
 //   [384, 448)  ACC0: dV (dkv) | dQ (dq)
 //   [448, 512)  ACC1: dK (dkv) | gradient of the qk_aug dims (dq)
-// Three slots let the S / dP MMAs of half-tile u+2 run while the elementwise
-// warps work on u and the gradient MMAs of u-1 wait for them.
-constexpr int kSlots = 3;
-constexpr uint32_t ACC0 = 384, ACC1 = 448;
+// S is double buffered so S of tile j+1 is computed while the elementwise
+// warps work on tile j; dP of tile j+1 starts once they have read dP of j.
+constexpr uint32_t DPC = 256, ACC0 = 384, ACC1 = 448;
 constexpr uint32_t kSmemBudget = 227 * 1024;   // dynamic shared memory per CTA
 constexpr float kLog2e = 1.4426950408889634f;
 
 __host__ __device__ constexpr uint32_t align1k(uint32_t x) { return (x + 1023u) & ~1023u; }
-__device__ __forceinline__ uint32_t slot_s(int k) { return (uint32_t)k * 128u; }
-__device__ __forceinline__ uint32_t slot_dp(int k) { return (uint32_t)k * 128u + 64u; }
-// The bf16 P / dS of a half go back over the fp32 columns they came from: the
-// warp holding columns [32ch, 32ch+32) writes its 16 packed columns at 32ch,
-// inside what it has already read itself (a write at 16ch would land on
-// columns the other warp of the quadrant may not have loaded yet).  K step kk
-// (16 bf16 = 8 columns) of the A operand therefore starts at column a_col(kk).
-__device__ __forceinline__ uint32_t a_col(int kk) { return (uint32_t)(kk * 8 + (kk >= 2 ? 16 : 0)); }
+__device__ __forceinline__ uint32_t sbuf(int b) { return (uint32_t)b * 128u; }
+// The warp of column half ch (tile columns [64ch, 64ch+64)) writes its bf16
+// pairs at buffer columns [64ch, 64ch+32): K step kk of the contraction (16
+// rows, 8 packed columns) of the TMEM A operand starts at a_col(kk).  In dkv
+// the dS^T pairs follow at +32.
+__device__ __forceinline__ uint32_t a_col(int kk) { return (uint32_t)(64 * (kk >> 2) + 8 * (kk & 3)); }
 
 // ------------------------------------------------------------------ prep
 __global__ void prep_kernel(const __nv_bfloat16 *__restrict__ out, int64_t o_sh, int64_t o_st,
@@ -154,9 +154,11 @@ struct Bars {
     uint64_t res_full;                 // the CTA's resident tiles are in shared memory
     uint64_t acc_done;                 // every MMA of the CTA completed
     uint64_t full[4], empty[4];        // streamed stage ring
-    uint64_t sdp_full[kSlots];         // S / dP of a half are in a TMEM slot
-    uint64_t p_full[kSlots];           // P / dS of that half are back in the slot (elementwise arrivals)
-    uint64_t slot_free[kSlots];        // the gradient MMAs that read the slot completed
+    uint64_t s_full[2];                // S of a tile is in its buffer
+    uint64_t p_full[2];                // P / dS are back in the buffer (elementwise arrivals)
+    uint64_t s_free[2];                // the gradient MMAs that read the buffer completed
+    uint64_t dp_full;                  // dP of a tile is in DP
+    uint64_t dp_free;                  // the elementwise warps have read DP (elementwise arrivals)
     uint64_t drain[2];                 // each issuing warp's MMAs completed (before TMEM is freed)
     volatile int stage_blk[4];         // block index of the tile in each stage
     volatile int stage_mk[4];          // its mask kind
@@ -169,11 +171,13 @@ struct Bars {
             mbar_init(&full[i], 1);
             mbar_init(&empty[i], 1);
         }
-        for (int i = 0; i < kSlots; ++i) {
-            mbar_init(&sdp_full[i], 1);
+        for (int i = 0; i < 2; ++i) {
+            mbar_init(&s_full[i], 1);
             mbar_init(&p_full[i], kElem);
-            mbar_init(&slot_free[i], 1);
+            mbar_init(&s_free[i], 1);
         }
+        mbar_init(&dp_full, 1);
+        mbar_init(&dp_free, kElem);
         mbar_init(&drain[0], 1);
         mbar_init(&drain[1], 1);
         abort_flag = 0;
@@ -195,6 +199,10 @@ __device__ __forceinline__ void ld_s_dp(uint32_t ts, uint32_t tdp, float (&s)[32
         s[e] = __uint_as_float(a[e]);
         dp[e] = __uint_as_float(b[e]);
     }
+}
+__device__ __forceinline__ void pack16(const float (&x)[32], uint32_t (&pk)[16]) {
+#pragma unroll
+    for (int e = 0; e < 16; ++e) pk[e] = pack_bf16(x[2 * e], x[2 * e + 1]);
 }
 // 32 values as 16 bf16 pairs at taddr
 __device__ __forceinline__ void st_bf16x32(uint32_t taddr, const float (&x)[32]) {
@@ -397,31 +405,33 @@ __global__ void __launch_bounds__(kThreads, 1) dkv_kernel(const __grid_constant_
     } else if (warp == 1) {
         // ---------------- S / dP issuer (whole warp, one elected lane issues)
         if (nq > 0) {
-            constexpr uint32_t idS = idesc_bf16(128, 64, false, false);
+            constexpr uint32_t idS = idesc_bf16(128, 128, false, false);
             const uint32_t sK = smem_u32(smem + L::K), sKA = smem_u32(smem + L::KA), sV = smem_u32(smem + L::V);
             bool ok = cx.waitw(&B.res_full, 0);
-            const int nu = 2 * nq;
-            // half-tile u: S / dP into slot u % 3 once the gradient MMAs of u - 3 released it
-            for (int u = 0; ok && u < nu; ++u) {
-                const int t = u >> 1, half = u & 1, st = t % NST, k = u % kSlots;
-                if (half == 0 && !cx.waitw(&B.full[st], (t / NST) & 1)) { ok = false; break; }
-                if (u >= kSlots && !cx.waitw(&B.slot_free[k], ((u / kSlots) - 1) & 1)) { ok = false; break; }
+            for (int t = 0; ok && t < nq; ++t) {
+                const int st = t % NST, b = t & 1;
+                if (!cx.waitw(&B.full[st], (t / NST) & 1)) { ok = false; break; }
+                if (t >= 2 && !cx.waitw(&B.s_free[b], ((t >> 1) - 1) & 1)) { ok = false; break; }
                 tc_fence_after();
                 const uint32_t sb = smem_u32(smem + L::STAGE0 + st * L::STAGE);
-                // S^T = K Q^T (+ Kaug Qaug^T), dP^T = V dO^T: 128 kv rows x 64 q columns of this half
+                // S^T = K Q^T (+ Kaug Qaug^T): 128 kv rows x 128 q columns
 #pragma unroll
                 for (int kk = 0; kk < 4; ++kk)
-                    mma_ss_w(tmem + slot_s(k), kmajor_desc(sK + kk * 32, 128),
-                             kmajor_desc(sb + L::SQ + half * 8192 + kk * 32, 128), idS, kk > 0);
+                    mma_ss_w(tmem + sbuf(b), kmajor_desc(sK + kk * 32, 128), kmajor_desc(sb + L::SQ + kk * 32, 128), idS,
+                             kk > 0);
 #pragma unroll
                 for (int a = 0; a < NA; ++a)
-                    mma_ss_w(tmem + slot_s(k), kmajor_desc(sKA + a * L::ATILE, 32),
-                             kmajor_desc(sb + L::SQA + a * L::ATILE + half * 2048, 32), idS, 1);
+                    mma_ss_w(tmem + sbuf(b), kmajor_desc(sKA + a * L::ATILE, 32),
+                             kmajor_desc(sb + L::SQA + a * L::ATILE, 32), idS, 1);
+                tc_commit_w(&B.s_full[b]);
+                // dP^T = V dO^T, once the elementwise warps have read dP^T of the previous tile
+                if (t >= 1 && !cx.waitw(&B.dp_free, (t - 1) & 1)) { ok = false; break; }
+                tc_fence_after();
 #pragma unroll
                 for (int kk = 0; kk < 4; ++kk)
-                    mma_ss_w(tmem + slot_dp(k), kmajor_desc(sV + kk * 32, 128),
-                             kmajor_desc(sb + L::SDO + half * 8192 + kk * 32, 128), idS, kk > 0);
-                tc_commit_w(&B.sdp_full[k]);
+                    mma_ss_w(tmem + DPC, kmajor_desc(sV + kk * 32, 128), kmajor_desc(sb + L::SDO + kk * 32, 128), idS,
+                             kk > 0);
+                tc_commit_w(&B.dp_full);
             }
             if (!ok) cx.give_up();
             tc_commit_w(&B.drain[0]);   // TMEM is freed only after this warp's MMAs completed
@@ -429,72 +439,82 @@ __global__ void __launch_bounds__(kThreads, 1) dkv_kernel(const __grid_constant_
         }
     } else if (warp == kGradWarp) {
         // ---------------- gradient issuer (whole warp): a second issuing warp, so
-        // the S / dP MMAs and these queue on the tensor pipe side by side and
-        // neither warp's waits leave it idle
+        // the S / dP MMAs and these queue on the tensor pipe side by side
         if (nq > 0) {
             constexpr uint32_t idG = idesc_bf16(128, 64, false, true);
-            auto grad = [&](int v) -> bool {
-                const int tv = v >> 1, hv = v & 1, stv = tv % NST, kv = v % kSlots;
-                if (!cx.waitw(&B.p_full[kv], (v / kSlots) & 1)) return false;
-                tc_fence_after();
-                const uint32_t sb = smem_u32(smem + L::STAGE0 + stv * L::STAGE);
-#pragma unroll
-                for (int kk = 0; kk < 4; ++kk)
-                    mma_ts_w(tmem + ACC0, tmem + slot_s(kv) + a_col(kk),
-                             mnmajor128_desc(sb + L::SDO + hv * 8192 + kk * 2048), idG, (v > 0 || kk > 0) ? 1u : 0u);
-#pragma unroll
-                for (int kk = 0; kk < 4; ++kk)
-                    mma_ts_w(tmem + ACC1, tmem + slot_dp(kv) + a_col(kk),
-                             mnmajor128_desc(sb + L::SQ + hv * 8192 + kk * 2048), idG, (v > 0 || kk > 0) ? 1u : 0u);
-                tc_commit_w(&B.slot_free[kv]);
-                if (hv == 1) tc_commit_w(&B.empty[stv]);
-                return true;
-            };
-            const int nu = 2 * nq;
             bool ok = true;
-            for (int v = 0; ok && v < nu; ++v) ok = grad(v);
+            for (int t = 0; ok && t < nq; ++t) {
+                const int st = t % NST, b = t & 1;
+                if (!cx.waitw(&B.p_full[b], (t >> 1) & 1)) { ok = false; break; }
+                tc_fence_after();
+                const uint32_t sb = smem_u32(smem + L::STAGE0 + st * L::STAGE);
+                // dV += P^T dO, dK += dS^T Q over the tile's 128 q rows
+#pragma unroll
+                for (int kk = 0; kk < 8; ++kk)
+                    mma_ts_w(tmem + ACC0, tmem + sbuf(b) + a_col(kk), mnmajor128_desc(sb + L::SDO + kk * 2048), idG,
+                             (t > 0 || kk > 0) ? 1u : 0u);
+#pragma unroll
+                for (int kk = 0; kk < 8; ++kk)
+                    mma_ts_w(tmem + ACC1, tmem + sbuf(b) + a_col(kk) + 32, mnmajor128_desc(sb + L::SQ + kk * 2048), idG,
+                             (t > 0 || kk > 0) ? 1u : 0u);
+                tc_commit_w(&B.s_free[b]);
+                tc_commit_w(&B.empty[st]);
+            }
             if (ok) tc_commit_w(&B.acc_done);
             else cx.give_up();
             tc_commit_w(&B.drain[1]);
             mbar_wait(&B.drain[1], 0, 500000000ull);
         }
     } else {
-        // ---------------- elementwise: thread = kv row c, 32 of the 64 columns of a half
+        // ---------------- elementwise: thread = kv row c, tile columns [64ch, 64ch+64) in two chunks of 32
         const int quad = warp & 3;
-        const int ch = (warp - 2) >> 2;                 // column half within the 64-column unit
+        const int ch = (warp - 2) >> 2;
         const int c = quad * 32 + lane;
         const int j = kb * BM + c;
         const uint32_t lb = (uint32_t)(quad * 32) << 16;
         const bool have_docs = p.docs != nullptr;
         const int doc_j = have_docs ? p.docs[j] : 0;
+        const uint64_t c2 = f2_pack(p.scale_log2, p.scale_log2);
         bool alive = true;
-        const int nu = 2 * nq;
-        int mk = MASK_DOCS, qb = 0;
-        for (int u = 0; u < nu && alive; ++u) {
-            const int t = u >> 1, half = u & 1, st = t % NST, k = u % kSlots;
-            if (half == 0) {
-                if (!cx.waitw(&B.full[st], (t / NST) & 1)) { alive = false; break; }
-                qb = B.stage_blk[st];
-                mk = B.stage_mk[st];
-            }
-            if (!cx.waitw(&B.sdp_full[k], (u / kSlots) & 1)) { alive = false; break; }
+        for (int t = 0; t < nq && alive; ++t) {
+            const int st = t % NST, b = t & 1;
+            if (!cx.waitw(&B.full[st], (t / NST) & 1)) { alive = false; break; }
+            const int qb = B.stage_blk[st];
+            const int mk = B.stage_mk[st];
+            if (!cx.waitw(&B.s_full[b], (t >> 1) & 1) || !cx.waitw(&B.dp_full, t & 1)) { alive = false; break; }
             tc_fence_after();
-            float s[32], dp[32];
-            ld_s_dp(tmem + lb + slot_s(k) + ch * 32, tmem + lb + slot_dp(k) + ch * 32, s, dp);
-            const uint8_t *sb = smem + L::STAGE0 + st * L::STAGE;
-            const int col0 = half * 64 + ch * 32;       // q row within the tile of the first column
-            const float4 *LS = reinterpret_cast<const float4 *>(sb + L::SLSE) + col0 / 4;
-            const float4 *DL = reinterpret_cast<const float4 *>(sb + L::SDEL) + col0 / 4;
-            const int i0 = qb * BM + col0;
-            const int lim = j - i0;                     // column e visible iff e >= lim (causal: j <= i)
-            const uint64_t c2 = f2_pack(p.scale_log2, p.scale_log2);
-            if (mk == MASK_FULL) dkv_piece<false>(s, dp, LS, DL, c2, mk, lim, p.docs, i0, doc_j);
-            else dkv_piece<true>(s, dp, LS, DL, c2, mk, lim, p.docs, i0, doc_j);
-            st_bf16x32(tmem + lb + slot_s(k) + ch * 32, s);
-            st_bf16x32(tmem + lb + slot_dp(k) + ch * 32, dp);
+            const uint8_t *sbp = smem + L::STAGE0 + st * L::STAGE;
+            const uint32_t tb = tmem + lb + sbuf(b) + ch * 64;
+            uint32_t ds0[16];
+#pragma unroll
+            for (int cc = 0; cc < 2; ++cc) {
+                float s[32], dp[32];
+                ld_s_dp(tb + cc * 32, tmem + lb + DPC + ch * 64 + cc * 32, s, dp);
+                if (cc == 1) {
+                    tc_fence_before();
+                    mbar_arrive(&B.dp_free);        // this warp's dP^T columns are in registers
+                }
+                const int col0 = ch * 64 + cc * 32;  // q row within the tile of the first column
+                const float4 *LS = reinterpret_cast<const float4 *>(sbp + L::SLSE) + col0 / 4;
+                const float4 *DL = reinterpret_cast<const float4 *>(sbp + L::SDEL) + col0 / 4;
+                const int i0 = qb * BM + col0;
+                const int lim = j - i0;              // column e visible iff e >= lim (causal: j <= i)
+                if (mk == MASK_FULL) dkv_piece<false>(s, dp, LS, DL, c2, mk, lim, p.docs, i0, doc_j);
+                else dkv_piece<true>(s, dp, LS, DL, c2, mk, lim, p.docs, i0, doc_j);
+                uint32_t pk[16];
+                pack16(s, pk);
+                tmem_st16(tb + cc * 16, pk);         // P^T pairs over columns this warp has read
+                if (cc == 0) {
+                    pack16(dp, ds0);                 // dS^T pairs of chunk 0 wait until chunk 1 is read
+                } else {
+                    pack16(dp, pk);
+                    tmem_st16(tb + 32, ds0);
+                    tmem_st16(tb + 48, pk);
+                }
+            }
             tmem_wait_st();
             tc_fence_before();
-            mbar_arrive(&B.p_full[k]);
+            mbar_arrive(&B.p_full[b]);
         }
         bool have = false;
         if (alive && nq > 0) {
@@ -716,31 +736,33 @@ __global__ void __launch_bounds__(kThreads, 1) dq_kernel(const __grid_constant__
     } else if (warp == 1) {
         // ---------------- S / dP issuer (whole warp, one elected lane issues)
         if (n > 0) {
-            constexpr uint32_t idS = idesc_bf16(128, 64, false, false);
+            constexpr uint32_t idS = idesc_bf16(128, 128, false, false);
             const uint32_t sQ = smem_u32(smem + L::Q), sQA = smem_u32(smem + L::QA), sDO = smem_u32(smem + L::DO);
             bool ok = cx.waitw(&B.res_full, 0);
-            const int nu = 2 * n;
-            // half-tile u: S / dP into slot u % 3 once the gradient MMAs of u - 3 released it
-            for (int u = 0; ok && u < nu; ++u) {
-                const int jj = u >> 1, half = u & 1, st = jj % NST, k = u % kSlots;
-                if (half == 0 && !cx.waitw(&B.full[st], (jj / NST) & 1)) { ok = false; break; }
-                if (u >= kSlots && !cx.waitw(&B.slot_free[k], ((u / kSlots) - 1) & 1)) { ok = false; break; }
+            for (int jj = 0; ok && jj < n; ++jj) {
+                const int st = jj % NST, b = jj & 1;
+                if (!cx.waitw(&B.full[st], (jj / NST) & 1)) { ok = false; break; }
+                if (jj >= 2 && !cx.waitw(&B.s_free[b], ((jj >> 1) - 1) & 1)) { ok = false; break; }
                 tc_fence_after();
                 const uint32_t sb = smem_u32(smem + L::STAGE0 + st * L::STAGE);
-                // S = Q K^T (+ Qaug Kaug^T), dP = dO V^T: 128 q rows x 64 kv columns of this half
+                // S = Q K^T (+ Qaug Kaug^T): 128 q rows x 128 kv columns
 #pragma unroll
                 for (int kk = 0; kk < 4; ++kk)
-                    mma_ss_w(tmem + slot_s(k), kmajor_desc(sQ + kk * 32, 128),
-                             kmajor_desc(sb + L::SK + half * 8192 + kk * 32, 128), idS, kk > 0);
+                    mma_ss_w(tmem + sbuf(b), kmajor_desc(sQ + kk * 32, 128), kmajor_desc(sb + L::SK + kk * 32, 128), idS,
+                             kk > 0);
 #pragma unroll
                 for (int a = 0; a < NA; ++a)
-                    mma_ss_w(tmem + slot_s(k), kmajor_desc(sQA + a * L::ATILE, 32),
-                             kmajor_desc(sb + L::SKA + a * L::ATILE + half * 2048, 32), idS, 1);
+                    mma_ss_w(tmem + sbuf(b), kmajor_desc(sQA + a * L::ATILE, 32),
+                             kmajor_desc(sb + L::SKA + a * L::ATILE, 32), idS, 1);
+                tc_commit_w(&B.s_full[b]);
+                // dP = dO V^T, once the elementwise warps have read dP of the previous tile
+                if (jj >= 1 && !cx.waitw(&B.dp_free, (jj - 1) & 1)) { ok = false; break; }
+                tc_fence_after();
 #pragma unroll
                 for (int kk = 0; kk < 4; ++kk)
-                    mma_ss_w(tmem + slot_dp(k), kmajor_desc(sDO + kk * 32, 128),
-                             kmajor_desc(sb + L::SV + half * 8192 + kk * 32, 128), idS, kk > 0);
-                tc_commit_w(&B.sdp_full[k]);
+                    mma_ss_w(tmem + DPC, kmajor_desc(sDO + kk * 32, 128), kmajor_desc(sb + L::SV + kk * 32, 128), idS,
+                             kk > 0);
+                tc_commit_w(&B.dp_full);
             }
             if (!ok) cx.give_up();
             tc_commit_w(&B.drain[0]);   // TMEM is freed only after this warp's MMAs completed
@@ -748,41 +770,37 @@ __global__ void __launch_bounds__(kThreads, 1) dq_kernel(const __grid_constant__
         }
     } else if (warp == kGradWarp) {
         // ---------------- gradient issuer (whole warp): a second issuing warp, so
-        // the S / dP MMAs and these queue on the tensor pipe side by side and
-        // neither warp's waits leave it idle
+        // the S / dP MMAs and these queue on the tensor pipe side by side
         if (n > 0) {
             constexpr uint32_t idG = idesc_bf16(128, 64, false, true);
             constexpr uint32_t idA = idesc_bf16(128, 16, false, true);
-            auto grad = [&](int v) -> bool {
-                const int jv = v >> 1, hv = v & 1, stv = jv % NST, kv = v % kSlots;
-                if (!cx.waitw(&B.p_full[kv], (v / kSlots) & 1)) return false;
+            bool ok = true;
+            for (int jj = 0; ok && jj < n; ++jj) {
+                const int st = jj % NST, b = jj & 1;
+                if (!cx.waitw(&B.p_full[b], (jj >> 1) & 1)) { ok = false; break; }
                 tc_fence_after();
-                const uint32_t sb = smem_u32(smem + L::STAGE0 + stv * L::STAGE);
+                const uint32_t sb = smem_u32(smem + L::STAGE0 + st * L::STAGE);
+                // dQ += dS K (+ dQaug += dS Kaug) over the tile's 128 kv rows
 #pragma unroll
-                for (int kk = 0; kk < 4; ++kk)
-                    mma_ts_w(tmem + ACC0, tmem + slot_s(kv) + a_col(kk),
-                             mnmajor128_desc(sb + L::SK + hv * 8192 + kk * 2048), idG, (v > 0 || kk > 0) ? 1u : 0u);
+                for (int kk = 0; kk < 8; ++kk)
+                    mma_ts_w(tmem + ACC0, tmem + sbuf(b) + a_col(kk), mnmajor128_desc(sb + L::SK + kk * 2048), idG,
+                             (jj > 0 || kk > 0) ? 1u : 0u);
 #pragma unroll
                 for (int a = 0; a < NA; ++a)
 #pragma unroll
-                    for (int kk = 0; kk < 4; ++kk)
-                        mma_ts_w(tmem + ACC1 + a * 16, tmem + slot_s(kv) + a_col(kk),
-                                 mnmajor32_desc(sb + L::SKA + a * L::ATILE + hv * 2048 + kk * 512), idA,
-                                 (v > 0 || kk > 0) ? 1u : 0u);
-                tc_commit_w(&B.slot_free[kv]);
-                if (hv == 1) tc_commit_w(&B.empty[stv]);
-                return true;
-            };
-            const int nu = 2 * n;
-            bool ok = true;
-            for (int v = 0; ok && v < nu; ++v) ok = grad(v);
+                    for (int kk = 0; kk < 8; ++kk)
+                        mma_ts_w(tmem + ACC1 + a * 16, tmem + sbuf(b) + a_col(kk),
+                                 mnmajor32_desc(sb + L::SKA + a * L::ATILE + kk * 512), idA, (jj > 0 || kk > 0) ? 1u : 0u);
+                tc_commit_w(&B.s_free[b]);
+                tc_commit_w(&B.empty[st]);
+            }
             if (ok) tc_commit_w(&B.acc_done);
             else cx.give_up();
             tc_commit_w(&B.drain[1]);
             mbar_wait(&B.drain[1], 0, 500000000ull);
         }
     } else {
-        // ---------------- elementwise: thread = q row i, 32 of the 64 columns of a half
+        // ---------------- elementwise: thread = q row i, tile columns [64ch, 64ch+64) in two chunks of 32
         const int quad = warp & 3;
         const int ch = (warp - 2) >> 2;
         const int r = quad * 32 + lane;
@@ -801,38 +819,41 @@ __global__ void __launch_bounds__(kThreads, 1) dq_kernel(const __grid_constant__
         const float kpos_i = __bfloat162float(__float2bfloat16_rn(__fmul_rn((float)i, p.s_aug)));
         float gsl = 0.f;
         bool alive = true;
-        const int nu = 2 * n;
-        int kb = 0, mk = MASK_DOCS;
-        bool bad = true;
         const uint64_t c2 = f2_pack(p.scale_log2, p.scale_log2), nl2 = f2_pack(-l2, -l2), nd2 = f2_pack(-dl, -dl);
-        for (int u = 0; u < nu && alive; ++u) {
-            const int jj = u >> 1, half = u & 1, st = jj % NST, k = u % kSlots;
-            if (half == 0) {
-                if (!cx.waitw(&B.full[st], (jj / NST) & 1)) { alive = false; break; }
-                kb = B.stage_blk[st];
-                bad = kb < 0 || kb >= p.QB;
-                mk = B.stage_mk[st];
-            }
-            if (!cx.waitw(&B.sdp_full[k], (u / kSlots) & 1)) { alive = false; break; }
+        for (int jj = 0; jj < n && alive; ++jj) {
+            const int st = jj % NST, b = jj & 1;
+            if (!cx.waitw(&B.full[st], (jj / NST) & 1)) { alive = false; break; }
+            const int kb = B.stage_blk[st];
+            const bool bad = kb < 0 || kb >= p.QB;
+            const int mk = B.stage_mk[st];
+            if (!cx.waitw(&B.s_full[b], (jj >> 1) & 1) || !cx.waitw(&B.dp_full, jj & 1)) { alive = false; break; }
             tc_fence_after();
-            float s[32], dp[32];
-            ld_s_dp(tmem + lb + slot_s(k) + ch * 32, tmem + lb + slot_dp(k) + ch * 32, s, dp);
-            const int j0 = kb * BM + half * 64 + ch * 32;
-            const int lim = i - j0;                     // column e visible iff e <= lim (causal: j <= i)
-            if (mk == MASK_FULL) dq_piece<false>(s, dp, c2, nl2, nd2, mk, lim, bad, p.docs, j0, doc_i);
-            else dq_piece<true>(s, dp, c2, nl2, nd2, mk, lim, bad, p.docs, j0, doc_i);
-            if (slope_acc && !bad) {
+            const uint32_t tb = tmem + lb + sbuf(b) + ch * 64;
 #pragma unroll
-                for (int e = 0; e < 32; ++e) {
-                    // the value scope_qk_aug_prepare stored: bf16(fp32(j) * s)
-                    const float kpos = __bfloat162float(__float2bfloat16_rn(__fmul_rn((float)(j0 + e), p.s_aug)));
-                    gsl = fmaf(s[e], kpos - kpos_i, gsl);
+            for (int cc = 0; cc < 2; ++cc) {
+                float s[32], dp[32];
+                ld_s_dp(tb + cc * 32, tmem + lb + DPC + ch * 64 + cc * 32, s, dp);
+                if (cc == 1) {
+                    tc_fence_before();
+                    mbar_arrive(&B.dp_free);        // this warp's dP columns are in registers
                 }
+                const int j0 = kb * BM + ch * 64 + cc * 32;
+                const int lim = i - j0;              // column e visible iff e <= lim (causal: j <= i)
+                if (mk == MASK_FULL) dq_piece<false>(s, dp, c2, nl2, nd2, mk, lim, bad, p.docs, j0, doc_i);
+                else dq_piece<true>(s, dp, c2, nl2, nd2, mk, lim, bad, p.docs, j0, doc_i);
+                if (slope_acc && !bad) {
+#pragma unroll
+                    for (int e = 0; e < 32; ++e) {
+                        // the value scope_qk_aug_prepare stored: bf16(fp32(j) * s)
+                        const float kpos = __bfloat162float(__float2bfloat16_rn(__fmul_rn((float)(j0 + e), p.s_aug)));
+                        gsl = fmaf(s[e], kpos - kpos_i, gsl);
+                    }
+                }
+                st_bf16x32(tb + cc * 16, s);         // dS pairs over columns this warp has read
             }
-            st_bf16x32(tmem + lb + slot_s(k) + ch * 32, s);
             tmem_wait_st();
             tc_fence_before();
-            mbar_arrive(&B.p_full[k]);
+            mbar_arrive(&B.p_full[b]);
         }
         bool have = false;
         if (alive && n > 0) {
