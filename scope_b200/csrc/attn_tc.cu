@@ -205,7 +205,7 @@ __global__ void __launch_bounds__(kThreads, 2) fwd_kernel(const __grid_constant_
         }
     } else if (warp == 1) {
         // ------------------------------------------------------------ tcgen05 issuer
-        if (n > 0) {   // the whole warp; one elected lane issues
+        if (n > 0) {   // the whole warp waits; lane 0 issues
             constexpr uint32_t idS = idesc_bf16(128, 128, false, false);
             constexpr uint32_t idO = idesc_bf16(128, 64, false, true);
             const uint32_t tS = tmem + S_COL, tO = tmem + O_COL, tP = tmem + P_COL;
@@ -216,16 +216,19 @@ __global__ void __launch_bounds__(kThreads, 2) fwd_kernel(const __grid_constant_
                 if (!warp_wait(kv_full + s, (j >> 1) & 1)) return false;
                 tc_fence_after();
                 const uint32_t sk = smem_u32(smem + L::STAGE0 + s * L::STAGE);
+                if (lane == 0) {
 #pragma unroll
-                for (int kk = 0; kk < HD / 16; ++kk)
-                    mma_ss_w(tS, kmajor_desc(sq + L::Q + kk * 32, 128), kmajor_desc(sk + L::K + kk * 32, 128), idS,
-                           kk > 0);
+                    for (int kk = 0; kk < HD / 16; ++kk)
+                        mma_ss(tS, kmajor_desc(sq + L::Q + kk * 32, 128), kmajor_desc(sk + L::K + kk * 32, 128), idS,
+                               kk > 0);
 #pragma unroll
-                for (int a = 0; a < NA; ++a)
-                    mma_ss_w(tS, kmajor_desc(sq + L::QA + a * L::ATILE, 32), kmajor_desc(sk + L::KA + a * L::ATILE, 32),
-                           idS, 1);
-                tc_commit_w(s_full);
-                tc_commit_w(kv_empty + s);   // K of this stage may be reloaded once S is done
+                    for (int a = 0; a < NA; ++a)
+                        mma_ss(tS, kmajor_desc(sq + L::QA + a * L::ATILE, 32), kmajor_desc(sk + L::KA + a * L::ATILE, 32),
+                               idS, 1);
+                    tc_commit(s_full);
+                    tc_commit(kv_empty + s);   // K of this stage may be reloaded once S is done
+                }
+                __syncwarp();
                 return true;
             };
             ok = ok && issue_S(0);
@@ -238,11 +241,14 @@ __global__ void __launch_bounds__(kThreads, 2) fwd_kernel(const __grid_constant_
                 if (!warp_wait(v_full + (j & 1), (j >> 1) & 1)) { ok = false; break; }
                 tc_fence_after();
                 const uint32_t sv = smem_u32(smem + L::STAGE0 + (j & 1) * L::STAGE + L::V);
+                if (lane == 0) {
 #pragma unroll
-                for (int kk = 0; kk < BM / 16; ++kk)
-                    mma_ts_w(tO, tP + kk * 8, mnmajor128_desc(sv + kk * 2048), idO, (j > 0 || kk > 0) ? 1u : 0u);
-                tc_commit_w(o_done);
-                tc_commit_w(v_empty + (j & 1));
+                    for (int kk = 0; kk < BM / 16; ++kk)
+                        mma_ts(tO, tP + kk * 8, mnmajor128_desc(sv + kk * 2048), idO, (j > 0 || kk > 0) ? 1u : 0u);
+                    tc_commit(o_done);
+                    tc_commit(v_empty + (j & 1));
+                }
+                __syncwarp();
             }
             if (!ok) give_up();
         }

@@ -403,7 +403,7 @@ __global__ void __launch_bounds__(kThreads, 1) dkv_kernel(const __grid_constant_
             for (int j = (t > NST ? t - NST : 0); j < t; ++j) mbar_wait(&B.full[j % NST], (j / NST) & 1, 500000000ull);
         }
     } else if (warp == 1) {
-        // ---------------- S / dP issuer (whole warp, one elected lane issues)
+        // ---------------- S / dP issuer (the whole warp waits, lane 0 issues)
         if (nq > 0) {
             constexpr uint32_t idS = idesc_bf16(128, 128, false, false);
             const uint32_t sK = smem_u32(smem + L::K), sKA = smem_u32(smem + L::KA), sV = smem_u32(smem + L::V);
@@ -415,26 +415,32 @@ __global__ void __launch_bounds__(kThreads, 1) dkv_kernel(const __grid_constant_
                 tc_fence_after();
                 const uint32_t sb = smem_u32(smem + L::STAGE0 + st * L::STAGE);
                 // S^T = K Q^T (+ Kaug Qaug^T): 128 kv rows x 128 q columns
+                if (lane == 0) {
 #pragma unroll
-                for (int kk = 0; kk < 4; ++kk)
-                    mma_ss_w(tmem + sbuf(b), kmajor_desc(sK + kk * 32, 128), kmajor_desc(sb + L::SQ + kk * 32, 128), idS,
-                             kk > 0);
+                    for (int kk = 0; kk < 4; ++kk)
+                        mma_ss(tmem + sbuf(b), kmajor_desc(sK + kk * 32, 128), kmajor_desc(sb + L::SQ + kk * 32, 128),
+                               idS, kk > 0);
 #pragma unroll
-                for (int a = 0; a < NA; ++a)
-                    mma_ss_w(tmem + sbuf(b), kmajor_desc(sKA + a * L::ATILE, 32),
-                             kmajor_desc(sb + L::SQA + a * L::ATILE, 32), idS, 1);
-                tc_commit_w(&B.s_full[b]);
+                    for (int a = 0; a < NA; ++a)
+                        mma_ss(tmem + sbuf(b), kmajor_desc(sKA + a * L::ATILE, 32),
+                               kmajor_desc(sb + L::SQA + a * L::ATILE, 32), idS, 1);
+                    tc_commit(&B.s_full[b]);
+                }
+                __syncwarp();
                 // dP^T = V dO^T, once the elementwise warps have read dP^T of the previous tile
                 if (t >= 1 && !cx.waitw(&B.dp_free, (t - 1) & 1)) { ok = false; break; }
                 tc_fence_after();
+                if (lane == 0) {
 #pragma unroll
-                for (int kk = 0; kk < 4; ++kk)
-                    mma_ss_w(tmem + DPC, kmajor_desc(sV + kk * 32, 128), kmajor_desc(sb + L::SDO + kk * 32, 128), idS,
-                             kk > 0);
-                tc_commit_w(&B.dp_full);
+                    for (int kk = 0; kk < 4; ++kk)
+                        mma_ss(tmem + DPC, kmajor_desc(sV + kk * 32, 128), kmajor_desc(sb + L::SDO + kk * 32, 128), idS,
+                               kk > 0);
+                    tc_commit(&B.dp_full);
+                }
+                __syncwarp();
             }
             if (!ok) cx.give_up();
-            tc_commit_w(&B.drain[0]);   // TMEM is freed only after this warp's MMAs completed
+            if (lane == 0) tc_commit(&B.drain[0]);   // TMEM is freed only after this warp's MMAs completed
             mbar_wait(&B.drain[0], 0, 500000000ull);
         }
     } else if (warp == kGradWarp) {
@@ -449,20 +455,23 @@ __global__ void __launch_bounds__(kThreads, 1) dkv_kernel(const __grid_constant_
                 tc_fence_after();
                 const uint32_t sb = smem_u32(smem + L::STAGE0 + st * L::STAGE);
                 // dV += P^T dO, dK += dS^T Q over the tile's 128 q rows
+                if (lane == 0) {
 #pragma unroll
-                for (int kk = 0; kk < 8; ++kk)
-                    mma_ts_w(tmem + ACC0, tmem + sbuf(b) + a_col(kk), mnmajor128_desc(sb + L::SDO + kk * 2048), idG,
-                             (t > 0 || kk > 0) ? 1u : 0u);
+                    for (int kk = 0; kk < 8; ++kk)
+                        mma_ts(tmem + ACC0, tmem + sbuf(b) + a_col(kk), mnmajor128_desc(sb + L::SDO + kk * 2048), idG,
+                               (t > 0 || kk > 0) ? 1u : 0u);
 #pragma unroll
-                for (int kk = 0; kk < 8; ++kk)
-                    mma_ts_w(tmem + ACC1, tmem + sbuf(b) + a_col(kk) + 32, mnmajor128_desc(sb + L::SQ + kk * 2048), idG,
-                             (t > 0 || kk > 0) ? 1u : 0u);
-                tc_commit_w(&B.s_free[b]);
-                tc_commit_w(&B.empty[st]);
+                    for (int kk = 0; kk < 8; ++kk)
+                        mma_ts(tmem + ACC1, tmem + sbuf(b) + a_col(kk) + 32, mnmajor128_desc(sb + L::SQ + kk * 2048), idG,
+                               (t > 0 || kk > 0) ? 1u : 0u);
+                    tc_commit(&B.s_free[b]);
+                    tc_commit(&B.empty[st]);
+                }
+                __syncwarp();
             }
-            if (ok) tc_commit_w(&B.acc_done);
-            else cx.give_up();
-            tc_commit_w(&B.drain[1]);
+            if (ok && lane == 0) tc_commit(&B.acc_done);
+            if (!ok) cx.give_up();
+            if (lane == 0) tc_commit(&B.drain[1]);
             mbar_wait(&B.drain[1], 0, 500000000ull);
         }
     } else {
@@ -734,7 +743,7 @@ __global__ void __launch_bounds__(kThreads, 1) dq_kernel(const __grid_constant__
                 mbar_wait(&B.full[j % NST], (j / NST) & 1, 500000000ull);
         }
     } else if (warp == 1) {
-        // ---------------- S / dP issuer (whole warp, one elected lane issues)
+        // ---------------- S / dP issuer (the whole warp waits, lane 0 issues)
         if (n > 0) {
             constexpr uint32_t idS = idesc_bf16(128, 128, false, false);
             const uint32_t sQ = smem_u32(smem + L::Q), sQA = smem_u32(smem + L::QA), sDO = smem_u32(smem + L::DO);
@@ -746,26 +755,32 @@ __global__ void __launch_bounds__(kThreads, 1) dq_kernel(const __grid_constant__
                 tc_fence_after();
                 const uint32_t sb = smem_u32(smem + L::STAGE0 + st * L::STAGE);
                 // S = Q K^T (+ Qaug Kaug^T): 128 q rows x 128 kv columns
+                if (lane == 0) {
 #pragma unroll
-                for (int kk = 0; kk < 4; ++kk)
-                    mma_ss_w(tmem + sbuf(b), kmajor_desc(sQ + kk * 32, 128), kmajor_desc(sb + L::SK + kk * 32, 128), idS,
-                             kk > 0);
+                    for (int kk = 0; kk < 4; ++kk)
+                        mma_ss(tmem + sbuf(b), kmajor_desc(sQ + kk * 32, 128), kmajor_desc(sb + L::SK + kk * 32, 128),
+                               idS, kk > 0);
 #pragma unroll
-                for (int a = 0; a < NA; ++a)
-                    mma_ss_w(tmem + sbuf(b), kmajor_desc(sQA + a * L::ATILE, 32),
-                             kmajor_desc(sb + L::SKA + a * L::ATILE, 32), idS, 1);
-                tc_commit_w(&B.s_full[b]);
+                    for (int a = 0; a < NA; ++a)
+                        mma_ss(tmem + sbuf(b), kmajor_desc(sQA + a * L::ATILE, 32),
+                               kmajor_desc(sb + L::SKA + a * L::ATILE, 32), idS, 1);
+                    tc_commit(&B.s_full[b]);
+                }
+                __syncwarp();
                 // dP = dO V^T, once the elementwise warps have read dP of the previous tile
                 if (jj >= 1 && !cx.waitw(&B.dp_free, (jj - 1) & 1)) { ok = false; break; }
                 tc_fence_after();
+                if (lane == 0) {
 #pragma unroll
-                for (int kk = 0; kk < 4; ++kk)
-                    mma_ss_w(tmem + DPC, kmajor_desc(sDO + kk * 32, 128), kmajor_desc(sb + L::SV + kk * 32, 128), idS,
-                             kk > 0);
-                tc_commit_w(&B.dp_full);
+                    for (int kk = 0; kk < 4; ++kk)
+                        mma_ss(tmem + DPC, kmajor_desc(sDO + kk * 32, 128), kmajor_desc(sb + L::SV + kk * 32, 128), idS,
+                               kk > 0);
+                    tc_commit(&B.dp_full);
+                }
+                __syncwarp();
             }
             if (!ok) cx.give_up();
-            tc_commit_w(&B.drain[0]);   // TMEM is freed only after this warp's MMAs completed
+            if (lane == 0) tc_commit(&B.drain[0]);   // TMEM is freed only after this warp's MMAs completed
             mbar_wait(&B.drain[0], 0, 500000000ull);
         }
     } else if (warp == kGradWarp) {
@@ -773,7 +788,10 @@ __global__ void __launch_bounds__(kThreads, 1) dq_kernel(const __grid_constant__
         // the S / dP MMAs and these queue on the tensor pipe side by side
         if (n > 0) {
             constexpr uint32_t idG = idesc_bf16(128, 64, false, true);
-            constexpr uint32_t idA = idesc_bf16(128, 16, false, true);
+            // the DA/16 aug sub-tiles (16 columns, 32-byte swizzle) lie 4 KiB apart:
+            // one MN-major operand of N = DA whose atoms the descriptor's
+            // leading byte offset (4 KiB) steps through
+            constexpr uint32_t idA = idesc_bf16(128, DA > 0 ? DA : 16, false, true);
             bool ok = true;
             for (int jj = 0; ok && jj < n; ++jj) {
                 const int st = jj % NST, b = jj & 1;
@@ -781,22 +799,25 @@ __global__ void __launch_bounds__(kThreads, 1) dq_kernel(const __grid_constant__
                 tc_fence_after();
                 const uint32_t sb = smem_u32(smem + L::STAGE0 + st * L::STAGE);
                 // dQ += dS K (+ dQaug += dS Kaug) over the tile's 128 kv rows
-#pragma unroll
-                for (int kk = 0; kk < 8; ++kk)
-                    mma_ts_w(tmem + ACC0, tmem + sbuf(b) + a_col(kk), mnmajor128_desc(sb + L::SK + kk * 2048), idG,
-                             (jj > 0 || kk > 0) ? 1u : 0u);
-#pragma unroll
-                for (int a = 0; a < NA; ++a)
+                if (lane == 0) {
 #pragma unroll
                     for (int kk = 0; kk < 8; ++kk)
-                        mma_ts_w(tmem + ACC1 + a * 16, tmem + sbuf(b) + a_col(kk),
-                                 mnmajor32_desc(sb + L::SKA + a * L::ATILE + kk * 512), idA, (jj > 0 || kk > 0) ? 1u : 0u);
-                tc_commit_w(&B.s_free[b]);
-                tc_commit_w(&B.empty[st]);
+                        mma_ts(tmem + ACC0, tmem + sbuf(b) + a_col(kk), mnmajor128_desc(sb + L::SK + kk * 2048), idG,
+                               (jj > 0 || kk > 0) ? 1u : 0u);
+                    if (NA > 0) {
+#pragma unroll
+                        for (int kk = 0; kk < 8; ++kk)
+                            mma_ts(tmem + ACC1, tmem + sbuf(b) + a_col(kk), mnmajor32_desc(sb + L::SKA + kk * 512), idA,
+                                   (jj > 0 || kk > 0) ? 1u : 0u);
+                    }
+                    tc_commit(&B.s_free[b]);
+                    tc_commit(&B.empty[st]);
+                }
+                __syncwarp();
             }
-            if (ok) tc_commit_w(&B.acc_done);
-            else cx.give_up();
-            tc_commit_w(&B.drain[1]);
+            if (ok && lane == 0) tc_commit(&B.acc_done);
+            if (!ok) cx.give_up();
+            if (lane == 0) tc_commit(&B.drain[1]);
             mbar_wait(&B.drain[1], 0, 500000000ull);
         }
     } else {

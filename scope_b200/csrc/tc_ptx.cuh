@@ -147,30 +147,11 @@ __device__ __forceinline__ void mma_ts(uint32_t d, uint32_t a, uint64_t b, uint3
         "r"(a), "l"(b), "r"(idesc), "r"(acc)
         : "memory");
 }
-// Warp-wide forms: the whole (converged) warp calls them with warp-uniform
-// operands and one elected lane issues the instruction, so the issuing warp's
-// waits and loop control stay warp-uniform (the same lane is elected every
-// time, so a commit covers the MMAs issued before it).
-__device__ __forceinline__ void tc_commit_w(uint64_t *bar) {
-    asm volatile(
-        "{\n\t.reg .pred e;\n\telect.sync _|e, 0xffffffff;\n\t"
-        "@e tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n\t}\n" ::"r"(smem_u32(bar))
-        : "memory");
-}
-__device__ __forceinline__ void mma_ss_w(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
-    asm volatile(
-        "{\n\t.reg .pred p, e;\n\telect.sync _|e, 0xffffffff;\n\tsetp.ne.b32 p, %4, 0;\n\t"
-        "@e tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(d),
-        "l"(a), "l"(b), "r"(idesc), "r"(acc)
-        : "memory");
-}
-__device__ __forceinline__ void mma_ts_w(uint32_t d, uint32_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
-    asm volatile(
-        "{\n\t.reg .pred p, e;\n\telect.sync _|e, 0xffffffff;\n\tsetp.ne.b32 p, %4, 0;\n\t"
-        "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}\n" ::"r"(d),
-        "r"(a), "l"(b), "r"(idesc), "r"(acc)
-        : "memory");
-}
+// Issuing: the whole issuing warp waits on its mbarriers (warp-uniform
+// control flow), then one lane issues a batch of MMAs and the commits that
+// track them, followed by __syncwarp().  (An elect.sync per instruction cost
+// the warps sharing the SM sub-partition ~5x more issue slots per MMA in a
+// measurement on B200.)
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 // After tcgen05.wait::ld: make the loaded registers opaque so no use of them
 // is scheduled above the wait (tcgen05.ld writes them asynchronously).
