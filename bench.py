@@ -36,7 +36,7 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
 from scope_b200 import PointerBlockMaskBuilder, SpectralScoreMod, flex_attention, trig_tables  # noqa: E402
-from scope_b200 import _lib  # noqa: E402
+from scope_b200 import _lib, shard  # noqa: E402
 from scope_b200.synth import BETA, CONFIGS, SCALE, make_inputs  # noqa: E402
 
 METRIC = "active-block attn TFLOP/s fwd+bwd at T=128k; tokens/s/GPU at 1/2/4/8 B200"
@@ -119,11 +119,9 @@ class Workload:
     """The per-rank inputs of one C3 layer (this rank's head shard)."""
 
     def __init__(self, cfg, rank, world, device, seed=0):
-        if cfg.H % world:
-            raise ValueError(f"H={cfg.H} heads do not split over {world} ranks")
+        self.heads = shard.head_slice(cfg.H, rank, world)
         hp = cfg.H // world
         self.cfg, self.rank, self.world, self.hp = cfg, rank, world, hp
-        self.heads = slice(rank * hp, (rank + 1) * hp)
         x = make_inputs(cfg, device=device, seed=seed, heads=self.heads)
         self.x = x
         self.cos_t, self.sin_t = trig_tables(x["omegas"], cfg.T)
@@ -139,8 +137,9 @@ class Workload:
                                              docs=x["docs"], budget_rep=x["budget_rep"],
                                              block_size=self.cfg.block_size)
 
-    def step(self, gather_out=None, gather_stats=None):
-        """mask build -> forward -> (async all-gather of outputs/stats) -> backward"""
+    def step(self, gather_out=None):
+        """mask build -> forward -> (async all-gather of the output heads, sum of the
+        pointer statistics over ranks) -> backward"""
         L = self.leaves
         for t in L.values():
             t.grad = None
@@ -150,10 +149,9 @@ class Workload:
         out = flex_attention(L["q"][None], L["k"][None], L["v"][None], bm, score_mod=sm, scale=SCALE)
         works = []
         if self.world > 1:
-            # outputs are [T, H/N, D] in memory per rank; gather head shards into [N, T, H/N, D]
-            works.append(dist.all_gather_into_tensor(gather_out, out[0].detach().permute(1, 0, 2).contiguous(),
-                                                     async_op=True))
-            works.append(dist.all_gather_into_tensor(gather_stats, bm.stats, async_op=True))
+            # out[0] is a [H/N, T, D] view of [T, H/N, D] storage: the gather takes it without a copy
+            works.append(shard.gather_heads(out[0].detach().transpose(0, 1), gather_out, async_op=True)[1])
+            works.append(shard.reduce_stats(bm.stats, async_op=True)[1])
         out.backward(self.x["do"][None])
         for w in works:
             w.wait()
@@ -210,7 +208,7 @@ def phase_times(wl, reps=3):
     return [a / reps for a in acc]
 
 
-def e2e_step(wl, host, dev):
+def e2e_step(wl, host, dev, gather_out=None):
     """The same step through the public API from pinned host buffers: H2D of
     every input, the step, D2H of the outputs and gradients."""
     for n, h in host["in"].items():
@@ -220,7 +218,7 @@ def e2e_step(wl, host, dev):
         L[n].data = dev[n]
     wl.x["do"] = dev["do"]
     wl.x["logits"], wl.x["gumbel"], wl.x["budget_rep"] = dev["logits"], dev["gumbel"], dev["budget_rep"]
-    bm, out = wl.step()
+    bm, out = wl.step(gather_out)
     host["out"]["out"].copy_(out[0], non_blocking=True)
     for n in ("q", "k", "v", "coeff_cos", "coeff_sin"):
         host["out"]["d" + n].copy_(L[n].grad, non_blocking=True)
@@ -228,9 +226,13 @@ def e2e_step(wl, host, dev):
 
 def cpu_reference(cfg, *, warmup=1, steps=3, heads=1, seconds_budget=60.0):
     """The reference's CPU path on a bounded sample: the numpy port of its
-    mask builder and torch's compiled CPU flex_attention on the qk_aug inputs
-    (forward; the reference raises NotImplementedError for a CPU backward).
-    Each step = build + one forward over ``heads`` heads of the config."""
+    mask builder, then the attention forward (the reference raises
+    NotImplementedError for a CPU backward) over ``heads`` heads of the config
+    on the qk_aug inputs -- torch's compiled CPU flex_attention, the kernel the
+    reference's flex_attention call runs on a CPU, or, where Inductor cannot
+    build that kernel on the host (it needs AVX-512 / AVX2 micro-GEMMs), the
+    oracle's block-sparse restatement of the same algorithm on every 4th q
+    block of the sample."""
     from oracle import mask_oracle as MO
     from oracle import attn_oracle as AO
     from torch.nn.attention.flex_attention import BlockMask, flex_attention as torch_flex
@@ -250,6 +252,8 @@ def cpu_reference(cfg, *, warmup=1, steps=3, heads=1, seconds_budget=60.0):
     qa, ka, va = AO.qk_aug_inputs(x["q"].float(), x["k"].float(), x["v"].float(), x["coeff_cos"], x["coeff_sin"],
                                   cos_t, sin_t, beta=BETA, scale=SCALE)
     fa = torch.compile(torch_flex, dynamic=False)
+    mode = {"kernel": "compiled"}
+    sample_rows = range(0, QB, 4)
 
     def one():
         t0 = time.perf_counter()
@@ -261,10 +265,20 @@ def cpu_reference(cfg, *, warmup=1, steps=3, heads=1, seconds_budget=60.0):
                                        budget_temp=cfg.budget_temp, with_transpose=False)
         kvi = torch.from_numpy(MO.flex_padded(m["kv_packed"], QB))[None]
         kvn = torch.from_numpy(m["kv_num"])[None]
-        bmk = BlockMask.from_kv_blocks(kvn, kvi, torch.zeros_like(kvn), torch.zeros_like(kvi), BLOCK_SIZE=bs,
-                                       mask_mod=document_causal)
-        fa(qa[None], ka[None], va[None], block_mask=bmk, scale=SCALE)
-        return time.perf_counter() - t0, int(m["kv_num"].sum())
+        t_build = time.perf_counter() - t0
+        if mode["kernel"] == "compiled":
+            try:
+                bmk = BlockMask.from_kv_blocks(kvn, kvi, torch.zeros_like(kvn), torch.zeros_like(kvi), BLOCK_SIZE=bs,
+                                               mask_mod=document_causal)
+                fa(qa[None], ka[None], va[None], block_mask=bmk, scale=SCALE)
+                return time.perf_counter() - t0, int(m["kv_num"].sum())
+            except Exception as e:  # Inductor could not build the CPU kernel on this host
+                mode["kernel"] = "oracle"
+                mode["why"] = f"{type(e).__name__}"
+                t0 = time.perf_counter() - t_build
+        _, pairs = AO.block_sparse_forward(qa, ka, va, kvn[0], kvi[0], docs, scale=SCALE, block_size=bs,
+                                           q_blocks=sample_rows)
+        return time.perf_counter() - t0, pairs
 
     for _ in range(max(1, warmup)):      # the first call compiles
         one()
@@ -277,10 +291,15 @@ def cpu_reference(cfg, *, warmup=1, steps=3, heads=1, seconds_budget=60.0):
             break
     sec = sum(times) / len(times)
     fwd_flops = 4 * bs * bs * 64 * P
+    if mode["kernel"] == "compiled":
+        what = "torch.compile'd CPU flex_attention"
+    else:
+        what = (f"the oracle's block-sparse fp32 forward on every 4th q block (the compiled CPU flex kernel "
+                f"failed to build here: {mode['why']})")
     return {"value": fwd_flops / sec / 1e12, "unit": "TFLOP/s", "cores": threads, "kind": "port",
             "sample": f"{cfg.name} with {heads} of {cfg.H} heads (T={T}), forward only (the reference has no CPU "
-                      f"backward): numpy port of the mask builder + torch.compile'd CPU flex_attention on the "
-                      f"qk_aug inputs, {len(times)} timed steps", "seconds_per_step": sec}
+                      f"backward): numpy port of the mask builder + {what} on the qk_aug inputs, "
+                      f"{len(times)} timed steps", "seconds_per_step": sec}
 
 
 def run_reference(args):
@@ -322,20 +341,18 @@ def main():
         import dataclasses
         cfg = dataclasses.replace(cfg, H=args.heads)
     wl = Workload(cfg, rank, world, "cuda")
-    gather_out = gather_stats = None
+    gather_out = None
     if world > 1:
-        gather_out = torch.empty(world, cfg.T, wl.hp, cfg.D, dtype=torch.bfloat16, device="cuda")
+        gather_out = shard.gather_buffer(cfg.T, cfg.H, cfg.D, world, torch.bfloat16, "cuda")
     bm0 = wl.build()
-    if world > 1:
-        gather_stats = torch.empty(world * bm0.stats.numel(), dtype=torch.int32, device="cuda")
     P_local = active_pairs(bm0)
     for _ in range(args.warmup):
-        wl.step(gather_out, gather_stats)
+        wl.step(gather_out)
     torch.cuda.synchronize()
     L = _lib.lib()
     n0 = L.scope_launch_count()
     with ClockSampler(local) as clk:
-        ms = time_steps(lambda: wl.step(gather_out, gather_stats), args.steps, world)
+        ms = time_steps(lambda: wl.step(gather_out), args.steps, world)
     launches = L.scope_launch_count() - n0
     P_t = torch.tensor([P_local], device="cuda", dtype=torch.int64)
     if world > 1:
@@ -378,10 +395,10 @@ def main():
         for n in ("coeff_cos", "coeff_sin"):
             host["out"]["d" + n] = torch.empty_like(wl.x[n], device="cpu").pin_memory()
         for _ in range(2):
-            e2e_step(wl, host, dev)
+            e2e_step(wl, host, dev, gather_out)
         torch.cuda.synchronize()
         e_steps = max(2, args.steps // 2)
-        ms_e = time_steps(lambda: e2e_step(wl, host, dev), e_steps, world)
+        ms_e = time_steps(lambda: e2e_step(wl, host, dev, gather_out), e_steps, world)
         h2d = sum(t.numel() * t.element_size() for t in host["in"].values())
         d2h = sum(t.numel() * t.element_size() for t in host["out"].values())
         e2e = {"value": flops / (ms_e / e_steps * 1e-3) / 1e12, "unit": "TFLOP/s",

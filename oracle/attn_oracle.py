@@ -234,3 +234,44 @@ def qk_aug_grads(q, k, v, do, mask, *, scale, beta, coeff_cos, coeff_sin, cos_ta
     if sl is not None:
         res["dslope"] = sl.grad
     return res
+
+
+def block_sparse_forward(q, k, v, kv_num, kv_idx, docs, *, scale: float, block_size: int = 128,
+                         q_blocks=None):
+    """Block-sparse forward at full sequence length, fp32 on the CPU: what
+    flex_attention computes for a BlockMask whose listed blocks are all partial
+    (document-causal mask_mod, model/attn_bias.py:674-679), one q block at a
+    time over the gathered keys of its list.  Used as the timed CPU baseline
+    where torch's compiled CPU flex kernel cannot be built (Inductor's CPU
+    template needs AVX-512 / AVX2 micro-GEMMs); results agree with `attention`.
+
+    q, k: [H, T, Dqk]; v: [H, T, Dv]; kv_num [H, QB]; kv_idx [H, QB, W];
+    docs [T].  q_blocks: optional iterable of q block indices (a bounded
+    sample); returns (out [H, T, Dv] fp32, zero outside the sample, and the
+    number of (q block, kv block) pairs processed)."""
+    H, T, _ = q.shape
+    bs = block_size
+    QB = T // bs
+    qf, kf, vf = q.float(), k.float(), v.float()
+    docs = docs.long()
+    out = torch.zeros(H, T, v.shape[-1], dtype=torch.float32)
+    pairs = 0
+    rows = range(QB) if q_blocks is None else q_blocks
+    for h in range(H):
+        for qb in rows:
+            n = int(kv_num[h, qb])
+            if n == 0:
+                continue
+            blocks = kv_idx[h, qb, :n].long()
+            pairs += n
+            cols = (blocks[:, None] * bs + torch.arange(bs)[None, :]).reshape(-1)
+            i = torch.arange(qb * bs, (qb + 1) * bs)
+            s = (qf[h, i] @ kf[h, cols].T) * scale
+            vis = (i[:, None] >= cols[None, :]) & (docs[i][:, None] == docs[cols][None, :])
+            s = s.masked_fill(~vis, float("-inf"))
+            m = s.amax(dim=-1, keepdim=True)
+            m = torch.where(torch.isfinite(m), m, torch.zeros_like(m))
+            p = torch.exp(s - m)
+            l = p.sum(dim=-1, keepdim=True)
+            out[h, i] = (p @ vf[h, cols]) / torch.where(l > 0, l, torch.ones_like(l))
+    return out, pairs

@@ -145,3 +145,28 @@ def test_qk_aug_equals_score_mod_up_to_rounding():
     g = AO.qk_aug_grads(x["q"], x["k"], x["v"], torch.zeros_like(x["q"]), mask, scale=0.12, beta=0.5,
                         coeff_cos=x["coeff_cos"], coeff_sin=x["coeff_sin"], cos_tab=cos_t, sin_tab=sin_t)
     assert (a - g["out"]).abs().max().item() < 5e-3
+
+
+def test_block_sparse_forward_matches_dense_oracle():
+    """The full-length block-sparse CPU forward (the timed CPU baseline) is the
+    same function as the dense oracle on a small case."""
+    from oracle import attn_oracle as AO
+    g = torch.Generator().manual_seed(3)
+    H, T, bs = 2, 1024, 128
+    QB = T // bs
+    q, k = torch.randn(H, T, 96, generator=g), torch.randn(H, T, 96, generator=g)
+    v = torch.randn(H, T, 64, generator=g)
+    docs = torch.zeros(T, dtype=torch.int32)
+    docs[300:] = 1
+    docs[700:] = 2
+    kvn = torch.zeros(H, QB, dtype=torch.int32)
+    kvi = torch.zeros(H, QB, QB, dtype=torch.int32)
+    for h in range(H):
+        for qb in range(QB):
+            bl = sorted({qb, max(0, qb - 1), 0, (qb * (h + 1)) // 3})
+            kvn[h, qb] = len(bl)
+            kvi[h, qb, :len(bl)] = torch.tensor(bl)
+    out, pairs = AO.block_sparse_forward(q, k, v, kvn, kvi, docs, scale=0.12, block_size=bs)
+    ref, _ = AO.attention(q, k, v, AO.dense_mask(kvn, kvi, T, bs, docs=docs), scale=0.12)
+    assert pairs == int(kvn.sum())
+    assert (out.double() - ref).abs().max().item() < 1e-5
