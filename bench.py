@@ -208,20 +208,80 @@ def phase_times(wl, reps=3):
     return [a / reps for a in acc]
 
 
-def e2e_step(wl, host, dev, gather_out=None):
-    """The same step through the public API from pinned host buffers: H2D of
-    every input, the step, D2H of the outputs and gradients."""
-    for n, h in host["in"].items():
-        dev[n].copy_(h, non_blocking=True)
-    L = wl.leaves
-    for n in ("q", "k", "v", "coeff_cos", "coeff_sin"):
-        L[n].data = dev[n]
-    wl.x["do"] = dev["do"]
-    wl.x["logits"], wl.x["gumbel"], wl.x["budget_rep"] = dev["logits"], dev["gumbel"], dev["budget_rep"]
-    bm, out = wl.step(gather_out)
-    host["out"]["out"].copy_(out[0], non_blocking=True)
-    for n in ("q", "k", "v", "coeff_cos", "coeff_sin"):
-        host["out"]["d" + n].copy_(L[n].grad, non_blocking=True)
+class E2EPipeline:
+    """The step through the public API from pinned host buffers, every step:
+    H2D of all of its inputs, the step, D2H of its output and gradients.
+    Copies run on their own streams so that the inputs of step i+1 travel
+    while step i computes and the results of step i travel back while step
+    i+1 computes (PCIe carries H2D and D2H at the same time); the device
+    inputs are double buffered."""
+
+    IN = ("q", "k", "v", "do", "coeff_cos", "coeff_sin", "logits", "gumbel", "budget_rep")
+
+    def __init__(self, wl, host, gather_out=None):
+        self.wl, self.host, self.gather_out = wl, host, gather_out
+        self.dev = [{n: wl.x[n].detach().clone() for n in self.IN} for _ in range(2)]
+        self.s_h2d, self.s_d2h = torch.cuda.Stream(), torch.cuda.Stream()
+        self.free = [None, None]        # compute done with a slot's inputs
+        self.i = 0
+
+    def start(self, ev0):
+        self.s_h2d.wait_event(ev0)
+
+    def step(self):
+        k = self.i % 2
+        cur = torch.cuda.current_stream()
+        dev = self.dev[k]
+        if self.free[k] is not None:
+            self.s_h2d.wait_event(self.free[k])
+        with torch.cuda.stream(self.s_h2d):
+            for n, h in self.host["in"].items():
+                dev[n].copy_(h, non_blocking=True)
+        cur.wait_stream(self.s_h2d)
+        wl, L = self.wl, self.wl.leaves
+        for n in ("q", "k", "v", "coeff_cos", "coeff_sin"):
+            L[n].data = dev[n]
+        wl.x["do"] = dev["do"]
+        wl.x["logits"], wl.x["gumbel"], wl.x["budget_rep"] = dev["logits"], dev["gumbel"], dev["budget_rep"]
+        bm, out = wl.step(self.gather_out)
+        self.free[k] = cur.record_event()
+        self.s_d2h.wait_stream(cur)
+        res = [("out", out[0].detach())] + [("d" + n, L[n].grad) for n in ("q", "k", "v", "coeff_cos", "coeff_sin")]
+        with torch.cuda.stream(self.s_d2h):
+            for n, t in res:
+                t.record_stream(self.s_d2h)
+                self.host["out"][n].copy_(t, non_blocking=True)
+        self.i += 1
+
+    def finish(self):
+        cur = torch.cuda.current_stream()
+        cur.wait_stream(self.s_h2d)
+        cur.wait_stream(self.s_d2h)
+
+
+def time_e2e(pipe, steps, world):
+    """Device time of `steps` pipelined end-to-end steps: from an event before
+    the first H2D to one after the last D2H, max over ranks."""
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    s = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(s)
+    pipe.start(e0)
+    for _ in range(steps):
+        pipe.step()
+    pipe.finish()
+    e1.record(s)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1)
+    if world > 1:
+        t = torch.tensor([ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = t.item()
+        dist.barrier()
+    return ms
 
 
 def cpu_reference(cfg, *, warmup=1, steps=3, heads=1, seconds_budget=60.0):
@@ -382,23 +442,31 @@ def main():
                 "achieved": ach, "peak": bf16, "unit": "TFLOP/s"}
     roof["frac"] = roof["achieved"] / roof["peak"]
     roof["peak_source"] = f"{src} (MEASURED_PEAKS.json burst)" if src == "measured" else "fallback"
-    roof["traffic"] = None
+    # DRAM bytes (read + write) per active block pair from one ncu capture of the
+    # full C3 step (profiles/c3_step_launch_list.md), scaled to this launch's pairs
+    if dom == 0:
+        roof["traffic"] = 0.073e9 * wl.hp / 16           # mask::build_kernel, per head
+    else:
+        per_pair = 1.693e9 / 238859 if dom == 1 else (0.559e9 + 3.120e9 + 2.596e9) / 238859
+        roof["traffic"] = per_pair * P_local
+    roof["traffic_unit"] = "bytes per launch"
+    roof["traffic_source"] = "ncu dram__bytes_read.sum + dram__bytes_write.sum of the C3 step, scaled to this launch"
 
     e2e = None
     if not args.no_e2e:
-        names_in = ("q", "k", "v", "do", "coeff_cos", "coeff_sin", "logits", "gumbel", "budget_rep")
-        dev = {n: wl.x[n].detach().clone() for n in names_in}
-        host = {"in": {n: dev[n].cpu().pin_memory() for n in names_in},
+        host = {"in": {n: wl.x[n].detach().cpu().pin_memory() for n in E2EPipeline.IN},
                 "out": {"out": torch.empty(cfg.T, wl.hp, D, dtype=torch.bfloat16).pin_memory().permute(1, 0, 2)}}
         for n in ("q", "k", "v"):
             host["out"]["d" + n] = torch.empty(cfg.T, wl.hp, D, dtype=torch.bfloat16).pin_memory().permute(1, 0, 2)
         for n in ("coeff_cos", "coeff_sin"):
             host["out"]["d" + n] = torch.empty_like(wl.x[n], device="cpu").pin_memory()
+        pipe = E2EPipeline(wl, host, gather_out)
         for _ in range(2):
-            e2e_step(wl, host, dev, gather_out)
+            pipe.step()
+        pipe.finish()
         torch.cuda.synchronize()
-        e_steps = max(2, args.steps // 2)
-        ms_e = time_steps(lambda: e2e_step(wl, host, dev, gather_out), e_steps, world)
+        e_steps = max(3, args.steps // 2)
+        ms_e = time_e2e(pipe, e_steps, world)
         h2d = sum(t.numel() * t.element_size() for t in host["in"].values())
         d2h = sum(t.numel() * t.element_size() for t in host["out"].values())
         e2e = {"value": flops / (ms_e / e_steps * 1e-3) / 1e12, "unit": "TFLOP/s",
