@@ -129,6 +129,20 @@ int scope_mask_build(const ScopeMaskArgs *args, scope_stream_t stream);
 int scope_mask_transpose(const uint32_t *q_bitmap, int32_t H, int32_t QB,
                          int32_t *q_num, int32_t *q_indices, scope_stream_t stream);
 
+/* Kernel tiles of a coarse mask (block_size 2*bs -> bs; the attention kernels
+ * tile at 128, config C5 builds its mask at 256).  No counterpart function in
+ * the reference: torch's flex kernel likewise runs a BLOCK_SIZE-256 mask on
+ * smaller tiles internally (SPARSE_Q/KV_BLOCK_SIZE multiples of its BLOCK_M /
+ * BLOCK_N, torch/_inductor/kernel/flex/templates/flex_attention.py.jinja:32-33).  Fine q block 2qb+s gets fine
+ * kv blocks 2kb, 2kb+1 of each listed kb, minus those wholly in its causal
+ * future; out lists [H, 2QB, kv_stride_out >= 2*kv_stride]; the caller zeroes
+ * q_bitmap_out [H, 2QB, ceil(2QB/32)].  Bad indices are skipped and set
+ * SCOPE_DEVERR_INDEX in err_flag (may be NULL). */
+int scope_mask_refine(const int32_t *kv_num, const int32_t *kv_indices, int32_t H, int32_t QB,
+                      int32_t kv_stride, int32_t *kv_num_out, int32_t *kv_indices_out,
+                      int32_t kv_stride_out, uint32_t *q_bitmap_out, int32_t *err_flag,
+                      scope_stream_t stream);
+
 /* ------------------------------------------------------------------------ */
 /* 2. spectral bias helpers                                                   */
 /* ------------------------------------------------------------------------ */

@@ -84,6 +84,7 @@ SIGNATURES = {
     "scope_mask_max_kv": (I32, [I32, I32, I32, I32]),
     "scope_mask_build": (I32, [ctypes.POINTER(ScopeMaskArgs), P]),
     "scope_mask_transpose": (I32, [P, I32, I32, P, P, P]),
+    "scope_mask_refine": (I32, [P, P, I32, I32, I32, P, P, I32, P, P, P]),
     "scope_trig_tables": (I32, [P, I32, I32, P, P, P]),
     "scope_qk_aug_prepare": (I32, [P, P, P, P, P, I32, I32, I32, I32, I32, F32, F32, I32, P, P, P]),
     "scope_attn_fwd": (I32, [ctypes.POINTER(ScopeAttnArgs), P]),

@@ -306,6 +306,8 @@ def flex_attention(query: Tensor, key: Tensor, value: Tensor, block_mask: ScopeB
     q, k, v = (_hd(t, 3) for t in (query, key, value))
     D = q.shape[-1]
     sc = float(scale) if scale is not None else 1.0 / math.sqrt(D)
+    if block_mask.BLOCK_SIZE[0] > 128:
+        block_mask = block_mask.kernel_tiles(128)    # e.g. a block-size-256 mask (config C5)
     bs = block_mask.BLOCK_SIZE[0]
     kv_num = block_mask.kv_num_blocks[0]
     kv_idx = block_mask.kv_indices[0]

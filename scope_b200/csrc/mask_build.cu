@@ -549,3 +549,55 @@ extern "C" int scope_mask_transpose(const uint32_t *q_bitmap, int32_t H, int32_t
     SCOPE_CHECK_LAUNCH();
     return SCOPE_OK;
 }
+
+// ---------------------------------------------------------------------------
+// Kernel tiles of a coarse mask: block_size 2*bs -> bs.  Fine q block
+// q' = 2*qb + s sees fine kv blocks 2*kb and 2*kb + 1 of every coarse kb in
+// its coarse row, minus those wholly in its causal future (fine kv block >
+// q', where every key follows every query); order stays ascending.  The
+// element mask (document-causal) is applied inside the tiles as before.
+namespace scope {
+namespace mask {
+__global__ void refine_kernel(const int32_t *__restrict__ kv_num, const int32_t *__restrict__ kv_idx, int H, int QB,
+                              int kv_stride, int32_t *__restrict__ kv_num_out, int32_t *__restrict__ kv_idx_out,
+                              int kv_stride_out, uint32_t *__restrict__ q_bitmap_out, int32_t *err) {
+    const int row = blockIdx.x * blockDim.x + threadIdx.x;   // (h, fine q block)
+    const int QF = 2 * QB;
+    if (row >= H * QF) return;
+    const int h = row / QF, qf = row - h * QF, qb = qf >> 1;
+    const int words = (QF + 31) / 32;
+    const int32_t *src = kv_idx + ((int64_t)h * QB + qb) * kv_stride;
+    int32_t *dst = kv_idx_out + (int64_t)row * kv_stride_out;
+    const int n = kv_num[(int64_t)h * QB + qb];
+    int m = 0;
+    for (int e = 0; e < n; ++e) {
+        const int kb = src[e];
+        if (kb < 0 || kb >= QB) {          // skipped, as the attention kernels would
+            set_err(err, SCOPE_DEVERR_INDEX);
+            continue;
+        }
+        for (int t = 0; t < 2; ++t) {
+            const int kf = 2 * kb + t;
+            if (kf > qf) break;
+            dst[m++] = kf;
+            atomicOr(q_bitmap_out + ((int64_t)h * QF + kf) * words + (qf >> 5), 1u << (qf & 31));
+        }
+    }
+    kv_num_out[row] = m;
+}
+}  // namespace mask
+}  // namespace scope
+
+extern "C" int scope_mask_refine(const int32_t *kv_num, const int32_t *kv_indices, int32_t H, int32_t QB,
+                                 int32_t kv_stride, int32_t *kv_num_out, int32_t *kv_indices_out,
+                                 int32_t kv_stride_out, uint32_t *q_bitmap_out, int32_t *err_flag,
+                                 scope_stream_t stream) {
+    if (!kv_num || !kv_indices || !kv_num_out || !kv_indices_out || !q_bitmap_out || H <= 0 || QB <= 0 ||
+        kv_stride <= 0 || kv_stride_out < 2 * kv_stride)
+        return SCOPE_ERR_INVALID;
+    const int rows = H * 2 * QB;
+    scope::mask::refine_kernel<<<ceil_div(rows, 256), 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+        kv_num, kv_indices, H, QB, kv_stride, kv_num_out, kv_indices_out, kv_stride_out, q_bitmap_out, err_flag);
+    SCOPE_CHECK_LAUNCH();
+    return SCOPE_OK;
+}

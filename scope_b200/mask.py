@@ -49,6 +49,7 @@ class ScopeBlockMask:
     max_kv: int = 0
     stats_layout: tuple = ()
     _q_cache: tuple | None = field(default=None, repr=False)
+    _tiles: "ScopeBlockMask | None" = field(default=None, repr=False)
 
     @property
     def num_heads(self) -> int:
@@ -79,6 +80,36 @@ class ScopeBlockMask:
     @property
     def q_indices(self):
         return self.q_lists(True)[1]
+
+    def kernel_tiles(self, tile: int = 128) -> "ScopeBlockMask":
+        """The same visibility on `tile`-row blocks, the tile the attention
+        kernels run: a mask built at block_size 2*tile (config C5 builds at
+        256) is refined by one kernel launch (fine lists, q-side bitmap,
+        block_info at the fine block size); a mask already at `tile` is
+        returned as is."""
+        bs = self.BLOCK_SIZE[0]
+        if bs == tile:
+            return self
+        if bs != 2 * tile:
+            raise ValueError(f"block size {bs}: the kernels tile at {tile} (block sizes {tile} and {2 * tile})")
+        if self._tiles is None:
+            H, QB = self.num_heads, self.num_q_blocks
+            T = self.seq_lengths[0]
+            dev = self.kv_num_blocks.device
+            QF = 2 * QB
+            kvi = self.kv_indices[0]
+            w = 2 * kvi.shape[-1]
+            kv_num = torch.empty(1, H, QF, dtype=torch.int32, device=dev)
+            kv_idx = torch.zeros(1, H, QF, w, dtype=torch.int32, device=dev)
+            qbm = torch.zeros(H, QF, (QF + 31) // 32, dtype=torch.int32, device=dev)
+            st = _lib.lib().scope_mask_refine(self.kv_num_blocks.data_ptr(), kvi.data_ptr(), H, QB, kvi.shape[-1],
+                                              kv_num.data_ptr(), kv_idx.data_ptr(), w, qbm.data_ptr(),
+                                              _lib.err_word_ptr(dev), _stream(dev))
+            _lib.check(st, "scope_mask_refine")
+            info = block_info(self.docs, T, tile, device=dev)
+            self._tiles = ScopeBlockMask(kv_num, kv_idx, qbm, info, (tile, tile), self.seq_lengths, docs=self.docs,
+                                         max_kv=2 * self.max_kv)
+        return self._tiles
 
     def pointer_stats(self) -> dict:
         """The reference's pointer statistics (model/attn_bias.py:839-849):
