@@ -147,6 +147,7 @@ __global__ void __launch_bounds__(kThreads, 2) fwd_kernel(const __grid_constant_
         tmem_alloc(tmem_slot, kTmemCols);
         tmem_relinquish();
     }
+    __syncwarp();   // every warp reaches the CTA barrier converged (the producer ran on lane 0 alone)
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
@@ -226,7 +227,9 @@ __global__ void __launch_bounds__(kThreads, 2) fwd_kernel(const __grid_constant_
                         mma_ss(tS, kmajor_desc(sq + L::QA + a * L::ATILE, 32), kmajor_desc(sk + L::KA + a * L::ATILE, 32),
                                idS, 1);
                     tc_commit(s_full);
-                    tc_commit(kv_empty + s);   // K of this stage may be reloaded once S is done
+                    // K of this stage may be reloaded once S is done; commit only arrivals
+                    // someone waits for (one still in flight at CTA exit delays the TMEM release)
+                    if (j + 2 < n) tc_commit(kv_empty + s);
                 }
                 __syncwarp();
                 return true;
@@ -246,7 +249,7 @@ __global__ void __launch_bounds__(kThreads, 2) fwd_kernel(const __grid_constant_
                     for (int kk = 0; kk < BM / 16; ++kk)
                         mma_ts(tO, tP + kk * 8, mnmajor128_desc(sv + kk * 2048), idO, (j > 0 || kk > 0) ? 1u : 0u);
                     tc_commit(o_done);
-                    tc_commit(v_empty + (j & 1));
+                    if (j + 2 < n) tc_commit(v_empty + (j & 1));
                 }
                 __syncwarp();
             }
@@ -393,6 +396,7 @@ __global__ void __launch_bounds__(kThreads, 2) fwd_kernel(const __grid_constant_
         if (p.lse && ch == 0)
             p.lse[(int64_t)h * p.T + i] = (ltot > 0.f) ? (m + log2f(ltot)) * 0.69314718055994531f : -INFINITY;
     }
+    __syncwarp();   // every warp reaches the CTA barrier converged (the producer ran on lane 0 alone)
     tc_fence_before();
     __syncthreads();
     if (warp == 1) {

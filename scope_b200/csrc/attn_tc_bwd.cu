@@ -358,6 +358,7 @@ __global__ void __launch_bounds__(kThreads, 1) dkv_kernel(const __grid_constant_
         tmem_alloc(&B.tmem_slot, kTmemCols);
         tmem_relinquish();
     }
+    __syncwarp();   // every warp reaches the CTA barrier converged (the producer ran on lane 0 alone)
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
@@ -464,8 +465,9 @@ __global__ void __launch_bounds__(kThreads, 1) dkv_kernel(const __grid_constant_
                     for (int kk = 0; kk < 8; ++kk)
                         mma_ts(tmem + ACC1, tmem + sbuf(b) + a_col(kk) + 32, mnmajor128_desc(sb + L::SQ + kk * 2048), idG,
                                (t > 0 || kk > 0) ? 1u : 0u);
-                    tc_commit(&B.s_free[b]);
-                    tc_commit(&B.empty[st]);
+                    // commit only arrivals someone waits for
+                    if (t + 2 < nq) tc_commit(&B.s_free[b]);
+                    if (t + NST < nq) tc_commit(&B.empty[st]);
                 }
                 __syncwarp();
             }
@@ -570,6 +572,7 @@ __global__ void __launch_bounds__(kThreads, 1) dkv_kernel(const __grid_constant_
             }
         }
     }
+    __syncwarp();   // every warp reaches the CTA barrier converged (the producer ran on lane 0 alone)
     tc_fence_before();
     __syncthreads();
     if (warp == 1) {
@@ -706,6 +709,7 @@ __global__ void __launch_bounds__(kThreads, 1) dq_kernel(const __grid_constant__
         tmem_alloc(&B.tmem_slot, kTmemCols);
         tmem_relinquish();
     }
+    __syncwarp();   // every warp reaches the CTA barrier converged (the producer ran on lane 0 alone)
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
@@ -810,8 +814,8 @@ __global__ void __launch_bounds__(kThreads, 1) dq_kernel(const __grid_constant__
                             mma_ts(tmem + ACC1, tmem + sbuf(b) + a_col(kk), mnmajor32_desc(sb + L::SKA + kk * 512), idA,
                                    (jj > 0 || kk > 0) ? 1u : 0u);
                     }
-                    tc_commit(&B.s_free[b]);
-                    tc_commit(&B.empty[st]);
+                    if (jj + 2 < n) tc_commit(&B.s_free[b]);     // only arrivals someone waits for
+                    if (jj + NST < n) tc_commit(&B.empty[st]);
                 }
                 __syncwarp();
             }
@@ -885,40 +889,73 @@ __global__ void __launch_bounds__(kThreads, 1) dq_kernel(const __grid_constant__
         store_row32(tmem + lb + ACC0 + ch * 32, p.scale,
                     p.g0 + (int64_t)h * p.g0_sh + (int64_t)i * p.g0_st + ch * 32, have);
         if (NA > 0 && p.dcoeff_cos) {
+            // gradient of the augmented dims -> coefficients (q_aug = s [A c + B s', A s' - B c, -slope]);
+            // the two warps of a quadrant split the K coefficients
             if (ch == 1) slope_part[r] = gsl;
-            elem_bar();
-            if (ch == 0) {
-                // gradient of the augmented dims -> coefficients (q_aug = s [A c + B s', A s' - B c, -slope])
-                float ga[DA > 0 ? DA : 1];
+            const int K = p.K;
+            const int kh = (K + 1) >> 1;
+            const int k0 = ch == 0 ? 0 : kh, nk = ch == 0 ? kh : K - kh;
+            constexpr int KM = DA > 0 ? DA / 2 : 1;     // K <= DA / 2
+            float cv[KM], sv[KM];
 #pragma unroll
-                for (int a = 0; a < NA; ++a) {
-                    uint32_t o[16];
-                    if (have) {
-                        tmem_ld16(tmem + lb + ACC1 + a * 16, o);
-                        tmem_wait_ld();
-                        pin(o);
-                    } else {
-#pragma unroll
-                        for (int e = 0; e < 16; ++e) o[e] = 0u;
-                    }
-#pragma unroll
-                    for (int e = 0; e < 16; ++e) ga[a * 16 + e] = __uint_as_float(o[e]) * p.scale;
+            for (int e = 0; e < KM; ++e) {              // independent table loads, issued together
+                if (e < nk) {
+                    cv[e] = bf16_to_f32(p.cos_tab[(int64_t)(k0 + e) * p.tab_len + i]);
+                    sv[e] = bf16_to_f32(p.sin_tab[(int64_t)(k0 + e) * p.tab_len + i]);
                 }
-                const int K = p.K;
-#pragma unroll
-                for (int k = 0; k < DA / 2; ++k) {
-                    if (k < K) {
-                        const float cv = bf16_to_f32(p.cos_tab[(int64_t)k * p.tab_len + i]);
-                        const float sv = bf16_to_f32(p.sin_tab[(int64_t)k * p.tab_len + i]);
-                        const float g0 = ga[k], g1 = ga[(K + k) < DA ? (K + k) : 0];
-                        p.dcoeff_cos[hrow * K + k] = p.s_aug * (g0 * cv + g1 * sv);
-                        p.dcoeff_sin[hrow * K + k] = p.s_aug * (g0 * sv - g1 * cv);
-                    }
-                }
-                if (slope_acc) p.dslope[hrow] = -p.s_aug * ((gsl + slope_part[r]) * p.scale);
             }
+            // this thread's aug-gradient row goes through shared memory (indexed by the
+            // runtime K); the stage ring is idle once every MMA has completed
+            float *grow = reinterpret_cast<float *>(smem + L::STAGE0) + (size_t)(ch * BM + r) * (DA > 0 ? DA : 1);
+#pragma unroll
+            for (int a = 0; a < NA; ++a) {
+                uint32_t o[16];
+                if (have) {
+                    tmem_ld16(tmem + lb + ACC1 + a * 16, o);
+                    tmem_wait_ld();
+                    pin(o);
+                } else {
+#pragma unroll
+                    for (int e = 0; e < 16; ++e) o[e] = 0u;
+                }
+#pragma unroll
+                for (int e = 0; e < 16; e += 4)
+                    *reinterpret_cast<float4 *>(grow + a * 16 + e) =
+                        make_float4(__uint_as_float(o[e]) * p.scale, __uint_as_float(o[e + 1]) * p.scale,
+                                    __uint_as_float(o[e + 2]) * p.scale, __uint_as_float(o[e + 3]) * p.scale);
+            }
+            float dc[KM], ds[KM];
+#pragma unroll
+            for (int e = 0; e < KM; ++e) {
+                if (e < nk) {
+                    const float g0 = grow[k0 + e], g1 = grow[K + k0 + e];
+                    dc[e] = p.s_aug * (g0 * cv[e] + g1 * sv[e]);
+                    ds[e] = p.s_aug * (g0 * sv[e] - g1 * cv[e]);
+                }
+            }
+            float *oc = p.dcoeff_cos + hrow * K + k0, *os = p.dcoeff_sin + hrow * K + k0;
+            if (((K | k0 | nk) & 3) == 0) {
+#pragma unroll
+                for (int e = 0; e < KM; e += 4) {
+                    if (e < nk) {
+                        *reinterpret_cast<float4 *>(oc + e) = make_float4(dc[e], dc[e + 1], dc[e + 2], dc[e + 3]);
+                        *reinterpret_cast<float4 *>(os + e) = make_float4(ds[e], ds[e + 1], ds[e + 2], ds[e + 3]);
+                    }
+                }
+            } else {
+#pragma unroll
+                for (int e = 0; e < KM; ++e) {
+                    if (e < nk) {
+                        oc[e] = dc[e];
+                        os[e] = ds[e];
+                    }
+                }
+            }
+            elem_bar();
+            if (ch == 0 && slope_acc) p.dslope[hrow] = -p.s_aug * ((gsl + slope_part[r]) * p.scale);
         }
     }
+    __syncwarp();   // every warp reaches the CTA barrier converged (the producer ran on lane 0 alone)
     tc_fence_before();
     __syncthreads();
     if (warp == 1) {
