@@ -113,7 +113,7 @@ struct Params {
     __nv_bfloat16 *g0, *g1;           // dkv: dK, dV      dq: dQ, (unused)
     int64_t g0_sh, g0_st, g1_sh, g1_st;
     // dq epilogue for the qk_aug bias
-    int K, has_slope, tab_len;
+    int K, has_slope, tab_len, tab_smem;   // tab_smem: table rows 16-byte aligned, staged by the producer
     const uint16_t *cos_tab, *sin_tab;
     float s_aug;
     float *dcoeff_cos, *dcoeff_sin, *dslope;
@@ -680,11 +680,15 @@ struct QL {
     static constexpr uint32_t STAGE0 = DO + TILE;
     static constexpr uint32_t SK = 0, SKA = TILE, SV = align1k(TILE + NA * ATILE);
     static constexpr uint32_t STAGE = SV + TILE;
-    static constexpr int NST = STAGE0 + 4 * STAGE + 2048 <= kSmemBudget ? 4 : 3;
+    // barriers, slope partials and the table rows after the ring; 1 KiB for the alignment of the base
+    static constexpr uint32_t EXTRA = 1024 + 512 + (DA > 0 ? DA : 1) * 256 + 1024;
+    static constexpr int NST = STAGE0 + 4 * STAGE + EXTRA + 1024 <= kSmemBudget ? 4 : 3;
     static constexpr uint32_t BAR = STAGE0 + NST * STAGE;
     static constexpr uint32_t RES_BYTES = 2 * TILE + NA * ATILE;
     static constexpr uint32_t SLOPE = align1k(BAR + sizeof(Bars));   // float[128]: slope partials of column half 1
-    static constexpr uint32_t TOTAL = SLOPE + 512;
+    // the q block's rows of the cos / sin tables (bf16 [DA/2][128] each) for the coefficient epilogue
+    static constexpr uint32_t TAB = SLOPE + 512;
+    static constexpr uint32_t TOTAL = TAB + (DA > 0 ? DA : 1) * 256;
     static constexpr uint32_t KV_BYTES = 2 * TILE + NA * ATILE;
 };
 
@@ -718,7 +722,15 @@ __global__ void __launch_bounds__(kThreads, 1) dq_kernel(const __grid_constant__
     if (warp == 0) {
         // ---------------- producer: Q / dO once, then the kv tiles of this q block's list, in order
         if (lane == 0 && n > 0) {
-            mbar_expect_tx(&B.res_full, L::RES_BYTES);
+            const bool tab = NA > 0 && p.dcoeff_cos && p.tab_smem;
+            mbar_expect_tx(&B.res_full, L::RES_BYTES + (tab ? 2u * p.K * 256u : 0u));
+            if (tab) {
+                for (int k = 0; k < p.K; ++k) {
+                    bulk_load(smem + L::TAB + k * 256, p.cos_tab + (int64_t)k * p.tab_len + qb * BM, 256, &B.res_full);
+                    bulk_load(smem + L::TAB + (DA / 2 + k) * 256, p.sin_tab + (int64_t)k * p.tab_len + qb * BM, 256,
+                              &B.res_full);
+                }
+            }
             tma_load_3d(&maps.q, smem + L::Q, &B.res_full, 0, qb * BM, h);
 #pragma unroll
             for (int a = 0; a < NA; ++a)
@@ -897,16 +909,30 @@ __global__ void __launch_bounds__(kThreads, 1) dq_kernel(const __grid_constant__
             const int k0 = ch == 0 ? 0 : kh, nk = ch == 0 ? kh : K - kh;
             constexpr int KM = DA > 0 ? DA / 2 : 1;     // K <= DA / 2
             float cv[KM], sv[KM];
+            if (p.tab_smem) {
+                // the producer staged this q block's table rows with the resident tiles
+                const bool ok = cx.waitw(&B.res_full, 0);
+                const uint16_t *tc = reinterpret_cast<const uint16_t *>(smem + L::TAB);
 #pragma unroll
-            for (int e = 0; e < KM; ++e) {              // independent table loads, issued together
-                if (e < nk) {
-                    cv[e] = bf16_to_f32(p.cos_tab[(int64_t)(k0 + e) * p.tab_len + i]);
-                    sv[e] = bf16_to_f32(p.sin_tab[(int64_t)(k0 + e) * p.tab_len + i]);
+                for (int e = 0; e < KM; ++e) {
+                    if (e < nk) {
+                        cv[e] = ok ? bf16_to_f32(tc[(k0 + e) * BM + r]) : 0.f;
+                        sv[e] = ok ? bf16_to_f32(tc[(KM + k0 + e) * BM + r]) : 0.f;
+                    }
+                }
+            } else {
+#pragma unroll
+                for (int e = 0; e < KM; ++e) {          // independent table loads, issued together
+                    if (e < nk) {
+                        cv[e] = bf16_to_f32(p.cos_tab[(int64_t)(k0 + e) * p.tab_len + i]);
+                        sv[e] = bf16_to_f32(p.sin_tab[(int64_t)(k0 + e) * p.tab_len + i]);
+                    }
                 }
             }
             // this thread's aug-gradient row goes through shared memory (indexed by the
-            // runtime K); the stage ring is idle once every MMA has completed
-            float *grow = reinterpret_cast<float *>(smem + L::STAGE0) + (size_t)(ch * BM + r) * (DA > 0 ? DA : 1);
+            // runtime K), column-major so a warp's accesses hit distinct banks; the
+            // stage ring is idle once every MMA has completed
+            float *grow = reinterpret_cast<float *>(smem + L::STAGE0) + ch * BM + r;   // element d at grow[d * 2 * BM]
 #pragma unroll
             for (int a = 0; a < NA; ++a) {
                 uint32_t o[16];
@@ -919,16 +945,13 @@ __global__ void __launch_bounds__(kThreads, 1) dq_kernel(const __grid_constant__
                     for (int e = 0; e < 16; ++e) o[e] = 0u;
                 }
 #pragma unroll
-                for (int e = 0; e < 16; e += 4)
-                    *reinterpret_cast<float4 *>(grow + a * 16 + e) =
-                        make_float4(__uint_as_float(o[e]) * p.scale, __uint_as_float(o[e + 1]) * p.scale,
-                                    __uint_as_float(o[e + 2]) * p.scale, __uint_as_float(o[e + 3]) * p.scale);
+                for (int e = 0; e < 16; ++e) grow[(a * 16 + e) * 2 * BM] = __uint_as_float(o[e]) * p.scale;
             }
             float dc[KM], ds[KM];
 #pragma unroll
             for (int e = 0; e < KM; ++e) {
                 if (e < nk) {
-                    const float g0 = grow[k0 + e], g1 = grow[K + k0 + e];
+                    const float g0 = grow[(k0 + e) * 2 * BM], g1 = grow[(K + k0 + e) * 2 * BM];
                     dc[e] = p.s_aug * (g0 * cv[e] + g1 * sv[e]);
                     ds[e] = p.s_aug * (g0 * sv[e] - g1 * cv[e]);
                 }
@@ -1082,6 +1105,7 @@ int launch_bwd(const ScopeAttnArgs &a, cudaStream_t s) {
         p.K = a.K;
         p.has_slope = a.slope != nullptr;
         p.tab_len = a.tab_len;
+        p.tab_smem = (a.tab_len % 8 == 0) && aligned16(a.cos_tab) && aligned16(a.sin_tab) && a.K <= DA / 2;
         p.cos_tab = a.cos_tab;
         p.sin_tab = a.sin_tab;
         p.s_aug = (float)sqrt((double)a.beta / (double)a.scale);
