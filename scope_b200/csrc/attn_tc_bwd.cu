@@ -151,8 +151,10 @@ __device__ __forceinline__ void elem_bar() { asm volatile("bar.sync 1, 256;" :::
 
 // mbarriers and small shared state of a backward CTA
 struct Bars {
-    uint64_t res_full;                 // the CTA's resident tiles are in shared memory
-    uint64_t acc_done;                 // every MMA of the CTA completed
+    uint64_t res_full[2];              // a work item's resident tiles are in shared memory (buffer ci & 1)
+    uint64_t acc_done;                 // every gradient MMA of a work item completed
+    uint64_t acc_free[2];              // the epilogue of work item ci read the accumulators and is done
+                                       // with resident buffer ci & 1 (elementwise arrivals)
     uint64_t full[4], empty[4];        // streamed stage ring
     uint64_t s_full[2];                // S of a tile is in its buffer
     uint64_t p_full[2];                // P / dS are back in the buffer (elementwise arrivals)
@@ -165,8 +167,11 @@ struct Bars {
     uint32_t tmem_slot;
     volatile int abort_flag, last_flag, pad;
     __device__ void init(int nst) {
-        mbar_init(&res_full, 1);
+        mbar_init(&res_full[0], 1);
+        mbar_init(&res_full[1], 1);
         mbar_init(&acc_done, 1);
+        mbar_init(&acc_free[0], kElem);
+        mbar_init(&acc_free[1], kElem);
         for (int i = 0; i < nst; ++i) {
             mbar_init(&full[i], 1);
             mbar_init(&empty[i], 1);
@@ -367,11 +372,11 @@ __global__ void __launch_bounds__(kThreads, 1) dkv_kernel(const __grid_constant_
     if (warp == 0) {
         // ---------------- producer: K / V once, then the q tiles that see this kv block, ascending
         if (lane == 0 && nq > 0) {
-            mbar_expect_tx(&B.res_full, L::RES_BYTES);
-            tma_load_3d(&maps.k, smem + L::K, &B.res_full, 0, kb * BM, h);
+            mbar_expect_tx(&B.res_full[0], L::RES_BYTES);
+            tma_load_3d(&maps.k, smem + L::K, &B.res_full[0], 0, kb * BM, h);
 #pragma unroll
-            for (int a = 0; a < NA; ++a) tma_load_2d(&maps.ka, smem + L::KA + a * L::ATILE, &B.res_full, 16 * a, kb * BM);
-            tma_load_3d(&maps.v, smem + L::V, &B.res_full, 0, kb * BM, h);
+            for (int a = 0; a < NA; ++a) tma_load_2d(&maps.ka, smem + L::KA + a * L::ATILE, &B.res_full[0], 16 * a, kb * BM);
+            tma_load_3d(&maps.v, smem + L::V, &B.res_full[0], 0, kb * BM, h);
             int w;
             uint32_t bits;
             seek_rank(brow, p.words, first, w, bits);
@@ -400,7 +405,7 @@ __global__ void __launch_bounds__(kThreads, 1) dkv_kernel(const __grid_constant_
                 ++t;
             }
             // never leave the CTA with a TMA write still in flight
-            mbar_wait(&B.res_full, 0, 500000000ull);
+            mbar_wait(&B.res_full[0], 0, 500000000ull);
             for (int j = (t > NST ? t - NST : 0); j < t; ++j) mbar_wait(&B.full[j % NST], (j / NST) & 1, 500000000ull);
         }
     } else if (warp == 1) {
@@ -408,7 +413,7 @@ __global__ void __launch_bounds__(kThreads, 1) dkv_kernel(const __grid_constant_
         if (nq > 0) {
             constexpr uint32_t idS = idesc_bf16(128, 128, false, false);
             const uint32_t sK = smem_u32(smem + L::K), sKA = smem_u32(smem + L::KA), sV = smem_u32(smem + L::V);
-            bool ok = cx.waitw(&B.res_full, 0);
+            bool ok = cx.waitw(&B.res_full[0], 0);
             for (int t = 0; ok && t < nq; ++t) {
                 const int st = t % NST, b = t & 1;
                 if (!cx.waitw(&B.full[st], (t / NST) & 1)) { ok = false; break; }
@@ -670,43 +675,50 @@ __global__ void __launch_bounds__(1024) plan_items_kernel(const int32_t *__restr
 }
 
 // ============================================================================ dQ
-// Resident: Q, the q_aug dims, dO.  Streamed per kv tile (ring of NST
-// stages): K, the k_aug dims, V.
+// Persistent: one CTA per SM walks the work items (head, q block) b, b + G,
+// b + 2G, ... (G CTAs), so that the next item's resident tiles load and its
+// first tiles run while the previous item's epilogue drains.  Resident per item
+// (two buffers, item ci in buffer ci & 1): Q, the q_aug dims, dO and the item's
+// rows of the cos / sin tables.  Streamed per kv tile (ring of NST stages, one
+// tile counter across items): K, the k_aug dims, V.
 template <int DA>
 struct QL {
     static constexpr int NA = DA / 16;
+    static constexpr int KM = DA > 0 ? DA / 2 : 1;                 // coefficients per row, K <= DA / 2
     static constexpr uint32_t TILE = BM * HD * 2, ATILE = BM * 16 * 2;
     static constexpr uint32_t Q = 0, QA = TILE, DO = align1k(TILE + NA * ATILE);
-    static constexpr uint32_t STAGE0 = DO + TILE;
+    static constexpr uint32_t TAB = DO + TILE;                       // bf16 [2][KM][128]: cos rows, sin rows
+    static constexpr uint32_t RESB = align1k(TAB + (NA > 0 ? KM * 512 : 0));
+    static constexpr uint32_t SCRATCH = (uint32_t)(DA > 0 ? DA : 1) * 2 * BM * 4;   // epilogue, inside a buffer
+    static_assert(SCRATCH <= RESB, "epilogue scratch must fit in a resident buffer");
+    static constexpr uint32_t STAGE0 = 2 * RESB;
     static constexpr uint32_t SK = 0, SKA = TILE, SV = align1k(TILE + NA * ATILE);
     static constexpr uint32_t STAGE = SV + TILE;
-    // barriers, slope partials and the table rows after the ring; 1 KiB for the alignment of the base
-    static constexpr uint32_t EXTRA = 1024 + 512 + (DA > 0 ? DA : 1) * 256 + 1024;
-    static constexpr int NST = STAGE0 + 4 * STAGE + EXTRA + 1024 <= kSmemBudget ? 4 : 3;
+    static constexpr uint32_t EXTRA = 1024 + 512 + 1024;            // barriers, slope partials, base alignment
+    static constexpr int NST = STAGE0 + 4 * STAGE + EXTRA <= kSmemBudget
+                                   ? 4
+                                   : (STAGE0 + 3 * STAGE + EXTRA <= kSmemBudget ? 3 : 2);
     static constexpr uint32_t BAR = STAGE0 + NST * STAGE;
-    static constexpr uint32_t RES_BYTES = 2 * TILE + NA * ATILE;
     static constexpr uint32_t SLOPE = align1k(BAR + sizeof(Bars));   // float[128]: slope partials of column half 1
-    // the q block's rows of the cos / sin tables (bf16 [DA/2][128] each) for the coefficient epilogue
-    static constexpr uint32_t TAB = SLOPE + 512;
-    static constexpr uint32_t TOTAL = TAB + (DA > 0 ? DA : 1) * 256;
+    static constexpr uint32_t TOTAL = SLOPE + 512;
+    static constexpr uint32_t RES_BYTES = 2 * TILE + NA * ATILE;
     static constexpr uint32_t KV_BYTES = 2 * TILE + NA * ATILE;
+    static_assert(TOTAL + 1024 <= kSmemBudget, "shared memory");
 };
 
 template <int DA>
 __global__ void __launch_bounds__(kThreads, 1) dq_kernel(const __grid_constant__ Maps maps, const Params p) {
     using L = QL<DA>;
-    constexpr int NA = L::NA, NST = L::NST;
+    constexpr int NA = L::NA, NST = L::NST, KM = L::KM;
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
     Bars &B = *reinterpret_cast<Bars *>(smem + L::BAR);
     float *slope_part = reinterpret_cast<float *>(smem + L::SLOPE);
     Ctx cx{&B.abort_flag, p.err};
 
-    const int qb = blockIdx.x, h = blockIdx.y;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int64_t mrow = (int64_t)h * p.QB + qb;
-    const int n = p.kv_num[mrow];
-    const int32_t *list = p.kv_idx + mrow * p.kv_stride;
+    const int n_items = p.H * p.QB, G = gridDim.x;
+    const bool tab = NA > 0 && p.dcoeff_cos && p.tab_smem;
 
     if (threadIdx.x == 0) B.init(NST);
     if (warp == 1) {
@@ -720,54 +732,76 @@ __global__ void __launch_bounds__(kThreads, 1) dq_kernel(const __grid_constant__
     const uint32_t tmem = B.tmem_slot;
 
     if (warp == 0) {
-        // ---------------- producer: Q / dO once, then the kv tiles of this q block's list, in order
-        if (lane == 0 && n > 0) {
-            const bool tab = NA > 0 && p.dcoeff_cos && p.tab_smem;
-            mbar_expect_tx(&B.res_full, L::RES_BYTES + (tab ? 2u * p.K * 256u : 0u));
-            if (tab) {
-                for (int k = 0; k < p.K; ++k) {
-                    bulk_load(smem + L::TAB + k * 256, p.cos_tab + (int64_t)k * p.tab_len + qb * BM, 256, &B.res_full);
-                    bulk_load(smem + L::TAB + (DA / 2 + k) * 256, p.sin_tab + (int64_t)k * p.tab_len + qb * BM, 256,
-                              &B.res_full);
+        // ---------------- producer: per item the resident tiles, then its kv tiles in list order
+        if (lane == 0) {
+            int gt = 0, ci = 0, last_res = -1;
+            bool ok = true;
+            for (int it = blockIdx.x; ok && it < n_items; it += G, ++ci) {
+                const int h = it / p.QB, qb = it - h * p.QB;
+                const int64_t mrow = (int64_t)h * p.QB + qb;
+                const int n = p.kv_num[mrow];
+                const int32_t *list = p.kv_idx + mrow * p.kv_stride;
+                const int rb = ci & 1;
+                uint8_t *res = smem + rb * L::RESB;
+                // buffer rb is free once the epilogue of item ci - 2 is done with it
+                if (ci >= 2 && !cx.wait1(&B.acc_free[rb], ((ci >> 1) - 1) & 1)) break;
+                if (n > 0) {
+                    mbar_expect_tx(&B.res_full[rb], L::RES_BYTES + (tab ? 2u * p.K * 256u : 0u));
+                    if (tab) {
+                        for (int k = 0; k < p.K; ++k) {
+                            bulk_load(res + L::TAB + k * 256, p.cos_tab + (int64_t)k * p.tab_len + qb * BM, 256,
+                                      &B.res_full[rb]);
+                            bulk_load(res + L::TAB + (KM + k) * 256, p.sin_tab + (int64_t)k * p.tab_len + qb * BM, 256,
+                                      &B.res_full[rb]);
+                        }
+                    }
+                    tma_load_3d(&maps.q, res + L::Q, &B.res_full[rb], 0, qb * BM, h);
+#pragma unroll
+                    for (int a = 0; a < NA; ++a)
+                        tma_load_3d(&maps.qa, res + L::QA + a * L::ATILE, &B.res_full[rb], 16 * a, qb * BM, h);
+                    tma_load_3d(&maps.dout, res + L::DO, &B.res_full[rb], 0, qb * BM, h);
+                    last_res = ci;
+                } else {
+                    mbar_arrive(&B.res_full[rb]);      // keeps the buffer's phases in step
+                }
+                for (int jj = 0; jj < n; ++jj, ++gt) {
+                    const int st = gt % NST;
+                    if (gt >= NST && !cx.wait1(&B.empty[st], ((gt / NST) - 1) & 1)) { ok = false; break; }
+                    int kb = list[jj];
+                    B.stage_blk[st] = kb;
+                    const bool bad = kb < 0 || kb >= p.QB;
+                    B.stage_mk[st] = bad ? MASK_DOCS : tile_mask_kind(qb, kb, p.docs != nullptr, p.block_info, p.QB);
+                    if (bad) kb = 0;   // masked by the elementwise warps
+                    uint8_t *sb = smem + L::STAGE0 + st * L::STAGE;
+                    mbar_expect_tx(&B.full[st], L::KV_BYTES);
+                    tma_load_3d(&maps.k, sb + L::SK, &B.full[st], 0, kb * BM, h);
+#pragma unroll
+                    for (int a = 0; a < NA; ++a)
+                        tma_load_2d(&maps.ka, sb + L::SKA + a * L::ATILE, &B.full[st], 16 * a, kb * BM);
+                    tma_load_3d(&maps.v, sb + L::SV, &B.full[st], 0, kb * BM, h);
                 }
             }
-            tma_load_3d(&maps.q, smem + L::Q, &B.res_full, 0, qb * BM, h);
-#pragma unroll
-            for (int a = 0; a < NA; ++a)
-                tma_load_3d(&maps.qa, smem + L::QA + a * L::ATILE, &B.res_full, 16 * a, qb * BM, h);
-            tma_load_3d(&maps.dout, smem + L::DO, &B.res_full, 0, qb * BM, h);
-            int issued = 0;
-            for (int jj = 0; jj < n; ++jj) {
-                const int st = jj % NST;
-                if (jj >= NST && !cx.wait1(&B.empty[st], ((jj / NST) - 1) & 1)) break;
-                int kb = list[jj];
-                B.stage_blk[st] = kb;
-                const bool bad = kb < 0 || kb >= p.QB;
-                B.stage_mk[st] = bad ? MASK_DOCS : tile_mask_kind(qb, kb, p.docs != nullptr, p.block_info, p.QB);
-                if (bad) kb = 0;   // masked by the elementwise warps
-                uint8_t *sb = smem + L::STAGE0 + st * L::STAGE;
-                mbar_expect_tx(&B.full[st], L::KV_BYTES);
-                tma_load_3d(&maps.k, sb + L::SK, &B.full[st], 0, kb * BM, h);
-#pragma unroll
-                for (int a = 0; a < NA; ++a)
-                    tma_load_2d(&maps.ka, sb + L::SKA + a * L::ATILE, &B.full[st], 16 * a, kb * BM);
-                tma_load_3d(&maps.v, sb + L::SV, &B.full[st], 0, kb * BM, h);
-                issued = jj + 1;
-            }
-            mbar_wait(&B.res_full, 0, 500000000ull);
-            for (int j = (issued > NST ? issued - NST : 0); j < issued; ++j)
-                mbar_wait(&B.full[j % NST], (j / NST) & 1, 500000000ull);
+            // never leave the CTA with a TMA write still in flight
+            if (last_res >= 0) mbar_wait(&B.res_full[last_res & 1], (last_res >> 1) & 1, 500000000ull);
+            for (int j = (gt > NST ? gt - NST : 0); j < gt; ++j) mbar_wait(&B.full[j % NST], (j / NST) & 1, 500000000ull);
         }
     } else if (warp == 1) {
         // ---------------- S / dP issuer (the whole warp waits, lane 0 issues)
-        if (n > 0) {
-            constexpr uint32_t idS = idesc_bf16(128, 128, false, false);
-            const uint32_t sQ = smem_u32(smem + L::Q), sQA = smem_u32(smem + L::QA), sDO = smem_u32(smem + L::DO);
-            bool ok = cx.waitw(&B.res_full, 0);
-            for (int jj = 0; ok && jj < n; ++jj) {
-                const int st = jj % NST, b = jj & 1;
-                if (!cx.waitw(&B.full[st], (jj / NST) & 1)) { ok = false; break; }
-                if (jj >= 2 && !cx.waitw(&B.s_free[b], ((jj >> 1) - 1) & 1)) { ok = false; break; }
+        constexpr uint32_t idS = idesc_bf16(128, 128, false, false);
+        int gt = 0, ci = 0;
+        bool ok = true;
+        for (int it = blockIdx.x; ok && it < n_items; it += G, ++ci) {
+            const int h = it / p.QB, qb = it - h * p.QB;
+            const int n = p.kv_num[(int64_t)h * p.QB + qb];
+            if (n == 0) continue;
+            const int rb = ci & 1;
+            const uint32_t res = smem_u32(smem + rb * L::RESB);
+            const uint32_t sQ = res + L::Q, sQA = res + L::QA, sDO = res + L::DO;
+            if (!cx.waitw(&B.res_full[rb], (ci >> 1) & 1)) { ok = false; break; }
+            for (int jj = 0; jj < n; ++jj, ++gt) {
+                const int st = gt % NST, b = gt & 1;
+                if (!cx.waitw(&B.full[st], (gt / NST) & 1)) { ok = false; break; }
+                if (gt >= 2 && !cx.waitw(&B.s_free[b], ((gt >> 1) - 1) & 1)) { ok = false; break; }
                 tc_fence_after();
                 const uint32_t sb = smem_u32(smem + L::STAGE0 + st * L::STAGE);
                 // S = Q K^T (+ Qaug Kaug^T): 128 q rows x 128 kv columns
@@ -784,7 +818,7 @@ __global__ void __launch_bounds__(kThreads, 1) dq_kernel(const __grid_constant__
                 }
                 __syncwarp();
                 // dP = dO V^T, once the elementwise warps have read dP of the previous tile
-                if (jj >= 1 && !cx.waitw(&B.dp_free, (jj - 1) & 1)) { ok = false; break; }
+                if (gt >= 1 && !cx.waitw(&B.dp_free, (gt - 1) & 1)) { ok = false; break; }
                 tc_fence_after();
                 if (lane == 0) {
 #pragma unroll
@@ -795,23 +829,32 @@ __global__ void __launch_bounds__(kThreads, 1) dq_kernel(const __grid_constant__
                 }
                 __syncwarp();
             }
-            if (!ok) cx.give_up();
-            if (lane == 0) tc_commit(&B.drain[0]);   // TMEM is freed only after this warp's MMAs completed
-            mbar_wait(&B.drain[0], 0, 500000000ull);
         }
+        if (!ok) cx.give_up();
+        if (lane == 0) tc_commit(&B.drain[0]);   // TMEM is freed only after this warp's MMAs completed
+        mbar_wait(&B.drain[0], 0, 500000000ull);
     } else if (warp == kGradWarp) {
         // ---------------- gradient issuer (whole warp): a second issuing warp, so
         // the S / dP MMAs and these queue on the tensor pipe side by side
-        if (n > 0) {
-            constexpr uint32_t idG = idesc_bf16(128, 64, false, true);
-            // the DA/16 aug sub-tiles (16 columns, 32-byte swizzle) lie 4 KiB apart:
-            // one MN-major operand of N = DA whose atoms the descriptor's
-            // leading byte offset (4 KiB) steps through
-            constexpr uint32_t idA = idesc_bf16(128, DA > 0 ? DA : 16, false, true);
-            bool ok = true;
-            for (int jj = 0; ok && jj < n; ++jj) {
-                const int st = jj % NST, b = jj & 1;
-                if (!cx.waitw(&B.p_full[b], (jj >> 1) & 1)) { ok = false; break; }
+        constexpr uint32_t idG = idesc_bf16(128, 64, false, true);
+        // the DA/16 aug sub-tiles (16 columns, 32-byte swizzle) lie 4 KiB apart:
+        // one MN-major operand of N = DA whose atoms the descriptor's
+        // leading byte offset (4 KiB) steps through
+        constexpr uint32_t idA = idesc_bf16(128, DA > 0 ? DA : 16, false, true);
+        int gt = 0, ci = 0;
+        bool ok = true;
+        for (int it = blockIdx.x; ok && it < n_items; it += G, ++ci) {
+            const int h = it / p.QB, qb = it - h * p.QB;
+            const int n = p.kv_num[(int64_t)h * p.QB + qb];
+            for (int jj = 0; jj < n; ++jj, ++gt) {
+                const int st = gt % NST, b = gt & 1;
+                if (!cx.waitw(&B.p_full[b], (gt >> 1) & 1)) { ok = false; break; }
+                // the first MMA of an item overwrites the accumulators: the previous
+                // item's epilogue must have read them
+                if (jj == 0 && ci >= 1 && !cx.waitw(&B.acc_free[(ci - 1) & 1], ((ci - 1) >> 1) & 1)) {
+                    ok = false;
+                    break;
+                }
                 tc_fence_after();
                 const uint32_t sb = smem_u32(smem + L::STAGE0 + st * L::STAGE);
                 // dQ += dS K (+ dQaug += dS Kaug) over the tile's 128 kv rows
@@ -826,156 +869,170 @@ __global__ void __launch_bounds__(kThreads, 1) dq_kernel(const __grid_constant__
                             mma_ts(tmem + ACC1, tmem + sbuf(b) + a_col(kk), mnmajor32_desc(sb + L::SKA + kk * 512), idA,
                                    (jj > 0 || kk > 0) ? 1u : 0u);
                     }
-                    if (jj + 2 < n) tc_commit(&B.s_free[b]);     // only arrivals someone waits for
-                    if (jj + NST < n) tc_commit(&B.empty[st]);
+                    tc_commit(&B.s_free[b]);
+                    tc_commit(&B.empty[st]);
                 }
                 __syncwarp();
             }
-            if (ok && lane == 0) tc_commit(&B.acc_done);
-            if (!ok) cx.give_up();
-            if (lane == 0) tc_commit(&B.drain[1]);
-            mbar_wait(&B.drain[1], 0, 500000000ull);
+            if (!ok) break;
+            if (lane == 0) tc_commit(&B.acc_done);   // every item, so the epilogue's phases stay in step
+            __syncwarp();
         }
+        if (!ok) cx.give_up();
+        if (lane == 0) tc_commit(&B.drain[1]);
+        mbar_wait(&B.drain[1], 0, 500000000ull);
     } else {
         // ---------------- elementwise: thread = q row i, tile columns [64ch, 64ch+64) in two chunks of 32
         const int quad = warp & 3;
         const int ch = (warp - 2) >> 2;
         const int r = quad * 32 + lane;
-        const int i = qb * BM + r;
         const uint32_t lb = (uint32_t)(quad * 32) << 16;
         const bool have_docs = p.docs != nullptr;
-        const int doc_i = have_docs ? p.docs[i] : 0;
-        const int64_t hrow = (int64_t)h * p.T + i;
-        const float l2 = p.lse2[hrow], dl = p.delta[hrow];
-        // The slope column of k_aug holds positions * s (up to ~T*s).  Its dS sum
-        // is accumulated here in fp32 from the unrounded dS, against positions
-        // relative to this query row: sum_j dS_ij = 0 in exact arithmetic, so
-        // subtracting k_aug[i] changes nothing but the rounding, which would
-        // otherwise amplify the small residual of that sum by ~i*s.
         const bool slope_acc = NA > 0 && p.has_slope && p.dslope;
-        const float kpos_i = __bfloat162float(__float2bfloat16_rn(__fmul_rn((float)i, p.s_aug)));
-        float gsl = 0.f;
+        const uint64_t c2 = f2_pack(p.scale_log2, p.scale_log2);
+        int gt = 0, ci = 0;
         bool alive = true;
-        const uint64_t c2 = f2_pack(p.scale_log2, p.scale_log2), nl2 = f2_pack(-l2, -l2), nd2 = f2_pack(-dl, -dl);
-        for (int jj = 0; jj < n && alive; ++jj) {
-            const int st = jj % NST, b = jj & 1;
-            if (!cx.waitw(&B.full[st], (jj / NST) & 1)) { alive = false; break; }
-            const int kb = B.stage_blk[st];
-            const bool bad = kb < 0 || kb >= p.QB;
-            const int mk = B.stage_mk[st];
-            if (!cx.waitw(&B.s_full[b], (jj >> 1) & 1) || !cx.waitw(&B.dp_full, jj & 1)) { alive = false; break; }
-            tc_fence_after();
-            const uint32_t tb = tmem + lb + sbuf(b) + ch * 64;
+        for (int it = blockIdx.x; alive && it < n_items; it += G, ++ci) {
+            const int h = it / p.QB, qb = it - h * p.QB;
+            const int n = p.kv_num[(int64_t)h * p.QB + qb];
+            const int rb = ci & 1;
+            uint8_t *res = smem + rb * L::RESB;
+            const int i = qb * BM + r;
+            const int doc_i = have_docs ? p.docs[i] : 0;
+            const int64_t hrow = (int64_t)h * p.T + i;
+            const float l2 = p.lse2[hrow], dl = p.delta[hrow];
+            const uint64_t nl2 = f2_pack(-l2, -l2), nd2 = f2_pack(-dl, -dl);
+            // The slope column of k_aug holds positions * s (up to ~T*s).  Its dS sum
+            // is accumulated here in fp32 from the unrounded dS, against positions
+            // relative to this query row: sum_j dS_ij = 0 in exact arithmetic, so
+            // subtracting k_aug[i] changes nothing but the rounding, which would
+            // otherwise amplify the small residual of that sum by ~i*s.
+            const float kpos_i = __bfloat162float(__float2bfloat16_rn(__fmul_rn((float)i, p.s_aug)));
+            float gsl = 0.f;
+            for (int jj = 0; jj < n; ++jj, ++gt) {
+                const int st = gt % NST, b = gt & 1;
+                if (!cx.waitw(&B.full[st], (gt / NST) & 1)) { alive = false; break; }
+                const int kb = B.stage_blk[st];
+                const bool bad = kb < 0 || kb >= p.QB;
+                const int mk = B.stage_mk[st];
+                if (!cx.waitw(&B.s_full[b], (gt >> 1) & 1) || !cx.waitw(&B.dp_full, gt & 1)) { alive = false; break; }
+                tc_fence_after();
+                const uint32_t tb = tmem + lb + sbuf(b) + ch * 64;
 #pragma unroll
-            for (int cc = 0; cc < 2; ++cc) {
-                float s[32], dp[32];
-                ld_s_dp(tb + cc * 32, tmem + lb + DPC + ch * 64 + cc * 32, s, dp);
-                if (cc == 1) {
-                    tc_fence_before();
-                    mbar_arrive(&B.dp_free);        // this warp's dP columns are in registers
-                }
-                const int j0 = kb * BM + ch * 64 + cc * 32;
-                const int lim = i - j0;              // column e visible iff e <= lim (causal: j <= i)
-                if (mk == MASK_FULL) dq_piece<false>(s, dp, c2, nl2, nd2, mk, lim, bad, p.docs, j0, doc_i);
-                else dq_piece<true>(s, dp, c2, nl2, nd2, mk, lim, bad, p.docs, j0, doc_i);
-                if (slope_acc && !bad) {
-#pragma unroll
-                    for (int e = 0; e < 32; ++e) {
-                        // the value scope_qk_aug_prepare stored: bf16(fp32(j) * s)
-                        const float kpos = __bfloat162float(__float2bfloat16_rn(__fmul_rn((float)(j0 + e), p.s_aug)));
-                        gsl = fmaf(s[e], kpos - kpos_i, gsl);
+                for (int cc = 0; cc < 2; ++cc) {
+                    float s[32], dp[32];
+                    ld_s_dp(tb + cc * 32, tmem + lb + DPC + ch * 64 + cc * 32, s, dp);
+                    if (cc == 1) {
+                        tc_fence_before();
+                        mbar_arrive(&B.dp_free);        // this warp's dP columns are in registers
                     }
+                    const int j0 = kb * BM + ch * 64 + cc * 32;
+                    const int lim = i - j0;              // column e visible iff e <= lim (causal: j <= i)
+                    if (mk == MASK_FULL) dq_piece<false>(s, dp, c2, nl2, nd2, mk, lim, bad, p.docs, j0, doc_i);
+                    else dq_piece<true>(s, dp, c2, nl2, nd2, mk, lim, bad, p.docs, j0, doc_i);
+                    if (slope_acc && !bad) {
+#pragma unroll
+                        for (int e = 0; e < 32; ++e) {
+                            // the value scope_qk_aug_prepare stored: bf16(fp32(j) * s)
+                            const float kpos =
+                                __bfloat162float(__float2bfloat16_rn(__fmul_rn((float)(j0 + e), p.s_aug)));
+                            gsl = fmaf(s[e], kpos - kpos_i, gsl);
+                        }
+                    }
+                    st_bf16x32(tb + cc * 16, s);         // dS pairs over columns this warp has read
                 }
-                st_bf16x32(tb + cc * 16, s);         // dS pairs over columns this warp has read
+                tmem_wait_st();
+                tc_fence_before();
+                mbar_arrive(&B.p_full[b]);
             }
-            tmem_wait_st();
-            tc_fence_before();
-            mbar_arrive(&B.p_full[b]);
-        }
-        bool have = false;
-        if (alive && n > 0) {
-            have = cx.waitw(&B.acc_done, 0);
+            if (!alive) break;
+            // ---------------- epilogue of the item
+            if (!cx.waitw(&B.acc_done, ci & 1)) { alive = false; break; }
             tc_fence_after();
-        }
-        // dQ: each column half stores 32 of the 64 columns
-        store_row32(tmem + lb + ACC0 + ch * 32, p.scale,
-                    p.g0 + (int64_t)h * p.g0_sh + (int64_t)i * p.g0_st + ch * 32, have);
-        if (NA > 0 && p.dcoeff_cos) {
-            // gradient of the augmented dims -> coefficients (q_aug = s [A c + B s', A s' - B c, -slope]);
-            // the two warps of a quadrant split the K coefficients
-            if (ch == 1) slope_part[r] = gsl;
-            const int K = p.K;
-            const int kh = (K + 1) >> 1;
-            const int k0 = ch == 0 ? 0 : kh, nk = ch == 0 ? kh : K - kh;
-            constexpr int KM = DA > 0 ? DA / 2 : 1;     // K <= DA / 2
-            float cv[KM], sv[KM];
-            if (p.tab_smem) {
-                // the producer staged this q block's table rows with the resident tiles
-                const bool ok = cx.waitw(&B.res_full, 0);
-                const uint16_t *tc = reinterpret_cast<const uint16_t *>(smem + L::TAB);
+            const bool have = n > 0;
+            // dQ: each column half stores 32 of the 64 columns
+            store_row32(tmem + lb + ACC0 + ch * 32, p.scale,
+                        p.g0 + (int64_t)h * p.g0_sh + (int64_t)i * p.g0_st + ch * 32, have);
+            if (NA > 0 && p.dcoeff_cos) {
+                // gradient of the augmented dims -> coefficients (q_aug = s [A c + B s', A s' - B c, -slope]);
+                // the two warps of a quadrant split the K coefficients
+                if (ch == 1) slope_part[r] = gsl;
+                const int K = p.K;
+                const int kh = (K + 1) >> 1;
+                const int k0 = ch == 0 ? 0 : kh, nk = ch == 0 ? kh : K - kh;
+                float cv[KM], sv[KM];
+                if (tab && have) {
+                    // the producer staged this item's table rows with its resident tiles
+                    const bool ok = cx.waitw(&B.res_full[rb], (ci >> 1) & 1);
+                    const uint16_t *tc = reinterpret_cast<const uint16_t *>(res + L::TAB);
 #pragma unroll
-                for (int e = 0; e < KM; ++e) {
-                    if (e < nk) {
-                        cv[e] = ok ? bf16_to_f32(tc[(k0 + e) * BM + r]) : 0.f;
-                        sv[e] = ok ? bf16_to_f32(tc[(KM + k0 + e) * BM + r]) : 0.f;
+                    for (int e = 0; e < KM; ++e) {
+                        if (e < nk) {
+                            cv[e] = ok ? bf16_to_f32(tc[(k0 + e) * BM + r]) : 0.f;
+                            sv[e] = ok ? bf16_to_f32(tc[(KM + k0 + e) * BM + r]) : 0.f;
+                        }
                     }
-                }
-            } else {
-#pragma unroll
-                for (int e = 0; e < KM; ++e) {          // independent table loads, issued together
-                    if (e < nk) {
-                        cv[e] = bf16_to_f32(p.cos_tab[(int64_t)(k0 + e) * p.tab_len + i]);
-                        sv[e] = bf16_to_f32(p.sin_tab[(int64_t)(k0 + e) * p.tab_len + i]);
-                    }
-                }
-            }
-            // this thread's aug-gradient row goes through shared memory (indexed by the
-            // runtime K), column-major so a warp's accesses hit distinct banks; the
-            // stage ring is idle once every MMA has completed
-            float *grow = reinterpret_cast<float *>(smem + L::STAGE0) + ch * BM + r;   // element d at grow[d * 2 * BM]
-#pragma unroll
-            for (int a = 0; a < NA; ++a) {
-                uint32_t o[16];
-                if (have) {
-                    tmem_ld16(tmem + lb + ACC1 + a * 16, o);
-                    tmem_wait_ld();
-                    pin(o);
                 } else {
 #pragma unroll
-                    for (int e = 0; e < 16; ++e) o[e] = 0u;
-                }
-#pragma unroll
-                for (int e = 0; e < 16; ++e) grow[(a * 16 + e) * 2 * BM] = __uint_as_float(o[e]) * p.scale;
-            }
-            float dc[KM], ds[KM];
-#pragma unroll
-            for (int e = 0; e < KM; ++e) {
-                if (e < nk) {
-                    const float g0 = grow[(k0 + e) * 2 * BM], g1 = grow[(K + k0 + e) * 2 * BM];
-                    dc[e] = p.s_aug * (g0 * cv[e] + g1 * sv[e]);
-                    ds[e] = p.s_aug * (g0 * sv[e] - g1 * cv[e]);
-                }
-            }
-            float *oc = p.dcoeff_cos + hrow * K + k0, *os = p.dcoeff_sin + hrow * K + k0;
-            if (((K | k0 | nk) & 3) == 0) {
-#pragma unroll
-                for (int e = 0; e < KM; e += 4) {
-                    if (e < nk) {
-                        *reinterpret_cast<float4 *>(oc + e) = make_float4(dc[e], dc[e + 1], dc[e + 2], dc[e + 3]);
-                        *reinterpret_cast<float4 *>(os + e) = make_float4(ds[e], ds[e + 1], ds[e + 2], ds[e + 3]);
+                    for (int e = 0; e < KM; ++e) {          // independent table loads, issued together
+                        if (e < nk) {
+                            cv[e] = bf16_to_f32(p.cos_tab[(int64_t)(k0 + e) * p.tab_len + i]);
+                            sv[e] = bf16_to_f32(p.sin_tab[(int64_t)(k0 + e) * p.tab_len + i]);
+                        }
                     }
                 }
-            } else {
+                elem_bar();   // every table read is done before the scratch overwrites the buffer
+                // this thread's aug-gradient row through shared memory (indexed by the runtime
+                // K), column-major so a warp's accesses hit distinct banks; the item's resident
+                // buffer is idle once its MMAs completed and stays ours until acc_free
+                float *grow = reinterpret_cast<float *>(res) + ch * BM + r;   // element d at grow[d * 2 * BM]
+#pragma unroll
+                for (int a = 0; a < NA; ++a) {
+                    uint32_t o[16];
+                    if (have) {
+                        tmem_ld16(tmem + lb + ACC1 + a * 16, o);
+                        tmem_wait_ld();
+                        pin(o);
+                    } else {
+#pragma unroll
+                        for (int e = 0; e < 16; ++e) o[e] = 0u;
+                    }
+#pragma unroll
+                    for (int e = 0; e < 16; ++e) grow[(a * 16 + e) * 2 * BM] = __uint_as_float(o[e]) * p.scale;
+                }
+                float dc[KM], ds[KM];
 #pragma unroll
                 for (int e = 0; e < KM; ++e) {
                     if (e < nk) {
-                        oc[e] = dc[e];
-                        os[e] = ds[e];
+                        const float g0 = grow[(k0 + e) * 2 * BM], g1 = grow[(K + k0 + e) * 2 * BM];
+                        dc[e] = p.s_aug * (g0 * cv[e] + g1 * sv[e]);
+                        ds[e] = p.s_aug * (g0 * sv[e] - g1 * cv[e]);
                     }
                 }
+                float *oc = p.dcoeff_cos + hrow * K + k0, *os = p.dcoeff_sin + hrow * K + k0;
+                if (((K | k0 | nk) & 3) == 0) {
+#pragma unroll
+                    for (int e = 0; e < KM; e += 4) {
+                        if (e < nk) {
+                            *reinterpret_cast<float4 *>(oc + e) = make_float4(dc[e], dc[e + 1], dc[e + 2], dc[e + 3]);
+                            *reinterpret_cast<float4 *>(os + e) = make_float4(ds[e], ds[e + 1], ds[e + 2], ds[e + 3]);
+                        }
+                    }
+                } else {
+#pragma unroll
+                    for (int e = 0; e < KM; ++e) {
+                        if (e < nk) {
+                            oc[e] = dc[e];
+                            os[e] = ds[e];
+                        }
+                    }
+                }
+                // (read between the two barriers: the next item's write comes after the second)
+                if (ch == 0 && slope_acc) p.dslope[hrow] = -p.s_aug * ((gsl + slope_part[r]) * p.scale);
+                elem_bar();
             }
-            elem_bar();
-            if (ch == 0 && slope_acc) p.dslope[hrow] = -p.s_aug * ((gsl + slope_part[r]) * p.scale);
+            tc_fence_before();
+            mbar_arrive(&B.acc_free[rb]);   // accumulators read, resident buffer rb released
         }
     }
     __syncwarp();   // every warp reaches the CTA barrier converged (the producer ran on lane 0 alone)
@@ -1117,7 +1174,12 @@ int launch_bwd(const ScopeAttnArgs &a, cudaStream_t s) {
     if (cudaFuncSetAttribute(tcbwd::dq_kernel<DA>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
         cudaSuccess)
         return SCOPE_ERR_CUDA;
-    tcbwd::dq_kernel<DA><<<dim3(QB, a.H), tcbwd::kThreads, smem, s>>>(maps, p);
+    // persistent: one CTA per SM (at most one per work item)
+    int dev = 0, n_sm = 148;
+    if (cudaGetDevice(&dev) != cudaSuccess || cudaDeviceGetAttribute(&n_sm, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+        return SCOPE_ERR_CUDA;
+    const int grid_q = std::min(a.H * QB, n_sm);
+    tcbwd::dq_kernel<DA><<<grid_q, tcbwd::kThreads, smem, s>>>(maps, p);
     SCOPE_CHECK_LAUNCH();
     return SCOPE_OK;
 }
