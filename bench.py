@@ -447,7 +447,7 @@ def main():
     if dom == 0:
         roof["traffic"] = 0.073e9 * wl.hp / 16           # mask::build_kernel, per head
     else:
-        per_pair = 1.693e9 / 238859 if dom == 1 else (0.559e9 + 3.120e9 + 2.596e9) / 238859
+        per_pair = 1.693e9 / 238859 if dom == 1 else (0.559e9 + 3.119e9 + 2.557e9) / 238859
         roof["traffic"] = per_pair * P_local
     roof["traffic_unit"] = "bytes per launch"
     roof["traffic_source"] = "ncu dram__bytes_read.sum + dram__bytes_write.sum of the C3 step, scaled to this launch"
