@@ -267,7 +267,11 @@ __global__ void __launch_bounds__(kThreads, 2) fwd_kernel(const __grid_constant_
                        tP = tmem + lane_base + P_COL + ch * 32;
         const bool have_docs = p.docs != nullptr;
         const int doc_i = have_docs ? p.docs[i] : 0;
-        const uint64_t c2 = f2_pack(p.scale_log2, p.scale_log2);
+        // scores are kept unscaled until the exponent: max(x) * c = max(x * c) for c > 0,
+        // and a negative scale is folded into the sign of the loaded scores
+        const bool neg = p.scale_log2 < 0.f;
+        const float cabs = fabsf(p.scale_log2);
+        const uint64_t c2 = f2_pack(cabs, cabs);
         float m = -INFINITY, l = 0.f;
         bool alive = true;
         int xphase = 0;                         // completed phases of this quadrant's exchange barrier
@@ -288,13 +292,13 @@ __global__ void __launch_bounds__(kThreads, 2) fwd_kernel(const __grid_constant_
                 pin(u0);
                 pin(u1);
 #pragma unroll
-                for (int e = 0; e < 32; e += 2) {
-                    const float2 a = f2_unpack(fmul2(f2_pack(__uint_as_float(u0[e]), __uint_as_float(u0[e + 1])), c2));
-                    const float2 b = f2_unpack(fmul2(f2_pack(__uint_as_float(u1[e]), __uint_as_float(u1[e + 1])), c2));
-                    x[e] = a.x;
-                    x[e + 1] = a.y;
-                    x[32 + e] = b.x;
-                    x[32 + e + 1] = b.y;
+                for (int e = 0; e < 32; ++e) {
+                    x[e] = __uint_as_float(u0[e]);
+                    x[32 + e] = __uint_as_float(u1[e]);
+                }
+                if (neg) {
+#pragma unroll
+                    for (int e = 0; e < 64; ++e) x[e] = -x[e];
                 }
             }
             tc_fence_before();
@@ -309,9 +313,14 @@ __global__ void __launch_bounds__(kThreads, 2) fwd_kernel(const __grid_constant_
                     if (!valid) x[c] = -INFINITY;
                 }
             }
-            float pmx = x[0];
+            // row max over this thread's 64 columns: 8 independent chains, then a tree
+            float pm[8];
 #pragma unroll
-            for (int c = 1; c < 64; ++c) pmx = fmaxf(pmx, x[c]);
+            for (int c = 0; c < 8; ++c) pm[c] = x[c];
+#pragma unroll
+            for (int c = 8; c < 64; ++c) pm[c & 7] = fmaxf(pm[c & 7], x[c]);
+            const float pmx = fmaxf(fmaxf(fmaxf(pm[0], pm[1]), fmaxf(pm[2], pm[3])),
+                                    fmaxf(fmaxf(pm[4], pm[5]), fmaxf(pm[6], pm[7]))) * cabs;
             // row max across the two column halves
             xmax[(j & 1) * 256 + ch * 128 + r] = pmx;
             mbar_arrive(xchg + quad);
@@ -327,34 +336,34 @@ __global__ void __launch_bounds__(kThreads, 2) fwd_kernel(const __grid_constant_
             }
             const float mref = (m == -INFINITY) ? 0.f : m;
             const uint64_t nm2 = f2_pack(-mref, -mref);
-            float rs = 0.f;
+            // p = 2^(x c - m) in one packed FMA per pair; the row sum in four packed partials
+            uint64_t acc[4] = {0ull, 0ull, 0ull, 0ull};
+            uint32_t pk[32];                  // P as bf16 pairs, packed as it is formed
 #pragma unroll
             for (int c = 0; c < 64; c += 2) {
-                const float2 d = f2_unpack(fadd2(f2_pack(x[c], x[c + 1]), nm2));
-                x[c] = ex2(d.x);
-                x[c + 1] = ex2(d.y);
-                rs += x[c] + x[c + 1];
+                const float2 d = f2_unpack(ffma2(f2_pack(x[c], x[c + 1]), c2, nm2));
+                const float p0 = ex2(d.x), p1 = ex2(d.y);
+                pk[c >> 1] = pack_bf16(p0, p1);
+                acc[(c >> 1) & 3] = fadd2(acc[(c >> 1) & 3], f2_pack(p0, p1));
             }
+            const float2 a01 = f2_unpack(fadd2(acc[0], acc[1])), a23 = f2_unpack(fadd2(acc[2], acc[3]));
+            const float rs = (a01.x + a01.y) + (a23.x + a23.y);
             l = l * alpha + rs;
+            // P V of the previous tile has read P and written O: P can be replaced, O rescaled
             if (j > 0) {
                 if (!warp_wait(o_done, (j - 1) & 1)) { give_up(); alive = false; break; }
                 tc_fence_after();
-                // tcgen05.ld/st are warp-collective: rescale O whenever any row of the warp needs it
-                if (__any_sync(0xffffffffu, rescale)) {
-                    uint32_t o[32];
-                    tmem_ld32_nw(tO, o);
-                    tmem_wait_ld();
-                    pin(o);
-#pragma unroll
-                    for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * alpha);
-                    tmem_st32(tO, o);
-                }
             }
-            {
-                uint32_t pk[32];
+            tmem_st32(tP, pk);
+            // tcgen05.ld/st are warp-collective: rescale O whenever any row of the warp needs it
+            if (j > 0 && __any_sync(0xffffffffu, rescale)) {
+                uint32_t o[32];
+                tmem_ld32_nw(tO, o);
+                tmem_wait_ld();
+                pin(o);
 #pragma unroll
-                for (int e = 0; e < 32; ++e) pk[e] = pack_bf16(x[2 * e], x[2 * e + 1]);
-                tmem_st32(tP, pk);
+                for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * alpha);
+                tmem_st32(tO, o);
             }
             tmem_wait_st();
             tc_fence_before();
