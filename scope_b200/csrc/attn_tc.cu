@@ -227,31 +227,50 @@ __global__ void __launch_bounds__(kThreads, 2) fwd_kernel(const __grid_constant_
                         mma_ss(tS, kmajor_desc(sq + L::QA + a * L::ATILE, 32), kmajor_desc(sk + L::KA + a * L::ATILE, 32),
                                idS, 1);
                     tc_commit(s_full);
-                    // K of this stage may be reloaded once S is done; commit only arrivals
-                    // someone waits for (one still in flight at CTA exit delays the TMEM release)
+                    // K of this stage may be reloaded once S is done (only when a later tile will be)
                     if (j + 2 < n) tc_commit(kv_empty + s);
                 }
                 __syncwarp();
                 return true;
             };
             ok = ok && issue_S(0);
-            for (int j = 0; ok && j < n; ++j) {
-                if (j + 1 < n) {
-                    if (!warp_wait(s_free, j & 1)) { ok = false; break; }
-                    if (!issue_S(j + 1)) { ok = false; break; }
+            // S_{js} and P V_{jp} are issued as soon as their inputs are ready, in
+            // whichever order they become ready: S_{j+1} needs K_{j+1} (a TMA load
+            // that may still be in flight) and the softmax's copy of S_j; P V_j needs
+            // P_j.  A late K must not hold back P V_j, which the next softmax waits on.
+            int js = 1, jp = 0;
+            uint64_t t_last = globaltimer_ns();
+            while (ok && jp < n) {
+                bool did = false;
+                if (js < n && mbar_test(s_free, (js - 1) & 1) && mbar_test(kv_full + (js & 1), (js >> 1) & 1)) {
+                    __syncwarp();
+                    if (!issue_S(js)) { ok = false; break; }
+                    ++js;
+                    did = true;
                 }
-                if (!warp_wait(p_full, j & 1)) { ok = false; break; }
-                if (!warp_wait(v_full + (j & 1), (j >> 1) & 1)) { ok = false; break; }
-                tc_fence_after();
-                const uint32_t sv = smem_u32(smem + L::STAGE0 + (j & 1) * L::STAGE + L::V);
-                if (lane == 0) {
+                if (jp < js && mbar_test(p_full, jp & 1) && mbar_test(v_full + (jp & 1), (jp >> 1) & 1)) {
+                    __syncwarp();
+                    tc_fence_after();
+                    const uint32_t sv = smem_u32(smem + L::STAGE0 + (jp & 1) * L::STAGE + L::V);
+                    if (lane == 0) {
 #pragma unroll
-                    for (int kk = 0; kk < BM / 16; ++kk)
-                        mma_ts(tO, tP + kk * 8, mnmajor128_desc(sv + kk * 2048), idO, (j > 0 || kk > 0) ? 1u : 0u);
-                    tc_commit(o_done);
-                    if (j + 2 < n) tc_commit(v_empty + (j & 1));
+                        for (int kk = 0; kk < BM / 16; ++kk)
+                            mma_ts(tO, tP + kk * 8, mnmajor128_desc(sv + kk * 2048), idO, (jp > 0 || kk > 0) ? 1u : 0u);
+                        tc_commit(o_done);
+                        if (jp + 2 < n) tc_commit(v_empty + (jp & 1));
+                    }
+                    __syncwarp();
+                    ++jp;
+                    did = true;
                 }
-                __syncwarp();
+                if (did) {
+                    t_last = globaltimer_ns();
+                } else if (*abort_flag || globaltimer_ns() - t_last > kWaitLimitNs) {
+                    ok = false;
+                } else {
+                    __nanosleep(32);   // leave the sub-partition's issue slots to the softmax warps
+                }
+                ok = __all_sync(0xffffffffu, ok);
             }
             if (!ok) give_up();
         }

@@ -64,6 +64,22 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, uint64
     }
 }
 
+// Non-blocking test of a phase, decided by lane 0 of a converged warp and
+// broadcast, so the whole warp takes the same branch.
+__device__ __forceinline__ bool mbar_test(uint64_t *bar, uint32_t parity) {
+    uint32_t ok = 0;
+    if ((threadIdx.x & 31) == 0) {
+        asm volatile(
+            "{\n\t.reg .pred p;\n\t"
+            "mbarrier.test_wait.parity.acquire.cta.shared::cta.b64 p, [%1], %2;\n\t"
+            "selp.u32 %0, 1, 0, p;\n\t}\n"
+            : "=r"(ok)
+            : "r"(smem_u32(bar)), "r"(parity)
+            : "memory");
+    }
+    return __shfl_sync(0xffffffffu, ok, 0) != 0;
+}
+
 // The same bounded wait with a suspend-time hint: the thread sleeps up to
 // `hint_ns` per try instead of polling, for waiters whose latency matters less
 // than the issue slots they would take from the warps sharing their SM
@@ -242,24 +258,6 @@ __device__ __forceinline__ float ex2(float x) {
     float y;
     asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
     return y;
-}
-
-// 2^x on the FMA pipe, for x <= 0 (a share of the exponentials the ex2 unit
-// would otherwise serialise on: it retires 16 per clock per SM, the FMA pipe
-// 128).  Range reduction x = n + f with n = floor(x) (read off the mantissa
-// of x + 1.5*2^23 added with round-down), 2^f on [0, 1) by a cubic fitted
-// here by iteratively reweighted least squares on Chebyshev nodes for
-// relative error (max 7.6e-5, below bf16's 3.9e-3 resolution of P), then
-// 2^n applied by adding n to the exponent field.  x is clamped at -126 (the
-// result there, ~1e-38, is zero to every consumer; one step lower the
-// exponent field would underflow into the sign).
-__device__ __forceinline__ float ex2_fma(float x) {
-    x = fmaxf(x, -126.f);
-    const float t = __fadd_rd(x, 12582912.f);   // 1.5 * 2^23 + floor(x)
-    const float f = x - (t - 12582912.f);       // x - floor(x), exact
-    const float p = fmaf(fmaf(fmaf(0.0780453235f, f, 0.226037711f), f, 0.695843577f), f, 0.999924779f);
-    // (floor(x) << 23) equals (bits(t) << 23) mod 2^32: the low 9 bits of 1.5 * 2^23's pattern are zero
-    return __int_as_float(__float_as_int(p) + (__float_as_int(t) << 23));
 }
 
 // packed fp32x2 arithmetic (one instruction for two lanes of work on sm_100)
