@@ -120,8 +120,24 @@ struct BuildParams {
     ScopeMaskArgs a;
     int max_kv;      // entries before de-duplication
     int per_warp;    // ints of shared memory per warp
+    int np2;         // max_kv rounded up to a power of two (the sort buffer)
     int n_stats;     // ints of the statistics block
     int words;       // bitmap words per row
+};
+
+// x / d, with the division replaced by an exact multiply when d is a power of
+// two (the configurations' temperatures): identical results, and the selection
+// scan over ~QB/2 candidates per row stops being bound by IEEE division.
+struct Divider {
+    float d, inv;
+    bool pow2;
+    __device__ explicit Divider(float d_) : d(d_) {
+        int e;
+        const float m = frexpf(d_, &e);
+        pow2 = (m == 0.5f) && e > -125 && e < 126;    // d = 2^(e-1): 1/d is exact and normal
+        inv = pow2 ? ldexpf(1.0f, 1 - e) : 0.f;
+    }
+    __device__ __forceinline__ float operator()(float x) const { return pow2 ? __fmul_rn(x, inv) : __fdiv_rn(x, d); }
 };
 
 __device__ __forceinline__ bool better(float av, int ai, float bv, int bi) {
@@ -172,7 +188,7 @@ __device__ void select_row(const ScopeMaskArgs &a, int h, int qb, int lane, int 
     }
     const float *lrow = a.sel_logits + (int64_t)h * a.sel_head_stride + (int64_t)qb * a.sel_row_stride;
     const float *grow = a.sel_gumbel + (int64_t)h * a.sel_head_stride + (int64_t)qb * a.sel_row_stride;
-    const float tau = a.sel_tau;
+    const Divider tau(a.sel_tau);
     const int n = qb + 1;
     const bool vec = (a.QB % 4 == 0) && (a.sel_row_stride % 4 == 0) && (a.sel_head_stride % 4 == 0) &&
                      ((reinterpret_cast<uintptr_t>(a.sel_logits) & 15) == 0) &&
@@ -193,12 +209,12 @@ __device__ void select_row(const ScopeMaskArgs &a, int h, int qb, int lane, int 
 #pragma unroll
             for (int e = 0; e < 8; ++e) {
                 int kb = (e < 4) ? base + e : b2 + e - 4;
-                if (kb < n) topm_insert(v, id, M, __fadd_rn(__fdiv_rn(lv[e], tau), gv[e]), kb);
+                if (kb < n) topm_insert(v, id, M, __fadd_rn(tau(lv[e]), gv[e]), kb);
             }
         }
     } else {
         for (int kb = lane; kb < n; kb += 32) {
-            float s = __fadd_rn(__fdiv_rn(__ldg(lrow + kb), tau), __ldg(grow + kb));
+            float s = __fadd_rn(tau(__ldg(lrow + kb)), __ldg(grow + kb));
             topm_insert(v, id, M, s, kb);
         }
     }
@@ -224,9 +240,8 @@ __global__ void __launch_bounds__(kWarps * 32) build_kernel(const BuildParams P)
     extern __shared__ int smem[];
     const ScopeMaskArgs &a = P.a;
     const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5, nw = blockDim.x >> 5;
-    int *vals = smem + wid * P.per_warp;
-    int *flag = vals + P.max_kv;
-    int *outl = flag + P.max_kv;
+    int *vals = smem + wid * P.per_warp;  // [np2]: the row's window entries, sorted in place
+    int *outl = vals + P.np2;             // [max_kv]: packed list
     int *cen = outl + P.max_kv;           // [kMaxM]
     int *rad = cen + kMaxM;               // [kMaxM]
     float *alloc = reinterpret_cast<float *>(rad + kMaxM);  // [kMaxM]
@@ -277,12 +292,17 @@ __global__ void __launch_bounds__(kWarps * 32) build_kernel(const BuildParams P)
         if (a.radius_mode == 0) {
             r = a.half_active;
         } else if (a.budget_rem > 0) {
+            // the M - 1 stick fractions are independent: one lane each; only the
+            // breaking itself (two dependent roundings per stick) runs in lane 0
+            if (lane < M - 1) {
+                float u = __fdiv_rn(brow[(int64_t)lane * a.budget_m_stride], a.budget_temp);
+                alloc[lane] = __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-u)));
+            }
+            __syncwarp();
             if (lane == 0) {
                 float rem = (float)a.budget_rem;
                 for (int m = 0; m < M - 1; ++m) {
-                    float u = __fdiv_rn(brow[(int64_t)m * a.budget_m_stride], a.budget_temp);
-                    float v = __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-u)));
-                    float bb = __fmul_rn(v, rem);
+                    float bb = __fmul_rn(alloc[m], rem);
                     alloc[m] = bb;
                     rem = __fsub_rn(rem, bb);
                 }
@@ -352,35 +372,44 @@ __global__ void __launch_bounds__(kWarps * 32) build_kernel(const BuildParams P)
             }
             vals[pos] = val;
         }
+        for (int pos = n + lane; pos < P.np2; pos += 32) vals[pos] = INT_MAX;   // sorts past every block
         __syncwarp();
 
         // ---- de-duplicate and pack (model/attn_bias.py:828-837) ----
-        int first_cnt = 0;
-        for (int pos = lane; pos < n; pos += 32) {
-            int v = vals[pos];
-            int f = 1;
-            for (int q = 0; q < pos; ++q)
-                if (vals[q] == v) {
-                    f = 0;
-                    break;
+        // The reference sorts, keeps the first of each run, and stably re-sorts on
+        // (!keep, value): the unique blocks ascending, then the repeats ascending.
+        // Here: a warp bitonic sort of the entries in shared memory, then runs
+        // are found by comparing neighbours and packed with ballot prefix counts.
+        const int N2 = P.np2;
+        for (int kk = 2; kk <= N2; kk <<= 1) {
+            for (int jj = kk >> 1; jj > 0; jj >>= 1) {
+                for (int t = lane; t < (N2 >> 1); t += 32) {
+                    const int i = ((t & ~(jj - 1)) << 1) | (t & (jj - 1));   // lower element of pair t
+                    const int l = i + jj;
+                    const int x = vals[i], y = vals[l];
+                    if ((x > y) == ((i & kk) == 0)) {
+                        vals[i] = y;
+                        vals[l] = x;
+                    }
                 }
-            flag[pos] = f;
-            first_cnt += f;
-        }
-#pragma unroll
-        for (int o = 16; o; o >>= 1) first_cnt += __shfl_xor_sync(0xffffffffu, first_cnt, o);
-        const int num = first_cnt;
-        __syncwarp();
-        for (int pos = lane; pos < n; pos += 32) {
-            int v = vals[pos];
-            int f = flag[pos];
-            int dst = f ? 0 : num;
-            for (int q = 0; q < n; ++q) {
-                int vq = vals[q], fq = flag[q];
-                if (f) dst += (fq && vq < v);
-                else dst += (!fq && (vq < v || (vq == v && q < pos)));
+                __syncwarp();
             }
-            outl[dst] = v;
+        }
+        int num = 0;
+        for (int c0 = 0; c0 < n; c0 += 32) {
+            const int pos = c0 + lane;
+            const bool first = pos < n && (pos == 0 || vals[pos - 1] != vals[pos]);
+            num += __popc(__ballot_sync(0xffffffffu, first));
+        }
+        int firsts_before = 0;
+        for (int c0 = 0; c0 < n; c0 += 32) {
+            const int pos = c0 + lane;
+            const int v = pos < n ? vals[pos] : 0;
+            const bool first = pos < n && (pos == 0 || vals[pos - 1] != v);
+            const unsigned fb = __ballot_sync(0xffffffffu, first);
+            const int pre = firsts_before + __popc(fb & ((1u << lane) - 1u));
+            if (pos < n) outl[first ? pre : num + (pos - pre)] = v;
+            firsts_before += __popc(fb);
         }
         __syncwarp();
 
@@ -515,7 +544,9 @@ extern "C" int scope_mask_build(const ScopeMaskArgs *args, scope_stream_t stream
     mask::BuildParams P;
     P.a = a;
     P.max_kv = max_kv;
-    P.per_warp = 3 * max_kv + 4 * mask::kMaxM;
+    P.np2 = 32;
+    while (P.np2 < max_kv) P.np2 <<= 1;
+    P.per_warp = P.np2 + max_kv + 4 * mask::kMaxM;
     P.n_stats = (max_kv + 1) + (a.half_blocks + 1) + (std::max(1, a.half_blocks * a.M) + 1) + 1;
     P.words = (a.QB + 31) / 32;
     int nwarps = mask::kWarps;
