@@ -3,20 +3,25 @@
 // One CTA computes one 128-row query block of one head against the kv
 // blocks its list names (kv_indices, in order), flash-attention style:
 //
-//   warp 0      TMA producer: Q (+ the qk_aug dims) once, then K (+aug) / V
-//               tiles of each listed kv block into a 2-stage ring.  Tiles are
-//               addressed by block index, so the sparse gather is just the
-//               TMA coordinate.  No multicast.
-//   warp 1      tcgen05 issuer (one thread): S = Q K^T (+ Qaug Kaug^T, the
-//               spectral bias of the qk_aug mode) into TMEM, then O += P V
-//               with P read from TMEM as the A operand.  It also owns the TMEM
+//   warp 0      TMA producer: Q (+ the qk_aug dims) once, then K (+aug) and V
+//               of each listed kv block into 2-stage rings with their own
+//               barriers (K is released once the S MMA that read it is done,
+//               V once P V is).  Tiles are addressed by block index, so the
+//               sparse gather is just the TMA coordinate.  No multicast.
+//   warp 1      tcgen05 issuer (the warp waits, lane 0 issues): S = Q K^T
+//               (+ Qaug Kaug^T, the spectral bias of the qk_aug mode) into
+//               TMEM, and O += P V with P read from TMEM as the A operand, in
+//               the order their inputs become ready.  It also owns the TMEM
 //               allocation.
-//   warps 2..5  softmax: one thread per query row.  S comes out of TMEM with
+//   warps 2..9  softmax: two threads per query row (one per 64-column half,
+//               the halves trading row max and row sum through shared memory
+//               behind a bounded mbarrier).  S comes out of TMEM with
 //               tcgen05.ld, the document-causal mask is applied only on tiles
-//               that need it (diagonal, document boundary), exponentials are
-//               taken in the log2 domain, P goes back to TMEM as bf16, and the
-//               running max is only moved when it grows by more than 2^8
-//               (otherwise O would need a rescale through TMEM every tile).
+//               the producer classified as needing it (diagonal, document
+//               boundary), exponentials are taken in the log2 domain, P goes
+//               back to TMEM as bf16, and the running max is only moved when
+//               it grows by more than 2^8 (otherwise O would need a rescale
+//               through TMEM every tile).
 //
 // TMEM (256 columns per CTA, two CTAs per SM): S [0,128), O [128,192),
 // P (bf16 pairs) [192,256).  S is single buffered: the issuer starts

@@ -1,13 +1,14 @@
 // Block-sparse SCOPE attention backward on the sm_100a tensor cores.
 //
-// Three launches, all on the caller's stream:
+// Launches, all on the caller's stream:
 //   prep   delta_i = sum_d dO_i . O_i  and  lse2_i = lse_i * log2(e)   (workspace)
-//   dkv    one CTA per (head, kv block): walks the q blocks that see this kv
-//          block (the builder's q-side bitmap, ascending) and accumulates
-//          dV += P^T dO and dK += dS^T Q in TMEM.
-//   dq     one CTA per (head, q block): walks the kv list like the forward and
-//          accumulates dQ += dS K (and, for the qk_aug spectral bias, the
-//          gradient of the augmented dims, turned into dcoeff_cos /
+//   plan   per (head, kv block) the number of q blocks that see it (from the
+//          builder's q-side bitmap) and the dK/dV work items
+//   dkv    one CTA per work item (a kv block and a run of the q blocks that see
+//          it, ascending): dV += P^T dO and dK += dS^T Q in TMEM.
+//   dq     persistent, one CTA per SM walking the (head, q block) items: the kv
+//          list like the forward, dQ += dS K (and, for the qk_aug spectral bias,
+//          the gradient of the augmented dims, turned into dcoeff_cos /
 //          dcoeff_sin / dslope in the epilogue by the chain rule of
 //          scoped_medium.py:380-421).
 // dQ is computed by its own kernel rather than with atomics so every output
@@ -17,14 +18,14 @@
 // at most kChunk q tiles handled by separate CTAs, whose fp32 partial sums meet
 // in a small slot buffer that the last chunk of the row converts to bf16.
 //
-// Both kernels share one pipeline.  A 128x128 tile is processed as two
-// halves of 64 columns.  TMEM (512 columns, one CTA per SM) holds two slots of
-// {S half, dP half} (fp32, 64 + 64 columns) and the accumulators.  While the
-// eight elementwise warps (two per TMEM lane quadrant, 32 columns each) turn
-// slot u into P / dS (bf16, written back over the S and dP columns each warp
-// read, where the next MMAs read them as their A operand), the issuer runs the
-// QK^T / dO V^T MMAs of slot u+1 and the gradient MMAs of slot u-1.  Every
-// wait is bounded (SCOPE_DEVERR_TIMEOUT).
+// Both kernels share one pipeline on whole 128x128 tiles (352 threads, one CTA
+// per SM, all 512 TMEM columns): a producer warp (TMA), an S / dP issuing warp,
+// a gradient issuing warp and eight elementwise warps (two per TMEM lane
+// quadrant, 64 columns each in two chunks of 32).  S is double buffered in
+// TMEM, dP single buffered and released as soon as the elementwise warps have
+// read it; P / dS go back into the S buffer as bf16 pairs over the columns
+// the writing warp read, where the gradient MMAs read them as their A
+// operand.  Every wait is bounded (SCOPE_DEVERR_TIMEOUT).
 #include <algorithm>
 #include <cmath>
 #include <cstring>
