@@ -40,16 +40,18 @@ using namespace tc;
 
 constexpr int BM = 128;
 constexpr int HD = 64;
-constexpr int kThreads = 352;          // producer, S/dP issuer, 8 elementwise warps, gradient issuer
-constexpr int kGradWarp = 10;
-constexpr int kElem = 256;             // elementwise threads
+constexpr int kElemWarps = 16;         // four per TMEM lane quadrant, 32 tile columns each
+constexpr int kThreads = 32 * (kElemWarps + 3);   // producer, S/dP issuer, elementwise warps, gradient issuer
+constexpr int kGradWarp = kElemWarps + 2;
+constexpr int kElem = 32 * kElemWarps; // elementwise threads
 constexpr int kChunk = 64;             // max q tiles per dK/dV work item
 constexpr int kSlotCap = 128;          // max kv rows whose q list is split
 constexpr uint32_t kTmemCols = 512;
 // TMEM columns (one CTA per SM owns all 512):
 //   [0, 256)    two S buffers: S (dq) or S^T (dkv) of a 128 x 128 tile, fp32;
-//               P / dS go back into the buffer as bf16 pairs, over columns the
-//               writing warp has already read
+//               P / dS of the 16 columns [16g, 16g+16) go back into those same
+//               columns as bf16 pairs (dkv: P^T at 16g, dS^T at 16g + 8; dq: dS
+//               at 16g), so every warp writes only over columns it has read
 //   [256, 384)  DP: dP (dq) or dP^T (dkv) of the tile, fp32, one buffer
 //   [384, 448)  ACC0: dV (dkv) | dQ (dq)
 //   [448, 512)  ACC1: dK (dkv) | gradient of the qk_aug dims (dq)
@@ -61,11 +63,10 @@ constexpr float kLog2e = 1.4426950408889634f;
 
 __host__ __device__ constexpr uint32_t align1k(uint32_t x) { return (x + 1023u) & ~1023u; }
 __device__ __forceinline__ uint32_t sbuf(int b) { return (uint32_t)b * 128u; }
-// The warp of column half ch (tile columns [64ch, 64ch+64)) writes its bf16
-// pairs at buffer columns [64ch, 64ch+32): K step kk of the contraction (16
-// rows, 8 packed columns) of the TMEM A operand starts at a_col(kk).  In dkv
-// the dS^T pairs follow at +32.
-__device__ __forceinline__ uint32_t a_col(int kk) { return (uint32_t)(64 * (kk >> 2) + 8 * (kk & 3)); }
+// K step kk of the gradient contraction (16 tile columns, 8 packed TMEM
+// columns) of the TMEM A operand starts at a_col(kk); in dkv the dS^T pairs
+// follow at +8.
+__device__ __forceinline__ uint32_t a_col(int kk) { return (uint32_t)(16 * kk); }
 
 // ------------------------------------------------------------------ prep
 __global__ void prep_kernel(const __nv_bfloat16 *__restrict__ out, int64_t o_sh, int64_t o_st,
@@ -148,7 +149,7 @@ struct Ctx {
     }
 };
 
-__device__ __forceinline__ void elem_bar() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
+__device__ __forceinline__ void elem_bar() { asm volatile("bar.sync 1, %0;" ::"n"(kElem) : "memory"); }
 
 // mbarriers and small shared state of a backward CTA
 struct Bars {
@@ -158,7 +159,8 @@ struct Bars {
                                        // with resident buffer ci & 1 (elementwise arrivals)
     uint64_t full[4], empty[4];        // streamed stage ring
     uint64_t s_full[2];                // S of a tile is in its buffer
-    uint64_t p_full[2];                // P / dS are back in the buffer (elementwise arrivals)
+    uint64_t p_half[2];                // P / dS of the even 16-column chunks are back (elementwise arrivals)
+    uint64_t p_full[2];                // P / dS of every chunk are back in the buffer (elementwise arrivals)
     uint64_t s_free[2];                // the gradient MMAs that read the buffer completed
     uint64_t dp_full;                  // dP of a tile is in DP
     uint64_t dp_free;                  // the elementwise warps have read DP (elementwise arrivals)
@@ -179,6 +181,7 @@ struct Bars {
         }
         for (int i = 0; i < 2; ++i) {
             mbar_init(&s_full[i], 1);
+            mbar_init(&p_half[i], kElem);
             mbar_init(&p_full[i], kElem);
             mbar_init(&s_free[i], 1);
         }
@@ -192,48 +195,52 @@ struct Bars {
     }
 };
 
-// S and dP columns [c0, c0+32) of a slot for this thread's TMEM lane, one wait
-__device__ __forceinline__ void ld_s_dp(uint32_t ts, uint32_t tdp, float (&s)[32], float (&dp)[32]) {
-    uint32_t a[32], b[32];
-    tmem_ld32_nw(ts, a);
-    tmem_ld32_nw(tdp, b);
+// A warp's start of a tile: its 32 dP columns and the first 16 S columns of
+// this thread's TMEM lane in one wait, so dP can be released right away
+__device__ __forceinline__ void ld_tile_start(uint32_t ts, uint32_t tdp, uint32_t (&s0)[16], uint32_t (&dp0)[16],
+                                              uint32_t (&dp1)[16]) {
+    tmem_ld16(ts, s0);
+    tmem_ld16(tdp, dp0);
+    tmem_ld16(tdp + 16, dp1);
     tmem_wait_ld();
-    pin(a);
-    pin(b);
-#pragma unroll
-    for (int e = 0; e < 32; ++e) {
-        s[e] = __uint_as_float(a[e]);
-        dp[e] = __uint_as_float(b[e]);
-    }
+    pin(s0);
+    pin(dp0);
+    pin(dp1);
 }
-__device__ __forceinline__ void pack16(const float (&x)[32], uint32_t (&pk)[16]) {
-#pragma unroll
-    for (int e = 0; e < 16; ++e) pk[e] = pack_bf16(x[2 * e], x[2 * e + 1]);
+__device__ __forceinline__ void ld_cols16(uint32_t taddr, uint32_t (&r)[16]) {
+    tmem_ld16(taddr, r);
+    tmem_wait_ld();
+    pin(r);
 }
-// 32 values as 16 bf16 pairs at taddr
-__device__ __forceinline__ void st_bf16x32(uint32_t taddr, const float (&x)[32]) {
-    uint32_t pk[16];
+// 16 values as 8 bf16 pairs at taddr
+__device__ __forceinline__ void st_bf16x16(uint32_t taddr, const float (&x)[16]) {
+    uint32_t pk[8];
 #pragma unroll
-    for (int e = 0; e < 16; ++e) pk[e] = pack_bf16(x[2 * e], x[2 * e + 1]);
-    tmem_st16(taddr, pk);
+    for (int e = 0; e < 8; ++e) pk[e] = pack_bf16(x[2 * e], x[2 * e + 1]);
+    tmem_st8(taddr, pk);
 }
-// 32 fp32 accumulator columns -> 64 bytes of a bf16 row in global memory
-__device__ __forceinline__ void store_row32(uint32_t taddr, float mul, __nv_bfloat16 *dst, bool have) {
-    uint32_t o[32];
+// N (16 or 32) fp32 accumulator columns -> 2N bytes of a bf16 row in global memory
+template <int N>
+__device__ __forceinline__ void store_row(uint32_t taddr, float mul, __nv_bfloat16 *dst, bool have) {
+    uint32_t o[N];
     if (have) {
-        tmem_ld32_nw(taddr, o);
+        if constexpr (N == 32) {
+            tmem_ld32_nw(taddr, o);
+        } else {
+            tmem_ld16(taddr, o);
+        }
         tmem_wait_ld();
         pin(o);
     } else {
 #pragma unroll
-        for (int e = 0; e < 32; ++e) o[e] = 0u;
+        for (int e = 0; e < N; ++e) o[e] = 0u;
     }
-    uint32_t w[16];
+    uint32_t w[N / 2];
 #pragma unroll
-    for (int e = 0; e < 16; ++e) w[e] = pack_bf16(__uint_as_float(o[2 * e]) * mul, __uint_as_float(o[2 * e + 1]) * mul);
+    for (int e = 0; e < N / 2; ++e) w[e] = pack_bf16(__uint_as_float(o[2 * e]) * mul, __uint_as_float(o[2 * e + 1]) * mul);
     uint4 *d = reinterpret_cast<uint4 *>(dst);
 #pragma unroll
-    for (int e = 0; e < 4; ++e) d[e] = make_uint4(w[4 * e], w[4 * e + 1], w[4 * e + 2], w[4 * e + 3]);
+    for (int e = 0; e < N / 8; ++e) d[e] = make_uint4(w[4 * e], w[4 * e + 1], w[4 * e + 2], w[4 * e + 3]);
 }
 
 // Tile masking: every element of a full tile is visible; a tile whose q and kv
@@ -253,13 +260,13 @@ __device__ __forceinline__ int tile_mask_kind(int qb, int kb, bool have_docs, co
     return same_doc ? MASK_CAUSAL : MASK_DOCS;
 }
 
-// One 32-column piece of the dK/dV elementwise stage, thread = kv row j:
+// One 16-column piece of the dK/dV elementwise stage, thread = kv row j:
 // P = exp2(S * scale*log2e - lse2), dS = P (dP - delta), masked when MASKED.
 template <bool MASKED>
-__device__ __forceinline__ void dkv_piece(float (&s)[32], float (&dp)[32], const float4 *LS, const float4 *DL,
+__device__ __forceinline__ void dkv_piece(float (&s)[16], float (&dp)[16], const float4 *LS, const float4 *DL,
                                           uint64_t c2, int mk, int lim, const int32_t *docs, int i0, int doc_j) {
 #pragma unroll
-    for (int e4 = 0; e4 < 8; ++e4) {
+    for (int e4 = 0; e4 < 4; ++e4) {
         const float4 l4 = LS[e4], d4 = DL[e4];
 #pragma unroll
         for (int q2 = 0; q2 < 2; ++q2) {
@@ -286,13 +293,13 @@ __device__ __forceinline__ void dkv_piece(float (&s)[32], float (&dp)[32], const
     }
 }
 
-// One 32-column piece of the dQ elementwise stage, thread = q row i; dS -> s.
+// One 16-column piece of the dQ elementwise stage, thread = q row i; dS -> s.
 template <bool MASKED>
-__device__ __forceinline__ void dq_piece(float (&s)[32], const float (&dp)[32], uint64_t c2, uint64_t nl2,
+__device__ __forceinline__ void dq_piece(float (&s)[16], const float (&dp)[16], uint64_t c2, uint64_t nl2,
                                          uint64_t nd2, int mk, int lim, bool bad, const int32_t *docs, int j0,
                                          int doc_i) {
 #pragma unroll
-    for (int e = 0; e < 32; e += 2) {
+    for (int e = 0; e < 16; e += 2) {
         const float2 x = f2_unpack(ffma2(f2_pack(s[e], s[e + 1]), c2, nl2));
         float p0 = ex2(x.x), p1 = ex2(x.y);
         if (MASKED) {
@@ -418,10 +425,22 @@ __global__ void __launch_bounds__(kThreads, 1) dkv_kernel(const __grid_constant_
             for (int t = 0; ok && t < nq; ++t) {
                 const int st = t % NST, b = t & 1;
                 if (!cx.waitw(&B.full[st], (t / NST) & 1)) { ok = false; break; }
+                const uint32_t sb = smem_u32(smem + L::STAGE0 + st * L::STAGE);
+                // dP^T = V dO^T first: the elementwise warps release dP^T of the previous tile
+                // as they start it, while S^T waits for the gradient MMAs of tile t-2
+                if (t >= 1 && !cx.waitw(&B.dp_free, (t - 1) & 1)) { ok = false; break; }
+                tc_fence_after();
+                if (lane == 0) {
+#pragma unroll
+                    for (int kk = 0; kk < 4; ++kk)
+                        mma_ss(tmem + DPC, kmajor_desc(sV + kk * 32, 128), kmajor_desc(sb + L::SDO + kk * 32, 128), idS,
+                               kk > 0);
+                    tc_commit(&B.dp_full);
+                }
+                __syncwarp();
+                // S^T = K Q^T (+ Kaug Qaug^T): 128 kv rows x 128 q columns
                 if (t >= 2 && !cx.waitw(&B.s_free[b], ((t >> 1) - 1) & 1)) { ok = false; break; }
                 tc_fence_after();
-                const uint32_t sb = smem_u32(smem + L::STAGE0 + st * L::STAGE);
-                // S^T = K Q^T (+ Kaug Qaug^T): 128 kv rows x 128 q columns
                 if (lane == 0) {
 #pragma unroll
                     for (int kk = 0; kk < 4; ++kk)
@@ -432,17 +451,6 @@ __global__ void __launch_bounds__(kThreads, 1) dkv_kernel(const __grid_constant_
                         mma_ss(tmem + sbuf(b), kmajor_desc(sKA + a * L::ATILE, 32),
                                kmajor_desc(sb + L::SQA + a * L::ATILE, 32), idS, 1);
                     tc_commit(&B.s_full[b]);
-                }
-                __syncwarp();
-                // dP^T = V dO^T, once the elementwise warps have read dP^T of the previous tile
-                if (t >= 1 && !cx.waitw(&B.dp_free, (t - 1) & 1)) { ok = false; break; }
-                tc_fence_after();
-                if (lane == 0) {
-#pragma unroll
-                    for (int kk = 0; kk < 4; ++kk)
-                        mma_ss(tmem + DPC, kmajor_desc(sV + kk * 32, 128), kmajor_desc(sb + L::SDO + kk * 32, 128), idS,
-                               kk > 0);
-                    tc_commit(&B.dp_full);
                 }
                 __syncwarp();
             }
@@ -458,24 +466,29 @@ __global__ void __launch_bounds__(kThreads, 1) dkv_kernel(const __grid_constant_
             bool ok = true;
             for (int t = 0; ok && t < nq; ++t) {
                 const int st = t % NST, b = t & 1;
-                if (!cx.waitw(&B.p_full[b], (t >> 1) & 1)) { ok = false; break; }
-                tc_fence_after();
                 const uint32_t sb = smem_u32(smem + L::STAGE0 + st * L::STAGE);
-                // dV += P^T dO, dK += dS^T Q over the tile's 128 q rows
-                if (lane == 0) {
+                // dV += P^T dO, dK += dS^T Q over the tile's 128 q rows: the even K steps
+                // (16-column chunks) as soon as every warp has written them, then the odd
+                for (int half = 0; half < 2; ++half) {
+                    if (!cx.waitw(half ? &B.p_full[b] : &B.p_half[b], (t >> 1) & 1)) { ok = false; break; }
+                    tc_fence_after();
+                    if (lane == 0) {
 #pragma unroll
-                    for (int kk = 0; kk < 8; ++kk)
-                        mma_ts(tmem + ACC0, tmem + sbuf(b) + a_col(kk), mnmajor128_desc(sb + L::SDO + kk * 2048), idG,
-                               (t > 0 || kk > 0) ? 1u : 0u);
-#pragma unroll
-                    for (int kk = 0; kk < 8; ++kk)
-                        mma_ts(tmem + ACC1, tmem + sbuf(b) + a_col(kk) + 32, mnmajor128_desc(sb + L::SQ + kk * 2048), idG,
-                               (t > 0 || kk > 0) ? 1u : 0u);
-                    // commit only arrivals someone waits for
-                    if (t + 2 < nq) tc_commit(&B.s_free[b]);
-                    if (t + NST < nq) tc_commit(&B.empty[st]);
+                        for (int k2 = 0; k2 < 4; ++k2) {
+                            const int kk = 2 * k2 + half;
+                            const uint32_t acc = (t > 0 || kk > 0) ? 1u : 0u;
+                            mma_ts(tmem + ACC0, tmem + sbuf(b) + a_col(kk), mnmajor128_desc(sb + L::SDO + kk * 2048),
+                                   idG, acc);
+                            mma_ts(tmem + ACC1, tmem + sbuf(b) + a_col(kk) + 8, mnmajor128_desc(sb + L::SQ + kk * 2048),
+                                   idG, acc);
+                        }
+                        // commit only arrivals someone waits for
+                        if (half && t + 2 < nq) tc_commit(&B.s_free[b]);
+                        if (half && t + NST < nq) tc_commit(&B.empty[st]);
+                    }
+                    __syncwarp();
                 }
-                __syncwarp();
+                if (!ok) break;
             }
             if (ok && lane == 0) tc_commit(&B.acc_done);
             if (!ok) cx.give_up();
@@ -483,9 +496,9 @@ __global__ void __launch_bounds__(kThreads, 1) dkv_kernel(const __grid_constant_
             mbar_wait(&B.drain[1], 0, 500000000ull);
         }
     } else {
-        // ---------------- elementwise: thread = kv row c, tile columns [64ch, 64ch+64) in two chunks of 32
+        // ---------------- elementwise: thread = kv row c, tile columns [32qc, 32qc+32) in two chunks of 16
         const int quad = warp & 3;
-        const int ch = (warp - 2) >> 2;
+        const int qc = (warp - 2) >> 2;
         const int c = quad * 32 + lane;
         const int j = kb * BM + c;
         const uint32_t lb = (uint32_t)(quad * 32) << 16;
@@ -501,64 +514,62 @@ __global__ void __launch_bounds__(kThreads, 1) dkv_kernel(const __grid_constant_
             if (!cx.waitw(&B.s_full[b], (t >> 1) & 1) || !cx.waitw(&B.dp_full, t & 1)) { alive = false; break; }
             tc_fence_after();
             const uint8_t *sbp = smem + L::STAGE0 + st * L::STAGE;
-            const uint32_t tb = tmem + lb + sbuf(b) + ch * 64;
-            uint32_t ds0[16];
+            uint32_t rs[16], rp0[16], rp1[16];
+            ld_tile_start(tmem + lb + sbuf(b) + qc * 32, tmem + lb + DPC + qc * 32, rs, rp0, rp1);
+            tc_fence_before();
+            mbar_arrive_warp(&B.dp_free);           // this warp's dP^T columns are in registers
 #pragma unroll
             for (int cc = 0; cc < 2; ++cc) {
-                float s[32], dp[32];
-                ld_s_dp(tb + cc * 32, tmem + lb + DPC + ch * 64 + cc * 32, s, dp);
-                if (cc == 1) {
-                    tc_fence_before();
-                    mbar_arrive(&B.dp_free);        // this warp's dP^T columns are in registers
+                const int col0 = qc * 32 + cc * 16;  // q row within the tile of the chunk's first column
+                const uint32_t tc = tmem + lb + sbuf(b) + col0;
+                if (cc == 1) ld_cols16(tc, rs);
+                float s[16], dp[16];
+#pragma unroll
+                for (int e = 0; e < 16; ++e) {
+                    s[e] = __uint_as_float(rs[e]);
+                    dp[e] = __uint_as_float(cc ? rp1[e] : rp0[e]);
                 }
-                const int col0 = ch * 64 + cc * 32;  // q row within the tile of the first column
                 const float4 *LS = reinterpret_cast<const float4 *>(sbp + L::SLSE) + col0 / 4;
                 const float4 *DL = reinterpret_cast<const float4 *>(sbp + L::SDEL) + col0 / 4;
                 const int i0 = qb * BM + col0;
                 const int lim = j - i0;              // column e visible iff e >= lim (causal: j <= i)
                 if (mk == MASK_FULL) dkv_piece<false>(s, dp, LS, DL, c2, mk, lim, p.docs, i0, doc_j);
                 else dkv_piece<true>(s, dp, LS, DL, c2, mk, lim, p.docs, i0, doc_j);
-                uint32_t pk[16];
-                pack16(s, pk);
-                tmem_st16(tb + cc * 16, pk);         // P^T pairs over columns this warp has read
+                st_bf16x16(tc, s);                   // P^T pairs, then dS^T pairs, over the chunk's own columns
+                st_bf16x16(tc + 8, dp);
                 if (cc == 0) {
-                    pack16(dp, ds0);                 // dS^T pairs of chunk 0 wait until chunk 1 is read
-                } else {
-                    pack16(dp, pk);
-                    tmem_st16(tb + 32, ds0);
-                    tmem_st16(tb + 48, pk);
+                    tmem_wait_st();
+                    tc_fence_before();
+                    mbar_arrive_warp(&B.p_half[b]);
                 }
             }
             tmem_wait_st();
             tc_fence_before();
-            mbar_arrive(&B.p_full[b]);
+            mbar_arrive_warp(&B.p_full[b]);
         }
         bool have = false;
         if (alive && nq > 0) {
             have = cx.waitw(&B.acc_done, 0);
             tc_fence_after();
         }
-        // dV from ACC0 (column half 0 warps), dK * scale from ACC1 (column half 1 warps)
-        const uint32_t acc = tmem + lb + (ch == 0 ? ACC0 : ACC1);
-        const float mul = ch == 0 ? 1.f : p.scale;
-        __nv_bfloat16 *dst = ch == 0 ? p.g1 + (int64_t)h * p.g1_sh + (int64_t)j * p.g1_st
-                                     : p.g0 + (int64_t)h * p.g0_sh + (int64_t)j * p.g0_st;
+        // dV from ACC0 (quarters 0, 1), dK * scale from ACC1 (quarters 2, 3): 32 columns per warp
+        const int half = qc >> 1, c32 = (qc & 1) * 32;
+        const uint32_t acc = tmem + lb + (half == 0 ? ACC0 : ACC1) + c32;
+        const float mul = half == 0 ? 1.f : p.scale;
+        __nv_bfloat16 *dst = (half == 0 ? p.g1 + (int64_t)h * p.g1_sh + (int64_t)j * p.g1_st
+                                        : p.g0 + (int64_t)h * p.g0_sh + (int64_t)j * p.g0_st) + c32;
         if (slot < 0) {
-            store_row32(acc, mul, dst, have);
-            store_row32(acc + 32, mul, dst + 32, have);
+            store_row<32>(acc, mul, dst, have);
         } else {
             // a chunk of a split row: add into the row's fp32 slot; the last chunk writes bf16
-            float *part = p.plan.partial + ((size_t)slot * BM + c) * 128 + ch * 64;
+            float *part = p.plan.partial + ((size_t)slot * BM + c) * 128 + qc * 32;
             if (have) {
+                uint32_t o[32];
+                tmem_ld32_nw(acc, o);
+                tmem_wait_ld();
+                pin(o);
 #pragma unroll
-                for (int hh = 0; hh < 2; ++hh) {
-                    uint32_t o[32];
-                    tmem_ld32_nw(acc + hh * 32, o);
-                    tmem_wait_ld();
-                    pin(o);
-#pragma unroll
-                    for (int e = 0; e < 32; ++e) atomicAdd(part + hh * 32 + e, __uint_as_float(o[e]) * mul);
-                }
+                for (int e = 0; e < 32; ++e) atomicAdd(part + e, __uint_as_float(o[e]) * mul);
             }
             __threadfence();
             elem_bar();
@@ -569,12 +580,12 @@ __global__ void __launch_bounds__(kThreads, 1) dkv_kernel(const __grid_constant_
             elem_bar();
             if (B.last_flag) {
                 __threadfence();
-                uint32_t w[32];
+                uint32_t w[16];
 #pragma unroll
-                for (int e = 0; e < 32; ++e) w[e] = pack_bf16(__ldcg(part + 2 * e), __ldcg(part + 2 * e + 1));
+                for (int e = 0; e < 16; ++e) w[e] = pack_bf16(__ldcg(part + 2 * e), __ldcg(part + 2 * e + 1));
                 uint4 *d = reinterpret_cast<uint4 *>(dst);
 #pragma unroll
-                for (int e = 0; e < 8; ++e) d[e] = make_uint4(w[4 * e], w[4 * e + 1], w[4 * e + 2], w[4 * e + 3]);
+                for (int e = 0; e < 4; ++e) d[e] = make_uint4(w[4 * e], w[4 * e + 1], w[4 * e + 2], w[4 * e + 3]);
             }
         }
     }
@@ -686,22 +697,20 @@ template <int DA>
 struct QL {
     static constexpr int NA = DA / 16;
     static constexpr int KM = DA > 0 ? DA / 2 : 1;                 // coefficients per row, K <= DA / 2
+    static constexpr int KM4 = (KM + 3) / 4;                        // per elementwise warp of a quadrant
     static constexpr uint32_t TILE = BM * HD * 2, ATILE = BM * 16 * 2;
     static constexpr uint32_t Q = 0, QA = TILE, DO = align1k(TILE + NA * ATILE);
     static constexpr uint32_t TAB = DO + TILE;                       // bf16 [2][KM][128]: cos rows, sin rows
     static constexpr uint32_t RESB = align1k(TAB + (NA > 0 ? KM * 512 : 0));
-    static constexpr uint32_t SCRATCH = (uint32_t)(DA > 0 ? DA : 1) * 2 * BM * 4;   // epilogue, inside a buffer
-    static_assert(SCRATCH <= RESB, "epilogue scratch must fit in a resident buffer");
     static constexpr uint32_t STAGE0 = 2 * RESB;
     static constexpr uint32_t SK = 0, SKA = TILE, SV = align1k(TILE + NA * ATILE);
     static constexpr uint32_t STAGE = SV + TILE;
-    static constexpr uint32_t EXTRA = 1024 + 512 + 1024;            // barriers, slope partials, base alignment
+    static constexpr uint32_t EXTRA = 1024 + 1024;                  // barriers, base alignment
     static constexpr int NST = STAGE0 + 4 * STAGE + EXTRA <= kSmemBudget
                                    ? 4
                                    : (STAGE0 + 3 * STAGE + EXTRA <= kSmemBudget ? 3 : 2);
     static constexpr uint32_t BAR = STAGE0 + NST * STAGE;
-    static constexpr uint32_t SLOPE = align1k(BAR + sizeof(Bars));   // float[128]: slope partials of column half 1
-    static constexpr uint32_t TOTAL = SLOPE + 512;
+    static constexpr uint32_t TOTAL = BAR + sizeof(Bars);
     static constexpr uint32_t RES_BYTES = 2 * TILE + NA * ATILE;
     static constexpr uint32_t KV_BYTES = 2 * TILE + NA * ATILE;
     static_assert(TOTAL + 1024 <= kSmemBudget, "shared memory");
@@ -710,11 +719,10 @@ struct QL {
 template <int DA>
 __global__ void __launch_bounds__(kThreads, 1) dq_kernel(const __grid_constant__ Maps maps, const Params p) {
     using L = QL<DA>;
-    constexpr int NA = L::NA, NST = L::NST, KM = L::KM;
+    constexpr int NA = L::NA, NST = L::NST, KM = L::KM, KM4 = L::KM4;
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
     Bars &B = *reinterpret_cast<Bars *>(smem + L::BAR);
-    float *slope_part = reinterpret_cast<float *>(smem + L::SLOPE);
     Ctx cx{&B.abort_flag, p.err};
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -802,10 +810,22 @@ __global__ void __launch_bounds__(kThreads, 1) dq_kernel(const __grid_constant__
             for (int jj = 0; jj < n; ++jj, ++gt) {
                 const int st = gt % NST, b = gt & 1;
                 if (!cx.waitw(&B.full[st], (gt / NST) & 1)) { ok = false; break; }
+                const uint32_t sb = smem_u32(smem + L::STAGE0 + st * L::STAGE);
+                // dP = dO V^T first: the elementwise warps release dP of the previous tile as
+                // they start it, while S waits for the gradient MMAs of tile gt-2
+                if (gt >= 1 && !cx.waitw(&B.dp_free, (gt - 1) & 1)) { ok = false; break; }
+                tc_fence_after();
+                if (lane == 0) {
+#pragma unroll
+                    for (int kk = 0; kk < 4; ++kk)
+                        mma_ss(tmem + DPC, kmajor_desc(sDO + kk * 32, 128), kmajor_desc(sb + L::SV + kk * 32, 128), idS,
+                               kk > 0);
+                    tc_commit(&B.dp_full);
+                }
+                __syncwarp();
+                // S = Q K^T (+ Qaug Kaug^T): 128 q rows x 128 kv columns
                 if (gt >= 2 && !cx.waitw(&B.s_free[b], ((gt >> 1) - 1) & 1)) { ok = false; break; }
                 tc_fence_after();
-                const uint32_t sb = smem_u32(smem + L::STAGE0 + st * L::STAGE);
-                // S = Q K^T (+ Qaug Kaug^T): 128 q rows x 128 kv columns
                 if (lane == 0) {
 #pragma unroll
                     for (int kk = 0; kk < 4; ++kk)
@@ -816,17 +836,6 @@ __global__ void __launch_bounds__(kThreads, 1) dq_kernel(const __grid_constant__
                         mma_ss(tmem + sbuf(b), kmajor_desc(sQA + a * L::ATILE, 32),
                                kmajor_desc(sb + L::SKA + a * L::ATILE, 32), idS, 1);
                     tc_commit(&B.s_full[b]);
-                }
-                __syncwarp();
-                // dP = dO V^T, once the elementwise warps have read dP of the previous tile
-                if (gt >= 1 && !cx.waitw(&B.dp_free, (gt - 1) & 1)) { ok = false; break; }
-                tc_fence_after();
-                if (lane == 0) {
-#pragma unroll
-                    for (int kk = 0; kk < 4; ++kk)
-                        mma_ss(tmem + DPC, kmajor_desc(sDO + kk * 32, 128), kmajor_desc(sb + L::SV + kk * 32, 128), idS,
-                               kk > 0);
-                    tc_commit(&B.dp_full);
                 }
                 __syncwarp();
             }
@@ -849,31 +858,37 @@ __global__ void __launch_bounds__(kThreads, 1) dq_kernel(const __grid_constant__
             const int n = p.kv_num[(int64_t)h * p.QB + qb];
             for (int jj = 0; jj < n; ++jj, ++gt) {
                 const int st = gt % NST, b = gt & 1;
-                if (!cx.waitw(&B.p_full[b], (gt >> 1) & 1)) { ok = false; break; }
-                // the first MMA of an item overwrites the accumulators: the previous
-                // item's epilogue must have read them
-                if (jj == 0 && ci >= 1 && !cx.waitw(&B.acc_free[(ci - 1) & 1], ((ci - 1) >> 1) & 1)) {
-                    ok = false;
-                    break;
-                }
-                tc_fence_after();
                 const uint32_t sb = smem_u32(smem + L::STAGE0 + st * L::STAGE);
-                // dQ += dS K (+ dQaug += dS Kaug) over the tile's 128 kv rows
-                if (lane == 0) {
-#pragma unroll
-                    for (int kk = 0; kk < 8; ++kk)
-                        mma_ts(tmem + ACC0, tmem + sbuf(b) + a_col(kk), mnmajor128_desc(sb + L::SK + kk * 2048), idG,
-                               (jj > 0 || kk > 0) ? 1u : 0u);
-                    if (NA > 0) {
-#pragma unroll
-                        for (int kk = 0; kk < 8; ++kk)
-                            mma_ts(tmem + ACC1, tmem + sbuf(b) + a_col(kk), mnmajor32_desc(sb + L::SKA + kk * 512), idA,
-                                   (jj > 0 || kk > 0) ? 1u : 0u);
+                // dQ += dS K (+ dQaug += dS Kaug) over the tile's 128 kv rows: the even K
+                // steps as soon as every warp has written them, then the odd
+                for (int half = 0; half < 2; ++half) {
+                    if (!cx.waitw(half ? &B.p_full[b] : &B.p_half[b], (gt >> 1) & 1)) { ok = false; break; }
+                    // the first MMA of an item overwrites the accumulators: the previous
+                    // item's epilogue must have read them
+                    if (!half && jj == 0 && ci >= 1 && !cx.waitw(&B.acc_free[(ci - 1) & 1], ((ci - 1) >> 1) & 1)) {
+                        ok = false;
+                        break;
                     }
-                    tc_commit(&B.s_free[b]);
-                    tc_commit(&B.empty[st]);
+                    tc_fence_after();
+                    if (lane == 0) {
+#pragma unroll
+                        for (int k2 = 0; k2 < 4; ++k2) {
+                            const int kk = 2 * k2 + half;
+                            const uint32_t acc = (jj > 0 || kk > 0) ? 1u : 0u;
+                            mma_ts(tmem + ACC0, tmem + sbuf(b) + a_col(kk), mnmajor128_desc(sb + L::SK + kk * 2048),
+                                   idG, acc);
+                            if (NA > 0)
+                                mma_ts(tmem + ACC1, tmem + sbuf(b) + a_col(kk), mnmajor32_desc(sb + L::SKA + kk * 512),
+                                       idA, acc);
+                        }
+                        if (half) {
+                            tc_commit(&B.s_free[b]);
+                            tc_commit(&B.empty[st]);
+                        }
+                    }
+                    __syncwarp();
                 }
-                __syncwarp();
+                if (!ok) break;
             }
             if (!ok) break;
             if (lane == 0) tc_commit(&B.acc_done);   // every item, so the epilogue's phases stay in step
@@ -883,9 +898,9 @@ __global__ void __launch_bounds__(kThreads, 1) dq_kernel(const __grid_constant__
         if (lane == 0) tc_commit(&B.drain[1]);
         mbar_wait(&B.drain[1], 0, 500000000ull);
     } else {
-        // ---------------- elementwise: thread = q row i, tile columns [64ch, 64ch+64) in two chunks of 32
+        // ---------------- elementwise: thread = q row i, tile columns [32qc, 32qc+32) in two chunks of 16
         const int quad = warp & 3;
-        const int ch = (warp - 2) >> 2;
+        const int qc = (warp - 2) >> 2;
         const int r = quad * 32 + lane;
         const uint32_t lb = (uint32_t)(quad * 32) << 16;
         const bool have_docs = p.docs != nullptr;
@@ -918,56 +933,86 @@ __global__ void __launch_bounds__(kThreads, 1) dq_kernel(const __grid_constant__
                 const int mk = B.stage_mk[st];
                 if (!cx.waitw(&B.s_full[b], (gt >> 1) & 1) || !cx.waitw(&B.dp_full, gt & 1)) { alive = false; break; }
                 tc_fence_after();
-                const uint32_t tb = tmem + lb + sbuf(b) + ch * 64;
+                uint32_t rs[16], rp0[16], rp1[16];
+                ld_tile_start(tmem + lb + sbuf(b) + qc * 32, tmem + lb + DPC + qc * 32, rs, rp0, rp1);
+                tc_fence_before();
+                mbar_arrive_warp(&B.dp_free);       // this warp's dP columns are in registers
 #pragma unroll
                 for (int cc = 0; cc < 2; ++cc) {
-                    float s[32], dp[32];
-                    ld_s_dp(tb + cc * 32, tmem + lb + DPC + ch * 64 + cc * 32, s, dp);
-                    if (cc == 1) {
-                        tc_fence_before();
-                        mbar_arrive(&B.dp_free);        // this warp's dP columns are in registers
+                    const int col0 = qc * 32 + cc * 16;
+                    const uint32_t tc = tmem + lb + sbuf(b) + col0;
+                    if (cc == 1) ld_cols16(tc, rs);
+                    float s[16], dp[16];
+#pragma unroll
+                    for (int e = 0; e < 16; ++e) {
+                        s[e] = __uint_as_float(rs[e]);
+                        dp[e] = __uint_as_float(cc ? rp1[e] : rp0[e]);
                     }
-                    const int j0 = kb * BM + ch * 64 + cc * 32;
+                    const int j0 = kb * BM + col0;
                     const int lim = i - j0;              // column e visible iff e <= lim (causal: j <= i)
                     if (mk == MASK_FULL) dq_piece<false>(s, dp, c2, nl2, nd2, mk, lim, bad, p.docs, j0, doc_i);
                     else dq_piece<true>(s, dp, c2, nl2, nd2, mk, lim, bad, p.docs, j0, doc_i);
                     if (slope_acc && !bad) {
 #pragma unroll
-                        for (int e = 0; e < 32; ++e) {
+                        for (int e = 0; e < 16; ++e) {
                             // the value scope_qk_aug_prepare stored: bf16(fp32(j) * s)
                             const float kpos =
                                 __bfloat162float(__float2bfloat16_rn(__fmul_rn((float)(j0 + e), p.s_aug)));
                             gsl = fmaf(s[e], kpos - kpos_i, gsl);
                         }
                     }
-                    st_bf16x32(tb + cc * 16, s);         // dS pairs over columns this warp has read
+                    st_bf16x16(tc, s);                   // dS pairs over the chunk's own columns
+                    if (cc == 0) {
+                        tmem_wait_st();
+                        tc_fence_before();
+                        mbar_arrive_warp(&B.p_half[b]);
+                    }
                 }
                 tmem_wait_st();
                 tc_fence_before();
-                mbar_arrive(&B.p_full[b]);
+                mbar_arrive_warp(&B.p_full[b]);
             }
             if (!alive) break;
             // ---------------- epilogue of the item
             if (!cx.waitw(&B.acc_done, ci & 1)) { alive = false; break; }
             tc_fence_after();
             const bool have = n > 0;
-            // dQ: each column half stores 32 of the 64 columns
-            store_row32(tmem + lb + ACC0 + ch * 32, p.scale,
-                        p.g0 + (int64_t)h * p.g0_sh + (int64_t)i * p.g0_st + ch * 32, have);
+            // dQ: each of the quadrant's four warps stores 16 of the 64 columns
+            store_row<16>(tmem + lb + ACC0 + qc * 16, p.scale,
+                          p.g0 + (int64_t)h * p.g0_sh + (int64_t)i * p.g0_st + qc * 16, have);
             if (NA > 0 && p.dcoeff_cos) {
                 // gradient of the augmented dims -> coefficients (q_aug = s [A c + B s', A s' - B c, -slope]);
-                // the two warps of a quadrant split the K coefficients
-                if (ch == 1) slope_part[r] = gsl;
+                // the four warps of a quadrant split the K coefficients, reading the two
+                // accumulator columns (k, K + k) of each coefficient k directly
                 const int K = p.K;
-                const int kh = (K + 1) >> 1;
-                const int k0 = ch == 0 ? 0 : kh, nk = ch == 0 ? kh : K - kh;
-                float cv[KM], sv[KM];
+                const int kq = (K + 3) >> 2;
+                const int k0 = qc * kq, nk = max(0, min(kq, K - k0));
+                float cv[KM4], sv[KM4], g0[KM4], g1[KM4];
+                {
+                    uint32_t o0[KM4], o1[KM4];
+#pragma unroll
+                    for (int e = 0; e < KM4; ++e) {
+                        o0[e] = o1[e] = 0u;
+                        if (have && e < nk) {
+                            tmem_ld1(tmem + lb + ACC1 + k0 + e, o0[e]);
+                            tmem_ld1(tmem + lb + ACC1 + K + k0 + e, o1[e]);
+                        }
+                    }
+                    tmem_wait_ld();
+                    pin(o0);
+                    pin(o1);
+#pragma unroll
+                    for (int e = 0; e < KM4; ++e) {
+                        g0[e] = __uint_as_float(o0[e]) * p.scale;
+                        g1[e] = __uint_as_float(o1[e]) * p.scale;
+                    }
+                }
                 if (tab && have) {
                     // the producer staged this item's table rows with its resident tiles
                     const bool ok = cx.waitw(&B.res_full[rb], (ci >> 1) & 1);
                     const uint16_t *tc = reinterpret_cast<const uint16_t *>(res + L::TAB);
 #pragma unroll
-                    for (int e = 0; e < KM; ++e) {
+                    for (int e = 0; e < KM4; ++e) {
                         if (e < nk) {
                             cv[e] = ok ? bf16_to_f32(tc[(k0 + e) * BM + r]) : 0.f;
                             sv[e] = ok ? bf16_to_f32(tc[(KM + k0 + e) * BM + r]) : 0.f;
@@ -975,65 +1020,36 @@ __global__ void __launch_bounds__(kThreads, 1) dq_kernel(const __grid_constant__
                     }
                 } else {
 #pragma unroll
-                    for (int e = 0; e < KM; ++e) {          // independent table loads, issued together
+                    for (int e = 0; e < KM4; ++e) {          // independent table loads, issued together
                         if (e < nk) {
                             cv[e] = bf16_to_f32(p.cos_tab[(int64_t)(k0 + e) * p.tab_len + i]);
                             sv[e] = bf16_to_f32(p.sin_tab[(int64_t)(k0 + e) * p.tab_len + i]);
                         }
                     }
                 }
-                elem_bar();   // every table read is done before the scratch overwrites the buffer
-                // this thread's aug-gradient row through shared memory (indexed by the runtime
-                // K), column-major so a warp's accesses hit distinct banks; the item's resident
-                // buffer is idle once its MMAs completed and stays ours until acc_free
-                float *grow = reinterpret_cast<float *>(res) + ch * BM + r;   // element d at grow[d * 2 * BM]
-#pragma unroll
-                for (int a = 0; a < NA; ++a) {
-                    uint32_t o[16];
-                    if (have) {
-                        tmem_ld16(tmem + lb + ACC1 + a * 16, o);
-                        tmem_wait_ld();
-                        pin(o);
-                    } else {
-#pragma unroll
-                        for (int e = 0; e < 16; ++e) o[e] = 0u;
-                    }
-#pragma unroll
-                    for (int e = 0; e < 16; ++e) grow[(a * 16 + e) * 2 * BM] = __uint_as_float(o[e]) * p.scale;
-                }
-                float dc[KM], ds[KM];
-#pragma unroll
-                for (int e = 0; e < KM; ++e) {
-                    if (e < nk) {
-                        const float g0 = grow[(k0 + e) * 2 * BM], g1 = grow[(K + k0 + e) * 2 * BM];
-                        dc[e] = p.s_aug * (g0 * cv[e] + g1 * sv[e]);
-                        ds[e] = p.s_aug * (g0 * sv[e] - g1 * cv[e]);
-                    }
-                }
                 float *oc = p.dcoeff_cos + hrow * K + k0, *os = p.dcoeff_sin + hrow * K + k0;
-                if (((K | k0 | nk) & 3) == 0) {
 #pragma unroll
-                    for (int e = 0; e < KM; e += 4) {
-                        if (e < nk) {
-                            *reinterpret_cast<float4 *>(oc + e) = make_float4(dc[e], dc[e + 1], dc[e + 2], dc[e + 3]);
-                            *reinterpret_cast<float4 *>(os + e) = make_float4(ds[e], ds[e + 1], ds[e + 2], ds[e + 3]);
-                        }
-                    }
-                } else {
-#pragma unroll
-                    for (int e = 0; e < KM; ++e) {
-                        if (e < nk) {
-                            oc[e] = dc[e];
-                            os[e] = ds[e];
-                        }
+                for (int e = 0; e < KM4; ++e) {
+                    if (e < nk) {
+                        oc[e] = p.s_aug * (g0[e] * cv[e] + g1[e] * sv[e]);
+                        os[e] = p.s_aug * (g0[e] * sv[e] - g1[e] * cv[e]);
                     }
                 }
-                // (read between the two barriers: the next item's write comes after the second)
-                if (ch == 0 && slope_acc) p.dslope[hrow] = -p.s_aug * ((gsl + slope_part[r]) * p.scale);
-                elem_bar();
+                if (slope_acc) {
+                    // the quadrant's four partial sums meet in shared memory, in the item's Q
+                    // tile (idle once its MMAs completed, ours until acc_free); the second
+                    // barrier keeps every read before the buffer is released
+                    float *slope_part = reinterpret_cast<float *>(res + L::Q);
+                    if (qc > 0) slope_part[(qc - 1) * BM + r] = gsl;
+                    elem_bar();
+                    if (qc == 0)
+                        p.dslope[hrow] =
+                            -p.s_aug * ((gsl + slope_part[r] + slope_part[BM + r] + slope_part[2 * BM + r]) * p.scale);
+                    elem_bar();
+                }
             }
             tc_fence_before();
-            mbar_arrive(&B.acc_free[rb]);   // accumulators read, resident buffer rb released
+            mbar_arrive_warp(&B.acc_free[rb]);   // accumulators read, resident buffer rb released
         }
     }
     __syncwarp();   // every warp reaches the CTA barrier converged (the producer ran on lane 0 alone)

@@ -28,6 +28,15 @@ __device__ __forceinline__ void fence_mbar_init() {
 __device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
     asm volatile("mbarrier.arrive.release.cta.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
+// One arrival per thread of the calling warp, made by lane 0 after the warp
+// synchronised (bar.warp.sync orders the lanes' prior memory operations, and
+// tcgen05 operations fenced with tcgen05.fence::before_thread_sync, before it).
+__device__ __forceinline__ void mbar_arrive_warp(uint64_t *bar) {
+    __syncwarp();
+    if ((threadIdx.x & 31) == 0)
+        asm volatile("mbarrier.arrive.release.cta.shared::cta.b64 _, [%0], 32;" ::"r"(smem_u32(bar)) : "memory");
+    __syncwarp();
+}
 __device__ __forceinline__ void mbar_expect_tx(uint64_t *bar, uint32_t bytes) {
     asm volatile("mbarrier.arrive.expect_tx.release.cta.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)),
                  "r"(bytes)
@@ -214,6 +223,9 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
         "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
         : SCOPE_R8(0), SCOPE_R8(8)
         : "r"(taddr));
+}
+__device__ __forceinline__ void tmem_ld1(uint32_t taddr, uint32_t &r) {
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x1.b32 {%0}, [%1];" : "=r"(r) : "r"(taddr));
 }
 __device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&r)[16]) {
     asm volatile(
