@@ -442,15 +442,18 @@ def main():
                 "achieved": ach, "peak": bf16, "unit": "TFLOP/s"}
     roof["frac"] = roof["achieved"] / roof["peak"]
     roof["peak_source"] = f"{src} (MEASURED_PEAKS.json burst)" if src == "measured" else "fallback"
-    # DRAM bytes (read + write) per active block pair from one ncu capture of the
-    # full C3 step (profiles/c3_step_launch_list.md), scaled to this launch's pairs
+    # DRAM bytes (read + write) per active block pair from ncu captures of the
+    # attention kernels on C3 with 4 of its 16 heads (59,741 pairs;
+    # profiles/attn_kernels_c3_4heads.md; the builder and the backward's prep
+    # kernel from the full C3 step, profiles/c3_step_launch_list.md), scaled to
+    # this launch's pairs
     if dom == 0:
         roof["traffic"] = 0.073e9 * wl.hp / 16           # mask::build_kernel, per head
     else:
-        per_pair = 1.693e9 / 238859 if dom == 1 else (0.559e9 + 3.119e9 + 2.557e9) / 238859
+        per_pair = 0.4101e9 / 59741 if dom == 1 else (0.559e9 / 238859 + (0.7305e9 + 0.6175e9) / 59741)
         roof["traffic"] = per_pair * P_local
     roof["traffic_unit"] = "bytes per launch"
-    roof["traffic_source"] = "ncu dram__bytes_read.sum + dram__bytes_write.sum of the C3 step, scaled to this launch"
+    roof["traffic_source"] = "ncu dram__bytes_read.sum + dram__bytes_write.sum per active block pair, scaled to this launch"
 
     e2e = None
     if not args.no_e2e:
