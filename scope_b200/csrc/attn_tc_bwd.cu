@@ -18,14 +18,16 @@
 // at most kChunk q tiles handled by separate CTAs, whose fp32 partial sums meet
 // in a small slot buffer that the last chunk of the row converts to bf16.
 //
-// Both kernels share one pipeline on whole 128x128 tiles (352 threads, one CTA
+// Both kernels share one pipeline on whole 128x128 tiles (608 threads, one CTA
 // per SM, all 512 TMEM columns): a producer warp (TMA), an S / dP issuing warp,
-// a gradient issuing warp and eight elementwise warps (two per TMEM lane
-// quadrant, 64 columns each in two chunks of 32).  S is double buffered in
-// TMEM, dP single buffered and released as soon as the elementwise warps have
-// read it; P / dS go back into the S buffer as bf16 pairs over the columns
-// the writing warp read, where the gradient MMAs read them as their A
-// operand.  Every wait is bounded (SCOPE_DEVERR_TIMEOUT).
+// a gradient issuing warp and sixteen elementwise warps (four per TMEM lane
+// quadrant, 32 columns each in two chunks of 16).  S is double buffered in
+// TMEM; dP is single buffered, read by every elementwise warp at the start of
+// a tile and released at once, and the next dP is issued before the next S.
+// P / dS go back into the S buffer as bf16 pairs within each chunk's own
+// columns, where the gradient MMAs read them as their A operand (the even
+// chunks' K steps as soon as they are written).  Every wait is bounded
+// (SCOPE_DEVERR_TIMEOUT).
 #include <algorithm>
 #include <cmath>
 #include <cstring>
