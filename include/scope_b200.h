@@ -162,6 +162,31 @@ int scope_qk_aug_prepare(const float *coeff_cos, const float *coeff_sin, const f
                          int32_t H, int32_t T, int32_t K, int32_t d_aug, float beta, float scale,
                          int32_t dtype, void *q_aug, void *k_aug, scope_stream_t stream);
 
+/* The coefficient block of SpectralBias.forward (model/attn_bias.py:306-324,
+ * 419-478): the per-query MLP (two bf16 linears with SiLU, weights shared by
+ * all heads or one set per head) and the mixture that produces the bias
+ * inputs.  Outputs as the reference returns them, batch 1.  T % 128 == 0,
+ * D == 64, hidden == 128, K in {6, 8, 16}, M in {2, 4, 8}. */
+typedef struct ScopeCoeffArgs {
+    int32_t H, T, D, hidden, K, M;
+    int32_t use_slope, subtract_b0;
+    const void *q;                    /* bf16 [H,T,D] view: element strides q_sh, q_st, last dim contiguous */
+    int64_t q_sh, q_st;
+    int32_t w_heads;                  /* 1 (share_across_heads) or H */
+    const void *w1, *b1;              /* bf16 [w_heads,hidden,D], [w_heads,hidden] */
+    const void *w2, *b2;              /* bf16 [w_heads,n_out,hidden], [w_heads,n_out]; n_out = 5M + use_slope */
+    const float *omegas, *log_omegas; /* [K], and their fp32 natural logs */
+    float delta_cap;                  /* clamp(delta_star_max_active, 0, T-1) */
+    float logw_min, logw_max, c_scale, width_min, width_max, eps;
+    float *coeff_cos, *coeff_sin;     /* [H,T,K] */
+    float *slope, *b0;                /* [H,T] (zeros when the term is off) */
+    float *delta_star, *pi, *budget_logits;   /* [H,T,M] */
+    float *delta_main, *width;        /* [H,T] */
+    uint16_t *mlp_out;                /* optional bf16 [H,T,n_out]: the MLP output y */
+    int32_t *err_flag;                /* optional device error word */
+} ScopeCoeffArgs;
+int scope_spectral_coeffs(const ScopeCoeffArgs *args, scope_stream_t stream);
+
 /* ------------------------------------------------------------------------ */
 /* 3. block-sparse attention                                                  */
 /* ------------------------------------------------------------------------ */

@@ -3,18 +3,21 @@
 Replaces, behind the reference's own interfaces:
   * SpectralBias.build_pointer_blockmask  -> PointerBlockMaskBuilder / build_mask
   * the spectral score_mod / qk_aug bias   -> SpectralScoreMod (evaluated in-kernel)
+  * SpectralBias.forward's coefficient block -> SpectralCoefficients / spectral_coefficients
   * flex_attention(q, k, v, block_mask, score_mod, scale) -> flex_attention
 Every op runs hand-written CUDA through the C ABI of libscope_b200.so
 (include/scope_b200.h); there is no CPU fallback.
 """
 from . import _lib
 from .attention import SpectralScoreMod, aug_dims, flex_attention, trig_tables
+from .coeff import CoeffOutputs, SpectralCoefficients, spectral_coefficients
 from .mask import PointerBlockMaskBuilder, ScopeBlockMask, block_info, build_mask
 from ._lib import device_errors
 
 __all__ = [
     "PointerBlockMaskBuilder", "ScopeBlockMask", "SpectralScoreMod", "aug_dims", "block_info", "build_mask",
-    "flex_attention", "trig_tables", "load_library", "device_errors",
+    "flex_attention", "trig_tables", "load_library", "device_errors", "CoeffOutputs", "SpectralCoefficients",
+    "spectral_coefficients",
 ]
 
 

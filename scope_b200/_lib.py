@@ -2,7 +2,7 @@
 
 The library is loaded once, in-tree.  If it is missing the import fails
 loudly: there is no CPU or library fallback for any op of this package.
-The two argument structs are mirrored field for field; ``check_abi()``
+The argument structs are mirrored field for field; ``check_abi()``
 compares their size and last-field offset with what the compiled library
 reports.
 """
@@ -79,6 +79,27 @@ class ScopeAttnArgs(ctypes.Structure):
 
 
 # symbols declared in include/scope_b200.h, with ctypes signatures
+class ScopeCoeffArgs(ctypes.Structure):
+    _fields_ = [
+        ("H", I32), ("T", I32), ("D", I32), ("hidden", I32), ("K", I32), ("M", I32),
+        ("use_slope", I32), ("subtract_b0", I32),
+        ("q", P),
+        ("q_sh", I64), ("q_st", I64),
+        ("w_heads", I32),
+        ("w1", P), ("b1", P), ("w2", P), ("b2", P),
+        ("omegas", P), ("log_omegas", P),
+        ("delta_cap", F32),
+        ("logw_min", F32), ("logw_max", F32), ("c_scale", F32), ("width_min", F32), ("width_max", F32),
+        ("eps", F32),
+        ("coeff_cos", P), ("coeff_sin", P),
+        ("slope", P), ("b0", P),
+        ("delta_star", P), ("pi", P), ("budget_logits", P),
+        ("delta_main", P), ("width", P),
+        ("mlp_out", P),
+        ("err_flag", P),
+    ]
+
+
 SIGNATURES = {
     "scope_block_info": (I32, [P, I32, I32, I32, I32, I32, P, P]),
     "scope_mask_max_kv": (I32, [I32, I32, I32, I32]),
@@ -87,6 +108,7 @@ SIGNATURES = {
     "scope_mask_refine": (I32, [P, P, I32, I32, I32, P, P, I32, P, P, P]),
     "scope_trig_tables": (I32, [P, I32, I32, P, P, P]),
     "scope_qk_aug_prepare": (I32, [P, P, P, P, P, I32, I32, I32, I32, I32, F32, F32, I32, P, P, P]),
+    "scope_spectral_coeffs": (I32, [ctypes.POINTER(ScopeCoeffArgs), P]),
     "scope_attn_fwd": (I32, [ctypes.POINTER(ScopeAttnArgs), P]),
     "scope_attn_bwd": (I32, [ctypes.POINTER(ScopeAttnArgs), P]),
     "scope_workspace_bytes": (ctypes.c_size_t, [ctypes.POINTER(ScopeAttnArgs)]),
@@ -131,7 +153,7 @@ def check(status: int, what: str) -> None:
 
 def check_abi() -> None:
     L = lib()
-    for which, S in ((0, ScopeMaskArgs), (1, ScopeAttnArgs)):
+    for which, S in ((0, ScopeMaskArgs), (1, ScopeAttnArgs), (2, ScopeCoeffArgs)):
         size, last = L.scope_abi_layout(which, 0), L.scope_abi_layout(which, 1)
         if size != ctypes.sizeof(S) or last != S.err_flag.offset:
             raise RuntimeError(f"scope_b200 ABI mismatch for {S.__name__}: C sizeof={size} last={last}, "

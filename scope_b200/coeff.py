@@ -1,0 +1,170 @@
+"""The coefficient block of SpectralBias.forward on the GPU.
+
+``SpectralCoefficients`` holds what the reference's ``SpectralBias`` holds for
+this block (model/attn_bias.py:83-160, 220-227, 290-324): the MLP weights
+(shared by the heads or one set per head), the log-spaced omegas and the
+knobs; ``forward(q)`` returns what ``SpectralBias.forward`` returns
+(model/attn_bias.py:381-622) with the trig tables of ``trig_tables``.  The
+MLP and the mixture run in one CUDA kernel (``scope_spectral_coeffs``);
+``spectral_coefficients`` is the functional form.
+
+Forward only: the outputs carry no autograd history (the reference trains
+this block; its backward is not built here), and the training regularisers
+(model/attn_bias.py:480-506) are not computed -- ``reg_loss`` is 0, as in
+the reference's eval mode.
+"""
+from __future__ import annotations
+
+import ctypes
+import math
+from dataclasses import dataclass
+from typing import Optional
+
+import torch
+from torch import Tensor
+
+from . import _lib
+from .attention import trig_tables
+from .mask import _stream
+
+OUT_NAMES = ("coeff_cos", "coeff_sin", "slope", "b0", "delta_star", "pi", "budget_logits", "delta_main", "width")
+
+
+@dataclass
+class CoeffOutputs:
+    coeff_cos: Tensor      # [1,H,T,K] f32
+    coeff_sin: Tensor      # [1,H,T,K]
+    slope: Tensor          # [1,H,T]
+    b0: Tensor             # [1,H,T]
+    delta_star: Tensor     # [1,H,T,M]
+    pi: Tensor             # [1,H,T,M]
+    budget_logits: Tensor  # [1,H,T,M]
+    delta_main: Tensor     # [1,H,T]
+    width: Tensor          # [1,H,T]
+    mlp_out: Optional[Tensor] = None   # [1,H,T,n_out] bf16 when requested
+
+
+def spectral_coefficients(q: Tensor, w1: Tensor, b1: Tensor, w2: Tensor, b2: Tensor, *, omegas: Tensor,
+                          log_omegas: Optional[Tensor] = None, M: int, delta_cap: float, logw_min: float,
+                          logw_max: float, use_slope: bool = True, subtract_b0: bool = True, c_scale: float = 0.01,
+                          width_min: float = 32.0, width_max: float = 256.0, eps: float = 1e-9,
+                          return_mlp: bool = False) -> CoeffOutputs:
+    """q [1,H,T,64] or [H,T,64] bf16 (any head/token strides, last dim
+    contiguous); w1 [hid,64] / b1 [hid] / w2 [n_out,hid] / b2 [n_out] shared,
+    or with a leading H dim per head, in q's dtype (the reference casts its
+    weights to q's dtype); n_out = 5M + use_slope; hid = 128."""
+    if q.dim() == 4:
+        if q.shape[0] != 1:
+            raise ValueError("spectral_coefficients: batch must be 1 (as the reference's flex path)")
+        q3 = q[0]
+    else:
+        q3 = q
+    if q3.dtype != torch.bfloat16 or not q3.is_cuda:
+        raise TypeError("spectral_coefficients: q must be a CUDA bf16 tensor")
+    H, T, D = q3.shape
+    if q3.stride(2) != 1:
+        raise ValueError("spectral_coefficients: q's last dim must be contiguous")
+    per_head = w1.dim() == 3
+    n_out = 5 * M + (1 if use_slope else 0)
+    K = omegas.numel()
+    dev = q3.device
+    bf = lambda t: t.to(device=dev, dtype=torch.bfloat16).contiguous()
+    w1, b1, w2, b2 = bf(w1), bf(b1), bf(w2), bf(b2)
+    if w2.shape[-2] != n_out or b2.shape[-1] != n_out:
+        raise ValueError(f"spectral_coefficients: w2/b2 must have {n_out} outputs (5M + use_slope)")
+    om = omegas.to(device=dev, dtype=torch.float32).contiguous()
+    lom = (log_omegas if log_omegas is not None else omegas.float().log()).to(device=dev, dtype=torch.float32)
+    lom = lom.contiguous()
+    f32 = dict(device=dev, dtype=torch.float32)
+    out = CoeffOutputs(
+        coeff_cos=torch.empty(1, H, T, K, **f32), coeff_sin=torch.empty(1, H, T, K, **f32),
+        slope=torch.empty(1, H, T, **f32), b0=torch.empty(1, H, T, **f32),
+        delta_star=torch.empty(1, H, T, M, **f32), pi=torch.empty(1, H, T, M, **f32),
+        budget_logits=torch.empty(1, H, T, M, **f32), delta_main=torch.empty(1, H, T, **f32),
+        width=torch.empty(1, H, T, **f32),
+        mlp_out=torch.empty(1, H, T, n_out, device=dev, dtype=torch.bfloat16) if return_mlp else None)
+    a = _lib.ScopeCoeffArgs()
+    a.H, a.T, a.D, a.hidden, a.K, a.M = H, T, D, w1.shape[-2], K, M
+    a.use_slope, a.subtract_b0 = int(use_slope), int(subtract_b0)
+    a.q, a.q_sh, a.q_st = q3.data_ptr(), q3.stride(0), q3.stride(1)
+    a.w_heads = H if per_head else 1
+    a.w1, a.b1, a.w2, a.b2 = w1.data_ptr(), b1.data_ptr(), w2.data_ptr(), b2.data_ptr()
+    a.omegas, a.log_omegas = om.data_ptr(), lom.data_ptr()
+    a.delta_cap = float(delta_cap)
+    a.logw_min, a.logw_max = float(logw_min), float(logw_max)
+    a.c_scale, a.width_min, a.width_max, a.eps = float(c_scale), float(width_min), float(width_max), float(eps)
+    for n in OUT_NAMES:
+        setattr(a, n, getattr(out, n).data_ptr())
+    a.mlp_out = out.mlp_out.data_ptr() if return_mlp else None
+    a.err_flag = _lib.err_word_ptr(dev)
+    _lib.check(_lib.lib().scope_spectral_coeffs(ctypes.byref(a), _stream(dev)), "scope_spectral_coeffs")
+    return out
+
+
+class SpectralCoefficients:
+    """The coefficient block of a SpectralBias: same constructor knobs for the
+    block (model/attn_bias.py:83-160), weights initialised as the reference
+    initialises them (model/attn_bias.py:290-304) unless loaded with
+    ``load_weights``."""
+
+    def __init__(self, *, head_dim: int, num_heads: int, L_train: int, L_max: int = 1_000_000, K: int = 6,
+                 M: int = 2, w_min: Optional[float] = None, w_max: Optional[float] = None,
+                 share_across_heads: bool = True, use_slope: bool = True, c_scale: float = 0.01,
+                 width_min: float = 32.0, width_max: float = 256.0, delta_star_max: Optional[int] = None,
+                 subtract_b0: bool = True, eps: float = 1e-9, device="cuda", seed: int = 0):
+        if head_dim != 64:
+            raise ValueError("SpectralCoefficients: head_dim must be 64")
+        self.H, self.K, self.M = num_heads, K, M
+        self.use_slope, self.subtract_b0 = use_slope, subtract_b0
+        self.c_scale, self.width_min, self.width_max, self.eps = c_scale, width_min, width_max, eps
+        w_min = float(w_min) if w_min is not None else 2 * math.pi / L_max
+        w_max = float(w_max) if w_max is not None else 2 * math.pi / L_train
+        self.omegas = torch.logspace(math.log10(w_min), math.log10(w_max), K, dtype=torch.float32).to(device)
+        self.log_omegas = self.omegas.log()
+        self.logw_min = float(torch.tensor(math.log(w_min), dtype=torch.float32))
+        self.logw_max = float(torch.tensor(math.log(w_max), dtype=torch.float32))
+        self.delta_star_max = int(delta_star_max) if delta_star_max is not None else int(L_train - 1)
+        self.delta_star_max_active = self.delta_star_max
+        hid, n_out = max(128, 2 * head_dim), 5 * M + (1 if use_slope else 0)
+        g = torch.Generator().manual_seed(seed)
+        Hw = 1 if share_across_heads else num_heads
+        b1_ = math.sqrt(3) * 0.5 * head_dim ** -0.5
+        self.w1 = ((torch.rand(Hw, hid, head_dim, generator=g) * 2 - 1) * b1_)
+        self.b1 = torch.zeros(Hw, hid)
+        self.w2 = torch.zeros(Hw, n_out, hid)
+        self.b2 = torch.zeros(Hw, n_out)
+        self.b2[:, :M] = torch.linspace(-6.0, -4.0, M)   # delta* starts small (the reference's output init)
+        self.share = share_across_heads
+        self.device = device
+
+    def set_delta_star_max_active(self, *, max_tokens: int):
+        """As SpectralBias.set_delta_star_max_active (model/attn_bias.py:366-371)."""
+        if max_tokens < 0:
+            raise ValueError("max_tokens must be >= 0")
+        self.delta_star_max_active = min(int(max_tokens), self.delta_star_max)
+
+    def load_weights(self, w1: Tensor, b1: Tensor, w2: Tensor, b2: Tensor):
+        """Weights in the reference's layout: shared [hid,D], [hid], [n_out,hid],
+        [n_out], or per head with a leading H dim."""
+        if w1.dim() == 2:
+            w1, b1, w2, b2 = w1[None], b1[None], w2[None], b2[None]
+        self.w1, self.b1, self.w2, self.b2 = (t.detach() for t in (w1, b1, w2, b2))
+        self.share = self.w1.shape[0] == 1
+
+    def forward(self, q: Tensor, *, return_mlp: bool = False):
+        """q [1,H,T,64] bf16 -> the outputs of SpectralBias.forward: coeff_cos,
+        coeff_sin, slope, b0, delta_star, pi, budget_logits, delta_main, width,
+        cos_wD, sin_wD, reg_loss (0)."""
+        T = q.shape[-2]
+        w = (lambda t: t[0]) if self.share else (lambda t: t)
+        o = spectral_coefficients(
+            q, w(self.w1), w(self.b1), w(self.w2), w(self.b2), omegas=self.omegas, log_omegas=self.log_omegas,
+            M=self.M, delta_cap=float(min(max(self.delta_star_max_active, 0), T - 1)), logw_min=self.logw_min,
+            logw_max=self.logw_max, use_slope=self.use_slope, subtract_b0=self.subtract_b0, c_scale=self.c_scale,
+            width_min=self.width_min, width_max=self.width_max, eps=self.eps, return_mlp=return_mlp)
+        cos_wD, sin_wD = trig_tables(self.omegas, T)
+        reg = torch.zeros((), device=q.device)
+        res = tuple(getattr(o, n) for n in OUT_NAMES) + (cos_wD, sin_wD, reg)
+        return (res, o.mlp_out) if return_mlp else res
+
+    __call__ = forward

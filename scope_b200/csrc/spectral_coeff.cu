@@ -1,0 +1,382 @@
+// SpectralBias coefficient block, forward (model/attn_bias.py:306-324, 419-478):
+// the per-query MLP q -> y and the mixture that turns y into the Fourier
+// coefficients the attention bias consumes, fused so that none of the
+// reference's [B,H,L,M,K] intermediates is materialised.
+//
+// One CTA of 128 threads per 128-token tile of one head (two CTAs per SM):
+//   TMA      q tile [128 x 64] bf16, W1 [128 x 64], W2 [n_out x 128] (zero rows
+//            up to NP = n_out rounded up to 16), 128-byte swizzled, K-major
+//   tcgen05  D1 = q W1^T into TMEM columns [0, 128)
+//   threads  x = bf16(D1 + b1), h = bf16(silu(x)), written back to shared memory
+//            in the same swizzled K-major layout as the A operand of
+//   tcgen05  D2 = h W2^T into TMEM columns [128, 128 + NP)
+//   threads  y = bf16(D2 + b2) (the reference runs both linears in the dtype of
+//            q, bf16; with one weight set per head its einsum rounds D to bf16
+//            before the bias add, and so does this kernel), then per token: delta* = sigmoid * cap, mu, sigma, pi =
+//            softmax, budget logits, slope = c tanh, the Gaussian weights a_mk
+//            over log omega, and coeff_cos/sin[k] = sum_m pi_m a_mk cos/sin(w_k delta*_m),
+//            b0 = sum_k coeff_cos, delta_main, width.
+// Thread r of the CTA owns token row r, which is also TMEM lane r.  Every
+// arithmetic step follows the reference's operation order with explicit
+// roundings (no contraction into FMAs where the reference rounds twice).
+#include <cmath>
+#include <cstring>
+
+#include "common.cuh"
+#include "tc_host.cuh"
+#include "tc_ptx.cuh"
+
+namespace scope {
+namespace coeff {
+
+using namespace tc;
+
+constexpr int BM = 128;       // tokens per tile
+constexpr int HD = 64;        // head dim (q)
+constexpr int HID = 128;      // MLP hidden width: max(128, 2 * head_dim)
+constexpr uint32_t kTmemCols = 256;
+
+struct Maps {
+    CUtensorMap q, w1, w2;
+};
+
+struct Params {
+    int H, T, K, M, n_out, use_slope, subtract_b0, w_heads;
+    const uint16_t *b1, *b2;
+    const float *omegas, *log_omegas;
+    float delta_cap, logw_min, logw_max, c_scale, width_min, width_max, eps;
+    float *coeff_cos, *coeff_sin, *slope, *b0, *delta_star, *pi, *budget, *delta_main, *width;
+    uint16_t *mlp_out;
+    int32_t *err;
+};
+
+__host__ __device__ constexpr uint32_t align1k(uint32_t x) { return (x + 1023u) & ~1023u; }
+
+template <int NP>
+struct Layout {
+    static constexpr uint32_t Q = 0, W1 = 16384, W2 = 32768;
+    static constexpr uint32_t W2SUB = align1k(NP * 128);       // one 64-column half of W2
+    static constexpr uint32_t HB = W2 + 2 * W2SUB;              // silu(x): two 64-column halves
+    static constexpr uint32_t BAR = HB + 2 * 16384;
+    static constexpr uint32_t TOTAL = BAR + 64;
+    static constexpr uint32_t TX = 2 * 16384 + 2 * NP * 128;    // bytes the TMA loads deliver
+};
+
+__device__ __forceinline__ float bf16r(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
+__device__ __forceinline__ float sigmoid_ref(float x) { return __fdiv_rn(1.f, __fadd_rn(1.f, expf(-x))); }
+
+template <int K, int M, int NP>
+__global__ void __launch_bounds__(128, 2) coeff_kernel(const __grid_constant__ Maps maps, const Params p) {
+    using L = Layout<NP>;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
+    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + L::BAR);   // [0] loads, [1] MMA 1, [2] MMA 2
+    uint32_t *tslot = reinterpret_cast<uint32_t *>(smem + L::BAR + 32);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, r = threadIdx.x;
+    const int tiles_per_head = p.T / BM;
+    const int h = blockIdx.x / tiles_per_head, t0 = (blockIdx.x - h * tiles_per_head) * BM;
+    const bool per_head = p.w_heads > 1;
+    const int hw = per_head ? h : 0;
+
+    if (threadIdx.x == 0) {
+        mbar_init(&bars[0], 1);
+        mbar_init(&bars[1], 1);
+        mbar_init(&bars[2], 1);
+        fence_mbar_init();
+    }
+    if (warp == 0) {
+        tmem_alloc(tslot, kTmemCols);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tslot;
+    const uint32_t lb = (uint32_t)(warp * 32) << 16;
+
+    if (threadIdx.x == 0) {
+        mbar_expect_tx(&bars[0], L::TX);
+        tma_load_3d(&maps.q, smem + L::Q, &bars[0], 0, t0, h);
+        tma_load_3d(&maps.w1, smem + L::W1, &bars[0], 0, 0, hw);
+        tma_load_3d(&maps.w2, smem + L::W2, &bars[0], 0, 0, hw);
+        tma_load_3d(&maps.w2, smem + L::W2 + L::W2SUB, &bars[0], 64, 0, hw);
+    }
+    bool ok = mbar_wait(&bars[0], 0);
+    const uint32_t sQ = smem_u32(smem + L::Q), sW1 = smem_u32(smem + L::W1), sW2 = smem_u32(smem + L::W2),
+                   sH = smem_u32(smem + L::HB);
+    if (threadIdx.x == 0 && ok) {
+        tc_fence_after();
+        constexpr uint32_t id1 = idesc_bf16(128, HID, false, false);
+#pragma unroll
+        for (int kk = 0; kk < HD / 16; ++kk)
+            mma_ss(tmem, kmajor_desc(sQ + kk * 32, 128), kmajor_desc(sW1 + kk * 32, 128), id1, kk > 0);
+        tc_commit(&bars[1]);
+    }
+    ok = __syncthreads_and(ok);
+    ok = ok && mbar_wait(&bars[1], 0);
+    tc_fence_after();
+
+    // ---- x = bf16(q W1^T + b1), h = bf16(silu(x)) -> shared memory (swizzled K-major rows)
+    if (ok) {
+        const uint16_t *b1 = p.b1 + (size_t)hw * HID;
+#pragma unroll 1
+        for (int c4 = 0; c4 < HID / 32; ++c4) {
+            uint32_t v[32];
+            tmem_ld32(tmem + lb + 32 * c4, v);
+            tmem_wait_ld();
+            pin(v);
+            uint32_t pk[16];
+#pragma unroll
+            for (int e = 0; e < 32; e += 2) {
+                float s2[2];
+#pragma unroll
+                for (int u = 0; u < 2; ++u) {
+                    const int j = 32 * c4 + e + u;
+                    // per-head weights: the reference's einsum rounds to bf16 before its bias add
+                    const float acc = per_head ? bf16r(__uint_as_float(v[e + u])) : __uint_as_float(v[e + u]);
+                    const float x = bf16r(__fadd_rn(acc, bf16_to_f32(__ldg(b1 + j))));
+                    s2[u] = bf16r(__fdiv_rn(x, __fadd_rn(1.f, expf(-x))));
+                }
+                pk[e / 2] = pack_bf16(s2[0], s2[1]);
+            }
+            // hidden columns [32 c4, 32 c4 + 32): half a = c4 / 2, 16-byte chunks (c4 % 2) * 4 .. + 3
+            uint8_t *half = smem + L::HB + (c4 >> 1) * 16384 + r * 128;
+#pragma unroll
+            for (int q4 = 0; q4 < 4; ++q4) {
+                const int chunk = (c4 & 1) * 4 + q4;
+                *reinterpret_cast<uint4 *>(half + ((chunk ^ (r & 7)) << 4)) =
+                    make_uint4(pk[4 * q4], pk[4 * q4 + 1], pk[4 * q4 + 2], pk[4 * q4 + 3]);
+            }
+        }
+    }
+    // generic-proxy writes of h must be visible to the tensor core's reads
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    tc_fence_before();
+    ok = __syncthreads_and(ok);
+    if (threadIdx.x == 0 && ok) {
+        tc_fence_after();
+        constexpr uint32_t id2 = idesc_bf16(128, NP, false, false);
+#pragma unroll
+        for (int kk = 0; kk < HID / 16; ++kk) {
+            const uint32_t a = (uint32_t)(kk >> 2) * 16384u + (kk & 3) * 32, b = (uint32_t)(kk >> 2) * L::W2SUB + (kk & 3) * 32;
+            mma_ss(tmem + HID, kmajor_desc(sH + a, 128), kmajor_desc(sW2 + b, 128), id2, kk > 0);
+        }
+        tc_commit(&bars[2]);
+    }
+    ok = ok && mbar_wait(&bars[2], 0);
+    tc_fence_after();
+
+    if (ok) {
+        // ---- y = bf16(h W2^T + b2)
+        float y[NP];
+        const uint16_t *b2 = p.b2 + (size_t)hw * p.n_out;
+#pragma unroll
+        for (int c = 0; c < NP; c += 16) {
+            uint32_t v[16];
+            tmem_ld16(tmem + lb + HID + c, v);
+            tmem_wait_ld();
+            pin(v);
+#pragma unroll
+            for (int e = 0; e < 16; ++e) {
+                const float acc = per_head ? bf16r(__uint_as_float(v[e])) : __uint_as_float(v[e]);
+                y[c + e] = c + e < p.n_out ? bf16r(__fadd_rn(acc, bf16_to_f32(__ldg(b2 + c + e)))) : 0.f;
+            }
+        }
+        const int64_t row = (int64_t)h * p.T + t0 + r;
+        if (p.mlp_out) {
+            uint16_t *mo = p.mlp_out + row * p.n_out;
+#pragma unroll
+            for (int o = 0; o < NP; ++o) {
+                if (o < p.n_out) {
+                    __nv_bfloat16 b = __float2bfloat16_rn(y[o]);
+                    mo[o] = *reinterpret_cast<uint16_t *>(&b);
+                }
+            }
+        }
+        // ---- heads (model/attn_bias.py:437-478), y columns: delta | mu | sigma | pi | budget | (slope)
+        float ds[M], mu[M], sg[M], pi[M];
+        float musum = 0.f, pmax = -INFINITY, dmain = 0.f;   // delta* of the first largest pi logit
+#pragma unroll
+        for (int m = 0; m < M; ++m) {
+            ds[m] = __fmul_rn(sigmoid_ref(y[m]), p.delta_cap);
+            mu[m] = __fadd_rn(p.logw_min, __fmul_rn(__fsub_rn(p.logw_max, p.logw_min), sigmoid_ref(y[M + m])));
+            sg[m] = __fadd_rn(0.25f, __fmul_rn(1.75f, sigmoid_ref(y[2 * M + m])));
+            musum = __fadd_rn(musum, mu[m]);
+            if (y[3 * M + m] > pmax) {
+                pmax = y[3 * M + m];
+                dmain = ds[m];
+            }
+        }
+        float psum = 0.f;
+#pragma unroll
+        for (int m = 0; m < M; ++m) {
+            pi[m] = expf(__fsub_rn(y[3 * M + m], pmax));
+            psum = __fadd_rn(psum, pi[m]);
+        }
+#pragma unroll
+        for (int m = 0; m < M; ++m) pi[m] = __fdiv_rn(pi[m], psum);
+        float cc[K], cs[K];
+#pragma unroll
+        for (int k = 0; k < K; ++k) cc[k] = cs[k] = 0.f;
+#pragma unroll
+        for (int m = 0; m < M; ++m) {
+            const float den = __fmul_rn(2.f, __fmul_rn(sg[m], sg[m]));
+            float a[K], asum = 0.f;
+#pragma unroll
+            for (int k = 0; k < K; ++k) {
+                const float d = __fsub_rn(__ldg(p.log_omegas + k), mu[m]);
+                a[k] = expf(__fdiv_rn(-__fmul_rn(d, d), den));
+                asum = __fadd_rn(asum, a[k]);
+            }
+            const float an = __fadd_rn(asum, p.eps);
+#pragma unroll
+            for (int k = 0; k < K; ++k) {
+                const float w = __fmul_rn(pi[m], __fdiv_rn(a[k], an));
+                float sn, c;
+                sincosf(__fmul_rn(__ldg(p.omegas + k), ds[m]), &sn, &c);
+                cc[k] = __fadd_rn(cc[k], __fmul_rn(w, c));
+                cs[k] = __fadd_rn(cs[k], __fmul_rn(w, sn));
+            }
+        }
+        float b0 = 0.f;
+        if (p.subtract_b0) {
+#pragma unroll
+            for (int k = 0; k < K; ++k) b0 = __fadd_rn(b0, cc[k]);
+        }
+        // ---- stores: [H,T,K] coefficients, [H,T,M] per-pointer values, [H,T] scalars
+        float *oc = p.coeff_cos + row * K, *os = p.coeff_sin + row * K;
+        if constexpr (K % 4 == 0) {
+#pragma unroll
+            for (int k = 0; k < K; k += 4) {
+                *reinterpret_cast<float4 *>(oc + k) = make_float4(cc[k], cc[k + 1], cc[k + 2], cc[k + 3]);
+                *reinterpret_cast<float4 *>(os + k) = make_float4(cs[k], cs[k + 1], cs[k + 2], cs[k + 3]);
+            }
+        } else {
+#pragma unroll
+            for (int k = 0; k < K; ++k) {
+                oc[k] = cc[k];
+                os[k] = cs[k];
+            }
+        }
+#pragma unroll
+        for (int m = 0; m < M; ++m) {
+            p.delta_star[row * M + m] = ds[m];
+            p.pi[row * M + m] = pi[m];
+            p.budget[row * M + m] = y[4 * M + m];
+        }
+        p.slope[row] = p.use_slope ? __fmul_rn(p.c_scale, tanhf(y[5 * M])) : 0.f;
+        p.b0[row] = b0;
+        p.delta_main[row] = dmain;
+        p.width[row] = __fadd_rn(p.width_min,
+                                 __fmul_rn(__fsub_rn(p.width_max, p.width_min), sigmoid_ref(__fdiv_rn(musum, (float)M))));
+    } else if (threadIdx.x == 0) {
+        set_err(p.err, SCOPE_DEVERR_TIMEOUT);
+    }
+    // the MMAs are complete (or their wait gave up: wait once more, bounded) before TMEM is freed
+    if (!ok && threadIdx.x == 0) {
+        mbar_wait(&bars[1], 0, 500000000ull);
+        mbar_wait(&bars[2], 0, 500000000ull);
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 0) {
+        tc_fence_after();
+        tmem_dealloc(tmem, kTmemCols);
+    }
+}
+
+// bf16 [rows][inner] weights per head: [w_heads][rows][inner], box (64, box_rows, 1)
+static bool map_weights(CUtensorMap *m, const void *base, int inner, int rows, int heads, int box_rows) {
+    cuuint64_t dims[3] = {(cuuint64_t)inner, (cuuint64_t)rows, (cuuint64_t)heads};
+    cuuint64_t strides[2] = {(cuuint64_t)inner * 2, (cuuint64_t)inner * rows * 2};
+    cuuint32_t box[3] = {64u, (cuuint32_t)box_rows, 1u};
+    cuuint32_t es[3] = {1, 1, 1};
+    auto fn = tchost::encode_fn();
+    return fn && fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void *>(base), dims, strides, box, es,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+template <int K, int M>
+static int launch(const ScopeCoeffArgs &a, cudaStream_t s) {
+    constexpr int NP = ((5 * M + 1) + 15) / 16 * 16;
+    using L = Layout<NP>;
+    Maps maps;
+    std::memset(&maps, 0, sizeof(maps));
+    if (!tchost::map3d(&maps.q, a.q, HD, a.T, a.H, a.q_st, a.q_sh, HD) ||
+        !map_weights(&maps.w1, a.w1, HD, HID, a.w_heads, HID) ||
+        !map_weights(&maps.w2, a.w2, HID, 5 * M + (a.use_slope ? 1 : 0), a.w_heads, NP))
+        return SCOPE_ERR_ALIGN;
+    Params p;
+    std::memset(&p, 0, sizeof(p));
+    p.H = a.H;
+    p.T = a.T;
+    p.K = K;
+    p.M = M;
+    p.n_out = 5 * M + (a.use_slope ? 1 : 0);
+    p.use_slope = a.use_slope;
+    p.subtract_b0 = a.subtract_b0;
+    p.w_heads = a.w_heads;
+    p.b1 = reinterpret_cast<const uint16_t *>(a.b1);
+    p.b2 = reinterpret_cast<const uint16_t *>(a.b2);
+    p.omegas = a.omegas;
+    p.log_omegas = a.log_omegas;
+    p.delta_cap = a.delta_cap;
+    p.logw_min = a.logw_min;
+    p.logw_max = a.logw_max;
+    p.c_scale = a.c_scale;
+    p.width_min = a.width_min;
+    p.width_max = a.width_max;
+    p.eps = a.eps;
+    p.coeff_cos = a.coeff_cos;
+    p.coeff_sin = a.coeff_sin;
+    p.slope = a.slope;
+    p.b0 = a.b0;
+    p.delta_star = a.delta_star;
+    p.pi = a.pi;
+    p.budget = a.budget_logits;
+    p.delta_main = a.delta_main;
+    p.width = a.width;
+    p.mlp_out = a.mlp_out;
+    p.err = a.err_flag;
+    const size_t smem = L::TOTAL + 1024;
+    if (cudaFuncSetAttribute(coeff_kernel<K, M, NP>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
+        cudaSuccess)
+        return SCOPE_ERR_CUDA;
+    coeff_kernel<K, M, NP><<<(unsigned)(a.H * (a.T / BM)), 128, smem, s>>>(maps, p);
+    SCOPE_CHECK_LAUNCH();
+    return SCOPE_OK;
+}
+
+template <int K>
+static int launch_m(const ScopeCoeffArgs &a, cudaStream_t s) {
+    switch (a.M) {
+        case 2: return launch<K, 2>(a, s);
+        case 4: return launch<K, 4>(a, s);
+        case 8: return launch<K, 8>(a, s);
+        default: return SCOPE_ERR_UNSUPPORTED;
+    }
+}
+
+}  // namespace coeff
+}  // namespace scope
+
+extern "C" int scope_spectral_coeffs(const ScopeCoeffArgs *args, scope_stream_t stream) {
+    using namespace scope::coeff;
+    if (!args) return SCOPE_ERR_INVALID;
+    const ScopeCoeffArgs &a = *args;
+    if (a.H <= 0 || a.T <= 0 || a.T % BM != 0 || a.D != HD || a.hidden != HID) return SCOPE_ERR_INVALID;
+    if (a.w_heads != 1 && a.w_heads != a.H) return SCOPE_ERR_INVALID;
+    if (!a.q || !a.w1 || !a.b1 || !a.w2 || !a.b2 || !a.omegas || !a.log_omegas || !a.coeff_cos || !a.coeff_sin ||
+        !a.slope || !a.b0 || !a.delta_star || !a.pi || !a.budget_logits || !a.delta_main || !a.width)
+        return SCOPE_ERR_INVALID;
+    if ((a.q_st * 2) % 16 != 0 || (a.q_sh * 2) % 16 != 0) return SCOPE_ERR_ALIGN;
+    cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    switch (a.K) {
+        case 6: return launch_m<6>(a, s);
+        case 8: return launch_m<8>(a, s);
+        case 16: return launch_m<16>(a, s);
+        default: return SCOPE_ERR_UNSUPPORTED;
+    }
+}

@@ -162,3 +162,40 @@ def attn_mask_knobs(case):
     if case["mask"] == "m_c1_like":
         return dict(M=2, local=2, half=1, glob=1, budget=2, total=False, temp=1.0)
     return dict(M=2, local=2, half=1, glob=1, budget=4, total=True, temp=0.5)
+
+
+# ---------------------------------------------------------------------------
+# SpectralBias coefficient block cases (model/attn_bias.py:306-324, 419-478)
+# ---------------------------------------------------------------------------
+COEFF_CASES = {
+    # the configs' K=16, M=8 with weights shared by the heads, slope and b0 on
+    "c_shared": dict(H=2, T=256, K=16, M=8, share=True, use_slope=True, subtract_b0=True,
+                     L_train=256, delta_star_max=None, seed=31),
+    # one weight set per head, no slope / b0, a schedule cap on delta*
+    "c_perhead": dict(H=3, T=128, K=8, M=4, share=False, use_slope=False, subtract_b0=False,
+                      L_train=512, delta_star_max=100, seed=32),
+    # the reference's constructor defaults K=6, M=2
+    "c_k6m2": dict(H=1, T=384, K=6, M=2, share=True, use_slope=True, subtract_b0=True,
+                   L_train=1024, delta_star_max=None, seed=33),
+}
+
+
+def coeff_inputs(case):
+    """q [1,H,T,64] and the MLP weights as bf16-representable float32 arrays
+    (w1 [Hw,128,64], b1 [Hw,128], w2 [Hw,n_out,128], b2 [Hw,n_out]; Hw = 1 when
+    shared).  The delta* logits get a negative bias so delta* spreads over the
+    cap instead of saturating."""
+    import torch
+    g = torch.Generator().manual_seed(case["seed"])
+    H, T, M = case["H"], case["T"], case["M"]
+    Hw = 1 if case["share"] else H
+    n_out = 5 * M + (1 if case["use_slope"] else 0)
+    bf = lambda t: t.to(torch.bfloat16).float()
+    q = bf(torch.randn(1, H, T, 64, generator=g))
+    w1 = bf(torch.randn(Hw, 128, 64, generator=g) * 0.125)
+    b1 = bf(torch.randn(Hw, 128, generator=g) * 0.1)
+    w2 = bf(torch.randn(Hw, n_out, 128, generator=g) * 0.08)
+    b2 = torch.randn(Hw, n_out, generator=g) * 0.5
+    b2[:, :M] += torch.linspace(-3.0, 1.0, M)
+    b2 = bf(b2)
+    return {"q": q.numpy(), "w1": w1.numpy(), "b1": b1.numpy(), "w2": w2.numpy(), "b2": b2.numpy()}

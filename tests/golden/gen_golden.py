@@ -16,7 +16,10 @@ Usage (in a checkout that has the reference sources):
   The CPU flex path returns no lse (``return_lse`` is unsupported there), so
   only the outputs are pinned; lse is pinned through the float64 restatement.
 
-Outputs: tests/golden/mask_<case>.npz and tests/golden/attn_<case>.npz.
+* Coefficient fixtures: ``SpectralBias.forward`` (model/attn_bias.py:419-478)
+  in eval mode and its ``_mlp_forward`` on seeded q and MLP weights.
+
+Outputs: tests/golden/mask_<case>.npz, attn_<case>.npz and coeff_<case>.npz.
 The reference is read only at generation time; the tests never import it.
 """
 from __future__ import annotations
@@ -188,6 +191,45 @@ def run_attn_case(SpectralBias, name, case):
     print(f"attn {name}: done")
 
 
+COEFF_OUTS = ("coeff_cos", "coeff_sin", "slope", "b0", "delta_star", "pi", "budget_logits", "delta_main", "width")
+
+
+def run_coeff_case(SpectralBias, name, case):
+    """SpectralBias.forward in eval mode (no regularisers) and its _mlp_forward,
+    with the case's weights loaded into the module's float32 parameters
+    (bf16-representable, so the module's cast to bf16 is exact)."""
+    x = C.coeff_inputs(case)
+    H, T, K, M = case["H"], case["T"], case["K"], case["M"]
+    sb = SpectralBias(head_dim=64, num_heads=H, L_train=case["L_train"], K=K, M=M,
+                      share_across_heads=case["share"], use_slope=case["use_slope"],
+                      subtract_b0=case["subtract_b0"], delta_star_max=case["delta_star_max"])
+    with torch.no_grad():
+        if case["share"]:
+            sb.mlp[0].weight.copy_(torch.from_numpy(x["w1"][0]))
+            sb.mlp[0].bias.copy_(torch.from_numpy(x["b1"][0]))
+            sb.mlp[2].weight.copy_(torch.from_numpy(x["w2"][0]))
+            sb.mlp[2].bias.copy_(torch.from_numpy(x["b2"][0]))
+        else:
+            sb.w1.copy_(torch.from_numpy(x["w1"]))
+            sb.b1.copy_(torch.from_numpy(x["b1"]))
+            sb.w2.copy_(torch.from_numpy(x["w2"]))
+            sb.b2.copy_(torch.from_numpy(x["b2"]))
+    sb.eval()
+    q = torch.from_numpy(x["q"]).to(torch.bfloat16)
+    with torch.no_grad():
+        outs = sb(q)
+        y = sb._mlp_forward(q).float()
+    res = {n: outs[i].float().numpy() for i, n in enumerate(COEFF_OUTS)}
+    np.savez_compressed(os.path.join(HERE, f"coeff_{name}.npz"), **res, y=y.numpy(),
+                        omegas=sb.omegas.numpy(), log_omegas=sb.log_omegas.numpy(),
+                        logw_min=sb.logw_min.numpy(), logw_max=sb.logw_max.numpy(),
+                        delta_star_max=np.array(int(sb._delta_star_max_active)),
+                        c_scale=np.array(sb.c_scale, np.float32), width_min=np.array(sb.width_min, np.float32),
+                        width_max=np.array(sb.width_max, np.float32), eps=np.array(sb.eps, np.float32),
+                        in_hash=np.array(C.input_hash(*(x[n] for n in sorted(x)))))
+    print(f"coeff {name}: done")
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", required=True, help="path of the onetensor/scope checkout")
@@ -204,6 +246,10 @@ def main():
         if a.only and a.only not in name:
             continue
         run_attn_case(SpectralBias, name, case)
+    for name, case in C.COEFF_CASES.items():
+        if a.only and a.only not in name:
+            continue
+        run_coeff_case(SpectralBias, name, case)
 
 
 if __name__ == "__main__":
