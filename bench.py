@@ -284,6 +284,61 @@ def time_e2e(pipe, steps, world):
     return ms
 
 
+def coeff_block(wl, cfg, hbm, *, reps=10, cpu=True):
+    """The SpectralBias coefficient block (model/attn_bias.py:306-324, 419-478)
+    on this rank's heads at the bench's T, M = 8 pointers, K of the config:
+    the fused kernel (scope_spectral_coeffs) timed with CUDA events over `reps`
+    calls (q, 2^17 tokens x 16 heads of bf16, is larger than L2), its HBM
+    roofline (q read once, every output written once), and on the host the
+    oracle's restatement of the reference's CPU computation on a bounded
+    sample (one head, 8192 tokens)."""
+    from scope_b200 import SpectralCoefficients, spectral_coefficients
+    from scope_b200.coeff import OUT_NAMES
+    H, T, K, M = wl.hp, cfg.T, cfg.K, 8
+    n_out = 5 * M + 1
+    sc = SpectralCoefficients(head_dim=64, num_heads=H, L_train=T, K=K, M=M, seed=7)
+    g = torch.Generator().manual_seed(8)
+    sc.load_weights(sc.w1[0], torch.randn(128, generator=g) * 0.1, torch.randn(n_out, 128, generator=g) * 0.08,
+                    sc.b2[0] + torch.randn(n_out, generator=g) * 0.5)
+    q = wl.x["q"].detach()
+    kw = dict(omegas=sc.omegas, log_omegas=sc.log_omegas, M=M, delta_cap=float(min(sc.delta_star_max, T - 1)),
+              logw_min=sc.logw_min, logw_max=sc.logw_max)
+    w = [t[0].to(device=q.device, dtype=torch.bfloat16) for t in (sc.w1, sc.b1, sc.w2, sc.b2)]
+    outs = [spectral_coefficients(q, *w, **kw) for _ in range(3)]
+    torch.cuda.synchronize()
+    s = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(s)
+    for _ in range(reps):
+        spectral_coefficients(q, *w, **kw)
+    e1.record(s)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / reps
+    tok = H * T
+    byts = tok * (64 * 2 + (2 * K + 3 * M + 4) * 4)
+    res = {"kernel": "scope_spectral_coeffs", "workload": f"{H} heads x T={T}, K={K}, M={M}, shared MLP 64-128-{n_out}",
+           "ms": ms, "tokens_per_s": tok / (ms * 1e-3),
+           "roofline": {"bound": "hbm", "achieved": byts / (ms * 1e-3) / 1e9, "peak": hbm, "unit": "GB/s",
+                        "frac": byts / (ms * 1e-3) / 1e9 / hbm, "algorithmic_bytes": byts},
+           "mlp_tflops": 2 * tok * (64 * 128 + 128 * n_out) / (ms * 1e-3) / 1e12}
+    del outs
+    if cpu:
+        from oracle import coeff_oracle as CO   # the CPU baseline only
+        n = 8192
+        qc = q[:1, :n].cpu()[None]
+        wc = [t[0] for t in (sc.w1, sc.b1, sc.w2, sc.b2)]
+        t0 = time.perf_counter()
+        y = CO.mlp(qc, *[t.to(torch.bfloat16) for t in wc])
+        CO.heads(y.float(), M=M, omegas=sc.omegas.cpu(), log_omegas=sc.log_omegas.cpu(),
+                 delta_cap=kw["delta_cap"], logw_min=sc.logw_min, logw_max=sc.logw_max, use_slope=True,
+                 subtract_b0=True, c_scale=sc.c_scale, width_min=sc.width_min, width_max=sc.width_max, eps=sc.eps)
+        dt = time.perf_counter() - t0
+        res["cpu_baseline"] = {"value": n / dt, "unit": "tokens/s", "cores": torch.get_num_threads(), "kind": "port",
+                               "sample": f"1 head x {n} tokens: the oracle's torch-CPU restatement of the reference's "
+                                         "MLP and mixture"}
+    return res
+
+
 def cpu_reference(cfg, *, warmup=1, steps=3, heads=1, seconds_budget=60.0):
     """The reference's CPU path on a bounded sample: the numpy port of its
     mask builder, then the attention forward (the reference raises
@@ -476,6 +531,8 @@ def main():
                "h2d_bytes_per_step": h2d * world, "d2h_bytes_per_step": d2h * world,
                "ms_per_step": ms_e / e_steps}
 
+    coeff = coeff_block(wl, cfg, hbm, cpu=(rank == 0 and world == 1 and not args.no_cpu_baseline))
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         try:
@@ -494,7 +551,7 @@ def main():
                            "spectral_impl": "qk_aug", "parallelism": f"heads/{world}",
                            "active_block_pairs": P, "l2": "inputs larger than L2 (q,k,v,dO 1 GiB)"},
                 "roofline": roof, "phases_ms": phases, "cpu_baseline": cpu, "e2e": e2e,
-                "clocks": clk.summary(), "gpu_launches": int(launches)}
+                "clocks": clk.summary(), "gpu_launches": int(launches), "coeff_block": coeff}
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.barrier()

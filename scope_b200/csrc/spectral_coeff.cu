@@ -3,7 +3,7 @@
 // coefficients the attention bias consumes, fused so that none of the
 // reference's [B,H,L,M,K] intermediates is materialised.
 //
-// One CTA of 128 threads per 128-token tile of one head (two CTAs per SM):
+// One CTA of 256 threads per 128-token tile of one head (two CTAs per SM):
 //   TMA      q tile [128 x 64] bf16, W1 [128 x 64], W2 [n_out x 128] (zero rows
 //            up to NP = n_out rounded up to 16), 128-byte swizzled, K-major
 //   tcgen05  D1 = q W1^T into TMEM columns [0, 128)
@@ -16,9 +16,16 @@
 //            softmax, budget logits, slope = c tanh, the Gaussian weights a_mk
 //            over log omega, and coeff_cos/sin[k] = sum_m pi_m a_mk cos/sin(w_k delta*_m),
 //            b0 = sum_k coeff_cos, delta_main, width.
-// Thread r of the CTA owns token row r, which is also TMEM lane r.  Every
-// arithmetic step follows the reference's operation order with explicit
-// roundings (no contraction into FMAs where the reference rounds twice).
+// Threads r and r + 128 share token row r (TMEM lane r): each forms half of
+// the hidden units and the mixture over half of the pointers, and the two
+// halves of the coefficient sums meet in shared memory.  The arithmetic
+// follows the reference's operation order with explicit roundings (no
+// contraction into FMAs where the reference rounds twice); divisions by a
+// per-row or per-pointer value are multiplications by its correctly rounded
+// reciprocal, cos/sin take the phase reduced to [-pi, pi] by a two-term 2*pi
+// (Cody and Waite), and the SiLU (rounded to bf16 right after) and the
+// Gaussian weights use the hardware exponent -- each within a few ulp of the
+// reference; delta*, mu, sigma and pi keep the accurate exponent.
 #include <cmath>
 #include <cstring>
 
@@ -63,17 +70,26 @@ struct Layout {
 };
 
 __device__ __forceinline__ float bf16r(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
-__device__ __forceinline__ float sigmoid_ref(float x) { return __fdiv_rn(1.f, __fadd_rn(1.f, expf(-x))); }
+__device__ __forceinline__ float sigmoid_ref(float x) { return __frcp_rn(__fadd_rn(1.f, expf(-x))); }
+// cos / sin of a float32 phase: reduce by the nearest multiple of 2*pi, split
+// in two float32 terms, then the hardware approximation on [-pi, pi]
+__device__ __forceinline__ void sincos_phase(float ph, float *s, float *c) {
+    constexpr float kTwoPiHi = 6.28318548202514648f, kTwoPiLo = -1.7484555314695172e-07f, kInvTwoPi = 0.159154943091895336f;
+    const float k = rintf(__fmul_rn(ph, kInvTwoPi));
+    float r = fmaf(-k, kTwoPiHi, ph);
+    r = fmaf(-k, kTwoPiLo, r);
+    __sincosf(r, s, c);
+}
 
 template <int K, int M, int NP>
-__global__ void __launch_bounds__(128, 2) coeff_kernel(const __grid_constant__ Maps maps, const Params p) {
+__global__ void __launch_bounds__(256, 2) coeff_kernel(const __grid_constant__ Maps maps, const Params p) {
     using L = Layout<NP>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
     uint64_t *bars = reinterpret_cast<uint64_t *>(smem + L::BAR);   // [0] loads, [1] MMA 1, [2] MMA 2
     uint32_t *tslot = reinterpret_cast<uint32_t *>(smem + L::BAR + 32);
 
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, r = threadIdx.x;
+    const int warp = threadIdx.x >> 5, r = threadIdx.x & 127, half = threadIdx.x >> 7;
     const int tiles_per_head = p.T / BM;
     const int h = blockIdx.x / tiles_per_head, t0 = (blockIdx.x - h * tiles_per_head) * BM;
     const bool per_head = p.w_heads > 1;
@@ -93,7 +109,7 @@ __global__ void __launch_bounds__(128, 2) coeff_kernel(const __grid_constant__ M
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tslot;
-    const uint32_t lb = (uint32_t)(warp * 32) << 16;
+    const uint32_t lb = (uint32_t)((warp & 3) * 32) << 16;
 
     if (threadIdx.x == 0) {
         mbar_expect_tx(&bars[0], L::TX);
@@ -121,7 +137,7 @@ __global__ void __launch_bounds__(128, 2) coeff_kernel(const __grid_constant__ M
     if (ok) {
         const uint16_t *b1 = p.b1 + (size_t)hw * HID;
 #pragma unroll 1
-        for (int c4 = 0; c4 < HID / 32; ++c4) {
+        for (int c4 = 2 * half; c4 < 2 * half + 2; ++c4) {
             uint32_t v[32];
             tmem_ld32(tmem + lb + 32 * c4, v);
             tmem_wait_ld();
@@ -136,7 +152,9 @@ __global__ void __launch_bounds__(128, 2) coeff_kernel(const __grid_constant__ M
                     // per-head weights: the reference's einsum rounds to bf16 before its bias add
                     const float acc = per_head ? bf16r(__uint_as_float(v[e + u])) : __uint_as_float(v[e + u]);
                     const float x = bf16r(__fadd_rn(acc, bf16_to_f32(__ldg(b1 + j))));
-                    s2[u] = bf16r(__fdiv_rn(x, __fadd_rn(1.f, expf(-x))));
+                    // rounded to bf16 at once: the hardware exponent and divide change it
+                    // only where x / (1 + e^-x) lies within ~1e-7 of a bf16 rounding boundary
+                    s2[u] = bf16r(__fdividef(x, __fadd_rn(1.f, __expf(-x))));
                 }
                 pk[e / 2] = pack_bf16(s2[0], s2[1]);
             }
@@ -165,6 +183,7 @@ __global__ void __launch_bounds__(128, 2) coeff_kernel(const __grid_constant__ M
         tc_commit(&bars[2]);
     }
     ok = ok && mbar_wait(&bars[2], 0);
+    ok = __syncthreads_and(ok);   // uniform: the exchange below synchronises all 256 threads
     tc_fence_after();
 
     if (ok) {
@@ -214,65 +233,81 @@ __global__ void __launch_bounds__(128, 2) coeff_kernel(const __grid_constant__ M
             pi[m] = expf(__fsub_rn(y[3 * M + m], pmax));
             psum = __fadd_rn(psum, pi[m]);
         }
+        const float rps = __frcp_rn(psum);
 #pragma unroll
-        for (int m = 0; m < M; ++m) pi[m] = __fdiv_rn(pi[m], psum);
+        for (int m = 0; m < M; ++m) pi[m] = __fmul_rn(pi[m], rps);
+        // the mixture over this thread's half of the pointers
         float cc[K], cs[K];
 #pragma unroll
         for (int k = 0; k < K; ++k) cc[k] = cs[k] = 0.f;
 #pragma unroll
-        for (int m = 0; m < M; ++m) {
-            const float den = __fmul_rn(2.f, __fmul_rn(sg[m], sg[m]));
+        for (int mm = 0; mm < M / 2; ++mm) {
+            const int m = half * (M / 2) + mm;
+            float dsm = ds[0], sgm = sg[0], mum = mu[0], pim = pi[0];
+#pragma unroll
+            for (int i = 1; i < M; ++i)
+                if (i == m) dsm = ds[i], sgm = sg[i], mum = mu[i], pim = pi[i];
+            const float rden = __frcp_rn(__fmul_rn(2.f, __fmul_rn(sgm, sgm)));
             float a[K], asum = 0.f;
 #pragma unroll
             for (int k = 0; k < K; ++k) {
-                const float d = __fsub_rn(__ldg(p.log_omegas + k), mu[m]);
-                a[k] = expf(__fdiv_rn(-__fmul_rn(d, d), den));
+                const float d = __fsub_rn(__ldg(p.log_omegas + k), mum);
+                a[k] = __expf(__fmul_rn(-__fmul_rn(d, d), rden));   // relative error ~1e-7
                 asum = __fadd_rn(asum, a[k]);
             }
-            const float an = __fadd_rn(asum, p.eps);
+            const float ran = __frcp_rn(__fadd_rn(asum, p.eps));
 #pragma unroll
             for (int k = 0; k < K; ++k) {
-                const float w = __fmul_rn(pi[m], __fdiv_rn(a[k], an));
+                const float w = __fmul_rn(pim, __fmul_rn(a[k], ran));
                 float sn, c;
-                sincosf(__fmul_rn(__ldg(p.omegas + k), ds[m]), &sn, &c);
+                sincos_phase(__fmul_rn(__ldg(p.omegas + k), dsm), &sn, &c);
                 cc[k] = __fadd_rn(cc[k], __fmul_rn(w, c));
                 cs[k] = __fadd_rn(cs[k], __fmul_rn(w, sn));
             }
         }
-        float b0 = 0.f;
-        if (p.subtract_b0) {
+        // exchange: half 0 finishes coeff_cos (needs half 1's cos sums), half 1 coeff_sin
+        float *xch = reinterpret_cast<float *>(smem + L::Q);   // [2][K][128] (16 KB at most): the q tile is idle now
 #pragma unroll
-            for (int k = 0; k < K; ++k) b0 = __fadd_rn(b0, cc[k]);
+        for (int k = 0; k < K; ++k) xch[(half * K + k) * 128 + r] = half ? cc[k] : cs[k];
+        asm volatile("bar.sync 1, 256;" ::: "memory");
+        float fin[K];
+#pragma unroll
+        for (int k = 0; k < K; ++k) {
+            const float other = xch[((1 - half) * K + k) * 128 + r];
+            fin[k] = half ? __fadd_rn(other, cs[k]) : __fadd_rn(cc[k], other);
         }
-        // ---- stores: [H,T,K] coefficients, [H,T,M] per-pointer values, [H,T] scalars
-        float *oc = p.coeff_cos + row * K, *os = p.coeff_sin + row * K;
+        float b0 = 0.f;
+        if (p.subtract_b0 && !half) {
+#pragma unroll
+            for (int k = 0; k < K; ++k) b0 = __fadd_rn(b0, fin[k]);
+        }
+        // ---- stores: [H,T,K] coefficients (cos by half 0, sin by half 1), [H,T,M], [H,T]
+        float *oc = (half ? p.coeff_sin : p.coeff_cos) + row * K;
         if constexpr (K % 4 == 0) {
 #pragma unroll
-            for (int k = 0; k < K; k += 4) {
-                *reinterpret_cast<float4 *>(oc + k) = make_float4(cc[k], cc[k + 1], cc[k + 2], cc[k + 3]);
-                *reinterpret_cast<float4 *>(os + k) = make_float4(cs[k], cs[k + 1], cs[k + 2], cs[k + 3]);
-            }
+            for (int k = 0; k < K; k += 4) *reinterpret_cast<float4 *>(oc + k) = make_float4(fin[k], fin[k + 1], fin[k + 2], fin[k + 3]);
         } else {
 #pragma unroll
-            for (int k = 0; k < K; ++k) {
-                oc[k] = cc[k];
-                os[k] = cs[k];
-            }
+            for (int k = 0; k < K; ++k) oc[k] = fin[k];
         }
+        if (!half) {
 #pragma unroll
-        for (int m = 0; m < M; ++m) {
-            p.delta_star[row * M + m] = ds[m];
-            p.pi[row * M + m] = pi[m];
-            p.budget[row * M + m] = y[4 * M + m];
+            for (int m = 0; m < M; ++m) {
+                p.delta_star[row * M + m] = ds[m];
+                p.pi[row * M + m] = pi[m];
+                p.budget[row * M + m] = y[4 * M + m];
+            }
+            p.b0[row] = b0;
+        } else {
+            p.slope[row] = p.use_slope ? __fmul_rn(p.c_scale, tanhf(y[5 * M])) : 0.f;
+            p.delta_main[row] = dmain;
+            p.width[row] = __fadd_rn(
+                p.width_min, __fmul_rn(__fsub_rn(p.width_max, p.width_min), sigmoid_ref(__fmul_rn(musum, 1.f / M))));
         }
-        p.slope[row] = p.use_slope ? __fmul_rn(p.c_scale, tanhf(y[5 * M])) : 0.f;
-        p.b0[row] = b0;
-        p.delta_main[row] = dmain;
-        p.width[row] = __fadd_rn(p.width_min,
-                                 __fmul_rn(__fsub_rn(p.width_max, p.width_min), sigmoid_ref(__fdiv_rn(musum, (float)M))));
     } else if (threadIdx.x == 0) {
         set_err(p.err, SCOPE_DEVERR_TIMEOUT);
     }
+
     // the MMAs are complete (or their wait gave up: wait once more, bounded) before TMEM is freed
     if (!ok && threadIdx.x == 0) {
         mbar_wait(&bars[1], 0, 500000000ull);
@@ -344,7 +379,7 @@ static int launch(const ScopeCoeffArgs &a, cudaStream_t s) {
     if (cudaFuncSetAttribute(coeff_kernel<K, M, NP>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
         cudaSuccess)
         return SCOPE_ERR_CUDA;
-    coeff_kernel<K, M, NP><<<(unsigned)(a.H * (a.T / BM)), 128, smem, s>>>(maps, p);
+    coeff_kernel<K, M, NP><<<(unsigned)(a.H * (a.T / BM)), 256, smem, s>>>(maps, p);
     SCOPE_CHECK_LAUNCH();
     return SCOPE_OK;
 }
