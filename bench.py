@@ -523,7 +523,9 @@ def main():
             pipe.step()
         pipe.finish()
         torch.cuda.synchronize()
-        e_steps = max(3, args.steps // 2)
+        # enough steps that the pipeline's fill (the first H2D) and drain (the last
+        # D2H), which overlap nothing, do not dominate the per-step figure
+        e_steps = max(8, args.steps)
         ms_e = time_e2e(pipe, e_steps, world)
         h2d = sum(t.numel() * t.element_size() for t in host["in"].values())
         d2h = sum(t.numel() * t.element_size() for t in host["out"].values())
