@@ -4,8 +4,9 @@
 //   prep   delta_i = sum_d dO_i . O_i  and  lse2_i = lse_i * log2(e)   (workspace)
 //   plan   per (head, kv block) the number of q blocks that see it (from the
 //          builder's q-side bitmap) and the dK/dV work items
-//   dkv    one CTA per work item (a kv block and a run of the q blocks that see
-//          it, ascending): dV += P^T dO and dK += dS^T Q in TMEM.
+//   dkv    persistent, one CTA per SM walking the work items (a kv block and a
+//          run of the q blocks that see it, ascending): dV += P^T dO and
+//          dK += dS^T Q in TMEM.
 //   dq     persistent, one CTA per SM walking the (head, q block) items: the kv
 //          list like the forward, dQ += dS K (and, for the qk_aug spectral bias,
 //          the gradient of the augmented dims, turned into dcoeff_cos /
@@ -320,22 +321,31 @@ __device__ __forceinline__ void dq_piece(float (&s)[16], const float (&dp)[16], 
 }
 
 // ============================================================================ dK / dV
-// Resident: K, the k_aug dims, V.  Streamed per q tile (ring of NST stages):
-// Q, the q_aug dims, dO, lse2, delta.
+// Persistent: one CTA per SM walks the work items b, b + G, b + 2G, ... of the
+// plan (G CTAs), so that the next item's resident tiles load and its first
+// tiles run while the previous item's epilogue drains.  Resident per item (two
+// buffers, item ci in buffer ci & 1): K, the k_aug dims, V.  Streamed per q tile
+// (ring of NST stages, one tile counter across items): Q, the q_aug dims, dO,
+// lse2, delta.
 template <int DA>
 struct KVL {
     static constexpr int NA = DA / 16;
     static constexpr uint32_t TILE = BM * HD * 2, ATILE = BM * 16 * 2;
-    static constexpr uint32_t K = 0, KA = TILE, V = align1k(TILE + NA * ATILE);
-    static constexpr uint32_t STAGE0 = V + TILE;
+    static constexpr uint32_t K = 0, KA = TILE, V = align1k(TILE + NA * ATILE);   // within a resident buffer
+    static constexpr uint32_t RESB = align1k(V + TILE);
+    static constexpr uint32_t STAGE0 = 2 * RESB;
     static constexpr uint32_t SQ = 0, SQA = TILE, SDO = align1k(TILE + NA * ATILE), SLSE = SDO + TILE,
                               SDEL = SLSE + 512;
     static constexpr uint32_t STAGE = align1k(SDEL + 512);
-    static constexpr int NST = STAGE0 + 4 * STAGE + 2048 <= kSmemBudget ? 4 : 3;
+    static constexpr uint32_t EXTRA = 1024 + 1024;                  // barriers, base alignment
+    static constexpr int NST = STAGE0 + 4 * STAGE + EXTRA <= kSmemBudget
+                                   ? 4
+                                   : (STAGE0 + 3 * STAGE + EXTRA <= kSmemBudget ? 3 : 2);
     static constexpr uint32_t BAR = STAGE0 + NST * STAGE;
     static constexpr uint32_t RES_BYTES = 2 * TILE + NA * ATILE;
     static constexpr uint32_t TOTAL = BAR + sizeof(Bars);
     static constexpr uint32_t Q_BYTES = 2 * TILE + NA * ATILE + 1024;
+    static_assert(TOTAL + 1024 <= kSmemBudget, "shared memory");
 };
 
 // rank-th set bit onward of a bitmap row: the word index and remaining bits
@@ -355,18 +365,13 @@ template <int DA>
 __global__ void __launch_bounds__(kThreads, 1) dkv_kernel(const __grid_constant__ Maps maps, const Params p) {
     using L = KVL<DA>;
     constexpr int NA = L::NA, NST = L::NST;
-    if ((int)blockIdx.x >= *p.plan.n_items) return;
-    const int4 item = p.plan.items[blockIdx.x];
-    const int slot = p.plan.item_slot[blockIdx.x];
-    const int h = item.x, kb = item.y, first = item.z, nq = item.w;
-
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
     Bars &B = *reinterpret_cast<Bars *>(smem + L::BAR);
     Ctx cx{&B.abort_flag, p.err};
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const uint32_t *brow = p.q_bitmap + ((int64_t)h * p.QB + kb) * p.words;
+    const int n_items = *p.plan.n_items, G = gridDim.x;
 
     if (threadIdx.x == 0) B.init(NST);
     if (warp == 1) {
@@ -380,57 +385,87 @@ __global__ void __launch_bounds__(kThreads, 1) dkv_kernel(const __grid_constant_
     const uint32_t tmem = B.tmem_slot;
 
     if (warp == 0) {
-        // ---------------- producer: K / V once, then the q tiles that see this kv block, ascending
-        if (lane == 0 && nq > 0) {
-            mbar_expect_tx(&B.res_full[0], L::RES_BYTES);
-            tma_load_3d(&maps.k, smem + L::K, &B.res_full[0], 0, kb * BM, h);
+        // ---------------- producer: per item K / V into its resident buffer, then the q tiles
+        // that see the kv block, ascending
+        if (lane == 0) {
+            int gt = 0, ci = 0, last_res = -1;
+            bool ok = true;
+            for (int it = blockIdx.x; ok && it < n_items; it += G, ++ci) {
+                const int4 item = p.plan.items[it];
+                const int h = item.x, kb = item.y, first = item.z, nq = item.w;
+                const int rb = ci & 1;
+                uint8_t *res = smem + rb * L::RESB;
+                // buffer rb is free once the epilogue of item ci - 2 is done with it
+                if (ci >= 2 && !cx.wait1(&B.acc_free[rb], ((ci >> 1) - 1) & 1)) break;
+                if (nq > 0) {
+                    mbar_expect_tx(&B.res_full[rb], L::RES_BYTES);
+                    tma_load_3d(&maps.k, res + L::K, &B.res_full[rb], 0, kb * BM, h);
 #pragma unroll
-            for (int a = 0; a < NA; ++a) tma_load_2d(&maps.ka, smem + L::KA + a * L::ATILE, &B.res_full[0], 16 * a, kb * BM);
-            tma_load_3d(&maps.v, smem + L::V, &B.res_full[0], 0, kb * BM, h);
-            int w;
-            uint32_t bits;
-            seek_rank(brow, p.words, first, w, bits);
-            int t = 0;
-            while (t < nq && w < p.words) {
-                if (!bits) {
-                    if (++w < p.words) bits = brow[w];
-                    continue;
+                    for (int a = 0; a < NA; ++a)
+                        tma_load_2d(&maps.ka, res + L::KA + a * L::ATILE, &B.res_full[rb], 16 * a, kb * BM);
+                    tma_load_3d(&maps.v, res + L::V, &B.res_full[rb], 0, kb * BM, h);
+                    last_res = ci;
+                } else {
+                    mbar_arrive(&B.res_full[rb]);      // keeps the buffer's phases in step
                 }
-                const int qb = w * 32 + __ffs(bits) - 1;
-                bits &= bits - 1;
-                const int st = t % NST;
-                if (t >= NST && !cx.wait1(&B.empty[st], ((t / NST) - 1) & 1)) break;
-                uint8_t *sb = smem + L::STAGE0 + st * L::STAGE;
-                B.stage_blk[st] = qb;
-                B.stage_mk[st] = tile_mask_kind(qb, kb, p.docs != nullptr, p.block_info, p.QB);
-                mbar_expect_tx(&B.full[st], L::Q_BYTES);
-                tma_load_3d(&maps.q, sb + L::SQ, &B.full[st], 0, qb * BM, h);
+                const uint32_t *brow = p.q_bitmap + ((int64_t)h * p.QB + kb) * p.words;
+                int w;
+                uint32_t bits;
+                seek_rank(brow, p.words, first, w, bits);
+                int t = 0;
+                while (t < nq && w < p.words) {
+                    if (!bits) {
+                        if (++w < p.words) bits = brow[w];
+                        continue;
+                    }
+                    const int qb = w * 32 + __ffs(bits) - 1;
+                    bits &= bits - 1;
+                    const int st = gt % NST;
+                    if (gt >= NST && !cx.wait1(&B.empty[st], ((gt / NST) - 1) & 1)) { ok = false; break; }
+                    uint8_t *sb = smem + L::STAGE0 + st * L::STAGE;
+                    B.stage_blk[st] = qb;
+                    B.stage_mk[st] = tile_mask_kind(qb, kb, p.docs != nullptr, p.block_info, p.QB);
+                    mbar_expect_tx(&B.full[st], L::Q_BYTES);
+                    tma_load_3d(&maps.q, sb + L::SQ, &B.full[st], 0, qb * BM, h);
 #pragma unroll
-                for (int a = 0; a < NA; ++a)
-                    tma_load_3d(&maps.qa, sb + L::SQA + a * L::ATILE, &B.full[st], 16 * a, qb * BM, h);
-                tma_load_3d(&maps.dout, sb + L::SDO, &B.full[st], 0, qb * BM, h);
-                const int64_t off = (int64_t)h * p.T + (int64_t)qb * BM;
-                bulk_load(sb + L::SLSE, p.lse2 + off, 512, &B.full[st]);
-                bulk_load(sb + L::SDEL, p.delta + off, 512, &B.full[st]);
-                ++t;
+                    for (int a = 0; a < NA; ++a)
+                        tma_load_3d(&maps.qa, sb + L::SQA + a * L::ATILE, &B.full[st], 16 * a, qb * BM, h);
+                    tma_load_3d(&maps.dout, sb + L::SDO, &B.full[st], 0, qb * BM, h);
+                    const int64_t off = (int64_t)h * p.T + (int64_t)qb * BM;
+                    bulk_load(sb + L::SLSE, p.lse2 + off, 512, &B.full[st]);
+                    bulk_load(sb + L::SDEL, p.delta + off, 512, &B.full[st]);
+                    ++t;
+                    ++gt;
+                }
+                if (ok && t < nq) {   // the plan promised more q blocks than the bitmap row holds
+                    set_err(p.err, SCOPE_DEVERR_INDEX);
+                    cx.give_up();
+                    ok = false;
+                }
             }
             // never leave the CTA with a TMA write still in flight
-            mbar_wait(&B.res_full[0], 0, 500000000ull);
-            for (int j = (t > NST ? t - NST : 0); j < t; ++j) mbar_wait(&B.full[j % NST], (j / NST) & 1, 500000000ull);
+            if (last_res >= 0) mbar_wait(&B.res_full[last_res & 1], (last_res >> 1) & 1, 500000000ull);
+            for (int j = (gt > NST ? gt - NST : 0); j < gt; ++j) mbar_wait(&B.full[j % NST], (j / NST) & 1, 500000000ull);
         }
     } else if (warp == 1) {
         // ---------------- S / dP issuer (the whole warp waits, lane 0 issues)
-        if (nq > 0) {
-            constexpr uint32_t idS = idesc_bf16(128, 128, false, false);
-            const uint32_t sK = smem_u32(smem + L::K), sKA = smem_u32(smem + L::KA), sV = smem_u32(smem + L::V);
-            bool ok = cx.waitw(&B.res_full[0], 0);
-            for (int t = 0; ok && t < nq; ++t) {
-                const int st = t % NST, b = t & 1;
-                if (!cx.waitw(&B.full[st], (t / NST) & 1)) { ok = false; break; }
+        constexpr uint32_t idS = idesc_bf16(128, 128, false, false);
+        int gt = 0, ci = 0;
+        bool ok = true;
+        for (int it = blockIdx.x; ok && it < n_items; it += G, ++ci) {
+            const int nq = p.plan.items[it].w;
+            if (nq == 0) continue;
+            const int rb = ci & 1;
+            const uint32_t res = smem_u32(smem + rb * L::RESB);
+            const uint32_t sK = res + L::K, sKA = res + L::KA, sV = res + L::V;
+            if (!cx.waitw(&B.res_full[rb], (ci >> 1) & 1)) { ok = false; break; }
+            for (int t = 0; t < nq; ++t, ++gt) {
+                const int st = gt % NST, b = gt & 1;
+                if (!cx.waitw(&B.full[st], (gt / NST) & 1)) { ok = false; break; }
                 const uint32_t sb = smem_u32(smem + L::STAGE0 + st * L::STAGE);
                 // dP^T = V dO^T first: the elementwise warps release dP^T of the previous tile
-                // as they start it, while S^T waits for the gradient MMAs of tile t-2
-                if (t >= 1 && !cx.waitw(&B.dp_free, (t - 1) & 1)) { ok = false; break; }
+                // as they start it, while S^T waits for the gradient MMAs of tile gt-2
+                if (gt >= 1 && !cx.waitw(&B.dp_free, (gt - 1) & 1)) { ok = false; break; }
                 tc_fence_after();
                 if (lane == 0) {
 #pragma unroll
@@ -441,7 +476,7 @@ __global__ void __launch_bounds__(kThreads, 1) dkv_kernel(const __grid_constant_
                 }
                 __syncwarp();
                 // S^T = K Q^T (+ Kaug Qaug^T): 128 kv rows x 128 q columns
-                if (t >= 2 && !cx.waitw(&B.s_free[b], ((t >> 1) - 1) & 1)) { ok = false; break; }
+                if (gt >= 2 && !cx.waitw(&B.s_free[b], ((gt >> 1) - 1) & 1)) { ok = false; break; }
                 tc_fence_after();
                 if (lane == 0) {
 #pragma unroll
@@ -456,23 +491,31 @@ __global__ void __launch_bounds__(kThreads, 1) dkv_kernel(const __grid_constant_
                 }
                 __syncwarp();
             }
-            if (!ok) cx.give_up();
-            if (lane == 0) tc_commit(&B.drain[0]);   // TMEM is freed only after this warp's MMAs completed
-            mbar_wait(&B.drain[0], 0, 500000000ull);
         }
+        if (!ok) cx.give_up();
+        if (lane == 0) tc_commit(&B.drain[0]);   // TMEM is freed only after this warp's MMAs completed
+        mbar_wait(&B.drain[0], 0, 500000000ull);
     } else if (warp == kGradWarp) {
         // ---------------- gradient issuer (whole warp): a second issuing warp, so
         // the S / dP MMAs and these queue on the tensor pipe side by side
-        if (nq > 0) {
-            constexpr uint32_t idG = idesc_bf16(128, 64, false, true);
-            bool ok = true;
-            for (int t = 0; ok && t < nq; ++t) {
-                const int st = t % NST, b = t & 1;
+        constexpr uint32_t idG = idesc_bf16(128, 64, false, true);
+        int gt = 0, ci = 0;
+        bool ok = true;
+        for (int it = blockIdx.x; ok && it < n_items; it += G, ++ci) {
+            const int nq = p.plan.items[it].w;
+            for (int t = 0; t < nq; ++t, ++gt) {
+                const int st = gt % NST, b = gt & 1;
                 const uint32_t sb = smem_u32(smem + L::STAGE0 + st * L::STAGE);
                 // dV += P^T dO, dK += dS^T Q over the tile's 128 q rows: the even K steps
                 // (16-column chunks) as soon as every warp has written them, then the odd
                 for (int half = 0; half < 2; ++half) {
-                    if (!cx.waitw(half ? &B.p_full[b] : &B.p_half[b], (t >> 1) & 1)) { ok = false; break; }
+                    if (!cx.waitw(half ? &B.p_full[b] : &B.p_half[b], (gt >> 1) & 1)) { ok = false; break; }
+                    // the first MMA of an item overwrites the accumulators: the previous
+                    // item's epilogue must have read them
+                    if (!half && t == 0 && ci >= 1 && !cx.waitw(&B.acc_free[(ci - 1) & 1], ((ci - 1) >> 1) & 1)) {
+                        ok = false;
+                        break;
+                    }
                     tc_fence_after();
                     if (lane == 0) {
 #pragma unroll
@@ -484,111 +527,125 @@ __global__ void __launch_bounds__(kThreads, 1) dkv_kernel(const __grid_constant_
                             mma_ts(tmem + ACC1, tmem + sbuf(b) + a_col(kk) + 8, mnmajor128_desc(sb + L::SQ + kk * 2048),
                                    idG, acc);
                         }
-                        // commit only arrivals someone waits for
-                        if (half && t + 2 < nq) tc_commit(&B.s_free[b]);
-                        if (half && t + NST < nq) tc_commit(&B.empty[st]);
+                        if (half) {
+                            tc_commit(&B.s_free[b]);
+                            tc_commit(&B.empty[st]);
+                        }
                     }
                     __syncwarp();
                 }
                 if (!ok) break;
             }
-            if (ok && lane == 0) tc_commit(&B.acc_done);
-            if (!ok) cx.give_up();
-            if (lane == 0) tc_commit(&B.drain[1]);
-            mbar_wait(&B.drain[1], 0, 500000000ull);
+            if (!ok) break;
+            if (lane == 0) tc_commit(&B.acc_done);   // every item, so the epilogue's phases stay in step
+            __syncwarp();
         }
+        if (!ok) cx.give_up();
+        if (lane == 0) tc_commit(&B.drain[1]);
+        mbar_wait(&B.drain[1], 0, 500000000ull);
     } else {
         // ---------------- elementwise: thread = kv row c, tile columns [32qc, 32qc+32) in two chunks of 16
         const int quad = warp & 3;
         const int qc = (warp - 2) >> 2;
         const int c = quad * 32 + lane;
-        const int j = kb * BM + c;
         const uint32_t lb = (uint32_t)(quad * 32) << 16;
         const bool have_docs = p.docs != nullptr;
-        const int doc_j = have_docs ? p.docs[j] : 0;
         const uint64_t c2 = f2_pack(p.scale_log2, p.scale_log2);
+        int gt = 0, ci = 0;
         bool alive = true;
-        for (int t = 0; t < nq && alive; ++t) {
-            const int st = t % NST, b = t & 1;
-            if (!cx.waitw(&B.full[st], (t / NST) & 1)) { alive = false; break; }
-            const int qb = B.stage_blk[st];
-            const int mk = B.stage_mk[st];
-            if (!cx.waitw(&B.s_full[b], (t >> 1) & 1) || !cx.waitw(&B.dp_full, t & 1)) { alive = false; break; }
-            tc_fence_after();
-            const uint8_t *sbp = smem + L::STAGE0 + st * L::STAGE;
-            uint32_t rs[16], rp0[16], rp1[16];
-            ld_tile_start(tmem + lb + sbuf(b) + qc * 32, tmem + lb + DPC + qc * 32, rs, rp0, rp1);
-            tc_fence_before();
-            mbar_arrive_warp(&B.dp_free);           // this warp's dP^T columns are in registers
+        for (int it = blockIdx.x; alive && it < n_items; it += G, ++ci) {
+            const int4 item = p.plan.items[it];
+            const int slot = p.plan.item_slot[it];
+            const int h = item.x, kb = item.y, nq = item.w;
+            const int rb = ci & 1;
+            const int j = kb * BM + c;
+            const int doc_j = have_docs ? p.docs[j] : 0;
+            for (int t = 0; t < nq; ++t, ++gt) {
+                const int st = gt % NST, b = gt & 1;
+                if (!cx.waitw(&B.full[st], (gt / NST) & 1)) { alive = false; break; }
+                const int qb = B.stage_blk[st];
+                const int mk = B.stage_mk[st];
+                if (!cx.waitw(&B.s_full[b], (gt >> 1) & 1) || !cx.waitw(&B.dp_full, gt & 1)) { alive = false; break; }
+                tc_fence_after();
+                const uint8_t *sbp = smem + L::STAGE0 + st * L::STAGE;
+                uint32_t rs[16], rp0[16], rp1[16];
+                ld_tile_start(tmem + lb + sbuf(b) + qc * 32, tmem + lb + DPC + qc * 32, rs, rp0, rp1);
+                tc_fence_before();
+                mbar_arrive_warp(&B.dp_free);           // this warp's dP^T columns are in registers
 #pragma unroll
-            for (int cc = 0; cc < 2; ++cc) {
-                const int col0 = qc * 32 + cc * 16;  // q row within the tile of the chunk's first column
-                const uint32_t tc = tmem + lb + sbuf(b) + col0;
-                if (cc == 1) ld_cols16(tc, rs);
-                float s[16], dp[16];
+                for (int cc = 0; cc < 2; ++cc) {
+                    const int col0 = qc * 32 + cc * 16;  // q row within the tile of the chunk's first column
+                    const uint32_t tc = tmem + lb + sbuf(b) + col0;
+                    if (cc == 1) ld_cols16(tc, rs);
+                    float s[16], dp[16];
 #pragma unroll
-                for (int e = 0; e < 16; ++e) {
-                    s[e] = __uint_as_float(rs[e]);
-                    dp[e] = __uint_as_float(cc ? rp1[e] : rp0[e]);
+                    for (int e = 0; e < 16; ++e) {
+                        s[e] = __uint_as_float(rs[e]);
+                        dp[e] = __uint_as_float(cc ? rp1[e] : rp0[e]);
+                    }
+                    const float4 *LS = reinterpret_cast<const float4 *>(sbp + L::SLSE) + col0 / 4;
+                    const float4 *DL = reinterpret_cast<const float4 *>(sbp + L::SDEL) + col0 / 4;
+                    const int i0 = qb * BM + col0;
+                    const int lim = j - i0;              // column e visible iff e >= lim (causal: j <= i)
+                    if (mk == MASK_FULL) dkv_piece<false>(s, dp, LS, DL, c2, mk, lim, p.docs, i0, doc_j);
+                    else dkv_piece<true>(s, dp, LS, DL, c2, mk, lim, p.docs, i0, doc_j);
+                    st_bf16x16(tc, s);                   // P^T pairs, then dS^T pairs, over the chunk's own columns
+                    st_bf16x16(tc + 8, dp);
+                    if (cc == 0) {
+                        tmem_wait_st();
+                        tc_fence_before();
+                        mbar_arrive_warp(&B.p_half[b]);
+                    }
                 }
-                const float4 *LS = reinterpret_cast<const float4 *>(sbp + L::SLSE) + col0 / 4;
-                const float4 *DL = reinterpret_cast<const float4 *>(sbp + L::SDEL) + col0 / 4;
-                const int i0 = qb * BM + col0;
-                const int lim = j - i0;              // column e visible iff e >= lim (causal: j <= i)
-                if (mk == MASK_FULL) dkv_piece<false>(s, dp, LS, DL, c2, mk, lim, p.docs, i0, doc_j);
-                else dkv_piece<true>(s, dp, LS, DL, c2, mk, lim, p.docs, i0, doc_j);
-                st_bf16x16(tc, s);                   // P^T pairs, then dS^T pairs, over the chunk's own columns
-                st_bf16x16(tc + 8, dp);
-                if (cc == 0) {
-                    tmem_wait_st();
-                    tc_fence_before();
-                    mbar_arrive_warp(&B.p_half[b]);
-                }
+                tmem_wait_st();
+                tc_fence_before();
+                mbar_arrive_warp(&B.p_full[b]);
             }
-            tmem_wait_st();
-            tc_fence_before();
-            mbar_arrive_warp(&B.p_full[b]);
-        }
-        bool have = false;
-        if (alive && nq > 0) {
-            have = cx.waitw(&B.acc_done, 0);
+            if (!alive) break;
+            // ---------------- epilogue of the item
+            if (!cx.waitw(&B.acc_done, ci & 1)) { alive = false; break; }
             tc_fence_after();
-        }
-        // dV from ACC0 (quarters 0, 1), dK * scale from ACC1 (quarters 2, 3): 32 columns per warp
-        const int half = qc >> 1, c32 = (qc & 1) * 32;
-        const uint32_t acc = tmem + lb + (half == 0 ? ACC0 : ACC1) + c32;
-        const float mul = half == 0 ? 1.f : p.scale;
-        __nv_bfloat16 *dst = (half == 0 ? p.g1 + (int64_t)h * p.g1_sh + (int64_t)j * p.g1_st
-                                        : p.g0 + (int64_t)h * p.g0_sh + (int64_t)j * p.g0_st) + c32;
-        if (slot < 0) {
-            store_row<32>(acc, mul, dst, have);
-        } else {
-            // a chunk of a split row: add into the row's fp32 slot; the last chunk writes bf16
-            float *part = p.plan.partial + ((size_t)slot * BM + c) * 128 + qc * 32;
-            if (have) {
-                uint32_t o[32];
-                tmem_ld32_nw(acc, o);
-                tmem_wait_ld();
-                pin(o);
+            const bool have = nq > 0;
+            // dV from ACC0 (quarters 0, 1), dK * scale from ACC1 (quarters 2, 3): 32 columns per warp
+            const int half = qc >> 1, c32 = (qc & 1) * 32;
+            const uint32_t acc = tmem + lb + (half == 0 ? ACC0 : ACC1) + c32;
+            const float mul = half == 0 ? 1.f : p.scale;
+            __nv_bfloat16 *dst = (half == 0 ? p.g1 + (int64_t)h * p.g1_sh + (int64_t)j * p.g1_st
+                                            : p.g0 + (int64_t)h * p.g0_sh + (int64_t)j * p.g0_st) + c32;
+            if (slot < 0) {
+                store_row<32>(acc, mul, dst, have);
+            } else {
+                // a chunk of a split row: add into the row's fp32 slot; the last chunk writes bf16
+                float *part = p.plan.partial + ((size_t)slot * BM + c) * 128 + qc * 32;
+                if (have) {
+                    uint32_t o[32];
+                    tmem_ld32_nw(acc, o);
+                    tmem_wait_ld();
+                    pin(o);
 #pragma unroll
-                for (int e = 0; e < 32; ++e) atomicAdd(part + e, __uint_as_float(o[e]) * mul);
-            }
-            __threadfence();
-            elem_bar();
-            if (threadIdx.x == 64) {
-                const int done = atomicAdd(p.plan.slot_done + slot, 1);
-                B.last_flag = (done == p.plan.slot_chunks[slot] - 1) ? 1 : 0;
-            }
-            elem_bar();
-            if (B.last_flag) {
+                    for (int e = 0; e < 32; ++e) atomicAdd(part + e, __uint_as_float(o[e]) * mul);
+                }
                 __threadfence();
-                uint32_t w[16];
+                elem_bar();
+                if (threadIdx.x == 64) {
+                    const int done = atomicAdd(p.plan.slot_done + slot, 1);
+                    B.last_flag = (done == p.plan.slot_chunks[slot] - 1) ? 1 : 0;
+                }
+                elem_bar();
+                const bool last = B.last_flag != 0;
+                elem_bar();   // every thread read the flag before a later item writes it again
+                if (last) {
+                    __threadfence();
+                    uint32_t w[16];
 #pragma unroll
-                for (int e = 0; e < 16; ++e) w[e] = pack_bf16(__ldcg(part + 2 * e), __ldcg(part + 2 * e + 1));
-                uint4 *d = reinterpret_cast<uint4 *>(dst);
+                    for (int e = 0; e < 16; ++e) w[e] = pack_bf16(__ldcg(part + 2 * e), __ldcg(part + 2 * e + 1));
+                    uint4 *d = reinterpret_cast<uint4 *>(dst);
 #pragma unroll
-                for (int e = 0; e < 4; ++e) d[e] = make_uint4(w[4 * e], w[4 * e + 1], w[4 * e + 2], w[4 * e + 3]);
+                    for (int e = 0; e < 4; ++e) d[e] = make_uint4(w[4 * e], w[4 * e + 1], w[4 * e + 2], w[4 * e + 3]);
+                }
             }
+            tc_fence_before();
+            mbar_arrive_warp(&B.acc_free[rb]);   // accumulators read, resident buffer rb released
         }
     }
     __syncwarp();   // every warp reaches the CTA barrier converged (the producer ran on lane 0 alone)
@@ -1169,7 +1226,11 @@ int launch_bwd(const ScopeAttnArgs &a, cudaStream_t s) {
     if (cudaFuncSetAttribute(tcbwd::dkv_kernel<DA>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
         cudaSuccess)
         return SCOPE_ERR_CUDA;
-    tcbwd::dkv_kernel<DA><<<ws.max_items, tcbwd::kThreads, smem, s>>>(maps, p);
+    // persistent: one CTA per SM walks the plan's items
+    int dev = 0, n_sm = 148;
+    if (cudaGetDevice(&dev) != cudaSuccess || cudaDeviceGetAttribute(&n_sm, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+        return SCOPE_ERR_CUDA;
+    tcbwd::dkv_kernel<DA><<<std::min(ws.max_items, n_sm), tcbwd::kThreads, smem, s>>>(maps, p);
     SCOPE_CHECK_LAUNCH();
 
     // dQ (+ coefficient gradients)
@@ -1194,9 +1255,6 @@ int launch_bwd(const ScopeAttnArgs &a, cudaStream_t s) {
         cudaSuccess)
         return SCOPE_ERR_CUDA;
     // persistent: one CTA per SM (at most one per work item)
-    int dev = 0, n_sm = 148;
-    if (cudaGetDevice(&dev) != cudaSuccess || cudaDeviceGetAttribute(&n_sm, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
-        return SCOPE_ERR_CUDA;
     const int grid_q = std::min(a.H * QB, n_sm);
     tcbwd::dq_kernel<DA><<<grid_q, tcbwd::kThreads, smem, s>>>(maps, p);
     SCOPE_CHECK_LAUNCH();
