@@ -106,6 +106,7 @@ struct Plan {
     const int32_t *slot_chunks;
     int32_t *slot_done;
     float *partial;           // [kSlotCap][128 rows][128]: dV (64) | dK (64)
+    int32_t *next_item;       // dK/dV items handed out beyond the first G (zeroed by the plan kernel)
 };
 
 struct Params {
@@ -172,12 +173,13 @@ struct Bars {
     volatile int stage_mk[4];          // its mask kind
     uint32_t tmem_slot;
     volatile int abort_flag, last_flag, pad;
-    __device__ void init(int nst) {
+    volatile int item_of[2];           // dkv: the work item in resident buffer b, -1 when none is left
+    __device__ void init(int nst, int acc_free_count) {
         mbar_init(&res_full[0], 1);
         mbar_init(&res_full[1], 1);
         mbar_init(&acc_done, 1);
-        mbar_init(&acc_free[0], kElem);
-        mbar_init(&acc_free[1], kElem);
+        mbar_init(&acc_free[0], acc_free_count);
+        mbar_init(&acc_free[1], acc_free_count);
         for (int i = 0; i < nst; ++i) {
             mbar_init(&full[i], 1);
             mbar_init(&empty[i], 1);
@@ -321,9 +323,11 @@ __device__ __forceinline__ void dq_piece(float (&s)[16], const float (&dp)[16], 
 }
 
 // ============================================================================ dK / dV
-// Persistent: one CTA per SM walks the work items b, b + G, b + 2G, ... of the
-// plan (G CTAs), so that the next item's resident tiles load and its first
-// tiles run while the previous item's epilogue drains.  Resident per item (two
+// Persistent: one CTA per SM walks work items of the plan (its block index
+// first, then the next unclaimed one from an atomic counter: the items range
+// from 1 to kChunk q tiles), so that the next item's resident tiles load and
+// its first tiles run while the previous item's epilogue drains.  The
+// producer publishes each item's index with the resident buffer's barrier.  Resident per item (two
 // buffers, item ci in buffer ci & 1): K, the k_aug dims, V.  Streamed per q tile
 // (ring of NST stages, one tile counter across items): Q, the q_aug dims, dO,
 // lse2, delta.
@@ -373,7 +377,9 @@ __global__ void __launch_bounds__(kThreads, 1) dkv_kernel(const __grid_constant_
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int n_items = *p.plan.n_items, G = gridDim.x;
 
-    if (threadIdx.x == 0) B.init(NST);
+    // acc_free of a resident buffer: the elementwise threads after the item's epilogue,
+    // and each issuing warp once it has read the item's index
+    if (threadIdx.x == 0) B.init(NST, kElem + 2);
     if (warp == 1) {
         tmem_alloc(&B.tmem_slot, kTmemCols);
         tmem_relinquish();
@@ -388,15 +394,22 @@ __global__ void __launch_bounds__(kThreads, 1) dkv_kernel(const __grid_constant_
         // ---------------- producer: per item K / V into its resident buffer, then the q tiles
         // that see the kv block, ascending
         if (lane == 0) {
-            int gt = 0, ci = 0, last_res = -1;
+            int gt = 0, last_res = -1;
             bool ok = true;
-            for (int it = blockIdx.x; ok && it < n_items; it += G, ++ci) {
-                const int4 item = p.plan.items[it];
-                const int h = item.x, kb = item.y, first = item.z, nq = item.w;
+            for (int ci = 0; ok; ++ci) {
+                // the first item of each CTA is its block index, the rest are handed out in order
+                const int it = ci == 0 ? (int)blockIdx.x : G + atomicAdd(p.plan.next_item, 1);
                 const int rb = ci & 1;
                 uint8_t *res = smem + rb * L::RESB;
-                // buffer rb is free once the epilogue of item ci - 2 is done with it
+                // buffer rb is free once every role is done with item ci - 2
                 if (ci >= 2 && !cx.wait1(&B.acc_free[rb], ((ci >> 1) - 1) & 1)) break;
+                B.item_of[rb] = it < n_items ? it : -1;
+                if (it >= n_items) {
+                    mbar_arrive(&B.res_full[rb]);      // publishes "no item left"
+                    break;
+                }
+                const int4 item = p.plan.items[it];
+                const int h = item.x, kb = item.y, first = item.z, nq = item.w;
                 if (nq > 0) {
                     mbar_expect_tx(&B.res_full[rb], L::RES_BYTES);
                     tma_load_3d(&maps.k, res + L::K, &B.res_full[rb], 0, kb * BM, h);
@@ -450,15 +463,17 @@ __global__ void __launch_bounds__(kThreads, 1) dkv_kernel(const __grid_constant_
     } else if (warp == 1) {
         // ---------------- S / dP issuer (the whole warp waits, lane 0 issues)
         constexpr uint32_t idS = idesc_bf16(128, 128, false, false);
-        int gt = 0, ci = 0;
+        int gt = 0;
         bool ok = true;
-        for (int it = blockIdx.x; ok && it < n_items; it += G, ++ci) {
-            const int nq = p.plan.items[it].w;
-            if (nq == 0) continue;
+        for (int ci = 0; ok; ++ci) {
             const int rb = ci & 1;
+            if (!cx.waitw(&B.res_full[rb], (ci >> 1) & 1)) { ok = false; break; }
+            const int it = B.item_of[rb];
+            if (lane == 0) mbar_arrive(&B.acc_free[rb]);   // the index is read
+            if (it < 0) break;
+            const int nq = p.plan.items[it].w;
             const uint32_t res = smem_u32(smem + rb * L::RESB);
             const uint32_t sK = res + L::K, sKA = res + L::KA, sV = res + L::V;
-            if (!cx.waitw(&B.res_full[rb], (ci >> 1) & 1)) { ok = false; break; }
             for (int t = 0; t < nq; ++t, ++gt) {
                 const int st = gt % NST, b = gt & 1;
                 if (!cx.waitw(&B.full[st], (gt / NST) & 1)) { ok = false; break; }
@@ -499,9 +514,14 @@ __global__ void __launch_bounds__(kThreads, 1) dkv_kernel(const __grid_constant_
         // ---------------- gradient issuer (whole warp): a second issuing warp, so
         // the S / dP MMAs and these queue on the tensor pipe side by side
         constexpr uint32_t idG = idesc_bf16(128, 64, false, true);
-        int gt = 0, ci = 0;
+        int gt = 0;
         bool ok = true;
-        for (int it = blockIdx.x; ok && it < n_items; it += G, ++ci) {
+        for (int ci = 0; ok; ++ci) {
+            const int rb = ci & 1;
+            if (!cx.waitw(&B.res_full[rb], (ci >> 1) & 1)) { ok = false; break; }
+            const int it = B.item_of[rb];
+            if (lane == 0) mbar_arrive(&B.acc_free[rb]);   // the index is read
+            if (it < 0) break;
             const int nq = p.plan.items[it].w;
             for (int t = 0; t < nq; ++t, ++gt) {
                 const int st = gt % NST, b = gt & 1;
@@ -551,13 +571,16 @@ __global__ void __launch_bounds__(kThreads, 1) dkv_kernel(const __grid_constant_
         const uint32_t lb = (uint32_t)(quad * 32) << 16;
         const bool have_docs = p.docs != nullptr;
         const uint64_t c2 = f2_pack(p.scale_log2, p.scale_log2);
-        int gt = 0, ci = 0;
+        int gt = 0;
         bool alive = true;
-        for (int it = blockIdx.x; alive && it < n_items; it += G, ++ci) {
+        for (int ci = 0; alive; ++ci) {
+            const int rb = ci & 1;
+            if (!cx.waitw(&B.res_full[rb], (ci >> 1) & 1)) { alive = false; break; }
+            const int it = B.item_of[rb];
+            if (it < 0) break;
             const int4 item = p.plan.items[it];
             const int slot = p.plan.item_slot[it];
             const int h = item.x, kb = item.y, nq = item.w;
-            const int rb = ci & 1;
             const int j = kb * BM + c;
             const int doc_j = have_docs ? p.docs[j] : 0;
             for (int t = 0; t < nq; ++t, ++gt) {
@@ -703,6 +726,7 @@ __global__ void __launch_bounds__(1024) plan_items_kernel(const int32_t *__restr
     const int per = (rows + blockDim.x - 1) / blockDim.x;
     const int r0 = threadIdx.x * per, r1 = min(rows, r0 + per);
     for (int i = threadIdx.x; i < kSlotCap; i += blockDim.x) plan.slot_done[i] = 0;
+    if (threadIdx.x == 0) *plan.next_item = 0;
     int nsplit = 0;
     for (int r = r0; r < r1; ++r) nsplit += nq[r] > kChunk;
     int tot;
@@ -788,7 +812,7 @@ __global__ void __launch_bounds__(kThreads, 1) dq_kernel(const __grid_constant__
     const int n_items = p.H * p.QB, G = gridDim.x;
     const bool tab = NA > 0 && p.dcoeff_cos && p.tab_smem;
 
-    if (threadIdx.x == 0) B.init(NST);
+    if (threadIdx.x == 0) B.init(NST, kElem);
     if (warp == 1) {
         tmem_alloc(&B.tmem_slot, kTmemCols);
         tmem_relinquish();
@@ -1175,6 +1199,7 @@ int launch_bwd(const ScopeAttnArgs &a, cudaStream_t s) {
     plan.slot_chunks = slot_chunks;
     plan.slot_done = reinterpret_cast<int32_t *>(base + ws.slot_done);
     plan.partial = reinterpret_cast<float *>(base + ws.partial);
+    plan.next_item = n_items + 1;   // the second word of the n_items allocation (256 bytes)
     const int prow = a.H * QB, words = (QB + 31) / 32;
     tcbwd::plan_count_kernel<<<(unsigned)((prow * 32 + 255) / 256), 256, 0, s>>>(a.q_bitmap, prow, words, nq);
     SCOPE_CHECK_LAUNCH();
