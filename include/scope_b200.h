@@ -187,6 +187,12 @@ typedef struct ScopeCoeffArgs {
 } ScopeCoeffArgs;
 int scope_spectral_coeffs(const ScopeCoeffArgs *args, scope_stream_t stream);
 
+/* Self-test of the bounded-wait failure path (no counterpart in the
+ * reference): one CTA allocates TMEM, waits at most limit_us microseconds
+ * (<= 1 s) on an mbarrier nothing arrives on, sets SCOPE_DEVERR_TIMEOUT in
+ * *err_flag (device memory), frees TMEM and exits. */
+int scope_selftest_wait_timeout(int32_t *err_flag, uint32_t limit_us, scope_stream_t stream);
+
 /* ------------------------------------------------------------------------ */
 /* 3. block-sparse attention                                                  */
 /* ------------------------------------------------------------------------ */

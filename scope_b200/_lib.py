@@ -109,6 +109,7 @@ SIGNATURES = {
     "scope_trig_tables": (I32, [P, I32, I32, P, P, P]),
     "scope_qk_aug_prepare": (I32, [P, P, P, P, P, I32, I32, I32, I32, I32, F32, F32, I32, P, P, P]),
     "scope_spectral_coeffs": (I32, [ctypes.POINTER(ScopeCoeffArgs), P]),
+    "scope_selftest_wait_timeout": (I32, [P, ctypes.c_uint32, P]),
     "scope_attn_fwd": (I32, [ctypes.POINTER(ScopeAttnArgs), P]),
     "scope_attn_bwd": (I32, [ctypes.POINTER(ScopeAttnArgs), P]),
     "scope_workspace_bytes": (ctypes.c_size_t, [ctypes.POINTER(ScopeAttnArgs)]),
