@@ -187,6 +187,24 @@ typedef struct ScopeCoeffArgs {
 } ScopeCoeffArgs;
 int scope_spectral_coeffs(const ScopeCoeffArgs *args, scope_stream_t stream);
 
+/* Backward of the coefficient block up to the MLP output: dL/dy [H,T,n_out]
+ * f32 from the MLP output y (mlp_out of the forward) and the upstream
+ * gradients of the block's outputs, each optional (NULL = zero).  The MLP's
+ * own backward (two bf16 linears and a SiLU) is the caller's: the reference
+ * runs it through torch autograd (model/attn_bias.py:306-324). */
+typedef struct ScopeCoeffBwdArgs {
+    int32_t H, T, K, M, use_slope, subtract_b0;
+    const uint16_t *mlp_out;                       /* bf16 [H,T,n_out] */
+    const float *dcoeff_cos, *dcoeff_sin;          /* [H,T,K] */
+    const float *db0, *dslope, *ddelta_main, *dwidth;   /* [H,T] */
+    const float *ddelta_star, *dpi, *dbudget_logits;    /* [H,T,M] */
+    const float *omegas, *log_omegas;              /* [K] */
+    float delta_cap, logw_min, logw_max, c_scale, width_min, width_max, eps;
+    float *dy;                                     /* [H,T,n_out] */
+    int32_t *err_flag;                             /* optional device error word */
+} ScopeCoeffBwdArgs;
+int scope_spectral_coeffs_bwd(const ScopeCoeffBwdArgs *args, scope_stream_t stream);
+
 /* Self-test of the bounded-wait failure path (no counterpart in the
  * reference): one CTA allocates TMEM, waits at most limit_us microseconds
  * (<= 1 s) on an mbarrier nothing arrives on, sets SCOPE_DEVERR_TIMEOUT in

@@ -100,6 +100,21 @@ class ScopeCoeffArgs(ctypes.Structure):
     ]
 
 
+class ScopeCoeffBwdArgs(ctypes.Structure):
+    _fields_ = [
+        ("H", I32), ("T", I32), ("K", I32), ("M", I32), ("use_slope", I32), ("subtract_b0", I32),
+        ("mlp_out", P),
+        ("dcoeff_cos", P), ("dcoeff_sin", P),
+        ("db0", P), ("dslope", P), ("ddelta_main", P), ("dwidth", P),
+        ("ddelta_star", P), ("dpi", P), ("dbudget_logits", P),
+        ("omegas", P), ("log_omegas", P),
+        ("delta_cap", F32), ("logw_min", F32), ("logw_max", F32), ("c_scale", F32), ("width_min", F32),
+        ("width_max", F32), ("eps", F32),
+        ("dy", P),
+        ("err_flag", P),
+    ]
+
+
 SIGNATURES = {
     "scope_block_info": (I32, [P, I32, I32, I32, I32, I32, P, P]),
     "scope_mask_max_kv": (I32, [I32, I32, I32, I32]),
@@ -109,6 +124,7 @@ SIGNATURES = {
     "scope_trig_tables": (I32, [P, I32, I32, P, P, P]),
     "scope_qk_aug_prepare": (I32, [P, P, P, P, P, I32, I32, I32, I32, I32, F32, F32, I32, P, P, P]),
     "scope_spectral_coeffs": (I32, [ctypes.POINTER(ScopeCoeffArgs), P]),
+    "scope_spectral_coeffs_bwd": (I32, [ctypes.POINTER(ScopeCoeffBwdArgs), P]),
     "scope_selftest_wait_timeout": (I32, [P, ctypes.c_uint32, P]),
     "scope_attn_fwd": (I32, [ctypes.POINTER(ScopeAttnArgs), P]),
     "scope_attn_bwd": (I32, [ctypes.POINTER(ScopeAttnArgs), P]),
@@ -154,7 +170,7 @@ def check(status: int, what: str) -> None:
 
 def check_abi() -> None:
     L = lib()
-    for which, S in ((0, ScopeMaskArgs), (1, ScopeAttnArgs), (2, ScopeCoeffArgs)):
+    for which, S in ((0, ScopeMaskArgs), (1, ScopeAttnArgs), (2, ScopeCoeffArgs), (3, ScopeCoeffBwdArgs)):
         size, last = L.scope_abi_layout(which, 0), L.scope_abi_layout(which, 1)
         if size != ctypes.sizeof(S) or last != S.err_flag.offset:
             raise RuntimeError(f"scope_b200 ABI mismatch for {S.__name__}: C sizeof={size} last={last}, "

@@ -8,10 +8,14 @@ knobs; ``forward(q)`` returns what ``SpectralBias.forward`` returns
 MLP and the mixture run in one CUDA kernel (``scope_spectral_coeffs``);
 ``spectral_coefficients`` is the functional form.
 
-Forward only: the outputs carry no autograd history (the reference trains
-this block; its backward is not built here), and the training regularisers
-(model/attn_bias.py:480-506) are not computed -- ``reg_loss`` is 0, as in
-the reference's eval mode.
+Backward: when q or a weight requires grad, the outputs carry autograd
+history.  The gradient up to the MLP output runs in a CUDA kernel
+(``scope_spectral_coeffs_bwd``: the chain rule through the mixture, the
+normalisation over frequencies, the softmax and the squashing functions);
+the MLP's own backward replays the reference's torch ops on the GPU (two bf16
+linears and a SiLU, model/attn_bias.py:306-324 -- plain library GEMMs).  The
+training regularisers (model/attn_bias.py:480-506) are not computed:
+``reg_loss`` is 0, as in the reference's eval mode.
 """
 from __future__ import annotations
 
@@ -44,7 +48,88 @@ class CoeffOutputs:
     mlp_out: Optional[Tensor] = None   # [1,H,T,n_out] bf16 when requested
 
 
+def _mlp_torch(q: Tensor, w1: Tensor, b1: Tensor, w2: Tensor, b2: Tensor) -> Tensor:
+    """The reference's MLP ops (model/attn_bias.py:306-324) in q's dtype: used to
+    carry dL/dy to q and the weights."""
+    dt = q.dtype
+    if w1.dim() == 2:
+        x = torch.nn.functional.silu(torch.nn.functional.linear(q, w1.to(dt), b1.to(dt)))
+        return torch.nn.functional.linear(x, w2.to(dt), b2.to(dt))
+    x = torch.einsum("bhld,hkd->bhlk", q, w1.to(dt)) + b1.to(dt)[None, :, None, :]
+    x = torch.nn.functional.silu(x)
+    return torch.einsum("bhlk,hok->bhlo", x, w2.to(dt)) + b2.to(dt)[None, :, None, :]
+
+
+def coeff_dy(y: Tensor, grads, *, omegas: Tensor, log_omegas: Tensor, M: int, delta_cap: float, logw_min: float,
+             logw_max: float, use_slope: bool, subtract_b0: bool, c_scale: float, width_min: float, width_max: float,
+             eps: float) -> Tensor:
+    """dL/dy [1,H,T,n_out] f32 from the MLP output y (bf16) and the upstream
+    gradients of (coeff_cos, coeff_sin, slope, b0, delta_star, pi,
+    budget_logits, delta_main, width), any of them None."""
+    _, H, T, n_out = y.shape
+    K = omegas.numel()
+    dev = y.device
+    dy = torch.empty(1, H, T, n_out, device=dev, dtype=torch.float32)
+    g = [None if t is None else t.to(device=dev, dtype=torch.float32).contiguous() for t in grads]
+    a = _lib.ScopeCoeffBwdArgs()
+    a.H, a.T, a.K, a.M, a.use_slope, a.subtract_b0 = H, T, K, M, int(use_slope), int(subtract_b0)
+    yc = y.contiguous()
+    a.mlp_out = yc.data_ptr()
+    names = ("dcoeff_cos", "dcoeff_sin", "dslope", "db0", "ddelta_star", "dpi", "dbudget_logits", "ddelta_main",
+             "dwidth")
+    for n, t in zip(names, g):
+        setattr(a, n, None if t is None else t.data_ptr())
+    om = omegas.to(device=dev, dtype=torch.float32).contiguous()
+    lom = log_omegas.to(device=dev, dtype=torch.float32).contiguous()
+    a.omegas, a.log_omegas = om.data_ptr(), lom.data_ptr()
+    a.delta_cap, a.logw_min, a.logw_max = float(delta_cap), float(logw_min), float(logw_max)
+    a.c_scale, a.width_min, a.width_max, a.eps = float(c_scale), float(width_min), float(width_max), float(eps)
+    a.dy = dy.data_ptr()
+    a.err_flag = _lib.err_word_ptr(dev)
+    _lib.check(_lib.lib().scope_spectral_coeffs_bwd(ctypes.byref(a), _stream(dev)), "scope_spectral_coeffs_bwd")
+    return dy
+
+
+class _CoeffFn(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, q, w1, b1, w2, b2, kw):
+        o = _coeff_forward(q, w1, b1, w2, b2, **kw, return_mlp=True)
+        ctx.mark_non_differentiable(o.mlp_out)
+        ctx.save_for_backward(q, w1, b1, w2, b2, o.mlp_out)
+        ctx.kw = kw
+        return tuple(getattr(o, n) for n in OUT_NAMES) + (o.mlp_out,)
+
+    @staticmethod
+    def backward(ctx, *grads):
+        q, w1, b1, w2, b2, y = ctx.saved_tensors
+        kw = {k: v for k, v in ctx.kw.items() if k not in ("return_mlp",)}
+        dy = coeff_dy(y, grads[:9], **kw)
+        leaves = [t.detach().requires_grad_(need) for t, need in zip((q, w1, b1, w2, b2), ctx.needs_input_grad[:5])]
+        with torch.enable_grad():
+            q4 = leaves[0] if leaves[0].dim() == 4 else leaves[0][None]
+            yr = _mlp_torch(q4, *leaves[1:]).float()
+            torch.autograd.backward(yr, dy)
+        return tuple(t.grad if need else None for t, need in zip(leaves, ctx.needs_input_grad[:5])) + (None,)
+
+
 def spectral_coefficients(q: Tensor, w1: Tensor, b1: Tensor, w2: Tensor, b2: Tensor, *, omegas: Tensor,
+                          log_omegas: Optional[Tensor] = None, M: int, delta_cap: float, logw_min: float,
+                          logw_max: float, use_slope: bool = True, subtract_b0: bool = True, c_scale: float = 0.01,
+                          width_min: float = 32.0, width_max: float = 256.0, eps: float = 1e-9,
+                          return_mlp: bool = False) -> CoeffOutputs:
+    """The coefficient block (see ``_coeff_forward`` for the shapes); with
+    autograd history when grad mode is on and q or a weight requires grad."""
+    lom = log_omegas if log_omegas is not None else omegas.float().log()
+    kw = dict(omegas=omegas, log_omegas=lom, M=M, delta_cap=delta_cap, logw_min=logw_min, logw_max=logw_max,
+              use_slope=use_slope, subtract_b0=subtract_b0, c_scale=c_scale, width_min=width_min,
+              width_max=width_max, eps=eps)
+    if torch.is_grad_enabled() and any(t.requires_grad for t in (q, w1, b1, w2, b2)):
+        outs = _CoeffFn.apply(q, w1, b1, w2, b2, kw)
+        return CoeffOutputs(*outs[:9], mlp_out=outs[9].detach() if return_mlp else None)
+    return _coeff_forward(q, w1, b1, w2, b2, **kw, return_mlp=return_mlp)
+
+
+def _coeff_forward(q: Tensor, w1: Tensor, b1: Tensor, w2: Tensor, b2: Tensor, *, omegas: Tensor,
                           log_omegas: Optional[Tensor] = None, M: int, delta_cap: float, logw_min: float,
                           logw_max: float, use_slope: bool = True, subtract_b0: bool = True, c_scale: float = 0.01,
                           width_min: float = 32.0, width_max: float = 256.0, eps: float = 1e-9,
@@ -69,7 +154,7 @@ def spectral_coefficients(q: Tensor, w1: Tensor, b1: Tensor, w2: Tensor, b2: Ten
     K = omegas.numel()
     dev = q3.device
     bf = lambda t: t.to(device=dev, dtype=torch.bfloat16).contiguous()
-    w1, b1, w2, b2 = bf(w1), bf(b1), bf(w2), bf(b2)
+    w1, b1, w2, b2 = (bf(t.detach()) for t in (w1, b1, w2, b2))
     if w2.shape[-2] != n_out or b2.shape[-1] != n_out:
         raise ValueError(f"spectral_coefficients: w2/b2 must have {n_out} outputs (5M + use_slope)")
     om = omegas.to(device=dev, dtype=torch.float32).contiguous()
@@ -86,6 +171,7 @@ def spectral_coefficients(q: Tensor, w1: Tensor, b1: Tensor, w2: Tensor, b2: Ten
     a = _lib.ScopeCoeffArgs()
     a.H, a.T, a.D, a.hidden, a.K, a.M = H, T, D, w1.shape[-2], K, M
     a.use_slope, a.subtract_b0 = int(use_slope), int(subtract_b0)
+    q3 = q3.detach()
     a.q, a.q_sh, a.q_st = q3.data_ptr(), q3.stride(0), q3.stride(1)
     a.w_heads = H if per_head else 1
     a.w1, a.b1, a.w2, a.b2 = w1.data_ptr(), b1.data_ptr(), w2.data_ptr(), b2.data_ptr()
@@ -148,7 +234,8 @@ class SpectralCoefficients:
         [n_out], or per head with a leading H dim."""
         if w1.dim() == 2:
             w1, b1, w2, b2 = w1[None], b1[None], w2[None], b2[None]
-        self.w1, self.b1, self.w2, self.b2 = (t.detach() for t in (w1, b1, w2, b2))
+        # kept as given: tensors that require grad receive the block's weight gradients
+        self.w1, self.b1, self.w2, self.b2 = w1, b1, w2, b2
         self.share = self.w1.shape[0] == 1
 
     def forward(self, q: Tensor, *, return_mlp: bool = False):

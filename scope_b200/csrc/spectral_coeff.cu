@@ -321,6 +321,129 @@ __global__ void __launch_bounds__(256, 2) coeff_kernel(const __grid_constant__ M
     }
 }
 
+// ============================================================================ backward
+// dL/dy for the MLP output y from the upstream gradients of the block's outputs
+// (model/attn_bias.py:437-478 differentiated): one thread per token recomputes
+// the heads from y and applies the chain rule through the mixture, the
+// Gaussian normalisation, the softmax and the squashing functions.  The MLP's
+// own backward (two bf16 linears and a SiLU) is left to the caller.
+struct BwdParams {
+    int rows, K, M, n_out, use_slope, subtract_b0;
+    const uint16_t *y;
+    const float *dcc, *dcs, *db0, *dslope, *ddelta_main, *dwidth, *dds, *dpi, *dbudget;
+    const float *omegas, *log_omegas;
+    float delta_cap, logw_min, logw_max, c_scale, width_min, width_max, eps;
+    float *dy;
+};
+
+template <int K, int M>
+__global__ void __launch_bounds__(128) coeff_bwd_kernel(const BwdParams p) {
+    const int64_t row = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (row >= p.rows) return;
+    const uint16_t *yr = p.y + row * p.n_out;
+    float sd[M], sm[M], ss[M], ds[M], mu[M], sg[M], pi[M];
+    float pmax = -INFINITY, musum = 0.f;
+    int imax = 0;
+#pragma unroll
+    for (int m = 0; m < M; ++m) {
+        sd[m] = sigmoid_ref(bf16_to_f32(yr[m]));
+        sm[m] = sigmoid_ref(bf16_to_f32(yr[M + m]));
+        ss[m] = sigmoid_ref(bf16_to_f32(yr[2 * M + m]));
+        ds[m] = sd[m] * p.delta_cap;
+        mu[m] = p.logw_min + (p.logw_max - p.logw_min) * sm[m];
+        sg[m] = 0.25f + 1.75f * ss[m];
+        musum += mu[m];
+        const float pl = bf16_to_f32(yr[3 * M + m]);
+        if (pl > pmax) {
+            pmax = pl;
+            imax = m;
+        }
+    }
+    float psum = 0.f;
+#pragma unroll
+    for (int m = 0; m < M; ++m) {
+        pi[m] = expf(bf16_to_f32(yr[3 * M + m]) - pmax);
+        psum += pi[m];
+    }
+#pragma unroll
+    for (int m = 0; m < M; ++m) pi[m] /= psum;
+    // upstream gradients of the per-frequency outputs; b0 = sum_k coeff_cos adds db0 to each
+    float e[K], f[K];
+    const float g_b0 = (p.subtract_b0 && p.db0) ? p.db0[row] : 0.f;
+#pragma unroll
+    for (int k = 0; k < K; ++k) {
+        e[k] = (p.dcc ? p.dcc[row * K + k] : 0.f) + g_b0;
+        f[k] = p.dcs ? p.dcs[row * K + k] : 0.f;
+    }
+    float dpi[M], dds[M], dmu[M], dsg[M];
+#pragma unroll
+    for (int m = 0; m < M; ++m) {
+        const float den = 2.f * sg[m] * sg[m];
+        float a[K], S = 0.f;
+#pragma unroll
+        for (int k = 0; k < K; ++k) {
+            const float d = p.log_omegas[k] - mu[m];
+            a[k] = expf(-(d * d) / den);
+            S += a[k];
+        }
+        const float Se = S + p.eps;
+        float gpi = 0.f, gdl = 0.f, dah[K], dot = 0.f;
+#pragma unroll
+        for (int k = 0; k < K; ++k) {
+            float sn, c;
+            sincosf(p.omegas[k] * ds[m], &sn, &c);
+            const float ah = a[k] / Se;
+            const float g = e[k] * c + f[k] * sn;
+            gpi += ah * g;
+            gdl += ah * p.omegas[k] * (f[k] * c - e[k] * sn);
+            dah[k] = pi[m] * g;
+            dot += dah[k] * a[k];
+        }
+        dpi[m] = gpi + (p.dpi ? p.dpi[row * M + m] : 0.f);
+        dds[m] = pi[m] * gdl + (p.dds ? p.dds[row * M + m] : 0.f);
+        // a_hat = a / (S + eps): da_k = dah_k / Se - sum_j dah_j a_j / Se^2
+        float gm = 0.f, gs = 0.f;
+        const float inv_s2 = 1.f / (sg[m] * sg[m]);
+#pragma unroll
+        for (int k = 0; k < K; ++k) {
+            const float da = dah[k] / Se - dot / (Se * Se);
+            const float d = p.log_omegas[k] - mu[m];
+            gm += da * a[k] * d * inv_s2;                    // d a / d mu    = a (l - mu) / sigma^2
+            gs += da * a[k] * d * d * inv_s2 / sg[m];        // d a / d sigma = a (l - mu)^2 / sigma^3
+        }
+        dmu[m] = gm;
+        dsg[m] = gs;
+    }
+    if (p.ddelta_main) {
+        const float g = p.ddelta_main[row];
+#pragma unroll
+        for (int m = 0; m < M; ++m)
+            if (m == imax) dds[m] += g;
+    }
+    if (p.dwidth) {
+        const float sw = sigmoid_ref(musum / (float)M);
+        const float g = p.dwidth[row] * (p.width_max - p.width_min) * sw * (1.f - sw) / (float)M;
+#pragma unroll
+        for (int m = 0; m < M; ++m) dmu[m] += g;
+    }
+    float pd = 0.f;
+#pragma unroll
+    for (int m = 0; m < M; ++m) pd += pi[m] * dpi[m];
+    float *dy = p.dy + row * p.n_out;
+#pragma unroll
+    for (int m = 0; m < M; ++m) {
+        dy[m] = dds[m] * p.delta_cap * sd[m] * (1.f - sd[m]);
+        dy[M + m] = dmu[m] * (p.logw_max - p.logw_min) * sm[m] * (1.f - sm[m]);
+        dy[2 * M + m] = dsg[m] * 1.75f * ss[m] * (1.f - ss[m]);
+        dy[3 * M + m] = pi[m] * (dpi[m] - pd);
+        dy[4 * M + m] = p.dbudget ? p.dbudget[row * M + m] : 0.f;
+    }
+    if (p.use_slope) {
+        const float t = tanhf(bf16_to_f32(yr[5 * M]));
+        dy[5 * M] = (p.dslope ? p.dslope[row] : 0.f) * p.c_scale * (1.f - t * t);
+    }
+}
+
 // bf16 [rows][inner] weights per head: [w_heads][rows][inner], box (64, box_rows, 1)
 static bool map_weights(CUtensorMap *m, const void *base, int inner, int rows, int heads, int box_rows) {
     cuuint64_t dims[3] = {(cuuint64_t)inner, (cuuint64_t)rows, (cuuint64_t)heads};
@@ -394,8 +517,68 @@ static int launch_m(const ScopeCoeffArgs &a, cudaStream_t s) {
     }
 }
 
+template <int K, int M>
+static int launch_bwd(const ScopeCoeffBwdArgs &a, cudaStream_t s) {
+    BwdParams p;
+    std::memset(&p, 0, sizeof(p));
+    p.rows = a.H * a.T;
+    p.K = K;
+    p.M = M;
+    p.n_out = 5 * M + (a.use_slope ? 1 : 0);
+    p.use_slope = a.use_slope;
+    p.subtract_b0 = a.subtract_b0;
+    p.y = a.mlp_out;
+    p.dcc = a.dcoeff_cos;
+    p.dcs = a.dcoeff_sin;
+    p.db0 = a.db0;
+    p.dslope = a.dslope;
+    p.ddelta_main = a.ddelta_main;
+    p.dwidth = a.dwidth;
+    p.dds = a.ddelta_star;
+    p.dpi = a.dpi;
+    p.dbudget = a.dbudget_logits;
+    p.omegas = a.omegas;
+    p.log_omegas = a.log_omegas;
+    p.delta_cap = a.delta_cap;
+    p.logw_min = a.logw_min;
+    p.logw_max = a.logw_max;
+    p.c_scale = a.c_scale;
+    p.width_min = a.width_min;
+    p.width_max = a.width_max;
+    p.eps = a.eps;
+    p.dy = a.dy;
+    coeff_bwd_kernel<K, M><<<(unsigned)((p.rows + 127) / 128), 128, 0, s>>>(p);
+    SCOPE_CHECK_LAUNCH();
+    return SCOPE_OK;
+}
+
+template <int K>
+static int launch_bwd_m(const ScopeCoeffBwdArgs &a, cudaStream_t s) {
+    switch (a.M) {
+        case 2: return launch_bwd<K, 2>(a, s);
+        case 4: return launch_bwd<K, 4>(a, s);
+        case 8: return launch_bwd<K, 8>(a, s);
+        default: return SCOPE_ERR_UNSUPPORTED;
+    }
+}
+
 }  // namespace coeff
 }  // namespace scope
+
+extern "C" int scope_spectral_coeffs_bwd(const ScopeCoeffBwdArgs *args, scope_stream_t stream) {
+    using namespace scope::coeff;
+    if (!args) return SCOPE_ERR_INVALID;
+    const ScopeCoeffBwdArgs &a = *args;
+    if (a.H <= 0 || a.T <= 0 || !a.mlp_out || !a.omegas || !a.log_omegas || !a.dy) return SCOPE_ERR_INVALID;
+    if ((int64_t)a.H * a.T > INT32_MAX) return SCOPE_ERR_INVALID;
+    cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    switch (a.K) {
+        case 6: return launch_bwd_m<6>(a, s);
+        case 8: return launch_bwd_m<8>(a, s);
+        case 16: return launch_bwd_m<16>(a, s);
+        default: return SCOPE_ERR_UNSUPPORTED;
+    }
+}
 
 extern "C" int scope_spectral_coeffs(const ScopeCoeffArgs *args, scope_stream_t stream) {
     using namespace scope::coeff;

@@ -199,3 +199,15 @@ def coeff_inputs(case):
     b2[:, :M] += torch.linspace(-3.0, 1.0, M)
     b2 = bf(b2)
     return {"q": q.numpy(), "w1": w1.numpy(), "b1": b1.numpy(), "w2": w2.numpy(), "b2": b2.numpy()}
+
+
+def coeff_upstream(case):
+    """Seeded upstream gradients of the block's nine outputs (coeff_cos,
+    coeff_sin, slope, b0, delta_star, pi, budget_logits, delta_main, width)."""
+    import torch
+    g = torch.Generator().manual_seed(case["seed"] + 100)
+    H, T, K, M = case["H"], case["T"], case["K"], case["M"]
+    shapes = ((1, H, T, K), (1, H, T, K), (1, H, T), (1, H, T), (1, H, T, M), (1, H, T, M), (1, H, T, M),
+              (1, H, T), (1, H, T))
+    scales = (1.0, 1.0, 10.0, 0.5, 1e-3, 0.5, 0.2, 1e-3, 1e-2)
+    return [(torch.randn(*sh, generator=g) * sc).numpy() for sh, sc in zip(shapes, scales)]

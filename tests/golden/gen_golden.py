@@ -215,11 +215,21 @@ def run_coeff_case(SpectralBias, name, case):
             sb.w2.copy_(torch.from_numpy(x["w2"]))
             sb.b2.copy_(torch.from_numpy(x["b2"]))
     sb.eval()
-    q = torch.from_numpy(x["q"]).to(torch.bfloat16)
+    q = torch.from_numpy(x["q"]).to(torch.bfloat16).requires_grad_(True)
+    outs = sb(q)
     with torch.no_grad():
-        outs = sb(q)
         y = sb._mlp_forward(q).float()
-    res = {n: outs[i].float().numpy() for i, n in enumerate(COEFF_OUTS)}
+    res = {n: outs[i].detach().float().numpy() for i, n in enumerate(COEFF_OUTS)}
+    # the backward from seeded upstream gradients of all nine outputs
+    ups = C.coeff_upstream(case)
+    live = [i for i in range(len(COEFF_OUTS)) if outs[i].requires_grad]   # slope / b0 are constants when off
+    torch.autograd.backward([outs[i] for i in live], [torch.from_numpy(ups[i]) for i in live])
+    if case["share"]:
+        wg = [sb.mlp[0].weight.grad[None], sb.mlp[0].bias.grad[None], sb.mlp[2].weight.grad[None],
+              sb.mlp[2].bias.grad[None]]
+    else:
+        wg = [sb.w1.grad, sb.b1.grad, sb.w2.grad, sb.b2.grad]
+    res.update(dq=q.grad.float().numpy(), **{n: t.numpy() for n, t in zip(("dw1", "db1", "dw2", "db2"), wg)})
     np.savez_compressed(os.path.join(HERE, f"coeff_{name}.npz"), **res, y=y.numpy(),
                         omegas=sb.omegas.numpy(), log_omegas=sb.log_omegas.numpy(),
                         logw_min=sb.logw_min.numpy(), logw_max=sb.logw_max.numpy(),

@@ -175,3 +175,82 @@ def test_c3_size_properties():
     qr = q[:, :, rows].cpu()
     yr = CO.mlp(qr, w["w1"], w["b1"], w["w2"], w["b2"]).float().numpy()
     assert (np.abs(yk.numpy()[None] - yr) <= _y_bound(qr, w, yr) + 1e-12).all()
+
+
+GRAD_NAMES = ("dq", "dw1", "db1", "dw2", "db2")
+
+
+def _oracle_backward(case, z, x, q_bf16):
+    """Autograd through the oracle (MLP + heads) from the fixture's upstream gradients."""
+    w = {n: torch.from_numpy(x[n]).clone().requires_grad_(True) for n in ("w1", "b1", "w2", "b2")}
+    ww = {n: (t[0] if case["share"] else t) for n, t in w.items()}
+    q = q_bf16.clone().requires_grad_(True)
+    y = CO.mlp(q, ww["w1"], ww["b1"], ww["w2"], ww["b2"]).float()
+    kn = _knobs(case, z)
+    kn.pop("omegas"), kn.pop("log_omegas")
+    r = CO.heads(y, omegas=z["omegas"], log_omegas=z["log_omegas"], **kn)
+    ups = C.coeff_upstream(case)
+    outs = [r[n] for n in OUTS]
+    live = [i for i in range(len(OUTS)) if outs[i].requires_grad]
+    torch.autograd.backward([outs[i] for i in live], [torch.from_numpy(ups[i]) for i in live])
+    return {"dq": q.grad.float(), "dw1": w["w1"].grad, "db1": w["b1"].grad, "dw2": w["w2"].grad,
+            "db2": w["b2"].grad}
+
+
+@pytest.mark.parametrize("name", list(C.COEFF_CASES))
+def test_oracle_backward_matches_reference_fixture(name):
+    case, x, z = _load(name)
+    g = _oracle_backward(case, z, x, torch.from_numpy(x["q"]).to(torch.bfloat16))
+    for n in GRAD_NAMES:
+        want = z[n]
+        err = np.abs(g[n].numpy() - want).max()
+        assert err <= 1e-3 * max(np.abs(want).max(), 1e-6), (n, float(err))
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("name", list(C.COEFF_CASES))
+def test_backward_kernel_dy_matches_oracle(name):
+    """dL/dy from the kernel against autograd through the oracle's heads, both
+    evaluated on the kernel's own MLP output."""
+    from scope_b200 import device_errors, spectral_coefficients
+    from scope_b200.coeff import coeff_dy
+    case, x, z = _load(name)
+    q = torch.from_numpy(x["q"]).to("cuda", torch.bfloat16)
+    kn = _knobs(case, z)
+    out = spectral_coefficients(q, **_weights(case, x), **kn, return_mlp=True)
+    ups = [torch.from_numpy(u) for u in C.coeff_upstream(case)]
+    ups_live = [u if (n not in ("slope",) or case["use_slope"]) and (n != "b0" or case["subtract_b0"]) else None
+                for n, u in zip(OUTS, ups)]
+    kw = {k: v for k, v in kn.items()}
+    dy = coeff_dy(out.mlp_out, [None if u is None else u.cuda() for u in ups_live], **kw)
+    torch.cuda.synchronize()
+    assert device_errors("cuda") == 0
+    yk = out.mlp_out.float().cpu().requires_grad_(True)
+    kn.pop("omegas"), kn.pop("log_omegas")
+    r = CO.heads(yk, omegas=z["omegas"], log_omegas=z["log_omegas"], **kn)
+    live = [i for i, u in enumerate(ups_live) if u is not None and r[OUTS[i]].requires_grad]
+    torch.autograd.backward([r[OUTS[i]] for i in live], [ups_live[i] for i in live])
+    want = yk.grad.numpy()
+    err = np.abs(dy.cpu().numpy() - want).max()
+    assert err <= 1e-4 * np.abs(want).max() + 1e-6, (float(err), float(np.abs(want).max()))
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("name", list(C.COEFF_CASES))
+def test_backward_matches_reference_fixture(name):
+    """Gradients of q and of the MLP weights through the autograd path (the dy
+    kernel, then the reference's MLP ops) against the reference's own."""
+    from scope_b200 import spectral_coefficients
+    case, x, z = _load(name)
+    q = torch.from_numpy(x["q"]).to("cuda", torch.bfloat16).requires_grad_(True)
+    w = {n: t.cuda().requires_grad_(True) for n, t in _weights(case, x).items()}
+    out = spectral_coefficients(q, **w, **_knobs(case, z))
+    ups = [torch.from_numpy(u).cuda() for u in C.coeff_upstream(case)]
+    outs = [getattr(out, n) for n in OUTS]
+    torch.autograd.backward(outs, ups)
+    got = {"dq": q.grad.float(), "dw1": w["w1"].grad, "db1": w["b1"].grad, "dw2": w["w2"].grad, "db2": w["b2"].grad}
+    for n in GRAD_NAMES:
+        want = z[n][0] if (case["share"] and n != "dq") else z[n]
+        g = got[n].float().cpu().numpy()
+        err = np.abs(g - want).max()
+        assert err <= 3e-2 * max(np.abs(want).max(), 1e-6), (n, float(err), float(np.abs(want).max()))
