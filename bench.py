@@ -321,6 +321,31 @@ def coeff_block(wl, cfg, hbm, *, reps=10, cpu=True):
            "roofline": {"bound": "hbm", "achieved": byts / (ms * 1e-3) / 1e9, "peak": hbm, "unit": "GB/s",
                         "frac": byts / (ms * 1e-3) / 1e9 / hbm, "algorithmic_bytes": byts},
            "mlp_tflops": 2 * tok * (64 * 128 + 128 * n_out) / (ms * 1e-3) / 1e12}
+    # backward: dL/dy kernel + the MLP replay (library GEMMs), from unit upstream gradients
+    # of the coefficients and the slope, with q and the weights requiring grad
+    from scope_b200.coeff import coeff_dy
+    qg = q.detach().requires_grad_(True)
+    wg = [t.detach().float().requires_grad_(True) for t in w]
+    ups = None
+    for i in range(3 + reps):
+        if i == 3:
+            torch.cuda.synchronize()
+            e0.record(s)
+        o = spectral_coefficients(qg, *wg, **kw)
+        if ups is None:
+            ups = [torch.ones_like(o.coeff_cos), torch.ones_like(o.coeff_sin), torch.ones_like(o.slope)]
+        torch.autograd.backward([o.coeff_cos, o.coeff_sin, o.slope], ups)
+    e1.record(s)
+    torch.cuda.synchronize()
+    res["fwd_bwd_ms"] = e0.elapsed_time(e1) / reps
+    yb = o.mlp_out if o.mlp_out is not None else spectral_coefficients(q, *w, **kw, return_mlp=True).mlp_out
+    e0.record(s)
+    for _ in range(reps):
+        coeff_dy(yb, [ups[0], ups[1], ups[2]] + [None] * 6, **kw, use_slope=True, subtract_b0=True, c_scale=sc.c_scale,
+                 width_min=sc.width_min, width_max=sc.width_max, eps=sc.eps)
+    e1.record(s)
+    torch.cuda.synchronize()
+    res["dy_kernel_ms"] = e0.elapsed_time(e1) / reps
     del outs
     if cpu:
         from oracle import coeff_oracle as CO   # the CPU baseline only
