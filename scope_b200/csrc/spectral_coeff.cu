@@ -366,7 +366,11 @@ __global__ void __launch_bounds__(128) coeff_bwd_kernel(const BwdParams p) {
         psum += pi[m];
     }
 #pragma unroll
-    for (int m = 0; m < M; ++m) pi[m] /= psum;
+    {
+        const float rps = __frcp_rn(psum);
+#pragma unroll
+        for (int m = 0; m < M; ++m) pi[m] *= rps;
+    }
     // upstream gradients of the per-frequency outputs; b0 = sum_k coeff_cos adds db0 to each
     float e[K], f[K];
     const float g_b0 = (p.subtract_b0 && p.db0) ? p.db0[row] : 0.f;
@@ -378,24 +382,24 @@ __global__ void __launch_bounds__(128) coeff_bwd_kernel(const BwdParams p) {
     float dpi[M], dds[M], dmu[M], dsg[M];
 #pragma unroll
     for (int m = 0; m < M; ++m) {
-        const float den = 2.f * sg[m] * sg[m];
+        const float rden = __frcp_rn(2.f * sg[m] * sg[m]);
         float a[K], S = 0.f;
 #pragma unroll
         for (int k = 0; k < K; ++k) {
-            const float d = p.log_omegas[k] - mu[m];
-            a[k] = expf(-(d * d) / den);
+            const float d = __ldg(p.log_omegas + k) - mu[m];
+            a[k] = __expf(-(d * d) * rden);
             S += a[k];
         }
-        const float Se = S + p.eps;
+        const float Se = S + p.eps, rSe = __frcp_rn(Se);
         float gpi = 0.f, gdl = 0.f, dah[K], dot = 0.f;
 #pragma unroll
         for (int k = 0; k < K; ++k) {
             float sn, c;
-            sincosf(p.omegas[k] * ds[m], &sn, &c);
-            const float ah = a[k] / Se;
+            sincos_phase(__ldg(p.omegas + k) * ds[m], &sn, &c);
+            const float ah = a[k] * rSe;
             const float g = e[k] * c + f[k] * sn;
             gpi += ah * g;
-            gdl += ah * p.omegas[k] * (f[k] * c - e[k] * sn);
+            gdl += ah * __ldg(p.omegas + k) * (f[k] * c - e[k] * sn);
             dah[k] = pi[m] * g;
             dot += dah[k] * a[k];
         }
@@ -406,8 +410,8 @@ __global__ void __launch_bounds__(128) coeff_bwd_kernel(const BwdParams p) {
         const float inv_s2 = 1.f / (sg[m] * sg[m]);
 #pragma unroll
         for (int k = 0; k < K; ++k) {
-            const float da = dah[k] / Se - dot / (Se * Se);
-            const float d = p.log_omegas[k] - mu[m];
+            const float da = (dah[k] - dot * rSe) * rSe;
+            const float d = __ldg(p.log_omegas + k) - mu[m];
             gm += da * a[k] * d * inv_s2;                    // d a / d mu    = a (l - mu) / sigma^2
             gs += da * a[k] * d * d * inv_s2 / sg[m];        // d a / d sigma = a (l - mu)^2 / sigma^3
         }
