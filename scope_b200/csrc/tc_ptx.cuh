@@ -89,28 +89,6 @@ __device__ __forceinline__ bool mbar_test(uint64_t *bar, uint32_t parity) {
     return __shfl_sync(0xffffffffu, ok, 0) != 0;
 }
 
-// The same bounded wait with a suspend-time hint: the thread sleeps up to
-// `hint_ns` per try instead of polling, for waiters whose latency matters less
-// than the issue slots they would take from the warps sharing their SM
-// sub-partition.
-__device__ __forceinline__ bool mbar_wait_sleep(uint64_t *bar, uint32_t parity, uint32_t hint_ns,
-                                                uint64_t limit_ns = kWaitLimitNs) {
-    const uint32_t a = smem_u32(bar);
-    const uint64_t t0 = globaltimer_ns();
-    for (;;) {
-        uint32_t ok;
-        asm volatile(
-            "{\n\t.reg .pred p;\n\t"
-            "mbarrier.try_wait.parity.acquire.cta.shared::cta.b64 p, [%1], %2, %3;\n\t"
-            "selp.u32 %0, 1, 0, p;\n\t}\n"
-            : "=r"(ok)
-            : "r"(a), "r"(parity), "r"(hint_ns)
-            : "memory");
-        if (ok) return true;
-        if (globaltimer_ns() - t0 > limit_ns) return false;
-    }
-}
-
 // ---------------------------------------------------------------- TMA
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap *m) {
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(m)) : "memory");
