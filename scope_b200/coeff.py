@@ -105,10 +105,20 @@ class _CoeffFn(torch.autograd.Function):
         kw = {k: v for k, v in ctx.kw.items() if k not in ("return_mlp",)}
         dy = coeff_dy(y, grads[:9], **kw)
         leaves = [t.detach().requires_grad_(need) for t, need in zip((q, w1, b1, w2, b2), ctx.needs_input_grad[:5])]
+        n_out = dy.shape[-1]
+        pad = (-n_out) % 16
         with torch.enable_grad():
             q4 = leaves[0] if leaves[0].dim() == 4 else leaves[0][None]
-            yr = _mlp_torch(q4, *leaves[1:]).float()
-            torch.autograd.backward(yr, dy)
+            w2p, b2p = leaves[3], leaves[4]
+            if pad:
+                # zero output rows change no real row of y, dx or dW2, and give the
+                # library GEMMs a multiple-of-16 output width
+                w2p = torch.nn.functional.pad(w2p, (0, 0, 0, pad))
+                b2p = torch.nn.functional.pad(b2p, (0, pad))
+                dy = torch.nn.functional.pad(dy, (0, pad))
+            yr = _mlp_torch(q4, leaves[1], leaves[2], w2p, b2p)
+            # the reference's y.float() passes its gradient back cast to y's dtype
+            torch.autograd.backward(yr, dy.to(yr.dtype))
         return tuple(t.grad if need else None for t, need in zip(leaves, ctx.needs_input_grad[:5])) + (None,)
 
 
