@@ -183,6 +183,8 @@ typedef struct ScopeCoeffArgs {
     float *delta_star, *pi, *budget_logits;   /* [H,T,M] */
     float *delta_main, *width;        /* [H,T] */
     uint16_t *mlp_out;                /* optional bf16 [H,T,n_out]: the MLP output y */
+    float *omega_reg;                 /* optional [H,T]: sum_m sum_k omega_k^2 a_mk^2 (a normalised over k),
+                                         the per-token term of the training penalty reg_omega */
     int32_t *err_flag;                /* optional device error word */
 } ScopeCoeffArgs;
 int scope_spectral_coeffs(const ScopeCoeffArgs *args, scope_stream_t stream);
@@ -198,6 +200,7 @@ typedef struct ScopeCoeffBwdArgs {
     const float *dcoeff_cos, *dcoeff_sin;          /* [H,T,K] */
     const float *db0, *dslope, *ddelta_main, *dwidth;   /* [H,T] */
     const float *ddelta_star, *dpi, *dbudget_logits;    /* [H,T,M] */
+    const float *domega_reg;                       /* [H,T]: gradient of the omega_reg output */
     const float *omegas, *log_omegas;              /* [K] */
     float delta_cap, logw_min, logw_max, c_scale, width_min, width_max, eps;
     float *dy;                                     /* [H,T,n_out] */

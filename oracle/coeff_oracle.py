@@ -11,10 +11,13 @@ on the CPU, what model/attn_bias.py computes:
   from the MLP output y: delta* = sigmoid * cap, mu, sigma, pi = softmax,
   slope = c tanh, the Gaussian weights a_mk over log omega normalised over k,
   coeff_cos/sin = sum_m pi_m a_mk cos/sin(w_k delta*_m), b0, delta_main, width.
+* ``reg_loss``: the training regularisers (model/attn_bias.py:480-506).
 
 Pinned against the reference's own outputs by tests/golden/coeff_*.npz.
 """
 from __future__ import annotations
+
+import math
 
 import torch
 import torch.nn.functional as F
@@ -69,4 +72,34 @@ def heads(y: torch.Tensor, *, M: int, omegas, log_omegas, delta_cap: float, logw
     delta_main = torch.gather(delta_star, -1, pi.argmax(dim=-1, keepdim=True)).squeeze(-1)
     width = width_min + (width_max - width_min) * torch.sigmoid(mu.mean(dim=-1))
     return dict(coeff_cos=coeff_cos, coeff_sin=coeff_sin, slope=slope, b0=b0, delta_star=delta_star, pi=pi,
-                budget_logits=budget, delta_main=delta_main, width=width, mu=mu, sigma=sigma)
+                budget_logits=budget, delta_main=delta_main, width=width, mu=mu, sigma=sigma, a_hat=a)
+
+
+def reg_loss(r: dict, *, omegas, T: int, M: int, delta_cap: float, eps: float, lambda_omega: float = 1e-5,
+             lambda_zero_mean: float = 1e-4, lambda_entropy: float = 1e-4, pi_entropy_floor_frac: float = 0.25,
+             lambda_delta_edge: float = 0.0, delta_edge_eps: float = 0.0):
+    """The training regularisers of SpectralBias.forward (model/attn_bias.py:480-506)
+    from the outputs of ``heads``: the omega penalty on the normalised Gaussian
+    weights, the entropy floor on pi, the zero-mean bias term and the delta-edge
+    term."""
+    w = torch.as_tensor(omegas, dtype=torch.float32)
+    reg = torch.zeros((), dtype=torch.float32)
+    if lambda_omega > 0:
+        reg = reg + lambda_omega * ((w ** 2) * r["a_hat"].square()).sum(dim=-1).mean()
+    if lambda_entropy > 0:
+        ent = -(r["pi"] * (r["pi"] + eps).log()).sum(dim=-1)
+        h_floor = float(pi_entropy_floor_frac) * math.log(M)
+        if h_floor > 0:
+            reg = reg + lambda_entropy * F.relu(ent.new_tensor(h_floor) - ent).mean()
+    if lambda_zero_mean > 0:
+        d = torch.arange(T, dtype=torch.float32)
+        cos_mean = torch.cos(w[:, None] * d[None, :]).mean(dim=-1)
+        sin_mean = torch.sin(w[:, None] * d[None, :]).mean(dim=-1)
+        mean_b = ((r["coeff_cos"] * cos_mean).sum(-1) + (r["coeff_sin"] * sin_mean).sum(-1)
+                  + r["slope"] * (0.5 * float(T - 1)) - r["b0"])
+        reg = reg + lambda_zero_mean * mean_b.mean().square()
+    if lambda_delta_edge > 0:
+        u = (r["delta_star"] / max(float(delta_cap), 1.0)).clamp(min=0.0, max=1.0)
+        edge = F.relu(delta_edge_eps - u) + F.relu(u - (1.0 - delta_edge_eps))
+        reg = reg + lambda_delta_edge * edge.mean()
+    return reg

@@ -96,6 +96,7 @@ class ScopeCoeffArgs(ctypes.Structure):
         ("delta_star", P), ("pi", P), ("budget_logits", P),
         ("delta_main", P), ("width", P),
         ("mlp_out", P),
+        ("omega_reg", P),
         ("err_flag", P),
     ]
 
@@ -107,6 +108,7 @@ class ScopeCoeffBwdArgs(ctypes.Structure):
         ("dcoeff_cos", P), ("dcoeff_sin", P),
         ("db0", P), ("dslope", P), ("ddelta_main", P), ("dwidth", P),
         ("ddelta_star", P), ("dpi", P), ("dbudget_logits", P),
+        ("domega_reg", P),
         ("omegas", P), ("log_omegas", P),
         ("delta_cap", F32), ("logw_min", F32), ("logw_max", F32), ("c_scale", F32), ("width_min", F32),
         ("width_max", F32), ("eps", F32),

@@ -8,14 +8,17 @@ knobs; ``forward(q)`` returns what ``SpectralBias.forward`` returns
 MLP and the mixture run in one CUDA kernel (``scope_spectral_coeffs``);
 ``spectral_coefficients`` is the functional form.
 
+Training mode (``train()``) adds the reference's regularisers to reg_loss
+(model/attn_bias.py:480-506): the omega penalty from a per-token term the
+kernel writes, the entropy floor, the zero-mean and the delta-edge terms from
+the block's outputs, all differentiable.
+
 Backward: when q or a weight requires grad, the outputs carry autograd
 history.  The gradient up to the MLP output runs in a CUDA kernel
 (``scope_spectral_coeffs_bwd``: the chain rule through the mixture, the
 normalisation over frequencies, the softmax and the squashing functions);
 the MLP's own backward replays the reference's torch ops on the GPU (two bf16
-linears and a SiLU, model/attn_bias.py:306-324 -- plain library GEMMs).  The
-training regularisers (model/attn_bias.py:480-506) are not computed:
-``reg_loss`` is 0, as in the reference's eval mode.
+linears and a SiLU, model/attn_bias.py:306-324 -- plain library GEMMs).
 """
 from __future__ import annotations
 
@@ -46,6 +49,7 @@ class CoeffOutputs:
     delta_main: Tensor     # [1,H,T]
     width: Tensor          # [1,H,T]
     mlp_out: Optional[Tensor] = None   # [1,H,T,n_out] bf16 when requested
+    omega_reg: Optional[Tensor] = None  # [1,H,T]: sum_m sum_k w_k^2 a_hat_mk^2, when requested
 
 
 def _mlp_torch(q: Tensor, w1: Tensor, b1: Tensor, w2: Tensor, b2: Tensor) -> Tensor:
@@ -65,18 +69,19 @@ def coeff_dy(y: Tensor, grads, *, omegas: Tensor, log_omegas: Tensor, M: int, de
              eps: float) -> Tensor:
     """dL/dy [1,H,T,n_out] f32 from the MLP output y (bf16) and the upstream
     gradients of (coeff_cos, coeff_sin, slope, b0, delta_star, pi,
-    budget_logits, delta_main, width), any of them None."""
+    budget_logits, delta_main, width[, omega_reg]), any of them None."""
     _, H, T, n_out = y.shape
     K = omegas.numel()
     dev = y.device
     dy = torch.empty(1, H, T, n_out, device=dev, dtype=torch.float32)
     g = [None if t is None else t.to(device=dev, dtype=torch.float32).contiguous() for t in grads]
+    g += [None] * (10 - len(g))
     a = _lib.ScopeCoeffBwdArgs()
     a.H, a.T, a.K, a.M, a.use_slope, a.subtract_b0 = H, T, K, M, int(use_slope), int(subtract_b0)
     yc = y.contiguous()
     a.mlp_out = yc.data_ptr()
     names = ("dcoeff_cos", "dcoeff_sin", "dslope", "db0", "ddelta_star", "dpi", "dbudget_logits", "ddelta_main",
-             "dwidth")
+             "dwidth", "domega_reg")
     for n, t in zip(names, g):
         setattr(a, n, None if t is None else t.data_ptr())
     om = omegas.to(device=dev, dtype=torch.float32).contiguous()
@@ -93,17 +98,17 @@ def coeff_dy(y: Tensor, grads, *, omegas: Tensor, log_omegas: Tensor, M: int, de
 class _CoeffFn(torch.autograd.Function):
     @staticmethod
     def forward(ctx, q, w1, b1, w2, b2, kw):
-        o = _coeff_forward(q, w1, b1, w2, b2, **kw, return_mlp=True)
+        o = _coeff_forward(q, w1, b1, w2, b2, **kw, return_mlp=True, return_omega=True)
         ctx.mark_non_differentiable(o.mlp_out)
         ctx.save_for_backward(q, w1, b1, w2, b2, o.mlp_out)
         ctx.kw = kw
-        return tuple(getattr(o, n) for n in OUT_NAMES) + (o.mlp_out,)
+        return tuple(getattr(o, n) for n in OUT_NAMES) + (o.mlp_out, o.omega_reg)
 
     @staticmethod
     def backward(ctx, *grads):
         q, w1, b1, w2, b2, y = ctx.saved_tensors
         kw = {k: v for k, v in ctx.kw.items() if k not in ("return_mlp",)}
-        dy = coeff_dy(y, grads[:9], **kw)
+        dy = coeff_dy(y, list(grads[:9]) + [grads[10]], **kw)
         leaves = [t.detach().requires_grad_(need) for t, need in zip((q, w1, b1, w2, b2), ctx.needs_input_grad[:5])]
         n_out = dy.shape[-1]
         pad = (-n_out) % 16
@@ -126,7 +131,7 @@ def spectral_coefficients(q: Tensor, w1: Tensor, b1: Tensor, w2: Tensor, b2: Ten
                           log_omegas: Optional[Tensor] = None, M: int, delta_cap: float, logw_min: float,
                           logw_max: float, use_slope: bool = True, subtract_b0: bool = True, c_scale: float = 0.01,
                           width_min: float = 32.0, width_max: float = 256.0, eps: float = 1e-9,
-                          return_mlp: bool = False) -> CoeffOutputs:
+                          return_mlp: bool = False, return_omega: bool = False) -> CoeffOutputs:
     """The coefficient block (see ``_coeff_forward`` for the shapes); with
     autograd history when grad mode is on and q or a weight requires grad."""
     lom = log_omegas if log_omegas is not None else omegas.float().log()
@@ -135,15 +140,16 @@ def spectral_coefficients(q: Tensor, w1: Tensor, b1: Tensor, w2: Tensor, b2: Ten
               width_max=width_max, eps=eps)
     if torch.is_grad_enabled() and any(t.requires_grad for t in (q, w1, b1, w2, b2)):
         outs = _CoeffFn.apply(q, w1, b1, w2, b2, kw)
-        return CoeffOutputs(*outs[:9], mlp_out=outs[9].detach() if return_mlp else None)
-    return _coeff_forward(q, w1, b1, w2, b2, **kw, return_mlp=return_mlp)
+        return CoeffOutputs(*outs[:9], mlp_out=outs[9].detach() if return_mlp else None,
+                            omega_reg=outs[10] if return_omega else None)
+    return _coeff_forward(q, w1, b1, w2, b2, **kw, return_mlp=return_mlp, return_omega=return_omega)
 
 
 def _coeff_forward(q: Tensor, w1: Tensor, b1: Tensor, w2: Tensor, b2: Tensor, *, omegas: Tensor,
                           log_omegas: Optional[Tensor] = None, M: int, delta_cap: float, logw_min: float,
                           logw_max: float, use_slope: bool = True, subtract_b0: bool = True, c_scale: float = 0.01,
                           width_min: float = 32.0, width_max: float = 256.0, eps: float = 1e-9,
-                          return_mlp: bool = False) -> CoeffOutputs:
+                          return_mlp: bool = False, return_omega: bool = False) -> CoeffOutputs:
     """q [1,H,T,64] or [H,T,64] bf16 (any head/token strides, last dim
     contiguous); w1 [hid,64] / b1 [hid] / w2 [n_out,hid] / b2 [n_out] shared,
     or with a leading H dim per head, in q's dtype (the reference casts its
@@ -177,7 +183,8 @@ def _coeff_forward(q: Tensor, w1: Tensor, b1: Tensor, w2: Tensor, b2: Tensor, *,
         delta_star=torch.empty(1, H, T, M, **f32), pi=torch.empty(1, H, T, M, **f32),
         budget_logits=torch.empty(1, H, T, M, **f32), delta_main=torch.empty(1, H, T, **f32),
         width=torch.empty(1, H, T, **f32),
-        mlp_out=torch.empty(1, H, T, n_out, device=dev, dtype=torch.bfloat16) if return_mlp else None)
+        mlp_out=torch.empty(1, H, T, n_out, device=dev, dtype=torch.bfloat16) if return_mlp else None,
+        omega_reg=torch.empty(1, H, T, **f32) if return_omega else None)
     a = _lib.ScopeCoeffArgs()
     a.H, a.T, a.D, a.hidden, a.K, a.M = H, T, D, w1.shape[-2], K, M
     a.use_slope, a.subtract_b0 = int(use_slope), int(subtract_b0)
@@ -192,6 +199,7 @@ def _coeff_forward(q: Tensor, w1: Tensor, b1: Tensor, w2: Tensor, b2: Tensor, *,
     for n in OUT_NAMES:
         setattr(a, n, getattr(out, n).data_ptr())
     a.mlp_out = out.mlp_out.data_ptr() if return_mlp else None
+    a.omega_reg = out.omega_reg.data_ptr() if return_omega else None
     a.err_flag = _lib.err_word_ptr(dev)
     _lib.check(_lib.lib().scope_spectral_coeffs(ctypes.byref(a), _stream(dev)), "scope_spectral_coeffs")
     return out
@@ -207,7 +215,9 @@ class SpectralCoefficients:
                  M: int = 2, w_min: Optional[float] = None, w_max: Optional[float] = None,
                  share_across_heads: bool = True, use_slope: bool = True, c_scale: float = 0.01,
                  width_min: float = 32.0, width_max: float = 256.0, delta_star_max: Optional[int] = None,
-                 subtract_b0: bool = True, eps: float = 1e-9, device="cuda", seed: int = 0):
+                 subtract_b0: bool = True, eps: float = 1e-9, lambda_omega: float = 1e-5,
+                 lambda_zero_mean: float = 1e-4, lambda_entropy: float = 1e-4, pi_entropy_floor_frac: float = 0.25,
+                 lambda_delta_edge: float = 0.0, delta_edge_eps: float = 0.0, device="cuda", seed: int = 0):
         if head_dim != 64:
             raise ValueError("SpectralCoefficients: head_dim must be 64")
         self.H, self.K, self.M = num_heads, K, M
@@ -232,6 +242,46 @@ class SpectralCoefficients:
         self.b2[:, :M] = torch.linspace(-6.0, -4.0, M)   # delta* starts small (the reference's output init)
         self.share = share_across_heads
         self.device = device
+        self.training = False
+        self.lambda_omega, self.lambda_zero_mean, self.lambda_entropy = lambda_omega, lambda_zero_mean, lambda_entropy
+        self.pi_entropy_floor_frac = pi_entropy_floor_frac
+        self.lambda_delta_edge, self.delta_edge_eps_active = lambda_delta_edge, delta_edge_eps
+
+    def train(self, mode: bool = True):
+        """Training mode adds the regularisers to reg_loss (model/attn_bias.py:480-506)."""
+        self.training = bool(mode)
+        return self
+
+    def eval(self):
+        return self.train(False)
+
+    def _reg_loss(self, o: CoeffOutputs, T: int, delta_cap: float) -> Tensor:
+        """The reference's training regularisers (model/attn_bias.py:480-506) from
+        the block's outputs; the omega penalty from the kernel's per-token term."""
+        dev = o.coeff_cos.device
+        reg = torch.zeros((), device=dev, dtype=torch.float32)
+        if self.lambda_omega > 0:
+            reg = reg + self.lambda_omega * (o.omega_reg.mean() / self.M)
+        if self.lambda_entropy > 0:
+            ent = -(o.pi * (o.pi + self.eps).log()).sum(dim=-1)
+            h_floor = float(self.pi_entropy_floor_frac) * math.log(self.M)
+            if h_floor > 0:
+                reg = reg + self.lambda_entropy * torch.relu(ent.new_tensor(h_floor) - ent).mean()
+        if self.lambda_zero_mean > 0:
+            d = torch.arange(T, device=dev, dtype=torch.float32)
+            w = self.omegas.to(dev)
+            cos_mean = torch.cos(w[:, None] * d[None, :]).mean(dim=-1)
+            sin_mean = torch.sin(w[:, None] * d[None, :]).mean(dim=-1)
+            mean_b = ((o.coeff_cos * cos_mean).sum(dim=-1) + (o.coeff_sin * sin_mean).sum(dim=-1)
+                      + o.slope * (0.5 * float(T - 1)) - o.b0)
+            reg = reg + self.lambda_zero_mean * mean_b.mean().square()
+        if self.lambda_delta_edge > 0:
+            denom = max(delta_cap, 1.0)
+            u = (o.delta_star / denom).clamp(min=0.0, max=1.0)
+            e = self.delta_edge_eps_active
+            edge = torch.relu(e - u) + torch.relu(u - (1.0 - e))
+            reg = reg + self.lambda_delta_edge * edge.mean()
+        return reg
 
     def set_delta_star_max_active(self, *, max_tokens: int):
         """As SpectralBias.set_delta_star_max_active (model/attn_bias.py:366-371)."""
@@ -254,13 +304,15 @@ class SpectralCoefficients:
         cos_wD, sin_wD, reg_loss (0)."""
         T = q.shape[-2]
         w = (lambda t: t[0]) if self.share else (lambda t: t)
+        cap = float(min(max(self.delta_star_max_active, 0), T - 1))
         o = spectral_coefficients(
             q, w(self.w1), w(self.b1), w(self.w2), w(self.b2), omegas=self.omegas, log_omegas=self.log_omegas,
-            M=self.M, delta_cap=float(min(max(self.delta_star_max_active, 0), T - 1)), logw_min=self.logw_min,
+            M=self.M, delta_cap=cap, logw_min=self.logw_min,
             logw_max=self.logw_max, use_slope=self.use_slope, subtract_b0=self.subtract_b0, c_scale=self.c_scale,
-            width_min=self.width_min, width_max=self.width_max, eps=self.eps, return_mlp=return_mlp)
+            width_min=self.width_min, width_max=self.width_max, eps=self.eps, return_mlp=return_mlp,
+            return_omega=self.training and self.lambda_omega > 0)
         cos_wD, sin_wD = trig_tables(self.omegas, T)
-        reg = torch.zeros((), device=q.device)
+        reg = self._reg_loss(o, T, cap) if self.training else torch.zeros((), device=q.device)
         res = tuple(getattr(o, n) for n in OUT_NAMES) + (cos_wD, sin_wD, reg)
         return (res, o.mlp_out) if return_mlp else res
 

@@ -54,6 +54,7 @@ struct Params {
     float delta_cap, logw_min, logw_max, c_scale, width_min, width_max, eps;
     float *coeff_cos, *coeff_sin, *slope, *b0, *delta_star, *pi, *budget, *delta_main, *width;
     uint16_t *mlp_out;
+    float *omega_reg;
     int32_t *err;
 };
 
@@ -237,7 +238,7 @@ __global__ void __launch_bounds__(256, 2) coeff_kernel(const __grid_constant__ M
 #pragma unroll
         for (int m = 0; m < M; ++m) pi[m] = __fmul_rn(pi[m], rps);
         // the mixture over this thread's half of the pointers
-        float cc[K], cs[K];
+        float cc[K], cs[K], om = 0.f;   // om: sum over this half's pointers of sum_k w_k^2 a_hat^2
 #pragma unroll
         for (int k = 0; k < K; ++k) cc[k] = cs[k] = 0.f;
 #pragma unroll
@@ -258,7 +259,9 @@ __global__ void __launch_bounds__(256, 2) coeff_kernel(const __grid_constant__ M
             const float ran = __frcp_rn(__fadd_rn(asum, p.eps));
 #pragma unroll
             for (int k = 0; k < K; ++k) {
-                const float w = __fmul_rn(pim, __fmul_rn(a[k], ran));
+                const float ah = __fmul_rn(a[k], ran), wk = __ldg(p.omegas + k);
+                om = __fadd_rn(om, __fmul_rn(__fmul_rn(wk, wk), __fmul_rn(ah, ah)));
+                const float w = __fmul_rn(pim, ah);
                 float sn, c;
                 sincos_phase(__fmul_rn(__ldg(p.omegas + k), dsm), &sn, &c);
                 cc[k] = __fadd_rn(cc[k], __fmul_rn(w, c));
@@ -269,6 +272,8 @@ __global__ void __launch_bounds__(256, 2) coeff_kernel(const __grid_constant__ M
         float *xch = reinterpret_cast<float *>(smem + L::Q);   // [2][K][128] (16 KB at most): the q tile is idle now
 #pragma unroll
         for (int k = 0; k < K; ++k) xch[(half * K + k) * 128 + r] = half ? cc[k] : cs[k];
+        float *xom = reinterpret_cast<float *>(smem + L::W1);   // [128]: W1 is idle now too
+        if (half) xom[r] = om;
         asm volatile("bar.sync 1, 256;" ::: "memory");
         float fin[K];
 #pragma unroll
@@ -298,6 +303,7 @@ __global__ void __launch_bounds__(256, 2) coeff_kernel(const __grid_constant__ M
                 p.budget[row * M + m] = y[4 * M + m];
             }
             p.b0[row] = b0;
+            if (p.omega_reg) p.omega_reg[row] = __fadd_rn(om, xom[r]);
         } else {
             p.slope[row] = p.use_slope ? __fmul_rn(p.c_scale, tanhf(y[5 * M])) : 0.f;
             p.delta_main[row] = dmain;
@@ -330,7 +336,7 @@ __global__ void __launch_bounds__(256, 2) coeff_kernel(const __grid_constant__ M
 struct BwdParams {
     int rows, K, M, n_out, use_slope, subtract_b0;
     const uint16_t *y;
-    const float *dcc, *dcs, *db0, *dslope, *ddelta_main, *dwidth, *dds, *dpi, *dbudget;
+    const float *dcc, *dcs, *db0, *dslope, *ddelta_main, *dwidth, *dds, *dpi, *dbudget, *dom;
     const float *omegas, *log_omegas;
     float delta_cap, logw_min, logw_max, c_scale, width_min, width_max, eps;
     float *dy;
@@ -380,6 +386,7 @@ __global__ void __launch_bounds__(128) coeff_bwd_kernel(const BwdParams p) {
         f[k] = p.dcs ? p.dcs[row * K + k] : 0.f;
     }
     float dpi[M], dds[M], dmu[M], dsg[M];
+    const float g_om = p.dom ? p.dom[row] : 0.f;   // gradient of sum_m sum_k w_k^2 a_hat_mk^2
 #pragma unroll
     for (int m = 0; m < M; ++m) {
         const float rden = __frcp_rn(2.f * sg[m] * sg[m]);
@@ -400,7 +407,7 @@ __global__ void __launch_bounds__(128) coeff_bwd_kernel(const BwdParams p) {
             const float g = e[k] * c + f[k] * sn;
             gpi += ah * g;
             gdl += ah * __ldg(p.omegas + k) * (f[k] * c - e[k] * sn);
-            dah[k] = pi[m] * g;
+            dah[k] = pi[m] * g + g_om * 2.f * __ldg(p.omegas + k) * __ldg(p.omegas + k) * ah;
             dot += dah[k] * a[k];
         }
         dpi[m] = gpi + (p.dpi ? p.dpi[row * M + m] : 0.f);
@@ -501,6 +508,7 @@ static int launch(const ScopeCoeffArgs &a, cudaStream_t s) {
     p.delta_main = a.delta_main;
     p.width = a.width;
     p.mlp_out = a.mlp_out;
+    p.omega_reg = a.omega_reg;
     p.err = a.err_flag;
     const size_t smem = L::TOTAL + 1024;
     if (cudaFuncSetAttribute(coeff_kernel<K, M, NP>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
@@ -541,6 +549,7 @@ static int launch_bwd(const ScopeCoeffBwdArgs &a, cudaStream_t s) {
     p.dds = a.ddelta_star;
     p.dpi = a.dpi;
     p.dbudget = a.dbudget_logits;
+    p.dom = a.domega_reg;
     p.omegas = a.omegas;
     p.log_omegas = a.log_omegas;
     p.delta_cap = a.delta_cap;

@@ -230,6 +230,34 @@ def run_coeff_case(SpectralBias, name, case):
     else:
         wg = [sb.w1.grad, sb.b1.grad, sb.w2.grad, sb.b2.grad]
     res.update(dq=q.grad.float().numpy(), **{n: t.numpy() for n, t in zip(("dw1", "db1", "dw2", "db2"), wg)})
+    # training mode: the regularisers join reg_loss (model/attn_bias.py:480-506); backward
+    # from the same upstream gradients plus 1 on reg_loss
+    sb.zero_grad(set_to_none=True)
+    sb.train()
+    qt = torch.from_numpy(x["q"]).to(torch.bfloat16).requires_grad_(True)
+    outs = sb(qt)
+    live = [i for i in range(len(COEFF_OUTS)) if outs[i].requires_grad]
+    torch.autograd.backward([outs[i] for i in live] + [outs[11]],
+                            [torch.from_numpy(ups[i]) for i in live] + [torch.ones(())])
+    if case["share"]:
+        wg = [sb.mlp[0].weight.grad[None], sb.mlp[0].bias.grad[None], sb.mlp[2].weight.grad[None],
+              sb.mlp[2].bias.grad[None]]
+    else:
+        wg = [sb.w1.grad, sb.b1.grad, sb.w2.grad, sb.b2.grad]
+    res.update(t_reg=outs[11].detach().numpy(), t_dq=qt.grad.float().numpy(),
+               **{"t_" + n: t.numpy() for n, t in zip(("dw1", "db1", "dw2", "db2"), wg)})
+    # the gradients of reg_loss alone (the regularisers' share is far below the others')
+    sb.zero_grad(set_to_none=True)
+    qr = torch.from_numpy(x["q"]).to(torch.bfloat16).requires_grad_(True)
+    outs = sb(qr)
+    outs[11].backward()
+    if case["share"]:
+        wg = [sb.mlp[0].weight.grad[None], sb.mlp[0].bias.grad[None], sb.mlp[2].weight.grad[None],
+              sb.mlp[2].bias.grad[None]]
+    else:
+        wg = [sb.w1.grad, sb.b1.grad, sb.w2.grad, sb.b2.grad]
+    res.update(r_dq=qr.grad.float().numpy(), **{"r_" + n: t.numpy() for n, t in zip(("dw1", "db1", "dw2", "db2"), wg)})
+    sb.eval()
     np.savez_compressed(os.path.join(HERE, f"coeff_{name}.npz"), **res, y=y.numpy(),
                         omegas=sb.omegas.numpy(), log_omegas=sb.log_omegas.numpy(),
                         logw_min=sb.logw_min.numpy(), logw_max=sb.logw_max.numpy(),

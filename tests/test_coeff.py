@@ -254,3 +254,47 @@ def test_backward_matches_reference_fixture(name):
         g = got[n].float().cpu().numpy()
         err = np.abs(g - want).max()
         assert err <= 3e-2 * max(np.abs(want).max(), 1e-6), (n, float(err), float(np.abs(want).max()))
+
+
+@pytest.mark.parametrize("name", list(C.COEFF_CASES))
+def test_oracle_regularisers_match_reference_fixture(name):
+    case, x, z = _load(name)
+    kn = _knobs(case, z)
+    kn.pop("omegas"), kn.pop("log_omegas")
+    r = CO.heads(torch.from_numpy(z["y"]), omegas=z["omegas"], log_omegas=z["log_omegas"], **kn)
+    reg = CO.reg_loss(r, omegas=z["omegas"], T=case["T"], M=case["M"], delta_cap=kn["delta_cap"], eps=kn["eps"])
+    assert abs(reg.item() - float(z["t_reg"])) <= 1e-5 * abs(float(z["t_reg"])), (reg.item(), float(z["t_reg"]))
+
+
+def _train_block(case, z, x):
+    from scope_b200 import SpectralCoefficients
+    sc = SpectralCoefficients(head_dim=64, num_heads=case["H"], L_train=case["L_train"], K=case["K"], M=case["M"],
+                              share_across_heads=case["share"], use_slope=case["use_slope"],
+                              subtract_b0=case["subtract_b0"], delta_star_max=case["delta_star_max"])
+    w = {n: t.cuda().float().requires_grad_(True) for n, t in _weights(case, x).items()}
+    sc.load_weights(w["w1"], w["b1"], w["w2"], w["b2"])
+    sc.omegas = torch.from_numpy(z["omegas"]).cuda()
+    sc.log_omegas = torch.from_numpy(z["log_omegas"]).cuda()
+    return sc.train(), w
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("name", list(C.COEFF_CASES))
+def test_training_regularisers_match_reference_fixture(name):
+    """reg_loss in training mode and the gradients of reg_loss alone (the
+    regularisers' share of the full gradient is ~1e-5 of it) against the
+    reference's."""
+    case, x, z = _load(name)
+    sc, w = _train_block(case, z, x)
+    q = torch.from_numpy(x["q"]).to("cuda", torch.bfloat16).requires_grad_(True)
+    res = sc(q)
+    reg = res[11]
+    want = float(z["t_reg"])
+    assert abs(reg.item() - want) <= 2e-3 * abs(want), (reg.item(), want)
+    reg.backward()
+    got = {"dq": q.grad.float(), "dw1": w["w1"].grad, "db1": w["b1"].grad, "dw2": w["w2"].grad, "db2": w["b2"].grad}
+    for n in GRAD_NAMES:
+        ref = z["r_" + n][0] if (case["share"] and n != "dq") else z["r_" + n]
+        g = got[n].float().cpu().numpy()
+        err = np.abs(g - ref).max()
+        assert err <= 5e-2 * max(np.abs(ref).max(), 1e-12), (n, float(err), float(np.abs(ref).max()))
