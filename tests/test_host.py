@@ -76,3 +76,22 @@ def test_ops_registered():
     import torch
     assert hasattr(torch.ops.scope, "sparse_attn")
     assert hasattr(torch.ops.scope, "sparse_attn_bwd")
+
+
+def test_coefficient_entry_points_reject_bad_arguments():
+    """Validation happens before any launch, so it runs without a GPU."""
+    import ctypes
+    import torch
+    from scope_b200 import _lib, spectral_coefficients
+    L = _lib.lib()
+    a = _lib.ScopeCoeffArgs()                      # all zero: no shape, no pointers
+    assert L.scope_spectral_coeffs(ctypes.byref(a), None) == -1
+    a.H, a.T, a.D, a.hidden, a.K, a.M = 2, 100, 64, 128, 16, 8   # T not a multiple of 128
+    assert L.scope_spectral_coeffs(ctypes.byref(a), None) == -1
+    b = _lib.ScopeCoeffBwdArgs()
+    assert L.scope_spectral_coeffs_bwd(ctypes.byref(b), None) == -1
+    assert L.scope_spectral_coeffs(None, None) == -1 and L.scope_spectral_coeffs_bwd(None, None) == -1
+    with pytest.raises(TypeError):                 # a CPU q is refused on the host side
+        spectral_coefficients(torch.zeros(1, 2, 128, 64, dtype=torch.bfloat16), torch.zeros(128, 64),
+                              torch.zeros(128), torch.zeros(41, 128), torch.zeros(41), omegas=torch.ones(16), M=8,
+                              delta_cap=127.0, logw_min=-5.0, logw_max=-1.0)
