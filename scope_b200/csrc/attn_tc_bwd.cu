@@ -106,7 +106,7 @@ struct Plan {
     const int32_t *slot_chunks;
     int32_t *slot_done;
     float *partial;           // [kSlotCap][128 rows][128]: dV (64) | dK (64)
-    int32_t *next_item;       // dK/dV items handed out beyond the first G (zeroed by the plan kernel)
+    int32_t *next_item;       // [2]: dK/dV, dQ items handed out beyond the first G (zeroed by the plan kernel)
 };
 
 struct Params {
@@ -403,6 +403,7 @@ __global__ void __launch_bounds__(kThreads, 1) dkv_kernel(const __grid_constant_
                 uint8_t *res = smem + rb * L::RESB;
                 // buffer rb is free once every role is done with item ci - 2
                 if (ci >= 2 && !cx.wait1(&B.acc_free[rb], ((ci >> 1) - 1) & 1)) break;
+                if (last_res == ci - 2) last_res = -1;   // its tiles were consumed, so they landed
                 B.item_of[rb] = it < n_items ? it : -1;
                 if (it >= n_items) {
                     mbar_arrive(&B.res_full[rb]);      // publishes "no item left"
@@ -726,7 +727,7 @@ __global__ void __launch_bounds__(1024) plan_items_kernel(const int32_t *__restr
     const int per = (rows + blockDim.x - 1) / blockDim.x;
     const int r0 = threadIdx.x * per, r1 = min(rows, r0 + per);
     for (int i = threadIdx.x; i < kSlotCap; i += blockDim.x) plan.slot_done[i] = 0;
-    if (threadIdx.x == 0) *plan.next_item = 0;
+    if (threadIdx.x == 0) plan.next_item[0] = plan.next_item[1] = 0;   // dK/dV and dQ item counters
     int nsplit = 0;
     for (int r = r0; r < r1; ++r) nsplit += nq[r] > kChunk;
     int tot;
@@ -770,9 +771,10 @@ __global__ void __launch_bounds__(1024) plan_items_kernel(const int32_t *__restr
 }
 
 // ============================================================================ dQ
-// Persistent: one CTA per SM walks the work items (head, q block) b, b + G,
-// b + 2G, ... (G CTAs), so that the next item's resident tiles load and its
-// first tiles run while the previous item's epilogue drains.  Resident per item
+// Persistent: one CTA per SM walks the work items (head, q block): its block
+// index first, then the next unclaimed one from an atomic counter (kv lists
+// run from 1 to ~80 tiles), so that the next item's resident tiles load and
+// its first tiles run while the previous item's epilogue drains.  Resident per item
 // (two buffers, item ci in buffer ci & 1): Q, the q_aug dims, dO and the item's
 // rows of the cos / sin tables.  Streamed per kv tile (ring of NST stages, one
 // tile counter across items): K, the k_aug dims, V.
@@ -812,7 +814,9 @@ __global__ void __launch_bounds__(kThreads, 1) dq_kernel(const __grid_constant__
     const int n_items = p.H * p.QB, G = gridDim.x;
     const bool tab = NA > 0 && p.dcoeff_cos && p.tab_smem;
 
-    if (threadIdx.x == 0) B.init(NST, kElem);
+    // acc_free of a resident buffer: the elementwise threads after the item's epilogue,
+    // and each issuing warp once it has read the item's index
+    if (threadIdx.x == 0) B.init(NST, kElem + 2);
     if (warp == 1) {
         tmem_alloc(&B.tmem_slot, kTmemCols);
         tmem_relinquish();
@@ -826,17 +830,25 @@ __global__ void __launch_bounds__(kThreads, 1) dq_kernel(const __grid_constant__
     if (warp == 0) {
         // ---------------- producer: per item the resident tiles, then its kv tiles in list order
         if (lane == 0) {
-            int gt = 0, ci = 0, last_res = -1;
+            int gt = 0, last_res = -1;
             bool ok = true;
-            for (int it = blockIdx.x; ok && it < n_items; it += G, ++ci) {
+            for (int ci = 0; ok; ++ci) {
+                // the first item of each CTA is its block index, the rest are handed out in order
+                const int it = ci == 0 ? (int)blockIdx.x : G + atomicAdd(p.plan.next_item + 1, 1);
+                const int rb = ci & 1;
+                uint8_t *res = smem + rb * L::RESB;
+                // buffer rb is free once every role is done with item ci - 2
+                if (ci >= 2 && !cx.wait1(&B.acc_free[rb], ((ci >> 1) - 1) & 1)) break;
+                if (last_res == ci - 2) last_res = -1;   // its tiles were consumed, so they landed
+                B.item_of[rb] = it < n_items ? it : -1;
+                if (it >= n_items) {
+                    mbar_arrive(&B.res_full[rb]);      // publishes "no item left"
+                    break;
+                }
                 const int h = it / p.QB, qb = it - h * p.QB;
                 const int64_t mrow = (int64_t)h * p.QB + qb;
                 const int n = p.kv_num[mrow];
                 const int32_t *list = p.kv_idx + mrow * p.kv_stride;
-                const int rb = ci & 1;
-                uint8_t *res = smem + rb * L::RESB;
-                // buffer rb is free once the epilogue of item ci - 2 is done with it
-                if (ci >= 2 && !cx.wait1(&B.acc_free[rb], ((ci >> 1) - 1) & 1)) break;
                 if (n > 0) {
                     mbar_expect_tx(&B.res_full[rb], L::RES_BYTES + (tab ? 2u * p.K * 256u : 0u));
                     if (tab) {
@@ -880,16 +892,19 @@ __global__ void __launch_bounds__(kThreads, 1) dq_kernel(const __grid_constant__
     } else if (warp == 1) {
         // ---------------- S / dP issuer (the whole warp waits, lane 0 issues)
         constexpr uint32_t idS = idesc_bf16(128, 128, false, false);
-        int gt = 0, ci = 0;
+        int gt = 0;
         bool ok = true;
-        for (int it = blockIdx.x; ok && it < n_items; it += G, ++ci) {
+        for (int ci = 0; ok; ++ci) {
+            const int rb = ci & 1;
+            if (!cx.waitw(&B.res_full[rb], (ci >> 1) & 1)) { ok = false; break; }
+            const int it = B.item_of[rb];
+            if (lane == 0) mbar_arrive(&B.acc_free[rb]);   // the index is read
+            if (it < 0) break;
             const int h = it / p.QB, qb = it - h * p.QB;
             const int n = p.kv_num[(int64_t)h * p.QB + qb];
             if (n == 0) continue;
-            const int rb = ci & 1;
             const uint32_t res = smem_u32(smem + rb * L::RESB);
             const uint32_t sQ = res + L::Q, sQA = res + L::QA, sDO = res + L::DO;
-            if (!cx.waitw(&B.res_full[rb], (ci >> 1) & 1)) { ok = false; break; }
             for (int jj = 0; jj < n; ++jj, ++gt) {
                 const int st = gt % NST, b = gt & 1;
                 if (!cx.waitw(&B.full[st], (gt / NST) & 1)) { ok = false; break; }
@@ -934,9 +949,14 @@ __global__ void __launch_bounds__(kThreads, 1) dq_kernel(const __grid_constant__
         // one MN-major operand of N = DA whose atoms the descriptor's
         // leading byte offset (4 KiB) steps through
         constexpr uint32_t idA = idesc_bf16(128, DA > 0 ? DA : 16, false, true);
-        int gt = 0, ci = 0;
+        int gt = 0;
         bool ok = true;
-        for (int it = blockIdx.x; ok && it < n_items; it += G, ++ci) {
+        for (int ci = 0; ok; ++ci) {
+            const int rb = ci & 1;
+            if (!cx.waitw(&B.res_full[rb], (ci >> 1) & 1)) { ok = false; break; }
+            const int it = B.item_of[rb];
+            if (lane == 0) mbar_arrive(&B.acc_free[rb]);   // the index is read
+            if (it < 0) break;
             const int h = it / p.QB, qb = it - h * p.QB;
             const int n = p.kv_num[(int64_t)h * p.QB + qb];
             for (int jj = 0; jj < n; ++jj, ++gt) {
@@ -989,12 +1009,15 @@ __global__ void __launch_bounds__(kThreads, 1) dq_kernel(const __grid_constant__
         const bool have_docs = p.docs != nullptr;
         const bool slope_acc = NA > 0 && p.has_slope && p.dslope;
         const uint64_t c2 = f2_pack(p.scale_log2, p.scale_log2);
-        int gt = 0, ci = 0;
+        int gt = 0;
         bool alive = true;
-        for (int it = blockIdx.x; alive && it < n_items; it += G, ++ci) {
+        for (int ci = 0; alive; ++ci) {
+            const int rb = ci & 1;
+            if (!cx.waitw(&B.res_full[rb], (ci >> 1) & 1)) { alive = false; break; }
+            const int it = B.item_of[rb];
+            if (it < 0) break;
             const int h = it / p.QB, qb = it - h * p.QB;
             const int n = p.kv_num[(int64_t)h * p.QB + qb];
-            const int rb = ci & 1;
             uint8_t *res = smem + rb * L::RESB;
             const int i = qb * BM + r;
             const int doc_i = have_docs ? p.docs[i] : 0;
