@@ -130,6 +130,7 @@ class Workload:
             pointer_global_blocks=cfg.global_blocks, pointer_budget_blocks=cfg.budget_blocks,
             pointer_budget_is_total=cfg.budget_is_total, pointer_budget_temp=cfg.budget_temp, debug_stats=True)
         self.leaves = {n: x[n].detach().requires_grad_(True) for n in ("q", "k", "v", "coeff_cos", "coeff_sin")}
+        self.gather_out = self.stats_out = None    # all-gather receive buffers (N > 1)
 
     def build(self):
         x = self.x
@@ -137,21 +138,27 @@ class Workload:
                                              docs=x["docs"], budget_rep=x["budget_rep"],
                                              block_size=self.cfg.block_size)
 
-    def step(self, gather_out=None):
-        """mask build -> forward -> (async all-gather of the output heads, sum of the
-        pointer statistics over ranks) -> backward"""
+    def step(self):
+        """mask build -> forward -> (async all-gathers of the output heads and of the
+        pointer statistics) -> backward"""
         L = self.leaves
         for t in L.values():
             t.grad = None
         bm = self.build()
         sm = SpectralScoreMod(coeff_cos=L["coeff_cos"], coeff_sin=L["coeff_sin"], cos_tab=self.cos_t,
                               sin_tab=self.sin_t, beta=BETA, impl="qk_aug")
-        out = flex_attention(L["q"][None], L["k"][None], L["v"][None], bm, score_mod=sm, scale=SCALE)
+        out = flex_attention(L["q"][None], L["k"][None], L["v"][None], bm, score_mod=sm, scale=SCALE,
+                             head_major_out=self.world > 1)
         works = []
         if self.world > 1:
-            # out[0] is a [H/N, T, D] view of [T, H/N, D] storage: the gather takes it without a copy
-            works.append(shard.gather_heads(out[0].detach().transpose(0, 1), gather_out, async_op=True)[1])
-            works.append(shard.reduce_stats(bm.stats, async_op=True)[1])
+            # out[0] is this rank's [H/N, T, D] head-major slice: the gather lands it in the
+            # [H, T, D] output without a copy or permute
+            if self.gather_out is None:
+                self.gather_out = shard.gather_buffer(self.cfg.T, self.cfg.H, self.cfg.D, self.world,
+                                                      out.dtype, out.device)
+                self.stats_out = shard.stats_buffer(bm.stats, self.world)
+            works.append(shard.gather_heads(out[0].detach(), self.gather_out, async_op=True)[1])
+            works.append(shard.gather_stats(bm.stats, self.stats_out, async_op=True)[1])
         out.backward(self.x["do"][None])
         for w in works:
             w.wait()
@@ -218,8 +225,8 @@ class E2EPipeline:
 
     IN = ("q", "k", "v", "do", "coeff_cos", "coeff_sin", "logits", "gumbel", "budget_rep")
 
-    def __init__(self, wl, host, gather_out=None):
-        self.wl, self.host, self.gather_out = wl, host, gather_out
+    def __init__(self, wl, host):
+        self.wl, self.host = wl, host
         self.dev = [{n: wl.x[n].detach().clone() for n in self.IN} for _ in range(2)]
         self.s_h2d, self.s_d2h = torch.cuda.Stream(), torch.cuda.Stream()
         self.free = [None, None]        # compute done with a slot's inputs
@@ -243,7 +250,7 @@ class E2EPipeline:
             L[n].data = dev[n]
         wl.x["do"] = dev["do"]
         wl.x["logits"], wl.x["gumbel"], wl.x["budget_rep"] = dev["logits"], dev["gumbel"], dev["budget_rep"]
-        bm, out = wl.step(self.gather_out)
+        bm, out = wl.step()
         self.free[k] = cur.record_event()
         self.s_d2h.wait_stream(cur)
         res = [("out", out[0].detach())] + [("d" + n, L[n].grad) for n in ("q", "k", "v", "coeff_cos", "coeff_sin")]
@@ -442,6 +449,136 @@ def cpu_reference(cfg, *, warmup=1, steps=3, heads=1, seconds_budget=60.0):
                       f"{len(times)} timed steps", "seconds_per_step": sec}
 
 
+def run_flex(args):
+    """torch's compiled flex_attention (Inductor Triton) on the GPU: the
+    reference's GPU path for this layer, on the same inputs and mask.  The
+    qk_aug dims are formed by the reference's torch ops (scoped_medium.py:
+    380-421), the call is the compiled standalone flex_attention of
+    scoped_medium.py:37-50 and :422, the mask is the reference's
+    BlockMask.from_kv_blocks call (model/attn_bias.py:851-874) over the
+    flex-padded lists of this configuration (built by this package's builder:
+    the reference's builder sources do not travel to the GPU box).  Times the
+    step (from_kv_blocks + qk_aug prep + forward + backward to q, k, v and the
+    coefficients) and each phase with CUDA events on the current stream."""
+    from torch.nn.attention.flex_attention import BlockMask, flex_attention as torch_flex
+    from scope_b200.synth import build_config_mask
+    torch.cuda.set_device(0)
+    cfg = CONFIGS[args.config]
+    if args.heads:
+        import dataclasses
+        cfg = dataclasses.replace(cfg, H=args.heads)
+    dev = torch.device("cuda", 0)
+    x = make_inputs(cfg, device=dev, seed=0)
+    H, T, D, K, bs = cfg.H, cfg.T, cfg.D, cfg.K, cfg.block_size
+    b = PointerBlockMaskBuilder(num_heads=H, M=cfg.M, pointer_local_blocks=cfg.local_eff,
+                                pointer_half_blocks=cfg.half_blocks, pointer_global_blocks=cfg.global_blocks,
+                                pointer_budget_blocks=cfg.budget_blocks, pointer_budget_is_total=cfg.budget_is_total,
+                                pointer_budget_temp=cfg.budget_temp)
+    bmp = b.select_and_build(pointer_logits=x["logits"], gumbel=x["gumbel"], tau=cfg.select_tau, docs=x["docs"],
+                             budget_rep=x["budget_rep"], block_size=bs, layout="flex_padded")
+    P = int(bmp.kv_num_blocks.sum().item())
+    docs = x["docs"].long()
+
+    def document_causal(b_, h, q_idx, kv_idx):
+        q_ = q_idx.to(torch.long)
+        k_ = kv_idx.to(torch.long)
+        return (q_ >= k_) & (docs[q_] == docs[k_])
+
+    kvn, kvi = bmp.kv_num_blocks.contiguous(), bmp.kv_indices.contiguous()
+
+    def make_mask():
+        return BlockMask.from_kv_blocks(kvn, kvi, torch.zeros_like(kvn), torch.zeros_like(kvi), BLOCK_SIZE=bs,
+                                        mask_mod=document_causal)
+
+    cos_t, sin_t = trig_tables(x["omegas"], T)
+    leaves = {n: x[n].detach().requires_grad_(True) for n in ("q", "k", "v", "coeff_cos", "coeff_sin")}
+    s_aug = math.sqrt(BETA / SCALE)
+
+    def prep():
+        # the reference's qk_aug ops (scoped_medium.py:384-421), B = 1
+        ct = cos_t.transpose(0, 1).to(torch.float32)[None].expand(H, T, K)
+        st = sin_t.transpose(0, 1).to(torch.float32)[None].expand(H, T, K)
+        cc, cs = leaves["coeff_cos"], leaves["coeff_sin"]
+        q_pos = (torch.cat([cc * ct + cs * st, cc * st - cs * ct], -1) * s_aug).to(torch.bfloat16)
+        k_pos = (torch.cat([ct, st], -1) * s_aug).to(torch.bfloat16)
+        qa = torch.cat([leaves["q"], q_pos], -1)
+        ka = torch.cat([leaves["k"], k_pos], -1)
+        va = torch.cat([leaves["v"], leaves["v"].new_zeros(H, T, q_pos.shape[-1])], -1)
+        return qa[None], ka[None], va[None]
+
+    fa = torch.compile(torch_flex, dynamic=False)
+    do = x["do"][None]
+    s = torch.cuda.current_stream()
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(5)]
+
+    def step(acc=None):
+        for t in leaves.values():
+            t.grad = None
+        ev[0].record(s)
+        bmask = make_mask()
+        ev[1].record(s)
+        qa, ka, va = prep()
+        ev[2].record(s)
+        y = fa(qa, ka, va, block_mask=bmask, scale=SCALE)[..., :D]
+        ev[3].record(s)
+        y.backward(do)
+        ev[4].record(s)
+        if acc is not None:
+            torch.cuda.synchronize()
+            for i in range(4):
+                acc[i] += ev[i].elapsed_time(ev[i + 1])
+
+    t0 = time.perf_counter()
+    step()
+    torch.cuda.synchronize()
+    compile_s = time.perf_counter() - t0
+    for _ in range(max(args.warmup, 3) - 1):
+        step()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(s)
+    for _ in range(args.steps):
+        step()
+    e1.record(s)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / args.steps
+    acc = [0.0] * 4
+    reps = 3
+    for _ in range(reps):
+        step(acc)
+    ph = [a / reps for a in acc]
+    flops = 14 * bs * bs * D * P
+    res = {"impl": "torch.compile(flex_attention), Inductor Triton, on the GPU", "value": flops / (ms * 1e-3) / 1e12,
+           "unit": "TFLOP/s", "ms_per_step": ms, "active_block_pairs": P, "steps": args.steps,
+           "phases_ms": {"from_kv_blocks_ms": ph[0], "qk_aug_prep_ms": ph[1], "forward_ms": ph[2],
+                         "backward_ms": ph[3]},
+           "attention_tflops": flops / ((ph[2] + ph[3]) * 1e-3) / 1e12, "compile_s": compile_s,
+           "config": {"workload": f"{cfg.name}: the same layer, head dim 64 + {2 * K} qk_aug dims", "H": H, "T": T,
+                      "block_size": bs, "K": K}}
+    return res
+
+
+def gpu_reference_subprocess(args, timeout_s=480):
+    """run_flex in a child process (bounded in time; a compile failure or
+    a slow compile cannot take the bench down with it)."""
+    cmd = [sys.executable, os.path.abspath(__file__), "--impl", "flex", "--config", args.config, "--steps", "5",
+           "--warmup", "3"]
+    if args.heads:
+        cmd += ["--heads", str(args.heads)]
+    try:
+        r = subprocess.run(cmd, capture_output=True, text=True, timeout=timeout_s)
+    except subprocess.TimeoutExpired:
+        return {"unavailable": f"torch.compile(flex_attention) did not finish within {timeout_s} s"}
+    for ln in reversed(r.stdout.splitlines()):
+        if ln.startswith("{"):
+            try:
+                return json.loads(ln)
+            except ValueError:
+                break
+    tail = (r.stderr or r.stdout).strip().splitlines()[-1:] or ["no output"]
+    return {"unavailable": f"flex_attention run failed (rc {r.returncode}): {tail[0][:200]}"}
+
+
 def run_reference(args):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
@@ -465,7 +602,8 @@ def main():
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--config", default="c3")
-    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference", "flex"])
+    ap.add_argument("--no-gpu-reference", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--heads", type=int, default=0,
@@ -474,6 +612,9 @@ def main():
     if args.impl == "reference":
         run_reference(args)
         return
+    if args.impl == "flex":
+        print(json.dumps(run_flex(args)), flush=True)
+        return
     args.warmup = max(args.warmup, 3)
     rank, world, local = setup_dist()
     cfg = CONFIGS[args.config]
@@ -481,18 +622,15 @@ def main():
         import dataclasses
         cfg = dataclasses.replace(cfg, H=args.heads)
     wl = Workload(cfg, rank, world, "cuda")
-    gather_out = None
-    if world > 1:
-        gather_out = shard.gather_buffer(cfg.T, cfg.H, cfg.D, world, torch.bfloat16, "cuda")
     bm0 = wl.build()
     P_local = active_pairs(bm0)
     for _ in range(args.warmup):
-        wl.step(gather_out)
+        wl.step()
     torch.cuda.synchronize()
     L = _lib.lib()
     n0 = L.scope_launch_count()
     with ClockSampler(local) as clk:
-        ms = time_steps(lambda: wl.step(gather_out), args.steps, world)
+        ms = time_steps(wl.step, args.steps, world)
     launches = L.scope_launch_count() - n0
     P_t = torch.tensor([P_local], device="cuda", dtype=torch.int64)
     if world > 1:
@@ -543,7 +681,7 @@ def main():
             host["out"]["d" + n] = torch.empty(cfg.T, wl.hp, D, dtype=torch.bfloat16).pin_memory().permute(1, 0, 2)
         for n in ("coeff_cos", "coeff_sin"):
             host["out"]["d" + n] = torch.empty_like(wl.x[n], device="cpu").pin_memory()
-        pipe = E2EPipeline(wl, host, gather_out)
+        pipe = E2EPipeline(wl, host)
         for _ in range(2):
             pipe.step()
         pipe.finish()
@@ -569,6 +707,18 @@ def main():
             cpu = {"value": None, "unit": "TFLOP/s", "cores": os.cpu_count(), "kind": "port",
                    "sample": f"failed: {type(e).__name__}: {e}"[:300]}
 
+    gref = None
+    if rank == 0 and world == 1 and not args.no_gpu_reference:
+        # torch's compiled flex_attention (Triton) on this GPU, same layer and inputs,
+        # in a child process (this process's buffers stay resident meanwhile)
+        torch.cuda.synchronize()
+        gref = gpu_reference_subprocess(args)
+        if "value" in gref:
+            gref["ours_over_reference"] = value / gref["value"]
+            ours_attn = (4 + 10) * bs * bs * D * P_local / ((ph[1] + ph[2]) * 1e-3) / 1e12
+            gref["ours_attention_tflops"] = ours_attn
+            gref["attention_ours_over_reference"] = ours_attn / gref["attention_tflops"]
+
     if rank == 0:
         line = {"metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
                 "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "strong",
@@ -578,7 +728,8 @@ def main():
                            "spectral_impl": "qk_aug", "parallelism": f"heads/{world}",
                            "active_block_pairs": P, "l2": "inputs larger than L2 (q,k,v,dO 1 GiB)"},
                 "roofline": roof, "phases_ms": phases, "cpu_baseline": cpu, "e2e": e2e,
-                "clocks": clk.summary(), "gpu_launches": int(launches), "coeff_block": coeff}
+                "clocks": clk.summary(), "gpu_launches": int(launches), "coeff_block": coeff,
+                "gpu_reference": gref}
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.barrier()

@@ -143,6 +143,18 @@ int scope_mask_refine(const int32_t *kv_num, const int32_t *kv_indices, int32_t 
                       int32_t kv_stride_out, uint32_t *q_bitmap_out, int32_t *err_flag,
                       scope_stream_t stream);
 
+/* q-side bitmap [H, QB, ceil(QB/32)] of a mask given only its kv lists: the
+ * q side of a torch BlockMask handed to the attention drop-in, which the
+ * reference builds by BlockMask.from_kv_blocks' dense transpose
+ * (model/attn_bias.py:867-874; torch/nn/attention/flex_attention.py:412-415).
+ * Bit qb of row (h, kb) is set for each kb among the first kv_num[h, qb]
+ * entries of row (h, qb) of kv_indices [H, QB, kv_stride].  The caller zeroes
+ * q_bitmap.  Indices outside [0, QB) are skipped (SCOPE_DEVERR_INDEX); counts
+ * outside [0, kv_stride] are clamped (SCOPE_DEVERR_SHAPE). */
+int scope_mask_bitmap_from_lists(const int32_t *kv_num, const int32_t *kv_indices, int32_t H, int32_t QB,
+                                 int32_t kv_stride, uint32_t *q_bitmap, int32_t *err_flag,
+                                 scope_stream_t stream);
+
 /* ------------------------------------------------------------------------ */
 /* 2. spectral bias helpers                                                   */
 /* ------------------------------------------------------------------------ */
@@ -274,9 +286,9 @@ int scope_attn_bwd(const ScopeAttnArgs *args, scope_stream_t stream);
 /* Workspace bytes scope_attn_bwd needs for these arguments. */
 size_t scope_workspace_bytes(const ScopeAttnArgs *args);
 
-/* Backward for callers that cannot allocate or pass a workspace (a CUDA graph
- * capture that must not allocate, a plugin host that owns all device memory, a
- * binding without a device allocator).  No counterpart in the reference.
+/* Backward for callers that cannot allocate or pass a workspace (a plugin host
+ * that owns all device memory and gives the library no allocator, a binding
+ * without a device allocator).  No counterpart in the reference.
  * Same arguments and results as scope_attn_bwd; args->workspace is ignored and
  * the scratch lives in one file-scope device array of
  * scope_static_scratch_bytes() bytes (32 MiB) that every GPU loading the
@@ -285,7 +297,8 @@ size_t scope_workspace_bytes(const ScopeAttnArgs *args);
  * SCOPE_ERR_WORKSPACE.  It calls no allocator.  Its first call on a device
  * looks up the array's device address (make that first call before any stream
  * capture).  All calls share the array: calls whose kernels overlap on the GPU
- * (different streams, or several devices' work on one context) race on it. */
+ * (different streams, or several devices' work on one context) race on it.  The device address is kept per device: cudaDeviceReset() between
+ * calls is not supported. */
 int scope_attn_bwd_static_scratch(const ScopeAttnArgs *args, scope_stream_t stream);
 
 /* Size in bytes of the array scope_attn_bwd_static_scratch uses. */

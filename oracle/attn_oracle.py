@@ -275,3 +275,135 @@ def block_sparse_forward(q, k, v, kv_num, kv_idx, docs, *, scale: float, block_s
             l = p.sum(dim=-1, keepdim=True)
             out[h, i] = (p @ vf[h, cols]) / torch.where(l > 0, l, torch.ones_like(l))
     return out, pairs
+
+
+class SampledRows:
+    """Forward and gradients of the qk_aug attention call on a SAMPLE of
+    query blocks and kv blocks at full sequence length, in float64 (TEST
+    ORACLE ONLY).
+
+    Restates scoped_medium.py:380-423 (the augmented dims, cast to q's dtype
+    as the reference casts them) followed by flex_attention
+    (scoped_medium.py:422, every listed block partial with the
+    document-causal mask_mod of model/attn_bias.py:674-679) and its autograd
+    backward, one block row at a time, so sizes like T = 2^17 (16 heads) and
+    2^20 stay within seconds of CPU time:
+
+    * ``q_block(h, qb)``: out, lse, dq (first 64 dims) and the gradient of
+      the augmented q dims of the 128 query rows of (h, qb), from the kv
+      blocks of its list (dq = scale · dS · K over the whole row);
+    * ``kv_block(h, kb)``: dk and dv of the kv rows of (h, kb), summed over
+      every query block whose list holds kb (each of those rows' lse and
+      delta = rowsum(dO ∘ out) from its own full list).
+
+    q, k, v, do: [H, T, 64] (CPU, the bf16 values as float); coeff_cos /
+    coeff_sin [H, T, K] float32; cos_tab / sin_tab [K, >= T] bf16; slope
+    [H, T] or None; kv_num [H, QB]; kv_idx [H, QB, W]; docs [T] or None."""
+
+    def __init__(self, q, k, v, do, kv_num, kv_idx, docs, *, block_size, scale, beta=None, coeff_cos=None,
+                 coeff_sin=None, cos_tab=None, sin_tab=None, slope=None, aug_dtype=torch.bfloat16):
+        self.q, self.k, self.v, self.do = q, k, v, do
+        self.kv_num = np.asarray(kv_num)
+        self.kv_idx = np.asarray(kv_idx)
+        self.docs = None if docs is None else torch.as_tensor(np.asarray(docs)).long()
+        self.bs, self.scale = int(block_size), float(scale)
+        self.cc, self.cs, self.slope = coeff_cos, coeff_sin, slope
+        self.ct, self.st = cos_tab, sin_tab
+        self.aug = coeff_cos is not None
+        self.aug_dtype = aug_dtype
+        self.s = math.sqrt(beta / float(scale)) if self.aug else 0.0
+        self.K = 0 if not self.aug else coeff_cos.shape[-1]
+        self._rowcache = {}
+
+    # augmented rows (scoped_medium.py:380-402), cast like the reference
+    def _q_rows(self, h, rows):
+        q = self.q[h, rows].to(torch.float64)
+        if not self.aug:
+            return q
+        c = self.ct[:, rows].to(torch.float32).T
+        sn = self.st[:, rows].to(torch.float32).T
+        A, B = self.cc[h, rows].to(torch.float32), self.cs[h, rows].to(torch.float32)
+        parts = [A * c + B * sn, A * sn - B * c]
+        if self.slope is not None:
+            parts.append((-self.slope[h, rows].to(torch.float32))[:, None])
+        qp = (torch.cat(parts, -1) * self.s).to(self.aug_dtype).to(torch.float64)
+        return torch.cat([q, qp], -1)
+
+    def _k_rows(self, h, rows):
+        k = self.k[h, rows].to(torch.float64)
+        if not self.aug:
+            return k
+        c = self.ct[:, rows].to(torch.float32).T
+        sn = self.st[:, rows].to(torch.float32).T
+        parts = [c, sn]
+        if self.slope is not None:
+            parts.append(rows.to(torch.float32)[:, None])
+        kp = (torch.cat(parts, -1) * self.s).to(self.aug_dtype).to(torch.float64)
+        return torch.cat([k, kp], -1)
+
+    def _row(self, h, qb):
+        """P, dS, the gathered columns and out / lse of one query block."""
+        key = (h, qb)
+        if key in self._rowcache:
+            return self._rowcache[key]
+        bs = self.bs
+        n = int(self.kv_num[h, qb])
+        i = torch.arange(qb * bs, (qb + 1) * bs)
+        blocks = torch.as_tensor(self.kv_idx[h, qb, :n].astype(np.int64))
+        cols = (blocks[:, None] * bs + torch.arange(bs)[None, :]).reshape(-1)
+        qa = self._q_rows(h, i)
+        ka = self._k_rows(h, cols)
+        s = (qa @ ka.T) * self.scale
+        vis = i[:, None] >= cols[None, :]
+        if self.docs is not None:
+            vis = vis & (self.docs[i][:, None] == self.docs[cols][None, :])
+        s = s.masked_fill(~vis, float("-inf"))
+        lse = torch.logsumexp(s, -1)
+        fin = torch.isfinite(lse)
+        p = torch.exp(s - torch.where(fin, lse, torch.zeros_like(lse))[:, None])
+        p = torch.where(vis, p, torch.zeros_like(p))
+        vv = self.v[h, cols].to(torch.float64)
+        out = p @ vv
+        do = self.do[h, i].to(torch.float64)
+        dp = do @ vv.T
+        delta = (do * out).sum(-1)
+        ds = p * (dp - delta[:, None])
+        res = dict(i=i, cols=cols, p=p, ds=ds, out=out, lse=lse, qa=qa, ka=ka, do=do)
+        self._rowcache[key] = res
+        return res
+
+    def q_block(self, h, qb):
+        r = self._row(h, qb)
+        dqa = (r["ds"] @ r["ka"]) * self.scale
+        res = {"out": r["out"], "lse": r["lse"], "dq": dqa[:, :64]}
+        if self.aug:
+            K, s = self.K, self.s
+            dg = dqa[:, 64:]
+            i = r["i"]
+            c = self.ct[:, i].to(torch.float64).T
+            sn = self.st[:, i].to(torch.float64).T
+            res["dcoeff_cos"] = s * (dg[:, :K] * c + dg[:, K:2 * K] * sn)
+            res["dcoeff_sin"] = s * (dg[:, :K] * sn - dg[:, K:2 * K] * c)
+            if self.slope is not None:
+                res["dslope"] = -s * dg[:, 2 * K]
+        return res
+
+    def q_list(self, h, kb):
+        n = self.kv_num[h]
+        W = self.kv_idx.shape[-1]
+        listed = (self.kv_idx[h] == kb) & (np.arange(W)[None, :] < n[:, None])
+        return np.nonzero(listed.any(1))[0]
+
+    def kv_block(self, h, kb):
+        bs = self.bs
+        dk = torch.zeros(bs, 64, dtype=torch.float64)
+        dv = torch.zeros(bs, 64, dtype=torch.float64)
+        qbs = self.q_list(h, kb)
+        for qb in qbs:
+            r = self._row(h, int(qb))
+            sel = (r["cols"] >= kb * bs) & (r["cols"] < (kb + 1) * bs)
+            p, ds = r["p"][:, sel], r["ds"][:, sel]
+            dv += p.T @ r["do"]
+            dk += (ds.T @ r["qa"][:, :64]) * self.scale
+            self._rowcache.pop((h, int(qb)), None)
+        return {"dk": dk, "dv": dv, "q_blocks": len(qbs)}

@@ -123,6 +123,7 @@ SIGNATURES = {
     "scope_mask_build": (I32, [ctypes.POINTER(ScopeMaskArgs), P]),
     "scope_mask_transpose": (I32, [P, I32, I32, P, P, P]),
     "scope_mask_refine": (I32, [P, P, I32, I32, I32, P, P, I32, P, P, P]),
+    "scope_mask_bitmap_from_lists": (I32, [P, P, I32, I32, I32, P, P, P]),
     "scope_trig_tables": (I32, [P, I32, I32, P, P, P]),
     "scope_qk_aug_prepare": (I32, [P, P, P, P, P, I32, I32, I32, I32, I32, F32, F32, I32, P, P, P]),
     "scope_spectral_coeffs": (I32, [ctypes.POINTER(ScopeCoeffArgs), P]),

@@ -33,6 +33,7 @@ from .mask import ScopeBlockMask, _stream
 DTYPES = {torch.float32: 0, torch.bfloat16: 1}
 BIAS_MODES = {"none": 0, "score_mod": 1, "qk_aug": 2}
 GATES = {"none": 0, "softplus": 1, "relu": 2}
+OP_CUDA_CORES, OP_HEAD_MAJOR_OUT = 0x1, 0x2     # `flags` of the custom ops
 
 
 def aug_dims(K: int, slope: bool) -> int:
@@ -161,12 +162,15 @@ def sparse_attn(q: Tensor, k: Tensor, v: Tensor, kv_num: Tensor, kv_indices: Ten
                 b0: Optional[Tensor], slope: Optional[Tensor], delta_main: Optional[Tensor],
                 width: Optional[Tensor], scale: float, beta: float, bias_mode: int, gate: int,
                 gate_lambda: float, gate_tau: float, block_size: int,
-                cuda_cores: bool) -> tuple[Tensor, Tensor, Tensor, Tensor]:
+                flags: int) -> tuple[Tensor, Tensor, Tensor, Tensor]:
     """Returns out, lse and (qk_aug mode) the augmented dims q_aug / k_aug,
-    which the backward reuses; empty tensors in the other modes."""
+    which the backward reuses; empty tensors in the other modes.  ``flags``:
+    OP_CUDA_CORES, OP_HEAD_MAJOR_OUT (out stored [H, T, D] instead of the
+    [T, H, D] storage of the reference's layout)."""
     _check_inputs(q, k, v, kv_num, kv_indices, block_size)
     H, T, D = q.shape
-    out = _new_like_layout(q)
+    cuda_cores = bool(flags & OP_CUDA_CORES)
+    out = torch.empty(H, T, D, dtype=q.dtype, device=q.device) if flags & OP_HEAD_MAJOR_OUT else _new_like_layout(q)
     lse = torch.empty(H, T, dtype=torch.float32, device=q.device)
     q_aug, k_aug = _prepare_aug(q, coeff_cos, coeff_sin, slope, cos_tab, sin_tab, beta, scale, bias_mode)
     a = _attn_args(q, k, v, out, lse, kv_num, kv_indices, q_bitmap, block_info, docs, coeff_cos, coeff_sin,
@@ -180,9 +184,9 @@ def sparse_attn(q: Tensor, k: Tensor, v: Tensor, kv_num: Tensor, kv_indices: Ten
 
 @sparse_attn.register_fake
 def _(q, k, v, kv_num, kv_indices, q_bitmap, block_info, docs, coeff_cos, coeff_sin, cos_tab, sin_tab,
-      b0, slope, delta_main, width, scale, beta, bias_mode, gate, gate_lambda, gate_tau, block_size, cuda_cores):
+      b0, slope, delta_main, width, scale, beta, bias_mode, gate, gate_lambda, gate_tau, block_size, flags):
     H, T, D = q.shape
-    out = q.new_empty(T, H, D).permute(1, 0, 2)
+    out = q.new_empty(H, T, D) if flags & OP_HEAD_MAJOR_OUT else q.new_empty(T, H, D).permute(1, 0, 2)
     if bias_mode == BIAS_MODES["qk_aug"]:
         da = aug_dims(coeff_cos.shape[-1], slope is not None)
         qa, ka = q.new_empty(H, T, da), q.new_empty(T, da)
@@ -199,8 +203,9 @@ def sparse_attn_bwd(dout: Tensor, q: Tensor, k: Tensor, v: Tensor, out: Tensor, 
                     delta_main: Optional[Tensor], width: Optional[Tensor], q_aug: Optional[Tensor],
                     k_aug: Optional[Tensor], scale: float, beta: float,
                     bias_mode: int, gate: int, gate_lambda: float, gate_tau: float, block_size: int,
-                    want_bias_grads: bool, cuda_cores: bool) -> list[Tensor]:
+                    want_bias_grads: bool, flags: int) -> list[Tensor]:
     H, T, D = q.shape
+    cuda_cores = bool(flags & OP_CUDA_CORES)
     if dout.stride(-1) != 1:
         dout = dout.contiguous()
     dq, dk, dv = _new_like_layout(q), _new_like_layout(k), _new_like_layout(v)
@@ -242,7 +247,7 @@ def sparse_attn_bwd(dout: Tensor, q: Tensor, k: Tensor, v: Tensor, out: Tensor, 
 @sparse_attn_bwd.register_fake
 def _(dout, q, k, v, out, lse, kv_num, kv_indices, q_bitmap, block_info, docs, coeff_cos, coeff_sin, cos_tab,
       sin_tab, b0, slope, delta_main, width, q_aug, k_aug, scale, beta, bias_mode, gate, gate_lambda, gate_tau,
-      block_size, want_bias_grads, cuda_cores):
+      block_size, want_bias_grads, flags):
     H, T, D = q.shape
     mk = lambda x: x.new_empty(T, H, D).permute(1, 0, 2)  # noqa: E731
     e = lambda: q.new_empty(0, dtype=torch.float32)  # noqa: E731
@@ -263,24 +268,24 @@ _TENSOR_ARGS = ("q", "k", "v", "kv_num", "kv_indices", "q_bitmap", "block_info",
 def _setup_context(ctx, inputs, output):
     (q, k, v, kv_num, kv_indices, q_bitmap, block_info, docs, coeff_cos, coeff_sin, cos_tab, sin_tab,
      b0, slope, delta_main, width, scale, beta, bias_mode, gate, gate_lambda, gate_tau, block_size,
-     cuda_cores) = inputs
+     flags) = inputs
     out, lse, q_aug, k_aug = output
     ctx.mark_non_differentiable(lse, q_aug, k_aug)
     ctx.save_for_backward(q, k, v, out, lse, kv_num, kv_indices, q_bitmap, block_info, docs, coeff_cos,
                           coeff_sin, cos_tab, sin_tab, b0, slope, delta_main, width, q_aug, k_aug)
-    ctx.scal = (scale, beta, bias_mode, gate, gate_lambda, gate_tau, block_size, cuda_cores)
+    ctx.scal = (scale, beta, bias_mode, gate, gate_lambda, gate_tau, block_size, flags)
 
 
 def _backward(ctx, dout, dlse, dq_aug, dk_aug):
     (q, k, v, out, lse, kv_num, kv_indices, q_bitmap, block_info, docs, coeff_cos, coeff_sin, cos_tab,
      sin_tab, b0, slope, delta_main, width, q_aug, k_aug) = ctx.saved_tensors
-    scale, beta, bias_mode, gate, gate_lambda, gate_tau, block_size, cuda_cores = ctx.scal
+    scale, beta, bias_mode, gate, gate_lambda, gate_tau, block_size, flags = ctx.scal
     nig = ctx.needs_input_grad
     want_bias = any(nig[i] for i in (8, 9, 12, 13, 14, 15))
     g = torch.ops.scope.sparse_attn_bwd(dout, q, k, v, out, lse, kv_num, kv_indices, q_bitmap, block_info, docs,
                                         coeff_cos, coeff_sin, cos_tab, sin_tab, b0, slope, delta_main, width,
                                         q_aug, k_aug, scale, beta, bias_mode, gate, gate_lambda, gate_tau,
-                                        block_size, want_bias, cuda_cores)
+                                        block_size, want_bias, flags)
     dq, dk, dv, dcc, dcs, db0, dsl, ddm, dw = g
     pick = lambda t: t if (t is not None and t.numel() > 0) else None  # noqa: E731
     return (dq, dk, dv, None, None, None, None, None, pick(dcc), pick(dcs), None, None, pick(db0), pick(dsl),
@@ -290,19 +295,29 @@ def _backward(ctx, dout, dlse, dq_aug, dk_aug):
 sparse_attn.register_autograd(_backward, setup_context=_setup_context)
 
 
-def flex_attention(query: Tensor, key: Tensor, value: Tensor, block_mask: ScopeBlockMask,
+def flex_attention(query: Tensor, key: Tensor, value: Tensor, block_mask,
                    score_mod: Optional[SpectralScoreMod] = None, scale: Optional[float] = None,
-                   return_lse: bool = False, cuda_cores: bool = False):
+                   return_lse: bool = False, cuda_cores: bool = False, docs: Optional[Tensor] = None,
+                   head_major_out: bool = False):
     """Block-sparse attention with the SCOPE spectral bias, same call shape
     as torch's flex_attention: q, k, v [1, H, T, D] (any head/token strides,
-    contiguous D), ``block_mask`` from the pointer builder, ``score_mod`` the
-    captured spectral-bias state or None.  Returns [1, H, T, D] in the input
-    dtype (and the [1, H, T] float32 natural-log lse with ``return_lse``).
+    contiguous D), ``block_mask`` from the pointer builder (``ScopeBlockMask``)
+    or a torch ``BlockMask`` such as the reference builder returns (then
+    ``docs`` carries the document ids its document_causal mask_mod captures,
+    see ``ScopeBlockMask.from_flex``), ``score_mod`` the captured
+    spectral-bias state or None.  Returns [1, H, T, D] in the input dtype (and
+    the [1, H, T] float32 natural-log lse with ``return_lse``).
     ``cuda_cores`` runs the CUDA-core kernels even where the tensor-core
-    kernels apply (to cross-check the two)."""
+    kernels apply (to cross-check the two).  ``head_major_out`` stores the
+    output as [H, T, D] (a head shard's slice of the [H, T, D] all-gather
+    buffer) instead of the [T, H, D] storage the reference's layout has."""
     squeeze = query.dim() == 4
     if squeeze and query.shape[0] != 1:
         raise ValueError("batch size must be 1 (as in the reference)")
+    if not isinstance(block_mask, ScopeBlockMask):
+        block_mask = ScopeBlockMask.from_flex(block_mask, docs=docs)
+    elif docs is not None:
+        raise ValueError("docs= goes with a torch BlockMask; a ScopeBlockMask carries its own")
     q, k, v = (_hd(t, 3) for t in (query, key, value))
     D = q.shape[-1]
     sc = float(scale) if scale is not None else 1.0 / math.sqrt(D)
@@ -333,7 +348,9 @@ def flex_attention(query: Tensor, key: Tensor, value: Tensor, block_mask: ScopeB
                                            docs, args["coeff_cos"], args["coeff_sin"], args["cos_tab"],
                                            args["sin_tab"], args["b0"], args["slope"], args["delta_main"],
                                            args["width"], sc, args["beta"], args["bias_mode"], args["gate"],
-                                           args["gate_lambda"], args["gate_tau"], bs, bool(cuda_cores))
+                                           args["gate_lambda"], args["gate_tau"], bs,
+                                           (OP_CUDA_CORES if cuda_cores else 0) |
+                                           (OP_HEAD_MAJOR_OUT if head_major_out else 0))
     if squeeze:
         out, lse = out.unsqueeze(0), lse.unsqueeze(0)
     return (out, lse) if return_lse else out

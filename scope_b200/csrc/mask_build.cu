@@ -632,3 +632,44 @@ extern "C" int scope_mask_refine(const int32_t *kv_num, const int32_t *kv_indice
     SCOPE_CHECK_LAUNCH();
     return SCOPE_OK;
 }
+
+// ---------------------------------------------------------------------------
+// q-side bitmap of a mask given only its kv lists (a torch BlockMask handed to
+// the attention drop-in): bit qb of row (h, kb) set for every kb among the
+// first kv_num[h, qb] entries of row (h, qb).  The caller zeroes the bitmap.
+namespace scope {
+namespace mask {
+__global__ void lists_bitmap_kernel(const int32_t *__restrict__ kv_num, const int32_t *__restrict__ kv_idx, int H,
+                                    int QB, int kv_stride, uint32_t *__restrict__ q_bitmap, int32_t *err) {
+    const int row = blockIdx.x * blockDim.x + threadIdx.x;   // (h, q block)
+    if (row >= H * QB) return;
+    const int h = row / QB, qb = row - h * QB;
+    const int words = (QB + 31) / 32;
+    const int32_t *src = kv_idx + (int64_t)row * kv_stride;
+    int n = kv_num[row];
+    if (n < 0 || n > kv_stride) {
+        set_err(err, SCOPE_DEVERR_SHAPE);
+        n = n < 0 ? 0 : kv_stride;
+    }
+    for (int e = 0; e < n; ++e) {
+        const int kb = src[e];
+        if (kb < 0 || kb >= QB) {            // skipped, as the attention kernels skip it
+            set_err(err, SCOPE_DEVERR_INDEX);
+            continue;
+        }
+        atomicOr(q_bitmap + ((int64_t)h * QB + kb) * words + (qb >> 5), 1u << (qb & 31));
+    }
+}
+}  // namespace mask
+}  // namespace scope
+
+extern "C" int scope_mask_bitmap_from_lists(const int32_t *kv_num, const int32_t *kv_indices, int32_t H, int32_t QB,
+                                            int32_t kv_stride, uint32_t *q_bitmap, int32_t *err_flag,
+                                            scope_stream_t stream) {
+    if (!kv_num || !kv_indices || !q_bitmap || H <= 0 || QB <= 0 || kv_stride <= 0) return SCOPE_ERR_INVALID;
+    const int rows = H * QB;
+    scope::mask::lists_bitmap_kernel<<<ceil_div(rows, 256), 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+        kv_num, kv_indices, H, QB, kv_stride, q_bitmap, err_flag);
+    SCOPE_CHECK_LAUNCH();
+    return SCOPE_OK;
+}

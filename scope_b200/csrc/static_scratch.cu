@@ -1,12 +1,14 @@
 // Backward entry point that allocates nothing and needs no caller workspace.
 //
-// Some callers cannot hand the backward a workspace: code running inside a
-// CUDA graph capture where allocating is not allowed, plugin hosts that own
-// every device allocation themselves, or FFI bindings that have no device
-// allocator at all.  For them the backward's scratch (per-row softmax
-// statistics, the work plan of the dK/dV pass) lives in one fixed-size,
-// file-scope device array instead.  Every GPU that loads this library holds
-// that array (kStaticScratchBytes) until the process exits.
+// Some callers cannot hand the backward a workspace: plugin hosts that own
+// every device allocation themselves and give a library no allocator, or FFI
+// bindings that have no device allocator at all.  For them the backward's
+// scratch (per-row softmax statistics, the work plan of the dK/dV pass)
+// lives in one fixed-size, file-scope device array instead.  Every GPU that
+// loads this library holds that array (kStaticScratchBytes) until the process
+// exits.  The array's device address is looked up once per device and kept:
+// a cudaDeviceReset() between calls is not supported (the library's module
+// is reloaded and the kept address would be stale).
 #include <mutex>
 
 #include "common.cuh"

@@ -111,6 +111,43 @@ class ScopeBlockMask:
                                          max_kv=2 * self.max_kv)
         return self._tiles
 
+    @classmethod
+    def from_flex(cls, block_mask, docs: torch.Tensor | None = None) -> "ScopeBlockMask":
+        """The kernels' view of a torch ``BlockMask`` (B = 1), e.g. the one the
+        reference's ``build_pointer_blockmask`` returns (model/attn_bias.py:
+        851-874): its kv lists as they are, the q-side bitmap from the lists
+        (one kernel launch), ``block_info`` from ``docs``.  A C ABI cannot run
+        the BlockMask's ``mask_mod``, so the document ids it captures travel as
+        ``docs`` ([T], None for a plain causal mask_mod); the reference's
+        document_causal mask_mod (model/attn_bias.py:674-679) is the one the
+        kernels apply.  Full blocks (listed blocks that skip the mask_mod) are
+        not supported: the reference's masks have none, and a mask with any is
+        rejected (checking that reads one device flag back to the host)."""
+        bs_q, bs_kv = block_mask.BLOCK_SIZE
+        if bs_q != bs_kv or bs_q not in (128, 256):
+            raise ValueError(f"BlockMask.BLOCK_SIZE {block_mask.BLOCK_SIZE}: the kernels take square 128 or 256 blocks")
+        kvn, kvi = block_mask.kv_num_blocks, block_mask.kv_indices
+        if kvn.dim() != 3 or kvn.shape[0] != 1 or kvi.dim() != 4 or kvi.shape[:3] != kvn.shape:
+            raise ValueError("BlockMask lists must be kv_num_blocks [1,H,QB] and kv_indices [1,H,QB,W]")
+        fkn = block_mask.full_kv_num_blocks
+        if fkn is not None and bool((fkn != 0).any()):
+            raise ValueError("BlockMask with full blocks: the kernels apply the mask_mod to every listed block")
+        T_q, T_kv = block_mask.seq_lengths
+        H, QB = kvn.shape[1], kvn.shape[2]
+        if T_q != T_kv or T_q != QB * bs_q:
+            raise ValueError("BlockMask must cover T query and T key positions (T = QB * BLOCK_SIZE)")
+        dev = kvn.device
+        kvn = kvn.to(torch.int32).contiguous()
+        kvi = kvi.to(torch.int32).contiguous()
+        words = (QB + 31) // 32
+        qbm = torch.zeros(H, QB, words, dtype=torch.int32, device=dev)
+        st = _lib.lib().scope_mask_bitmap_from_lists(kvn.data_ptr(), kvi.data_ptr(), H, QB, kvi.shape[-1],
+                                                     qbm.data_ptr(), _lib.err_word_ptr(dev), _stream(dev))
+        _lib.check(st, "scope_mask_bitmap_from_lists")
+        d = None if docs is None else docs.to(device=dev, dtype=torch.int32).contiguous()
+        info = block_info(d, T_q, bs_q, device=dev)
+        return cls(kvn, kvi, qbm, info, (bs_q, bs_q), (T_q, T_q), docs=d, max_kv=kvi.shape[-1])
+
     def pointer_stats(self) -> dict:
         """The reference's pointer statistics (model/attn_bias.py:839-849):
         kv_unique_hist, ptr_radius_hist, ptr_extra_sum_hist, radius0 count."""

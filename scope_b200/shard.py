@@ -7,11 +7,14 @@ q / k / v.  Rank r of N therefore owns heads [r*H/N, (r+1)*H/N) and runs the
 path on them with no collective inside the step.  The layer's results are
 combined afterwards, which is the path's one exchange:
 
-  * the attention output [T, H, D] is an all-gather of the ranks' head slices
-    (NCCL over NVLink on a B200 node), and
+  * the attention output is an all-gather of the ranks' head slices (NCCL
+    over NVLink on a B200 node): each rank writes its [H/N, T, D] slice
+    head-major (``flex_attention(..., head_major_out=True)``), so the
+    gathered buffer is the [H, T, D] output with no permute, and
   * the builder's pointer statistics (histograms of list lengths, radii and
-    centre offsets over all heads, the reference's debug stats of
-    model/attn_bias.py:839-849) are a sum over ranks.
+    centre offsets over this rank's heads, the reference's debug stats of
+    model/attn_bias.py:839-849) are all-gathered as [N, n] rows; their sum
+    over ranks is the statistics of the whole layer.
 
 The reference itself trains with data parallelism only (a gradient
 all-reduce, scoped_medium.py:2415); head sharding is this implementation's way of
@@ -36,37 +39,38 @@ def head_slice(H: int, rank: int, world: int) -> slice:
 
 
 def gather_buffer(T: int, H: int, D: int, world: int, dtype: torch.dtype, device) -> torch.Tensor:
-    """Receive buffer of gather_heads: [world, T, H/world, D]."""
-    return torch.empty(world, T, H // world, D, dtype=dtype, device=device)
+    """Receive buffer of gather_heads: the [H, T, D] output of the layer."""
+    return torch.empty(H, T, D, dtype=dtype, device=device)
 
 
 def gather_heads(out_local: torch.Tensor, buf: torch.Tensor, group=None, async_op: bool = False):
     """All-gather of the ranks' output head slices.
 
-    out_local: this rank's output, [T, H/N, D] (any strides; the attention
-    writes [H/N, T, D] views of [T, H/N, D] storage, which this takes as
-    `out.transpose(0, 1)` without a copy when contiguous that way).
-    buf: gather_buffer(...).  Returns (full, work): `full` is the [T, H, D]
-    view of `buf` (head h of rank r at r*H/N + h), valid once `work` (None
-    unless async_op) has been waited on.
+    out_local: this rank's [H/N, T, D] output, head-major contiguous (what
+    ``flex_attention(..., head_major_out=True)`` writes; other layouts are
+    copied first).  buf: gather_buffer(...), [H, T, D]; rank r's heads land
+    at [r*H/N, (r+1)*H/N).  Returns (buf, work): buf holds the layer's
+    [H, T, D] output once `work` (None unless async_op) has been waited on.
     """
-    world, T, hp, D = buf.shape
+    H, T, D = buf.shape
     src = out_local if out_local.is_contiguous() else out_local.contiguous()
-    if tuple(src.shape) != (T, hp, D):
-        raise ValueError(f"local output {tuple(src.shape)} does not match the buffer's slice {(T, hp, D)}")
-    # the receive tensor as the ranks' inputs stacked along dim 0 (the form every backend takes)
-    work = dist.all_gather_into_tensor(buf.view(world * T, hp, D), src, group=group, async_op=async_op)
-    full = buf.permute(1, 0, 2, 3)            # [T, N, H/N, D]: head index r*H/N + h
-    return full, work
+    world = dist.get_world_size(group)
+    if tuple(src.shape) != (H // world, T, D):
+        raise ValueError(f"local output {tuple(src.shape)} does not match the buffer's slice {(H // world, T, D)}")
+    work = dist.all_gather_into_tensor(buf, src, group=group, async_op=async_op)
+    return buf, work
 
 
-def full_heads(full: torch.Tensor) -> torch.Tensor:
-    """[T, N, H/N, D] -> [T, H, D] (a copy)."""
-    T, world, hp, D = full.shape
-    return full.reshape(T, world * hp, D)
+def stats_buffer(stats_local: torch.Tensor, world: int) -> torch.Tensor:
+    """Receive buffer of gather_stats: [world, n]."""
+    return torch.empty(world, stats_local.numel(), dtype=stats_local.dtype, device=stats_local.device)
 
 
-def reduce_stats(stats_local: torch.Tensor, group=None, async_op: bool = False) -> Tuple[torch.Tensor, Optional[object]]:
-    """Sum of the ranks' pointer-statistics histograms, in place."""
-    work = dist.all_reduce(stats_local, op=dist.ReduceOp.SUM, group=group, async_op=async_op)
-    return stats_local, work
+def gather_stats(stats_local: torch.Tensor, buf: torch.Tensor, group=None,
+                 async_op: bool = False) -> Tuple[torch.Tensor, Optional[object]]:
+    """All-gather of the ranks' pointer-statistics histograms into buf [N, n]
+    (row r = rank r's heads); ``buf.sum(0)`` is the whole layer's."""
+    # the receive tensor as the ranks' inputs concatenated (the form every backend takes)
+    work = dist.all_gather_into_tensor(buf.view(-1), stats_local.contiguous().view(-1), group=group,
+                                       async_op=async_op)
+    return buf, work

@@ -169,3 +169,21 @@ def make_inputs(cfg: Config, *, device="cuda", seed: int = 0, heads: slice | Non
 def doc_ids_from_tokens(input_seq: torch.Tensor, eod_token_id: int = 50256) -> torch.Tensor:
     """docs = (input_seq == EOD).cumsum(0) (scoped_medium.py:588)."""
     return (input_seq == eod_token_id).cumsum(0).to(torch.int32)
+
+
+def config_builder(cfg: Config, num_heads: int | None = None, *, debug_stats: bool = False):
+    """The pointer block-mask builder with the configuration's knobs."""
+    from .mask import PointerBlockMaskBuilder
+    return PointerBlockMaskBuilder(
+        num_heads=cfg.H if num_heads is None else num_heads, M=cfg.M, pointer_local_blocks=cfg.local_eff,
+        pointer_half_blocks=cfg.half_blocks, pointer_global_blocks=cfg.global_blocks,
+        pointer_budget_blocks=cfg.budget_blocks, pointer_budget_is_total=cfg.budget_is_total,
+        pointer_budget_temp=cfg.budget_temp, debug_stats=debug_stats)
+
+
+def build_config_mask(cfg: Config, x: dict, builder=None):
+    """The configuration's mask from the inputs of ``make_inputs``: Gumbel
+    top-M selection over the pointer logits fused with the build."""
+    b = builder if builder is not None else config_builder(cfg, x["logits"].shape[0])
+    return b.select_and_build(pointer_logits=x["logits"], gumbel=x["gumbel"], tau=cfg.select_tau, docs=x["docs"],
+                              budget_rep=x["budget_rep"], block_size=cfg.block_size)

@@ -36,7 +36,7 @@ def test_opcheck_sparse_attn():
     bm, q, k, v, cc, cs, ct, st = _case()
     args = (q[0].detach().requires_grad_(True), k[0].detach().requires_grad_(True), v[0].detach().requires_grad_(True),
             bm.kv_num_blocks[0], bm.kv_indices[0], bm.q_bitmap, bm.block_info, bm.docs, cc, cs, ct, st, None, None,
-            None, None, 0.12, 0.5, 2, 0, 0.0, 1.0, 128, False)
+            None, None, 0.12, 0.5, 2, 0, 0.0, 1.0, 128, 0)
     torch.library.opcheck(torch.ops.scope.sparse_attn.default, args,
                           test_utils=("test_schema", "test_autograd_registration", "test_faketensor",
                                       "test_aot_dispatch_dynamic"))

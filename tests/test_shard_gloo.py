@@ -1,7 +1,8 @@
 """Head sharding across ranks (scope_b200.shard) as world_size-2 gloo process
 groups on the CPU: each rank takes its heads of a seeded layer output and
 its own pointer-statistics histogram; the all-gather must rebuild the full
-[T, H, D] output and the reduction must equal the sum of the histograms.
+[H, T, D] output (no permute) and the gathered histograms must be the
+ranks' own, in rank order.
 The GPU run of the same path is bench.py --gpus N (NCCL)."""
 import os
 import socket
@@ -26,7 +27,7 @@ def _free_port():
 
 def _full_output():
     g = torch.Generator().manual_seed(7)
-    return torch.randn(T, H, D, generator=g).to(torch.bfloat16)
+    return torch.randn(H, T, D, generator=g).to(torch.bfloat16)
 
 
 def _stats(rank):
@@ -41,15 +42,17 @@ def _worker(rank, world, port, q):
         dist.init_process_group("gloo", rank=rank, world_size=world)
         full = _full_output()
         hs = shard.head_slice(H, rank, world)
-        # the attention writes [H/N, T, D] views of [T, H/N, D] storage
-        local = full[:, hs, :].contiguous().permute(1, 0, 2).permute(1, 0, 2)
+        # the attention writes this rank's heads head-major: [H/N, T, D]
+        local = full[hs].contiguous()
         buf = shard.gather_buffer(T, H, D, world, torch.bfloat16, "cpu")
         out, work = shard.gather_heads(local, buf, async_op=True)
-        st, work2 = shard.reduce_stats(_stats(rank), async_op=True)
+        mine = _stats(rank)
+        sbuf = shard.stats_buffer(mine, world)
+        st, work2 = shard.gather_stats(mine, sbuf, async_op=True)
         work.wait()
         work2.wait()
-        ok_out = torch.equal(shard.full_heads(out), full)
-        ok_st = torch.equal(st, sum(_stats(r) for r in range(world)))
+        ok_out = torch.equal(out, full) and out.data_ptr() == buf.data_ptr()
+        ok_st = torch.equal(st, torch.stack([_stats(r) for r in range(world)]))
         q.put((rank, ok_out, ok_st, None))
     except Exception as e:  # reported to the parent
         q.put((rank, False, False, repr(e)))
@@ -59,7 +62,7 @@ def _worker(rank, world, port, q):
 
 
 @pytest.mark.parametrize("world", [2])
-def test_head_shards_gather_and_stats_reduce_over_gloo(world):
+def test_head_shards_gather_outputs_and_stats_over_gloo(world):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
@@ -72,7 +75,7 @@ def test_head_shards_gather_and_stats_reduce_over_gloo(world):
     for rank, ok_out, ok_st, err in sorted(res):
         assert err is None, (rank, err)
         assert ok_out, f"rank {rank}: gathered output differs"
-        assert ok_st, f"rank {rank}: reduced statistics differ"
+        assert ok_st, f"rank {rank}: gathered statistics differ"
 
 
 def test_head_slice_rules():

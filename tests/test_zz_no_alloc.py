@@ -1,8 +1,8 @@
 """The allocation-free backward entry point (scope_attn_bwd_static_scratch).
 
-Callers that cannot allocate device memory or pass a workspace — a CUDA graph
-capture that must not allocate, a plugin host that owns all device memory, a
-binding with no device allocator — use this variant; its scratch is a
+Callers that cannot allocate device memory or pass a workspace — a plugin host
+that owns all device memory, a binding with no device allocator — use this
+variant; its scratch is a
 fixed-size device array inside the library.  These tests call it through the
 C ABI and compare it with the regular entry point (which gets a workspace
 from the caller) on the same inputs, twice in a row, since every call reuses
