@@ -11,11 +11,20 @@ across the N ranks; the outputs and pointer statistics are all-gathered over
 NCCL (the path's only collective).  Metric: active-block attention TFLOP/s
 fwd+bwd = 14 * bs^2 * D * sum(kv_num_blocks) / step time, whole job.
 
+The same line carries:
+  * ``gpu_reference``: the reference's GPU path on this GPU, same layer and
+    inputs -- torch.compile(flex_attention) (Inductor Triton) fwd + bwd with
+    the reference's BlockMask.from_kv_blocks and qk_aug tensor ops (run as
+    ``--impl flex`` in a child process, N = 1);
+  * ``decoder``: configuration C4, the 24-layer SCOPE decoder trained
+    data-parallel over the N ranks (tokens/s per GPU, the metric's second half);
+  * ``roofline``, ``phases_ms``, ``cpu_baseline``, ``e2e``, ``clocks``,
+    ``coeff_block`` (the SpectralBias coefficient block kernel).
+
 --impl reference times the reference's CPU path on the host cores (the
 numpy port of its mask builder + torch's compiled CPU flex_attention, forward
-only: the reference has no CPU backward).  --impl flex times torch's
-compiled flex_attention (Triton) on the GPU with the same mask and inputs,
-for comparison; it is not the driver's reference arm.
+only: the reference has no CPU backward).  --impl flex prints the
+gpu_reference measurement on its own; it is not the driver's reference arm.
 """
 from __future__ import annotations
 
@@ -190,9 +199,19 @@ def time_steps(fn, steps, world):
     return ms
 
 
+def gpu_hold(ms=30.0):
+    """Keep the current stream busy for about `ms` (a device-side sleep), so
+    that the host enqueues the work that follows before the GPU reaches it:
+    events recorded after the hold then time device work, not host launch
+    gaps."""
+    torch.cuda._sleep(int(ms * 1e-3 * 2.0e9))
+
+
 def phase_times(wl, reps=3):
     """Average device time of each phase of the step, with CUDA events on the
-    stream the kernels are launched on (the current stream)."""
+    stream the kernels are launched on (the current stream); each repetition
+    is queued behind a device-side hold, so host launch overhead is not
+    counted."""
     s = torch.cuda.current_stream()
     ev = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
     acc = [0.0, 0.0, 0.0]
@@ -200,6 +219,7 @@ def phase_times(wl, reps=3):
     for _ in range(reps):
         for t in L.values():
             t.grad = None
+        gpu_hold()
         ev[0].record(s)
         bm = wl.build()
         ev[1].record(s)
@@ -315,6 +335,7 @@ def coeff_block(wl, cfg, hbm, *, reps=10, cpu=True):
     torch.cuda.synchronize()
     s = torch.cuda.current_stream()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    gpu_hold()
     e0.record(s)
     for _ in range(reps):
         spectral_coefficients(q, *w, **kw)
@@ -337,6 +358,7 @@ def coeff_block(wl, cfg, hbm, *, reps=10, cpu=True):
     for i in range(3 + reps):
         if i == 3:
             torch.cuda.synchronize()
+            gpu_hold()
             e0.record(s)
         o = spectral_coefficients(qg, *wg, **kw)
         if ups is None:
@@ -346,6 +368,8 @@ def coeff_block(wl, cfg, hbm, *, reps=10, cpu=True):
     torch.cuda.synchronize()
     res["fwd_bwd_ms"] = e0.elapsed_time(e1) / reps
     yb = o.mlp_out if o.mlp_out is not None else spectral_coefficients(q, *w, **kw, return_mlp=True).mlp_out
+    torch.cuda.synchronize()
+    gpu_hold()
     e0.record(s)
     for _ in range(reps):
         coeff_dy(yb, [ups[0], ups[1], ups[2]] + [None] * 6, **kw, use_slope=True, subtract_b0=True, c_scale=sc.c_scale,
@@ -368,6 +392,46 @@ def coeff_block(wl, cfg, hbm, *, reps=10, cpu=True):
         res["cpu_baseline"] = {"value": n / dt, "unit": "tokens/s", "cores": torch.get_num_threads(), "kind": "port",
                                "sample": f"1 head x {n} tokens: the oracle's torch-CPU restatement of the reference's "
                                          "MLP and mixture"}
+    return res
+
+
+def decoder_bench(rank, world, *, steps=4, warmup=2, T=65536):
+    """Configuration C4: the 24-layer SCOPE decoder (scope_b200.decoder) trained
+    data-parallel, one sequence of T uniform token ids per rank (shifted
+    targets), forward + backward + bucketed gradient all-reduce + AdamW step.
+    Returns tokens/s per GPU (the metric's second half) and the model FLOP rate
+    (6 x matmul parameters per token plus 14 bs^2 D per active block pair)."""
+    from scope_b200.decoder import BucketedAllReduce, ScopeDecoder, synthetic_tokens
+    torch.manual_seed(0)
+    model = ScopeDecoder(max_seq_len=T).cuda()
+    opt = torch.optim.AdamW(model.parameters(), lr=1e-4, betas=(0.9, 0.95), fused=True)
+    dp = BucketedAllReduce(model.parameters()) if world > 1 else None
+    inp, tgt = synthetic_tokens(T, seed=1000 + rank, device="cuda")
+
+    def step():
+        if dp is not None:
+            dp.zero_grad()
+        else:
+            opt.zero_grad(set_to_none=False)
+        model(inp, tgt).backward()
+        if dp is not None:
+            dp.wait()
+        opt.step()
+
+    for _ in range(warmup):
+        step()
+    ms = time_steps(step, steps, world) / steps
+    pairs = model.attention_pairs()
+    flops = model.flops_per_token() * T + 14 * 128 * 128 * 64 * pairs
+    res = {"workload": "c4: 24 layers, d_model 1024, 16 heads x 64, MLP 4x, vocab 50304, T=65536 per GPU, "
+                       "SCOPE attention (K=8, pointer mask: local 8, 4 pointer blocks) on every layer",
+           "tokens_per_s_per_gpu": T / (ms * 1e-3), "tokens_per_s": world * T / (ms * 1e-3), "ms_per_step": ms,
+           "steps": steps, "warmup": warmup, "parallelism": f"dp{world}",
+           "model_tflops_per_gpu": flops / (ms * 1e-3) / 1e12, "attention_block_pairs_per_layer": pairs / 24,
+           "params": sum(p.numel() for p in model.parameters()), "optimizer": "AdamW (fused)",
+           "grad_allreduce": "bucketed, overlapped with the backward (NCCL)" if world > 1 else "none (1 GPU)"}
+    del model, opt, dp
+    torch.cuda.empty_cache()
     return res
 
 
@@ -604,6 +668,7 @@ def main():
     ap.add_argument("--config", default="c3")
     ap.add_argument("--impl", default="ours", choices=["ours", "reference", "flex"])
     ap.add_argument("--no-gpu-reference", action="store_true")
+    ap.add_argument("--no-decoder", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--heads", type=int, default=0,
@@ -698,6 +763,10 @@ def main():
 
     coeff = coeff_block(wl, cfg, hbm, cpu=(rank == 0 and world == 1 and not args.no_cpu_baseline))
 
+    decoder = None
+    if not args.no_decoder and not args.heads and args.config == "c3":
+        decoder = decoder_bench(rank, world)
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         try:
@@ -729,7 +798,7 @@ def main():
                            "active_block_pairs": P, "l2": "inputs larger than L2 (q,k,v,dO 1 GiB)"},
                 "roofline": roof, "phases_ms": phases, "cpu_baseline": cpu, "e2e": e2e,
                 "clocks": clk.summary(), "gpu_launches": int(launches), "coeff_block": coeff,
-                "gpu_reference": gref}
+                "gpu_reference": gref, "decoder": decoder}
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.barrier()

@@ -1,33 +1,49 @@
 // Block-sparse SCOPE attention backward on the sm_100a tensor cores.
 //
 // Launches, all on the caller's stream:
-//   prep   delta_i = sum_d dO_i . O_i  and  lse2_i = lse_i * log2(e)   (workspace)
-//   plan   per (head, kv block) the number of q blocks that see it (from the
-//          builder's q-side bitmap) and the dK/dV work items
-//   dkv    persistent, one CTA per SM walking the work items (a kv block and a
-//          run of the q blocks that see it, ascending): dV += P^T dO and
-//          dK += dS^T Q in TMEM.
-//   dq     persistent, one CTA per SM walking the (head, q block) items: the kv
-//          list like the forward, dQ += dS K (and, for the qk_aug spectral bias,
-//          the gradient of the augmented dims, turned into dcoeff_cos /
-//          dcoeff_sin / dslope in the epilogue by the chain rule of
-//          scoped_medium.py:380-421).
-// dQ is computed by its own kernel rather than with atomics so every output
-// is written once, deterministically.  A kv block that many q blocks see (a
-// global / sink block is seen by every q block of its document) would make one
-// dK/dV CTA walk a list of up to QB tiles; `plan` cuts such lists into chunks of
-// at most kChunk q tiles handled by separate CTAs, whose fp32 partial sums meet
-// in a small slot buffer that the last chunk of the row converts to bf16.
+//   prep    delta_i = sum_d dO_i . O_i  and  lse2_i = lse_i * log2(e)   (workspace)
+//   plan    per (head, kv block) the number of q blocks that see it (from the
+//           builder's q-side bitmap) and the work items: a kv block and a run
+//           of the q blocks that see it, ascending
+//   dkvq    persistent, one CTA per SM walking the work items.  Per (kv block,
+//           q block) tile it recomputes S^T and dP^T once and produces all
+//           three gradients: dV += P^T dO and dK += dS^T Q accumulate in TMEM
+//           over the item; dQ (and, for the qk_aug spectral bias, the gradient
+//           of the augmented q dims) = dS [K | K_aug] is formed in TMEM per
+//           tile and added into an fp32 accumulator in global memory by
+//           dedicated drain warps (red.global.add, L2-resident adds).
+//   finish  dQ accumulator -> bf16 dq (x scale); the augmented-dim gradient ->
+//           dcoeff_cos / dcoeff_sin / dslope by the chain rule of
+//           scoped_medium.py:380-421.
+// A kv block that many q blocks see (a global / sink block is seen by every q
+// block of its document) would make one CTA walk a list of up to QB tiles;
+// `plan` cuts such lists into chunks of at most kChunk q tiles handled by
+// separate items, whose fp32 dK / dV partial sums meet in a small slot buffer
+// that the last chunk of the row converts to bf16.
 //
-// Both kernels share one pipeline on whole 128x128 tiles (608 threads, one CTA
-// per SM, all 512 TMEM columns): a producer warp (TMA), an S / dP issuing warp,
-// a gradient issuing warp and sixteen elementwise warps (four per TMEM lane
-// quadrant, 32 columns each in two chunks of 16).  S is double buffered in
-// TMEM; dP is single buffered, read by every elementwise warp at the start of
-// a tile and released at once, and the next dP is issued before the next S.
-// P / dS go back into the S buffer as bf16 pairs within each chunk's own
-// columns, where the gradient MMAs read them as their A operand (the even
-// chunks' K steps as soon as they are written).  Every wait is bounded
+// dkvq, per CTA (one per SM, 768 threads, all 512 TMEM columns):
+//   warp 0       producer (TMA): per item K (+ K_aug) and V; per tile Q
+//                (+ Q_aug), dO, lse2, delta into an NST-stage ring
+//   warp 1       S / dP issuer: S^T = K Q^T (+ K_aug Q_aug^T) into SB once the
+//                previous tile's dV MMAs read their P^T from it; dP^T = V dO^T
+//                into DPB once the previous tile's dK MMAs read their dS^T
+//   warp 2       gradient issuer: dV += P^T dO (P^T from TMEM, the even K steps
+//                as soon as every warp wrote its first 16 columns), dK += dS^T Q
+//                (dS^T from TMEM), dQ = dS [K | K_aug] (dS from shared memory)
+//                into DQ once the drain warps copied out the previous tile's
+//   warp 3       no role (it completes the first warpgroup)
+//   warps 4-19   elementwise (four per TMEM lane quadrant): thread = kv row,
+//                32 q columns each: P = exp2(S scale log2e - lse2) (masked),
+//                P^T as bf16 pairs over the warp's own S^T columns; then dP^T 16
+//                columns at a time, dS = P (dP - delta) as bf16 pairs over the
+//                chunk's own dP^T columns and into the shared-memory dS tile
+//   warps 20-23  dQ drain: per tile, the dQ accumulator rows of their lane
+//                quadrant out of TMEM and added into global memory
+// TMEM columns: SB [0,128) S^T, then P^T as bf16 pairs over the read columns;
+// DPB [128,256) dP^T, then dS^T as bf16 pairs; DV [256,320); DK [320,384);
+// DQ [384, 448 + DA) dQ | aug-dim gradient.  The kernel is bound by shared-memory
+// bandwidth: per tile the SS MMAs read ~170 KB of operands, TMA writes ~41 KB,
+// dS and the dQ staging boxes add ~80 KB.  Every wait is bounded
 // (SCOPE_DEVERR_TIMEOUT).
 #include <algorithm>
 #include <cmath>
@@ -43,33 +59,25 @@ using namespace tc;
 
 constexpr int BM = 128;
 constexpr int HD = 64;
-constexpr int kElemWarps = 16;         // four per TMEM lane quadrant, 32 tile columns each
-constexpr int kThreads = 32 * (kElemWarps + 3);   // producer, S/dP issuer, elementwise warps, gradient issuer
-constexpr int kGradWarp = kElemWarps + 2;
-constexpr int kElem = 32 * kElemWarps; // elementwise threads
-constexpr int kChunk = 64;             // max q tiles per dK/dV work item
-constexpr int kSlotCap = 128;          // max kv rows whose q list is split
+constexpr int kElemWarps = 16;          // four per TMEM lane quadrant, 32 tile columns each
+constexpr int kElemWarp0 = 4;           // warpgroups 1-4
+constexpr int kDrainWarp0 = kElemWarp0 + kElemWarps;   // warpgroup 5
+constexpr int kThreads = 32 * (kDrainWarp0 + 4);       // 768: six warpgroups
+constexpr int kElem = 32 * kElemWarps;  // elementwise threads
+constexpr int kDrain = 128;             // drain threads
+constexpr int kDrainBoxes = 3;          // staging boxes per drain warp (reduces in flight)
+constexpr int kIdxWarps = 2 + kElemWarps + 4;   // the issuers, elementwise and drain warps read each item index
+constexpr int kChunk = 64;              // max q tiles per dK/dV work item
+constexpr int kSlotCap = 128;           // max kv rows whose q list is split
 constexpr uint32_t kTmemCols = 512;
-// TMEM columns (one CTA per SM owns all 512):
-//   [0, 256)    two S buffers: S (dq) or S^T (dkv) of a 128 x 128 tile, fp32;
-//               P / dS of the 16 columns [16g, 16g+16) go back into those same
-//               columns as bf16 pairs (dkv: P^T at 16g, dS^T at 16g + 8; dq: dS
-//               at 16g), so every warp writes only over columns it has read
-//   [256, 384)  DP: dP (dq) or dP^T (dkv) of the tile, fp32, one buffer
-//   [384, 448)  ACC0: dV (dkv) | dQ (dq)
-//   [448, 512)  ACC1: dK (dkv) | gradient of the qk_aug dims (dq)
-// S is double buffered so S of tile j+1 is computed while the elementwise
-// warps work on tile j; dP of tile j+1 starts once they have read dP of j.
-constexpr uint32_t DPC = 256, ACC0 = 384, ACC1 = 448;
+constexpr uint32_t SB = 0, DPB = 128, DV = 256, DK = 320, DQ = 384;
+// TMEM column of the bf16 P^T pairs of K step kk (q rows 16kk..16kk+15) of the dV MMA:
+// warp kk/2's chunk kk%2, written over the first 16 of that warp's 32 S^T columns
+__device__ __forceinline__ uint32_t pcol(int kk) { return (uint32_t)(32 * (kk >> 1) + 8 * (kk & 1)); }
 constexpr uint32_t kSmemBudget = 227 * 1024;   // dynamic shared memory per CTA
 constexpr float kLog2e = 1.4426950408889634f;
 
 __host__ __device__ constexpr uint32_t align1k(uint32_t x) { return (x + 1023u) & ~1023u; }
-__device__ __forceinline__ uint32_t sbuf(int b) { return (uint32_t)b * 128u; }
-// K step kk of the gradient contraction (16 tile columns, 8 packed TMEM
-// columns) of the TMEM A operand starts at a_col(kk); in dkv the dS^T pairs
-// follow at +8.
-__device__ __forceinline__ uint32_t a_col(int kk) { return (uint32_t)(16 * kk); }
 
 // ------------------------------------------------------------------ prep
 __global__ void prep_kernel(const __nv_bfloat16 *__restrict__ out, int64_t o_sh, int64_t o_st,
@@ -106,32 +114,29 @@ struct Plan {
     const int32_t *slot_chunks;
     int32_t *slot_done;
     float *partial;           // [kSlotCap][128 rows][128]: dV (64) | dK (64)
-    int32_t *next_item;       // [2]: dK/dV, dQ items handed out beyond the first G (zeroed by the plan kernel)
+    int32_t *next_item;       // items handed out beyond the first G (zeroed by the plan kernel)
 };
 
 struct Params {
-    int H, T, QB, words, kv_stride;
+    int H, T, QB, words;
     const uint32_t *q_bitmap;
-    const int32_t *kv_num, *kv_idx;
     const int32_t *block_info, *docs;
     const float *lse2, *delta;
     float scale, scale_log2;
-    __nv_bfloat16 *g0, *g1;           // dkv: dK, dV      dq: dQ, (unused)
-    int64_t g0_sh, g0_st, g1_sh, g1_st;
-    // dq epilogue for the qk_aug bias
-    int K, has_slope, tab_len, tab_smem;   // tab_smem: table rows 16-byte aligned, staged by the producer
-    const uint16_t *cos_tab, *sin_tab;
+    __nv_bfloat16 *dk, *dv;
+    int64_t dk_sh, dk_st, dv_sh, dv_st;
+    float *dq_acc;            // [H, T, 64 + DA] fp32, zeroed before the launch
+    float *slope_acc;         // [H, T] fp32 (qk_aug with slope), zeroed
     float s_aug;
-    float *dcoeff_cos, *dcoeff_sin, *dslope;
     Plan plan;
     int32_t *err;
 };
 
 struct Maps {
-    CUtensorMap q, k, v, dout, qa, ka;
+    CUtensorMap q, k16, v, dout, qa, ka;   // k16: K in 16-column boxes (32-byte swizzle)
+    CUtensorMap dqa;                       // the fp32 dQ accumulator [H*T, 64 + DA], 32 x 16 boxes
 };
 
-// helpers shared by both kernels ------------------------------------------------
 struct Ctx {
     volatile int *abort_flag;
     int32_t *err;
@@ -154,76 +159,55 @@ struct Ctx {
 };
 
 __device__ __forceinline__ void elem_bar() { asm volatile("bar.sync 1, %0;" ::"n"(kElem) : "memory"); }
+__device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
 
 // mbarriers and small shared state of a backward CTA
 struct Bars {
-    uint64_t res_full[2];              // a work item's resident tiles are in shared memory (buffer ci & 1)
-    uint64_t acc_done;                 // every gradient MMA of a work item completed
-    uint64_t acc_free[2];              // the epilogue of work item ci read the accumulators and is done
-                                       // with resident buffer ci & 1 (elementwise arrivals)
+    uint64_t res_full;                 // an item's K (+aug), V are in shared memory (tx bytes)
+    uint64_t acc_done;                 // every gradient MMA of an item completed
+    uint64_t acc_free;                 // the item's epilogue read dV / dK (elementwise arrivals)
+    uint64_t idx_taken;                // every consuming warp read the item index (one arrival per warp)
     uint64_t full[4], empty[4];        // streamed stage ring
-    uint64_t s_full[2];                // S of a tile is in its buffer
-    uint64_t p_half[2];                // P / dS of the even 16-column chunks are back (elementwise arrivals)
-    uint64_t p_full[2];                // P / dS of every chunk are back in the buffer (elementwise arrivals)
-    uint64_t s_free[2];                // the gradient MMAs that read the buffer completed
-    uint64_t dp_full;                  // dP of a tile is in DP
-    uint64_t dp_free;                  // the elementwise warps have read DP (elementwise arrivals)
+    uint64_t s_full;                   // S^T of a tile is in SB
+    uint64_t p_full;                   // all of P^T is back in the S buffer
+    uint64_t pv_done;                  // the dV MMAs that read P^T completed
+    uint64_t dp_full;                  // dP^T of a tile is in DPB
+    uint64_t ds_ready;                 // dS^T back in DPB and dS in shared memory
+    uint64_t dp_free;                  // the dK MMAs that read dS^T completed
+    uint64_t dq_full;                  // dQ of a tile is in DQ (and the dS tile in shared memory is free)
+    uint64_t dq_free;                  // the drain warps copied DQ out
     uint64_t drain[2];                 // each issuing warp's MMAs completed (before TMEM is freed)
-    volatile int stage_blk[4];         // block index of the tile in each stage
+    volatile int stage_blk[4];         // q block of the tile in each stage
     volatile int stage_mk[4];          // its mask kind
     uint32_t tmem_slot;
-    volatile int abort_flag, last_flag, pad;
-    volatile int item_of[2];           // dkv: the work item in resident buffer b, -1 when none is left
-    __device__ void init(int nst, int acc_free_count) {
-        mbar_init(&res_full[0], 1);
-        mbar_init(&res_full[1], 1);
+    volatile int abort_flag, last_flag, item_of;
+    __device__ void init(int nst) {
+        mbar_init(&res_full, 1);
         mbar_init(&acc_done, 1);
-        mbar_init(&acc_free[0], acc_free_count);
-        mbar_init(&acc_free[1], acc_free_count);
+        mbar_init(&acc_free, kElem);
+        mbar_init(&idx_taken, kIdxWarps);
         for (int i = 0; i < nst; ++i) {
             mbar_init(&full[i], 1);
             mbar_init(&empty[i], 1);
         }
-        for (int i = 0; i < 2; ++i) {
-            mbar_init(&s_full[i], 1);
-            mbar_init(&p_half[i], kElem);
-            mbar_init(&p_full[i], kElem);
-            mbar_init(&s_free[i], 1);
-        }
+        mbar_init(&s_full, 1);
+        mbar_init(&dq_full, 1);
+        mbar_init(&dq_free, kDrain);
+        mbar_init(&p_full, kElem);
+        mbar_init(&pv_done, 1);
         mbar_init(&dp_full, 1);
-        mbar_init(&dp_free, kElem);
+        mbar_init(&ds_ready, kElem);
+        mbar_init(&dp_free, 1);
         mbar_init(&drain[0], 1);
         mbar_init(&drain[1], 1);
         abort_flag = 0;
         last_flag = 0;
+        item_of = 0;
         fence_mbar_init();
     }
 };
 
-// A warp's start of a tile: its 32 dP columns and the first 16 S columns of
-// this thread's TMEM lane in one wait, so dP can be released right away
-__device__ __forceinline__ void ld_tile_start(uint32_t ts, uint32_t tdp, uint32_t (&s0)[16], uint32_t (&dp0)[16],
-                                              uint32_t (&dp1)[16]) {
-    tmem_ld16(ts, s0);
-    tmem_ld16(tdp, dp0);
-    tmem_ld16(tdp + 16, dp1);
-    tmem_wait_ld();
-    pin(s0);
-    pin(dp0);
-    pin(dp1);
-}
-__device__ __forceinline__ void ld_cols16(uint32_t taddr, uint32_t (&r)[16]) {
-    tmem_ld16(taddr, r);
-    tmem_wait_ld();
-    pin(r);
-}
-// 16 values as 8 bf16 pairs at taddr
-__device__ __forceinline__ void st_bf16x16(uint32_t taddr, const float (&x)[16]) {
-    uint32_t pk[8];
-#pragma unroll
-    for (int e = 0; e < 8; ++e) pk[e] = pack_bf16(x[2 * e], x[2 * e + 1]);
-    tmem_st8(taddr, pk);
-}
 // N (16 or 32) fp32 accumulator columns -> 2N bytes of a bf16 row in global memory
 template <int N>
 __device__ __forceinline__ void store_row(uint32_t taddr, float mul, __nv_bfloat16 *dst, bool have) {
@@ -265,19 +249,19 @@ __device__ __forceinline__ int tile_mask_kind(int qb, int kb, bool have_docs, co
     return same_doc ? MASK_CAUSAL : MASK_DOCS;
 }
 
-// One 16-column piece of the dK/dV elementwise stage, thread = kv row j:
-// P = exp2(S * scale*log2e - lse2), dS = P (dP - delta), masked when MASKED.
+// P for 16 columns, thread = kv row j: P = exp2(S * scale*log2e - lse2), zero
+// where the element is masked (column e visible iff e >= lim, and in j's
+// document on boundary tiles).
 template <bool MASKED>
-__device__ __forceinline__ void dkv_piece(float (&s)[16], float (&dp)[16], const float4 *LS, const float4 *DL,
-                                          uint64_t c2, int mk, int lim, const int32_t *docs, int i0, int doc_j) {
+__device__ __forceinline__ void p_piece(float *s, const float4 *LS, uint64_t c2, int mk, int lim,
+                                        const int32_t *docs, int i0, int doc_j) {
 #pragma unroll
     for (int e4 = 0; e4 < 4; ++e4) {
-        const float4 l4 = LS[e4], d4 = DL[e4];
+        const float4 l4 = LS[e4];
 #pragma unroll
         for (int q2 = 0; q2 < 2; ++q2) {
             const int e = e4 * 4 + 2 * q2;
             const uint64_t nl = q2 ? f2_pack(-l4.z, -l4.w) : f2_pack(-l4.x, -l4.y);
-            const uint64_t nd = q2 ? f2_pack(-d4.z, -d4.w) : f2_pack(-d4.x, -d4.y);
             const float2 x = f2_unpack(ffma2(f2_pack(s[e], s[e + 1]), c2, nl));
             float p0 = ex2(x.x), p1 = ex2(x.y);
             if (MASKED) {
@@ -289,68 +273,45 @@ __device__ __forceinline__ void dkv_piece(float (&s)[16], float (&dp)[16], const
                 p0 = v0 ? p0 : 0.f;
                 p1 = v1 ? p1 : 0.f;
             }
-            const float2 ds = f2_unpack(fmul2(f2_pack(p0, p1), fadd2(f2_pack(dp[e], dp[e + 1]), nd)));
             s[e] = p0;
             s[e + 1] = p1;
+        }
+    }
+}
+
+// dS = P (dP - delta) for 16 columns, into dp
+__device__ __forceinline__ void ds_piece(const float *p, float *dp, const float4 *DL) {
+#pragma unroll
+    for (int e4 = 0; e4 < 4; ++e4) {
+        const float4 d4 = DL[e4];
+#pragma unroll
+        for (int q2 = 0; q2 < 2; ++q2) {
+            const int e = e4 * 4 + 2 * q2;
+            const uint64_t nd = q2 ? f2_pack(-d4.z, -d4.w) : f2_pack(-d4.x, -d4.y);
+            const float2 ds = f2_unpack(fmul2(f2_pack(p[e], p[e + 1]), fadd2(f2_pack(dp[e], dp[e + 1]), nd)));
             dp[e] = ds.x;
             dp[e + 1] = ds.y;
         }
     }
 }
 
-// One 16-column piece of the dQ elementwise stage, thread = q row i; dS -> s.
-template <bool MASKED>
-__device__ __forceinline__ void dq_piece(float (&s)[16], const float (&dp)[16], uint64_t c2, uint64_t nl2,
-                                         uint64_t nd2, int mk, int lim, bool bad, const int32_t *docs, int j0,
-                                         int doc_i) {
+// Column sums of a warp's 32-row x 16-column block: lane l returns the sum over
+// the 32 lanes of v[l & 15] (a butterfly that halves the values each lane carries
+// every round, then the two 16-lane halves added).
+__device__ __forceinline__ float warp_column_sums16(float (&v)[16]) {
+    const int lane = threadIdx.x & 31;
 #pragma unroll
-    for (int e = 0; e < 16; e += 2) {
-        const float2 x = f2_unpack(ffma2(f2_pack(s[e], s[e + 1]), c2, nl2));
-        float p0 = ex2(x.x), p1 = ex2(x.y);
-        if (MASKED) {
-            bool v0 = e <= lim && !bad, v1 = e + 1 <= lim && !bad;
-            if (mk == MASK_DOCS && docs && !bad) {
-                v0 = v0 && (__ldg(docs + j0 + e) == doc_i);
-                v1 = v1 && (__ldg(docs + j0 + e + 1) == doc_i);
-            }
-            p0 = v0 ? p0 : 0.f;
-            p1 = v1 ? p1 : 0.f;
+    for (int w = 8; w >= 1; w >>= 1) {
+        const bool hi = (lane & w) != 0;
+#pragma unroll
+        for (int e = 0; e < w; ++e) {
+            const float send = hi ? v[e] : v[e + w];
+            const float keep = hi ? v[e + w] : v[e];
+            v[e] = keep + __shfl_xor_sync(0xffffffffu, send, w);
         }
-        const float2 ds = f2_unpack(fmul2(f2_pack(p0, p1), fadd2(f2_pack(dp[e], dp[e + 1]), nd2)));
-        s[e] = ds.x;
-        s[e + 1] = ds.y;
     }
+    return v[0] + __shfl_xor_sync(0xffffffffu, v[0], 16);
 }
-
-// ============================================================================ dK / dV
-// Persistent: one CTA per SM walks work items of the plan (its block index
-// first, then the next unclaimed one from an atomic counter: the items range
-// from 1 to kChunk q tiles), so that the next item's resident tiles load and
-// its first tiles run while the previous item's epilogue drains.  The
-// producer publishes each item's index with the resident buffer's barrier.  Resident per item (two
-// buffers, item ci in buffer ci & 1): K, the k_aug dims, V.  Streamed per q tile
-// (ring of NST stages, one tile counter across items): Q, the q_aug dims, dO,
-// lse2, delta.
-template <int DA>
-struct KVL {
-    static constexpr int NA = DA / 16;
-    static constexpr uint32_t TILE = BM * HD * 2, ATILE = BM * 16 * 2;
-    static constexpr uint32_t K = 0, KA = TILE, V = align1k(TILE + NA * ATILE);   // within a resident buffer
-    static constexpr uint32_t RESB = align1k(V + TILE);
-    static constexpr uint32_t STAGE0 = 2 * RESB;
-    static constexpr uint32_t SQ = 0, SQA = TILE, SDO = align1k(TILE + NA * ATILE), SLSE = SDO + TILE,
-                              SDEL = SLSE + 512;
-    static constexpr uint32_t STAGE = align1k(SDEL + 512);
-    static constexpr uint32_t EXTRA = 1024 + 1024;                  // barriers, base alignment
-    static constexpr int NST = STAGE0 + 4 * STAGE + EXTRA <= kSmemBudget
-                                   ? 4
-                                   : (STAGE0 + 3 * STAGE + EXTRA <= kSmemBudget ? 3 : 2);
-    static constexpr uint32_t BAR = STAGE0 + NST * STAGE;
-    static constexpr uint32_t RES_BYTES = 2 * TILE + NA * ATILE;
-    static constexpr uint32_t TOTAL = BAR + sizeof(Bars);
-    static constexpr uint32_t Q_BYTES = 2 * TILE + NA * ATILE + 1024;
-    static_assert(TOTAL + 1024 <= kSmemBudget, "shared memory");
-};
 
 // rank-th set bit onward of a bitmap row: the word index and remaining bits
 __device__ __forceinline__ void seek_rank(const uint32_t *row, int words, int rank, int &w, uint32_t &bits) {
@@ -364,10 +325,52 @@ __device__ __forceinline__ void seek_rank(const uint32_t *row, int words, int ra
     }
     for (; rank > 0 && bits; --rank) bits &= bits - 1;
 }
+// next set bit of the walk (-1 past the end)
+__device__ __forceinline__ int next_bit(const uint32_t *row, int words, int &w, uint32_t &bits) {
+    while (!bits) {
+        if (++w >= words) return -1;
+        bits = row[w];
+    }
+    const int qb = w * 32 + __ffs(bits) - 1;
+    bits &= bits - 1;
+    return qb;
+}
 
+// Shared memory of a dkvq CTA.  K and the aug dims of a kv block are 16-column
+// sub-tiles (32-byte swizzle) 4 KiB apart, so [K | K_aug] is one MN-major B
+// operand of N = 64 + DA for dQ and K-major A operands (one per K step) for S^T.
+// dS is stored MN-major (128-byte swizzle, two 64-column halves 16 KiB apart),
+// the A operand of dQ = dS [K | K_aug].
 template <int DA>
-__global__ void __launch_bounds__(kThreads, 1) dkv_kernel(const __grid_constant__ Maps maps, const Params p) {
-    using L = KVL<DA>;
+struct FL {
+    static constexpr int NA = DA / 16;
+    static constexpr int NKA = 4 + NA;                        // K + K_aug sub-tiles
+    static constexpr uint32_t TILE = BM * HD * 2, ATILE = BM * 16 * 2;
+    static constexpr uint32_t RK = 0, RV = align1k(NKA * ATILE);
+    static constexpr uint32_t RESB = align1k(RV + TILE);
+    static constexpr uint32_t DS = RESB;                      // dS tile, 32 KiB
+    static constexpr uint32_t STAGE0 = DS + 2 * TILE;
+    static constexpr uint32_t SQ = 0, SQA = TILE, SDO = align1k(TILE + NA * ATILE), SLSE = SDO + TILE,
+                              SDEL = SLSE + 512;
+    static constexpr uint32_t STAGE = align1k(SDEL + 512);
+    static constexpr uint32_t EXTRA = 1024 + 1024;            // barriers, base alignment
+    static constexpr uint32_t DRN_BYTES = 4 * kDrainBoxes * 2048;   // drain staging: 32 x 16 fp32 boxes
+    static constexpr int NST = STAGE0 + 4 * STAGE + DRN_BYTES + EXTRA <= kSmemBudget
+                                   ? 4
+                                   : (STAGE0 + 3 * STAGE + DRN_BYTES + EXTRA <= kSmemBudget ? 3 : 2);
+    static constexpr uint32_t DRN = STAGE0 + NST * STAGE;       // 1024-aligned (STAGE0, STAGE are)
+    static constexpr uint32_t BAR = DRN + DRN_BYTES;
+    static constexpr uint32_t RES_BYTES = NKA * ATILE + TILE;
+    static constexpr uint32_t Q_BYTES = 2 * TILE + NA * ATILE + 1024;
+    static constexpr uint32_t TOTAL = BAR + sizeof(Bars);
+    static constexpr int DQN = 64 + DA;                       // dQ accumulator columns
+    static_assert(TOTAL + 1024 <= kSmemBudget, "shared memory");
+    static_assert(DQ + DQN <= kTmemCols, "tensor memory");
+};
+
+template <int DA, bool SLOPE>
+__global__ void __launch_bounds__(kThreads, 1) dkvq_kernel(const __grid_constant__ Maps maps, const Params p) {
+    using L = FL<DA>;
     constexpr int NA = L::NA, NST = L::NST;
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
@@ -377,63 +380,58 @@ __global__ void __launch_bounds__(kThreads, 1) dkv_kernel(const __grid_constant_
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int n_items = *p.plan.n_items, G = gridDim.x;
 
-    // acc_free of a resident buffer: the elementwise threads after the item's epilogue,
-    // and each issuing warp once it has read the item's index
-    if (threadIdx.x == 0) B.init(NST, kElem + 2);
+    if (threadIdx.x == 0) B.init(NST);
     if (warp == 1) {
         tmem_alloc(&B.tmem_slot, kTmemCols);
         tmem_relinquish();
     }
-    __syncwarp();   // every warp reaches the CTA barrier converged (the producer ran on lane 0 alone)
+    __syncwarp();
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = B.tmem_slot;
+    const uint32_t sK = smem_u32(smem + L::RK), sV = smem_u32(smem + L::RV), sDS = smem_u32(smem + L::DS);
 
     if (warp == 0) {
-        // ---------------- producer: per item K / V into its resident buffer, then the q tiles
-        // that see the kv block, ascending
+        // ---------------- producer: per item K (+aug) / V, then the q tiles that see the kv block
         if (lane == 0) {
             int gt = 0, last_res = -1;
             bool ok = true;
             for (int ci = 0; ok; ++ci) {
                 // the first item of each CTA is its block index, the rest are handed out in order
                 const int it = ci == 0 ? (int)blockIdx.x : G + atomicAdd(p.plan.next_item, 1);
-                const int rb = ci & 1;
-                uint8_t *res = smem + rb * L::RESB;
-                // buffer rb is free once every role is done with item ci - 2
-                if (ci >= 2 && !cx.wait1(&B.acc_free[rb], ((ci >> 1) - 1) & 1)) break;
-                if (last_res == ci - 2) last_res = -1;   // its tiles were consumed, so they landed
-                B.item_of[rb] = it < n_items ? it : -1;
+                // the item index may be replaced once every warp read the previous one, the
+                // residents once every MMA of the previous item completed
+                if (ci >= 1 && (!cx.wait1(&B.idx_taken, (ci - 1) & 1) || !cx.wait1(&B.acc_done, (ci - 1) & 1))) break;
+                last_res = -1;
+                B.item_of = it < n_items ? it : -1;
                 if (it >= n_items) {
-                    mbar_arrive(&B.res_full[rb]);      // publishes "no item left"
+                    mbar_arrive(&B.res_full);      // publishes "no item left"
                     break;
                 }
                 const int4 item = p.plan.items[it];
                 const int h = item.x, kb = item.y, first = item.z, nq = item.w;
                 if (nq > 0) {
-                    mbar_expect_tx(&B.res_full[rb], L::RES_BYTES);
-                    tma_load_3d(&maps.k, res + L::K, &B.res_full[rb], 0, kb * BM, h);
+                    mbar_expect_tx(&B.res_full, L::RES_BYTES);
+#pragma unroll
+                    for (int a = 0; a < 4; ++a)
+                        tma_load_3d(&maps.k16, smem + L::RK + a * L::ATILE, &B.res_full, 16 * a, kb * BM, h);
 #pragma unroll
                     for (int a = 0; a < NA; ++a)
-                        tma_load_2d(&maps.ka, res + L::KA + a * L::ATILE, &B.res_full[rb], 16 * a, kb * BM);
-                    tma_load_3d(&maps.v, res + L::V, &B.res_full[rb], 0, kb * BM, h);
+                        tma_load_2d(&maps.ka, smem + L::RK + (4 + a) * L::ATILE, &B.res_full, 16 * a, kb * BM);
+                    tma_load_3d(&maps.v, smem + L::RV, &B.res_full, 0, kb * BM, h);
                     last_res = ci;
                 } else {
-                    mbar_arrive(&B.res_full[rb]);      // keeps the buffer's phases in step
+                    mbar_arrive(&B.res_full);      // keeps the phases in step
                 }
                 const uint32_t *brow = p.q_bitmap + ((int64_t)h * p.QB + kb) * p.words;
                 int w;
                 uint32_t bits;
                 seek_rank(brow, p.words, first, w, bits);
                 int t = 0;
-                while (t < nq && w < p.words) {
-                    if (!bits) {
-                        if (++w < p.words) bits = brow[w];
-                        continue;
-                    }
-                    const int qb = w * 32 + __ffs(bits) - 1;
-                    bits &= bits - 1;
+                for (; t < nq; ++t) {
+                    const int qb = next_bit(brow, p.words, w, bits);
+                    if (qb < 0) break;
                     const int st = gt % NST;
                     if (gt >= NST && !cx.wait1(&B.empty[st], ((gt / NST) - 1) & 1)) { ok = false; break; }
                     uint8_t *sb = smem + L::STAGE0 + st * L::STAGE;
@@ -448,7 +446,6 @@ __global__ void __launch_bounds__(kThreads, 1) dkv_kernel(const __grid_constant_
                     const int64_t off = (int64_t)h * p.T + (int64_t)qb * BM;
                     bulk_load(sb + L::SLSE, p.lse2 + off, 512, &B.full[st]);
                     bulk_load(sb + L::SDEL, p.delta + off, 512, &B.full[st]);
-                    ++t;
                     ++gt;
                 }
                 if (ok && t < nq) {   // the plan promised more q blocks than the bitmap row holds
@@ -458,7 +455,7 @@ __global__ void __launch_bounds__(kThreads, 1) dkv_kernel(const __grid_constant_
                 }
             }
             // never leave the CTA with a TMA write still in flight
-            if (last_res >= 0) mbar_wait(&B.res_full[last_res & 1], (last_res >> 1) & 1, 500000000ull);
+            if (last_res >= 0) mbar_wait(&B.res_full, last_res & 1, 500000000ull);
             for (int j = (gt > NST ? gt - NST : 0); j < gt; ++j) mbar_wait(&B.full[j % NST], (j / NST) & 1, 500000000ull);
         }
     } else if (warp == 1) {
@@ -467,43 +464,41 @@ __global__ void __launch_bounds__(kThreads, 1) dkv_kernel(const __grid_constant_
         int gt = 0;
         bool ok = true;
         for (int ci = 0; ok; ++ci) {
-            const int rb = ci & 1;
-            if (!cx.waitw(&B.res_full[rb], (ci >> 1) & 1)) { ok = false; break; }
-            const int it = B.item_of[rb];
-            if (lane == 0) mbar_arrive(&B.acc_free[rb]);   // the index is read
+            if (!cx.waitw(&B.res_full, ci & 1)) { ok = false; break; }
+            const int it = B.item_of;
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&B.idx_taken);
             if (it < 0) break;
             const int nq = p.plan.items[it].w;
-            const uint32_t res = smem_u32(smem + rb * L::RESB);
-            const uint32_t sK = res + L::K, sKA = res + L::KA, sV = res + L::V;
             for (int t = 0; t < nq; ++t, ++gt) {
-                const int st = gt % NST, b = gt & 1;
+                const int st = gt % NST;
                 if (!cx.waitw(&B.full[st], (gt / NST) & 1)) { ok = false; break; }
                 const uint32_t sb = smem_u32(smem + L::STAGE0 + st * L::STAGE);
-                // dP^T = V dO^T first: the elementwise warps release dP^T of the previous tile
-                // as they start it, while S^T waits for the gradient MMAs of tile gt-2
+                // S^T = K Q^T (+ K_aug Q_aug^T) into SB once the dV MMAs of the previous tile
+                // read their P^T from it
+                if (gt >= 1 && !cx.waitw(&B.pv_done, (gt - 1) & 1)) { ok = false; break; }
+                tc_fence_after();
+                if (lane == 0) {
+#pragma unroll
+                    for (int kk = 0; kk < 4; ++kk)
+                        mma_ss(tmem + SB, kmajor_desc(sK + kk * L::ATILE, 32),
+                               kmajor_desc(sb + L::SQ + kk * 32, 128), idS, kk > 0);
+#pragma unroll
+                    for (int a = 0; a < NA; ++a)
+                        mma_ss(tmem + SB, kmajor_desc(sK + (4 + a) * L::ATILE, 32),
+                               kmajor_desc(sb + L::SQA + a * L::ATILE, 32), idS, 1);
+                    tc_commit(&B.s_full);
+                }
+                __syncwarp();
+                // dP^T = V dO^T once the dK MMAs of the previous tile read its dS^T
                 if (gt >= 1 && !cx.waitw(&B.dp_free, (gt - 1) & 1)) { ok = false; break; }
                 tc_fence_after();
                 if (lane == 0) {
 #pragma unroll
                     for (int kk = 0; kk < 4; ++kk)
-                        mma_ss(tmem + DPC, kmajor_desc(sV + kk * 32, 128), kmajor_desc(sb + L::SDO + kk * 32, 128), idS,
+                        mma_ss(tmem + DPB, kmajor_desc(sV + kk * 32, 128), kmajor_desc(sb + L::SDO + kk * 32, 128), idS,
                                kk > 0);
                     tc_commit(&B.dp_full);
-                }
-                __syncwarp();
-                // S^T = K Q^T (+ Kaug Qaug^T): 128 kv rows x 128 q columns
-                if (gt >= 2 && !cx.waitw(&B.s_free[b], ((gt >> 1) - 1) & 1)) { ok = false; break; }
-                tc_fence_after();
-                if (lane == 0) {
-#pragma unroll
-                    for (int kk = 0; kk < 4; ++kk)
-                        mma_ss(tmem + sbuf(b), kmajor_desc(sK + kk * 32, 128), kmajor_desc(sb + L::SQ + kk * 32, 128),
-                               idS, kk > 0);
-#pragma unroll
-                    for (int a = 0; a < NA; ++a)
-                        mma_ss(tmem + sbuf(b), kmajor_desc(sKA + a * L::ATILE, 32),
-                               kmajor_desc(sb + L::SQA + a * L::ATILE, 32), idS, 1);
-                    tc_commit(&B.s_full[b]);
                 }
                 __syncwarp();
             }
@@ -511,131 +506,195 @@ __global__ void __launch_bounds__(kThreads, 1) dkv_kernel(const __grid_constant_
         if (!ok) cx.give_up();
         if (lane == 0) tc_commit(&B.drain[0]);   // TMEM is freed only after this warp's MMAs completed
         mbar_wait(&B.drain[0], 0, 500000000ull);
-    } else if (warp == kGradWarp) {
-        // ---------------- gradient issuer (whole warp): a second issuing warp, so
-        // the S / dP MMAs and these queue on the tensor pipe side by side
+    } else if (warp == 2) {
+        // ---------------- gradient issuer (whole warp)
         constexpr uint32_t idG = idesc_bf16(128, 64, false, true);
+        constexpr uint32_t idQ = idesc_bf16(128, L::DQN, true, true);
         int gt = 0;
         bool ok = true;
         for (int ci = 0; ok; ++ci) {
-            const int rb = ci & 1;
-            if (!cx.waitw(&B.res_full[rb], (ci >> 1) & 1)) { ok = false; break; }
-            const int it = B.item_of[rb];
-            if (lane == 0) mbar_arrive(&B.acc_free[rb]);   // the index is read
+            if (!cx.waitw(&B.res_full, ci & 1)) { ok = false; break; }
+            const int it = B.item_of;
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&B.idx_taken);
             if (it < 0) break;
             const int nq = p.plan.items[it].w;
             for (int t = 0; t < nq; ++t, ++gt) {
-                const int st = gt % NST, b = gt & 1;
+                const int st = gt % NST;
                 const uint32_t sb = smem_u32(smem + L::STAGE0 + st * L::STAGE);
-                // dV += P^T dO, dK += dS^T Q over the tile's 128 q rows: the even K steps
-                // (16-column chunks) as soon as every warp has written them, then the odd
-                for (int half = 0; half < 2; ++half) {
-                    if (!cx.waitw(half ? &B.p_full[b] : &B.p_half[b], (gt >> 1) & 1)) { ok = false; break; }
-                    // the first MMA of an item overwrites the accumulators: the previous
-                    // item's epilogue must have read them
-                    if (!half && t == 0 && ci >= 1 && !cx.waitw(&B.acc_free[(ci - 1) & 1], ((ci - 1) >> 1) & 1)) {
-                        ok = false;
-                        break;
-                    }
-                    tc_fence_after();
-                    if (lane == 0) {
+                // dV += P^T dO
+                if (!cx.waitw(&B.p_full, gt & 1)) { ok = false; break; }
+                // the first MMA of an item overwrites dV / dK: the previous item's epilogue must have read them
+                if (t == 0 && ci >= 1 && !cx.waitw(&B.acc_free, (ci - 1) & 1)) { ok = false; break; }
+                tc_fence_after();
+                if (lane == 0) {
 #pragma unroll
-                        for (int k2 = 0; k2 < 4; ++k2) {
-                            const int kk = 2 * k2 + half;
-                            const uint32_t acc = (t > 0 || kk > 0) ? 1u : 0u;
-                            mma_ts(tmem + ACC0, tmem + sbuf(b) + a_col(kk), mnmajor128_desc(sb + L::SDO + kk * 2048),
-                                   idG, acc);
-                            mma_ts(tmem + ACC1, tmem + sbuf(b) + a_col(kk) + 8, mnmajor128_desc(sb + L::SQ + kk * 2048),
-                                   idG, acc);
-                        }
-                        if (half) {
-                            tc_commit(&B.s_free[b]);
-                            tc_commit(&B.empty[st]);
-                        }
-                    }
-                    __syncwarp();
+                    for (int kk = 0; kk < 8; ++kk)
+                        mma_ts(tmem + DV, tmem + SB + pcol(kk), mnmajor128_desc(sb + L::SDO + kk * 2048), idG,
+                               (t > 0 || kk > 0) ? 1u : 0u);
+                    tc_commit(&B.pv_done);
                 }
-                if (!ok) break;
+                __syncwarp();
+                // dK += dS^T Q
+                if (!cx.waitw(&B.ds_ready, gt & 1)) { ok = false; break; }
+                tc_fence_after();
+                if (lane == 0) {
+#pragma unroll
+                    for (int kk = 0; kk < 8; ++kk)
+                        mma_ts(tmem + DK, tmem + DPB + pcol(kk), mnmajor128_desc(sb + L::SQ + kk * 2048), idG,
+                               (t > 0 || kk > 0) ? 1u : 0u);
+                    tc_commit(&B.dp_free);
+                }
+                __syncwarp();
+                // dQ (| aug-dim gradient) = dS [K | K_aug] once the drain warps took the previous tile's
+                if (gt >= 1 && !cx.waitw(&B.dq_free, (gt - 1) & 1)) { ok = false; break; }
+                tc_fence_after();
+                if (lane == 0) {
+#pragma unroll
+                    for (int kk = 0; kk < 8; ++kk)
+                        mma_ss(tmem + DQ, mnmajor128_desc(sDS + kk * 2048), mnmajor32_desc(sK + kk * 512), idQ,
+                               kk > 0 ? 1u : 0u);
+                    tc_commit(&B.dq_full);
+                    tc_commit(&B.empty[st]);
+                }
+                __syncwarp();
             }
             if (!ok) break;
-            if (lane == 0) tc_commit(&B.acc_done);   // every item, so the epilogue's phases stay in step
+            if (lane == 0) tc_commit(&B.acc_done);   // every item, so the phases stay in step
             __syncwarp();
         }
         if (!ok) cx.give_up();
         if (lane == 0) tc_commit(&B.drain[1]);
         mbar_wait(&B.drain[1], 0, 500000000ull);
-    } else {
-        // ---------------- elementwise: thread = kv row c, tile columns [32qc, 32qc+32) in two chunks of 16
+    } else if (warp < kElemWarp0) {
+        // warp 3: no role
+    } else if (warp < kDrainWarp0) {
+        // ---------------- elementwise: thread = kv row c, tile columns [32qc, 32qc+32)
         const int quad = warp & 3;
-        const int qc = (warp - 2) >> 2;
+        const int qc = (warp - kElemWarp0) >> 2;
         const int c = quad * 32 + lane;
         const uint32_t lb = (uint32_t)(quad * 32) << 16;
         const bool have_docs = p.docs != nullptr;
         const uint64_t c2 = f2_pack(p.scale_log2, p.scale_log2);
+        // this thread's row of the dS tile (MN-major, 128-byte swizzle): two 16-byte chunks per 16 columns
+        uint8_t *ds_row = smem + L::DS + (qc >> 1) * 16384 + c * 128;
+        const int ch0 = (qc & 1) * 4;                   // 16-byte chunk of column 32qc within its half
         int gt = 0;
         bool alive = true;
         for (int ci = 0; alive; ++ci) {
-            const int rb = ci & 1;
-            if (!cx.waitw(&B.res_full[rb], (ci >> 1) & 1)) { alive = false; break; }
-            const int it = B.item_of[rb];
+            if (!cx.waitw(&B.res_full, ci & 1)) { alive = false; break; }
+            const int it = B.item_of;
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&B.idx_taken);
             if (it < 0) break;
             const int4 item = p.plan.items[it];
             const int slot = p.plan.item_slot[it];
             const int h = item.x, kb = item.y, nq = item.w;
             const int j = kb * BM + c;
             const int doc_j = have_docs ? p.docs[j] : 0;
+            const float kpos_j = SLOPE ? __bfloat162float(__float2bfloat16_rn(__fmul_rn((float)j, p.s_aug))) : 0.f;
             for (int t = 0; t < nq; ++t, ++gt) {
-                const int st = gt % NST, b = gt & 1;
+                const int st = gt % NST;
                 if (!cx.waitw(&B.full[st], (gt / NST) & 1)) { alive = false; break; }
                 const int qb = B.stage_blk[st];
                 const int mk = B.stage_mk[st];
-                if (!cx.waitw(&B.s_full[b], (gt >> 1) & 1) || !cx.waitw(&B.dp_full, gt & 1)) { alive = false; break; }
-                tc_fence_after();
                 const uint8_t *sbp = smem + L::STAGE0 + st * L::STAGE;
-                uint32_t rs[16], rp0[16], rp1[16];
-                ld_tile_start(tmem + lb + sbuf(b) + qc * 32, tmem + lb + DPC + qc * 32, rs, rp0, rp1);
-                tc_fence_before();
-                mbar_arrive_warp(&B.dp_free);           // this warp's dP^T columns are in registers
+                const int i0 = qb * BM + qc * 32;
+                const int lim = j - i0;                  // column e visible iff e >= lim (causal: j <= i)
+                const float4 *LS = reinterpret_cast<const float4 *>(sbp + L::SLSE) + qc * 8;
+                const float4 *DL = reinterpret_cast<const float4 *>(sbp + L::SDEL) + qc * 8;
+                // S^T -> registers; P; P^T back over the warp's own (already read) columns:
+                // 16-column chunk cc at columns [32qc + 8cc, +8) as bf16 pairs
+                if (!cx.waitw(&B.s_full, gt & 1)) { alive = false; break; }
+                tc_fence_after();
+                float s[32];
+                {
+                    uint32_t r[32];
+                    tmem_ld32(tmem + lb + SB + qc * 32, r);
+                    tmem_wait_ld();
+                    pin(r);
 #pragma unroll
-                for (int cc = 0; cc < 2; ++cc) {
-                    const int col0 = qc * 32 + cc * 16;  // q row within the tile of the chunk's first column
-                    const uint32_t tc = tmem + lb + sbuf(b) + col0;
-                    if (cc == 1) ld_cols16(tc, rs);
-                    float s[16], dp[16];
+                    for (int e = 0; e < 32; ++e) s[e] = __uint_as_float(r[e]);
+                }
+                if (mk == MASK_FULL) {
+                    p_piece<false>(s, LS, c2, mk, lim, p.docs, i0, doc_j);
+                    p_piece<false>(s + 16, LS + 4, c2, mk, lim - 16, p.docs, i0 + 16, doc_j);
+                } else {
+                    p_piece<true>(s, LS, c2, mk, lim, p.docs, i0, doc_j);
+                    p_piece<true>(s + 16, LS + 4, c2, mk, lim - 16, p.docs, i0 + 16, doc_j);
+                }
+                {
+                    uint32_t w[16];
 #pragma unroll
-                    for (int e = 0; e < 16; ++e) {
-                        s[e] = __uint_as_float(rs[e]);
-                        dp[e] = __uint_as_float(cc ? rp1[e] : rp0[e]);
-                    }
-                    const float4 *LS = reinterpret_cast<const float4 *>(sbp + L::SLSE) + col0 / 4;
-                    const float4 *DL = reinterpret_cast<const float4 *>(sbp + L::SDEL) + col0 / 4;
-                    const int i0 = qb * BM + col0;
-                    const int lim = j - i0;              // column e visible iff e >= lim (causal: j <= i)
-                    if (mk == MASK_FULL) dkv_piece<false>(s, dp, LS, DL, c2, mk, lim, p.docs, i0, doc_j);
-                    else dkv_piece<true>(s, dp, LS, DL, c2, mk, lim, p.docs, i0, doc_j);
-                    st_bf16x16(tc, s);                   // P^T pairs, then dS^T pairs, over the chunk's own columns
-                    st_bf16x16(tc + 8, dp);
-                    if (cc == 0) {
-                        tmem_wait_st();
-                        tc_fence_before();
-                        mbar_arrive_warp(&B.p_half[b]);
-                    }
+                    for (int e = 0; e < 16; ++e) w[e] = pack_bf16(s[2 * e], s[2 * e + 1]);
+                    tmem_st16(tmem + lb + SB + qc * 32, w);
                 }
                 tmem_wait_st();
                 tc_fence_before();
-                mbar_arrive_warp(&B.p_full[b]);
+                // the gradient issuer consumed the previous tile's P^T (its dV MMAs completed)
+                // before this arrival starts the next phase
+                if (gt >= 1 && !cx.waitw(&B.pv_done, (gt - 1) & 1)) { alive = false; break; }
+                mbar_arrive_warp(&B.p_full);
+                // dP^T -> registers; dS = P (dP - delta); dS^T as bf16 pairs over the warp's
+                // first 16 dP^T columns and dS into the shared-memory tile
+                if (!cx.waitw(&B.dp_full, gt & 1)) { alive = false; break; }
+                tc_fence_after();
+                float d[32];
+                {
+                    uint32_t r[32];
+                    tmem_ld32(tmem + lb + DPB + qc * 32, r);
+                    tmem_wait_ld();
+                    pin(r);
+#pragma unroll
+                    for (int e = 0; e < 32; ++e) d[e] = __uint_as_float(r[e]);
+                }
+                ds_piece(s, d, DL);
+                ds_piece(s + 16, d + 16, DL + 4);
+                if constexpr (SLOPE) {
+                    // slope column of the aug-dim gradient in fp32 from the unrounded dS,
+                    // against positions relative to each query row: sum_j dS_ij = 0 in exact
+                    // arithmetic, so subtracting k_aug[i] changes nothing but the rounding,
+                    // which would otherwise amplify the small residual of that sum by ~i*s
+#pragma unroll
+                    for (int cc = 0; cc < 2; ++cc) {
+                        float v[16];
+#pragma unroll
+                        for (int e = 0; e < 16; ++e) {
+                            const float kpos_i =
+                                __bfloat162float(__float2bfloat16_rn(__fmul_rn((float)(i0 + 16 * cc + e), p.s_aug)));
+                            v[e] = d[16 * cc + e] * (kpos_j - kpos_i);
+                        }
+                        const float col = warp_column_sums16(v);
+                        if (lane < 16) atomicAdd(p.slope_acc + (int64_t)h * p.T + i0 + 16 * cc + lane, col);
+                    }
+                }
+                {
+                    uint32_t w[16];
+#pragma unroll
+                    for (int e = 0; e < 16; ++e) w[e] = pack_bf16(d[2 * e], d[2 * e + 1]);
+                    tmem_st16(tmem + lb + DPB + qc * 32, w);
+                    // the dS tile in shared memory is free once the previous tile's dQ MMAs completed
+                    if (gt >= 1 && !cx.waitw(&B.dq_full, (gt - 1) & 1)) { alive = false; break; }
+#pragma unroll
+                    for (int q4 = 0; q4 < 4; ++q4)
+                        *reinterpret_cast<uint4 *>(ds_row + (((ch0 + q4) ^ (c & 7)) << 4)) =
+                            make_uint4(w[4 * q4], w[4 * q4 + 1], w[4 * q4 + 2], w[4 * q4 + 3]);
+                }
+                tmem_wait_st();
+                fence_async_smem();
+                tc_fence_before();
+                mbar_arrive_warp(&B.ds_ready);
             }
             if (!alive) break;
-            // ---------------- epilogue of the item
+            // ---------------- epilogue of the item: dV, dK * scale
             if (!cx.waitw(&B.acc_done, ci & 1)) { alive = false; break; }
             tc_fence_after();
             const bool have = nq > 0;
-            // dV from ACC0 (quarters 0, 1), dK * scale from ACC1 (quarters 2, 3): 32 columns per warp
             const int half = qc >> 1, c32 = (qc & 1) * 32;
-            const uint32_t acc = tmem + lb + (half == 0 ? ACC0 : ACC1) + c32;
+            const uint32_t acc = tmem + lb + (half == 0 ? DV : DK) + c32;
             const float mul = half == 0 ? 1.f : p.scale;
-            __nv_bfloat16 *dst = (half == 0 ? p.g1 + (int64_t)h * p.g1_sh + (int64_t)j * p.g1_st
-                                            : p.g0 + (int64_t)h * p.g0_sh + (int64_t)j * p.g0_st) + c32;
+            __nv_bfloat16 *dst = (half == 0 ? p.dv + (int64_t)h * p.dv_sh + (int64_t)j * p.dv_st
+                                            : p.dk + (int64_t)h * p.dk_sh + (int64_t)j * p.dk_st) + c32;
             if (slot < 0) {
                 store_row<32>(acc, mul, dst, have);
             } else {
@@ -651,7 +710,7 @@ __global__ void __launch_bounds__(kThreads, 1) dkv_kernel(const __grid_constant_
                 }
                 __threadfence();
                 elem_bar();
-                if (threadIdx.x == 64) {
+                if (threadIdx.x == 32 * kElemWarp0) {
                     const int done = atomicAdd(p.plan.slot_done + slot, 1);
                     B.last_flag = (done == p.plan.slot_chunks[slot] - 1) ? 1 : 0;
                 }
@@ -663,14 +722,73 @@ __global__ void __launch_bounds__(kThreads, 1) dkv_kernel(const __grid_constant_
                     uint32_t w[16];
 #pragma unroll
                     for (int e = 0; e < 16; ++e) w[e] = pack_bf16(__ldcg(part + 2 * e), __ldcg(part + 2 * e + 1));
-                    uint4 *d = reinterpret_cast<uint4 *>(dst);
+                    uint4 *dd = reinterpret_cast<uint4 *>(dst);
 #pragma unroll
-                    for (int e = 0; e < 4; ++e) d[e] = make_uint4(w[4 * e], w[4 * e + 1], w[4 * e + 2], w[4 * e + 3]);
+                    for (int e = 0; e < 4; ++e) dd[e] = make_uint4(w[4 * e], w[4 * e + 1], w[4 * e + 2], w[4 * e + 3]);
                 }
             }
             tc_fence_before();
-            mbar_arrive_warp(&B.acc_free[rb]);   // accumulators read, resident buffer rb released
+            mbar_arrive_warp(&B.acc_free);   // dV / dK read
         }
+    } else {
+        // ---------------- dQ drain: the 32 q rows of this warp's lane quadrant, DQN fp32 columns
+        // each, added into the accumulator 16 columns at a time: TMEM -> registers (a row per
+        // thread) -> a 32 x 16 box in shared memory (64-byte swizzle, so the row-per-lane
+        // stores are conflict free) -> one TMA tensor reduce-add of the box.  The warp's
+        // boxes rotate; a box is rewritten once the reduce that read it is done reading.
+        // The q blocks come from the same bitmap walk the producer makes.
+        const int quad = warp & 3;
+        const uint32_t lb = (uint32_t)(quad * 32) << 16;
+        constexpr int DQN = L::DQN;
+        uint8_t *stg = smem + L::DRN + (warp - kDrainWarp0) * (kDrainBoxes * 2048);
+        int issued = 0;                                  // reduces issued by lane 0 (bulk groups)
+        int gt = 0;
+        bool alive = true;
+        for (int ci = 0; alive; ++ci) {
+            if (!cx.waitw(&B.res_full, ci & 1)) { alive = false; break; }
+            const int it = B.item_of;
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&B.idx_taken);
+            if (it < 0) break;
+            const int4 item = p.plan.items[it];
+            const int h = item.x, kb = item.y, first = item.z, nq = item.w;
+            const uint32_t *brow = p.q_bitmap + ((int64_t)h * p.QB + kb) * p.words;
+            int w;
+            uint32_t bits;
+            seek_rank(brow, p.words, first, w, bits);
+            for (int t = 0; t < nq; ++t, ++gt) {
+                const int qb = next_bit(brow, p.words, w, bits);
+                if (!cx.waitw(&B.dq_full, gt & 1)) { alive = false; break; }
+                tc_fence_after();
+                const int row0 = (int)((int64_t)h * p.T + (int64_t)qb * BM + quad * 32);
+#pragma unroll
+                for (int c0 = 0; c0 < DQN; c0 += 16) {
+                    uint8_t *box = stg + (issued % kDrainBoxes) * 2048;
+                    if (lane == 0 && issued >= kDrainBoxes) bulk_wait_group_read<kDrainBoxes - 1>();   // this box's previous reduce
+                    __syncwarp();
+                    uint32_t o[16];
+                    tmem_ld16(tmem + lb + DQ + c0, o);
+                    tmem_wait_ld();
+                    pin(o);
+                    if (c0 + 16 >= DQN) {
+                        tc_fence_before();
+                        mbar_arrive_warp(&B.dq_free);   // the accumulator is in registers
+                    }
+#pragma unroll
+                    for (int e = 0; e < 4; ++e)
+                        *reinterpret_cast<uint4 *>(box + lane * 64 + ((e ^ ((lane >> 1) & 3)) << 4)) =
+                            make_uint4(o[4 * e], o[4 * e + 1], o[4 * e + 2], o[4 * e + 3]);
+                    fence_async_smem();
+                    __syncwarp();
+                    if (lane == 0 && qb >= 0) {
+                        tma_reduce_add_2d(&maps.dqa, box, c0, row0);
+                        bulk_commit_group();
+                    }
+                    ++issued;
+                }
+            }
+        }
+        if (lane == 0) bulk_wait_group_all();            // every reduce completed before the CTA exits
     }
     __syncwarp();   // every warp reaches the CTA barrier converged (the producer ran on lane 0 alone)
     tc_fence_before();
@@ -770,418 +888,63 @@ __global__ void __launch_bounds__(1024) plan_items_kernel(const int32_t *__restr
     if (threadIdx.x == 0) *n_items = tot_s + tot_u;
 }
 
-// ============================================================================ dQ
-// Persistent: one CTA per SM walks the work items (head, q block): its block
-// index first, then the next unclaimed one from an atomic counter (kv lists
-// run from 1 to ~80 tiles), so that the next item's resident tiles load and
-// its first tiles run while the previous item's epilogue drains.  Resident per item
-// (two buffers, item ci in buffer ci & 1): Q, the q_aug dims, dO and the item's
-// rows of the cos / sin tables.  Streamed per kv tile (ring of NST stages, one
-// tile counter across items): K, the k_aug dims, V.
-template <int DA>
-struct QL {
-    static constexpr int NA = DA / 16;
-    static constexpr int KM = DA > 0 ? DA / 2 : 1;                 // coefficients per row, K <= DA / 2
-    static constexpr int KM4 = (KM + 3) / 4;                        // per elementwise warp of a quadrant
-    static constexpr uint32_t TILE = BM * HD * 2, ATILE = BM * 16 * 2;
-    static constexpr uint32_t Q = 0, QA = TILE, DO = align1k(TILE + NA * ATILE);
-    static constexpr uint32_t TAB = DO + TILE;                       // bf16 [2][KM][128]: cos rows, sin rows
-    static constexpr uint32_t RESB = align1k(TAB + (NA > 0 ? KM * 512 : 0));
-    static constexpr uint32_t STAGE0 = 2 * RESB;
-    static constexpr uint32_t SK = 0, SKA = TILE, SV = align1k(TILE + NA * ATILE);
-    static constexpr uint32_t STAGE = SV + TILE;
-    static constexpr uint32_t EXTRA = 1024 + 1024;                  // barriers, base alignment
-    static constexpr int NST = STAGE0 + 4 * STAGE + EXTRA <= kSmemBudget
-                                   ? 4
-                                   : (STAGE0 + 3 * STAGE + EXTRA <= kSmemBudget ? 3 : 2);
-    static constexpr uint32_t BAR = STAGE0 + NST * STAGE;
-    static constexpr uint32_t TOTAL = BAR + sizeof(Bars);
-    static constexpr uint32_t RES_BYTES = 2 * TILE + NA * ATILE;
-    static constexpr uint32_t KV_BYTES = 2 * TILE + NA * ATILE;
-    static_assert(TOTAL + 1024 <= kSmemBudget, "shared memory");
+// ============================================================================ finish
+// One warp per (head, row): dq = bf16(scale * acc[0:64]); the aug-dim gradient
+// g = scale * acc[64:] -> dcoeff_cos[k] = s (g_k cos_ik + g_{K+k} sin_ik),
+// dcoeff_sin[k] = s (g_k sin_ik - g_{K+k} cos_ik) (q_aug = s [A c + B s', A s' - B c, -slope]),
+// dslope = -s * scale * (the fp32 slope sums).
+struct FinishParams {
+    const float *acc;
+    int ld, H, T, K, tab_len;
+    float scale, s_aug;
+    __nv_bfloat16 *dq;
+    int64_t dq_sh, dq_st;
+    const uint16_t *cos_tab, *sin_tab;
+    float *dcoeff_cos, *dcoeff_sin;
+    const float *slope_acc;
+    float *dslope;
 };
 
-template <int DA>
-__global__ void __launch_bounds__(kThreads, 1) dq_kernel(const __grid_constant__ Maps maps, const Params p) {
-    using L = QL<DA>;
-    constexpr int NA = L::NA, NST = L::NST, KM = L::KM, KM4 = L::KM4;
-    extern __shared__ uint8_t smem_raw[];
-    uint8_t *smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
-    Bars &B = *reinterpret_cast<Bars *>(smem + L::BAR);
-    Ctx cx{&B.abort_flag, p.err};
-
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int n_items = p.H * p.QB, G = gridDim.x;
-    const bool tab = NA > 0 && p.dcoeff_cos && p.tab_smem;
-
-    // acc_free of a resident buffer: the elementwise threads after the item's epilogue,
-    // and each issuing warp once it has read the item's index
-    if (threadIdx.x == 0) B.init(NST, kElem + 2);
-    if (warp == 1) {
-        tmem_alloc(&B.tmem_slot, kTmemCols);
-        tmem_relinquish();
-    }
-    __syncwarp();   // every warp reaches the CTA barrier converged (the producer ran on lane 0 alone)
-    tc_fence_before();
-    __syncthreads();
-    tc_fence_after();
-    const uint32_t tmem = B.tmem_slot;
-
-    if (warp == 0) {
-        // ---------------- producer: per item the resident tiles, then its kv tiles in list order
-        if (lane == 0) {
-            int gt = 0, last_res = -1;
-            bool ok = true;
-            for (int ci = 0; ok; ++ci) {
-                // the first item of each CTA is its block index, the rest are handed out in order
-                const int it = ci == 0 ? (int)blockIdx.x : G + atomicAdd(p.plan.next_item + 1, 1);
-                const int rb = ci & 1;
-                uint8_t *res = smem + rb * L::RESB;
-                // buffer rb is free once every role is done with item ci - 2
-                if (ci >= 2 && !cx.wait1(&B.acc_free[rb], ((ci >> 1) - 1) & 1)) break;
-                if (last_res == ci - 2) last_res = -1;   // its tiles were consumed, so they landed
-                B.item_of[rb] = it < n_items ? it : -1;
-                if (it >= n_items) {
-                    mbar_arrive(&B.res_full[rb]);      // publishes "no item left"
-                    break;
-                }
-                const int h = it / p.QB, qb = it - h * p.QB;
-                const int64_t mrow = (int64_t)h * p.QB + qb;
-                const int n = p.kv_num[mrow];
-                const int32_t *list = p.kv_idx + mrow * p.kv_stride;
-                if (n > 0) {
-                    mbar_expect_tx(&B.res_full[rb], L::RES_BYTES + (tab ? 2u * p.K * 256u : 0u));
-                    if (tab) {
-                        for (int k = 0; k < p.K; ++k) {
-                            bulk_load(res + L::TAB + k * 256, p.cos_tab + (int64_t)k * p.tab_len + qb * BM, 256,
-                                      &B.res_full[rb]);
-                            bulk_load(res + L::TAB + (KM + k) * 256, p.sin_tab + (int64_t)k * p.tab_len + qb * BM, 256,
-                                      &B.res_full[rb]);
-                        }
-                    }
-                    tma_load_3d(&maps.q, res + L::Q, &B.res_full[rb], 0, qb * BM, h);
-#pragma unroll
-                    for (int a = 0; a < NA; ++a)
-                        tma_load_3d(&maps.qa, res + L::QA + a * L::ATILE, &B.res_full[rb], 16 * a, qb * BM, h);
-                    tma_load_3d(&maps.dout, res + L::DO, &B.res_full[rb], 0, qb * BM, h);
-                    last_res = ci;
-                } else {
-                    mbar_arrive(&B.res_full[rb]);      // keeps the buffer's phases in step
-                }
-                for (int jj = 0; jj < n; ++jj, ++gt) {
-                    const int st = gt % NST;
-                    if (gt >= NST && !cx.wait1(&B.empty[st], ((gt / NST) - 1) & 1)) { ok = false; break; }
-                    int kb = list[jj];
-                    B.stage_blk[st] = kb;
-                    const bool bad = kb < 0 || kb >= p.QB;
-                    B.stage_mk[st] = bad ? MASK_DOCS : tile_mask_kind(qb, kb, p.docs != nullptr, p.block_info, p.QB);
-                    if (bad) kb = 0;   // masked by the elementwise warps
-                    uint8_t *sb = smem + L::STAGE0 + st * L::STAGE;
-                    mbar_expect_tx(&B.full[st], L::KV_BYTES);
-                    tma_load_3d(&maps.k, sb + L::SK, &B.full[st], 0, kb * BM, h);
-#pragma unroll
-                    for (int a = 0; a < NA; ++a)
-                        tma_load_2d(&maps.ka, sb + L::SKA + a * L::ATILE, &B.full[st], 16 * a, kb * BM);
-                    tma_load_3d(&maps.v, sb + L::SV, &B.full[st], 0, kb * BM, h);
-                }
-            }
-            // never leave the CTA with a TMA write still in flight
-            if (last_res >= 0) mbar_wait(&B.res_full[last_res & 1], (last_res >> 1) & 1, 500000000ull);
-            for (int j = (gt > NST ? gt - NST : 0); j < gt; ++j) mbar_wait(&B.full[j % NST], (j / NST) & 1, 500000000ull);
-        }
-    } else if (warp == 1) {
-        // ---------------- S / dP issuer (the whole warp waits, lane 0 issues)
-        constexpr uint32_t idS = idesc_bf16(128, 128, false, false);
-        int gt = 0;
-        bool ok = true;
-        for (int ci = 0; ok; ++ci) {
-            const int rb = ci & 1;
-            if (!cx.waitw(&B.res_full[rb], (ci >> 1) & 1)) { ok = false; break; }
-            const int it = B.item_of[rb];
-            if (lane == 0) mbar_arrive(&B.acc_free[rb]);   // the index is read
-            if (it < 0) break;
-            const int h = it / p.QB, qb = it - h * p.QB;
-            const int n = p.kv_num[(int64_t)h * p.QB + qb];
-            if (n == 0) continue;
-            const uint32_t res = smem_u32(smem + rb * L::RESB);
-            const uint32_t sQ = res + L::Q, sQA = res + L::QA, sDO = res + L::DO;
-            for (int jj = 0; jj < n; ++jj, ++gt) {
-                const int st = gt % NST, b = gt & 1;
-                if (!cx.waitw(&B.full[st], (gt / NST) & 1)) { ok = false; break; }
-                const uint32_t sb = smem_u32(smem + L::STAGE0 + st * L::STAGE);
-                // dP = dO V^T first: the elementwise warps release dP of the previous tile as
-                // they start it, while S waits for the gradient MMAs of tile gt-2
-                if (gt >= 1 && !cx.waitw(&B.dp_free, (gt - 1) & 1)) { ok = false; break; }
-                tc_fence_after();
-                if (lane == 0) {
-#pragma unroll
-                    for (int kk = 0; kk < 4; ++kk)
-                        mma_ss(tmem + DPC, kmajor_desc(sDO + kk * 32, 128), kmajor_desc(sb + L::SV + kk * 32, 128), idS,
-                               kk > 0);
-                    tc_commit(&B.dp_full);
-                }
-                __syncwarp();
-                // S = Q K^T (+ Qaug Kaug^T): 128 q rows x 128 kv columns
-                if (gt >= 2 && !cx.waitw(&B.s_free[b], ((gt >> 1) - 1) & 1)) { ok = false; break; }
-                tc_fence_after();
-                if (lane == 0) {
-#pragma unroll
-                    for (int kk = 0; kk < 4; ++kk)
-                        mma_ss(tmem + sbuf(b), kmajor_desc(sQ + kk * 32, 128), kmajor_desc(sb + L::SK + kk * 32, 128),
-                               idS, kk > 0);
-#pragma unroll
-                    for (int a = 0; a < NA; ++a)
-                        mma_ss(tmem + sbuf(b), kmajor_desc(sQA + a * L::ATILE, 32),
-                               kmajor_desc(sb + L::SKA + a * L::ATILE, 32), idS, 1);
-                    tc_commit(&B.s_full[b]);
-                }
-                __syncwarp();
-            }
-        }
-        if (!ok) cx.give_up();
-        if (lane == 0) tc_commit(&B.drain[0]);   // TMEM is freed only after this warp's MMAs completed
-        mbar_wait(&B.drain[0], 0, 500000000ull);
-    } else if (warp == kGradWarp) {
-        // ---------------- gradient issuer (whole warp): a second issuing warp, so
-        // the S / dP MMAs and these queue on the tensor pipe side by side
-        constexpr uint32_t idG = idesc_bf16(128, 64, false, true);
-        // the DA/16 aug sub-tiles (16 columns, 32-byte swizzle) lie 4 KiB apart:
-        // one MN-major operand of N = DA whose atoms the descriptor's
-        // leading byte offset (4 KiB) steps through
-        constexpr uint32_t idA = idesc_bf16(128, DA > 0 ? DA : 16, false, true);
-        int gt = 0;
-        bool ok = true;
-        for (int ci = 0; ok; ++ci) {
-            const int rb = ci & 1;
-            if (!cx.waitw(&B.res_full[rb], (ci >> 1) & 1)) { ok = false; break; }
-            const int it = B.item_of[rb];
-            if (lane == 0) mbar_arrive(&B.acc_free[rb]);   // the index is read
-            if (it < 0) break;
-            const int h = it / p.QB, qb = it - h * p.QB;
-            const int n = p.kv_num[(int64_t)h * p.QB + qb];
-            for (int jj = 0; jj < n; ++jj, ++gt) {
-                const int st = gt % NST, b = gt & 1;
-                const uint32_t sb = smem_u32(smem + L::STAGE0 + st * L::STAGE);
-                // dQ += dS K (+ dQaug += dS Kaug) over the tile's 128 kv rows: the even K
-                // steps as soon as every warp has written them, then the odd
-                for (int half = 0; half < 2; ++half) {
-                    if (!cx.waitw(half ? &B.p_full[b] : &B.p_half[b], (gt >> 1) & 1)) { ok = false; break; }
-                    // the first MMA of an item overwrites the accumulators: the previous
-                    // item's epilogue must have read them
-                    if (!half && jj == 0 && ci >= 1 && !cx.waitw(&B.acc_free[(ci - 1) & 1], ((ci - 1) >> 1) & 1)) {
-                        ok = false;
-                        break;
-                    }
-                    tc_fence_after();
-                    if (lane == 0) {
-#pragma unroll
-                        for (int k2 = 0; k2 < 4; ++k2) {
-                            const int kk = 2 * k2 + half;
-                            const uint32_t acc = (jj > 0 || kk > 0) ? 1u : 0u;
-                            mma_ts(tmem + ACC0, tmem + sbuf(b) + a_col(kk), mnmajor128_desc(sb + L::SK + kk * 2048),
-                                   idG, acc);
-                            if (NA > 0)
-                                mma_ts(tmem + ACC1, tmem + sbuf(b) + a_col(kk), mnmajor32_desc(sb + L::SKA + kk * 512),
-                                       idA, acc);
-                        }
-                        if (half) {
-                            tc_commit(&B.s_free[b]);
-                            tc_commit(&B.empty[st]);
-                        }
-                    }
-                    __syncwarp();
-                }
-                if (!ok) break;
-            }
-            if (!ok) break;
-            if (lane == 0) tc_commit(&B.acc_done);   // every item, so the epilogue's phases stay in step
-            __syncwarp();
-        }
-        if (!ok) cx.give_up();
-        if (lane == 0) tc_commit(&B.drain[1]);
-        mbar_wait(&B.drain[1], 0, 500000000ull);
-    } else {
-        // ---------------- elementwise: thread = q row i, tile columns [32qc, 32qc+32) in two chunks of 16
-        const int quad = warp & 3;
-        const int qc = (warp - 2) >> 2;
-        const int r = quad * 32 + lane;
-        const uint32_t lb = (uint32_t)(quad * 32) << 16;
-        const bool have_docs = p.docs != nullptr;
-        const bool slope_acc = NA > 0 && p.has_slope && p.dslope;
-        const uint64_t c2 = f2_pack(p.scale_log2, p.scale_log2);
-        int gt = 0;
-        bool alive = true;
-        for (int ci = 0; alive; ++ci) {
-            const int rb = ci & 1;
-            if (!cx.waitw(&B.res_full[rb], (ci >> 1) & 1)) { alive = false; break; }
-            const int it = B.item_of[rb];
-            if (it < 0) break;
-            const int h = it / p.QB, qb = it - h * p.QB;
-            const int n = p.kv_num[(int64_t)h * p.QB + qb];
-            uint8_t *res = smem + rb * L::RESB;
-            const int i = qb * BM + r;
-            const int doc_i = have_docs ? p.docs[i] : 0;
-            const int64_t hrow = (int64_t)h * p.T + i;
-            const float l2 = p.lse2[hrow], dl = p.delta[hrow];
-            const uint64_t nl2 = f2_pack(-l2, -l2), nd2 = f2_pack(-dl, -dl);
-            // The slope column of k_aug holds positions * s (up to ~T*s).  Its dS sum
-            // is accumulated here in fp32 from the unrounded dS, against positions
-            // relative to this query row: sum_j dS_ij = 0 in exact arithmetic, so
-            // subtracting k_aug[i] changes nothing but the rounding, which would
-            // otherwise amplify the small residual of that sum by ~i*s.
-            const float kpos_i = __bfloat162float(__float2bfloat16_rn(__fmul_rn((float)i, p.s_aug)));
-            float gsl = 0.f;
-            for (int jj = 0; jj < n; ++jj, ++gt) {
-                const int st = gt % NST, b = gt & 1;
-                if (!cx.waitw(&B.full[st], (gt / NST) & 1)) { alive = false; break; }
-                const int kb = B.stage_blk[st];
-                const bool bad = kb < 0 || kb >= p.QB;
-                const int mk = B.stage_mk[st];
-                if (!cx.waitw(&B.s_full[b], (gt >> 1) & 1) || !cx.waitw(&B.dp_full, gt & 1)) { alive = false; break; }
-                tc_fence_after();
-                uint32_t rs[16], rp0[16], rp1[16];
-                ld_tile_start(tmem + lb + sbuf(b) + qc * 32, tmem + lb + DPC + qc * 32, rs, rp0, rp1);
-                tc_fence_before();
-                mbar_arrive_warp(&B.dp_free);       // this warp's dP columns are in registers
-#pragma unroll
-                for (int cc = 0; cc < 2; ++cc) {
-                    const int col0 = qc * 32 + cc * 16;
-                    const uint32_t tc = tmem + lb + sbuf(b) + col0;
-                    if (cc == 1) ld_cols16(tc, rs);
-                    float s[16], dp[16];
-#pragma unroll
-                    for (int e = 0; e < 16; ++e) {
-                        s[e] = __uint_as_float(rs[e]);
-                        dp[e] = __uint_as_float(cc ? rp1[e] : rp0[e]);
-                    }
-                    const int j0 = kb * BM + col0;
-                    const int lim = i - j0;              // column e visible iff e <= lim (causal: j <= i)
-                    if (mk == MASK_FULL) dq_piece<false>(s, dp, c2, nl2, nd2, mk, lim, bad, p.docs, j0, doc_i);
-                    else dq_piece<true>(s, dp, c2, nl2, nd2, mk, lim, bad, p.docs, j0, doc_i);
-                    if (slope_acc && !bad) {
-#pragma unroll
-                        for (int e = 0; e < 16; ++e) {
-                            // the value scope_qk_aug_prepare stored: bf16(fp32(j) * s)
-                            const float kpos =
-                                __bfloat162float(__float2bfloat16_rn(__fmul_rn((float)(j0 + e), p.s_aug)));
-                            gsl = fmaf(s[e], kpos - kpos_i, gsl);
-                        }
-                    }
-                    st_bf16x16(tc, s);                   // dS pairs over the chunk's own columns
-                    if (cc == 0) {
-                        tmem_wait_st();
-                        tc_fence_before();
-                        mbar_arrive_warp(&B.p_half[b]);
-                    }
-                }
-                tmem_wait_st();
-                tc_fence_before();
-                mbar_arrive_warp(&B.p_full[b]);
-            }
-            if (!alive) break;
-            // ---------------- epilogue of the item
-            if (!cx.waitw(&B.acc_done, ci & 1)) { alive = false; break; }
-            tc_fence_after();
-            const bool have = n > 0;
-            // dQ: each of the quadrant's four warps stores 16 of the 64 columns
-            store_row<16>(tmem + lb + ACC0 + qc * 16, p.scale,
-                          p.g0 + (int64_t)h * p.g0_sh + (int64_t)i * p.g0_st + qc * 16, have);
-            if (NA > 0 && p.dcoeff_cos) {
-                // gradient of the augmented dims -> coefficients (q_aug = s [A c + B s', A s' - B c, -slope]);
-                // the four warps of a quadrant split the K coefficients, reading the two
-                // accumulator columns (k, K + k) of each coefficient k directly
-                const int K = p.K;
-                const int kq = (K + 3) >> 2;
-                const int k0 = qc * kq, nk = max(0, min(kq, K - k0));
-                float cv[KM4], sv[KM4], g0[KM4], g1[KM4];
-                {
-                    uint32_t o0[KM4], o1[KM4];
-#pragma unroll
-                    for (int e = 0; e < KM4; ++e) {
-                        o0[e] = o1[e] = 0u;
-                        if (have && e < nk) {
-                            tmem_ld1(tmem + lb + ACC1 + k0 + e, o0[e]);
-                            tmem_ld1(tmem + lb + ACC1 + K + k0 + e, o1[e]);
-                        }
-                    }
-                    tmem_wait_ld();
-                    pin(o0);
-                    pin(o1);
-#pragma unroll
-                    for (int e = 0; e < KM4; ++e) {
-                        g0[e] = __uint_as_float(o0[e]) * p.scale;
-                        g1[e] = __uint_as_float(o1[e]) * p.scale;
-                    }
-                }
-                if (tab && have) {
-                    // the producer staged this item's table rows with its resident tiles
-                    const bool ok = cx.waitw(&B.res_full[rb], (ci >> 1) & 1);
-                    const uint16_t *tc = reinterpret_cast<const uint16_t *>(res + L::TAB);
-#pragma unroll
-                    for (int e = 0; e < KM4; ++e) {
-                        if (e < nk) {
-                            cv[e] = ok ? bf16_to_f32(tc[(k0 + e) * BM + r]) : 0.f;
-                            sv[e] = ok ? bf16_to_f32(tc[(KM + k0 + e) * BM + r]) : 0.f;
-                        }
-                    }
-                } else {
-#pragma unroll
-                    for (int e = 0; e < KM4; ++e) {          // independent table loads, issued together
-                        if (e < nk) {
-                            cv[e] = bf16_to_f32(p.cos_tab[(int64_t)(k0 + e) * p.tab_len + i]);
-                            sv[e] = bf16_to_f32(p.sin_tab[(int64_t)(k0 + e) * p.tab_len + i]);
-                        }
-                    }
-                }
-                float *oc = p.dcoeff_cos + hrow * K + k0, *os = p.dcoeff_sin + hrow * K + k0;
-#pragma unroll
-                for (int e = 0; e < KM4; ++e) {
-                    if (e < nk) {
-                        oc[e] = p.s_aug * (g0[e] * cv[e] + g1[e] * sv[e]);
-                        os[e] = p.s_aug * (g0[e] * sv[e] - g1[e] * cv[e]);
-                    }
-                }
-                if (slope_acc) {
-                    // the quadrant's four partial sums meet in shared memory, in the item's Q
-                    // tile (idle once its MMAs completed, ours until acc_free); the second
-                    // barrier keeps every read before the buffer is released
-                    float *slope_part = reinterpret_cast<float *>(res + L::Q);
-                    if (qc > 0) slope_part[(qc - 1) * BM + r] = gsl;
-                    elem_bar();
-                    if (qc == 0)
-                        p.dslope[hrow] =
-                            -p.s_aug * ((gsl + slope_part[r] + slope_part[BM + r] + slope_part[2 * BM + r]) * p.scale);
-                    elem_bar();
-                }
-            }
-            tc_fence_before();
-            mbar_arrive_warp(&B.acc_free[rb]);   // accumulators read, resident buffer rb released
+__global__ void finish_kernel(const FinishParams f) {
+    const int64_t row = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    const int lane = threadIdx.x & 31;
+    if (row >= (int64_t)f.H * f.T) return;
+    const int h = (int)(row / f.T), i = (int)(row % f.T);
+    const float *a = f.acc + row * f.ld;
+    if (lane < 16) {
+        const float4 v = *reinterpret_cast<const float4 *>(a + 4 * lane);
+        uint2 o = make_uint2(pack_bf16(v.x * f.scale, v.y * f.scale), pack_bf16(v.z * f.scale, v.w * f.scale));
+        *reinterpret_cast<uint2 *>(f.dq + h * f.dq_sh + (int64_t)i * f.dq_st + 4 * lane) = o;
+    } else if (f.dcoeff_cos) {
+        for (int k = lane - 16; k < f.K; k += 16) {
+            const float g0 = a[64 + k] * f.scale, g1 = a[64 + f.K + k] * f.scale;
+            const float cv = bf16_to_f32(f.cos_tab[(int64_t)k * f.tab_len + i]);
+            const float sv = bf16_to_f32(f.sin_tab[(int64_t)k * f.tab_len + i]);
+            f.dcoeff_cos[row * f.K + k] = f.s_aug * (g0 * cv + g1 * sv);
+            f.dcoeff_sin[row * f.K + k] = f.s_aug * (g0 * sv - g1 * cv);
         }
     }
-    __syncwarp();   // every warp reaches the CTA barrier converged (the producer ran on lane 0 alone)
-    tc_fence_before();
-    __syncthreads();
-    if (warp == 1) {
-        tc_fence_after();
-        tmem_dealloc(tmem, kTmemCols);
-    }
+    if (lane == 0 && f.dslope) f.dslope[row] = -f.s_aug * (f.slope_acc[row] * f.scale);
 }
 
 }  // namespace tcbwd
 
 namespace tchost {
 
-// Workspace of the backward: delta, lse*log2(e), and the dK/dV work plan.
+// Workspace of the backward: delta, lse*log2(e), the work plan, the dK/dV
+// slot partials, the fp32 dQ accumulator [H, T, 64 + DA] and the fp32 slope
+// sums [H, T].
 struct BwdWorkspace {
-    size_t delta, lse2, nq, items, item_slot, n_items, slot_chunks, slot_done, partial, total;
-    int max_items;
+    size_t delta, lse2, nq, items, item_slot, n_items, slot_chunks, slot_done, partial, dq_acc, slope_acc, total;
+    int max_items, dq_ld;
 };
 
-BwdWorkspace bwd_workspace(int H, int T, int block_size) {
+BwdWorkspace bwd_workspace(int H, int T, int block_size, int d_aug) {
     auto up = [](size_t x) { return (x + 255) & ~(size_t)255; };
     BwdWorkspace w;
     const int QB = T / block_size;
     w.max_items = H * QB + tcbwd::kSlotCap * ((QB + tcbwd::kChunk - 1) / tcbwd::kChunk);
+    w.dq_ld = 64 + d_aug;
     size_t o = 0;
     w.delta = o;       o += up((size_t)H * T * 4);
     w.lse2 = o;        o += up((size_t)H * T * 4);
@@ -1192,24 +955,28 @@ BwdWorkspace bwd_workspace(int H, int T, int block_size) {
     w.slot_chunks = o; o += up((size_t)tcbwd::kSlotCap * 4);
     w.slot_done = o;   o += up((size_t)tcbwd::kSlotCap * 4);
     w.partial = o;     o += up((size_t)tcbwd::kSlotCap * 128 * 128 * 4);
+    w.dq_acc = o;      o += up((size_t)H * T * w.dq_ld * 4);
+    w.slope_acc = o;   o += up((size_t)H * T * 4);
     w.total = o;
     return w;
 }
 
-template <int DA>
+template <int DA, bool SLOPE>
 int launch_bwd(const ScopeAttnArgs &a, cudaStream_t s) {
     const int QB = a.T / 128;
-    const BwdWorkspace ws = bwd_workspace(a.H, a.T, 128);
+    const BwdWorkspace ws = bwd_workspace(a.H, a.T, 128, DA);
     uint8_t *base = reinterpret_cast<uint8_t *>(a.workspace);
     float *delta = reinterpret_cast<float *>(base + ws.delta);
     float *lse2 = reinterpret_cast<float *>(base + ws.lse2);
+    float *dq_acc = reinterpret_cast<float *>(base + ws.dq_acc);
+    float *slope_acc = reinterpret_cast<float *>(base + ws.slope_acc);
     const int64_t rows = (int64_t)a.H * a.T;
     tcbwd::prep_kernel<<<(unsigned)((rows + 255) / 256), 256, 0, s>>>(
         reinterpret_cast<const __nv_bfloat16 *>(a.out), a.o_sh, a.o_st, reinterpret_cast<const __nv_bfloat16 *>(a.dout),
         a.do_sh, a.do_st, a.lse, a.H, a.T, delta, lse2);
     SCOPE_CHECK_LAUNCH();
 
-    // dK/dV work plan: long q lists are cut into chunks
+    // work plan: long q lists are cut into chunks
     tcbwd::Plan plan;
     int32_t *nq = reinterpret_cast<int32_t *>(base + ws.nq);
     int4 *items = reinterpret_cast<int4 *>(base + ws.items);
@@ -1230,15 +997,18 @@ int launch_bwd(const ScopeAttnArgs &a, cudaStream_t s) {
     SCOPE_CHECK_LAUNCH();
     if (cudaMemsetAsync(plan.partial, 0, (size_t)tcbwd::kSlotCap * 128 * 128 * 4, s) != cudaSuccess)
         return SCOPE_ERR_CUDA;
+    // the dQ accumulator and the slope sums start at zero (adjacent in the workspace)
+    if (cudaMemsetAsync(dq_acc, 0, ws.total - ws.dq_acc, s) != cudaSuccess) return SCOPE_ERR_CUDA;
 
     tcbwd::Maps maps;
     std::memset(&maps, 0, sizeof(maps));
     bool ok = map3d(&maps.q, a.q, 64, a.T, a.H, a.q_st, a.q_sh, 64) &&
-              map3d(&maps.k, a.k, 64, a.T, a.H, a.k_st, a.k_sh, 64) &&
+              map3d(&maps.k16, a.k, 64, a.T, a.H, a.k_st, a.k_sh, 16) &&
               map3d(&maps.v, a.v, 64, a.T, a.H, a.v_st, a.v_sh, 64) &&
               map3d(&maps.dout, a.dout, 64, a.T, a.H, a.do_st, a.do_sh, 64);
     if (DA) ok = ok && map3d(&maps.qa, a.q_aug, DA, a.T, a.H, DA, (int64_t)a.T * DA, 16) &&
                  map2d(&maps.ka, a.k_aug, DA, a.T, 16);
+    ok = ok && map2d_f32_sw64(&maps.dqa, dq_acc, ws.dq_ld, (int64_t)a.H * a.T, 32);
     if (!ok) return SCOPE_ERR_ALIGN;
 
     tcbwd::Params p;
@@ -1247,64 +1017,63 @@ int launch_bwd(const ScopeAttnArgs &a, cudaStream_t s) {
     p.T = a.T;
     p.QB = QB;
     p.words = words;
-    p.kv_stride = a.kv_stride;
     p.q_bitmap = a.q_bitmap;
-    p.kv_num = a.kv_num;
-    p.kv_idx = a.kv_indices;
     p.block_info = a.block_info;
     p.docs = a.docs;
     p.lse2 = lse2;
     p.delta = delta;
     p.scale = a.scale;
     p.scale_log2 = a.scale * 1.4426950408889634f;
+    p.dk = reinterpret_cast<__nv_bfloat16 *>(a.dk);
+    p.dk_sh = a.dk_sh;
+    p.dk_st = a.dk_st;
+    p.dv = reinterpret_cast<__nv_bfloat16 *>(a.dv);
+    p.dv_sh = a.dv_sh;
+    p.dv_st = a.dv_st;
+    p.dq_acc = dq_acc;
+    p.slope_acc = slope_acc;
+    p.s_aug = (float)sqrt((double)a.beta / (double)a.scale);
     p.plan = plan;
     p.err = a.err_flag;
 
-    // dK, dV
-    p.g0 = reinterpret_cast<__nv_bfloat16 *>(a.dk);
-    p.g0_sh = a.dk_sh;
-    p.g0_st = a.dk_st;
-    p.g1 = reinterpret_cast<__nv_bfloat16 *>(a.dv);
-    p.g1_sh = a.dv_sh;
-    p.g1_st = a.dv_st;
     // each CTA takes all 512 TMEM columns, so ask for enough shared memory that a
     // second CTA never lands on the SM just to wait inside tcgen05.alloc
     const size_t kOneCtaPerSm = 120 * 1024;
-    size_t smem = std::max<size_t>(tcbwd::KVL<DA>::TOTAL + 1024, kOneCtaPerSm);
-    if (cudaFuncSetAttribute(tcbwd::dkv_kernel<DA>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
+    const size_t smem = std::max<size_t>(tcbwd::FL<DA>::TOTAL + 1024, kOneCtaPerSm);
+    if (cudaFuncSetAttribute(tcbwd::dkvq_kernel<DA, SLOPE>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
         cudaSuccess)
         return SCOPE_ERR_CUDA;
-    // persistent: one CTA per SM walks the plan's items
     int dev = 0, n_sm = 148;
     if (cudaGetDevice(&dev) != cudaSuccess || cudaDeviceGetAttribute(&n_sm, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
         return SCOPE_ERR_CUDA;
-    tcbwd::dkv_kernel<DA><<<std::min(ws.max_items, n_sm), tcbwd::kThreads, smem, s>>>(maps, p);
+    // persistent: one CTA per SM walks the plan's items
+    tcbwd::dkvq_kernel<DA, SLOPE><<<std::min(ws.max_items, n_sm), tcbwd::kThreads, smem, s>>>(maps, p);
     SCOPE_CHECK_LAUNCH();
 
-    // dQ (+ coefficient gradients)
-    p.g0 = reinterpret_cast<__nv_bfloat16 *>(a.dq);
-    p.g0_sh = a.dq_sh;
-    p.g0_st = a.dq_st;
-    p.g1 = nullptr;
-    if (a.bias_mode == SCOPE_BIAS_QK_AUG) {
-        p.K = a.K;
-        p.has_slope = a.slope != nullptr;
-        p.tab_len = a.tab_len;
-        p.tab_smem = (a.tab_len % 8 == 0) && aligned16(a.cos_tab) && aligned16(a.sin_tab) && a.K <= DA / 2;
-        p.cos_tab = a.cos_tab;
-        p.sin_tab = a.sin_tab;
-        p.s_aug = (float)sqrt((double)a.beta / (double)a.scale);
-        p.dcoeff_cos = a.dcoeff_cos;
-        p.dcoeff_sin = a.dcoeff_sin;
-        p.dslope = a.dslope;
+    tcbwd::FinishParams f;
+    std::memset(&f, 0, sizeof(f));
+    f.acc = dq_acc;
+    f.ld = ws.dq_ld;
+    f.H = a.H;
+    f.T = a.T;
+    f.scale = a.scale;
+    f.s_aug = p.s_aug;
+    f.dq = reinterpret_cast<__nv_bfloat16 *>(a.dq);
+    f.dq_sh = a.dq_sh;
+    f.dq_st = a.dq_st;
+    if (DA && a.dcoeff_cos) {
+        f.K = a.K;
+        f.tab_len = a.tab_len;
+        f.cos_tab = a.cos_tab;
+        f.sin_tab = a.sin_tab;
+        f.dcoeff_cos = a.dcoeff_cos;
+        f.dcoeff_sin = a.dcoeff_sin;
+        if (SLOPE) {
+            f.slope_acc = slope_acc;
+            f.dslope = a.dslope;
+        }
     }
-    smem = std::max<size_t>(tcbwd::QL<DA>::TOTAL + 1024, kOneCtaPerSm);
-    if (cudaFuncSetAttribute(tcbwd::dq_kernel<DA>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
-        cudaSuccess)
-        return SCOPE_ERR_CUDA;
-    // persistent: one CTA per SM (at most one per work item)
-    const int grid_q = std::min(a.H * QB, n_sm);
-    tcbwd::dq_kernel<DA><<<grid_q, tcbwd::kThreads, smem, s>>>(maps, p);
+    tcbwd::finish_kernel<<<(unsigned)((rows + 7) / 8), 256, 0, s>>>(f);
     SCOPE_CHECK_LAUNCH();
     return SCOPE_OK;
 }
@@ -1312,18 +1081,19 @@ int launch_bwd(const ScopeAttnArgs &a, cudaStream_t s) {
 }  // namespace tchost
 }  // namespace scope
 
-size_t scope_bwd_workspace_bytes(int H, int T, int block_size) {
-    return scope::tchost::bwd_workspace(H, T, block_size).total;
+size_t scope_bwd_workspace_bytes(int H, int T, int block_size, int d_aug) {
+    return scope::tchost::bwd_workspace(H, T, block_size, d_aug).total;
 }
 
 int scope_tc_bwd(const ScopeAttnArgs &a, cudaStream_t s) {
     using namespace scope::tchost;
+    const bool slope = a.bias_mode == SCOPE_BIAS_QK_AUG && a.slope && a.dslope && a.dcoeff_cos;
     switch (a.bias_mode == SCOPE_BIAS_QK_AUG ? a.d_aug : 0) {
-        case 0: return launch_bwd<0>(a, s);
-        case 16: return launch_bwd<16>(a, s);
-        case 32: return launch_bwd<32>(a, s);
-        case 48: return launch_bwd<48>(a, s);
-        case 64: return launch_bwd<64>(a, s);
+        case 0: return launch_bwd<0, false>(a, s);
+        case 16: return slope ? launch_bwd<16, true>(a, s) : launch_bwd<16, false>(a, s);
+        case 32: return slope ? launch_bwd<32, true>(a, s) : launch_bwd<32, false>(a, s);
+        case 48: return slope ? launch_bwd<48, true>(a, s) : launch_bwd<48, false>(a, s);
+        case 64: return slope ? launch_bwd<64, true>(a, s) : launch_bwd<64, false>(a, s);
         default: return SCOPE_ERR_INVALID;
     }
 }

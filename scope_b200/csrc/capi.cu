@@ -16,7 +16,7 @@ int scope_simt_bwd(const ScopeAttnArgs &a, cudaStream_t s);
 int scope_tc_fwd(const ScopeAttnArgs &a, cudaStream_t s);
 int scope_tc_bwd(const ScopeAttnArgs &a, cudaStream_t s);
 bool scope_tc_eligible(const ScopeAttnArgs &a, bool bwd);
-size_t scope_bwd_workspace_bytes(int H, int T, int block_size);
+size_t scope_bwd_workspace_bytes(int H, int T, int block_size, int d_aug);
 
 namespace {
 
@@ -58,8 +58,9 @@ int validate(const ScopeAttnArgs &a, bool bwd) {
 
 extern "C" size_t scope_workspace_bytes(const ScopeAttnArgs *a) {
     if (!a || a->H <= 0 || a->T <= 0 || a->block_size <= 0 || a->T % a->block_size) return 0;
-    // delta_i = rowsum(dO * O), lse_i * log2(e) (float32 [H, T] each) and the dK/dV work plan
-    return scope_bwd_workspace_bytes(a->H, a->T, a->block_size);
+    // delta_i = rowsum(dO * O), lse_i * log2(e) (float32 [H, T] each), the dK/dV work plan and
+    // the fp32 dQ accumulator of the tensor-core backward
+    return scope_bwd_workspace_bytes(a->H, a->T, a->block_size, a->bias_mode == SCOPE_BIAS_QK_AUG ? a->d_aug : 0);
 }
 
 extern "C" int scope_attn_fwd(const ScopeAttnArgs *args, scope_stream_t stream) {

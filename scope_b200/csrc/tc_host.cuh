@@ -52,6 +52,18 @@ inline bool map2d(CUtensorMap *m, const void *base, int inner, int T, int box_in
                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// [rows][inner] fp32 with 64-byte swizzle, box (16, box_rows): the target of
+// tensor reduce-adds from 64-byte-swizzled shared-memory boxes
+inline bool map2d_f32_sw64(CUtensorMap *m, const void *base, int inner, int64_t rows, int box_rows) {
+    cuuint64_t dims[2] = {(cuuint64_t)inner, (cuuint64_t)rows};
+    cuuint64_t strides[1] = {(cuuint64_t)inner * 4};
+    cuuint32_t box[2] = {16u, (cuuint32_t)box_rows};
+    cuuint32_t es[2] = {1, 1};
+    return encode_fn()(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<void *>(base), dims, strides, box, es,
+                       CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                       CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 inline bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
 
 }  // namespace tchost

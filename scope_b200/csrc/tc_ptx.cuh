@@ -107,6 +107,22 @@ __device__ __forceinline__ void tma_load_3d(const CUtensorMap *m, void *dst, uin
         : "memory");
 }
 
+// element-wise add of a shared-memory box into the tensor map's box at (x, y) (fp32
+// maps: x must be a multiple of 4); tracked by the issuing thread's bulk groups
+__device__ __forceinline__ void tma_reduce_add_2d(const CUtensorMap *m, const void *src, int x, int y) {
+    asm volatile("cp.reduce.async.bulk.tensor.2d.global.shared::cta.add.tile.bulk_group [%0, {%2, %3}], [%1];"
+                 ::"l"(reinterpret_cast<uint64_t>(m)), "r"(smem_u32(src)), "r"(x), "r"(y)
+                 : "memory");
+}
+__device__ __forceinline__ void bulk_commit_group() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// wait until at most N of this thread's bulk groups are still reading shared memory
+template <int N>
+__device__ __forceinline__ void bulk_wait_group_read() {
+    asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
+}
+// wait until every bulk group of this thread completed
+__device__ __forceinline__ void bulk_wait_group_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+
 // contiguous global -> shared copy of `bytes` (multiple of 16, both ends 16-byte aligned)
 __device__ __forceinline__ void bulk_load(void *dst, const void *src, uint32_t bytes, uint64_t *bar) {
     asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(

@@ -59,6 +59,9 @@ def test_compiled_layer_matches_eager():
         torch.cuda.synchronize()
         res[name] = [loss.detach()] + [t.grad for t in leaves]
     # the attention op runs the same kernels; Inductor's fused square().sum() may
-    # round the loss (and so dout = 2 out) differently from eager in the last bit
-    for a, b in zip(res["eager"], res["compiled"]):
-        torch.testing.assert_close(b.float(), a.float(), rtol=1e-5, atol=1e-5)
+    # round the loss (and so dout = 2 out) differently from eager in the last bit,
+    # and dq and the coefficient gradients are fp32 partial sums added in arrival
+    # order (a last-bit difference can move a bf16 result by one step)
+    for n, a, b in zip(("loss", "dq", "dk", "dv", "dcc", "dcs"), res["eager"], res["compiled"]):
+        tol = 1e-5 if n in ("loss", "dk", "dv") else 1e-2
+        torch.testing.assert_close(b.float(), a.float(), rtol=tol, atol=tol)

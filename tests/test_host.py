@@ -55,10 +55,16 @@ def test_validation_rejects_before_launch():
     assert L.scope_mask_build(ctypes.byref(m), None) == -1        # M > 16
     assert L.scope_block_info(None, 100, 128, 1, 0, 0, None, None) == -1
     assert L.scope_qk_aug_prepare(None, None, None, None, None, 0, 1, 1, 1, 16, 0.5, 0.12, 1, None, None, None) == -1
+    # the backward's workspace: delta and lse2 [H, T], the fp32 dQ accumulator
+    # [H, T, 64 + d_aug] and slope sums [H, T], the work plan
     a2 = _lib.ScopeAttnArgs()
     a2.H, a2.T, a2.block_size = 16, 131072, 128
+    a2.bias_mode, a2.d_aug = 2, 32
     ws = L.scope_workspace_bytes(ctypes.byref(a2))
-    assert 2 * 16 * 131072 * 4 < ws < L.scope_static_scratch_bytes()   # config 3 fits the static scratch
+    assert 16 * 131072 * (2 * 4 + 96 * 4 + 4) <= ws < 16 * 131072 * (2 * 4 + 96 * 4 + 4) + (16 << 20)
+    assert ws > L.scope_static_scratch_bytes()           # config 3 is beyond the static scratch
+    a2.H, a2.T = 2, 2048
+    assert L.scope_workspace_bytes(ctypes.byref(a2)) < L.scope_static_scratch_bytes()
 
 
 def test_mask_max_kv():
