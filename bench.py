@@ -174,6 +174,44 @@ class Workload:
         return bm, out
 
 
+def capture_step(wl, world):
+    """The step captured in a CUDA graph (kernels, memsets and, at N > 1, the
+    NCCL all-gathers), after warm-up steps on a side stream; replaying it
+    costs the host ~10 us instead of the Python launch path of the mask
+    builder, the custom ops and autograd.  Every rank captures or none does
+    (a rank that fails reports it and all ranks run the step eagerly).
+    Returns (graph or None, launches per step, reason)."""
+    L = _lib.lib()
+    torch.cuda.synchronize()
+    n0 = L.scope_launch_count()
+    wl.step()
+    torch.cuda.synchronize()
+    per_step = L.scope_launch_count() - n0
+    graph, why = None, ""
+    try:
+        side = torch.cuda.Stream()
+        side.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(side):
+            for _ in range(2):
+                wl.step()
+        torch.cuda.current_stream().wait_stream(side)
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            wl.step()
+        torch.cuda.synchronize()
+        graph = g
+    except Exception as e:  # the eager step is measured instead
+        why = f"{type(e).__name__}: {e}"[:200]
+    ok = torch.tensor([1 if graph is not None else 0], device="cuda", dtype=torch.int32)
+    if world > 1:
+        dist.all_reduce(ok, op=dist.ReduceOp.MIN)
+    if int(ok.item()) == 0:
+        graph = None
+        why = why or "another rank could not capture the step"
+    return graph, per_step, why
+
+
 def active_pairs(bm):
     return int(bm.kv_num_blocks.sum().item())
 
@@ -669,6 +707,7 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference", "flex"])
     ap.add_argument("--no-gpu-reference", action="store_true")
     ap.add_argument("--no-decoder", action="store_true")
+    ap.add_argument("--no-graph", action="store_true", help="time the step eagerly instead of as a CUDA graph")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--heads", type=int, default=0,
@@ -693,10 +732,18 @@ def main():
         wl.step()
     torch.cuda.synchronize()
     L = _lib.lib()
+    graph, per_step, graph_why = (None, 0, "disabled (--no-graph)")
+    if not args.no_graph:
+        graph, per_step, graph_why = capture_step(wl, world)
+    step_fn = graph.replay if graph is not None else wl.step
+    for _ in range(2):
+        step_fn()
+    torch.cuda.synchronize()
     n0 = L.scope_launch_count()
     with ClockSampler(local) as clk:
-        ms = time_steps(wl.step, args.steps, world)
-    launches = L.scope_launch_count() - n0
+        ms = time_steps(step_fn, args.steps, world)
+    # a graph replay launches the captured kernels without calling the library
+    launches = per_step * args.steps if graph is not None else L.scope_launch_count() - n0
     P_t = torch.tensor([P_local], device="cuda", dtype=torch.int64)
     if world > 1:
         dist.all_reduce(P_t)
@@ -708,6 +755,26 @@ def main():
 
     # per-phase device times (builder / forward / backward) on this rank
     ph = phase_times(wl)
+    # the mask builder alone against its HBM roofline: the causal candidate logits and
+    # Gumbel noise read, the lists and counts written (block_info, the zeroed bitmap and
+    # statistics included in the time)
+    QBc = cfg.QB
+    mb_bytes = wl.hp * (QBc * (QBc + 1) // 2) * 8 + wl.hp * QBc * (4 + 4 * bm0.kv_indices.shape[-1])
+    torch.cuda.synchronize()
+    s0 = torch.cuda.current_stream()
+    eb0, eb1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    gpu_hold()
+    eb0.record(s0)
+    for _ in range(10):
+        wl.build()
+    eb1.record(s0)
+    torch.cuda.synchronize()
+    mb_ms = eb0.elapsed_time(eb1) / 10
+    hbm_peak = peaks()[0]
+    mask_builder = {"kernel": "scope_mask_build (+ block_info, zeroed bitmap and statistics)", "ms": mb_ms,
+                    "algorithmic_bytes": mb_bytes, "achieved_gbs": mb_bytes / (mb_ms * 1e-3) / 1e9,
+                    "peak_gbs": hbm_peak, "frac": mb_bytes / (mb_ms * 1e-3) / 1e9 / hbm_peak,
+                    "unit": "GB/s", "bound": "hbm"}
     hbm, bf16, src = peaks()
     f_fwd, f_bwd = 4 * bs * bs * D * P_local, 10 * bs * bs * D * P_local
     phases = {"mask_build_ms": ph[0], "forward_ms": ph[1], "backward_ms": ph[2]}
@@ -798,8 +865,12 @@ def main():
                            "active_block_pairs": P, "l2": "inputs larger than L2 (q,k,v,dO 1 GiB)"},
                 "roofline": roof, "phases_ms": phases, "cpu_baseline": cpu, "e2e": e2e,
                 "clocks": clk.summary(), "gpu_launches": int(launches), "coeff_block": coeff,
-                "gpu_reference": gref, "decoder": decoder}
+                "gpu_reference": gref, "decoder": decoder, "mask_builder": mask_builder,
+                "step_launch": {"cuda_graph": graph is not None, "kernels_per_step": per_step,
+                                "note": graph_why or "the timed steps replay one CUDA graph of the whole step"}}
         print(json.dumps(line), flush=True)
+    del graph                     # a graph holding NCCL work is released before the process group
+    torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()

@@ -204,8 +204,7 @@ int scope_spectral_coeffs(const ScopeCoeffArgs *args, scope_stream_t stream);
 /* Backward of the coefficient block up to the MLP output: dL/dy [H,T,n_out]
  * f32 from the MLP output y (mlp_out of the forward) and the upstream
  * gradients of the block's outputs, each optional (NULL = zero).  The MLP's
- * own backward (two bf16 linears and a SiLU) is the caller's: the reference
- * runs it through torch autograd (model/attn_bias.py:306-324). */
+ * own backward follows (scope_spectral_mlp_bwd). */
 typedef struct ScopeCoeffBwdArgs {
     int32_t H, T, K, M, use_slope, subtract_b0;
     const uint16_t *mlp_out;                       /* bf16 [H,T,n_out] */
@@ -219,6 +218,26 @@ typedef struct ScopeCoeffBwdArgs {
     int32_t *err_flag;                             /* optional device error word */
 } ScopeCoeffBwdArgs;
 int scope_spectral_coeffs_bwd(const ScopeCoeffBwdArgs *args, scope_stream_t stream);
+
+/* Backward of the coefficient block's MLP with weights shared by the heads:
+ * from dL/dy to dL/dq, dL/dW1, dL/db1 and dL/dW2 (dL/db2 is the column sum
+ * of dy).  Replaces the autograd backward of SpectralBias._mlp_forward
+ * (model/attn_bias.py:306-318): linear(q, W1, b1) -> silu -> linear(., W2, b2)
+ * in bf16, with the same roundings (each linear's output, the SiLU and its
+ * backward rounded to bf16).  The weight gradients are fp32 sums the caller
+ * zeroes; the reference's are those sums rounded to bf16. */
+typedef struct ScopeCoeffMlpBwdArgs {
+    int32_t H, T, n_out;              /* T % 128 == 0, n_out <= 96, hidden 128, head dim 64 */
+    const void *q;                    /* bf16 [H,T,64] view (last dim contiguous) */
+    int64_t q_sh, q_st;
+    const void *w1, *b1, *w2;         /* bf16 [128,64], [128], [n_out,128] */
+    const void *dy;                   /* bf16 [H*T, NP]: dL/dy, zero columns from n_out to NP = n_out
+                                         rounded up to 16 */
+    void *dq;                         /* bf16 [H,T,64] contiguous */
+    float *dw1, *db1, *dw2;           /* fp32 [128,64], [128], [n_out,128]: sums added */
+    int32_t *err_flag;                /* optional device error word */
+} ScopeCoeffMlpBwdArgs;
+int scope_spectral_mlp_bwd(const ScopeCoeffMlpBwdArgs *args, scope_stream_t stream);
 
 /* Self-test of the bounded-wait failure path (no counterpart in the
  * reference): one CTA allocates TMEM, waits at most limit_us microseconds
@@ -307,8 +326,10 @@ size_t scope_static_scratch_bytes(void);
 /* Name of a scope_status value. */
 const char *scope_error_string(int status);
 
-/* Struct layout self-check for bindings: which = 0 (ScopeMaskArgs) or 1
- * (ScopeAttnArgs); what = 0 (sizeof) or 1 (offset of the last field, err_flag). */
+/* Struct layout self-check for bindings: which = 0 (ScopeMaskArgs), 1
+ * (ScopeAttnArgs), 2 (ScopeCoeffArgs), 3 (ScopeCoeffBwdArgs) or 4
+ * (ScopeCoeffMlpBwdArgs); what = 0 (sizeof) or 1 (offset of the last field,
+ * err_flag). */
 size_t scope_abi_layout(int which, int what);
 
 /* Number of kernels this library has launched in this process (all devices).

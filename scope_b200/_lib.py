@@ -78,6 +78,19 @@ class ScopeAttnArgs(ctypes.Structure):
     ]
 
 
+class ScopeCoeffMlpBwdArgs(ctypes.Structure):
+    _fields_ = [
+        ("H", I32), ("T", I32), ("n_out", I32),
+        ("q", P),
+        ("q_sh", I64), ("q_st", I64),
+        ("w1", P), ("b1", P), ("w2", P),
+        ("dy", P),
+        ("dq", P),
+        ("dw1", P), ("db1", P), ("dw2", P),
+        ("err_flag", P),
+    ]
+
+
 # symbols declared in include/scope_b200.h, with ctypes signatures
 class ScopeCoeffArgs(ctypes.Structure):
     _fields_ = [
@@ -128,6 +141,7 @@ SIGNATURES = {
     "scope_qk_aug_prepare": (I32, [P, P, P, P, P, I32, I32, I32, I32, I32, F32, F32, I32, P, P, P]),
     "scope_spectral_coeffs": (I32, [ctypes.POINTER(ScopeCoeffArgs), P]),
     "scope_spectral_coeffs_bwd": (I32, [ctypes.POINTER(ScopeCoeffBwdArgs), P]),
+    "scope_spectral_mlp_bwd": (I32, [ctypes.POINTER(ScopeCoeffMlpBwdArgs), P]),
     "scope_selftest_wait_timeout": (I32, [P, ctypes.c_uint32, P]),
     "scope_attn_fwd": (I32, [ctypes.POINTER(ScopeAttnArgs), P]),
     "scope_attn_bwd": (I32, [ctypes.POINTER(ScopeAttnArgs), P]),
@@ -173,7 +187,8 @@ def check(status: int, what: str) -> None:
 
 def check_abi() -> None:
     L = lib()
-    for which, S in ((0, ScopeMaskArgs), (1, ScopeAttnArgs), (2, ScopeCoeffArgs), (3, ScopeCoeffBwdArgs)):
+    for which, S in ((0, ScopeMaskArgs), (1, ScopeAttnArgs), (2, ScopeCoeffArgs), (3, ScopeCoeffBwdArgs),
+                     (4, ScopeCoeffMlpBwdArgs)):
         size, last = L.scope_abi_layout(which, 0), L.scope_abi_layout(which, 1)
         if size != ctypes.sizeof(S) or last != S.err_flag.offset:
             raise RuntimeError(f"scope_b200 ABI mismatch for {S.__name__}: C sizeof={size} last={last}, "

@@ -17,8 +17,10 @@ Backward: when q or a weight requires grad, the outputs carry autograd
 history.  The gradient up to the MLP output runs in a CUDA kernel
 (``scope_spectral_coeffs_bwd``: the chain rule through the mixture, the
 normalisation over frequencies, the softmax and the squashing functions);
-the MLP's own backward replays the reference's torch ops on the GPU (two bf16
-linears and a SiLU, model/attn_bias.py:306-324 -- plain library GEMMs).
+with weights shared by the heads (the reference's default) the MLP's own
+backward is one tensor-core kernel (``scope_spectral_mlp_bwd``); with one
+weight set per head it replays the reference's torch ops on the GPU (two
+bf16 linears and a SiLU, model/attn_bias.py:306-324).
 """
 from __future__ import annotations
 
@@ -95,6 +97,40 @@ def coeff_dy(y: Tensor, grads, *, omegas: Tensor, log_omegas: Tensor, M: int, de
     return dy
 
 
+def mlp_backward(q: Tensor, w1: Tensor, b1: Tensor, w2: Tensor, dy: Tensor, needs) -> tuple:
+    """Gradients of the shared-weight MLP (model/attn_bias.py:306-318) from
+    dL/dy [1,H,T,n_out] f32: (dq, dW1, db1, dW2, db2) in the inputs' dtypes
+    (None where not needed), from one launch of ``scope_spectral_mlp_bwd``.
+    The reference back-propagates dy cast to y's dtype (bf16) through its bf16
+    linears; its weight gradients are bf16 results cast to the weights' dtype,
+    which the fp32 sums of the kernel are rounded to here."""
+    q4 = q if q.dim() == 4 else q[None]
+    _, H, T, D = q4.shape
+    n_out = dy.shape[-1]
+    npad = (n_out + 15) // 16 * 16
+    dev = q4.device
+    dyb = torch.zeros(H * T, npad, device=dev, dtype=torch.bfloat16)
+    dyb[:, :n_out] = dy.reshape(H * T, n_out)
+    bf = lambda t: t.detach().to(device=dev, dtype=torch.bfloat16).contiguous()  # noqa: E731
+    w1b, b1b, w2b = bf(w1), bf(b1), bf(w2)
+    q3 = q4[0].detach()
+    dq = torch.empty(1, H, T, D, device=dev, dtype=torch.bfloat16)
+    f32 = dict(device=dev, dtype=torch.float32)
+    dw1, db1, dw2 = torch.zeros(w1.shape, **f32), torch.zeros(b1.shape, **f32), torch.zeros(w2.shape, **f32)
+    a = _lib.ScopeCoeffMlpBwdArgs()
+    a.H, a.T, a.n_out = H, T, n_out
+    a.q, a.q_sh, a.q_st = q3.data_ptr(), q3.stride(0), q3.stride(1)
+    a.w1, a.b1, a.w2 = w1b.data_ptr(), b1b.data_ptr(), w2b.data_ptr()
+    a.dy, a.dq = dyb.data_ptr(), dq.data_ptr()
+    a.dw1, a.db1, a.dw2 = dw1.data_ptr(), db1.data_ptr(), dw2.data_ptr()
+    a.err_flag = _lib.err_word_ptr(dev)
+    _lib.check(_lib.lib().scope_spectral_mlp_bwd(ctypes.byref(a), _stream(dev)), "scope_spectral_mlp_bwd")
+    db2 = dyb[:, :n_out].float().sum(0)
+    rnd = lambda g, like: g.to(torch.bfloat16).to(like.dtype)  # noqa: E731
+    out = (dq if q.dim() == 4 else dq[0], rnd(dw1, w1), rnd(db1, b1), rnd(dw2, w2), rnd(db2, w2))
+    return tuple(g if need else None for g, need in zip(out, needs))
+
+
 class _CoeffFn(torch.autograd.Function):
     @staticmethod
     def forward(ctx, q, w1, b1, w2, b2, kw):
@@ -109,6 +145,10 @@ class _CoeffFn(torch.autograd.Function):
         q, w1, b1, w2, b2, y = ctx.saved_tensors
         kw = {k: v for k, v in ctx.kw.items() if k not in ("return_mlp",)}
         dy = coeff_dy(y, list(grads[:9]) + [grads[10]], **kw)
+        if w1.dim() == 2:
+            # weights shared by the heads (the reference's default): the fused tensor-core MLP backward
+            return mlp_backward(q, w1, b1, w2, dy, ctx.needs_input_grad[:5]) + (None,)
+        # one weight set per head: the reference's MLP ops replayed through autograd
         leaves = [t.detach().requires_grad_(need) for t, need in zip((q, w1, b1, w2, b2), ctx.needs_input_grad[:5])]
         n_out = dy.shape[-1]
         pad = (-n_out) % 16

@@ -97,11 +97,13 @@ extern "C" const char *scope_error_string(int status) {
 }
 
 extern "C" size_t scope_abi_layout(int which, int what) {
-    // which: 0 ScopeMaskArgs, 1 ScopeAttnArgs, 2 ScopeCoeffArgs, 3 ScopeCoeffBwdArgs; what: 0 sizeof, 1 offset of the last field
+    // which: 0 ScopeMaskArgs, 1 ScopeAttnArgs, 2 ScopeCoeffArgs, 3 ScopeCoeffBwdArgs, 4 ScopeCoeffMlpBwdArgs;
+    // what: 0 sizeof, 1 offset of the last field
     if (which == 0) return what == 0 ? sizeof(ScopeMaskArgs) : offsetof(ScopeMaskArgs, err_flag);
     if (which == 1) return what == 0 ? sizeof(ScopeAttnArgs) : offsetof(ScopeAttnArgs, err_flag);
     if (which == 2) return what == 0 ? sizeof(ScopeCoeffArgs) : offsetof(ScopeCoeffArgs, err_flag);
     if (which == 3) return what == 0 ? sizeof(ScopeCoeffBwdArgs) : offsetof(ScopeCoeffBwdArgs, err_flag);
+    if (which == 4) return what == 0 ? sizeof(ScopeCoeffMlpBwdArgs) : offsetof(ScopeCoeffMlpBwdArgs, err_flag);
     return 0;
 }
 

@@ -236,6 +236,62 @@ __device__ void select_row(const ScopeMaskArgs &a, int h, int qb, int lane, int 
     __syncwarp();
 }
 
+// The same selection for rows of at most 32 * 32 candidates with every score in
+// registers (compile-time indices, nothing in local memory): lane l holds the
+// candidates kb = l + 32 e and a bitmask of those already taken; each lane
+// keeps its best (score, block) among the untaken cached; per round a warp
+// argmax picks the winner and only the winning lane rescans.  Order and ties
+// as select_row; once every candidate is taken the rest of the centres are qb.
+__device__ void select_row_regs(const ScopeMaskArgs &a, int h, int qb, int lane, int *cen) {
+    constexpr int NE = 32;
+    const float *lrow = a.sel_logits + (int64_t)h * a.sel_head_stride + (int64_t)qb * a.sel_row_stride;
+    const float *grow = a.sel_gumbel + (int64_t)h * a.sel_head_stride + (int64_t)qb * a.sel_row_stride;
+    const Divider tau(a.sel_tau);
+    const int n = qb + 1;
+    float sc[NE];
+#pragma unroll
+    for (int e = 0; e < NE; ++e) {
+        const int kb = lane + 32 * e;
+        sc[e] = (kb < n) ? __fadd_rn(tau(__ldg(lrow + kb)), __ldg(grow + kb)) : -INFINITY;
+    }
+    uint32_t taken = 0u;
+    auto lane_best = [&](float &bv, int &bi) {
+        bv = -INFINITY;
+        bi = INT_MAX;
+#pragma unroll
+        for (int e = 0; e < NE; ++e) {
+            const int kb = lane + 32 * e;
+            if (kb < n && !((taken >> e) & 1u) && better(sc[e], kb, bv, bi)) {
+                bv = sc[e];
+                bi = kb;
+            }
+        }
+    };
+    float lv;
+    int li;
+    lane_best(lv, li);
+    for (int r = 0; r < a.M; ++r) {
+        float bv = lv;
+        int bi = li;
+#pragma unroll
+        for (int o = 16; o; o >>= 1) {
+            const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+            const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+            if (better(ov, oi, bv, bi)) {
+                bv = ov;
+                bi = oi;
+            }
+        }
+        if (lane == 0) cen[r] = (bi == INT_MAX) ? qb : bi;
+        if (bi != INT_MAX && li == bi) {
+            // the winner is this lane's cached best: mark it taken and rescan
+            taken |= 1u << ((bi - lane) >> 5);
+            lane_best(lv, li);
+        }
+    }
+    __syncwarp();
+}
+
 __global__ void __launch_bounds__(kWarps * 32) build_kernel(const BuildParams P) {
     extern __shared__ int smem[];
     const ScopeMaskArgs &a = P.a;
@@ -269,7 +325,8 @@ __global__ void __launch_bounds__(kWarps * 32) build_kernel(const BuildParams P)
 
         // ---- pointer centres (model/attn_bias.py:779-784) ----
         if (a.sel_logits) {
-            select_row(a, h, qb, lane, cen);
+            if (qb < 32 * 32) select_row_regs(a, h, qb, lane, cen);
+            else select_row(a, h, qb, lane, cen);
         } else if (lane < M) {
             float d = a.delta_rep[(int64_t)h * a.delta_head_stride + (int64_t)qb * a.delta_row_stride +
                                   (int64_t)lane * a.delta_m_stride];
