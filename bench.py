@@ -245,16 +245,18 @@ def gpu_hold(ms=30.0):
     torch.cuda._sleep(int(ms * 1e-3 * 2.0e9))
 
 
-def phase_times(wl, reps=3):
-    """Average device time of each phase of the step, with CUDA events on the
+def phase_times(wl, reps=5):
+    """Median device time of each phase of the step, with CUDA events on the
     stream the kernels are launched on (the current stream); each repetition
     is queued behind a device-side hold, so host launch overhead is not
-    counted."""
+    counted.  One untimed repetition goes first (the caching allocator may
+    grow, and synchronise, on the first eager step after a graph capture), and
+    the median drops a repetition the host still fell behind on."""
     s = torch.cuda.current_stream()
     ev = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
-    acc = [0.0, 0.0, 0.0]
+    samples = [[], [], []]
     L = wl.leaves
-    for _ in range(reps):
+    for rep in range(reps + 1):
         for t in L.values():
             t.grad = None
         gpu_hold()
@@ -268,9 +270,10 @@ def phase_times(wl, reps=3):
         out.backward(wl.x["do"][None])
         ev[3].record(s)
         torch.cuda.synchronize()
-        for i in range(3):
-            acc[i] += ev[i].elapsed_time(ev[i + 1])
-    return [a / reps for a in acc]
+        if rep > 0:
+            for i in range(3):
+                samples[i].append(ev[i].elapsed_time(ev[i + 1]))
+    return [statistics.median(x) for x in samples]
 
 
 class E2EPipeline:

@@ -245,6 +245,12 @@ int scope_spectral_mlp_bwd(const ScopeCoeffMlpBwdArgs *args, scope_stream_t stre
  * *err_flag (device memory), frees TMEM and exits. */
 int scope_selftest_wait_timeout(int32_t *err_flag, uint32_t limit_us, scope_stream_t stream);
 
+/* Self-test of the FMA-pipe exponential the attention forward uses for a
+ * share of its exponentials (no counterpart in the reference): y[i] = 2^x[i]
+ * for n float32 values in device memory, x <= 127 (inputs below -125 give
+ * about 2^-125). */
+int scope_selftest_exp2_fma(const float *x, float *y, int32_t n, scope_stream_t stream);
+
 /* ------------------------------------------------------------------------ */
 /* 3. block-sparse attention                                                  */
 /* ------------------------------------------------------------------------ */

@@ -143,6 +143,7 @@ SIGNATURES = {
     "scope_spectral_coeffs_bwd": (I32, [ctypes.POINTER(ScopeCoeffBwdArgs), P]),
     "scope_spectral_mlp_bwd": (I32, [ctypes.POINTER(ScopeCoeffMlpBwdArgs), P]),
     "scope_selftest_wait_timeout": (I32, [P, ctypes.c_uint32, P]),
+    "scope_selftest_exp2_fma": (I32, [P, P, I32, P]),
     "scope_attn_fwd": (I32, [ctypes.POINTER(ScopeAttnArgs), P]),
     "scope_attn_bwd": (I32, [ctypes.POINTER(ScopeAttnArgs), P]),
     "scope_workspace_bytes": (ctypes.c_size_t, [ctypes.POINTER(ScopeAttnArgs)]),

@@ -10,15 +10,17 @@
 //               sparse gather is just the TMA coordinate.  No multicast.
 //   warp 1      tcgen05 issuer (the warp waits, lane 0 issues): S = Q K^T
 //               (+ Qaug Kaug^T, the spectral bias of the qk_aug mode) into
-//               TMEM, and O += P V with P read from TMEM as the A operand, in
-//               the order their inputs become ready.  It also owns the TMEM
-//               allocation.
+//               TMEM, and O += P V with P read from TMEM as the A operand, in a
+//               fixed order (S_{j+1}, then P V_j) with sleeping waits.  It also
+//               owns the TMEM allocation.
 //   warps 2..9  softmax: two threads per query row (one per 64-column half,
 //               the halves trading row max and row sum through shared memory
 //               behind a bounded mbarrier).  S comes out of TMEM with
 //               tcgen05.ld, the document-causal mask is applied only on tiles
 //               the producer classified as needing it (diagonal, document
-//               boundary), exponentials are taken in the log2 domain, P goes
+//               boundary; branch-free selects, document ids read 16 bytes at a
+//               time), exponentials are taken in the log2 domain (one pair in
+//               eight on the FMA pipe, ex2_fma2, the rest on the MUFU), P goes
 //               back to TMEM as bf16, and the running max is only moved when
 //               it grows by more than 2^8 (otherwise O would need a rescale
 //               through TMEM every tile).
@@ -49,6 +51,13 @@ constexpr int kThreads = 320;   // producer, issuer, 8 softmax warps (two per TM
 constexpr int kSoftmax = 256;
 constexpr uint32_t kTmemCols = 256;
 constexpr uint32_t S_COL = 0, O_COL = 128, P_COL = 192;
+// of every 8 exponential pairs, this many are evaluated on the FMA pipe
+// (ex2_fma2) and the rest on the MUFU: the two pipes then share the softmax's
+// exponentials instead of the MUFU alone bounding it
+#ifndef SCOPE_FWD_POLY_PAIRS
+#define SCOPE_FWD_POLY_PAIRS 1
+#endif
+constexpr int kPolyPairs = SCOPE_FWD_POLY_PAIRS;
 
 __host__ __device__ constexpr uint32_t align1k(uint32_t x) { return (x + 1023u) & ~1023u; }
 
@@ -167,6 +176,11 @@ __global__ void __launch_bounds__(kThreads, 2) fwd_kernel(const __grid_constant_
         bool ok = !*abort_flag && mbar_wait(bar, parity);
         return __all_sync(0xffffffffu, ok);
     };
+    // the issuer warp only waits: it sleeps between polls
+    auto idle_wait = [&](uint64_t *bar, uint32_t parity) -> bool {
+        bool ok = !*abort_flag && mbar_wait_idle(bar, parity);
+        return __all_sync(0xffffffffu, ok);
+    };
 
     if (warp == 0) {
         // ------------------------------------------------------------ producer
@@ -178,7 +192,7 @@ __global__ void __launch_bounds__(kThreads, 2) fwd_kernel(const __grid_constant_
             int issued = 0, kissued = 0;   // stages whose V / K loads were issued
             for (int j = 0; j < n; ++j) {
                 const int s = j & 1;
-                if (j >= 2 && (*abort_flag || !mbar_wait(kv_empty + s, ((j >> 1) - 1) & 1))) {
+                if (j >= 2 && (*abort_flag || !mbar_wait_idle(kv_empty + s, ((j >> 1) - 1) & 1))) {
                     give_up();
                     break;
                 }
@@ -192,7 +206,7 @@ __global__ void __launch_bounds__(kThreads, 2) fwd_kernel(const __grid_constant_
                 tma_load_3d(&maps.k, st + L::K, kv_full + s, 0, kb * BM, h);
 #pragma unroll
                 for (int a = 0; a < NA; ++a) tma_load_2d(&maps.ka, st + L::KA + a * L::ATILE, kv_full + s, 16 * a, kb * BM);
-                if (j >= 2 && (*abort_flag || !mbar_wait(v_empty + s, ((j >> 1) - 1) & 1))) {
+                if (j >= 2 && (*abort_flag || !mbar_wait_idle(v_empty + s, ((j >> 1) - 1) & 1))) {
                     give_up();
                     issued = j;
                     kissued = j + 1;
@@ -216,10 +230,10 @@ __global__ void __launch_bounds__(kThreads, 2) fwd_kernel(const __grid_constant_
             constexpr uint32_t idO = idesc_bf16(128, 64, false, true);
             const uint32_t tS = tmem + S_COL, tO = tmem + O_COL, tP = tmem + P_COL;
             const uint32_t sq = smem_u32(smem + L::Q);
-            bool ok = warp_wait(q_full, 0);
+            bool ok = idle_wait(q_full, 0);
             auto issue_S = [&](int j) -> bool {
                 const int s = j & 1;
-                if (!warp_wait(kv_full + s, (j >> 1) & 1)) return false;
+                if (!idle_wait(kv_full + s, (j >> 1) & 1)) return false;
                 tc_fence_after();
                 const uint32_t sk = smem_u32(smem + L::STAGE0 + s * L::STAGE);
                 if (lane == 0) {
@@ -239,43 +253,30 @@ __global__ void __launch_bounds__(kThreads, 2) fwd_kernel(const __grid_constant_
                 return true;
             };
             ok = ok && issue_S(0);
-            // S_{js} and P V_{jp} are issued as soon as their inputs are ready, in
-            // whichever order they become ready: S_{j+1} needs K_{j+1} (a TMA load
-            // that may still be in flight) and the softmax's copy of S_j; P V_j needs
-            // P_j.  A late K must not hold back P V_j, which the next softmax waits on.
-            int js = 1, jp = 0;
-            uint64_t t_last = globaltimer_ns();
-            while (ok && jp < n) {
-                bool did = false;
-                if (js < n && mbar_test(s_free, (js - 1) & 1) && mbar_test(kv_full + (js & 1), (js >> 1) & 1)) {
-                    __syncwarp();
-                    if (!issue_S(js)) { ok = false; break; }
-                    ++js;
-                    did = true;
-                }
-                if (jp < js && mbar_test(p_full, jp & 1) && mbar_test(v_full + (jp & 1), (jp >> 1) & 1)) {
-                    __syncwarp();
-                    tc_fence_after();
-                    const uint32_t sv = smem_u32(smem + L::STAGE0 + (jp & 1) * L::STAGE + L::V);
-                    if (lane == 0) {
-#pragma unroll
-                        for (int kk = 0; kk < BM / 16; ++kk)
-                            mma_ts(tO, tP + kk * 8, mnmajor128_desc(sv + kk * 2048), idO, (jp > 0 || kk > 0) ? 1u : 0u);
-                        tc_commit(o_done);
-                        if (jp + 2 < n) tc_commit(v_empty + (jp & 1));
-                    }
-                    __syncwarp();
-                    ++jp;
-                    did = true;
-                }
-                if (did) {
-                    t_last = globaltimer_ns();
-                } else if (*abort_flag || globaltimer_ns() - t_last > kWaitLimitNs) {
+            // Fixed order: S_{j+1} as soon as the softmax holds S_j in registers (and
+            // K_{j+1} has landed), then P V_j once P_j is in TMEM.  S_{j+1} is always
+            // ready first, so the order costs nothing, and the waits block in the
+            // barrier (the warp is suspended, not polling the issue slots away from
+            // the softmax warps on its sub-partition).
+            for (int j = 0; ok && j < n; ++j) {
+                if (j + 1 < n && !(idle_wait(s_free, j & 1) && issue_S(j + 1))) {
                     ok = false;
-                } else {
-                    __nanosleep(32);   // leave the sub-partition's issue slots to the softmax warps
+                    break;
                 }
-                ok = __all_sync(0xffffffffu, ok);
+                if (!idle_wait(p_full, j & 1) || !idle_wait(v_full + (j & 1), (j >> 1) & 1)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t sv = smem_u32(smem + L::STAGE0 + (j & 1) * L::STAGE + L::V);
+                if (lane == 0) {
+#pragma unroll
+                    for (int kk = 0; kk < BM / 16; ++kk)
+                        mma_ts(tO, tP + kk * 8, mnmajor128_desc(sv + kk * 2048), idO, (j > 0 || kk > 0) ? 1u : 0u);
+                    tc_commit(o_done);
+                    if (j + 2 < n) tc_commit(v_empty + (j & 1));
+                }
+                __syncwarp();
             }
             if (!ok) give_up();
         }
@@ -290,6 +291,7 @@ __global__ void __launch_bounds__(kThreads, 2) fwd_kernel(const __grid_constant_
         const uint32_t tS = tmem + lane_base + S_COL + ch * 64, tO = tmem + lane_base + O_COL + ch * 32,
                        tP = tmem + lane_base + P_COL + ch * 32;
         const bool have_docs = p.docs != nullptr;
+        const bool docs_vec = (reinterpret_cast<uintptr_t>(p.docs) & 15) == 0;
         const int doc_i = have_docs ? p.docs[i] : 0;
         // scores are kept unscaled until the exponent: max(x) * c = max(x * c) for c > 0,
         // and a negative scale is folded into the sign of the loaded scores
@@ -329,22 +331,35 @@ __global__ void __launch_bounds__(kThreads, 2) fwd_kernel(const __grid_constant_
             mbar_arrive(s_free);
             if (mk != 0) {
                 const int j0 = kb * BM + ch * 64;
-                const int lim = i - j0;                 // column c visible iff c <= lim
+                const int lim = mk == 3 ? -1 : i - j0;  // column c visible iff c <= lim
+                // document ids of the 64 columns (tiles of kind 2 only), 16 bytes at a time
+                // where the pointer allows it (j0 is a multiple of 64)
+                const int32_t *dp = have_docs ? p.docs + j0 : p.docs;
 #pragma unroll
-                for (int c = 0; c < 64; ++c) {
-                    bool valid = mk != 3 && c <= lim;
-                    if (mk == 2) valid = valid && (__ldg(p.docs + j0 + c) == doc_i);
-                    if (!valid) x[c] = -INFINITY;
+                for (int c4 = 0; c4 < 16; ++c4) {
+                    int4 d = make_int4(doc_i, doc_i, doc_i, doc_i);
+                    if (mk == 2)
+                        d = docs_vec ? __ldg(reinterpret_cast<const int4 *>(dp) + c4)
+                                     : make_int4(__ldg(dp + 4 * c4), __ldg(dp + 4 * c4 + 1), __ldg(dp + 4 * c4 + 2),
+                                                 __ldg(dp + 4 * c4 + 3));
+                    const int c = 4 * c4;
+                    x[c] = (c <= lim && d.x == doc_i) ? x[c] : -INFINITY;
+                    x[c + 1] = (c + 1 <= lim && d.y == doc_i) ? x[c + 1] : -INFINITY;
+                    x[c + 2] = (c + 2 <= lim && d.z == doc_i) ? x[c + 2] : -INFINITY;
+                    x[c + 3] = (c + 3 <= lim && d.w == doc_i) ? x[c + 3] : -INFINITY;
                 }
             }
-            // row max over this thread's 64 columns: 8 independent chains, then a tree
+            // row max over this thread's 64 columns: 8 independent chains of
+            // three-input maxima (column c in chain c & 7), then a tree
             float pm[8];
 #pragma unroll
-            for (int c = 0; c < 8; ++c) pm[c] = x[c];
-#pragma unroll
-            for (int c = 8; c < 64; ++c) pm[c & 7] = fmaxf(pm[c & 7], x[c]);
-            const float pmx = fmaxf(fmaxf(fmaxf(pm[0], pm[1]), fmaxf(pm[2], pm[3])),
-                                    fmaxf(fmaxf(pm[4], pm[5]), fmaxf(pm[6], pm[7]))) * cabs;
+            for (int k = 0; k < 8; ++k) {
+                pm[k] = fmax3(x[k], x[8 + k], x[16 + k]);
+                pm[k] = fmax3(pm[k], x[24 + k], x[32 + k]);
+                pm[k] = fmax3(pm[k], x[40 + k], x[48 + k]);
+                pm[k] = fmaxf(pm[k], x[56 + k]);
+            }
+            const float pmx = fmax3(fmax3(pm[0], pm[1], pm[2]), fmax3(pm[3], pm[4], pm[5]), fmaxf(pm[6], pm[7])) * cabs;
             // row max across the two column halves
             xmax[(j & 1) * 256 + ch * 128 + r] = pmx;
             mbar_arrive(xchg + quad);
@@ -366,9 +381,15 @@ __global__ void __launch_bounds__(kThreads, 2) fwd_kernel(const __grid_constant_
 #pragma unroll
             for (int c = 0; c < 64; c += 2) {
                 const float2 d = f2_unpack(ffma2(f2_pack(x[c], x[c + 1]), c2, nm2));
-                const float p0 = ex2(d.x), p1 = ex2(d.y);
-                pk[c >> 1] = pack_bf16(p0, p1);
-                acc[(c >> 1) & 3] = fadd2(acc[(c >> 1) & 3], f2_pack(p0, p1));
+                uint64_t pp;
+                if (((c >> 1) & 7) < kPolyPairs) {
+                    pp = ex2_fma2(d.x, d.y);   // this share of the pairs on the FMA pipe
+                } else {
+                    pp = f2_pack(ex2(d.x), ex2(d.y));
+                }
+                const float2 pf = f2_unpack(pp);
+                pk[c >> 1] = pack_bf16(pf.x, pf.y);
+                acc[(c >> 1) & 3] = fadd2(acc[(c >> 1) & 3], pp);
             }
             const float2 a01 = f2_unpack(fadd2(acc[0], acc[1])), a23 = f2_unpack(fadd2(acc[2], acc[3]));
             const float rs = (a01.x + a01.y) + (a23.x + a23.y);

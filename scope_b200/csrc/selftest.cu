@@ -34,6 +34,17 @@ __global__ void wait_timeout_kernel(int32_t *err, uint64_t limit_ns) {
     }
 }
 
+// ex2_fma2 over a vector (the FMA-pipe exponential of the attention forward),
+// so a test can hold it against exp2's error bound
+__global__ void exp2_fma_kernel(const float *__restrict__ x, float *__restrict__ y, int n) {
+    const int i = 2 * (blockIdx.x * blockDim.x + threadIdx.x);
+    if (i >= n) return;
+    const float x1 = (i + 1 < n) ? x[i + 1] : 0.f;
+    const float2 r = f2_unpack(ex2_fma2(x[i], x1));
+    y[i] = r.x;
+    if (i + 1 < n) y[i + 1] = r.y;
+}
+
 }  // namespace selftest
 }  // namespace scope
 
@@ -41,6 +52,16 @@ extern "C" int scope_selftest_wait_timeout(int32_t *err_flag, uint32_t limit_us,
     if (!err_flag || limit_us == 0 || limit_us > 1000000) return SCOPE_ERR_INVALID;
     scope::selftest::wait_timeout_kernel<<<1, 64, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
         err_flag, (uint64_t)limit_us * 1000ull);
+    SCOPE_CHECK_LAUNCH();
+    return SCOPE_OK;
+}
+
+extern "C" int scope_selftest_exp2_fma(const float *x, float *y, int32_t n, scope_stream_t stream) {
+    if (!x || !y || n < 0) return SCOPE_ERR_INVALID;
+    if (n == 0) return SCOPE_OK;
+    const int pairs = (n + 1) / 2;
+    scope::selftest::exp2_fma_kernel<<<(unsigned)((pairs + 255) / 256), 256, 0,
+                                       reinterpret_cast<cudaStream_t>(stream)>>>(x, y, n);
     SCOPE_CHECK_LAUNCH();
     return SCOPE_OK;
 }

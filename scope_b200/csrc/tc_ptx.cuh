@@ -73,6 +73,27 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, uint64
     }
 }
 
+// The same bounded wait for warps that only wait (the TMA producer and the
+// tcgen05 issuer): each poll carries a suspend-time hint, so the warp sleeps in
+// the barrier until the phase completes instead of re-polling.
+__device__ __forceinline__ bool mbar_wait_idle(uint64_t *bar, uint32_t parity, uint64_t limit_ns = kWaitLimitNs) {
+    const uint32_t a = smem_u32(bar);
+    if (mbar_try_wait(a, parity)) return true;
+    const uint64_t t0 = globaltimer_ns();
+    for (;;) {
+        uint32_t ok;
+        asm volatile(
+            "{\n\t.reg .pred p;\n\t"
+            "mbarrier.try_wait.parity.acquire.cta.shared::cta.b64 p, [%1], %2, %3;\n\t"
+            "selp.u32 %0, 1, 0, p;\n\t}\n"
+            : "=r"(ok)
+            : "r"(a), "r"(parity), "r"(1000000u)
+            : "memory");
+        if (ok) return true;
+        if (globaltimer_ns() - t0 > limit_ns) return false;
+    }
+}
+
 // Non-blocking test of a phase, decided by lane 0 of a converged warp and
 // broadcast, so the whole warp takes the same branch.
 __device__ __forceinline__ bool mbar_test(uint64_t *bar, uint32_t parity) {
@@ -291,6 +312,38 @@ __device__ __forceinline__ uint64_t fmul2(uint64_t a, uint64_t b) {
     uint64_t r;
     asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
     return r;
+}
+
+// max of three (one instruction on sm_100)
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+    float d;
+    asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+    return d;
+}
+
+// 2^x of a pair on the FMA pipe, to take load off the MUFU ex2.  Cody-Waite
+// style reduction for base 2: x = n + f with n = round(x) (x + 1.5*2^23 puts n
+// in the low mantissa bits; the subtractions are exact), 2^f by a degree-3
+// polynomial whose coefficients minimise the relative error on [-1/2, 1/2]
+// (Remez exchange, gen_exp2_poly.py: 7.5e-5 max relative error in float32),
+// then n added to the exponent field.  x is clamped below at -125 so the
+// exponent stays normal (-inf gives about 2^-125, not 0); x must be <= 127.
+__device__ __forceinline__ uint64_t ex2_fma2(float x0, float x1) {
+    constexpr float kMagic = 12582912.f, C0 = 0.9999280571937561f, C1 = 0.6932609677314758f,
+                    C2 = 0.2426111251115799f, C3 = 0.0551716685295105f;
+    const uint64_t d = f2_pack(fmaxf(x0, -125.f), fmaxf(x1, -125.f));
+    const uint64_t t = fadd2(d, f2_pack(kMagic, kMagic));
+    const uint64_t r = fadd2(t, f2_pack(-kMagic, -kMagic));
+    const uint64_t f = ffma2(r, f2_pack(-1.f, -1.f), d);
+    uint64_t q = ffma2(f2_pack(C3, C3), f, f2_pack(C2, C2));
+    q = ffma2(q, f, f2_pack(C1, C1));
+    q = ffma2(q, f, f2_pack(C0, C0));
+    uint32_t t0, t1, q0, q1;
+    asm("mov.b64 {%0, %1}, %2;" : "=r"(t0), "=r"(t1) : "l"(t));
+    asm("mov.b64 {%0, %1}, %2;" : "=r"(q0), "=r"(q1) : "l"(q));
+    uint64_t out;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(out) : "r"(q0 + (t0 << 23)), "r"(q1 + (t1 << 23)));
+    return out;
 }
 
 __device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
