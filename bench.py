@@ -352,6 +352,49 @@ def time_e2e(pipe, steps, world):
     return ms
 
 
+def score_mod_leg(wl, cfg, bm, pairs, *, reps=5):
+    """The layer with the score_mod closure (scoped_medium.py:425-457) instead of
+    qk_aug: Fourier sum in the QK MMA, b0, slope * Δ and the softplus gate
+    per element, their gradients from per-query column sums.  Same mask and
+    inputs as the step; fwd and bwd each timed with CUDA events after a
+    device-side hold (TFLOP/s on active block pairs, as the headline)."""
+    from scope_b200 import SpectralScoreMod, flex_attention
+    hp, T, D, bs = wl.hp, cfg.T, cfg.D, 128
+    g = torch.Generator(device="cuda").manual_seed(17)
+    dev = wl.x["q"].device
+    extra = {"b0": 0.1 * torch.randn(hp, T, generator=g, device=dev),
+             "slope": 0.01 * torch.tanh(torch.randn(hp, T, generator=g, device=dev)),
+             "delta_main": torch.rand(hp, T, generator=g, device=dev) * 4096.0,
+             "width": 32.0 + torch.rand(hp, T, generator=g, device=dev) * 224.0}
+    L = wl.leaves
+    lv = {n: t.detach().requires_grad_(True) for n, t in extra.items()}
+    s = torch.cuda.current_stream()
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+    fw, bw = [], []
+    for rep in range(reps + 2):
+        for t in list(L.values()) + list(lv.values()):
+            t.grad = None
+        sm = SpectralScoreMod(coeff_cos=L["coeff_cos"], coeff_sin=L["coeff_sin"], cos_tab=wl.cos_t,
+                              sin_tab=wl.sin_t, beta=BETA, b0=lv["b0"], slope=lv["slope"],
+                              delta_main=lv["delta_main"], width=lv["width"], gate="softplus", impl="score_mod")
+        gpu_hold()
+        ev[0].record(s)
+        out = flex_attention(L["q"][None], L["k"][None], L["v"][None], bm, score_mod=sm, scale=SCALE)
+        ev[1].record(s)
+        out.backward(wl.x["do"][None])
+        ev[2].record(s)
+        torch.cuda.synchronize()
+        if rep >= 2:
+            fw.append(ev[0].elapsed_time(ev[1]))
+            bw.append(ev[1].elapsed_time(ev[2]))
+    f_ms, b_ms = statistics.median(fw), statistics.median(bw)
+    fl = 14 * bs * bs * D * pairs
+    return {"workload": f"{cfg.name} layer, score_mod closure (K={cfg.K}, b0, slope, softplus gate)",
+            "forward_ms": f_ms, "backward_ms": b_ms, "tflops": fl / ((f_ms + b_ms) * 1e-3) / 1e12,
+            "forward_tflops": 4 * bs * bs * D * pairs / (f_ms * 1e-3) / 1e12,
+            "backward_tflops": 10 * bs * bs * D * pairs / (b_ms * 1e-3) / 1e12}
+
+
 def coeff_block(wl, cfg, hbm, *, reps=10, cpu=True):
     """The SpectralBias coefficient block (model/attn_bias.py:306-324, 419-478)
     on this rank's heads at the bench's T, M = 8 pointers, K of the config:
@@ -401,6 +444,9 @@ def coeff_block(wl, cfg, hbm, *, reps=10, cpu=True):
             torch.cuda.synchronize()
             gpu_hold()
             e0.record(s)
+        qg.grad = None                       # a training step starts from cleared gradients
+        for t in wg:
+            t.grad = None
         o = spectral_coefficients(qg, *wg, **kw)
         if ups is None:
             ups = [torch.ones_like(o.coeff_cos), torch.ones_like(o.coeff_sin), torch.ones_like(o.slope)]
@@ -710,6 +756,7 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference", "flex"])
     ap.add_argument("--no-gpu-reference", action="store_true")
     ap.add_argument("--no-decoder", action="store_true")
+    ap.add_argument("--no-score-mod", action="store_true", help="skip the score_mod-closure layer leg")
     ap.add_argument("--no-graph", action="store_true", help="time the step eagerly instead of as a CUDA graph")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
@@ -832,6 +879,7 @@ def main():
                "ms_per_step": ms_e / e_steps}
 
     coeff = coeff_block(wl, cfg, hbm, cpu=(rank == 0 and world == 1 and not args.no_cpu_baseline))
+    smod = None if args.no_score_mod else score_mod_leg(wl, cfg, bm0, P_local)
 
     decoder = None
     if not args.no_decoder and not args.heads and args.config == "c3":
@@ -868,7 +916,7 @@ def main():
                            "active_block_pairs": P, "l2": "inputs larger than L2 (q,k,v,dO 1 GiB)"},
                 "roofline": roof, "phases_ms": phases, "cpu_baseline": cpu, "e2e": e2e,
                 "clocks": clk.summary(), "gpu_launches": int(launches), "coeff_block": coeff,
-                "gpu_reference": gref, "decoder": decoder, "mask_builder": mask_builder,
+                "gpu_reference": gref, "decoder": decoder, "mask_builder": mask_builder, "score_mod": smod,
                 "step_launch": {"cuda_graph": graph is not None, "kernels_per_step": per_step,
                                 "note": graph_why or "the timed steps replay one CUDA graph of the whole step"}}
         print(json.dumps(line), flush=True)

@@ -214,7 +214,11 @@ typedef struct ScopeCoeffBwdArgs {
     const float *domega_reg;                       /* [H,T]: gradient of the omega_reg output */
     const float *omegas, *log_omegas;              /* [K] */
     float delta_cap, logw_min, logw_max, c_scale, width_min, width_max, eps;
-    float *dy;                                     /* [H,T,n_out] */
+    float *dy;                                     /* [H,T,n_out], or NULL with dy_bf16 */
+    void *dy_bf16;                                 /* or bf16 [H,T,dy_ld], zero padded past n_out: the
+                                                      rounding the reference's bf16 MLP backward applies,
+                                                      in the layout scope_spectral_mlp_bwd reads */
+    int32_t dy_ld;                                 /* row stride of dy_bf16: multiple of 8, >= n_out */
     int32_t *err_flag;                             /* optional device error word */
 } ScopeCoeffBwdArgs;
 int scope_spectral_coeffs_bwd(const ScopeCoeffBwdArgs *args, scope_stream_t stream);

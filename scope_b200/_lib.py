@@ -125,7 +125,7 @@ class ScopeCoeffBwdArgs(ctypes.Structure):
         ("omegas", P), ("log_omegas", P),
         ("delta_cap", F32), ("logw_min", F32), ("logw_max", F32), ("c_scale", F32), ("width_min", F32),
         ("width_max", F32), ("eps", F32),
-        ("dy", P),
+        ("dy", P), ("dy_bf16", P), ("dy_ld", I32),
         ("err_flag", P),
     ]
 

@@ -132,8 +132,21 @@ def _check_inputs(q, k, v, kv_num, kv_indices, block_size):
         raise ValueError("block mask does not match q (heads or q blocks)")
 
 
-def _prepare_aug(q, coeff_cos, coeff_sin, slope, cos_tab, sin_tab, beta, scale, bias_mode):
-    if bias_mode != BIAS_MODES["qk_aug"]:
+def _smod_on_tensor_cores(q, coeff_cos, bias_mode, block_size, cuda_cores) -> bool:
+    """score_mod runs on the tensor-core kernels (its Fourier sum in augmented
+    dims, the slope and gate terms per element) for bf16 inputs in 128-token
+    blocks with K <= 16; otherwise on the CUDA cores."""
+    return (bias_mode == BIAS_MODES["score_mod"] and q.dtype == torch.bfloat16 and block_size == 128
+            and not cuda_cores and coeff_cos is not None and coeff_cos.shape[-1] <= 16)
+
+
+def _prepare_aug(q, coeff_cos, coeff_sin, slope, cos_tab, sin_tab, beta, scale, bias_mode, block_size=128,
+                 cuda_cores=False):
+    """Augmented dims: qk_aug mode (with the slope column when there is a
+    slope), or the score_mod mode's Fourier sum alone on the tensor cores."""
+    if bias_mode == BIAS_MODES["score_mod"] and _smod_on_tensor_cores(q, coeff_cos, bias_mode, block_size, cuda_cores):
+        slope = None
+    elif bias_mode != BIAS_MODES["qk_aug"]:
         return None, None
     H, T, _ = q.shape
     K = coeff_cos.shape[-1]
@@ -163,8 +176,9 @@ def sparse_attn(q: Tensor, k: Tensor, v: Tensor, kv_num: Tensor, kv_indices: Ten
                 width: Optional[Tensor], scale: float, beta: float, bias_mode: int, gate: int,
                 gate_lambda: float, gate_tau: float, block_size: int,
                 flags: int) -> tuple[Tensor, Tensor, Tensor, Tensor]:
-    """Returns out, lse and (qk_aug mode) the augmented dims q_aug / k_aug,
-    which the backward reuses; empty tensors in the other modes.  ``flags``:
+    """Returns out, lse and (qk_aug mode, and score_mod on the tensor cores) the
+    augmented dims q_aug / k_aug, which the backward reuses; empty tensors
+    otherwise.  ``flags``:
     OP_CUDA_CORES, OP_HEAD_MAJOR_OUT (out stored [H, T, D] instead of the
     [T, H, D] storage of the reference's layout)."""
     _check_inputs(q, k, v, kv_num, kv_indices, block_size)
@@ -172,7 +186,8 @@ def sparse_attn(q: Tensor, k: Tensor, v: Tensor, kv_num: Tensor, kv_indices: Ten
     cuda_cores = bool(flags & OP_CUDA_CORES)
     out = torch.empty(H, T, D, dtype=q.dtype, device=q.device) if flags & OP_HEAD_MAJOR_OUT else _new_like_layout(q)
     lse = torch.empty(H, T, dtype=torch.float32, device=q.device)
-    q_aug, k_aug = _prepare_aug(q, coeff_cos, coeff_sin, slope, cos_tab, sin_tab, beta, scale, bias_mode)
+    q_aug, k_aug = _prepare_aug(q, coeff_cos, coeff_sin, slope, cos_tab, sin_tab, beta, scale, bias_mode,
+                                block_size, cuda_cores)
     a = _attn_args(q, k, v, out, lse, kv_num, kv_indices, q_bitmap, block_info, docs, coeff_cos, coeff_sin,
                    cos_tab, sin_tab, b0, slope, delta_main, width, scale, beta, bias_mode, gate, gate_lambda,
                    gate_tau, block_size, q_aug, k_aug, cuda_cores)
@@ -187,8 +202,9 @@ def _(q, k, v, kv_num, kv_indices, q_bitmap, block_info, docs, coeff_cos, coeff_
       b0, slope, delta_main, width, scale, beta, bias_mode, gate, gate_lambda, gate_tau, block_size, flags):
     H, T, D = q.shape
     out = q.new_empty(H, T, D) if flags & OP_HEAD_MAJOR_OUT else q.new_empty(T, H, D).permute(1, 0, 2)
-    if bias_mode == BIAS_MODES["qk_aug"]:
-        da = aug_dims(coeff_cos.shape[-1], slope is not None)
+    if bias_mode == BIAS_MODES["qk_aug"] or _smod_on_tensor_cores(q, coeff_cos, bias_mode, block_size,
+                                                                  bool(flags & OP_CUDA_CORES)):
+        da = aug_dims(coeff_cos.shape[-1], slope is not None and bias_mode == BIAS_MODES["qk_aug"])
         qa, ka = q.new_empty(H, T, da), q.new_empty(T, da)
     else:
         qa, ka = q.new_empty(0), q.new_empty(0)
@@ -210,7 +226,8 @@ def sparse_attn_bwd(dout: Tensor, q: Tensor, k: Tensor, v: Tensor, out: Tensor, 
         dout = dout.contiguous()
     dq, dk, dv = _new_like_layout(q), _new_like_layout(k), _new_like_layout(v)
     if q_aug is None or q_aug.numel() == 0:
-        q_aug, k_aug = _prepare_aug(q, coeff_cos, coeff_sin, slope, cos_tab, sin_tab, beta, scale, bias_mode)
+        q_aug, k_aug = _prepare_aug(q, coeff_cos, coeff_sin, slope, cos_tab, sin_tab, beta, scale, bias_mode,
+                                    block_size, cuda_cores)
     a = _attn_args(q, k, v, out, lse, kv_num, kv_indices, q_bitmap, block_info, docs, coeff_cos, coeff_sin,
                    cos_tab, sin_tab, b0, slope, delta_main, width, scale, beta, bias_mode, gate, gate_lambda,
                    gate_tau, block_size, q_aug, k_aug, cuda_cores)

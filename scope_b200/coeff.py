@@ -68,14 +68,19 @@ def _mlp_torch(q: Tensor, w1: Tensor, b1: Tensor, w2: Tensor, b2: Tensor) -> Ten
 
 def coeff_dy(y: Tensor, grads, *, omegas: Tensor, log_omegas: Tensor, M: int, delta_cap: float, logw_min: float,
              logw_max: float, use_slope: bool, subtract_b0: bool, c_scale: float, width_min: float, width_max: float,
-             eps: float) -> Tensor:
-    """dL/dy [1,H,T,n_out] f32 from the MLP output y (bf16) and the upstream
-    gradients of (coeff_cos, coeff_sin, slope, b0, delta_star, pi,
-    budget_logits, delta_main, width[, omega_reg]), any of them None."""
+             eps: float, padded_bf16: bool = False) -> Tensor:
+    """dL/dy from the MLP output y (bf16) and the upstream gradients of
+    (coeff_cos, coeff_sin, slope, b0, delta_star, pi, budget_logits,
+    delta_main, width[, omega_reg]), any of them None: [1,H,T,n_out] f32, or
+    with ``padded_bf16`` the bf16 rows [H*T, n_out rounded up to 16] (zero
+    padded) that the MLP backward reads."""
     _, H, T, n_out = y.shape
     K = omegas.numel()
     dev = y.device
-    dy = torch.empty(1, H, T, n_out, device=dev, dtype=torch.float32)
+    if padded_bf16:
+        dy = torch.empty(H * T, (n_out + 15) // 16 * 16, device=dev, dtype=torch.bfloat16)
+    else:
+        dy = torch.empty(1, H, T, n_out, device=dev, dtype=torch.float32)
     g = [None if t is None else t.to(device=dev, dtype=torch.float32).contiguous() for t in grads]
     g += [None] * (10 - len(g))
     a = _lib.ScopeCoeffBwdArgs()
@@ -91,26 +96,33 @@ def coeff_dy(y: Tensor, grads, *, omegas: Tensor, log_omegas: Tensor, M: int, de
     a.omegas, a.log_omegas = om.data_ptr(), lom.data_ptr()
     a.delta_cap, a.logw_min, a.logw_max = float(delta_cap), float(logw_min), float(logw_max)
     a.c_scale, a.width_min, a.width_max, a.eps = float(c_scale), float(width_min), float(width_max), float(eps)
-    a.dy = dy.data_ptr()
+    if padded_bf16:
+        a.dy_bf16, a.dy_ld = dy.data_ptr(), dy.shape[-1]
+    else:
+        a.dy = dy.data_ptr()
     a.err_flag = _lib.err_word_ptr(dev)
     _lib.check(_lib.lib().scope_spectral_coeffs_bwd(ctypes.byref(a), _stream(dev)), "scope_spectral_coeffs_bwd")
     return dy
 
 
-def mlp_backward(q: Tensor, w1: Tensor, b1: Tensor, w2: Tensor, dy: Tensor, needs) -> tuple:
+def mlp_backward(q: Tensor, w1: Tensor, b1: Tensor, w2: Tensor, dy: Tensor, needs, n_out: Optional[int] = None) -> tuple:
     """Gradients of the shared-weight MLP (model/attn_bias.py:306-318) from
-    dL/dy [1,H,T,n_out] f32: (dq, dW1, db1, dW2, db2) in the inputs' dtypes
-    (None where not needed), from one launch of ``scope_spectral_mlp_bwd``.
+    dL/dy: (dq, dW1, db1, dW2, db2) in the inputs' dtypes (None where not
+    needed), from one launch of ``scope_spectral_mlp_bwd``.  ``dy`` is
+    [1,H,T,n_out] f32, or already the bf16 rows [H*T, n_out rounded up to 16]
+    (zero padded; give ``n_out``) that ``coeff_dy(padded_bf16=True)`` writes.
     The reference back-propagates dy cast to y's dtype (bf16) through its bf16
     linears; its weight gradients are bf16 results cast to the weights' dtype,
     which the fp32 sums of the kernel are rounded to here."""
     q4 = q if q.dim() == 4 else q[None]
     _, H, T, D = q4.shape
-    n_out = dy.shape[-1]
-    npad = (n_out + 15) // 16 * 16
     dev = q4.device
-    dyb = torch.zeros(H * T, npad, device=dev, dtype=torch.bfloat16)
-    dyb[:, :n_out] = dy.reshape(H * T, n_out)
+    if dy.dtype == torch.bfloat16 and dy.dim() == 2:
+        dyb = dy
+    else:
+        n_out = dy.shape[-1]
+        dyb = torch.zeros(H * T, (n_out + 15) // 16 * 16, device=dev, dtype=torch.bfloat16)
+        dyb[:, :n_out] = dy.reshape(H * T, n_out)
     bf = lambda t: t.detach().to(device=dev, dtype=torch.bfloat16).contiguous()  # noqa: E731
     w1b, b1b, w2b = bf(w1), bf(b1), bf(w2)
     q3 = q4[0].detach()
@@ -125,7 +137,7 @@ def mlp_backward(q: Tensor, w1: Tensor, b1: Tensor, w2: Tensor, dy: Tensor, need
     a.dw1, a.db1, a.dw2 = dw1.data_ptr(), db1.data_ptr(), dw2.data_ptr()
     a.err_flag = _lib.err_word_ptr(dev)
     _lib.check(_lib.lib().scope_spectral_mlp_bwd(ctypes.byref(a), _stream(dev)), "scope_spectral_mlp_bwd")
-    db2 = dyb[:, :n_out].float().sum(0)
+    db2 = dyb[:, :n_out].sum(0, dtype=torch.float32)
     rnd = lambda g, like: g.to(torch.bfloat16).to(like.dtype)  # noqa: E731
     out = (dq if q.dim() == 4 else dq[0], rnd(dw1, w1), rnd(db1, b1), rnd(dw2, w2), rnd(db2, w2))
     return tuple(g if need else None for g, need in zip(out, needs))
@@ -144,10 +156,12 @@ class _CoeffFn(torch.autograd.Function):
     def backward(ctx, *grads):
         q, w1, b1, w2, b2, y = ctx.saved_tensors
         kw = {k: v for k, v in ctx.kw.items() if k not in ("return_mlp",)}
-        dy = coeff_dy(y, list(grads[:9]) + [grads[10]], **kw)
         if w1.dim() == 2:
-            # weights shared by the heads (the reference's default): the fused tensor-core MLP backward
-            return mlp_backward(q, w1, b1, w2, dy, ctx.needs_input_grad[:5]) + (None,)
+            # weights shared by the heads (the reference's default): dL/dy straight into the padded
+            # bf16 rows the fused tensor-core MLP backward reads
+            dyb = coeff_dy(y, list(grads[:9]) + [grads[10]], **kw, padded_bf16=True)
+            return mlp_backward(q, w1, b1, w2, dyb, ctx.needs_input_grad[:5], n_out=y.shape[-1]) + (None,)
+        dy = coeff_dy(y, list(grads[:9]) + [grads[10]], **kw)
         # one weight set per head: the reference's MLP ops replayed through autograd
         leaves = [t.detach().requires_grad_(need) for t, need in zip((q, w1, b1, w2, b2), ctx.needs_input_grad[:5])]
         n_out = dy.shape[-1]

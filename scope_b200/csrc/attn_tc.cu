@@ -106,12 +106,41 @@ struct FwdParams {
     int32_t *err;
 };
 
+// score_mod mode (the Fourier sum is in the aug dims): per-row slope, Δ_main,
+// width and b0 [H,T] (or null), the gate's lambda and 1/tau, beta / scale
+// (bias units -> unscaled score units), and beta for the lse's b0 term
+struct SmodParams {
+    const float *slope, *dmain, *width, *b0;
+    float gate_lambda, gate_itau, bias_k, beta;
+};
+
 struct Maps {
     CUtensorMap q, k, v, qa, ka;   // qa / ka: 16-column boxes of the qk_aug dims
 };
 
-template <int DA>
-__global__ void __launch_bounds__(kThreads, 2) fwd_kernel(const __grid_constant__ Maps maps, const FwdParams p) {
+// Bias of the score_mod mode beyond the Fourier sum, for Δ = i - j
+// (scoped_medium.py:425-457): slope Δ - lambda gate((|Δ - Δ_main| - width) / tau),
+// gate = softplus (torch's, threshold 20) or relu.  SM: 0 off, 1 no gate,
+// 2 softplus gate, 3 relu gate.
+template <int SM>
+__device__ __forceinline__ float smod_bias(float dl, float slope, float dm, float w, float lam, float itau) {
+    float b = slope * dl;
+    if constexpr (SM >= 2) {
+        const float u = (fabsf(dl - dm) - w) * itau;
+        float g;
+        if constexpr (SM == 3) {
+            g = fmaxf(u, 0.f);
+        } else {
+            g = u > 20.f ? u : 0.69314718055994531f * lg2(1.f + ex2(u * 1.4426950408889634f));
+        }
+        b = fmaf(-lam, g, b);
+    }
+    return b;
+}
+
+template <int DA, int SM>
+__global__ void __launch_bounds__(kThreads, 2) fwd_kernel(const __grid_constant__ Maps maps, const FwdParams p,
+                                                          const __grid_constant__ SmodParams sp) {
     using L = Layout<DA>;
     constexpr int NA = L::NA;
     extern __shared__ uint8_t smem_raw[];
@@ -292,6 +321,15 @@ __global__ void __launch_bounds__(kThreads, 2) fwd_kernel(const __grid_constant_
                        tP = tmem + lane_base + P_COL + ch * 32;
         const bool have_docs = p.docs != nullptr;
         const bool docs_vec = (reinterpret_cast<uintptr_t>(p.docs) & 15) == 0;
+        float sm_slope = 0.f, sm_dm = 0.f, sm_w = 0.f;
+        if constexpr (SM != 0) {
+            const int64_t hrow = (int64_t)h * p.T + i;
+            sm_slope = sp.slope ? sp.slope[hrow] : 0.f;
+            if constexpr (SM >= 2) {
+                sm_dm = sp.dmain[hrow];
+                sm_w = sp.width[hrow];
+            }
+        }
         const int doc_i = have_docs ? p.docs[i] : 0;
         // scores are kept unscaled until the exponent: max(x) * c = max(x * c) for c > 0,
         // and a negative scale is folded into the sign of the loaded scores
@@ -329,6 +367,14 @@ __global__ void __launch_bounds__(kThreads, 2) fwd_kernel(const __grid_constant_
             }
             tc_fence_before();
             mbar_arrive(s_free);
+            if constexpr (SM != 0) {
+                // the elementwise terms of the score_mod bias, in unscaled score units
+                const float dbase = (float)(i - (kb * BM + ch * 64));
+#pragma unroll
+                for (int c = 0; c < 64; ++c)
+                    x[c] = fmaf(sp.bias_k,
+                                smod_bias<SM>(dbase - (float)c, sm_slope, sm_dm, sm_w, sp.gate_lambda, sp.gate_itau), x[c]);
+            }
             if (mk != 0) {
                 const int j0 = kb * BM + ch * 64;
                 const int lim = mk == 3 ? -1 : i - j0;  // column c visible iff c <= lim
@@ -447,8 +493,13 @@ __global__ void __launch_bounds__(kThreads, 2) fwd_kernel(const __grid_constant_
 #pragma unroll
             for (int e = 0; e < 4; ++e) dst[e] = make_uint4(w[4 * e], w[4 * e + 1], w[4 * e + 2], w[4 * e + 3]);
         }
-        if (p.lse && ch == 0)
-            p.lse[(int64_t)h * p.T + i] = (ltot > 0.f) ? (m + log2f(ltot)) * 0.69314718055994531f : -INFINITY;
+        if (p.lse && ch == 0) {
+            float lse = (ltot > 0.f) ? (m + log2f(ltot)) * 0.69314718055994531f : -INFINITY;
+            if constexpr (SM != 0) {
+                if (sp.b0) lse -= sp.beta * sp.b0[(int64_t)h * p.T + i];   // the score_mod bias's row constant -beta b0
+            }
+            p.lse[(int64_t)h * p.T + i] = lse;
+        }
     }
     __syncwarp();   // every warp reaches the CTA barrier converged (the producer ran on lane 0 alone)
     tc_fence_before();
@@ -466,7 +517,7 @@ __global__ void __launch_bounds__(kThreads, 2) fwd_kernel(const __grid_constant_
 // ---------------------------------------------------------------------------
 namespace tchost {
 
-template <int DA>
+template <int DA, int SM>
 int launch_fwd(const ScopeAttnArgs &a, cudaStream_t s) {
     using L = tcfwd::Layout<DA>;
     tcfwd::Maps maps;
@@ -492,12 +543,21 @@ int launch_fwd(const ScopeAttnArgs &a, cudaStream_t s) {
     p.o_st = a.o_st;
     p.lse = a.lse;
     p.err = a.err_flag;
+    tcfwd::SmodParams sp;
+    sp.slope = a.slope;
+    sp.dmain = a.delta_main;
+    sp.width = a.width;
+    sp.b0 = a.b0;
+    sp.gate_lambda = a.gate_lambda;
+    sp.gate_itau = (a.gate_tau != 0.f) ? 1.f / a.gate_tau : 0.f;
+    sp.bias_k = a.beta / a.scale;
+    sp.beta = a.beta;
     const size_t smem = L::TOTAL + 1024;
-    if (cudaFuncSetAttribute(tcfwd::fwd_kernel<DA>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
+    if (cudaFuncSetAttribute(tcfwd::fwd_kernel<DA, SM>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
         cudaSuccess)
         return SCOPE_ERR_CUDA;
     dim3 grid(p.QB, a.H);
-    tcfwd::fwd_kernel<DA><<<grid, tcfwd::kThreads, smem, s>>>(maps, p);
+    tcfwd::fwd_kernel<DA, SM><<<grid, tcfwd::kThreads, smem, s>>>(maps, p, sp);
     SCOPE_CHECK_LAUNCH();
     return SCOPE_OK;
 }
@@ -507,9 +567,20 @@ int launch_fwd(const ScopeAttnArgs &a, cudaStream_t s) {
 
 using namespace scope;
 
+// score_mod variant of the kernels: 0 (no score_mod), 1 (no gate), 2 (softplus), 3 (relu)
+int scope_tc_smod(const ScopeAttnArgs &a) {
+    if (a.bias_mode != SCOPE_BIAS_SCORE_MOD) return 0;
+    if (a.gate == SCOPE_GATE_NONE || !(a.gate_lambda > 0.f)) return 1;
+    return a.gate == SCOPE_GATE_SOFTPLUS ? 2 : 3;
+}
+
 bool scope_tc_eligible(const ScopeAttnArgs &a, bool bwd) {
     if (a.dtype != SCOPE_BF16 || a.block_size != 128 || a.D != 64) return false;
-    if (a.bias_mode == SCOPE_BIAS_SCORE_MOD) return false;
+    // score_mod runs here with its Fourier sum in the aug dims (q_aug / k_aug from
+    // scope_qk_aug_prepare without the slope column); without them, on the CUDA cores
+    if (a.bias_mode == SCOPE_BIAS_SCORE_MOD &&
+        (!a.q_aug || !a.k_aug || a.d_aug != (2 * a.K + 15) / 16 * 16 || a.d_aug > 32))
+        return false;
     if (a.bias_mode == SCOPE_BIAS_QK_AUG && a.d_aug != 16 && a.d_aug != 32 && a.d_aug != 48 && a.d_aug != 64)
         return false;
     if (!scope_device_supported() || !tchost::encode_fn()) return false;
@@ -520,18 +591,27 @@ bool scope_tc_eligible(const ScopeAttnArgs &a, bool bwd) {
     const int n = bwd ? 8 : 4;
     for (int i = 0; i < n; ++i)
         if (!tchost::aligned16(ptrs[i]) || strides[2 * i] % 8 || strides[2 * i + 1] % 8) return false;
-    if (a.bias_mode == SCOPE_BIAS_QK_AUG && (!tchost::aligned16(a.q_aug) || !tchost::aligned16(a.k_aug))) return false;
+    if (a.bias_mode != SCOPE_BIAS_NONE && (!tchost::aligned16(a.q_aug) || !tchost::aligned16(a.k_aug))) return false;
     if (bwd && (!a.q_bitmap || !a.lse)) return false;
     return true;
 }
 
 int scope_tc_fwd(const ScopeAttnArgs &a, cudaStream_t s) {
+    const int sm = scope_tc_smod(a);
+    if (sm) {
+        const bool d16 = a.d_aug == 16;
+        switch (sm) {
+            case 1: return d16 ? tchost::launch_fwd<16, 1>(a, s) : tchost::launch_fwd<32, 1>(a, s);
+            case 2: return d16 ? tchost::launch_fwd<16, 2>(a, s) : tchost::launch_fwd<32, 2>(a, s);
+            default: return d16 ? tchost::launch_fwd<16, 3>(a, s) : tchost::launch_fwd<32, 3>(a, s);
+        }
+    }
     switch (a.bias_mode == SCOPE_BIAS_QK_AUG ? a.d_aug : 0) {
-        case 0: return tchost::launch_fwd<0>(a, s);
-        case 16: return tchost::launch_fwd<16>(a, s);
-        case 32: return tchost::launch_fwd<32>(a, s);
-        case 48: return tchost::launch_fwd<48>(a, s);
-        case 64: return tchost::launch_fwd<64>(a, s);
+        case 0: return tchost::launch_fwd<0, 0>(a, s);
+        case 16: return tchost::launch_fwd<16, 0>(a, s);
+        case 32: return tchost::launch_fwd<32, 0>(a, s);
+        case 48: return tchost::launch_fwd<48, 0>(a, s);
+        case 64: return tchost::launch_fwd<64, 0>(a, s);
         default: return SCOPE_ERR_INVALID;
     }
 }

@@ -80,10 +80,20 @@ constexpr float kLog2e = 1.4426950408889634f;
 __host__ __device__ constexpr uint32_t align1k(uint32_t x) { return (x + 1023u) & ~1023u; }
 
 // ------------------------------------------------------------------ prep
+// score_mod mode: the forward's lse includes the row constant -beta b0, which
+// the recomputed scores leave out, so it is added back here; the per-row slope,
+// Δ_main and width are copied next to each other (zeros for absent terms) for
+// the producer's per-tile bulk loads.
+struct PrepSmod {
+    const float *b0, *slope, *dmain, *width;
+    float beta;
+    float *par;   // [3][H*T]: slope, Δ_main, width
+};
+
 __global__ void prep_kernel(const __nv_bfloat16 *__restrict__ out, int64_t o_sh, int64_t o_st,
                             const __nv_bfloat16 *__restrict__ dout, int64_t do_sh, int64_t do_st,
                             const float *__restrict__ lse, int H, int T, float *__restrict__ delta,
-                            float *__restrict__ lse2) {
+                            float *__restrict__ lse2, const PrepSmod sm) {
     int64_t row = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (row >= (int64_t)H * T) return;
     const int h = (int)(row / T), t = (int)(row % T);
@@ -103,7 +113,14 @@ __global__ void prep_kernel(const __nv_bfloat16 *__restrict__ out, int64_t o_sh,
         }
     }
     delta[row] = s;
-    const float l = lse[row];
+    float l = lse[row];
+    if (sm.par) {
+        if (sm.b0 && l != -INFINITY) l += sm.beta * sm.b0[row];
+        const int64_t n = (int64_t)H * T;
+        sm.par[row] = sm.slope ? sm.slope[row] : 0.f;
+        sm.par[n + row] = sm.dmain ? sm.dmain[row] : 0.f;
+        sm.par[2 * n + row] = sm.width ? sm.width[row] : 0.f;
+    }
     lse2[row] = (l == -INFINITY) ? INFINITY : l * kLog2e;   // rows that saw nothing get P = 0
 }
 
@@ -126,8 +143,13 @@ struct Params {
     __nv_bfloat16 *dk, *dv;
     int64_t dk_sh, dk_st, dv_sh, dv_st;
     float *dq_acc;            // [H, T, 64 + DA] fp32, zeroed before the launch
-    float *slope_acc;         // [H, T] fp32 (qk_aug with slope), zeroed
+    float *slope_acc;         // [H, T] fp32 (qk_aug with slope; score_mod: sum_j dS_ij (i - j)), zeroed
     float s_aug;
+    // score_mod: per-row slope, Δ_main, width [3][H*T] (staged per tile), the gate
+    // sums [H, T] (zeroed), beta*log2(e), the gate's lambda and 1/tau
+    const float *par;
+    float *dm_acc, *w_acc;
+    float bias2, gate_lambda, gate_itau;
     Plan plan;
     int32_t *err;
 };
@@ -249,19 +271,51 @@ __device__ __forceinline__ int tile_mask_kind(int qb, int kb, bool have_docs, co
     return same_doc ? MASK_CAUSAL : MASK_DOCS;
 }
 
+// Bias of the score_mod mode beyond the Fourier sum, for Δ = i - j
+// (scoped_medium.py:425-457): slope Δ - lambda gate((|Δ - Δ_main| - width) / tau).
+// SM: 0 off, 1 no gate, 2 softplus gate (torch's, threshold 20), 3 relu gate.
+template <int SM>
+__device__ __forceinline__ float smod_bias(float dl, float slope, float dm, float w, float lam, float itau) {
+    float b = slope * dl;
+    if constexpr (SM >= 2) {
+        const float u = (fabsf(dl - dm) - w) * itau;
+        float g;
+        if constexpr (SM == 3) {
+            g = fmaxf(u, 0.f);
+        } else {
+            g = u > 20.f ? u : 0.69314718055994531f * lg2(1.f + ex2(u * kLog2e));
+        }
+        b = fmaf(-lam, g, b);
+    }
+    return b;
+}
+
+// score_mod parameters of the 32 q rows of a thread's columns (staged per tile)
+struct SmodCols {
+    const float *slope, *dm, *w;
+};
+
 // P for 16 columns, thread = kv row j: P = exp2(S * scale*log2e - lse2), zero
 // where the element is masked (column e visible iff e >= lim, and in j's
 // document on boundary tiles).
-template <bool MASKED>
+template <bool MASKED, int SM = 0>
 __device__ __forceinline__ void p_piece(float *s, const float4 *LS, uint64_t c2, int mk, int lim,
-                                        const int32_t *docs, int i0, int doc_j) {
+                                        const int32_t *docs, int i0, int doc_j, const SmodCols &sc = SmodCols{},
+                                        float bias2 = 0.f, float lam = 0.f, float itau = 0.f) {
 #pragma unroll
     for (int e4 = 0; e4 < 4; ++e4) {
         const float4 l4 = LS[e4];
 #pragma unroll
         for (int q2 = 0; q2 < 2; ++q2) {
             const int e = e4 * 4 + 2 * q2;
-            const uint64_t nl = q2 ? f2_pack(-l4.z, -l4.w) : f2_pack(-l4.x, -l4.y);
+            uint64_t nl = q2 ? f2_pack(-l4.z, -l4.w) : f2_pack(-l4.x, -l4.y);
+            if constexpr (SM != 0) {
+                // + beta log2(e) (slope Δ - lambda gate), Δ = i - j = e - lim
+                const float2 n2 = f2_unpack(nl);
+                const float b0v = smod_bias<SM>((float)(e - lim), sc.slope[e], sc.dm[e], sc.w[e], lam, itau);
+                const float b1v = smod_bias<SM>((float)(e + 1 - lim), sc.slope[e + 1], sc.dm[e + 1], sc.w[e + 1], lam, itau);
+                nl = f2_pack(fmaf(bias2, b0v, n2.x), fmaf(bias2, b1v, n2.y));
+            }
             const float2 x = f2_unpack(ffma2(f2_pack(s[e], s[e + 1]), c2, nl));
             float p0 = ex2(x.x), p1 = ex2(x.y);
             if (MASKED) {
@@ -341,7 +395,7 @@ __device__ __forceinline__ int next_bit(const uint32_t *row, int words, int &w, 
 // operand of N = 64 + DA for dQ and K-major A operands (one per K step) for S^T.
 // dS is stored MN-major (128-byte swizzle, two 64-column halves 16 KiB apart),
 // the A operand of dQ = dS [K | K_aug].
-template <int DA>
+template <int DA, int SM = 0>
 struct FL {
     static constexpr int NA = DA / 16;
     static constexpr int NKA = 4 + NA;                        // K + K_aug sub-tiles
@@ -351,8 +405,9 @@ struct FL {
     static constexpr uint32_t DS = RESB;                      // dS tile, 32 KiB
     static constexpr uint32_t STAGE0 = DS + 2 * TILE;
     static constexpr uint32_t SQ = 0, SQA = TILE, SDO = align1k(TILE + NA * ATILE), SLSE = SDO + TILE,
-                              SDEL = SLSE + 512;
-    static constexpr uint32_t STAGE = align1k(SDEL + 512);
+                              SDEL = SLSE + 512, SPAR = SDEL + 512;   // SPAR: score_mod slope, Δ_main, width
+    static constexpr uint32_t PAR_BYTES = SM ? 3 * 512 : 0;
+    static constexpr uint32_t STAGE = align1k(SPAR + PAR_BYTES);
     static constexpr uint32_t EXTRA = 1024 + 1024;            // barriers, base alignment
     static constexpr uint32_t DRN_BYTES = 4 * kDrainBoxes * 2048;   // drain staging: 32 x 16 fp32 boxes
     static constexpr int NST = STAGE0 + 4 * STAGE + DRN_BYTES + EXTRA <= kSmemBudget
@@ -361,16 +416,16 @@ struct FL {
     static constexpr uint32_t DRN = STAGE0 + NST * STAGE;       // 1024-aligned (STAGE0, STAGE are)
     static constexpr uint32_t BAR = DRN + DRN_BYTES;
     static constexpr uint32_t RES_BYTES = NKA * ATILE + TILE;
-    static constexpr uint32_t Q_BYTES = 2 * TILE + NA * ATILE + 1024;
+    static constexpr uint32_t Q_BYTES = 2 * TILE + NA * ATILE + 1024 + PAR_BYTES;
     static constexpr uint32_t TOTAL = BAR + sizeof(Bars);
     static constexpr int DQN = 64 + DA;                       // dQ accumulator columns
     static_assert(TOTAL + 1024 <= kSmemBudget, "shared memory");
     static_assert(DQ + DQN <= kTmemCols, "tensor memory");
 };
 
-template <int DA, bool SLOPE>
+template <int DA, bool SLOPE, int SM>
 __global__ void __launch_bounds__(kThreads, 1) dkvq_kernel(const __grid_constant__ Maps maps, const Params p) {
-    using L = FL<DA>;
+    using L = FL<DA, SM>;
     constexpr int NA = L::NA, NST = L::NST;
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
@@ -446,6 +501,12 @@ __global__ void __launch_bounds__(kThreads, 1) dkvq_kernel(const __grid_constant
                     const int64_t off = (int64_t)h * p.T + (int64_t)qb * BM;
                     bulk_load(sb + L::SLSE, p.lse2 + off, 512, &B.full[st]);
                     bulk_load(sb + L::SDEL, p.delta + off, 512, &B.full[st]);
+                    if constexpr (SM != 0) {
+                        const int64_t n = (int64_t)p.H * p.T;
+#pragma unroll
+                        for (int a = 0; a < 3; ++a)
+                            bulk_load(sb + L::SPAR + a * 512, p.par + a * n + off, 512, &B.full[st]);
+                    }
                     ++gt;
                 }
                 if (ok && t < nq) {   // the plan promised more q blocks than the bitmap row holds
@@ -616,12 +677,17 @@ __global__ void __launch_bounds__(kThreads, 1) dkvq_kernel(const __grid_constant
 #pragma unroll
                     for (int e = 0; e < 32; ++e) s[e] = __uint_as_float(r[e]);
                 }
+                // score_mod: slope, Δ_main, width of this thread's 32 q rows
+                const float *spar = reinterpret_cast<const float *>(sbp + L::SPAR) + qc * 32;
+                const SmodCols sc0{spar, spar + 128, spar + 256}, sc1{spar + 16, spar + 144, spar + 272};
                 if (mk == MASK_FULL) {
-                    p_piece<false>(s, LS, c2, mk, lim, p.docs, i0, doc_j);
-                    p_piece<false>(s + 16, LS + 4, c2, mk, lim - 16, p.docs, i0 + 16, doc_j);
+                    p_piece<false, SM>(s, LS, c2, mk, lim, p.docs, i0, doc_j, sc0, p.bias2, p.gate_lambda, p.gate_itau);
+                    p_piece<false, SM>(s + 16, LS + 4, c2, mk, lim - 16, p.docs, i0 + 16, doc_j, sc1, p.bias2,
+                                       p.gate_lambda, p.gate_itau);
                 } else {
-                    p_piece<true>(s, LS, c2, mk, lim, p.docs, i0, doc_j);
-                    p_piece<true>(s + 16, LS + 4, c2, mk, lim - 16, p.docs, i0 + 16, doc_j);
+                    p_piece<true, SM>(s, LS, c2, mk, lim, p.docs, i0, doc_j, sc0, p.bias2, p.gate_lambda, p.gate_itau);
+                    p_piece<true, SM>(s + 16, LS + 4, c2, mk, lim - 16, p.docs, i0 + 16, doc_j, sc1, p.bias2,
+                                      p.gate_lambda, p.gate_itau);
                 }
                 {
                     uint32_t w[16];
@@ -666,6 +732,43 @@ __global__ void __launch_bounds__(kThreads, 1) dkvq_kernel(const __grid_constant
                         }
                         const float col = warp_column_sums16(v);
                         if (lane < 16) atomicAdd(p.slope_acc + (int64_t)h * p.T + i0 + 16 * cc + lane, col);
+                    }
+                }
+                if constexpr (SM != 0) {
+                    // gradients of the per-row score_mod terms, summed over this tile's kv rows
+                    // (the warp's 32 lanes) per q row: dS Δ for the slope; for the gate
+                    // dS gate'(u) sign(Δ - Δ_main) and dS gate'(u), scaled in the finish kernel
+                    const int64_t rowq = (int64_t)h * p.T + i0;
+#pragma unroll
+                    for (int cc = 0; cc < 2; ++cc) {
+                        float v[16];
+#pragma unroll
+                        for (int e = 0; e < 16; ++e) v[e] = d[16 * cc + e] * (float)(16 * cc + e - lim);
+                        const float col = warp_column_sums16(v);
+                        if (lane < 16) atomicAdd(p.slope_acc + rowq + 16 * cc + lane, col);
+                        if constexpr (SM >= 2) {
+                            float vg[16], vd[16];
+#pragma unroll
+                            for (int e = 0; e < 16; ++e) {
+                                const int ee = 16 * cc + e;
+                                const float dl = (float)(ee - lim), dm = spar[128 + ee];
+                                const float u = (fabsf(dl - dm) - spar[256 + ee]) * p.gate_itau;
+                                float gp;
+                                if constexpr (SM == 3) {
+                                    gp = u > 0.f ? 1.f : 0.f;
+                                } else {
+                                    gp = u > 20.f ? 1.f : __frcp_rn(1.f + ex2(-u * kLog2e));
+                                }
+                                vg[e] = d[ee] * gp;
+                                vd[e] = dl > dm ? vg[e] : (dl < dm ? -vg[e] : 0.f);
+                            }
+                            const float cg = warp_column_sums16(vg);
+                            const float cd = warp_column_sums16(vd);
+                            if (lane < 16) {
+                                atomicAdd(p.w_acc + rowq + 16 * cc + lane, cg);
+                                atomicAdd(p.dm_acc + rowq + 16 * cc + lane, cd);
+                            }
+                        }
                     }
                 }
                 {
@@ -903,6 +1006,12 @@ struct FinishParams {
     float *dcoeff_cos, *dcoeff_sin;
     const float *slope_acc;
     float *dslope;
+    // score_mod: dslope = beta * sum dS (i - j); dΔ_main / dwidth = beta lambda / tau * the
+    // gate sums; db0 = 0 (a per-row constant of the scores: softmax is invariant to it)
+    int smod;
+    float beta, gate_k;
+    const float *dm_acc, *w_acc;
+    float *ddelta_main, *dwidth, *db0;
 };
 
 __global__ void finish_kernel(const FinishParams f) {
@@ -924,7 +1033,16 @@ __global__ void finish_kernel(const FinishParams f) {
             f.dcoeff_sin[row * f.K + k] = f.s_aug * (g0 * sv - g1 * cv);
         }
     }
-    if (lane == 0 && f.dslope) f.dslope[row] = -f.s_aug * (f.slope_acc[row] * f.scale);
+    if (lane == 0) {
+        if (f.smod) {
+            if (f.dslope) f.dslope[row] = f.beta * f.slope_acc[row];
+            if (f.ddelta_main) f.ddelta_main[row] = f.gate_k * f.dm_acc[row];
+            if (f.dwidth) f.dwidth[row] = f.gate_k * f.w_acc[row];
+            if (f.db0) f.db0[row] = 0.f;
+        } else if (f.dslope) {
+            f.dslope[row] = -f.s_aug * (f.slope_acc[row] * f.scale);
+        }
+    }
 }
 
 }  // namespace tcbwd
@@ -935,11 +1053,13 @@ namespace tchost {
 // slot partials, the fp32 dQ accumulator [H, T, 64 + DA] and the fp32 slope
 // sums [H, T].
 struct BwdWorkspace {
-    size_t delta, lse2, nq, items, item_slot, n_items, slot_chunks, slot_done, partial, dq_acc, slope_acc, total;
+    size_t delta, lse2, nq, items, item_slot, n_items, slot_chunks, slot_done, partial, par, dq_acc, slope_acc,
+        dm_acc, w_acc, total;
     int max_items, dq_ld;
 };
 
-BwdWorkspace bwd_workspace(int H, int T, int block_size, int d_aug) {
+// smod: the score_mod mode's per-row parameters [3][H*T] and gate sums [2][H*T]
+BwdWorkspace bwd_workspace(int H, int T, int block_size, int d_aug, bool smod) {
     auto up = [](size_t x) { return (x + 255) & ~(size_t)255; };
     BwdWorkspace w;
     const int QB = T / block_size;
@@ -955,25 +1075,38 @@ BwdWorkspace bwd_workspace(int H, int T, int block_size, int d_aug) {
     w.slot_chunks = o; o += up((size_t)tcbwd::kSlotCap * 4);
     w.slot_done = o;   o += up((size_t)tcbwd::kSlotCap * 4);
     w.partial = o;     o += up((size_t)tcbwd::kSlotCap * 128 * 128 * 4);
+    w.par = o;         o += smod ? up((size_t)3 * H * T * 4) : 0;
     w.dq_acc = o;      o += up((size_t)H * T * w.dq_ld * 4);
     w.slope_acc = o;   o += up((size_t)H * T * 4);
+    w.dm_acc = o;      o += smod ? up((size_t)H * T * 4) : 0;
+    w.w_acc = o;       o += smod ? up((size_t)H * T * 4) : 0;
     w.total = o;
     return w;
 }
 
-template <int DA, bool SLOPE>
+template <int DA, bool SLOPE, int SM>
 int launch_bwd(const ScopeAttnArgs &a, cudaStream_t s) {
     const int QB = a.T / 128;
-    const BwdWorkspace ws = bwd_workspace(a.H, a.T, 128, DA);
+    const BwdWorkspace ws = bwd_workspace(a.H, a.T, 128, DA, SM != 0);
     uint8_t *base = reinterpret_cast<uint8_t *>(a.workspace);
     float *delta = reinterpret_cast<float *>(base + ws.delta);
     float *lse2 = reinterpret_cast<float *>(base + ws.lse2);
     float *dq_acc = reinterpret_cast<float *>(base + ws.dq_acc);
     float *slope_acc = reinterpret_cast<float *>(base + ws.slope_acc);
     const int64_t rows = (int64_t)a.H * a.T;
+    tcbwd::PrepSmod psm;
+    std::memset(&psm, 0, sizeof(psm));
+    if (SM) {
+        psm.b0 = a.b0;
+        psm.slope = a.slope;
+        psm.dmain = SM >= 2 ? a.delta_main : nullptr;
+        psm.width = SM >= 2 ? a.width : nullptr;
+        psm.beta = a.beta;
+        psm.par = reinterpret_cast<float *>(base + ws.par);
+    }
     tcbwd::prep_kernel<<<(unsigned)((rows + 255) / 256), 256, 0, s>>>(
         reinterpret_cast<const __nv_bfloat16 *>(a.out), a.o_sh, a.o_st, reinterpret_cast<const __nv_bfloat16 *>(a.dout),
-        a.do_sh, a.do_st, a.lse, a.H, a.T, delta, lse2);
+        a.do_sh, a.do_st, a.lse, a.H, a.T, delta, lse2, psm);
     SCOPE_CHECK_LAUNCH();
 
     // work plan: long q lists are cut into chunks
@@ -997,7 +1130,7 @@ int launch_bwd(const ScopeAttnArgs &a, cudaStream_t s) {
     SCOPE_CHECK_LAUNCH();
     if (cudaMemsetAsync(plan.partial, 0, (size_t)tcbwd::kSlotCap * 128 * 128 * 4, s) != cudaSuccess)
         return SCOPE_ERR_CUDA;
-    // the dQ accumulator and the slope sums start at zero (adjacent in the workspace)
+    // the dQ accumulator, the slope and gate sums start at zero (adjacent in the workspace)
     if (cudaMemsetAsync(dq_acc, 0, ws.total - ws.dq_acc, s) != cudaSuccess) return SCOPE_ERR_CUDA;
 
     tcbwd::Maps maps;
@@ -1033,21 +1166,29 @@ int launch_bwd(const ScopeAttnArgs &a, cudaStream_t s) {
     p.dq_acc = dq_acc;
     p.slope_acc = slope_acc;
     p.s_aug = (float)sqrt((double)a.beta / (double)a.scale);
+    if (SM) {
+        p.par = psm.par;
+        p.dm_acc = reinterpret_cast<float *>(base + ws.dm_acc);
+        p.w_acc = reinterpret_cast<float *>(base + ws.w_acc);
+        p.bias2 = a.beta * 1.4426950408889634f;
+        p.gate_lambda = a.gate_lambda;
+        p.gate_itau = (a.gate_tau != 0.f) ? 1.f / a.gate_tau : 0.f;
+    }
     p.plan = plan;
     p.err = a.err_flag;
 
     // each CTA takes all 512 TMEM columns, so ask for enough shared memory that a
     // second CTA never lands on the SM just to wait inside tcgen05.alloc
     const size_t kOneCtaPerSm = 120 * 1024;
-    const size_t smem = std::max<size_t>(tcbwd::FL<DA>::TOTAL + 1024, kOneCtaPerSm);
-    if (cudaFuncSetAttribute(tcbwd::dkvq_kernel<DA, SLOPE>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
-        cudaSuccess)
+    const size_t smem = std::max<size_t>(tcbwd::FL<DA, SM>::TOTAL + 1024, kOneCtaPerSm);
+    if (cudaFuncSetAttribute(tcbwd::dkvq_kernel<DA, SLOPE, SM>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)smem) != cudaSuccess)
         return SCOPE_ERR_CUDA;
     int dev = 0, n_sm = 148;
     if (cudaGetDevice(&dev) != cudaSuccess || cudaDeviceGetAttribute(&n_sm, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
         return SCOPE_ERR_CUDA;
     // persistent: one CTA per SM walks the plan's items
-    tcbwd::dkvq_kernel<DA, SLOPE><<<std::min(ws.max_items, n_sm), tcbwd::kThreads, smem, s>>>(maps, p);
+    tcbwd::dkvq_kernel<DA, SLOPE, SM><<<std::min(ws.max_items, n_sm), tcbwd::kThreads, smem, s>>>(maps, p);
     SCOPE_CHECK_LAUNCH();
 
     tcbwd::FinishParams f;
@@ -1073,6 +1214,18 @@ int launch_bwd(const ScopeAttnArgs &a, cudaStream_t s) {
             f.dslope = a.dslope;
         }
     }
+    if (SM) {
+        f.smod = 1;
+        f.beta = a.beta;
+        f.gate_k = a.beta * p.gate_lambda * p.gate_itau;
+        f.slope_acc = slope_acc;
+        f.dm_acc = p.dm_acc;
+        f.w_acc = p.w_acc;
+        f.dslope = a.slope ? a.dslope : nullptr;
+        f.ddelta_main = SM >= 2 ? a.ddelta_main : nullptr;
+        f.dwidth = SM >= 2 ? a.dwidth : nullptr;
+        f.db0 = a.b0 ? a.db0 : nullptr;
+    }
     tcbwd::finish_kernel<<<(unsigned)((rows + 7) / 8), 256, 0, s>>>(f);
     SCOPE_CHECK_LAUNCH();
     return SCOPE_OK;
@@ -1081,19 +1234,30 @@ int launch_bwd(const ScopeAttnArgs &a, cudaStream_t s) {
 }  // namespace tchost
 }  // namespace scope
 
-size_t scope_bwd_workspace_bytes(int H, int T, int block_size, int d_aug) {
-    return scope::tchost::bwd_workspace(H, T, block_size, d_aug).total;
+size_t scope_bwd_workspace_bytes(int H, int T, int block_size, int d_aug, bool smod) {
+    return scope::tchost::bwd_workspace(H, T, block_size, d_aug, smod).total;
 }
+
+int scope_tc_smod(const ScopeAttnArgs &a);
 
 int scope_tc_bwd(const ScopeAttnArgs &a, cudaStream_t s) {
     using namespace scope::tchost;
+    const int sm = scope_tc_smod(a);
+    if (sm) {
+        const bool d16 = a.d_aug == 16;
+        switch (sm) {
+            case 1: return d16 ? launch_bwd<16, false, 1>(a, s) : launch_bwd<32, false, 1>(a, s);
+            case 2: return d16 ? launch_bwd<16, false, 2>(a, s) : launch_bwd<32, false, 2>(a, s);
+            default: return d16 ? launch_bwd<16, false, 3>(a, s) : launch_bwd<32, false, 3>(a, s);
+        }
+    }
     const bool slope = a.bias_mode == SCOPE_BIAS_QK_AUG && a.slope && a.dslope && a.dcoeff_cos;
     switch (a.bias_mode == SCOPE_BIAS_QK_AUG ? a.d_aug : 0) {
-        case 0: return launch_bwd<0, false>(a, s);
-        case 16: return slope ? launch_bwd<16, true>(a, s) : launch_bwd<16, false>(a, s);
-        case 32: return slope ? launch_bwd<32, true>(a, s) : launch_bwd<32, false>(a, s);
-        case 48: return slope ? launch_bwd<48, true>(a, s) : launch_bwd<48, false>(a, s);
-        case 64: return slope ? launch_bwd<64, true>(a, s) : launch_bwd<64, false>(a, s);
+        case 0: return launch_bwd<0, false, 0>(a, s);
+        case 16: return slope ? launch_bwd<16, true, 0>(a, s) : launch_bwd<16, false, 0>(a, s);
+        case 32: return slope ? launch_bwd<32, true, 0>(a, s) : launch_bwd<32, false, 0>(a, s);
+        case 48: return slope ? launch_bwd<48, true, 0>(a, s) : launch_bwd<48, false, 0>(a, s);
+        case 64: return slope ? launch_bwd<64, true, 0>(a, s) : launch_bwd<64, false, 0>(a, s);
         default: return SCOPE_ERR_INVALID;
     }
 }

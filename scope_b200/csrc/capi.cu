@@ -1,8 +1,9 @@
 // extern "C" attention entry points: argument validation and dispatch.
 //
-// bf16 inputs with the qk_aug (or no) bias and 128-token blocks run on the
-// tcgen05 tensor-core kernels; float32 inputs and the exact score_mod
-// closure run on the CUDA-core kernels.  Nothing here falls back silently: a
+// bf16 inputs with 128-token blocks run on the tcgen05 tensor-core kernels: no
+// bias, the qk_aug bias, and the score_mod closure when its Fourier sum comes
+// with augmented dims (q_aug / k_aug); float32 inputs, and score_mod without
+// them, run on the CUDA-core kernels.  Nothing here falls back silently: a
 // combination neither path supports returns an error status.
 #include <atomic>
 #include <cmath>
@@ -16,7 +17,7 @@ int scope_simt_bwd(const ScopeAttnArgs &a, cudaStream_t s);
 int scope_tc_fwd(const ScopeAttnArgs &a, cudaStream_t s);
 int scope_tc_bwd(const ScopeAttnArgs &a, cudaStream_t s);
 bool scope_tc_eligible(const ScopeAttnArgs &a, bool bwd);
-size_t scope_bwd_workspace_bytes(int H, int T, int block_size, int d_aug);
+size_t scope_bwd_workspace_bytes(int H, int T, int block_size, int d_aug, bool smod);
 
 namespace {
 
@@ -33,7 +34,9 @@ int validate(const ScopeAttnArgs &a, bool bwd) {
             break;
         case SCOPE_BIAS_SCORE_MOD:
             if (a.K < 1 || a.K > 16 || !a.coeff_cos || !a.coeff_sin || !a.cos_tab || !a.sin_tab) return SCOPE_ERR_INVALID;
-            if (a.tab_len < a.T || a.d_aug != 0) return SCOPE_ERR_INVALID;
+            if (a.tab_len < a.T) return SCOPE_ERR_INVALID;
+            // d_aug 0: CUDA cores; else the Fourier dims from scope_qk_aug_prepare (no slope column)
+            if (a.d_aug != 0 && (!a.q_aug || !a.k_aug || a.d_aug != (2 * a.K + 15) / 16 * 16)) return SCOPE_ERR_INVALID;
             if (a.gate != SCOPE_GATE_NONE && (!a.delta_main || !a.width || !(a.gate_tau != 0.f))) return SCOPE_ERR_INVALID;
             if (a.gate < 0 || a.gate > 2) return SCOPE_ERR_INVALID;
             break;
@@ -60,7 +63,9 @@ extern "C" size_t scope_workspace_bytes(const ScopeAttnArgs *a) {
     if (!a || a->H <= 0 || a->T <= 0 || a->block_size <= 0 || a->T % a->block_size) return 0;
     // delta_i = rowsum(dO * O), lse_i * log2(e) (float32 [H, T] each), the dK/dV work plan and
     // the fp32 dQ accumulator of the tensor-core backward
-    return scope_bwd_workspace_bytes(a->H, a->T, a->block_size, a->bias_mode == SCOPE_BIAS_QK_AUG ? a->d_aug : 0);
+    const bool aug = a->bias_mode == SCOPE_BIAS_QK_AUG || (a->bias_mode == SCOPE_BIAS_SCORE_MOD && a->d_aug > 0);
+    return scope_bwd_workspace_bytes(a->H, a->T, a->block_size, aug ? a->d_aug : 0,
+                                     a->bias_mode == SCOPE_BIAS_SCORE_MOD && a->d_aug > 0);
 }
 
 extern "C" int scope_attn_fwd(const ScopeAttnArgs *args, scope_stream_t stream) {

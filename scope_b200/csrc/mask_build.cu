@@ -292,7 +292,210 @@ __device__ void select_row_regs(const ScopeMaskArgs &a, int h, int qb, int lane,
     __syncwarp();
 }
 
-__global__ void __launch_bounds__(kWarps * 32) build_kernel(const BuildParams P) {
+// The same selection by a threshold filter, for rows of at most 32 * 32
+// candidates (lane l holds kb = 128 g + 4 l + c, g < 8, c < 4).  The M-th
+// largest of the 32 lane maxima is a lower bound for the M-th best score
+// (those M lane maxima are M distinct candidates), so only candidates scoring
+// at least that can win.  They are compacted into shared memory and one warp
+// bitonic sort under the same order as better() ranks them.  Returns false,
+// leaving cen untouched, when more than 32 candidates pass or a score is NaN:
+// the caller then runs select_row_regs, so the result is the same either way.
+__device__ bool select_row_thr(const ScopeMaskArgs &a, int h, int qb, int lane, int *cen, float *sv, int *si) {
+    const float *lrow = a.sel_logits + (int64_t)h * a.sel_head_stride + (int64_t)qb * a.sel_row_stride;
+    const float *grow = a.sel_gumbel + (int64_t)h * a.sel_head_stride + (int64_t)qb * a.sel_row_stride;
+    const Divider tau(a.sel_tau);
+    const int n = qb + 1, M = a.M;
+    const bool vec = (a.QB % 4 == 0) && (a.sel_row_stride % 4 == 0) && (a.sel_head_stride % 4 == 0) &&
+                     ((reinterpret_cast<uintptr_t>(a.sel_logits) & 15) == 0) &&
+                     ((reinterpret_cast<uintptr_t>(a.sel_gumbel) & 15) == 0);
+    float sc[32];
+#pragma unroll
+    for (int g = 0; g < 8; ++g) {
+        const int b = 128 * g + 4 * lane;
+        float lv[4] = {0.f, 0.f, 0.f, 0.f}, gv[4] = {0.f, 0.f, 0.f, 0.f};
+        if (b < n) {
+            if (vec) {
+                const float4 l4 = __ldg(reinterpret_cast<const float4 *>(lrow + b));
+                const float4 g4 = __ldg(reinterpret_cast<const float4 *>(grow + b));
+                lv[0] = l4.x; lv[1] = l4.y; lv[2] = l4.z; lv[3] = l4.w;
+                gv[0] = g4.x; gv[1] = g4.y; gv[2] = g4.z; gv[3] = g4.w;
+            } else {
+#pragma unroll
+                for (int c = 0; c < 4; ++c)
+                    if (b + c < n) {
+                        lv[c] = __ldg(lrow + b + c);
+                        gv[c] = __ldg(grow + b + c);
+                    }
+            }
+        }
+#pragma unroll
+        for (int c = 0; c < 4; ++c) sc[4 * g + c] = (b + c < n) ? __fadd_rn(tau(lv[c]), gv[c]) : -INFINITY;
+    }
+    // lane maximum, and a NaN probe (a NaN anywhere makes the sum NaN)
+    float lm = sc[0], sum = 0.f;
+#pragma unroll
+    for (int e = 1; e < 32; ++e) lm = fmaxf(lm, sc[e]);
+#pragma unroll
+    for (int e = 0; e < 32; ++e) sum += (sc[e] == -INFINITY) ? 0.f : sc[e];
+    if (__any_sync(0xffffffffu, isnan(sum))) return false;
+    // the M-th largest lane maximum: a descending bitonic sort of the 32 values
+    float t = lm;
+#pragma unroll
+    for (int k = 2; k <= 32; k <<= 1) {
+#pragma unroll
+        for (int j = k >> 1; j > 0; j >>= 1) {
+            const float o = __shfl_xor_sync(0xffffffffu, t, j);
+            const bool desc = (lane & k) == 0, lower = (lane & j) == 0;
+            t = (lower == desc) ? fmaxf(t, o) : fminf(t, o);
+        }
+    }
+    const float thr = __shfl_sync(0xffffffffu, t, M - 1);
+    // the candidates that can win, compacted in lane order
+    uint32_t hit = 0u;
+#pragma unroll
+    for (int e = 0; e < 32; ++e) {
+        const int kb = 128 * (e >> 2) + 4 * lane + (e & 3);
+        if (kb < n && sc[e] >= thr) hit |= 1u << e;
+    }
+    const int cnt = __popc(hit);
+    int pre = cnt;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const int y = __shfl_up_sync(0xffffffffu, pre, o);
+        if (lane >= o) pre += y;
+    }
+    const int total = __shfl_sync(0xffffffffu, pre, 31);
+    if (total > 32) return false;
+    int pos = pre - cnt;
+#pragma unroll
+    for (int e = 0; e < 32; ++e) {
+        if ((hit >> e) & 1u) {
+            sv[pos] = sc[e];
+            si[pos] = 128 * (e >> 2) + 4 * lane + (e & 3);
+            ++pos;
+        }
+    }
+    __syncwarp();
+    float v = lane < total ? sv[lane] : -INFINITY;
+    int id = lane < total ? si[lane] : INT_MAX;
+    __syncwarp();
+    // warp bitonic sort, best first under better()
+#pragma unroll
+    for (int k = 2; k <= 32; k <<= 1) {
+#pragma unroll
+        for (int j = k >> 1; j > 0; j >>= 1) {
+            const float ov = __shfl_xor_sync(0xffffffffu, v, j);
+            const int oi = __shfl_xor_sync(0xffffffffu, id, j);
+            const bool desc = (lane & k) == 0, lower = (lane & j) == 0;
+            if ((lower == desc) ? better(ov, oi, v, id) : better(v, id, ov, oi)) {
+                v = ov;
+                id = oi;
+            }
+        }
+    }
+    if (lane < M) cen[lane] = (id == INT_MAX) ? qb : id;
+    __syncwarp();
+    return true;
+}
+
+// Ascending bitonic sort of 32 E ints held E per lane (element i = E lane + k):
+// partners closer than E are in the same lane, the others one shuffle away.
+template <int E>
+__device__ __forceinline__ void warp_sort_regs(int (&v)[E], int lane) {
+#pragma unroll
+    for (int k = 2; k <= 32 * E; k <<= 1) {
+#pragma unroll
+        for (int j = k >> 1; j > 0; j >>= 1) {
+            if (j < E) {
+#pragma unroll
+                for (int q = 0; q < E; ++q) {
+                    const int pq = q ^ j;
+                    if (pq > q) {
+                        const bool asc = ((E * lane + q) & k) == 0;
+                        const int lo = min(v[q], v[pq]), hi = max(v[q], v[pq]);
+                        v[q] = asc ? lo : hi;
+                        v[pq] = asc ? hi : lo;
+                    }
+                }
+            } else {
+                const int lj = j / E;
+                const bool lower = (lane & lj) == 0;
+#pragma unroll
+                for (int q = 0; q < E; ++q) {
+                    const int o = __shfl_xor_sync(0xffffffffu, v[q], lj);
+                    const bool asc = ((E * lane + q) & k) == 0;
+                    v[q] = (lower == asc) ? min(v[q], o) : max(v[q], o);
+                }
+            }
+        }
+    }
+}
+
+// The window entries of a row (model/attn_bias.py:786-825): entry pos of the
+// local blocks, the M pointer windows and the global blocks.
+__device__ __forceinline__ int window_entry(const ScopeMaskArgs &a, int pos, int qb, int dsp, int dsl, const int *cen,
+                                            const int *rad) {
+    const int L = a.local_blocks, M = a.M, p = a.half_blocks, span = 2 * p + 1;
+    if (pos < L) return max(max(qb - pos, 0), dsl);
+    if (pos < L + M * span) {
+        const int q = pos - L, m = q / span, c = cen[m];
+        if (p > 0) {
+            const int o = q - m * span - p;
+            int w = min(max(c + o, 0), a.QB - 1);
+            w = max(min(w, qb), dsp);
+            return (abs(o) <= rad[m]) ? w : c;
+        }
+        return c;
+    }
+    const int i = pos - L - M * span;
+    const int g = min(dsp + i, qb);
+    return (i < a.global_active) ? g : qb;
+}
+
+// Window entries sorted and packed in registers (rows of at most 32 E
+// entries): unique blocks ascending, then the repeats ascending, into outl;
+// returns the number of unique blocks.
+template <int E>
+__device__ int pack_row_regs(const ScopeMaskArgs &a, int n, int qb, int dsp, int dsl, const int *cen, const int *rad,
+                             int lane, int *outl) {
+    int v[E];
+#pragma unroll
+    for (int q = 0; q < E; ++q) {
+        const int pos = E * lane + q;
+        v[q] = pos < n ? window_entry(a, pos, qb, dsp, dsl, cen, rad) : INT_MAX;   // INT_MAX sorts past every block
+    }
+    warp_sort_regs<E>(v, lane);
+    const int prev_lane_last = __shfl_up_sync(0xffffffffu, v[E - 1], 1);
+    bool first[E];
+    int cnt = 0;
+#pragma unroll
+    for (int q = 0; q < E; ++q) {
+        const int pos = E * lane + q;
+        const int prev = q > 0 ? v[q - 1] : prev_lane_last;
+        first[q] = pos < n && (pos == 0 || prev != v[q]);
+        cnt += first[q] ? 1 : 0;
+    }
+    int pre = cnt;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const int y = __shfl_up_sync(0xffffffffu, pre, o);
+        if (lane >= o) pre += y;
+    }
+    const int num = __shfl_sync(0xffffffffu, pre, 31);
+    int fb = pre - cnt;   // firsts before this lane's first element
+#pragma unroll
+    for (int q = 0; q < E; ++q) {
+        const int pos = E * lane + q;
+        if (pos < n) outl[first[q] ? fb : num + (pos - fb)] = v[q];
+        fb += first[q] ? 1 : 0;
+    }
+    __syncwarp();
+    return num;
+}
+
+// four CTAs (32 warps) per SM: the row's selection and sort are latency chains
+// that more warps in flight hide better than more registers per thread would
+__global__ void __launch_bounds__(kWarps * 32, 4) build_kernel(const BuildParams P) {
     extern __shared__ int smem[];
     const ScopeMaskArgs &a = P.a;
     const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5, nw = blockDim.x >> 5;
@@ -302,6 +505,8 @@ __global__ void __launch_bounds__(kWarps * 32) build_kernel(const BuildParams P)
     int *rad = cen + kMaxM;               // [kMaxM]
     float *alloc = reinterpret_cast<float *>(rad + kMaxM);  // [kMaxM]
     float *frac = alloc + kMaxM;          // [kMaxM]
+    float *selv = frac + kMaxM;           // [32]: select_row_thr's candidates
+    int *seli = reinterpret_cast<int *>(selv + 32);   // [32]
     int *hist = smem + nw * P.per_warp;   // [n_stats] per CTA
     const bool want_stats = a.stats != nullptr;
     if (want_stats)
@@ -325,8 +530,11 @@ __global__ void __launch_bounds__(kWarps * 32) build_kernel(const BuildParams P)
 
         // ---- pointer centres (model/attn_bias.py:779-784) ----
         if (a.sel_logits) {
-            if (qb < 32 * 32) select_row_regs(a, h, qb, lane, cen);
-            else select_row(a, h, qb, lane, cen);
+            if (qb < 32 * 32) {
+                if (!select_row_thr(a, h, qb, lane, cen, selv, seli)) select_row_regs(a, h, qb, lane, cen);
+            } else {
+                select_row(a, h, qb, lane, cen);
+            }
         } else if (lane < M) {
             float d = a.delta_rep[(int64_t)h * a.delta_head_stride + (int64_t)qb * a.delta_row_stride +
                                   (int64_t)lane * a.delta_m_stride];
@@ -405,7 +613,14 @@ __global__ void __launch_bounds__(kWarps * 32) build_kernel(const BuildParams P)
         if (lane < M) rad[lane] = r;
         __syncwarp();
 
-        // ---- window pieces (model/attn_bias.py:786-825) ----
+        // ---- window pieces (model/attn_bias.py:786-825), de-duplicated and packed
+        // (model/attn_bias.py:828-837): in registers for rows of up to 128 entries ----
+        int num = 0;
+        if (P.np2 <= 128) {
+            if (P.np2 == 32) num = pack_row_regs<1>(a, n, qb, dsp, dsl, cen, rad, lane, outl);
+            else if (P.np2 == 64) num = pack_row_regs<2>(a, n, qb, dsp, dsl, cen, rad, lane, outl);
+            else num = pack_row_regs<4>(a, n, qb, dsp, dsl, cen, rad, lane, outl);
+        } else {
         for (int pos = lane; pos < n; pos += 32) {
             int val;
             if (pos < L) {
@@ -452,7 +667,6 @@ __global__ void __launch_bounds__(kWarps * 32) build_kernel(const BuildParams P)
                 __syncwarp();
             }
         }
-        int num = 0;
         for (int c0 = 0; c0 < n; c0 += 32) {
             const int pos = c0 + lane;
             const bool first = pos < n && (pos == 0 || vals[pos - 1] != vals[pos]);
@@ -469,6 +683,7 @@ __global__ void __launch_bounds__(kWarps * 32) build_kernel(const BuildParams P)
             firsts_before += __popc(fb);
         }
         __syncwarp();
+        }
 
         // ---- outputs ----
         if (lane == 0) a.kv_num[row] = num;
@@ -603,7 +818,7 @@ extern "C" int scope_mask_build(const ScopeMaskArgs *args, scope_stream_t stream
     P.max_kv = max_kv;
     P.np2 = 32;
     while (P.np2 < max_kv) P.np2 <<= 1;
-    P.per_warp = P.np2 + max_kv + 4 * mask::kMaxM;
+    P.per_warp = P.np2 + max_kv + 4 * mask::kMaxM + 64;
     P.n_stats = (max_kv + 1) + (a.half_blocks + 1) + (std::max(1, a.half_blocks * a.M) + 1) + 1;
     P.words = (a.QB + 31) / 32;
     int nwarps = mask::kWarps;
@@ -621,7 +836,12 @@ extern "C" int scope_mask_build(const ScopeMaskArgs *args, scope_stream_t stream
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
     int rows = a.H * a.QB;
-    int grid = std::min(ceil_div(rows, nwarps), sms * 8);
+    // one wave of resident CTAs, rows taken in a grid-stride loop
+    int per_sm = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, mask::build_kernel, nwarps * 32, smem) != cudaSuccess ||
+        per_sm < 1)
+        per_sm = 1;
+    int grid = std::min(ceil_div(rows, nwarps), sms * per_sm);
     mask::build_kernel<<<grid, nwarps * 32, smem, s>>>(P);
     SCOPE_CHECK_LAUNCH();
     return SCOPE_OK;

@@ -205,14 +205,28 @@ __global__ void __launch_bounds__(256, 2) coeff_kernel(const __grid_constant__ M
         }
         const int64_t row = (int64_t)h * p.T + t0 + r;
         if (p.mlp_out) {
-            uint16_t *mo = p.mlp_out + row * p.n_out;
+            // the tile's 128 rows of y are contiguous in global memory: staged in shared
+            // memory (the q tile is idle now) and written out 16 bytes at a time
+            uint16_t *sy = reinterpret_cast<uint16_t *>(smem + L::Q);
+            if (!half) {
 #pragma unroll
-            for (int o = 0; o < NP; ++o) {
-                if (o < p.n_out) {
-                    __nv_bfloat16 b = __float2bfloat16_rn(y[o]);
-                    mo[o] = *reinterpret_cast<uint16_t *>(&b);
+                for (int o = 0; o < NP; ++o) {
+                    if (o < p.n_out) {
+                        __nv_bfloat16 b = __float2bfloat16_rn(y[o]);
+                        sy[r * p.n_out + o] = *reinterpret_cast<uint16_t *>(&b);
+                    }
                 }
             }
+            asm volatile("bar.sync 1, 256;" ::: "memory");
+            uint16_t *g = p.mlp_out + ((int64_t)h * p.T + t0) * p.n_out;
+            const int bytes = BM * p.n_out * 2;           // a multiple of 256
+            if ((reinterpret_cast<uintptr_t>(g) & 15) == 0) {
+                for (int o = threadIdx.x; o < bytes / 16; o += 256)
+                    reinterpret_cast<uint4 *>(g)[o] = reinterpret_cast<const uint4 *>(sy)[o];
+            } else {
+                for (int o = threadIdx.x; o < bytes / 2; o += 256) g[o] = sy[o];
+            }
+            asm volatile("bar.sync 1, 256;" ::: "memory");   // the region is reused for the exchange below
         }
         // ---- heads (model/attn_bias.py:437-478), y columns: delta | mu | sigma | pi | budget | (slope)
         float ds[M], mu[M], sg[M], pi[M];
@@ -340,6 +354,8 @@ struct BwdParams {
     const float *omegas, *log_omegas;
     float delta_cap, logw_min, logw_max, c_scale, width_min, width_max, eps;
     float *dy;
+    uint16_t *dyb;    // or bf16 rows of dyb_ld (zero padded), written 16 bytes at a time
+    int dyb_ld;
 };
 
 template <int K, int M>
@@ -440,18 +456,45 @@ __global__ void __launch_bounds__(128) coeff_bwd_kernel(const BwdParams p) {
     float pd = 0.f;
 #pragma unroll
     for (int m = 0; m < M; ++m) pd += pi[m] * dpi[m];
-    float *dy = p.dy + row * p.n_out;
+    constexpr int NO = 5 * M + 1;
+    float o[NO];
 #pragma unroll
     for (int m = 0; m < M; ++m) {
-        dy[m] = dds[m] * p.delta_cap * sd[m] * (1.f - sd[m]);
-        dy[M + m] = dmu[m] * (p.logw_max - p.logw_min) * sm[m] * (1.f - sm[m]);
-        dy[2 * M + m] = dsg[m] * 1.75f * ss[m] * (1.f - ss[m]);
-        dy[3 * M + m] = pi[m] * (dpi[m] - pd);
-        dy[4 * M + m] = p.dbudget ? p.dbudget[row * M + m] : 0.f;
+        o[m] = dds[m] * p.delta_cap * sd[m] * (1.f - sd[m]);
+        o[M + m] = dmu[m] * (p.logw_max - p.logw_min) * sm[m] * (1.f - sm[m]);
+        o[2 * M + m] = dsg[m] * 1.75f * ss[m] * (1.f - ss[m]);
+        o[3 * M + m] = pi[m] * (dpi[m] - pd);
+        o[4 * M + m] = p.dbudget ? p.dbudget[row * M + m] : 0.f;
     }
+    o[5 * M] = 0.f;
     if (p.use_slope) {
         const float t = tanhf(bf16_to_f32(yr[5 * M]));
-        dy[5 * M] = (p.dslope ? p.dslope[row] : 0.f) * p.c_scale * (1.f - t * t);
+        o[5 * M] = (p.dslope ? p.dslope[row] : 0.f) * p.c_scale * (1.f - t * t);
+    }
+    if (p.dyb) {
+        // bf16 pairs, zero past n_out, 16 bytes at a time (dyb_ld <= NPD, a multiple of 8)
+        constexpr int NPD = (NO + 15) / 16 * 16;
+        uint4 *d = reinterpret_cast<uint4 *>(p.dyb + row * p.dyb_ld);
+#pragma unroll
+        for (int c8 = 0; c8 < NPD / 8; ++c8) {
+            if (8 * c8 < p.dyb_ld) {
+                uint32_t w[4];
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    const int c0 = 8 * c8 + 2 * e, c1 = c0 + 1;
+                    const float v0 = (c0 < NO && c0 < p.n_out) ? o[c0 < NO ? c0 : 0] : 0.f;
+                    const float v1 = (c1 < NO && c1 < p.n_out) ? o[c1 < NO ? c1 : 0] : 0.f;
+                    __nv_bfloat162 b = __floats2bfloat162_rn(v0, v1);
+                    w[e] = *reinterpret_cast<uint32_t *>(&b);
+                }
+                d[c8] = make_uint4(w[0], w[1], w[2], w[3]);
+            }
+        }
+    } else {
+        float *dy = p.dy + row * p.n_out;
+#pragma unroll
+        for (int c = 0; c < NO; ++c)
+            if (c < p.n_out) dy[c] = o[c];
     }
 }
 
@@ -560,6 +603,13 @@ static int launch_bwd(const ScopeCoeffBwdArgs &a, cudaStream_t s) {
     p.width_max = a.width_max;
     p.eps = a.eps;
     p.dy = a.dy;
+    p.dyb = reinterpret_cast<uint16_t *>(a.dy_bf16);
+    p.dyb_ld = a.dy_ld;
+    if (p.dyb) {
+        constexpr int NPD = (5 * M + 1 + 15) / 16 * 16;
+        if (p.dy || a.dy_ld % 8 || a.dy_ld < p.n_out || a.dy_ld > NPD) return SCOPE_ERR_INVALID;
+        if (reinterpret_cast<uintptr_t>(a.dy_bf16) & 15) return SCOPE_ERR_ALIGN;
+    }
     coeff_bwd_kernel<K, M><<<(unsigned)((p.rows + 127) / 128), 128, 0, s>>>(p);
     SCOPE_CHECK_LAUNCH();
     return SCOPE_OK;
@@ -582,7 +632,8 @@ extern "C" int scope_spectral_coeffs_bwd(const ScopeCoeffBwdArgs *args, scope_st
     using namespace scope::coeff;
     if (!args) return SCOPE_ERR_INVALID;
     const ScopeCoeffBwdArgs &a = *args;
-    if (a.H <= 0 || a.T <= 0 || !a.mlp_out || !a.omegas || !a.log_omegas || !a.dy) return SCOPE_ERR_INVALID;
+    if (a.H <= 0 || a.T <= 0 || !a.mlp_out || !a.omegas || !a.log_omegas || (!a.dy && !a.dy_bf16))
+        return SCOPE_ERR_INVALID;
     if ((int64_t)a.H * a.T > INT32_MAX) return SCOPE_ERR_INVALID;
     cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
     switch (a.K) {

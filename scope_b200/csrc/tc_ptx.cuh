@@ -287,6 +287,12 @@ __device__ __forceinline__ float ex2(float x) {
     return y;
 }
 
+__device__ __forceinline__ float lg2(float x) {
+    float y;
+    asm("lg2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
 // packed fp32x2 arithmetic (one instruction for two lanes of work on sm_100)
 __device__ __forceinline__ uint64_t f2_pack(float lo, float hi) {
     uint64_t r;
