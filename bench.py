@@ -237,6 +237,21 @@ def time_steps(fn, steps, world):
     return ms
 
 
+# DRAM bytes (read + write) of one launch of each phase's dominant kernel, from
+# single ncu --set full captures of this build (cold L2, as ncu replays), and
+# the units that launch processed.  Refresh them with a new capture when a
+# kernel changes.
+NCU_TRAFFIC = {
+    "builder": {"bytes": 71.20e6 + 1.82e6, "units": 16,
+                "capture": "ncu build_kernel, C3 (16 heads, 1024 q blocks each)"},
+    "forward": {"bytes": 349.83e6 + 55.75e6, "units": 59741,
+                "capture": "ncu fwd_kernel<32,0>, C3 with 4 of 16 heads (59,741 active pairs)"},
+    "backward": {"bytes": 1023.21e6 + 486.42e6, "units": 59741,
+                 "capture": "ncu dkvq_kernel<32,0,0> (prep, plan and finish kernels not included), "
+                            "C3 with 4 of 16 heads (59,741 active pairs)"},
+}
+
+
 def gpu_hold(ms=30.0):
     """Keep the current stream busy for about `ms` (a device-side sleep), so
     that the host enqueues the work that follows before the GPU reaches it:
@@ -842,18 +857,13 @@ def main():
                 "achieved": ach, "peak": bf16, "unit": "TFLOP/s"}
     roof["frac"] = roof["achieved"] / roof["peak"]
     roof["peak_source"] = f"{src} (MEASURED_PEAKS.json burst)" if src == "measured" else "fallback"
-    # DRAM bytes (read + write) per active block pair from ncu captures of the
-    # attention kernels on C3 with 4 of its 16 heads (59,741 pairs;
-    # profiles/attn_kernels_c3_4heads.md; the builder and the backward's prep
-    # kernel from the full C3 step, profiles/c3_step_launch_list.md), scaled to
-    # this launch's pairs
-    if dom == 0:
-        roof["traffic"] = 0.073e9 * wl.hp / 16           # mask::build_kernel, per head
-    else:
-        per_pair = 0.4101e9 / 59741 if dom == 1 else (0.559e9 / 238859 + (0.7305e9 + 0.6175e9) / 59741)
-        roof["traffic"] = per_pair * P_local
+    # DRAM traffic of the dominant kernel from one ncu capture of this build
+    # (dram__bytes_read.sum + dram__bytes_write.sum), scaled to this launch
+    cap = NCU_TRAFFIC["builder" if dom == 0 else ("forward" if dom == 1 else "backward")]
+    units = wl.hp if dom == 0 else P_local
+    roof["traffic"] = cap["bytes"] / cap["units"] * units
     roof["traffic_unit"] = "bytes per launch"
-    roof["traffic_source"] = "ncu dram__bytes_read.sum + dram__bytes_write.sum per active block pair, scaled to this launch"
+    roof["traffic_source"] = cap["capture"] + ", scaled to this launch's " + ("heads" if dom == 0 else "active pairs")
 
     e2e = None
     if not args.no_e2e:

@@ -284,8 +284,13 @@ typedef struct ScopeAttnArgs {
     const float *b0, *slope, *delta_main, *width; /* [H,T] each or NULL */
     int32_t gate;                     /* scope_gate */
     float beta, gate_lambda, gate_tau;
-    const void *q_aug, *k_aug;        /* qk_aug: from scope_qk_aug_prepare */
-    int32_t d_aug;                    /* multiple of 16 (0 when bias_mode != QK_AUG) */
+    const void *q_aug, *k_aug;        /* qk_aug: from scope_qk_aug_prepare (with the slope column when
+                                         there is a slope).  score_mod: optional; from scope_qk_aug_prepare
+                                         WITHOUT the slope column (slope = NULL), they put the closure's
+                                         Fourier sum on the tensor cores (bf16, 128-token blocks), the
+                                         backward reusing what the forward was given */
+    int32_t d_aug;                    /* multiple of 16: qk_aug 16..64; score_mod 16 * ceil(2K / 16) with
+                                         q_aug, else 0 (CUDA cores); 0 for no bias */
     /* backward only */
     const void *dout;
     int64_t do_sh, do_st;

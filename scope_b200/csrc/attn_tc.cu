@@ -8,11 +8,12 @@
 //               barriers (K is released once the S MMA that read it is done,
 //               V once P V is).  Tiles are addressed by block index, so the
 //               sparse gather is just the TMA coordinate.  No multicast.
-//   warp 1      tcgen05 issuer (the warp waits, lane 0 issues): S = Q K^T
-//               (+ Qaug Kaug^T, the spectral bias of the qk_aug mode) into
-//               TMEM, and O += P V with P read from TMEM as the A operand, in a
-//               fixed order (S_{j+1}, then P V_j) with sleeping waits.  It also
-//               owns the TMEM allocation.
+//               The same thread issues O += P V_j (P read from TMEM as the A
+//               operand) once P_j is ready, just before it reloads V_j's stage.
+//   warp 1      S issuer (the warp waits, lane 0 issues): S = Q K^T (+ Qaug
+//               Kaug^T, the spectral bias) into TMEM as soon as the softmax
+//               holds the previous S in registers, with sleeping waits.  It
+//               also owns the TMEM allocation.
 //   warps 2..9  softmax: two threads per query row (one per 64-column half,
 //               the halves trading row max and row sum through shared memory
 //               behind a bounded mbarrier).  S comes out of TMEM with
@@ -211,6 +212,20 @@ __global__ void __launch_bounds__(kThreads, 2) fwd_kernel(const __grid_constant_
         return __all_sync(0xffffffffu, ok);
     };
 
+    // P V_j, issued by the producer thread: once P_j is in TMEM and V_j has landed
+    auto issue_pv = [&](int j) -> bool {
+        if (*abort_flag || !mbar_wait_idle(p_full, j & 1) || !mbar_wait_idle(v_full + (j & 1), (j >> 1) & 1))
+            return false;
+        tc_fence_after();
+        constexpr uint32_t idO = idesc_bf16(128, 64, false, true);
+        const uint32_t sv = smem_u32(smem + L::STAGE0 + (j & 1) * L::STAGE + L::V);
+#pragma unroll
+        for (int kk = 0; kk < BM / 16; ++kk)
+            mma_ts(tmem + O_COL, tmem + P_COL + kk * 8, mnmajor128_desc(sv + kk * 2048), idO, (j > 0 || kk > 0) ? 1u : 0u);
+        tc_commit(o_done);
+        if (j + 2 < n) tc_commit(v_empty + (j & 1));
+        return true;
+    };
     if (warp == 0) {
         // ------------------------------------------------------------ producer
         if (lane == 0 && n > 0) {
@@ -235,6 +250,13 @@ __global__ void __launch_bounds__(kThreads, 2) fwd_kernel(const __grid_constant_
                 tma_load_3d(&maps.k, st + L::K, kv_full + s, 0, kb * BM, h);
 #pragma unroll
                 for (int a = 0; a < NA; ++a) tma_load_2d(&maps.ka, st + L::KA + a * L::ATILE, kv_full + s, 16 * a, kb * BM);
+                // P V of two tiles back, once its P is ready (its V stage is reloaded next)
+                if (j >= 2 && !issue_pv(j - 2)) {
+                    give_up();
+                    issued = j;
+                    kissued = j + 1;
+                    break;
+                }
                 if (j >= 2 && (*abort_flag || !mbar_wait_idle(v_empty + s, ((j >> 1) - 1) & 1))) {
                     give_up();
                     issued = j;
@@ -245,6 +267,11 @@ __global__ void __launch_bounds__(kThreads, 2) fwd_kernel(const __grid_constant_
                 tma_load_3d(&maps.v, st + L::V, v_full + s, 0, kb * BM, h);
                 issued = kissued = j + 1;
             }
+            for (int j = (n > 2 ? n - 2 : 0); j < n && issued == n; ++j)
+                if (!issue_pv(j)) {
+                    give_up();
+                    break;
+                }
             // never leave the CTA with a TMA write still in flight
             mbar_wait(q_full, 0, 500000000ull);
             for (int j = (kissued > 2 ? kissued - 2 : 0); j < kissued; ++j)
@@ -256,8 +283,7 @@ __global__ void __launch_bounds__(kThreads, 2) fwd_kernel(const __grid_constant_
         // ------------------------------------------------------------ tcgen05 issuer
         if (n > 0) {   // the whole warp waits; lane 0 issues
             constexpr uint32_t idS = idesc_bf16(128, 128, false, false);
-            constexpr uint32_t idO = idesc_bf16(128, 64, false, true);
-            const uint32_t tS = tmem + S_COL, tO = tmem + O_COL, tP = tmem + P_COL;
+            const uint32_t tS = tmem + S_COL;
             const uint32_t sq = smem_u32(smem + L::Q);
             bool ok = idle_wait(q_full, 0);
             auto issue_S = [&](int j) -> bool {
@@ -282,31 +308,15 @@ __global__ void __launch_bounds__(kThreads, 2) fwd_kernel(const __grid_constant_
                 return true;
             };
             ok = ok && issue_S(0);
-            // Fixed order: S_{j+1} as soon as the softmax holds S_j in registers (and
-            // K_{j+1} has landed), then P V_j once P_j is in TMEM.  S_{j+1} is always
-            // ready first, so the order costs nothing, and the waits block in the
-            // barrier (the warp is suspended, not polling the issue slots away from
-            // the softmax warps on its sub-partition).
-            for (int j = 0; ok && j < n; ++j) {
-                if (j + 1 < n && !(idle_wait(s_free, j & 1) && issue_S(j + 1))) {
-                    ok = false;
-                    break;
-                }
-                if (!idle_wait(p_full, j & 1) || !idle_wait(v_full + (j & 1), (j >> 1) & 1)) {
-                    ok = false;
-                    break;
-                }
-                tc_fence_after();
-                const uint32_t sv = smem_u32(smem + L::STAGE0 + (j & 1) * L::STAGE + L::V);
-                if (lane == 0) {
-#pragma unroll
-                    for (int kk = 0; kk < BM / 16; ++kk)
-                        mma_ts(tO, tP + kk * 8, mnmajor128_desc(sv + kk * 2048), idO, (j > 0 || kk > 0) ? 1u : 0u);
-                    tc_commit(o_done);
-                    if (j + 2 < n) tc_commit(v_empty + (j & 1));
-                }
-                __syncwarp();
-            }
+            // S_{j+1} as soon as the softmax holds S_j in registers and K_{j+1} has
+            // landed; the waits block in the barrier (the warp sleeps instead of
+            // polling issue slots away from the softmax warps on its sub-partition).
+            // P V is issued by the producer thread: each tcgen05.mma holds its
+            // issuing warp for about its execution time, so splitting the two kinds
+            // of MMA over two warps (on two sub-partitions, other ones for the SM's
+            // second CTA) spreads that cost instead of piling it on one.
+            for (int j = 0; ok && j + 1 < n; ++j)
+                ok = idle_wait(s_free, j & 1) && issue_S(j + 1);
             if (!ok) give_up();
         }
     } else {

@@ -6,7 +6,9 @@
 //
 // Persistent: one CTA per SM walks the 128-token tiles (all heads share the
 // weights).  Per tile:
-//   TMA      q [128 x 64] and dy [128 x NP] (bf16, NP = n_out padded to 16)
+//   TMA      q [128 x 64] and dy [128 x NP] (bf16, NP = n_out padded to 16),
+//            double buffered: tile t+1's loads are issued right after tile t's
+//            first MMAs, so their latency overlaps tile t's work
 //   tcgen05  X = q W1^T (128 hidden columns) and DH = dy W2 (128)
 //   threads  x = bf16(X + b1), s = sigmoid(x), h = bf16(x s), dh = bf16(DH),
 //            dx = bf16(dh s (1 + x (1 - s))); h and dx into shared memory
@@ -40,10 +42,12 @@ struct Lay {
     static constexpr uint32_t W1 = 0;                               // [128 hid][64 d], 128-byte swizzle
     static constexpr uint32_t W2SUB = align1k(NP * 128);             // W2 [NP][64 hid] per half
     static constexpr uint32_t W2 = 16384;
-    static constexpr uint32_t Q = align1k(W2 + 2 * W2SUB);           // [128 tok][64 d]
-    static constexpr uint32_t ONES = Q + 16384;                      // [128 tok][64]: column 0 = 1
-    static constexpr uint32_t DY = ONES + 16384;                     // 8 sub-tiles [128 tok][16], 32-byte swizzle
-    static constexpr uint32_t H = DY + 8 * 4096;                     // [128 tok][128 hid]: two halves
+    static constexpr uint32_t Q = align1k(W2 + 2 * W2SUB);           // 2 x [128 tok][64 d]
+    // [128 tok][64]: column 0 = 1, the second N atom of [q | 1] for either q buffer (LBO = ONES - q)
+    static constexpr uint32_t ONES = Q + 2 * 16384;
+    static constexpr uint32_t DY = ONES + 16384;                     // 2 x 8 sub-tiles [128 tok][16], 32-byte swizzle
+    static constexpr uint32_t DYB = 8 * 4096;                        // one dy buffer
+    static constexpr uint32_t H = DY + 2 * DYB;                      // [128 tok][128 hid]: two halves
     static constexpr uint32_t DX = H + 32768;
     static constexpr uint32_t BAR = DX + 32768;
     static constexpr uint32_t TOTAL = BAR + 128;
@@ -70,7 +74,8 @@ __global__ void __launch_bounds__(256, 1) mlp_bwd_kernel(const __grid_constant__
     using L = Lay<NP>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
-    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + L::BAR);   // 0 weights, 1 tile, 2 X/DH, 3 DQ, 4 accumulators
+    // 0 weights, 1 / 5 tile in buffer 0 / 1, 2 X/DH, 3 DQ, 4 accumulators
+    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + L::BAR);
     uint32_t *tslot = reinterpret_cast<uint32_t *>(smem + L::BAR + 64);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int quad = warp & 3, half = warp >> 2;
@@ -78,7 +83,7 @@ __global__ void __launch_bounds__(256, 1) mlp_bwd_kernel(const __grid_constant__
     const uint32_t lb = (uint32_t)(quad * 32) << 16;
 
     if (threadIdx.x == 0) {
-        for (int i = 0; i < 5; ++i) mbar_init(&bars[i], 1);
+        for (int i = 0; i < 6; ++i) mbar_init(&bars[i], 1);
         fence_mbar_init();
     }
     if (warp == 0) {
@@ -93,8 +98,10 @@ __global__ void __launch_bounds__(256, 1) mlp_bwd_kernel(const __grid_constant__
             // element (row, 0) sits in chunk 0 ^ (row & 7) of the row (128-byte swizzle)
             ones[i] = (chunk == (row & 7)) ? make_uint4(0x3F80u, 0u, 0u, 0u) : make_uint4(0u, 0u, 0u, 0u);
         }
-        uint4 *pad = reinterpret_cast<uint4 *>(smem + L::DY + (NP / 16) * 4096);
-        for (int i = threadIdx.x; i < (8 - NP / 16) * 4096 / 16; i += blockDim.x) pad[i] = make_uint4(0u, 0u, 0u, 0u);
+        for (int b = 0; b < 2; ++b) {
+            uint4 *pad = reinterpret_cast<uint4 *>(smem + L::DY + b * L::DYB + (NP / 16) * 4096);
+            for (int i = threadIdx.x; i < (8 - NP / 16) * 4096 / 16; i += blockDim.x) pad[i] = make_uint4(0u, 0u, 0u, 0u);
+        }
     }
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
     tc_fence_before();
@@ -111,34 +118,50 @@ __global__ void __launch_bounds__(256, 1) mlp_bwd_kernel(const __grid_constant__
     }
     const int tiles_per_head = p.T / BM;
     const uint16_t *b1 = p.b1;
+    // tile loads into buffer b (its barrier: bars[1] for buffer 0, bars[5] for buffer 1)
+    auto load_tile = [&](int tile, int b) {
+        const int h = tile / tiles_per_head, t0 = (tile - h * tiles_per_head) * BM;
+        uint64_t *bar = &bars[b ? 5 : 1];
+        mbar_expect_tx(bar, L::T_BYTES);
+        tma_load_3d(&maps.q, smem + L::Q + b * 16384, bar, 0, t0, h);
+#pragma unroll
+        for (int a = 0; a < NP / 16; ++a)
+            tma_load_2d(&maps.dy, smem + L::DY + b * L::DYB + a * 4096, bar, 16 * a, h * p.T + t0);
+    };
+    int pend_b = -1, pend_par = 0;   // a prefetch not yet consumed (thread 0): drained before exit
+    if (threadIdx.x == 0 && (int)blockIdx.x < p.tiles) {
+        load_tile(blockIdx.x, 0);
+        pend_b = 0;
+    }
     bool ok = true;
     int it = 0;
     for (int tile = blockIdx.x; tile < p.tiles && ok; tile += gridDim.x, ++it) {
         const int h = tile / tiles_per_head, t0 = (tile - h * tiles_per_head) * BM;
-        // ---- loads and the first two MMAs (one thread); the previous tile's MMAs
-        // read q, dy, h and dx, so they must be done before those are replaced
+        const int b = it & 1;
+        const uint32_t sQb = sQ + b * 16384, sDYb = sDY + b * L::DYB;
+        // ---- the first two MMAs (one thread), then the next tile's loads into the other
+        // buffer once the previous tile's MMAs, which read it (and h, dx), completed
         if (threadIdx.x == 0) {
-            if (it > 0) ok = mbar_wait(&bars[4], (it - 1) & 1);
-            if (ok) {
-                mbar_expect_tx(&bars[1], L::T_BYTES);
-                tma_load_3d(&maps.q, smem + L::Q, &bars[1], 0, t0, h);
-#pragma unroll
-                for (int a = 0; a < NP / 16; ++a)
-                    tma_load_2d(&maps.dy, smem + L::DY + a * 4096, &bars[1], 16 * a, h * p.T + t0);
-                ok = (it > 0 || mbar_wait(&bars[0], 0)) && mbar_wait(&bars[1], it & 1);
-            }
+            ok = (it > 0 || mbar_wait(&bars[0], 0)) && mbar_wait(&bars[b ? 5 : 1], (it >> 1) & 1);
+            if (ok) pend_b = -1;
             if (ok) {
                 tc_fence_after();
                 constexpr uint32_t idX = idesc_bf16(128, HID, false, false);
 #pragma unroll
                 for (int kk = 0; kk < HD / 16; ++kk)
-                    mma_ss(tmem + TX, kmajor_desc(sQ + kk * 32, 128), kmajor_desc(sW1 + kk * 32, 128), idX, kk > 0);
+                    mma_ss(tmem + TX, kmajor_desc(sQb + kk * 32, 128), kmajor_desc(sW1 + kk * 32, 128), idX, kk > 0);
                 constexpr uint32_t idDH = idesc_bf16(128, HID, false, true);
 #pragma unroll
                 for (int kk = 0; kk < NP / 16; ++kk)
-                    mma_ss(tmem + TDH, kmajor_desc(sDY + kk * 4096, 32), smem_desc(sW2 + kk * 2048, L::W2SUB, 1024, SW128),
+                    mma_ss(tmem + TDH, kmajor_desc(sDYb + kk * 4096, 32), smem_desc(sW2 + kk * 2048, L::W2SUB, 1024, SW128),
                            idDH, kk > 0);
                 tc_commit(&bars[2]);
+            }
+            if (ok && it > 0) ok = mbar_wait(&bars[4], (it - 1) & 1);
+            if (ok && tile + (int)gridDim.x < p.tiles) {
+                load_tile(tile + gridDim.x, b ^ 1);
+                pend_b = b ^ 1;
+                pend_par = ((it + 1) >> 1) & 1;
             }
         }
         ok = __syncthreads_and(ok);
@@ -201,8 +224,10 @@ __global__ void __launch_bounds__(256, 1) mlp_bwd_kernel(const __grid_constant__
 #pragma unroll
             for (int kk = 0; kk < BM / 16; ++kk) {
                 const uint32_t acc = (it > 0 || kk > 0) ? 1u : 0u;
-                mma_ss(tmem + TW2, mnmajor32_desc(sDY + kk * 512), mnmajor128_desc(sH + kk * 2048), idW2, acc);
-                mma_ss(tmem + TW1, mnmajor128_desc(sDX + kk * 2048), mnmajor128_desc(sQ + kk * 2048), idW1, acc);
+                mma_ss(tmem + TW2, mnmajor32_desc(sDYb + kk * 512), mnmajor128_desc(sH + kk * 2048), idW2, acc);
+                // [q | 1]: the B operand's second 64-column atom is the ones tile, LBO bytes after q
+                mma_ss(tmem + TW1, mnmajor128_desc(sDX + kk * 2048),
+                       smem_desc(sQb + kk * 2048, (uint32_t)(L::ONES - L::Q) - b * 16384u, 1024, SW128), idW1, acc);
             }
             tc_commit(&bars[4]);
         }
@@ -228,6 +253,8 @@ __global__ void __launch_bounds__(256, 1) mlp_bwd_kernel(const __grid_constant__
         __syncthreads();
     }
     if (!ok) set_err(p.err, SCOPE_DEVERR_TIMEOUT);
+    // never leave the CTA with a TMA write still in flight
+    if (threadIdx.x == 0 && pend_b >= 0) mbar_wait(&bars[pend_b ? 5 : 1], pend_par, 500000000ull);
     // ---- the CTA's weight-gradient sums -> global
     bool fin = ok && it > 0;
     if (threadIdx.x == 0 && fin) fin = mbar_wait(&bars[4], (it - 1) & 1);

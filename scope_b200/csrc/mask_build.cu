@@ -119,6 +119,7 @@ __global__ void __launch_bounds__(1024) block_info_pass2(int QB, int bs, int doc
 struct BuildParams {
     ScopeMaskArgs a;
     int max_kv;      // entries before de-duplication
+    uint32_t span_mul;   // ceil(2^32 / span), span = 2 half_blocks + 1 (0 when span is 1): q / span = umulhi(q, span_mul)
     int per_warp;    // ints of shared memory per warp
     int np2;         // max_kv rounded up to a power of two (the sort buffer)
     int n_stats;     // ints of the statistics block
@@ -331,13 +332,17 @@ __device__ bool select_row_thr(const ScopeMaskArgs &a, int h, int qb, int lane, 
 #pragma unroll
         for (int c = 0; c < 4; ++c) sc[4 * g + c] = (b + c < n) ? __fadd_rn(tau(lv[c]), gv[c]) : -INFINITY;
     }
-    // lane maximum, and a NaN probe (a NaN anywhere makes the sum NaN)
-    float lm = sc[0], sum = 0.f;
+    // lane maximum with NaN propagation (max.NaN), so a NaN anywhere shows in it
+    float lm = sc[0];
 #pragma unroll
-    for (int e = 1; e < 32; ++e) lm = fmaxf(lm, sc[e]);
-#pragma unroll
-    for (int e = 0; e < 32; ++e) sum += (sc[e] == -INFINITY) ? 0.f : sc[e];
-    if (__any_sync(0xffffffffu, isnan(sum))) return false;
+    for (int e = 1; e < 32; e += 2) {
+        if (e + 1 < 32) {
+            asm("max.NaN.f32 %0, %1, %2, %3;" : "=f"(lm) : "f"(lm), "f"(sc[e]), "f"(sc[e + 1]));
+        } else {
+            asm("max.NaN.f32 %0, %1, %2;" : "=f"(lm) : "f"(lm), "f"(sc[e]));
+        }
+    }
+    if (__any_sync(0xffffffffu, isnan(lm))) return false;
     // the M-th largest lane maximum: a descending bitonic sort of the 32 values
     float t = lm;
 #pragma unroll
@@ -433,12 +438,12 @@ __device__ __forceinline__ void warp_sort_regs(int (&v)[E], int lane) {
 
 // The window entries of a row (model/attn_bias.py:786-825): entry pos of the
 // local blocks, the M pointer windows and the global blocks.
-__device__ __forceinline__ int window_entry(const ScopeMaskArgs &a, int pos, int qb, int dsp, int dsl, const int *cen,
-                                            const int *rad) {
+__device__ __forceinline__ int window_entry(const ScopeMaskArgs &a, uint32_t span_mul, int pos, int qb, int dsp,
+                                            int dsl, const int *cen, const int *rad) {
     const int L = a.local_blocks, M = a.M, p = a.half_blocks, span = 2 * p + 1;
     if (pos < L) return max(max(qb - pos, 0), dsl);
     if (pos < L + M * span) {
-        const int q = pos - L, m = q / span, c = cen[m];
+        const int q = pos - L, m = span_mul ? (int)__umulhi((uint32_t)q, span_mul) : q, c = cen[m];
         if (p > 0) {
             const int o = q - m * span - p;
             int w = min(max(c + o, 0), a.QB - 1);
@@ -456,13 +461,13 @@ __device__ __forceinline__ int window_entry(const ScopeMaskArgs &a, int pos, int
 // entries): unique blocks ascending, then the repeats ascending, into outl;
 // returns the number of unique blocks.
 template <int E>
-__device__ int pack_row_regs(const ScopeMaskArgs &a, int n, int qb, int dsp, int dsl, const int *cen, const int *rad,
-                             int lane, int *outl) {
+__device__ int pack_row_regs(const ScopeMaskArgs &a, uint32_t span_mul, int n, int qb, int dsp, int dsl, const int *cen,
+                             const int *rad, int lane, int *outl) {
     int v[E];
 #pragma unroll
     for (int q = 0; q < E; ++q) {
         const int pos = E * lane + q;
-        v[q] = pos < n ? window_entry(a, pos, qb, dsp, dsl, cen, rad) : INT_MAX;   // INT_MAX sorts past every block
+        v[q] = pos < n ? window_entry(a, span_mul, pos, qb, dsp, dsl, cen, rad) : INT_MAX;   // INT_MAX sorts past every block
     }
     warp_sort_regs<E>(v, lane);
     const int prev_lane_last = __shfl_up_sync(0xffffffffu, v[E - 1], 1);
@@ -617,9 +622,9 @@ __global__ void __launch_bounds__(kWarps * 32, 4) build_kernel(const BuildParams
         // (model/attn_bias.py:828-837): in registers for rows of up to 128 entries ----
         int num = 0;
         if (P.np2 <= 128) {
-            if (P.np2 == 32) num = pack_row_regs<1>(a, n, qb, dsp, dsl, cen, rad, lane, outl);
-            else if (P.np2 == 64) num = pack_row_regs<2>(a, n, qb, dsp, dsl, cen, rad, lane, outl);
-            else num = pack_row_regs<4>(a, n, qb, dsp, dsl, cen, rad, lane, outl);
+            if (P.np2 == 32) num = pack_row_regs<1>(a, P.span_mul, n, qb, dsp, dsl, cen, rad, lane, outl);
+            else if (P.np2 == 64) num = pack_row_regs<2>(a, P.span_mul, n, qb, dsp, dsl, cen, rad, lane, outl);
+            else num = pack_row_regs<4>(a, P.span_mul, n, qb, dsp, dsl, cen, rad, lane, outl);
         } else {
         for (int pos = lane; pos < n; pos += 32) {
             int val;
@@ -821,6 +826,11 @@ extern "C" int scope_mask_build(const ScopeMaskArgs *args, scope_stream_t stream
     P.per_warp = P.np2 + max_kv + 4 * mask::kMaxM + 64;
     P.n_stats = (max_kv + 1) + (a.half_blocks + 1) + (std::max(1, a.half_blocks * a.M) + 1) + 1;
     P.words = (a.QB + 31) / 32;
+    {
+        // 0 stands for span 1 (q / 1 = q); otherwise exact for every q the rows hold (q < 2^20)
+        const uint64_t span = 2ull * (uint64_t)a.half_blocks + 1ull;
+        P.span_mul = span == 1 ? 0u : (uint32_t)(((1ull << 32) + span - 1) / span);
+    }
     int nwarps = mask::kWarps;
     size_t smem = (size_t)(nwarps * P.per_warp + P.n_stats) * sizeof(int);
     while (smem > 160 * 1024 && nwarps > 1) {

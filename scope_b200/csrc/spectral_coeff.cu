@@ -358,40 +358,59 @@ struct BwdParams {
     int dyb_ld;
 };
 
+// Two threads per token (lanes 2t, 2t+1): each takes half of the M mixture
+// components -- the K-frequency inner loops, the expensive part -- and the
+// few sums over all components (softmax max / sum, the mean of mu, the
+// argmax for delta_main, sum_m pi dpi) are completed with one shuffle each.
 template <int K, int M>
-__global__ void __launch_bounds__(128) coeff_bwd_kernel(const BwdParams p) {
-    const int64_t row = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-    if (row >= p.rows) return;
+__global__ void __launch_bounds__(256) coeff_bwd_kernel(const BwdParams p) {
+    constexpr int MH = M / 2;
+    const int half = threadIdx.x & 1;
+    const int64_t row0 = (int64_t)blockIdx.x * 128 + (threadIdx.x >> 1);
+    const bool valid = row0 < p.rows;
+    const int64_t row = valid ? row0 : p.rows - 1;   // both lanes take part in the shuffles
     const uint16_t *yr = p.y + row * p.n_out;
-    float sd[M], sm[M], ss[M], ds[M], mu[M], sg[M], pi[M];
+    const int mb = half * MH;                        // this lane's first component
+    float sd[MH], sm[MH], ss[MH], ds[MH], mu[MH], sg[MH], pi[MH], pl[MH];
     float pmax = -INFINITY, musum = 0.f;
     int imax = 0;
 #pragma unroll
-    for (int m = 0; m < M; ++m) {
-        sd[m] = sigmoid_ref(bf16_to_f32(yr[m]));
-        sm[m] = sigmoid_ref(bf16_to_f32(yr[M + m]));
-        ss[m] = sigmoid_ref(bf16_to_f32(yr[2 * M + m]));
-        ds[m] = sd[m] * p.delta_cap;
-        mu[m] = p.logw_min + (p.logw_max - p.logw_min) * sm[m];
-        sg[m] = 0.25f + 1.75f * ss[m];
-        musum += mu[m];
-        const float pl = bf16_to_f32(yr[3 * M + m]);
-        if (pl > pmax) {
-            pmax = pl;
+    for (int mm = 0; mm < MH; ++mm) {
+        const int m = mb + mm;
+        sd[mm] = sigmoid_ref(bf16_to_f32(yr[m]));
+        sm[mm] = sigmoid_ref(bf16_to_f32(yr[M + m]));
+        ss[mm] = sigmoid_ref(bf16_to_f32(yr[2 * M + m]));
+        ds[mm] = sd[mm] * p.delta_cap;
+        mu[mm] = p.logw_min + (p.logw_max - p.logw_min) * sm[mm];
+        sg[mm] = 0.25f + 1.75f * ss[mm];
+        musum += mu[mm];
+        pl[mm] = bf16_to_f32(yr[3 * M + m]);
+        if (pl[mm] > pmax) {
+            pmax = pl[mm];
             imax = m;
         }
     }
+    // the first largest pi logit over both halves (lane 0's components come first)
+    {
+        const float op = __shfl_xor_sync(0xffffffffu, pmax, 1);
+        const int oi = __shfl_xor_sync(0xffffffffu, imax, 1);
+        if (op > pmax || (op == pmax && oi < imax)) {
+            pmax = op;
+            imax = oi;
+        }
+    }
+    musum += __shfl_xor_sync(0xffffffffu, musum, 1);
     float psum = 0.f;
 #pragma unroll
-    for (int m = 0; m < M; ++m) {
-        pi[m] = expf(bf16_to_f32(yr[3 * M + m]) - pmax);
-        psum += pi[m];
+    for (int mm = 0; mm < MH; ++mm) {
+        pi[mm] = expf(pl[mm] - pmax);
+        psum += pi[mm];
     }
-#pragma unroll
+    psum += __shfl_xor_sync(0xffffffffu, psum, 1);
     {
         const float rps = __frcp_rn(psum);
 #pragma unroll
-        for (int m = 0; m < M; ++m) pi[m] *= rps;
+        for (int mm = 0; mm < MH; ++mm) pi[mm] *= rps;
     }
     // upstream gradients of the per-frequency outputs; b0 = sum_k coeff_cos adds db0 to each
     float e[K], f[K];
@@ -401,15 +420,16 @@ __global__ void __launch_bounds__(128) coeff_bwd_kernel(const BwdParams p) {
         e[k] = (p.dcc ? p.dcc[row * K + k] : 0.f) + g_b0;
         f[k] = p.dcs ? p.dcs[row * K + k] : 0.f;
     }
-    float dpi[M], dds[M], dmu[M], dsg[M];
+    float dpi[MH], dds[MH], dmu[MH], dsg[MH];
     const float g_om = p.dom ? p.dom[row] : 0.f;   // gradient of sum_m sum_k w_k^2 a_hat_mk^2
 #pragma unroll
-    for (int m = 0; m < M; ++m) {
-        const float rden = __frcp_rn(2.f * sg[m] * sg[m]);
+    for (int mm = 0; mm < MH; ++mm) {
+        const int m = mb + mm;
+        const float rden = __frcp_rn(2.f * sg[mm] * sg[mm]);
         float a[K], S = 0.f;
 #pragma unroll
         for (int k = 0; k < K; ++k) {
-            const float d = __ldg(p.log_omegas + k) - mu[m];
+            const float d = __ldg(p.log_omegas + k) - mu[mm];
             a[k] = __expf(-(d * d) * rden);
             S += a[k];
         }
@@ -418,83 +438,101 @@ __global__ void __launch_bounds__(128) coeff_bwd_kernel(const BwdParams p) {
 #pragma unroll
         for (int k = 0; k < K; ++k) {
             float sn, c;
-            sincos_phase(__ldg(p.omegas + k) * ds[m], &sn, &c);
+            sincos_phase(__ldg(p.omegas + k) * ds[mm], &sn, &c);
             const float ah = a[k] * rSe;
             const float g = e[k] * c + f[k] * sn;
             gpi += ah * g;
             gdl += ah * __ldg(p.omegas + k) * (f[k] * c - e[k] * sn);
-            dah[k] = pi[m] * g + g_om * 2.f * __ldg(p.omegas + k) * __ldg(p.omegas + k) * ah;
+            dah[k] = pi[mm] * g + g_om * 2.f * __ldg(p.omegas + k) * __ldg(p.omegas + k) * ah;
             dot += dah[k] * a[k];
         }
-        dpi[m] = gpi + (p.dpi ? p.dpi[row * M + m] : 0.f);
-        dds[m] = pi[m] * gdl + (p.dds ? p.dds[row * M + m] : 0.f);
+        dpi[mm] = gpi + (p.dpi ? p.dpi[row * M + m] : 0.f);
+        dds[mm] = pi[mm] * gdl + (p.dds ? p.dds[row * M + m] : 0.f);
         // a_hat = a / (S + eps): da_k = dah_k / Se - sum_j dah_j a_j / Se^2
         float gm = 0.f, gs = 0.f;
-        const float inv_s2 = 1.f / (sg[m] * sg[m]);
+        const float inv_s2 = 1.f / (sg[mm] * sg[mm]);
 #pragma unroll
         for (int k = 0; k < K; ++k) {
             const float da = (dah[k] - dot * rSe) * rSe;
-            const float d = __ldg(p.log_omegas + k) - mu[m];
+            const float d = __ldg(p.log_omegas + k) - mu[mm];
             gm += da * a[k] * d * inv_s2;                    // d a / d mu    = a (l - mu) / sigma^2
-            gs += da * a[k] * d * d * inv_s2 / sg[m];        // d a / d sigma = a (l - mu)^2 / sigma^3
+            gs += da * a[k] * d * d * inv_s2 / sg[mm];       // d a / d sigma = a (l - mu)^2 / sigma^3
         }
-        dmu[m] = gm;
-        dsg[m] = gs;
+        dmu[mm] = gm;
+        dsg[mm] = gs;
     }
     if (p.ddelta_main) {
         const float g = p.ddelta_main[row];
 #pragma unroll
-        for (int m = 0; m < M; ++m)
-            if (m == imax) dds[m] += g;
+        for (int mm = 0; mm < MH; ++mm)
+            if (mb + mm == imax) dds[mm] += g;
     }
     if (p.dwidth) {
         const float sw = sigmoid_ref(musum / (float)M);
         const float g = p.dwidth[row] * (p.width_max - p.width_min) * sw * (1.f - sw) / (float)M;
 #pragma unroll
-        for (int m = 0; m < M; ++m) dmu[m] += g;
+        for (int mm = 0; mm < MH; ++mm) dmu[mm] += g;
     }
     float pd = 0.f;
 #pragma unroll
-    for (int m = 0; m < M; ++m) pd += pi[m] * dpi[m];
-    constexpr int NO = 5 * M + 1;
-    float o[NO];
+    for (int mm = 0; mm < MH; ++mm) pd += pi[mm] * dpi[mm];
+    pd += __shfl_xor_sync(0xffffffffu, pd, 1);
+    // this lane's outputs: column g M + mb + mm of each group g (delta | mu | sigma | pi | budget)
+    float o[5][MH];
 #pragma unroll
-    for (int m = 0; m < M; ++m) {
-        o[m] = dds[m] * p.delta_cap * sd[m] * (1.f - sd[m]);
-        o[M + m] = dmu[m] * (p.logw_max - p.logw_min) * sm[m] * (1.f - sm[m]);
-        o[2 * M + m] = dsg[m] * 1.75f * ss[m] * (1.f - ss[m]);
-        o[3 * M + m] = pi[m] * (dpi[m] - pd);
-        o[4 * M + m] = p.dbudget ? p.dbudget[row * M + m] : 0.f;
+    for (int mm = 0; mm < MH; ++mm) {
+        const int m = mb + mm;
+        o[0][mm] = dds[mm] * p.delta_cap * sd[mm] * (1.f - sd[mm]);
+        o[1][mm] = dmu[mm] * (p.logw_max - p.logw_min) * sm[mm] * (1.f - sm[mm]);
+        o[2][mm] = dsg[mm] * 1.75f * ss[mm] * (1.f - ss[mm]);
+        o[3][mm] = pi[mm] * (dpi[mm] - pd);
+        o[4][mm] = p.dbudget ? p.dbudget[row * M + m] : 0.f;
     }
-    o[5 * M] = 0.f;
+    float oslope = 0.f;
     if (p.use_slope) {
         const float t = tanhf(bf16_to_f32(yr[5 * M]));
-        o[5 * M] = (p.dslope ? p.dslope[row] : 0.f) * p.c_scale * (1.f - t * t);
+        oslope = (p.dslope ? p.dslope[row] : 0.f) * p.c_scale * (1.f - t * t);
     }
     if (p.dyb) {
-        // bf16 pairs, zero past n_out, 16 bytes at a time (dyb_ld <= NPD, a multiple of 8)
+        // the whole row in both lanes (the partner's components by shuffle), then each
+        // lane writes half of its 16-byte chunks (bf16 pairs, zero past n_out)
+        constexpr int NO = 5 * M + 1;
         constexpr int NPD = (NO + 15) / 16 * 16;
+        float full[NO];
+#pragma unroll
+        for (int g = 0; g < 5; ++g) {
+#pragma unroll
+            for (int mm = 0; mm < MH; ++mm) {
+                const float other = __shfl_xor_sync(0xffffffffu, o[g][mm], 1);
+                full[g * M + mm] = half ? other : o[g][mm];
+                full[g * M + MH + mm] = half ? o[g][mm] : other;
+            }
+        }
+        full[5 * M] = oslope;
         uint4 *d = reinterpret_cast<uint4 *>(p.dyb + row * p.dyb_ld);
 #pragma unroll
         for (int c8 = 0; c8 < NPD / 8; ++c8) {
-            if (8 * c8 < p.dyb_ld) {
+            if (valid && (c8 & 1) == half && 8 * c8 < p.dyb_ld) {
                 uint32_t w[4];
 #pragma unroll
-                for (int e = 0; e < 4; ++e) {
-                    const int c0 = 8 * c8 + 2 * e, c1 = c0 + 1;
-                    const float v0 = (c0 < NO && c0 < p.n_out) ? o[c0 < NO ? c0 : 0] : 0.f;
-                    const float v1 = (c1 < NO && c1 < p.n_out) ? o[c1 < NO ? c1 : 0] : 0.f;
+                for (int e4 = 0; e4 < 4; ++e4) {
+                    const int c0 = 8 * c8 + 2 * e4, c1 = c0 + 1;
+                    const float v0 = (c0 < NO && c0 < p.n_out) ? full[c0 < NO ? c0 : 0] : 0.f;
+                    const float v1 = (c1 < NO && c1 < p.n_out) ? full[c1 < NO ? c1 : 0] : 0.f;
                     __nv_bfloat162 b = __floats2bfloat162_rn(v0, v1);
-                    w[e] = *reinterpret_cast<uint32_t *>(&b);
+                    w[e4] = *reinterpret_cast<uint32_t *>(&b);
                 }
                 d[c8] = make_uint4(w[0], w[1], w[2], w[3]);
             }
         }
-    } else {
+    } else if (valid) {
         float *dy = p.dy + row * p.n_out;
 #pragma unroll
-        for (int c = 0; c < NO; ++c)
-            if (c < p.n_out) dy[c] = o[c];
+        for (int g = 0; g < 5; ++g) {
+#pragma unroll
+            for (int mm = 0; mm < MH; ++mm) dy[g * M + mb + mm] = o[g][mm];
+        }
+        if (p.use_slope && half == 0) dy[5 * M] = oslope;
     }
 }
 
@@ -610,7 +648,7 @@ static int launch_bwd(const ScopeCoeffBwdArgs &a, cudaStream_t s) {
         if (p.dy || a.dy_ld % 8 || a.dy_ld < p.n_out || a.dy_ld > NPD) return SCOPE_ERR_INVALID;
         if (reinterpret_cast<uintptr_t>(a.dy_bf16) & 15) return SCOPE_ERR_ALIGN;
     }
-    coeff_bwd_kernel<K, M><<<(unsigned)((p.rows + 127) / 128), 128, 0, s>>>(p);
+    coeff_bwd_kernel<K, M><<<(unsigned)((p.rows + 127) / 128), 256, 0, s>>>(p);
     SCOPE_CHECK_LAUNCH();
     return SCOPE_OK;
 }
