@@ -930,7 +930,13 @@ def main():
                 "step_launch": {"cuda_graph": graph is not None, "kernels_per_step": per_step,
                                 "note": graph_why or "the timed steps replay one CUDA graph of the whole step"}}
         print(json.dumps(line), flush=True)
-    del graph                     # a graph holding NCCL work is released before the process group
+    # a graph holding NCCL work must be destroyed before the process group, or the
+    # exit waits for good: reset() frees the graph and its executable even while
+    # references to it (step_fn is its bound replay) remain
+    torch.cuda.synchronize()
+    if graph is not None:
+        graph.reset()
+    del step_fn, graph
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
