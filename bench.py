@@ -244,7 +244,7 @@ def time_steps(fn, steps, world):
 NCU_TRAFFIC = {
     "builder": {"bytes": 71.20e6 + 1.82e6, "units": 16,
                 "capture": "ncu build_kernel, C3 (16 heads, 1024 q blocks each)"},
-    "forward": {"bytes": 349.83e6 + 55.75e6, "units": 59741,
+    "forward": {"bytes": 349.86e6 + 55.44e6, "units": 59741,
                 "capture": "ncu fwd_kernel<32,0>, C3 with 4 of 16 heads (59,741 active pairs)"},
     "backward": {"bytes": 1023.21e6 + 486.42e6, "units": 59741,
                  "capture": "ncu dkvq_kernel<32,0,0> (prep, plan and finish kernels not included), "
