@@ -27,11 +27,13 @@
 //   warp 1       S / dP issuer: S^T = K Q^T (+ K_aug Q_aug^T) into SB once the
 //                previous tile's dV MMAs read their P^T from it; dP^T = V dO^T
 //                into DPB once the previous tile's dK MMAs read their dS^T
-//   warp 2       gradient issuer: dV += P^T dO (P^T from TMEM, the even K steps
-//                as soon as every warp wrote its first 16 columns), dK += dS^T Q
-//                (dS^T from TMEM), dQ = dS [K | K_aug] (dS from shared memory)
-//                into DQ once the drain warps copied out the previous tile's
-//   warp 3       no role (it completes the first warpgroup)
+//   warp 2       gradient issuer: dV += P^T dO (P^T from TMEM), dK += dS^T Q
+//                (dS^T from TMEM); it releases the tile's stage
+//   warp 3       dQ issuer: dQ = dS [K | K_aug] (dS from shared memory) into DQ
+//                once the drain warps copied out the previous tile's.  Each
+//                tcgen05.mma holds its issuing warp about as long as the tensor
+//                pipe takes to run it, and that cost lands on the warp's
+//                sub-partition: three issuing warps spread it
 //   warps 4-19   elementwise (four per TMEM lane quadrant): thread = kv row,
 //                32 q columns each: P = exp2(S scale log2e - lse2) (masked),
 //                P^T as bf16 pairs over the warp's own S^T columns; then dP^T 16
@@ -66,7 +68,7 @@ constexpr int kThreads = 32 * (kDrainWarp0 + 4);       // 768: six warpgroups
 constexpr int kElem = 32 * kElemWarps;  // elementwise threads
 constexpr int kDrain = 128;             // drain threads
 constexpr int kDrainBoxes = 3;          // staging boxes per drain warp (reduces in flight)
-constexpr int kIdxWarps = 2 + kElemWarps + 4;   // the issuers, elementwise and drain warps read each item index
+constexpr int kIdxWarps = 3 + kElemWarps + 4;   // the issuers, elementwise and drain warps read each item index
 constexpr int kChunk = 64;              // max q tiles per dK/dV work item
 constexpr int kSlotCap = 128;           // max kv rows whose q list is split
 constexpr uint32_t kTmemCols = 512;
@@ -199,14 +201,14 @@ struct Bars {
     uint64_t dp_free;                  // the dK MMAs that read dS^T completed
     uint64_t dq_full;                  // dQ of a tile is in DQ (and the dS tile in shared memory is free)
     uint64_t dq_free;                  // the drain warps copied DQ out
-    uint64_t drain[2];                 // each issuing warp's MMAs completed (before TMEM is freed)
+    uint64_t drain[3];                 // each issuing warp's MMAs completed (before TMEM is freed)
     volatile int stage_blk[4];         // q block of the tile in each stage
     volatile int stage_mk[4];          // its mask kind
     uint32_t tmem_slot;
     volatile int abort_flag, last_flag, item_of;
     __device__ void init(int nst) {
         mbar_init(&res_full, 1);
-        mbar_init(&acc_done, 1);
+        mbar_init(&acc_done, 2);   // the gradient issuer and the dQ issuer
         mbar_init(&acc_free, kElem);
         mbar_init(&idx_taken, kIdxWarps);
         for (int i = 0; i < nst; ++i) {
@@ -223,6 +225,7 @@ struct Bars {
         mbar_init(&dp_free, 1);
         mbar_init(&drain[0], 1);
         mbar_init(&drain[1], 1);
+        mbar_init(&drain[2], 1);
         abort_flag = 0;
         last_flag = 0;
         item_of = 0;
@@ -568,9 +571,8 @@ __global__ void __launch_bounds__(kThreads, 1) dkvq_kernel(const __grid_constant
         if (lane == 0) tc_commit(&B.drain[0]);   // TMEM is freed only after this warp's MMAs completed
         mbar_wait(&B.drain[0], 0, 500000000ull);
     } else if (warp == 2) {
-        // ---------------- gradient issuer (whole warp)
+        // ---------------- gradient issuer (whole warp): dV and dK
         constexpr uint32_t idG = idesc_bf16(128, 64, false, true);
-        constexpr uint32_t idQ = idesc_bf16(128, L::DQN, true, true);
         int gt = 0;
         bool ok = true;
         for (int ci = 0; ok; ++ci) {
@@ -605,18 +607,7 @@ __global__ void __launch_bounds__(kThreads, 1) dkvq_kernel(const __grid_constant
                         mma_ts(tmem + DK, tmem + DPB + pcol(kk), mnmajor128_desc(sb + L::SQ + kk * 2048), idG,
                                (t > 0 || kk > 0) ? 1u : 0u);
                     tc_commit(&B.dp_free);
-                }
-                __syncwarp();
-                // dQ (| aug-dim gradient) = dS [K | K_aug] once the drain warps took the previous tile's
-                if (gt >= 1 && !cx.waitw(&B.dq_free, (gt - 1) & 1)) { ok = false; break; }
-                tc_fence_after();
-                if (lane == 0) {
-#pragma unroll
-                    for (int kk = 0; kk < 8; ++kk)
-                        mma_ss(tmem + DQ, mnmajor128_desc(sDS + kk * 2048), mnmajor32_desc(sK + kk * 512), idQ,
-                               kk > 0 ? 1u : 0u);
-                    tc_commit(&B.dq_full);
-                    tc_commit(&B.empty[st]);
+                    tc_commit(&B.empty[st]);   // the stage's last readers were dV and dK
                 }
                 __syncwarp();
             }
@@ -628,7 +619,38 @@ __global__ void __launch_bounds__(kThreads, 1) dkvq_kernel(const __grid_constant
         if (lane == 0) tc_commit(&B.drain[1]);
         mbar_wait(&B.drain[1], 0, 500000000ull);
     } else if (warp < kElemWarp0) {
-        // warp 3: no role
+        // ---------------- dQ issuer (whole warp): dQ (| aug-dim gradient) = dS [K | K_aug]
+        // once dS is in shared memory and the drain warps took the previous tile's
+        constexpr uint32_t idQ = idesc_bf16(128, L::DQN, true, true);
+        int gt = 0;
+        bool ok = true;
+        for (int ci = 0; ok; ++ci) {
+            if (!cx.waitw(&B.res_full, ci & 1)) { ok = false; break; }
+            const int it = B.item_of;
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&B.idx_taken);
+            if (it < 0) break;
+            const int nq = p.plan.items[it].w;
+            for (int t = 0; t < nq; ++t, ++gt) {
+                if (!cx.waitw(&B.ds_ready, gt & 1)) { ok = false; break; }
+                if (gt >= 1 && !cx.waitw(&B.dq_free, (gt - 1) & 1)) { ok = false; break; }
+                tc_fence_after();
+                if (lane == 0) {
+#pragma unroll
+                    for (int kk = 0; kk < 8; ++kk)
+                        mma_ss(tmem + DQ, mnmajor128_desc(sDS + kk * 2048), mnmajor32_desc(sK + kk * 512), idQ,
+                               kk > 0 ? 1u : 0u);
+                    tc_commit(&B.dq_full);
+                }
+                __syncwarp();
+            }
+            if (!ok) break;
+            if (lane == 0) tc_commit(&B.acc_done);   // the item's dQ MMAs read K: the residents wait for them too
+            __syncwarp();
+        }
+        if (!ok) cx.give_up();
+        if (lane == 0) tc_commit(&B.drain[2]);
+        mbar_wait(&B.drain[2], 0, 500000000ull);
     } else if (warp < kDrainWarp0) {
         // ---------------- elementwise: thread = kv row c, tile columns [32qc, 32qc+32)
         const int quad = warp & 3;
