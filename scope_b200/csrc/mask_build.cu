@@ -293,14 +293,16 @@ __device__ void select_row_regs(const ScopeMaskArgs &a, int h, int qb, int lane,
     __syncwarp();
 }
 
-// The same selection by a threshold filter, for rows of at most 32 * 32
-// candidates (lane l holds kb = 128 g + 4 l + c, g < 8, c < 4).  The M-th
-// largest of the 32 lane maxima is a lower bound for the M-th best score
-// (those M lane maxima are M distinct candidates), so only candidates scoring
-// at least that can win.  They are compacted into shared memory and one warp
-// bitonic sort under the same order as better() ranks them.  Returns false,
-// leaving cen untouched, when more than 32 candidates pass or a score is NaN:
-// the caller then runs select_row_regs, so the result is the same either way.
+// The same selection by a threshold filter, 1,024 candidates (a chunk) at a
+// time: lane l holds kb = c0 + 128 g + 4 l + c (g < 8, c < 4) of chunk c0.
+// The M-th largest of the 32 lane maxima bounds the chunk's own M-th best
+// score (those lane maxima are M distinct candidates), and the running M-th
+// best of the earlier chunks bounds what can still enter, so only candidates
+// scoring at least both are compacted into shared memory, next to the running
+// top-M, and ranked by one warp bitonic sort under the order better() uses.
+// Returns false, leaving cen untouched, when a chunk passes more candidates
+// than fit beside the running list or a score is NaN: the caller then runs an
+// exact path, so the result is the same either way.
 __device__ bool select_row_thr(const ScopeMaskArgs &a, int h, int qb, int lane, int *cen, float *sv, int *si) {
     const float *lrow = a.sel_logits + (int64_t)h * a.sel_head_stride + (int64_t)qb * a.sel_row_stride;
     const float *grow = a.sel_gumbel + (int64_t)h * a.sel_head_stride + (int64_t)qb * a.sel_row_stride;
@@ -309,94 +311,112 @@ __device__ bool select_row_thr(const ScopeMaskArgs &a, int h, int qb, int lane, 
     const bool vec = (a.QB % 4 == 0) && (a.sel_row_stride % 4 == 0) && (a.sel_head_stride % 4 == 0) &&
                      ((reinterpret_cast<uintptr_t>(a.sel_logits) & 15) == 0) &&
                      ((reinterpret_cast<uintptr_t>(a.sel_gumbel) & 15) == 0);
-    float sc[32];
+    // the running top-M: lane r < kept holds entry r, best first
+    float v = -INFINITY;
+    int id = INT_MAX;
+    int kept = 0;
+    float thr_run = -INFINITY;   // its M-th score once M are kept
+    for (int c0 = 0; c0 < n; c0 += 1024) {
+        float sc[32];
 #pragma unroll
-    for (int g = 0; g < 8; ++g) {
-        const int b = 128 * g + 4 * lane;
-        float lv[4] = {0.f, 0.f, 0.f, 0.f}, gv[4] = {0.f, 0.f, 0.f, 0.f};
-        if (b < n) {
-            if (vec) {
-                const float4 l4 = __ldg(reinterpret_cast<const float4 *>(lrow + b));
-                const float4 g4 = __ldg(reinterpret_cast<const float4 *>(grow + b));
-                lv[0] = l4.x; lv[1] = l4.y; lv[2] = l4.z; lv[3] = l4.w;
-                gv[0] = g4.x; gv[1] = g4.y; gv[2] = g4.z; gv[3] = g4.w;
+        for (int g = 0; g < 8; ++g) {
+            const int b = c0 + 128 * g + 4 * lane;
+            float lv[4] = {0.f, 0.f, 0.f, 0.f}, gv[4] = {0.f, 0.f, 0.f, 0.f};
+            if (b < n) {
+                if (vec) {
+                    const float4 l4 = __ldg(reinterpret_cast<const float4 *>(lrow + b));
+                    const float4 g4 = __ldg(reinterpret_cast<const float4 *>(grow + b));
+                    lv[0] = l4.x; lv[1] = l4.y; lv[2] = l4.z; lv[3] = l4.w;
+                    gv[0] = g4.x; gv[1] = g4.y; gv[2] = g4.z; gv[3] = g4.w;
+                } else {
+#pragma unroll
+                    for (int c = 0; c < 4; ++c)
+                        if (b + c < n) {
+                            lv[c] = __ldg(lrow + b + c);
+                            gv[c] = __ldg(grow + b + c);
+                        }
+                }
+            }
+#pragma unroll
+            for (int c = 0; c < 4; ++c) sc[4 * g + c] = (b + c < n) ? __fadd_rn(tau(lv[c]), gv[c]) : -INFINITY;
+        }
+        // lane maximum with NaN propagation (max.NaN), so a NaN anywhere shows in it
+        float lm = sc[0];
+#pragma unroll
+        for (int e = 1; e < 32; e += 2) {
+            if (e + 1 < 32) {
+                asm("max.NaN.f32 %0, %1, %2, %3;" : "=f"(lm) : "f"(lm), "f"(sc[e]), "f"(sc[e + 1]));
             } else {
-#pragma unroll
-                for (int c = 0; c < 4; ++c)
-                    if (b + c < n) {
-                        lv[c] = __ldg(lrow + b + c);
-                        gv[c] = __ldg(grow + b + c);
-                    }
+                asm("max.NaN.f32 %0, %1, %2;" : "=f"(lm) : "f"(lm), "f"(sc[e]));
             }
         }
+        if (__any_sync(0xffffffffu, isnan(lm))) return false;
+        // the M-th largest lane maximum: a descending bitonic sort of the 32 values
+        float t = lm;
 #pragma unroll
-        for (int c = 0; c < 4; ++c) sc[4 * g + c] = (b + c < n) ? __fadd_rn(tau(lv[c]), gv[c]) : -INFINITY;
-    }
-    // lane maximum with NaN propagation (max.NaN), so a NaN anywhere shows in it
-    float lm = sc[0];
+        for (int k = 2; k <= 32; k <<= 1) {
 #pragma unroll
-    for (int e = 1; e < 32; e += 2) {
-        if (e + 1 < 32) {
-            asm("max.NaN.f32 %0, %1, %2, %3;" : "=f"(lm) : "f"(lm), "f"(sc[e]), "f"(sc[e + 1]));
-        } else {
-            asm("max.NaN.f32 %0, %1, %2;" : "=f"(lm) : "f"(lm), "f"(sc[e]));
-        }
-    }
-    if (__any_sync(0xffffffffu, isnan(lm))) return false;
-    // the M-th largest lane maximum: a descending bitonic sort of the 32 values
-    float t = lm;
-#pragma unroll
-    for (int k = 2; k <= 32; k <<= 1) {
-#pragma unroll
-        for (int j = k >> 1; j > 0; j >>= 1) {
-            const float o = __shfl_xor_sync(0xffffffffu, t, j);
-            const bool desc = (lane & k) == 0, lower = (lane & j) == 0;
-            t = (lower == desc) ? fmaxf(t, o) : fminf(t, o);
-        }
-    }
-    const float thr = __shfl_sync(0xffffffffu, t, M - 1);
-    // the candidates that can win, compacted in lane order
-    uint32_t hit = 0u;
-#pragma unroll
-    for (int e = 0; e < 32; ++e) {
-        const int kb = 128 * (e >> 2) + 4 * lane + (e & 3);
-        if (kb < n && sc[e] >= thr) hit |= 1u << e;
-    }
-    const int cnt = __popc(hit);
-    int pre = cnt;
-#pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-        const int y = __shfl_up_sync(0xffffffffu, pre, o);
-        if (lane >= o) pre += y;
-    }
-    const int total = __shfl_sync(0xffffffffu, pre, 31);
-    if (total > 32) return false;
-    int pos = pre - cnt;
-#pragma unroll
-    for (int e = 0; e < 32; ++e) {
-        if ((hit >> e) & 1u) {
-            sv[pos] = sc[e];
-            si[pos] = 128 * (e >> 2) + 4 * lane + (e & 3);
-            ++pos;
-        }
-    }
-    __syncwarp();
-    float v = lane < total ? sv[lane] : -INFINITY;
-    int id = lane < total ? si[lane] : INT_MAX;
-    __syncwarp();
-    // warp bitonic sort, best first under better()
-#pragma unroll
-    for (int k = 2; k <= 32; k <<= 1) {
-#pragma unroll
-        for (int j = k >> 1; j > 0; j >>= 1) {
-            const float ov = __shfl_xor_sync(0xffffffffu, v, j);
-            const int oi = __shfl_xor_sync(0xffffffffu, id, j);
-            const bool desc = (lane & k) == 0, lower = (lane & j) == 0;
-            if ((lower == desc) ? better(ov, oi, v, id) : better(v, id, ov, oi)) {
-                v = ov;
-                id = oi;
+            for (int j = k >> 1; j > 0; j >>= 1) {
+                const float o = __shfl_xor_sync(0xffffffffu, t, j);
+                const bool desc = (lane & k) == 0, lower = (lane & j) == 0;
+                t = (lower == desc) ? fmaxf(t, o) : fminf(t, o);
             }
         }
+        const float thr = fmaxf(__shfl_sync(0xffffffffu, t, M - 1), thr_run);
+        // the candidates that can still win, compacted in lane order after the running list
+        uint32_t hit = 0u;
+#pragma unroll
+        for (int e = 0; e < 32; ++e) {
+            const int kb = c0 + 128 * (e >> 2) + 4 * lane + (e & 3);
+            if (kb < n && sc[e] >= thr) hit |= 1u << e;
+        }
+        const int cnt = __popc(hit);
+        int pre = cnt;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int y = __shfl_up_sync(0xffffffffu, pre, o);
+            if (lane >= o) pre += y;
+        }
+        const int total = __shfl_sync(0xffffffffu, pre, 31);
+        if (kept + total > 32) return false;
+        if (lane < kept) {
+            sv[lane] = v;
+            si[lane] = id;
+        }
+        int pos = kept + pre - cnt;
+#pragma unroll
+        for (int e = 0; e < 32; ++e) {
+            if ((hit >> e) & 1u) {
+                sv[pos] = sc[e];
+                si[pos] = c0 + 128 * (e >> 2) + 4 * lane + (e & 3);
+                ++pos;
+            }
+        }
+        __syncwarp();
+        const int m = kept + total;
+        v = lane < m ? sv[lane] : -INFINITY;
+        id = lane < m ? si[lane] : INT_MAX;
+        __syncwarp();
+        // warp bitonic sort, best first under better()
+#pragma unroll
+        for (int k = 2; k <= 32; k <<= 1) {
+#pragma unroll
+            for (int j = k >> 1; j > 0; j >>= 1) {
+                const float ov = __shfl_xor_sync(0xffffffffu, v, j);
+                const int oi = __shfl_xor_sync(0xffffffffu, id, j);
+                const bool desc = (lane & k) == 0, lower = (lane & j) == 0;
+                if ((lower == desc) ? better(ov, oi, v, id) : better(v, id, ov, oi)) {
+                    v = ov;
+                    id = oi;
+                }
+            }
+        }
+        kept = min(m, M);
+        if (lane >= kept) {
+            v = -INFINITY;
+            id = INT_MAX;
+        }
+        if (kept == M) thr_run = __shfl_sync(0xffffffffu, v, M - 1);
     }
     if (lane < M) cen[lane] = (id == INT_MAX) ? qb : id;
     __syncwarp();
@@ -535,10 +555,9 @@ __global__ void __launch_bounds__(kWarps * 32, 4) build_kernel(const BuildParams
 
         // ---- pointer centres (model/attn_bias.py:779-784) ----
         if (a.sel_logits) {
-            if (qb < 32 * 32) {
-                if (!select_row_thr(a, h, qb, lane, cen, selv, seli)) select_row_regs(a, h, qb, lane, cen);
-            } else {
-                select_row(a, h, qb, lane, cen);
+            if (!select_row_thr(a, h, qb, lane, cen, selv, seli)) {
+                if (qb < 32 * 32) select_row_regs(a, h, qb, lane, cen);
+                else select_row(a, h, qb, lane, cen);
             }
         } else if (lane < M) {
             float d = a.delta_rep[(int64_t)h * a.delta_head_stride + (int64_t)qb * a.delta_row_stride +

@@ -194,3 +194,26 @@ def test_block_info_matches_oracle():
             np.testing.assert_array_equal(got[1], dsl)
             np.testing.assert_array_equal(got[2], mn)
             np.testing.assert_array_equal(got[3], mx)
+
+
+@pytest.mark.parametrize("M,ties", [(8, False), (16, False), (8, True)])
+def test_selection_long_rows_matches_oracle(M, ties):
+    """Rows of up to 2,600 candidate blocks (C5 reaches 4,096): the selection
+    streams them 1,024 at a time against a running top-M.  Continuous scores
+    take that path; heavily tied scores (logits on a 0.5 grid, no noise) send
+    rows to the exact fallback.  Centres must equal the oracle's on every row."""
+    rng = np.random.default_rng(77 + M + int(ties))
+    H, QB, bs = 2, 2600, 128
+    if ties:
+        logits = (np.round(rng.standard_normal((H, QB, QB)) * 2) / 2).astype(np.float32)
+        g = np.zeros((H, QB, QB), np.float32)
+    else:
+        logits = rng.standard_normal((H, QB, QB)).astype(np.float32)
+        g = MO.gumbel_from_uniform(rng.random((H, QB, QB)).astype(np.float32))
+    tau = 0.5
+    ref = MO.select_pointer_blocks(logits, g, M=M, tau=tau)
+    bm = build_mask(H=H, T=QB * bs, block_size=bs, M=M, device=DEV,
+                    sel_logits=torch.from_numpy(logits).to(DEV), sel_gumbel=torch.from_numpy(g).to(DEV), sel_tau=tau,
+                    budget_rep=torch.from_numpy(rng.standard_normal((H, QB, M)).astype(np.float32)).to(DEV),
+                    local_blocks=4, half_blocks=2, global_blocks=1, budget_blocks=4, debug=True)
+    np.testing.assert_array_equal(bm.centres.cpu().numpy(), ref)
