@@ -615,6 +615,52 @@ def cpu_reference(cfg, *, warmup=1, steps=3, heads=1, seconds_budget=60.0):
                       f"{len(times)} timed steps", "seconds_per_step": sec}
 
 
+def torch_builder_ops(logits, gumbel, budget_rep, *, tau, M, L, p, G, budget_rem, temp):
+    """The reference builder's steps (model/attn_bias.py:721-837) as eager torch
+    ops on the GPU -- Gumbel top-M over the causal candidates, stick-breaking
+    radius allocation with largest-remainder rounding, the local / pointer /
+    global window entries, then sort, de-duplicate and pack (unique blocks
+    ascending, repeats after) -- without the document clamp.  Timed beside
+    this package's builder kernel as the GPU-torch form of the same work; on
+    one document its lists equal the oracle's (a CPU test checks that)."""
+    H, QB, _ = logits.shape
+    dev = logits.device
+    qb = torch.arange(QB, device=dev)
+    causal = qb[None, :] <= qb[:, None]
+    s = torch.where(causal, logits / tau + gumbel, torch.full_like(logits, -float("inf")))
+    cen = torch.topk(s, M, dim=-1).indices                                   # [H, QB, M]
+    cen = torch.minimum(cen, qb[None, :, None])
+    # radius: M - 1 stick fractions, the last piece the rest; largest-remainder rounding
+    u = torch.sigmoid(budget_rep[..., : M - 1] / temp)
+    rem = torch.full(u.shape[:-1], float(budget_rem), device=dev)
+    pieces = []
+    for m in range(M - 1):
+        b = u[..., m] * rem
+        pieces.append(b)
+        rem = rem - b
+    pieces.append(rem)
+    alloc = torch.stack(pieces, -1)
+    fl = torch.floor(alloc)
+    fr = alloc - fl
+    left = (budget_rem - fl.sum(-1, keepdim=True)).clamp(0, M)
+    rank = torch.sort(torch.sort(-fr, dim=-1, stable=True).indices, dim=-1).indices
+    r = (fl + (rank < left).float()).clamp(0, p).long()
+    # window entries
+    local = (qb[:, None] - torch.arange(L, device=dev)[None, :]).clamp(min=0).expand(H, QB, L)
+    offs = torch.arange(-p, p + 1, device=dev)
+    w = (cen[..., None] + offs).clamp(0, QB - 1)
+    w = torch.minimum(w, qb[None, :, None, None])
+    w = torch.where(offs.abs() <= r[..., None], w, cen[..., None]).reshape(H, QB, -1)
+    glob = torch.minimum(torch.arange(G, device=dev)[None, :], qb[:, None]).expand(H, QB, G)
+    ent = torch.cat([local, w, glob], -1)
+    srt = ent.sort(-1).values
+    first = torch.ones_like(srt, dtype=torch.bool)
+    first[..., 1:] = srt[..., 1:] != srt[..., :-1]
+    key = (~first).long() * QB + srt
+    packed = srt.gather(-1, torch.sort(key, dim=-1, stable=True).indices)
+    return first.sum(-1).to(torch.int32), packed.to(torch.int32)
+
+
 def run_flex(args):
     """torch's compiled flex_attention (Inductor Triton) on the GPU: the
     reference's GPU path for this layer, on the same inputs and mask.  The
@@ -713,12 +759,33 @@ def run_flex(args):
     for _ in range(reps):
         step(acc)
     ph = [a / reps for a in acc]
+    # the builder's work as eager torch ops on the GPU, beside this package's kernel
+    L_, p_, G_ = cfg.local_eff, cfg.half_blocks, cfg.global_blocks
+    # integer radius budget (model/attn_bias.py:724-734)
+    if cfg.budget_is_total:
+        extra = max(min(cfg.budget_blocks, L_ + cfg.M + 2 * cfg.M * p_) - L_ - cfg.M, 0)
+    else:
+        extra = max(0, cfg.budget_blocks)
+    brem = min(extra // 2, cfg.M * p_)
+    bkw = dict(tau=cfg.select_tau, M=cfg.M, L=L_, p=p_, G=G_, budget_rem=brem, temp=cfg.budget_temp)
+    for _ in range(3):
+        torch_builder_ops(x["logits"], x["gumbel"], x["budget_rep"], **bkw)
+    torch.cuda.synchronize()
+    e0.record(s)
+    for _ in range(5):
+        torch_builder_ops(x["logits"], x["gumbel"], x["budget_rep"], **bkw)
+    e1.record(s)
+    torch.cuda.synchronize()
+    torch_builder_ms = e0.elapsed_time(e1) / 5
     flops = 14 * bs * bs * D * P
     res = {"impl": "torch.compile(flex_attention), Inductor Triton, on the GPU", "value": flops / (ms * 1e-3) / 1e12,
            "unit": "TFLOP/s", "ms_per_step": ms, "active_block_pairs": P, "steps": args.steps,
            "phases_ms": {"from_kv_blocks_ms": ph[0], "qk_aug_prep_ms": ph[1], "forward_ms": ph[2],
                          "backward_ms": ph[3]},
            "attention_tflops": flops / ((ph[2] + ph[3]) * 1e-3) / 1e12, "compile_s": compile_s,
+           "builder_torch_ops_ms": torch_builder_ms,
+           "builder_note": "the reference builder's steps as eager torch ops on this GPU (torch_builder_ops); "
+                           "with BlockMask.from_kv_blocks (from_kv_blocks_ms) that is its mask path",
            "config": {"workload": f"{cfg.name}: the same layer, head dim 64 + {2 * K} qk_aug dims", "H": H, "T": T,
                       "block_size": bs, "K": K}}
     return res
@@ -915,6 +982,10 @@ def main():
             ours_attn = (4 + 10) * bs * bs * D * P_local / ((ph[1] + ph[2]) * 1e-3) / 1e12
             gref["ours_attention_tflops"] = ours_attn
             gref["attention_ours_over_reference"] = ours_attn / gref["attention_tflops"]
+            if "builder_torch_ops_ms" in gref:
+                # the mask path: torch ops + BlockMask.from_kv_blocks against this package's builder phase
+                gref["mask_ours_over_reference"] = (gref["builder_torch_ops_ms"] +
+                                                    gref["phases_ms"]["from_kv_blocks_ms"]) / ph[0]
 
     if rank == 0:
         line = {"metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,

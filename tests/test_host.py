@@ -101,3 +101,28 @@ def test_coefficient_entry_points_reject_bad_arguments():
         spectral_coefficients(torch.zeros(1, 2, 128, 64, dtype=torch.bfloat16), torch.zeros(128, 64),
                               torch.zeros(128), torch.zeros(41, 128), torch.zeros(41), omegas=torch.ones(16), M=8,
                               delta_cap=127.0, logw_min=-5.0, logw_max=-1.0)
+
+
+def test_bench_torch_builder_ops_match_oracle():
+    """The flex arm of the bench times the reference builder's steps as eager
+    torch ops; on one document (no clamping) they give the oracle's lists."""
+    import numpy as np
+    import torch
+
+    import bench
+    from oracle import mask_oracle as MO
+    H, QB, M, L, p, G, bud, bs = 2, 48, 6, 4, 3, 2, 40, 16
+    g = torch.Generator().manual_seed(1)
+    lg, gu = torch.randn(H, QB, QB, generator=g), torch.randn(H, QB, QB, generator=g)
+    br = torch.randn(H, QB, M, generator=g)
+    brem = MO.resolve_budget_rem(M=M, local_blocks=L, half_blocks=p, budget_blocks=bud, budget_is_total=True)
+    num, packed = bench.torch_builder_ops(lg, gu, br, tau=0.5, M=M, L=L, p=p, G=G, budget_rem=brem, temp=0.7)
+    cen = MO.select_pointer_blocks(lg.numpy(), gu.numpy(), M=M, tau=0.5)
+    o = MO.build_pointer_blockmask(docs=np.zeros(QB * bs, np.int32), block_size=bs, M=M, budget_rep=br.numpy(),
+                                   centres=cen, local_blocks=L, half_blocks=p, global_blocks_max=G,
+                                   budget_blocks=bud, budget_is_total=True, budget_temp=0.7, with_transpose=False)
+    assert np.array_equal(o["kv_num"], num.numpy())
+    for h in range(H):
+        for q in range(QB):
+            n = int(num[h, q])
+            assert np.array_equal(o["kv_packed"][h, q, :n], packed[h, q, :n].numpy())
