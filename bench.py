@@ -410,6 +410,83 @@ def score_mod_leg(wl, cfg, bm, pairs, *, reps=5):
             "backward_tflops": 10 * bs * bs * D * pairs / (b_ms * 1e-3) / 1e12}
 
 
+def torch_teacher_mass(q_sel, k_sel, q_pos, k_pos, docs, scale):
+    """The reference teacher's dense block-mass loop (scoped_medium.py:1793-1819)
+    as the same eager torch ops on the GPU: per query block, bf16 scores
+    against every key, the document-causal mask, softmax, column sums
+    scattered into kv blocks."""
+    H, L, _ = q_sel.shape
+    dev = q_sel.device
+    bs = 128
+    nb = L // bs
+    k_idx = torch.arange(L, device=dev)
+    k_blocks = torch.floor_divide(k_idx, bs)
+    mass_all = torch.zeros(H, nb, nb, device=dev)
+    for qb in range(nb):
+        qs, qe = qb * bs, (qb + 1) * bs
+        scores = torch.matmul(q_sel[:, qs:qe], k_sel.transpose(-2, -1)) * scale
+        scores = scores + torch.matmul(q_pos[:, qs:qe], k_pos.transpose(-2, -1)) * scale
+        q_idx = torch.arange(qs, qe, device=dev)
+        mask = (docs[qs:qe][:, None] == docs[None, :]) & (q_idx[:, None] >= k_idx[None, :])
+        w = torch.softmax(scores.float().masked_fill(~mask, -1.0e9), dim=-1)
+        m = torch.zeros(H, nb, device=dev)
+        m.scatter_add_(1, k_blocks[None].expand(H, -1), w.sum(dim=1))
+        mass_all[:, qb] = m
+    return mass_all
+
+
+def teacher_leg(cfg, heads, *, L=4096, reps=5):
+    """The spectral teacher's block mass (scoped_medium.py:1793-1819) at the
+    reference's default teacher length (4096 tokens) on this rank's heads, K
+    of the config with the slope column: this package's kernel
+    (teacher_block_mass) against the reference's loop as eager torch ops on
+    the same GPU, each timed with CUDA events (median of `reps`)."""
+    from scope_b200 import teacher_block_mass
+    dev = torch.device("cuda", torch.cuda.current_device())
+    g = torch.Generator(device=dev).manual_seed(29)
+    K = cfg.K
+    q = torch.randn(heads, L, 64, generator=g, device=dev).to(torch.bfloat16)
+    k = torch.randn(heads, L, 64, generator=g, device=dev).to(torch.bfloat16)
+    s_aug = math.sqrt(BETA / SCALE)
+    cc = 0.3 * torch.randn(heads, L, K, generator=g, device=dev)
+    cs = 0.3 * torch.randn(heads, L, K, generator=g, device=dev)
+    ph = torch.tensor([math.pi * 2.0 ** (-i) for i in range(K)], device=dev)[:, None] * torch.arange(L, device=dev)
+    ct = torch.cos(ph).to(torch.bfloat16).float().T[None].expand(heads, L, K)
+    st = torch.sin(ph).to(torch.bfloat16).float().T[None].expand(heads, L, K)
+    slope = 0.01 * torch.tanh(torch.randn(heads, L, generator=g, device=dev))
+    pos = torch.arange(L, device=dev, dtype=torch.float32)[None, :, None].expand(heads, L, 1)
+    q_pos = (torch.cat([cc * ct + cs * st, cc * st - cs * ct, -slope[..., None]], -1) * s_aug).to(torch.bfloat16)
+    k_pos = (torch.cat([ct, st, pos], -1) * s_aug).to(torch.bfloat16)
+    cuts = torch.zeros(L, dtype=torch.int64, device=dev)
+    cuts[[700, 1500, 2600]] = 1
+    docs = cuts.cumsum(0)
+    s = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+
+    def timed(fn):
+        for _ in range(2):
+            fn()
+        ts = []
+        for _ in range(reps):
+            torch.cuda.synchronize()
+            e0.record(s)
+            fn()
+            e1.record(s)
+            torch.cuda.synchronize()
+            ts.append(e0.elapsed_time(e1))
+        return statistics.median(ts)
+
+    ours = timed(lambda: teacher_block_mass(q, k, docs, scale=SCALE, q_pos=q_pos, k_pos=k_pos))
+    ref = timed(lambda: torch_teacher_mass(q, k, q_pos, k_pos, docs, SCALE))
+    diff = (teacher_block_mass(q, k, docs, scale=SCALE, q_pos=q_pos, k_pos=k_pos) -
+            torch_teacher_mass(q, k, q_pos, k_pos, docs, SCALE)).abs().max().item()
+    return {"workload": f"teacher block mass, {heads} heads x {L} tokens, K={K} + slope, 4 documents",
+            "ours_ms": ours, "reference_torch_ms": ref, "ours_over_reference": ref / ours,
+            "max_abs_diff_vs_reference_ops": diff,
+            "note": "reference = scoped_medium.py:1793-1819 as eager torch ops on this GPU (bf16 matmuls round "
+                    "the scores to bf16; the kernel keeps them in float32)"}
+
+
 def coeff_block(wl, cfg, hbm, *, reps=10, cpu=True):
     """The SpectralBias coefficient block (model/attn_bias.py:306-324, 419-478)
     on this rank's heads at the bench's T, M = 8 pointers, K of the config:
@@ -839,6 +916,7 @@ def main():
     ap.add_argument("--no-gpu-reference", action="store_true")
     ap.add_argument("--no-decoder", action="store_true")
     ap.add_argument("--no-score-mod", action="store_true", help="skip the score_mod-closure layer leg")
+    ap.add_argument("--no-teacher", action="store_true", help="skip the teacher block-mass leg")
     ap.add_argument("--no-graph", action="store_true", help="time the step eagerly instead of as a CUDA graph")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
@@ -957,6 +1035,7 @@ def main():
 
     coeff = coeff_block(wl, cfg, hbm, cpu=(rank == 0 and world == 1 and not args.no_cpu_baseline))
     smod = None if args.no_score_mod else score_mod_leg(wl, cfg, bm0, P_local)
+    teacher = None if args.no_teacher else teacher_leg(cfg, wl.hp)
 
     decoder = None
     if not args.no_decoder and not args.heads and args.config == "c3":
@@ -998,6 +1077,7 @@ def main():
                 "roofline": roof, "phases_ms": phases, "cpu_baseline": cpu, "e2e": e2e,
                 "clocks": clk.summary(), "gpu_launches": int(launches), "coeff_block": coeff,
                 "gpu_reference": gref, "decoder": decoder, "mask_builder": mask_builder, "score_mod": smod,
+                "teacher": teacher,
                 "step_launch": {"cuda_graph": graph is not None, "kernels_per_step": per_step,
                                 "note": graph_why or "the timed steps replay one CUDA graph of the whole step"}}
         print(json.dumps(line), flush=True)

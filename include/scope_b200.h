@@ -320,6 +320,21 @@ int scope_attn_bwd(const ScopeAttnArgs *args, scope_stream_t stream);
 /* Workspace bytes scope_attn_bwd needs for these arguments. */
 size_t scope_workspace_bytes(const ScopeAttnArgs *args);
 
+/* Teacher block mass.  Replaces the teacher's dense loop at
+ * scoped_medium.py:1793-1819: for each head h and 128-row query block qb,
+ * the dense document-causal softmax of (q k^T + q_aug k_aug^T) * scale over
+ * all keys, summed over the block's rows and over the keys of each kv block
+ * kb, into mass[h, qb, kb] ([H, QB, QB] float32; zero above the diagonal;
+ * each (h, qb) row sums to 128).  Reads q, k, the strides, docs, block_info
+ * (scope_block_info with doc_clamp 1 and no reset), scale, H, T, D (64),
+ * block_size (128), dtype (bf16), err_flag and, with bias_mode
+ * SCOPE_BIAS_QK_AUG, q_aug [H, T, d_aug] and k_aug [T, d_aug] (the teacher's
+ * q_pos / k_pos, zero-padded to d_aug = 16, 32, 48 or 64 columns); the other
+ * fields are ignored.  Documents are runs of equal ids (the reference's
+ * cumulative count of separator tokens).  Tensor cores only:
+ * SCOPE_ERR_UNSUPPORTED off sm_100. */
+int scope_block_mass(const ScopeAttnArgs *args, float *mass, scope_stream_t stream);
+
 /* Backward for callers that cannot allocate or pass a workspace (a plugin host
  * that owns all device memory and gives the library no allocator, a binding
  * without a device allocator).  No counterpart in the reference.

@@ -407,3 +407,38 @@ class SampledRows:
             dk += (ds.T @ r["qa"][:, :64]) * self.scale
             self._rowcache.pop((h, int(qb)), None)
         return {"dk": dk, "dv": dv, "q_blocks": len(qbs)}
+
+
+def teacher_block_mass(q, k, docs, *, scale: float, q_pos=None, k_pos=None, block_size: int = 128):
+    """Teacher block mass of scoped_medium.py:1793-1819, in float64: for each
+    head and query block, the dense document-causal softmax over all keys of
+    (q k^T + q_pos k_pos^T) * scale, each row's probabilities summed over the
+    keys of every kv block and over the block's query rows.
+
+    q, k [H, T, D] and q_pos [H, T, P], k_pos [H, T, P] or [T, P] (the
+    reference's augmented dims, already scaled by sqrt(beta / scale) and cast
+    to q's dtype), docs [T].  Returns mass [H, QB, QB] (float64); entry
+    [h, qb, kb] is zero above the diagonal and sums to block_size over kb."""
+    H, T, _ = q.shape
+    bs = block_size
+    QB = T // bs
+    qd, kd = q.double(), k.double()
+    docs = torch.as_tensor(docs).long()
+    if q_pos is not None:
+        qp = q_pos.double()
+        kp = k_pos.double()
+        if kp.dim() == 2:
+            kp = kp[None].expand(H, T, -1)
+    kblk = torch.arange(T) // bs
+    mass = torch.zeros(H, QB, QB, dtype=torch.float64)
+    for qb in range(QB):
+        i = torch.arange(qb * bs, (qb + 1) * bs)
+        s = torch.einsum("hid,hjd->hij", qd[:, i], kd) * scale
+        if q_pos is not None:
+            s = s + torch.einsum("hid,hjd->hij", qp[:, i], kp) * scale
+        vis = (i[:, None] >= torch.arange(T)[None, :]) & (docs[i][:, None] == docs[None, :])
+        s = s.masked_fill(~vis[None], float("-inf"))
+        p = torch.softmax(s, dim=-1)
+        colsum = p.sum(dim=1)                                    # [H, T]
+        mass[:, qb].index_add_(1, kblk, colsum)
+    return mass

@@ -5,6 +5,7 @@ Replaces, behind the reference's own interfaces:
   * the spectral score_mod / qk_aug bias   -> SpectralScoreMod (evaluated in-kernel)
   * SpectralBias.forward's coefficient block -> SpectralCoefficients / spectral_coefficients
   * flex_attention(q, k, v, block_mask, score_mod, scale) -> flex_attention
+  * the spectral teacher's dense block-mass loop        -> teacher_block_mass
 Every op runs hand-written CUDA through the C ABI of libscope_b200.so
 (include/scope_b200.h); there is no CPU fallback.
 """
@@ -12,12 +13,13 @@ from . import _lib
 from .attention import SpectralScoreMod, aug_dims, flex_attention, trig_tables
 from .coeff import CoeffOutputs, SpectralCoefficients, spectral_coefficients
 from .mask import PointerBlockMaskBuilder, ScopeBlockMask, block_info, build_mask
+from .teacher import teacher_block_mass
 from ._lib import device_errors
 
 __all__ = [
     "PointerBlockMaskBuilder", "ScopeBlockMask", "SpectralScoreMod", "aug_dims", "block_info", "build_mask",
     "flex_attention", "trig_tables", "load_library", "device_errors", "CoeffOutputs", "SpectralCoefficients",
-    "spectral_coefficients",
+    "spectral_coefficients", "teacher_block_mass",
 ]
 
 

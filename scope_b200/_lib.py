@@ -147,6 +147,7 @@ SIGNATURES = {
     "scope_attn_fwd": (I32, [ctypes.POINTER(ScopeAttnArgs), P]),
     "scope_attn_bwd": (I32, [ctypes.POINTER(ScopeAttnArgs), P]),
     "scope_workspace_bytes": (ctypes.c_size_t, [ctypes.POINTER(ScopeAttnArgs)]),
+    "scope_block_mass": (I32, [ctypes.POINTER(ScopeAttnArgs), P, P]),
     "scope_attn_bwd_static_scratch": (I32, [ctypes.POINTER(ScopeAttnArgs), P]),
     "scope_static_scratch_bytes": (ctypes.c_size_t, []),
     "scope_error_string": (ctypes.c_char_p, [I32]),

@@ -113,6 +113,7 @@ struct FwdParams {
 struct SmodParams {
     const float *slope, *dmain, *width, *b0;
     float gate_lambda, gate_itau, bias_k, beta;
+    float *mass;   // block-mass variant: [H, QB, QB] output, zeroed before the launch
 };
 
 struct Maps {
@@ -139,7 +140,12 @@ __device__ __forceinline__ float smod_bias(float dl, float slope, float dm, floa
     return b;
 }
 
-template <int DA, int SM>
+// MASS: the teacher's dense block mass (scoped_medium.py:1793-1819) instead of
+// attention: the kv list is implicit (every block from the document start of
+// the q block's first row up to the diagonal), the tiles run twice -- once for
+// the row max and sum, once for the probabilities, whose sum over each tile is
+// added into mass[h, qb, kb] -- and no V is loaded or multiplied.
+template <int DA, int SM, bool MASS = false>
 __global__ void __launch_bounds__(kThreads, 2) fwd_kernel(const __grid_constant__ Maps maps, const FwdParams p,
                                                           const __grid_constant__ SmodParams sp) {
     using L = Layout<DA>;
@@ -166,7 +172,10 @@ __global__ void __launch_bounds__(kThreads, 2) fwd_kernel(const __grid_constant_
     const int qb = blockIdx.x, h = blockIdx.y;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int64_t mrow = (int64_t)h * p.QB + qb;
-    const int n = p.kv_num[mrow];
+    // the mass variant's blocks: kb0 .. qb, kb0 the document start block of the q block's first row
+    const int kb0 = MASS ? ((p.docs && p.block_info) ? min(max(p.block_info[p.QB + qb], 0), qb) : 0) : 0;
+    const int n = MASS ? qb - kb0 + 1 : p.kv_num[mrow];
+    const int ntile = MASS ? 2 * n : n;   // tiles the producer, the issuer and the softmax walk
     const int32_t *list = p.kv_idx + mrow * p.kv_stride;
 
     if (threadIdx.x == 0) {
@@ -226,7 +235,36 @@ __global__ void __launch_bounds__(kThreads, 2) fwd_kernel(const __grid_constant_
         if (j + 2 < n) tc_commit(v_empty + (j & 1));
         return true;
     };
-    if (warp == 0) {
+    if (warp == 0 && MASS) {
+        // ------------------------------------------------------------ producer (mass): K only, both passes
+        if (lane == 0 && n > 0) {
+            mbar_expect_tx(q_full, L::Q_BYTES);
+            tma_load_3d(&maps.q, smem + L::Q, q_full, 0, qb * BM, h);
+#pragma unroll
+            for (int a = 0; a < NA; ++a) tma_load_3d(&maps.qa, smem + L::QA + a * L::ATILE, q_full, 16 * a, qb * BM, h);
+            int kissued = 0;
+            for (int j = 0; j < ntile; ++j) {
+                const int s = j & 1;
+                if (j >= 2 && (*abort_flag || !mbar_wait_idle(kv_empty + s, ((j >> 1) - 1) & 1))) {
+                    give_up();
+                    break;
+                }
+                const int kb = kb0 + (j < n ? j : j - n);
+                stage_kb[j & 3] = kb;
+                stage_mk[j & 3] = tile_kind(qb, kb, p.docs != nullptr, p.block_info, p.QB);
+                uint8_t *st = smem + L::STAGE0 + s * L::STAGE;
+                mbar_expect_tx(kv_full + s, L::K_BYTES);
+                tma_load_3d(&maps.k, st + L::K, kv_full + s, 0, kb * BM, h);
+#pragma unroll
+                for (int a = 0; a < NA; ++a) tma_load_2d(&maps.ka, st + L::KA + a * L::ATILE, kv_full + s, 16 * a, kb * BM);
+                kissued = j + 1;
+            }
+            // never leave the CTA with a TMA write still in flight
+            mbar_wait(q_full, 0, 500000000ull);
+            for (int j = (kissued > 2 ? kissued - 2 : 0); j < kissued; ++j)
+                mbar_wait(kv_full + (j & 1), (j >> 1) & 1, 500000000ull);
+        }
+    } else if (warp == 0) {
         // ------------------------------------------------------------ producer
         if (lane == 0 && n > 0) {
             mbar_expect_tx(q_full, L::Q_BYTES);
@@ -302,7 +340,7 @@ __global__ void __launch_bounds__(kThreads, 2) fwd_kernel(const __grid_constant_
                                idS, 1);
                     tc_commit(s_full);
                     // K of this stage may be reloaded once S is done (only when a later tile will be)
-                    if (j + 2 < n) tc_commit(kv_empty + s);
+                    if (j + 2 < ntile) tc_commit(kv_empty + s);
                 }
                 __syncwarp();
                 return true;
@@ -315,7 +353,7 @@ __global__ void __launch_bounds__(kThreads, 2) fwd_kernel(const __grid_constant_
             // issuing warp for about its execution time, so splitting the two kinds
             // of MMA over two warps (on two sub-partitions, other ones for the SM's
             // second CTA) spreads that cost instead of piling it on one.
-            for (int j = 0; ok && j + 1 < n; ++j)
+            for (int j = 0; ok && j + 1 < ntile; ++j)
                 ok = idle_wait(s_free, j & 1) && issue_S(j + 1);
             if (!ok) give_up();
         }
@@ -349,7 +387,17 @@ __global__ void __launch_bounds__(kThreads, 2) fwd_kernel(const __grid_constant_
         float m = -INFINITY, l = 0.f;
         bool alive = true;
         int xphase = 0;                         // completed phases of this quadrant's exchange barrier
-        for (int j = 0; j < n && alive; ++j) {
+        float mlse = 0.f;                       // mass variant, second pass: m + log2(row sum)
+        for (int j = 0; j < ntile && alive; ++j) {
+            if (MASS && j == n) {
+                // between the passes: the row sum across the two column halves
+                xsum[ch * 128 + r] = l;
+                mbar_arrive(xchg + quad);
+                if (!warp_wait(xchg + quad, xphase & 1)) { give_up(); alive = false; break; }
+                ++xphase;
+                const float ltot = l + xsum[(1 - ch) * 128 + r];
+                mlse = (ltot > 0.f && m != -INFINITY) ? m + lg2(ltot) : INFINITY;
+            }
             // the producer classified this tile: 0 full, 1 causal only, 2 document ids, 3 bad index
             if (!warp_wait(kv_full + (j & 1), (j >> 1) & 1)) { give_up(); alive = false; break; }
             const int kb = stage_kb[j & 3];
@@ -405,6 +453,24 @@ __global__ void __launch_bounds__(kThreads, 2) fwd_kernel(const __grid_constant_
                     x[c + 3] = (c + 3 <= lim && d.w == doc_i) ? x[c + 3] : -INFINITY;
                 }
             }
+            if (MASS && j >= n) {
+                // second pass: this tile's probabilities 2^(x c - mlse), summed over the
+                // thread's 64 columns, the warp's 32 rows, and added into the block mass
+                const uint64_t nl2 = f2_pack(-mlse, -mlse);
+                uint64_t acc[4] = {0ull, 0ull, 0ull, 0ull};
+#pragma unroll
+                for (int c = 0; c < 64; c += 2) {
+                    const float2 d = f2_unpack(ffma2(f2_pack(x[c], x[c + 1]), c2, nl2));
+                    const uint64_t pp = (((c >> 1) & 7) < kPolyPairs) ? ex2_fma2(d.x, d.y) : f2_pack(ex2(d.x), ex2(d.y));
+                    acc[(c >> 1) & 3] = fadd2(acc[(c >> 1) & 3], pp);
+                }
+                const float2 a01 = f2_unpack(fadd2(acc[0], acc[1])), a23 = f2_unpack(fadd2(acc[2], acc[3]));
+                float rs = (a01.x + a01.y) + (a23.x + a23.y);
+#pragma unroll
+                for (int o = 16; o; o >>= 1) rs += __shfl_xor_sync(0xffffffffu, rs, o);
+                if (lane == 0) atomicAdd(sp.mass + mrow * p.QB + kb, rs);
+                continue;
+            }
             // row max over this thread's 64 columns: 8 independent chains of
             // three-input maxima (column c in chain c & 7), then a tree
             float pm[8];
@@ -450,6 +516,7 @@ __global__ void __launch_bounds__(kThreads, 2) fwd_kernel(const __grid_constant_
             const float2 a01 = f2_unpack(fadd2(acc[0], acc[1])), a23 = f2_unpack(fadd2(acc[2], acc[3]));
             const float rs = (a01.x + a01.y) + (a23.x + a23.y);
             l = l * alpha + rs;
+            if (MASS) continue;   // first pass of the mass variant: statistics only
             // P V of the previous tile has read P and written O: P can be replaced, O rescaled
             if (j > 0) {
                 if (!warp_wait(o_done, (j - 1) & 1)) { give_up(); alive = false; break; }
@@ -470,45 +537,48 @@ __global__ void __launch_bounds__(kThreads, 2) fwd_kernel(const __grid_constant_
             tc_fence_before();
             mbar_arrive(p_full);
         }
-        // epilogue: row sum across the halves, O / l -> bf16, lse
-        bool have_o = false;
-        if (alive) {
-            xsum[ch * 128 + r] = l;
-            mbar_arrive(xchg + quad);
-            alive = warp_wait(xchg + quad, xphase & 1);
-            if (!alive) give_up();
-        }
-        const float ltot = alive ? l + xsum[(1 - ch) * 128 + r] : 0.f;
-        if (alive && n > 0) {
-            have_o = warp_wait(o_done, (n - 1) & 1);
-            if (!have_o) give_up();
-            tc_fence_after();
-        }
-        __nv_bfloat16 *orow = p.out + (int64_t)h * p.o_sh + (int64_t)i * p.o_st + ch * 32;
-        const float inv = (ltot > 0.f) ? 1.f / ltot : 0.f;
-        {
-            uint32_t o[32];
-            if (have_o) {
-                tmem_ld32_nw(tO, o);
-                tmem_wait_ld();
-                pin(o);
-            } else {
-#pragma unroll
-                for (int e = 0; e < 32; ++e) o[e] = 0u;
+        // epilogue: row sum across the halves, O / l -> bf16, lse (the mass
+        // variant wrote its output in the second pass)
+        if constexpr (!MASS) {
+            bool have_o = false;
+            if (alive) {
+                xsum[ch * 128 + r] = l;
+                mbar_arrive(xchg + quad);
+                alive = warp_wait(xchg + quad, xphase & 1);
+                if (!alive) give_up();
             }
-            uint32_t w[16];
-#pragma unroll
-            for (int e = 0; e < 16; ++e) w[e] = pack_bf16(__uint_as_float(o[2 * e]) * inv, __uint_as_float(o[2 * e + 1]) * inv);
-            uint4 *dst = reinterpret_cast<uint4 *>(orow);
-#pragma unroll
-            for (int e = 0; e < 4; ++e) dst[e] = make_uint4(w[4 * e], w[4 * e + 1], w[4 * e + 2], w[4 * e + 3]);
-        }
-        if (p.lse && ch == 0) {
-            float lse = (ltot > 0.f) ? (m + log2f(ltot)) * 0.69314718055994531f : -INFINITY;
-            if constexpr (SM != 0) {
-                if (sp.b0) lse -= sp.beta * sp.b0[(int64_t)h * p.T + i];   // the score_mod bias's row constant -beta b0
+            const float ltot = alive ? l + xsum[(1 - ch) * 128 + r] : 0.f;
+            if (alive && n > 0) {
+                have_o = warp_wait(o_done, (n - 1) & 1);
+                if (!have_o) give_up();
+                tc_fence_after();
             }
-            p.lse[(int64_t)h * p.T + i] = lse;
+            __nv_bfloat16 *orow = p.out + (int64_t)h * p.o_sh + (int64_t)i * p.o_st + ch * 32;
+            const float inv = (ltot > 0.f) ? 1.f / ltot : 0.f;
+            {
+                uint32_t o[32];
+                if (have_o) {
+                    tmem_ld32_nw(tO, o);
+                    tmem_wait_ld();
+                    pin(o);
+                } else {
+#pragma unroll
+                    for (int e = 0; e < 32; ++e) o[e] = 0u;
+                }
+                uint32_t w[16];
+#pragma unroll
+                for (int e = 0; e < 16; ++e) w[e] = pack_bf16(__uint_as_float(o[2 * e]) * inv, __uint_as_float(o[2 * e + 1]) * inv);
+                uint4 *dst = reinterpret_cast<uint4 *>(orow);
+#pragma unroll
+                for (int e = 0; e < 4; ++e) dst[e] = make_uint4(w[4 * e], w[4 * e + 1], w[4 * e + 2], w[4 * e + 3]);
+            }
+            if (p.lse && ch == 0) {
+                float lse = (ltot > 0.f) ? (m + log2f(ltot)) * 0.69314718055994531f : -INFINITY;
+                if constexpr (SM != 0) {
+                    if (sp.b0) lse -= sp.beta * sp.b0[(int64_t)h * p.T + i];   // the score_mod bias's row constant -beta b0
+                }
+                p.lse[(int64_t)h * p.T + i] = lse;
+            }
         }
     }
     __syncwarp();   // every warp reaches the CTA barrier converged (the producer ran on lane 0 alone)
@@ -572,10 +642,68 @@ int launch_fwd(const ScopeAttnArgs &a, cudaStream_t s) {
     return SCOPE_OK;
 }
 
+// the teacher's block mass: fwd_kernel's mass variant over the implicit
+// document-causal lists, into a zeroed [H, QB, QB] float32 buffer
+template <int DA>
+int launch_mass(const ScopeAttnArgs &a, float *mass, cudaStream_t s) {
+    using L = tcfwd::Layout<DA>;
+    tcfwd::Maps maps;
+    std::memset(&maps, 0, sizeof(maps));
+    bool ok = map3d(&maps.q, a.q, 64, a.T, a.H, a.q_st, a.q_sh, 64) &&
+              map3d(&maps.k, a.k, 64, a.T, a.H, a.k_st, a.k_sh, 64);
+    if (DA) ok = ok && map3d(&maps.qa, a.q_aug, DA, a.T, a.H, DA, (int64_t)a.T * DA, 16) &&
+                 map2d(&maps.ka, a.k_aug, DA, a.T, 16);
+    if (!ok) return SCOPE_ERR_ALIGN;
+    tcfwd::FwdParams p;
+    std::memset(&p, 0, sizeof(p));
+    p.H = a.H;
+    p.T = a.T;
+    p.QB = a.T / 128;
+    p.block_info = a.block_info;
+    p.docs = a.docs;
+    p.scale_log2 = a.scale * 1.4426950408889634f;
+    p.err = a.err_flag;
+    tcfwd::SmodParams sp;
+    std::memset(&sp, 0, sizeof(sp));
+    sp.mass = mass;
+    if (cudaMemsetAsync(mass, 0, sizeof(float) * (size_t)a.H * p.QB * p.QB, s) != cudaSuccess) return SCOPE_ERR_CUDA;
+    const size_t smem = L::TOTAL + 1024;
+    if (cudaFuncSetAttribute(tcfwd::fwd_kernel<DA, 0, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
+        cudaSuccess)
+        return SCOPE_ERR_CUDA;
+    dim3 grid(p.QB, a.H);
+    tcfwd::fwd_kernel<DA, 0, true><<<grid, tcfwd::kThreads, smem, s>>>(maps, p, sp);
+    SCOPE_CHECK_LAUNCH();
+    return SCOPE_OK;
+}
+
 }  // namespace tchost
 }  // namespace scope
 
 using namespace scope;
+
+extern "C" int scope_block_mass(const ScopeAttnArgs *args, float *mass, scope_stream_t stream) {
+    if (!args || !mass) return SCOPE_ERR_INVALID;
+    const ScopeAttnArgs &a = *args;
+    if (a.H <= 0 || a.T <= 0 || a.block_size != 128 || a.T % 128 != 0 || a.D != 64 || !a.q || !a.k)
+        return SCOPE_ERR_INVALID;
+    if (a.dtype != SCOPE_BF16) return SCOPE_ERR_DTYPE;
+    if (a.bias_mode != SCOPE_BIAS_NONE && a.bias_mode != SCOPE_BIAS_QK_AUG) return SCOPE_ERR_INVALID;
+    const int da = a.bias_mode == SCOPE_BIAS_QK_AUG ? a.d_aug : 0;
+    if (da && (!a.q_aug || !a.k_aug || (da != 16 && da != 32 && da != 48 && da != 64))) return SCOPE_ERR_INVALID;
+    if (!tchost::aligned16(a.q) || !tchost::aligned16(a.k) || a.q_sh % 8 || a.q_st % 8 || a.k_sh % 8 || a.k_st % 8 ||
+        (da && (!tchost::aligned16(a.q_aug) || !tchost::aligned16(a.k_aug))))
+        return SCOPE_ERR_ALIGN;
+    if (!scope_device_supported() || !tchost::encode_fn()) return SCOPE_ERR_UNSUPPORTED;
+    cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    switch (da) {
+        case 0: return tchost::launch_mass<0>(a, mass, s);
+        case 16: return tchost::launch_mass<16>(a, mass, s);
+        case 32: return tchost::launch_mass<32>(a, mass, s);
+        case 48: return tchost::launch_mass<48>(a, mass, s);
+        default: return tchost::launch_mass<64>(a, mass, s);
+    }
+}
 
 // score_mod variant of the kernels: 0 (no score_mod), 1 (no gate), 2 (softplus), 3 (relu)
 int scope_tc_smod(const ScopeAttnArgs &a) {

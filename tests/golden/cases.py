@@ -165,6 +165,21 @@ def attn_mask_knobs(case):
 
 
 # ---------------------------------------------------------------------------
+# teacher block-mass cases (scoped_medium.py:1760-1819): the reference's own
+# code run on float32 inputs (the formula pinned tightly) and on bf16 inputs
+# (its training dtype: scores rounded to bf16 by the bf16 matmuls)
+# ---------------------------------------------------------------------------
+TEACHER_CASES = {
+    "t_slope_multi_f32": dict(H=2, T=1024, K=8, slope=True, spectral=True, docs="multi", dtype="float32", seed=31),
+    "t_slope_multi_bf16": dict(H=2, T=1024, K=8, slope=True, spectral=True, docs="multi", dtype="bfloat16",
+                               seed=31),
+    "t_fourier_single_f32": dict(H=2, T=768, K=4, slope=False, spectral=True, docs="single", dtype="float32",
+                                 seed=32),
+    "t_plain_multi_f32": dict(H=1, T=768, K=4, slope=False, spectral=False, docs="multi", dtype="float32", seed=33),
+}
+
+
+# ---------------------------------------------------------------------------
 # SpectralBias coefficient block cases (model/attn_bias.py:306-324, 419-478)
 # ---------------------------------------------------------------------------
 COEFF_CASES = {

@@ -18,8 +18,11 @@ Usage (in a checkout that has the reference sources):
 
 * Coefficient fixtures: ``SpectralBias.forward`` (model/attn_bias.py:419-478)
   in eval mode and its ``_mlp_forward`` on seeded q and MLP weights.
+* Teacher fixtures: the teacher's no-grad block (scoped_medium.py:1761-1819),
+  its source lines executed unmodified on seeded inputs.
 
-Outputs: tests/golden/mask_<case>.npz, attn_<case>.npz and coeff_<case>.npz.
+Outputs: tests/golden/mask_<case>.npz, attn_<case>.npz, coeff_<case>.npz and
+teacher_<case>.npz.
 The reference is read only at generation time; the tests never import it.
 """
 from __future__ import annotations
@@ -191,6 +194,49 @@ def run_attn_case(SpectralBias, name, case):
     print(f"attn {name}: done")
 
 
+def reference_teacher_source(reference):
+    """The body of the teacher's no-grad block (scoped_medium.py:1761-1819:
+    the augmented dims, then the per-query-block dense softmax and its
+    scatter into kv blocks), read from the reference file and dedented."""
+    import textwrap
+    with open(os.path.join(reference, "scoped_medium.py")) as f:
+        src = f.read().splitlines()
+    head = next(i for i, ln in enumerate(src) if "teacher dense attention" in ln)
+    start = next(i for i in range(head, len(src)) if "q_bhtd = q.transpose(1, 2)" in src[i])
+    end = next(i for i in range(start, len(src)) if "teacher_mass[:, qb, :] = mass" in src[i])
+    return textwrap.dedent("\n".join(src[start:end + 1]))
+
+
+def run_teacher_case(reference, name, case):
+    """Runs the reference's teacher block unmodified in a namespace holding its
+    free variables: q, k [1, T, H, 64], the coefficient block's outputs
+    [1, H, T, K], the bf16 trig tables, docs, and stand-ins for ``sb``,
+    ``args`` and ``attn`` carrying the knobs it reads."""
+    import types
+    H, T, K = case["H"], case["T"], case["K"]
+    dt = getattr(torch, case["dtype"])
+    x = C.attn_inputs(dict(H=H, T=T, K=K, seed=case["seed"]))
+    docs = torch.from_numpy(C.attn_docs(dict(T=T, docs=case["docs"])))
+    cos_wD, sin_wD = AO.trig_tables(x["omegas"], T)
+    scale, beta = 0.12, 0.5
+    ns = dict(torch=torch, math=math, device=torch.device("cpu"), teacher_len=T, docs=docs,
+              q=x["q"].to(dt).transpose(0, 1)[None], k=x["k"].to(dt).transpose(0, 1)[None],
+              coeff_cos=x["coeff_cos"][None], coeff_sin=x["coeff_sin"][None], slope=x["slope"][None],
+              cos_wD=cos_wD, sin_wD=sin_wD,
+              _select_teacher_heads=lambda nh, dev: torch.arange(nh, device=dev),
+              sb=types.SimpleNamespace(use_slope=case["slope"], beta=beta, K=K),
+              args=types.SimpleNamespace(spectral_bias=case["spectral"]),
+              attn=types.SimpleNamespace(num_heads=H, attn_scale=scale))
+    exec(compile(reference_teacher_source(reference), "scoped_medium.py:teacher", "exec"), ns)
+    out = dict(q=x["q"].to(dt).float().numpy(), k=x["k"].to(dt).float().numpy(), docs=docs.numpy(),
+               scale=np.array(scale, np.float32), mass=ns["teacher_mass"].numpy())
+    if case["spectral"]:
+        out["q_pos"] = ns["q_pos"].float().numpy()
+        out["k_pos"] = ns["k_pos"].float().numpy()
+    np.savez_compressed(os.path.join(HERE, f"teacher_{name}.npz"), **out)
+    print(f"teacher {name}: done")
+
+
 COEFF_OUTS = ("coeff_cos", "coeff_sin", "slope", "b0", "delta_star", "pi", "budget_logits", "delta_main", "width")
 
 
@@ -288,6 +334,10 @@ def main():
         if a.only and a.only not in name:
             continue
         run_coeff_case(SpectralBias, name, case)
+    for name, case in C.TEACHER_CASES.items():
+        if a.only and a.only not in name:
+            continue
+        run_teacher_case(a.reference, name, case)
 
 
 if __name__ == "__main__":

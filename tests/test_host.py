@@ -54,6 +54,15 @@ def test_validation_rejects_before_launch():
     m.H, m.QB, m.M, m.block_size = 1, 4, 17, 128
     assert L.scope_mask_build(ctypes.byref(m), None) == -1        # M > 16
     assert L.scope_block_info(None, 100, 128, 1, 0, 0, None, None) == -1
+    b = _lib.ScopeAttnArgs()
+    assert L.scope_block_mass(ctypes.byref(b), None, None) == -1  # no output
+    assert L.scope_block_mass(ctypes.byref(b), 16, None) == -1    # empty args
+    b.H, b.T, b.D, b.block_size, b.dtype, b.q, b.k = 2, 256, 64, 128, 0, 16, 16
+    assert L.scope_block_mass(ctypes.byref(b), 16, None) == -2    # float32: bf16 only
+    b.dtype, b.bias_mode, b.d_aug = 1, 2, 24
+    assert L.scope_block_mass(ctypes.byref(b), 16, None) == -1    # d_aug not a multiple of 16
+    b.bias_mode = 1
+    assert L.scope_block_mass(ctypes.byref(b), 16, None) == -1    # score_mod closure: not the teacher's form
     assert L.scope_qk_aug_prepare(None, None, None, None, None, 0, 1, 1, 1, 16, 0.5, 0.12, 1, None, None, None) == -1
     # the backward's workspace: delta and lse2 [H, T], the fp32 dQ accumulator
     # [H, T, 64 + d_aug] and slope sums [H, T], the work plan

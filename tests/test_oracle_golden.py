@@ -170,3 +170,21 @@ def test_block_sparse_forward_matches_dense_oracle():
     ref, _ = AO.attention(q, k, v, AO.dense_mask(kvn, kvi, T, bs, docs=docs), scale=0.12)
     assert pairs == int(kvn.sum())
     assert (out.double() - ref).abs().max().item() < 1e-5
+
+
+@pytest.mark.parametrize("name", ["t_slope_multi_f32", "t_fourier_single_f32", "t_plain_multi_f32",
+                                  "t_slope_multi_bf16"])
+def test_teacher_mass_oracle_matches_reference(name):
+    """The float64 teacher block mass against the reference's teacher block
+    (scoped_medium.py:1761-1819) run on the same inputs: float32 inputs within
+    2e-4 (its float32 sums), bf16 inputs within 0.05 (its bf16 matmuls round
+    every score to bf16 before the softmax; measured 0.011)."""
+    f = _load(f"teacher_{name}.npz")
+    qp = torch.from_numpy(f["q_pos"]) if "q_pos" in f.files else None
+    kp = torch.from_numpy(f["k_pos"]) if "k_pos" in f.files else None
+    m = AO.teacher_block_mass(torch.from_numpy(f["q"]), torch.from_numpy(f["k"]), torch.from_numpy(f["docs"]),
+                              scale=float(f["scale"]), q_pos=qp, k_pos=kp).numpy()
+    bound = 0.05 if name.endswith("bf16") else 2e-4
+    assert np.abs(m - f["mass"]).max() < bound
+    # every query row's probabilities sum to one
+    assert np.abs(m.sum(-1) - 128.0).max() < 1e-9
