@@ -250,8 +250,6 @@ __global__ void __launch_bounds__(kThreads, 2) fwd_kernel(const __grid_constant_
                     break;
                 }
                 const int kb = kb0 + (j < n ? j : j - n);
-                stage_kb[j & 3] = kb;
-                stage_mk[j & 3] = tile_kind(qb, kb, p.docs != nullptr, p.block_info, p.QB);
                 uint8_t *st = smem + L::STAGE0 + s * L::STAGE;
                 mbar_expect_tx(kv_full + s, L::K_BYTES);
                 tma_load_3d(&maps.k, st + L::K, kv_full + s, 0, kb * BM, h);
@@ -398,10 +396,19 @@ __global__ void __launch_bounds__(kThreads, 2) fwd_kernel(const __grid_constant_
                 const float ltot = l + xsum[(1 - ch) * 128 + r];
                 mlse = (ltot > 0.f && m != -INFINITY) ? m + lg2(ltot) : INFINITY;
             }
-            // the producer classified this tile: 0 full, 1 causal only, 2 document ids, 3 bad index
-            if (!warp_wait(kv_full + (j & 1), (j >> 1) & 1)) { give_up(); alive = false; break; }
-            const int kb = stage_kb[j & 3];
-            const int mk = stage_mk[j & 3];
+            // the producer classified this tile: 0 full, 1 causal only, 2 document ids, 3 bad index.
+            // The mass variant computes both itself: its producer is held back only by
+            // the S MMAs, so a stage's kv_full may complete its next phase before these
+            // warps would wait on it (S_j done already implies K_j landed).
+            int kb, mk;
+            if constexpr (MASS) {
+                kb = kb0 + (j < n ? j : j - n);
+                mk = tile_kind(qb, kb, have_docs, p.block_info, p.QB);
+            } else {
+                if (!warp_wait(kv_full + (j & 1), (j >> 1) & 1)) { give_up(); alive = false; break; }
+                kb = stage_kb[j & 3];
+                mk = stage_mk[j & 3];
+            }
             if (mk == 3 && r == 0 && ch == 0) set_err(p.err, SCOPE_DEVERR_INDEX);
             if (!warp_wait(s_full, j & 1)) { give_up(); alive = false; break; }
             tc_fence_after();
