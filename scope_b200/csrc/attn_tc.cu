@@ -337,8 +337,9 @@ __global__ void __launch_bounds__(kThreads, 2) fwd_kernel(const __grid_constant_
                         mma_ss(tS, kmajor_desc(sq + L::QA + a * L::ATILE, 32), kmajor_desc(sk + L::KA + a * L::ATILE, 32),
                                idS, 1);
                     tc_commit(s_full);
-                    // K of this stage may be reloaded once S is done (only when a later tile will be)
-                    if (j + 2 < ntile) tc_commit(kv_empty + s);
+                    // mass variant: K of this stage may be reloaded once S is done (only when a
+                    // later tile will be)
+                    if (MASS && j + 2 < ntile) tc_commit(kv_empty + s);
                 }
                 __syncwarp();
                 return true;
@@ -351,8 +352,14 @@ __global__ void __launch_bounds__(kThreads, 2) fwd_kernel(const __grid_constant_
             // issuing warp for about its execution time, so splitting the two kinds
             // of MMA over two warps (on two sub-partitions, other ones for the SM's
             // second CTA) spreads that cost instead of piling it on one.
-            for (int j = 0; ok && j + 1 < ntile; ++j)
-                ok = idle_wait(s_free, j & 1) && issue_S(j + 1);
+            for (int j = 0; ok && j + 1 < ntile; ++j) {
+                ok = idle_wait(s_free, j & 1);
+                // attention variant: K_j's stage is released once the softmax holds S_j (so
+                // S_j is done), not when S_j completes: the softmax warps wait on kv_full of
+                // tile j before they read S_j, and K_{j+2} must not land there first
+                if (!MASS && ok && lane == 0 && j + 2 < ntile) mbar_arrive(kv_empty + (j & 1));
+                ok = ok && issue_S(j + 1);
+            }
             if (!ok) give_up();
         }
     } else {
@@ -396,10 +403,10 @@ __global__ void __launch_bounds__(kThreads, 2) fwd_kernel(const __grid_constant_
                 const float ltot = l + xsum[(1 - ch) * 128 + r];
                 mlse = (ltot > 0.f && m != -INFINITY) ? m + lg2(ltot) : INFINITY;
             }
-            // the producer classified this tile: 0 full, 1 causal only, 2 document ids, 3 bad index.
-            // The mass variant computes both itself: its producer is held back only by
-            // the S MMAs, so a stage's kv_full may complete its next phase before these
-            // warps would wait on it (S_j done already implies K_j landed).
+            // this tile's kv block and mask kind: 0 full, 1 causal only, 2 document ids,
+            // 3 bad index.  The producer classified it; the mass variant, whose producer
+            // refills a K stage as soon as the S MMA that read it is done (which can move
+            // kv_full two phases on before these warps wait on it), computes both itself.
             int kb, mk;
             if constexpr (MASS) {
                 kb = kb0 + (j < n ? j : j - n);
