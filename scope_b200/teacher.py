@@ -64,11 +64,11 @@ def teacher_block_mass(q: Tensor, k: Tensor, docs: Optional[Tensor] = None, *, s
         raise ValueError("q and k must be [H, T, 64] (or [1, H, T, 64]) of one shape")
     if q.dtype != torch.bfloat16 or k.dtype != torch.bfloat16:
         raise TypeError("teacher_block_mass takes bf16 q and k")
-    if not q.is_cuda or not k.is_cuda:
-        raise RuntimeError("scope_b200 ops run on CUDA tensors only")
     H, T, D = q.shape
     if D != 64 or T % BLOCK:
         raise ValueError("head_dim must be 64 and T a multiple of 128")
+    if not q.is_cuda or not k.is_cuda:
+        raise RuntimeError("scope_b200 ops run on CUDA tensors only")
     if q.stride(-1) != 1:
         q = q.contiguous()
     if k.stride(-1) != 1:

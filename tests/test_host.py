@@ -135,3 +135,19 @@ def test_bench_torch_builder_ops_match_oracle():
         for q in range(QB):
             n = int(num[h, q])
             assert np.array_equal(o["kv_packed"][h, q, :n], packed[h, q, :n].numpy())
+
+
+def test_teacher_block_mass_rejects_bad_inputs():
+    """Argument checks of teacher_block_mass, before any device work."""
+    import torch
+
+    from scope_b200 import teacher_block_mass
+    q = torch.zeros(2, 256, 64, dtype=torch.bfloat16)
+    with pytest.raises(RuntimeError):
+        teacher_block_mass(q, q, scale=0.12)                              # CPU tensors
+    with pytest.raises(TypeError):
+        teacher_block_mass(q.float(), q.float(), scale=0.12)              # bf16 only
+    with pytest.raises(ValueError):
+        teacher_block_mass(q, q[:1], scale=0.12)                          # q and k differ
+    with pytest.raises(ValueError):
+        teacher_block_mass(q[:, :200], q[:, :200], scale=0.12)            # T not a multiple of 128
