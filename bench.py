@@ -1024,14 +1024,17 @@ def main():
         pipe.finish()
         torch.cuda.synchronize()
         # enough steps that the pipeline's fill (the first H2D) and drain (the last
-        # D2H), which overlap nothing, do not dominate the per-step figure
-        e_steps = max(8, args.steps)
+        # D2H), which overlap nothing, do not dominate the per-step figure: over 20
+        # steps they add about a tenth of a step to each
+        e_steps = max(20, args.steps)
         ms_e = time_e2e(pipe, e_steps, world)
         h2d = sum(t.numel() * t.element_size() for t in host["in"].values())
         d2h = sum(t.numel() * t.element_size() for t in host["out"].values())
         e2e = {"value": flops / (ms_e / e_steps * 1e-3) / 1e12, "unit": "TFLOP/s",
                "h2d_bytes_per_step": h2d * world, "d2h_bytes_per_step": d2h * world,
-               "ms_per_step": ms_e / e_steps}
+               "ms_per_step": ms_e / e_steps, "steps": e_steps,
+               "note": "pipelined: step i+1's inputs travel while step i computes and step i's results "
+                       "travel back; the first H2D and the last D2H are inside the timed region"}
 
     coeff = coeff_block(wl, cfg, hbm, cpu=(rank == 0 and world == 1 and not args.no_cpu_baseline))
     smod = None if args.no_score_mod else score_mod_leg(wl, cfg, bm0, P_local)
