@@ -19,8 +19,9 @@ ABI): per (head, query block) the kv blocks from the document start of the
 block's first row to the diagonal, each 128 x 128 score tile formed once for
 the row statistics and once for the probabilities, no [T, T] scores in HBM.
 Scores stay in float32 from the bf16 inputs; the reference's bf16 matmuls
-round each score to bf16 before its softmax, which moves a block's mass by
-about 1e-2 at these magnitudes.  Runs under no_grad, as the reference's.
+round each score to bf16 before its softmax, which moves a block's mass
+(out of 128) by up to about 0.05 on unit-variance q and k at 4,096 tokens.
+Runs under no_grad, as the reference's.
 """
 from __future__ import annotations
 
