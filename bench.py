@@ -692,21 +692,32 @@ def cpu_reference(cfg, *, warmup=1, steps=3, heads=1, seconds_budget=60.0):
                       f"{len(times)} timed steps", "seconds_per_step": sec}
 
 
-def torch_builder_ops(logits, gumbel, budget_rep, *, tau, M, L, p, G, budget_rem, temp):
-    """The reference builder's steps (model/attn_bias.py:721-837) as eager torch
-    ops on the GPU -- Gumbel top-M over the causal candidates, stick-breaking
-    radius allocation with largest-remainder rounding, the local / pointer /
-    global window entries, then sort, de-duplicate and pack (unique blocks
-    ascending, repeats after) -- without the document clamp.  Timed beside
-    this package's builder kernel as the GPU-torch form of the same work; on
-    one document its lists equal the oracle's (a CPU test checks that)."""
+def torch_builder_ops(logits, gumbel, budget_rep, *, tau, M, L, p, G, budget_rem, temp, docs=None,
+                      block_size=128):
+    """The reference builder's steps (model/attn_bias.py:688-837) as eager torch
+    ops on the GPU -- the document starts of each block (change points, running
+    max), Gumbel top-M over the causal candidates, stick-breaking radius
+    allocation with largest-remainder rounding, the local / pointer / global
+    window entries with their document clamps, then sort, de-duplicate and
+    pack (unique blocks ascending, repeats after).  Timed beside this
+    package's builder kernel as the GPU-torch form of the same work; its lists
+    equal the oracle's (a CPU test checks that)."""
     H, QB, _ = logits.shape
     dev = logits.device
     qb = torch.arange(QB, device=dev)
+    dsp = dsl = torch.zeros(QB, dtype=torch.long, device=dev)
+    if docs is not None:
+        T = docs.shape[0]
+        tok = torch.arange(T, device=dev)
+        change = torch.ones(T, dtype=torch.bool, device=dev)
+        change[1:] = docs[1:] != docs[:-1]
+        dst = torch.where(change, tok, torch.zeros_like(tok)).cummax(0).values
+        dsp = torch.div(dst[(qb + 1) * block_size - 1], block_size, rounding_mode="floor")
+        dsl = torch.div(dst[qb * block_size], block_size, rounding_mode="floor")
     causal = qb[None, :] <= qb[:, None]
     s = torch.where(causal, logits / tau + gumbel, torch.full_like(logits, -float("inf")))
     cen = torch.topk(s, M, dim=-1).indices                                   # [H, QB, M]
-    cen = torch.minimum(cen, qb[None, :, None])
+    cen = torch.maximum(torch.minimum(cen, qb[None, :, None]), dsp[None, :, None])
     # radius: M - 1 stick fractions, the last piece the rest; largest-remainder rounding
     u = torch.sigmoid(budget_rep[..., : M - 1] / temp)
     rem = torch.full(u.shape[:-1], float(budget_rem), device=dev)
@@ -723,12 +734,13 @@ def torch_builder_ops(logits, gumbel, budget_rep, *, tau, M, L, p, G, budget_rem
     rank = torch.sort(torch.sort(-fr, dim=-1, stable=True).indices, dim=-1).indices
     r = (fl + (rank < left).float()).clamp(0, p).long()
     # window entries
-    local = (qb[:, None] - torch.arange(L, device=dev)[None, :]).clamp(min=0).expand(H, QB, L)
+    local = torch.maximum((qb[:, None] - torch.arange(L, device=dev)[None, :]).clamp(min=0), dsl[:, None])
+    local = local.expand(H, QB, L)
     offs = torch.arange(-p, p + 1, device=dev)
     w = (cen[..., None] + offs).clamp(0, QB - 1)
-    w = torch.minimum(w, qb[None, :, None, None])
+    w = torch.maximum(torch.minimum(w, qb[None, :, None, None]), dsp[None, :, None, None])
     w = torch.where(offs.abs() <= r[..., None], w, cen[..., None]).reshape(H, QB, -1)
-    glob = torch.minimum(torch.arange(G, device=dev)[None, :], qb[:, None]).expand(H, QB, G)
+    glob = torch.minimum(dsp[:, None] + torch.arange(G, device=dev)[None, :], qb[:, None]).expand(H, QB, G)
     ent = torch.cat([local, w, glob], -1)
     srt = ent.sort(-1).values
     first = torch.ones_like(srt, dtype=torch.bool)
@@ -844,7 +856,8 @@ def run_flex(args):
     else:
         extra = max(0, cfg.budget_blocks)
     brem = min(extra // 2, cfg.M * p_)
-    bkw = dict(tau=cfg.select_tau, M=cfg.M, L=L_, p=p_, G=G_, budget_rem=brem, temp=cfg.budget_temp)
+    bkw = dict(tau=cfg.select_tau, M=cfg.M, L=L_, p=p_, G=G_, budget_rem=brem, temp=cfg.budget_temp,
+               docs=x["docs"].long(), block_size=bs)
     for _ in range(3):
         torch_builder_ops(x["logits"], x["gumbel"], x["budget_rep"], **bkw)
     torch.cuda.synchronize()

@@ -112,9 +112,10 @@ def test_coefficient_entry_points_reject_bad_arguments():
                               delta_cap=127.0, logw_min=-5.0, logw_max=-1.0)
 
 
-def test_bench_torch_builder_ops_match_oracle():
+@pytest.mark.parametrize("cuts", [(), (100, 300, 301, 560)])
+def test_bench_torch_builder_ops_match_oracle(cuts):
     """The flex arm of the bench times the reference builder's steps as eager
-    torch ops; on one document (no clamping) they give the oracle's lists."""
+    torch ops; they give the oracle's lists, with and without documents."""
     import numpy as np
     import torch
 
@@ -124,10 +125,14 @@ def test_bench_torch_builder_ops_match_oracle():
     g = torch.Generator().manual_seed(1)
     lg, gu = torch.randn(H, QB, QB, generator=g), torch.randn(H, QB, QB, generator=g)
     br = torch.randn(H, QB, M, generator=g)
+    d = np.zeros(QB * bs, np.int64)
+    d[list(cuts)] = 1
+    docs = np.cumsum(d)
     brem = MO.resolve_budget_rem(M=M, local_blocks=L, half_blocks=p, budget_blocks=bud, budget_is_total=True)
-    num, packed = bench.torch_builder_ops(lg, gu, br, tau=0.5, M=M, L=L, p=p, G=G, budget_rem=brem, temp=0.7)
+    num, packed = bench.torch_builder_ops(lg, gu, br, tau=0.5, M=M, L=L, p=p, G=G, budget_rem=brem, temp=0.7,
+                                          docs=torch.from_numpy(docs), block_size=bs)
     cen = MO.select_pointer_blocks(lg.numpy(), gu.numpy(), M=M, tau=0.5)
-    o = MO.build_pointer_blockmask(docs=np.zeros(QB * bs, np.int32), block_size=bs, M=M, budget_rep=br.numpy(),
+    o = MO.build_pointer_blockmask(docs=docs, block_size=bs, M=M, budget_rep=br.numpy(),
                                    centres=cen, local_blocks=L, half_blocks=p, global_blocks_max=G,
                                    budget_blocks=bud, budget_is_total=True, budget_temp=0.7, with_transpose=False)
     assert np.array_equal(o["kv_num"], num.numpy())
