@@ -35,6 +35,11 @@
 // Every mbarrier wait is bounded; a wait that gives up sets
 // SCOPE_DEVERR_TIMEOUT in the error word and the CTA winds down (draining
 // its own TMA loads, freeing TMEM) instead of hanging.
+//
+// The same kernel with MASS set computes the spectral teacher's dense block
+// mass (scoped_medium.py:1793-1819, entry point scope_block_mass): no V, the
+// kv blocks from the document start of the q block to the diagonal, walked
+// twice (row statistics, then the probabilities summed per kv block).
 #include <cmath>
 #include <cstring>
 
